@@ -1,0 +1,249 @@
+/*
+ * gsb200.h — C ABI of the B200 (sm_100a) Gaussian-splatting render-and-loss
+ * hot path (libgsb200.so).
+ *
+ * Conventions shared by every entry point:
+ *  - All array arguments are DEVICE pointers to flat, dense buffers with the
+ *    reference's layouts (documented per call).  Camera arrays (view[16],
+ *    intrinsics[4], center[3]) and small scalars that the reference keeps on
+ *    the device (cluster_count[1], pair_count[1], grad_scale[1]) are device
+ *    pointers too, so no call ever synchronises with the host.
+ *  - Launches are asynchronous on `stream`.  Return value: GSB_OK, or a
+ *    GSB_ERR_* code for invalid parameters, a too-small workspace, or a
+ *    launch failure.  Arena overflow is reported as data (overflow[1]).
+ *  - Calls that need temporaries take (workspace, workspace_bytes); query
+ *    the size with the matching *_workspace_size().  Workspace base must be
+ *    256-byte aligned (cudaMalloc / torch allocations are).
+ *  - Outputs are written in full where the reference defines them; the
+ *    undefined regions are the reference's (arena tail past pair_count,
+ *    compact-gradient tail, projected fields outside the listed clusters).
+ *
+ * Reference interfaces replaced (imgengineer/jax-gs, src/jaxgs/...):
+ *  each declaration cites the cutlass_call launcher it replaces.
+ */
+#ifndef GSB200_H
+#define GSB200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define GSB_API __attribute__((visibility("default")))
+#else
+#define GSB_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef void* gsb_stream_t; /* a cudaStream_t */
+
+enum {
+    GSB_OK = 0,
+    GSB_ERR_INVALID = 1,    /* bad shape / unsupported option */
+    GSB_ERR_WORKSPACE = 2,  /* workspace too small or misaligned */
+    GSB_ERR_LAUNCH = 3,     /* CUDA launch error */
+    GSB_ERR_NULL = 4        /* required pointer is NULL */
+};
+
+#define GSB_ABI_VERSION 1
+
+/* Library ABI version (GSB_ABI_VERSION). */
+GSB_API int gsb_abi_version(void);
+/* Last CUDA error string seen by the library (thread-local). */
+GSB_API const char* gsb_last_error(void);
+
+/* ------------------------------------------------------------------------
+ * Cluster culling + compaction.
+ * Replaces scene/cluster.py:40-67 (frustum_cluster_mask) and
+ * kernels/cluster_compact.py:31-44 (compact_visible_clusters; XLA cumsum +
+ * CuTe _scatter), as called by render/pipeline.py:18-44.
+ * center/extent: [num_clusters,3]; valid: [num_clusters] u8;
+ * planes: [6,4] device floats (a,b,c,d).  Outputs: ids[num_clusters] (stable
+ * ascending visible cluster ids; tail undefined), count[1],
+ * visible_slots[capacity] u8 (slot mask, repeat of the cluster mask).
+ * ------------------------------------------------------------------------ */
+typedef struct {
+    int num_clusters;
+    int cluster_size;
+    int capacity;
+} gsb_cluster_params;
+
+GSB_API size_t gsb_cluster_compact_workspace_size(const gsb_cluster_params* p);
+GSB_API int gsb_cluster_compact(gsb_stream_t stream, const gsb_cluster_params* p, void* workspace,
+                        size_t workspace_bytes, const float* center, const float* extent,
+                        const uint8_t* valid, const float* planes, int32_t* ids,
+                        int32_t* count, uint8_t* visible_slots);
+
+/* ------------------------------------------------------------------------
+ * Projection forward.
+ * Replaces kernels/projector.py:17-100 (_project_gaussian_arrays ->
+ * cutlass_call(launch_projection), kernels/projection.py:213-285).
+ * Inputs: xyz[C*3], log_scale[C*3], rotation[C*4] (wxyz), opacity[C] (logit),
+ * sh[C*sh_dim*3], alive[C] u8, view[16] (row-major world-to-camera),
+ * intrinsics[4] (fx,fy,cx,cy), center[3]; cluster_ids / cluster_count used
+ * when compacted.  Outputs: mean[C*2], depth[C], conic[C*4], radius[C],
+ * color[C*3], alpha[C], visible[C] i8.
+ * ------------------------------------------------------------------------ */
+typedef struct {
+    int capacity;
+    int sh_dim;            /* coefficients stored per Gaussian (1,4,9,16) */
+    int degree;            /* active SH degree, 0..3, (degree+1)^2 <= sh_dim */
+    int width, height;
+    float near_plane, far_plane;
+    int cluster_size;
+    int compacted;          /* 1: only the listed clusters' slots */
+    int clear_invisible;    /* compacted only: zero the other slots' fields */
+    int visible_color_only; /* culled slots get colour 0 instead of SH */
+} gsb_project_params;
+
+GSB_API int gsb_project_fwd(gsb_stream_t stream, const gsb_project_params* p, const float* xyz,
+                    const float* log_scale, const float* rotation, const float* opacity,
+                    const float* sh, const uint8_t* alive, const float* view,
+                    const float* intrinsics, const float* center, const int32_t* cluster_ids,
+                    const int32_t* cluster_count, float* mean, float* depth, float* conic,
+                    float* radius, float* color, float* alpha, int8_t* visible);
+
+/* ------------------------------------------------------------------------
+ * Projection pullback (parameter gradients).
+ * Replaces kernels/projector.py:240-307 (_compute_projection_gradients ->
+ * cutlass_call(launch_projection_backward), projection_backward.py:393-472).
+ * Cotangents: gmean[C*2], gdepth[C] (unused if rgb_only), gconic[C*4],
+ * gradius[C] (unused if rgb_only), gcolor[C*3], galpha[C].
+ * Outputs (compact visible-cluster order when compact_gradients, else pool
+ * order): gxyz[C*3], glog_scale[C*3], grotation[C*4], gopacity[C],
+ * gsh[C*sh_gradient_dim*3].
+ * ------------------------------------------------------------------------ */
+typedef struct {
+    int capacity;
+    int sh_dim;
+    int sh_gradient_dim;   /* sh_dim, (degree+1)^2 (active only) or 1 (colour only) */
+    int degree;
+    float near_plane;
+    int cluster_size;
+    int compacted;
+    int compact_gradients;
+    int rgb_only;
+    int sh_color_only;
+} gsb_project_bwd_params;
+
+GSB_API int gsb_project_bwd(gsb_stream_t stream, const gsb_project_bwd_params* p, const float* xyz,
+                    const float* log_scale, const float* rotation, const float* opacity,
+                    const float* sh, const float* view, const float* intrinsics,
+                    const float* center, const float* color, const int32_t* cluster_ids,
+                    const int32_t* cluster_count, const float* gmean, const float* gdepth,
+                    const float* gconic, const float* gradius, const float* gcolor,
+                    const float* galpha, float* gxyz, float* glog_scale, float* grotation,
+                    float* gopacity, float* gsh);
+
+/* ------------------------------------------------------------------------
+ * Tile binning (AccuTile count, depth sort, scan, emission, stable tile sort,
+ * tile ranges) in one call.
+ * Replaces kernels/sorted_binning.py:9-117 (build_sorted_visibility_table_cute:
+ * launch_count_pairs, jax.lax.sort, launch_pair_offsets, launch_emit_pairs,
+ * pair_sort.sort_pairs_by_tile, launch_tile_ranges).
+ * Inputs: mean[C*2], conic[C*4], alpha[C], depth[C], visible[C] i8.
+ * Outputs: point_counts[C], gaussian_ids[max_pairs] (valid prefix ends at
+ * min(pair_count, max_pairs)), tile_offsets[T+1], pair_count[1] (unclamped),
+ * overflow[1] (pair_count > max_pairs).  T = ceil(W/tile_w)*ceil(H/tile_h).
+ * ------------------------------------------------------------------------ */
+typedef struct {
+    int capacity;
+    int width, height;
+    int tile_w, tile_h;    /* reference tile_size (width) and tile_height */
+    int64_t max_pairs;     /* arena capacity, < 2^31 */
+} gsb_bin_params;
+
+GSB_API size_t gsb_bin_workspace_size(const gsb_bin_params* p);
+GSB_API int gsb_bin(gsb_stream_t stream, const gsb_bin_params* p, void* workspace,
+            size_t workspace_bytes, const float* mean, const float* conic, const float* alpha,
+            const float* depth, const int8_t* visible, int32_t* point_counts,
+            int32_t* gaussian_ids, int32_t* tile_offsets, int32_t* pair_count,
+            int32_t* overflow);
+
+/* ------------------------------------------------------------------------
+ * fp32 rasterization forward.
+ * Replaces kernels/sorted_rasterizer.py:15-70 (_forward_arrays ->
+ * cutlass_call(launch_forward_sorted), sorted_rasterize.py:28-88), extended to
+ * the rectangular tiles of the packed path (tile_w x tile_h with tile_w a
+ * multiple of 8 and tile_h a multiple of 4).
+ * Inputs: mean[C*2], conic[C*4], depth[C], color[C*3], alpha[C] (opacity
+ * after sigmoid), visible[C] i8, gaussian_ids, tile_offsets[T+1],
+ * background[3].
+ * Outputs: rgb[H*W*3], out_depth[H*W] (may be NULL), out_alpha[H*W] (may be
+ * NULL), final_t[H*W], last[H*W] (one past the last composited pair),
+ * backward_work[T] (max over the tile's pixels of last - tile start),
+ * splats[C*12] (48-byte staged records reused by the backward pass).
+ * ------------------------------------------------------------------------ */
+typedef struct {
+    int capacity;
+    int width, height;
+    int tile_w, tile_h;
+} gsb_raster_params;
+
+GSB_API size_t gsb_raster_workspace_size(const gsb_raster_params* p);
+GSB_API int gsb_raster_fwd(gsb_stream_t stream, const gsb_raster_params* p, void* workspace,
+                   size_t workspace_bytes, const float* mean, const float* conic,
+                   const float* depth, const float* color, const float* alpha,
+                   const int8_t* visible, const int32_t* gaussian_ids,
+                   const int32_t* tile_offsets, const float* background, float* rgb,
+                   float* out_depth, float* out_alpha, float* final_t, int32_t* last,
+                   int32_t* backward_work, float* splats);
+
+/* ------------------------------------------------------------------------
+ * fp32 rasterization backward.
+ * Replaces kernels/sorted_rasterizer.py:165-236 (the launch_backward_sorted
+ * call inside rasterize_loss_and_grad; kernel sorted_rasterize.py:91-236).
+ * Inputs: the forward's splats/final_t/last/backward_work, depth[C] (for the
+ * depth cotangent), gaussian_ids, tile_offsets, background[3], drgb[H*W*3],
+ * ddepth[H*W] and dalpha[H*W] (may be NULL = zero).  cluster_ids/count:
+ * when non-NULL only the listed clusters' cotangents are zeroed (the table
+ * must reference no other Gaussian, kernels/packed_rasterize.py:753-758);
+ * otherwise the whole pool is zeroed.
+ * Outputs (accumulated): gmean[C*2], gconic[C*4], gdepth[C], gcolor[C*3],
+ * galpha[C].
+ * ------------------------------------------------------------------------ */
+typedef struct {
+    int capacity;
+    int width, height;
+    int tile_w, tile_h;
+    int cluster_size;
+} gsb_raster_bwd_params;
+
+GSB_API int gsb_raster_bwd(gsb_stream_t stream, const gsb_raster_bwd_params* p, void* workspace,
+                   size_t workspace_bytes, const float* splats, const float* depth,
+                   const int32_t* gaussian_ids, const int32_t* tile_offsets,
+                   const float* background, const float* final_t, const int32_t* last,
+                   const int32_t* backward_work, const float* drgb, const float* ddepth,
+                   const float* dalpha, const int32_t* cluster_ids,
+                   const int32_t* cluster_count, float* gmean, float* gconic, float* gdepth,
+                   float* gcolor, float* galpha);
+
+/* ------------------------------------------------------------------------
+ * Fused L1(0.8) + SSIM(0.2) loss and image gradient.
+ * Replaces kernels/fused_loss.py:333-352 (fused_loss_and_grad /
+ * _fused_loss_and_grad_with_scale -> cutlass_call(_launch)).
+ * image[H*W*3] f32; target[H*W*3] u8 (target_u8=1) or f32 in [0,1].
+ * clip_input=1 evaluates the loss on clip(image,0,1) and multiplies the
+ * gradient by the clip's derivative (1 inside, 1/2 at 0 or 1, 0 outside),
+ * as kernels/sorted_rasterizer.py:206-209 does with jax.vjp(jnp.clip).
+ * Outputs: loss[1] (mean over 3HW), grad[H*W*3], scale[1] = max(max|grad|,
+ * 1e-12) (may be NULL).
+ * ------------------------------------------------------------------------ */
+typedef struct {
+    int width, height;
+    int target_u8;
+    int clip_input;
+} gsb_loss_params;
+
+GSB_API size_t gsb_loss_workspace_size(const gsb_loss_params* p);
+GSB_API int gsb_loss(gsb_stream_t stream, const gsb_loss_params* p, void* workspace,
+             size_t workspace_bytes, const float* image, const void* target, float* loss,
+             float* grad, float* scale);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GSB200_H */

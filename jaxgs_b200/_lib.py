@@ -1,0 +1,120 @@
+"""ctypes binding of libgsb200.so (include/gsb200.h).
+
+The product path has no fallback: if the library (built for sm_100a by
+jaxgs_b200.build) is missing or fails to load, importing this module raises.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from pathlib import Path
+
+_HERE = Path(__file__).resolve().parent
+LIB_PATH = _HERE / "libgsb200.so"
+
+GSB_OK = 0
+_ERRORS = {1: "invalid parameters", 2: "workspace too small or misaligned", 3: "CUDA launch error",
+           4: "required pointer is NULL"}
+
+
+class ClusterParams(ctypes.Structure):
+    _fields_ = [("num_clusters", ctypes.c_int), ("cluster_size", ctypes.c_int),
+                ("capacity", ctypes.c_int)]
+
+
+class ProjectParams(ctypes.Structure):
+    _fields_ = [("capacity", ctypes.c_int), ("sh_dim", ctypes.c_int), ("degree", ctypes.c_int),
+                ("width", ctypes.c_int), ("height", ctypes.c_int),
+                ("near_plane", ctypes.c_float), ("far_plane", ctypes.c_float),
+                ("cluster_size", ctypes.c_int), ("compacted", ctypes.c_int),
+                ("clear_invisible", ctypes.c_int), ("visible_color_only", ctypes.c_int)]
+
+
+class ProjectBwdParams(ctypes.Structure):
+    _fields_ = [("capacity", ctypes.c_int), ("sh_dim", ctypes.c_int),
+                ("sh_gradient_dim", ctypes.c_int), ("degree", ctypes.c_int),
+                ("near_plane", ctypes.c_float), ("cluster_size", ctypes.c_int),
+                ("compacted", ctypes.c_int), ("compact_gradients", ctypes.c_int),
+                ("rgb_only", ctypes.c_int), ("sh_color_only", ctypes.c_int)]
+
+
+class BinParams(ctypes.Structure):
+    _fields_ = [("capacity", ctypes.c_int), ("width", ctypes.c_int), ("height", ctypes.c_int),
+                ("tile_w", ctypes.c_int), ("tile_h", ctypes.c_int), ("max_pairs", ctypes.c_int64)]
+
+
+class RasterParams(ctypes.Structure):
+    _fields_ = [("capacity", ctypes.c_int), ("width", ctypes.c_int), ("height", ctypes.c_int),
+                ("tile_w", ctypes.c_int), ("tile_h", ctypes.c_int)]
+
+
+class RasterBwdParams(ctypes.Structure):
+    _fields_ = [("capacity", ctypes.c_int), ("width", ctypes.c_int), ("height", ctypes.c_int),
+                ("tile_w", ctypes.c_int), ("tile_h", ctypes.c_int), ("cluster_size", ctypes.c_int)]
+
+
+class LossParams(ctypes.Structure):
+    _fields_ = [("width", ctypes.c_int), ("height", ctypes.c_int), ("target_u8", ctypes.c_int),
+                ("clip_input", ctypes.c_int)]
+
+
+# Symbols declared by include/gsb200.h.
+SYMBOLS = (
+    "gsb_abi_version", "gsb_last_error",
+    "gsb_cluster_compact_workspace_size", "gsb_cluster_compact",
+    "gsb_project_fwd", "gsb_project_bwd",
+    "gsb_bin_workspace_size", "gsb_bin",
+    "gsb_raster_workspace_size", "gsb_raster_fwd", "gsb_raster_bwd",
+    "gsb_loss_workspace_size", "gsb_loss",
+)
+
+
+def _load():
+    if not LIB_PATH.exists():
+        raise RuntimeError(
+            f"{LIB_PATH} is missing: build the sm_100a kernels with `python -m jaxgs_b200.build` "
+            "(there is no CPU fallback)")
+    lib = ctypes.CDLL(str(LIB_PATH))
+    vp, sz = ctypes.c_void_p, ctypes.c_size_t
+    lib.gsb_abi_version.restype = ctypes.c_int
+    lib.gsb_abi_version.argtypes = []
+    lib.gsb_last_error.restype = ctypes.c_char_p
+    lib.gsb_last_error.argtypes = []
+    for name in ("gsb_cluster_compact_workspace_size", "gsb_bin_workspace_size",
+                 "gsb_raster_workspace_size", "gsb_loss_workspace_size"):
+        getattr(lib, name).restype = sz
+        getattr(lib, name).argtypes = [vp]
+    lib.gsb_cluster_compact.restype = ctypes.c_int
+    lib.gsb_cluster_compact.argtypes = [vp, vp, vp, sz] + [vp] * 7
+    lib.gsb_project_fwd.restype = ctypes.c_int
+    lib.gsb_project_fwd.argtypes = [vp, vp] + [vp] * 18
+    lib.gsb_project_bwd.restype = ctypes.c_int
+    lib.gsb_project_bwd.argtypes = [vp, vp] + [vp] * 22
+    lib.gsb_bin.restype = ctypes.c_int
+    lib.gsb_bin.argtypes = [vp, vp, vp, sz] + [vp] * 10
+    lib.gsb_raster_fwd.restype = ctypes.c_int
+    lib.gsb_raster_fwd.argtypes = [vp, vp, vp, sz] + [vp] * 16
+    lib.gsb_raster_bwd.restype = ctypes.c_int
+    lib.gsb_raster_bwd.argtypes = [vp, vp, vp, sz] + [vp] * 18
+    lib.gsb_loss.restype = ctypes.c_int
+    lib.gsb_loss.argtypes = [vp, vp, vp, sz] + [vp] * 5
+    return lib
+
+
+lib = _load()
+if lib.gsb_abi_version() != 1:
+    raise RuntimeError("libgsb200.so ABI version mismatch; rebuild with `python -m jaxgs_b200.build`")
+
+
+def check(code: int, what: str) -> None:
+    """Raise like the reference's pre-launch checks (ValueError for bad shapes)."""
+    if code == GSB_OK:
+        return
+    detail = _ERRORS.get(code, f"error {code}")
+    if code == 3:
+        raise RuntimeError(f"{what}: {detail}: {lib.gsb_last_error().decode()}")
+    raise ValueError(f"{what}: {detail}")
+
+
+def ref(struct) -> ctypes.c_void_p:
+    return ctypes.cast(ctypes.pointer(struct), ctypes.c_void_p)

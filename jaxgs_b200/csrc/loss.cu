@@ -1,0 +1,285 @@
+// Fused L1(0.8) + SSIM(0.2) loss, image gradient and gradient scale (sm_100a).
+//
+// Semantics: reference/loss.py:6-43 (11x11 Gaussian window, sigma 1.5, SAME
+// zero padding, C1 = 0.01^2, C2 = 0.03^2) with the per-pixel gradient of
+// kernels/fused_loss.py:229-288: for every pixel the SSIM partials
+// dS/dmu_x, dS/dE[x^2], dS/dE[xy] are formed from the window statistics and
+// blurred once more, grad = blur(p0) + 2x blur(p1) + y blur(p2)
+// + 0.8 sign(x - y) / (3HW).
+//
+// One CTA per 32x16 output tile and channel loop.  The CTA stages a 52x36
+// zero-padded patch of image and target (10-pixel halo), computes the five
+// window statistics over the 42x26 region whose partials the output needs
+// (separable: horizontal then vertical 11-tap passes in shared memory), the
+// partials and the loss there, then blurs the partials back onto the 32x16
+// tile.  The loss map and the partials never reach global memory.  Per-CTA
+// loss sums and |grad| maxima are reduced by a second, single-block kernel in
+// a fixed order, so the scalar results are deterministic.
+#include "gsb_common.cuh"
+
+namespace gsb {
+namespace {
+
+constexpr int kTW = 32, kTH = 16, kR = 5;
+constexpr int kSW = kTW + 2 * kR, kSH = kTH + 2 * kR;  // 42 x 26 statistics region
+constexpr int kPW = kSW + 2 * kR, kPH = kSH + 2 * kR;  // 52 x 36 staged patch
+constexpr int kThreads = 256;
+
+// exp(-(d/1.5)^2 / 2) normalised, correctly rounded to float32.
+__constant__ float kTaps[11] = {0.001028380123898387f, 0.0075987582094967365f,
+                                0.036000773310661316f, 0.10936068743467331f,
+                                0.21300554275512695f,  0.26601171493530273f,
+                                0.21300554275512695f,  0.10936068743467331f,
+                                0.036000773310661316f, 0.0075987582094967365f,
+                                0.001028380123898387f};
+
+struct LossSmem {
+    float x[kPH][kPW];
+    float y[kPH][kPW];
+    float h[5][kPH][kSW];      // horizontal sums of x, x^2, y, y^2, xy
+    float part[3][kSH][kSW];   // p0, p1, p2
+    float hp[3][kSH][kTW + 1]; // horizontally blurred partials
+};
+
+__device__ __forceinline__ float clip01(float v) { return fminf(fmaxf(v, 0.0f), 1.0f); }
+
+// d clip(v, 0, 1) / dv with jnp.maximum/minimum tie semantics (1/2 at a bound).
+__device__ __forceinline__ float clip_grad(float v)
+{
+    if (v > 0.0f && v < 1.0f) return 1.0f;
+    if (v == 0.0f || v == 1.0f) return 0.5f;
+    return 0.0f;
+}
+
+template <bool U8, bool CLIP>
+__global__ void __launch_bounds__(kThreads) loss_kernel(int width, int height,
+                                                        const float* __restrict__ image,
+                                                        const void* __restrict__ target_raw,
+                                                        float* __restrict__ grad,
+                                                        float* __restrict__ block_loss,
+                                                        uint32_t* __restrict__ block_scale)
+{
+    extern __shared__ float4 smem_raw[];
+    LossSmem& S = *reinterpret_cast<LossSmem*>(smem_raw);
+    __shared__ float warp_loss[kThreads / 32];
+    __shared__ uint32_t warp_scale[kThreads / 32];
+    const int tid = threadIdx.x;
+    const int x0 = blockIdx.x * kTW, y0 = blockIdx.y * kTH;
+    const float inv_n = 1.0f / (3.0f * (float)width * (float)height);
+    const float weight = -0.2f * inv_n;
+    float loss = 0.0f;
+    uint32_t scale_bits = 0;
+    const uint8_t* t8 = static_cast<const uint8_t*>(target_raw);
+    const float* tf = static_cast<const float*>(target_raw);
+    for (int c = 0; c < 3; c++) {
+        // 1. Stage the zero-padded patch.
+        for (int k = tid; k < kPH * kPW; k += kThreads) {
+            int r = k / kPW, q = k % kPW;
+            int gx = x0 + q - 2 * kR, gy = y0 + r - 2 * kR;
+            float xv = 0.0f, yv = 0.0f;
+            if (gx >= 0 && gx < width && gy >= 0 && gy < height) {
+                int64_t idx = ((int64_t)gy * width + gx) * 3 + c;
+                xv = image[idx];
+                if (CLIP) xv = clip01(xv);
+                yv = U8 ? (float)t8[idx] * (float)(1.0 / 255.0) : tf[idx];
+            }
+            S.x[r][q] = xv;
+            S.y[r][q] = yv;
+        }
+        __syncthreads();
+        // 2. Horizontal window sums over the statistics columns.
+        for (int k = tid; k < kPH * kSW; k += kThreads) {
+            int r = k / kSW, q = k % kSW;
+            float sx = 0.f, sxx = 0.f, sy = 0.f, syy = 0.f, sxy = 0.f;
+#pragma unroll
+            for (int t = 0; t < 11; t++) {
+                float w = kTaps[t], a = S.x[r][q + t], b = S.y[r][q + t];
+                sx += w * a;
+                sxx += w * a * a;
+                sy += w * b;
+                syy += w * b * b;
+                sxy += w * a * b;
+            }
+            S.h[0][r][q] = sx;
+            S.h[1][r][q] = sxx;
+            S.h[2][r][q] = sy;
+            S.h[3][r][q] = syy;
+            S.h[4][r][q] = sxy;
+        }
+        __syncthreads();
+        // 3. Vertical sums -> statistics -> SSIM partials and loss.
+        for (int k = tid; k < kSH * kSW; k += kThreads) {
+            int r = k / kSW, q = k % kSW;
+            float m[5] = {0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int t = 0; t < 11; t++) {
+                float w = kTaps[t];
+#pragma unroll
+                for (int s = 0; s < 5; s++) m[s] += w * S.h[s][r + t][q];
+            }
+            int gx = x0 + q - kR, gy = y0 + r - kR;
+            float p0 = 0.f, p1 = 0.f, p2 = 0.f;
+            if (gx >= 0 && gx < width && gy >= 0 && gy < height) {
+                float mx = m[0], xx = m[1], my = m[2], yy = m[3], xy = m[4];
+                float A = mx * mx + my * my + 1e-4f;
+                float B = (xx - mx * mx) + (yy - my * my) + 9e-4f;
+                float Cc = 2.0f * mx * my + 1e-4f;
+                float D = 2.0f * (xy - mx * my) + 9e-4f;
+                float inv_ab = 1.0f / (A * B);
+                float ssim = Cc * D * inv_ab;
+                p0 = (2.0f * my * (D - Cc) * inv_ab + 2.0f * mx * ssim * (1.0f / B - 1.0f / A)) * weight;
+                p1 = -ssim / B * weight;
+                p2 = 2.0f * Cc * inv_ab * weight;
+                if (r >= kR && r < kR + kTH && q >= kR && q < kR + kTW) {
+                    float xv = S.x[r + kR][q + kR], yv = S.y[r + kR][q + kR];
+                    loss += 0.2f * (1.0f - ssim) + 0.8f * fabsf(xv - yv);
+                }
+            }
+            S.part[0][r][q] = p0;
+            S.part[1][r][q] = p1;
+            S.part[2][r][q] = p2;
+        }
+        __syncthreads();
+        // 4. Horizontal blur of the partials onto the tile columns.
+        for (int k = tid; k < kSH * kTW; k += kThreads) {
+            int r = k / kTW, q = k % kTW;
+            float a = 0.f, b = 0.f, d = 0.f;
+#pragma unroll
+            for (int t = 0; t < 11; t++) {
+                float w = kTaps[t];
+                a += w * S.part[0][r][q + t];
+                b += w * S.part[1][r][q + t];
+                d += w * S.part[2][r][q + t];
+            }
+            S.hp[0][r][q] = a;
+            S.hp[1][r][q] = b;
+            S.hp[2][r][q] = d;
+        }
+        __syncthreads();
+        // 5. Vertical blur -> image gradient.
+        for (int k = tid; k < kTH * kTW; k += kThreads) {
+            int r = k / kTW, q = k % kTW;
+            int px = x0 + q, py = y0 + r;
+            if (px < width && py < height) {
+                float a = 0.f, b = 0.f, d = 0.f;
+#pragma unroll
+                for (int t = 0; t < 11; t++) {
+                    float w = kTaps[t];
+                    a += w * S.hp[0][r + t][q];
+                    b += w * S.hp[1][r + t][q];
+                    d += w * S.hp[2][r + t][q];
+                }
+                float xv = S.x[r + 2 * kR][q + 2 * kR], yv = S.y[r + 2 * kR][q + 2 * kR];
+                float sign = xv > yv ? 1.0f : (xv < yv ? -1.0f : 0.0f);
+                float value = a + 2.0f * xv * b + yv * d + 0.8f * sign * inv_n;
+                int64_t idx = ((int64_t)py * width + px) * 3 + c;
+                if (CLIP) value *= clip_grad(image[idx]);
+                grad[idx] = value;
+                scale_bits = max(scale_bits, __float_as_uint(value) & 0x7fffffffu);
+            }
+        }
+        __syncthreads();
+    }
+    loss = warp_sum(loss);
+#pragma unroll
+    for (int d = 16; d > 0; d >>= 1) scale_bits = max(scale_bits, __shfl_xor_sync(GSB_FULL_MASK, scale_bits, d));
+    if ((tid & 31) == 0) {
+        warp_loss[tid >> 5] = loss;
+        warp_scale[tid >> 5] = scale_bits;
+    }
+    __syncthreads();
+    if (tid == 0) {
+        float total = 0.0f;
+        uint32_t sb = 0;
+        for (int w = 0; w < kThreads / 32; w++) {
+            total += warp_loss[w];
+            sb = max(sb, warp_scale[w]);
+        }
+        int b = blockIdx.y * gridDim.x + blockIdx.x;
+        block_loss[b] = total;
+        block_scale[b] = sb;
+    }
+}
+
+// Fixed-order reduction of the per-CTA partials (deterministic).
+__global__ void __launch_bounds__(1024) loss_finish_kernel(int blocks, float inv_n,
+                                                           const float* __restrict__ block_loss,
+                                                           const uint32_t* __restrict__ block_scale,
+                                                           float* loss, float* scale)
+{
+    __shared__ double partial[32];
+    __shared__ uint32_t pscale[32];
+    double s = 0.0;
+    uint32_t m = 0;
+    for (int b = threadIdx.x; b < blocks; b += blockDim.x) {
+        s += (double)block_loss[b];
+        m = max(m, block_scale[b]);
+    }
+    s = warp_sum(s);
+#pragma unroll
+    for (int d = 16; d > 0; d >>= 1) m = max(m, __shfl_xor_sync(GSB_FULL_MASK, m, d));
+    if ((threadIdx.x & 31) == 0) {
+        partial[threadIdx.x >> 5] = s;
+        pscale[threadIdx.x >> 5] = m;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double t = 0.0;
+        uint32_t mm = 0;
+        for (int w = 0; w < (int)(blockDim.x >> 5); w++) {
+            t += partial[w];
+            mm = max(mm, pscale[w]);
+        }
+        *loss = (float)(t * (double)inv_n);
+        if (scale) {
+            float v = __uint_as_float(mm);
+            *scale = (v != v) ? v : fmaxf(v, 1e-12f);
+        }
+    }
+}
+
+int loss_blocks(const gsb_loss_params& p) { return ceil_div(p.width, kTW) * ceil_div(p.height, kTH); }
+
+}  // namespace
+}  // namespace gsb
+
+using namespace gsb;
+
+extern "C" size_t gsb_loss_workspace_size(const gsb_loss_params* p)
+{
+    if (!p || p->width <= 0 || p->height <= 0) return 0;
+    return 2 * (((size_t)loss_blocks(*p) * 4 + 255) & ~size_t(255));
+}
+
+extern "C" int gsb_loss(gsb_stream_t stream, const gsb_loss_params* p, void* workspace,
+                        size_t workspace_bytes, const float* image, const void* target,
+                        float* loss, float* grad, float* scale)
+{
+    if (!p) return GSB_ERR_NULL;
+    if (p->width <= 0 || p->height <= 0) return GSB_ERR_INVALID;
+    if (!workspace || workspace_bytes < gsb_loss_workspace_size(p)) return GSB_ERR_WORKSPACE;
+    if (!image || !target || !loss || !grad) return GSB_ERR_NULL;
+    cudaStream_t s = as_stream(stream);
+    int blocks = loss_blocks(*p);
+    size_t half = ((size_t)blocks * 4 + 255) & ~size_t(255);
+    float* block_loss = static_cast<float*>(workspace);
+    uint32_t* block_scale = reinterpret_cast<uint32_t*>(static_cast<char*>(workspace) + half);
+    dim3 grid(ceil_div(p->width, kTW), ceil_div(p->height, kTH));
+    size_t smem = sizeof(LossSmem);
+    auto launch = [&](auto kernel) {
+        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        kernel<<<grid, kThreads, smem, s>>>(p->width, p->height, image, target, grad, block_loss,
+                                            block_scale);
+    };
+    if (p->target_u8) {
+        if (p->clip_input) launch(loss_kernel<true, true>);
+        else launch(loss_kernel<true, false>);
+    } else {
+        if (p->clip_input) launch(loss_kernel<false, true>);
+        else launch(loss_kernel<false, false>);
+    }
+    if (int e = check_launch()) return e;
+    float inv_n = 1.0f / (3.0f * (float)p->width * (float)p->height);
+    loss_finish_kernel<<<1, 1024, 0, s>>>(blocks, inv_n, block_loss, block_scale, loss, scale);
+    return check_launch();
+}

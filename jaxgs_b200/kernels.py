@@ -1,0 +1,343 @@
+"""Torch-facing entry points of the hot path, one per reference binding.
+
+Each function keeps the reference binding's name, argument meaning and error
+behaviour (ValueError / RuntimeError before launch) and calls the C ABI of
+libgsb200.so on the current CUDA stream.  Outputs are allocated with torch;
+nothing synchronises with the host.
+
+Reference bindings mirrored (src/jaxgs/...):
+  project_cute / project_with_compact_pullback   kernels/projector.py:103-395
+  compact_visible_clusters                        kernels/cluster_compact.py:31-44
+  build_sorted_visibility_table_cute              kernels/sorted_binning.py:9-117
+  rasterize_forward / rasterize_loss_and_grad     kernels/sorted_rasterizer.py:15-236
+  fused_loss_and_grad(_with_scale)                kernels/fused_loss.py:333-352
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import _lib as L
+from .scene import CapacityConfig
+from .types import (DeviceCamera, GaussianArrays, ProjectedGaussians, RasterCache, RenderResult,
+                    SortedVisibilityTable)
+
+_f32 = torch.float32
+_i32 = torch.int32
+
+
+def _ptr(t: torch.Tensor | None):
+    return None if t is None else t.data_ptr()
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _require_cuda(t: torch.Tensor, what: str) -> None:
+    if not t.is_cuda:
+        raise RuntimeError(f"{what} requires CUDA tensors (the sm_100a path has no CPU fallback)")
+
+
+def _workspace(nbytes: int, device) -> torch.Tensor:
+    return torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=device)
+
+
+def _c(t: torch.Tensor, dtype=None) -> torch.Tensor:
+    if dtype is not None and t.dtype != dtype:
+        t = t.to(dtype)
+    return t if t.is_contiguous() else t.contiguous()
+
+
+# ---------------------------------------------------------------------------
+# Cluster culling (render/pipeline.py:18-44)
+# ---------------------------------------------------------------------------
+def compact_visible_clusters(bounds, camera: DeviceCamera, config: CapacityConfig):
+    """frustum_cluster_mask + compact_visible_clusters.
+
+    bounds: (center [N,3], extent [N,3], valid [N] bool) device tensors.
+    Returns ((ids [N] int32, count [1] int32), visible_slots [C] bool).
+    """
+    center, extent, valid = bounds
+    _require_cuda(center, "compact_visible_clusters")
+    n = int(valid.shape[0])
+    ids = torch.empty(max(n, 1), dtype=_i32, device=center.device)
+    count = torch.empty(1, dtype=_i32, device=center.device)
+    slots = torch.empty(config.max_gaussians, dtype=torch.uint8, device=center.device)
+    p = L.ClusterParams(n, config.cluster_size, config.max_gaussians)
+    ws = _workspace(L.lib.gsb_cluster_compact_workspace_size(L.ref(p)), center.device)
+    L.check(L.lib.gsb_cluster_compact(_stream(), L.ref(p), _ptr(ws), ws.numel(),
+                                      _ptr(_c(center, _f32)), _ptr(_c(extent, _f32)),
+                                      _ptr(_c(valid, torch.uint8)), _ptr(_c(camera.planes, _f32)),
+                                      _ptr(ids), _ptr(count), _ptr(slots)),
+            "compact_visible_clusters")
+    return (ids[:n] if n else ids[:0], count), slots.bool()
+
+
+def render_preprocess(cluster_bounds, camera: DeviceCamera, gaussians: GaussianArrays,
+                      pp: CapacityConfig):
+    """render/pipeline.py:18-44: visible clusters, slot mask, culled pool view."""
+    clusters, slots = compact_visible_clusters(cluster_bounds, camera, pp)
+    return clusters, slots, gaussians.replace(alive=gaussians.alive & slots)
+
+
+# ---------------------------------------------------------------------------
+# Projection (kernels/projector.py)
+# ---------------------------------------------------------------------------
+def _project(pool: GaussianArrays, camera: DeviceCamera, config: CapacityConfig,
+             active_degree: int | None, clusters, clear_invisible: bool,
+             visible_color_only: bool) -> ProjectedGaussians:
+    _require_cuda(pool.xyz, "projection")
+    C = config.max_gaussians
+    if pool.capacity != C:
+        raise ValueError("pool capacity must equal config.max_gaussians")
+    degree = config.sh_degree if active_degree is None else active_degree
+    if not 0 <= degree <= config.sh_degree:
+        raise ValueError("active_degree must fit the pool's SH coefficients")
+    dev = pool.xyz.device
+    mean = torch.empty(C, 2, dtype=_f32, device=dev)
+    depth = torch.empty(C, dtype=_f32, device=dev)
+    conic = torch.empty(C, 2, 2, dtype=_f32, device=dev)
+    radius = torch.empty(C, dtype=_f32, device=dev)
+    color = torch.empty(C, 3, dtype=_f32, device=dev)
+    alpha = torch.empty(C, dtype=_f32, device=dev)
+    visible = torch.empty(C, dtype=torch.int8, device=dev)
+    ids, count = (None, None) if clusters is None else clusters
+    p = L.ProjectParams(C, int(pool.sh.shape[1]), degree, camera.width, camera.height, camera.near,
+                        camera.far, config.cluster_size, int(clusters is not None),
+                        int(clear_invisible), int(visible_color_only))
+    L.check(L.lib.gsb_project_fwd(
+        _stream(), L.ref(p), _ptr(_c(pool.xyz, _f32)), _ptr(_c(pool.log_scale, _f32)),
+        _ptr(_c(pool.rotation, _f32)), _ptr(_c(pool.opacity, _f32)), _ptr(_c(pool.sh, _f32)),
+        _ptr(_c(pool.alive, torch.uint8)), _ptr(_c(camera.world_to_camera, _f32)),
+        _ptr(_c(camera.intrinsics, _f32)), _ptr(_c(camera.center, _f32)),
+        _ptr(None if ids is None else _c(ids, _i32)), _ptr(None if count is None else _c(count, _i32)),
+        _ptr(mean), _ptr(depth), _ptr(conic), _ptr(radius), _ptr(color), _ptr(alpha),
+        _ptr(visible)), "projection")
+    return ProjectedGaussians(mean, depth, conic, radius, color, alpha, visible)
+
+
+def project_cute(pool: GaussianArrays, camera: DeviceCamera, config: CapacityConfig,
+                 active_degree: int | None = None, compacted_clusters=None,
+                 clear_invisible: bool = True) -> ProjectedGaussians:
+    """kernels/projector.py:103-127 (plus the compact options of :17-100)."""
+    return _project(pool, camera, config, active_degree, compacted_clusters, clear_invisible, False)
+
+
+project = project_cute
+
+
+def compute_projection_gradients(parameters, camera: DeviceCamera, projected_color,
+                                 cotangents: ProjectedGaussians, config: CapacityConfig,
+                                 active_degree: int | None, visible_clusters,
+                                 compact_gradients: bool, rgb_only: bool = False,
+                                 active_sh_only: bool = False, sh_color_only: bool = False):
+    """kernels/projector.py:240-307: parameter gradients from cotangents."""
+    xyz, log_scale, rotation, opacity, sh = parameters
+    _require_cuda(xyz, "projection pullback")
+    C = config.max_gaussians
+    degree = config.sh_degree if active_degree is None else active_degree
+    sh_dim = int(sh.shape[1])
+    shg = 1 if sh_color_only else ((degree + 1) ** 2 if active_sh_only else sh_dim)
+    dev = xyz.device
+    out = [torch.empty(C, 3, dtype=_f32, device=dev), torch.empty(C, 3, dtype=_f32, device=dev),
+           torch.empty(C, 4, dtype=_f32, device=dev), torch.empty(C, 1, dtype=_f32, device=dev),
+           torch.empty(C, shg, 3, dtype=_f32, device=dev)]
+    ids, count = (None, None) if visible_clusters is None else visible_clusters
+    p = L.ProjectBwdParams(C, sh_dim, shg, degree, camera.near, config.cluster_size,
+                           int(visible_clusters is not None), int(compact_gradients),
+                           int(rgb_only), int(sh_color_only))
+    zeros = None
+    gdepth, gradius = cotangents.depth, cotangents.radius
+    if rgb_only:
+        gdepth = gradius = None
+    L.check(L.lib.gsb_project_bwd(
+        _stream(), L.ref(p), _ptr(_c(xyz, _f32)), _ptr(_c(log_scale, _f32)),
+        _ptr(_c(rotation, _f32)), _ptr(_c(opacity, _f32)), _ptr(_c(sh, _f32)),
+        _ptr(_c(camera.world_to_camera, _f32)), _ptr(_c(camera.intrinsics, _f32)),
+        _ptr(_c(camera.center, _f32)), _ptr(_c(projected_color, _f32)),
+        _ptr(None if ids is None else _c(ids, _i32)), _ptr(None if count is None else _c(count, _i32)),
+        _ptr(_c(cotangents.mean, _f32)), _ptr(None if gdepth is None else _c(gdepth, _f32)),
+        _ptr(_c(cotangents.conic, _f32)), _ptr(None if gradius is None else _c(gradius, _f32)),
+        _ptr(_c(cotangents.color, _f32)), _ptr(_c(cotangents.alpha, _f32)),
+        *[_ptr(o) for o in out]), "projection pullback")
+    del zeros
+    return tuple(out)
+
+
+def project_with_compact_pullback(pool: GaussianArrays, camera: DeviceCamera,
+                                  config: CapacityConfig, active_degree: int, clusters, *,
+                                  rgb_only: bool = False, active_sh_only: bool = False,
+                                  sh_color_only: bool = False, visible_color_only: bool = False):
+    """kernels/projector.py:310-395: projection and a pullback producing
+    gradients in visible-cluster order (only clusters[0][:count] rows valid)."""
+    if not 0 <= active_degree <= config.sh_degree:
+        raise ValueError("active_degree must fit the pool's SH coefficients")
+    parameters = (pool.xyz, pool.log_scale, pool.rotation, pool.opacity, pool.sh)
+    projected = _project(pool, camera, config, active_degree, clusters, False, visible_color_only)
+
+    def pullback(cotangents: ProjectedGaussians):
+        return compute_projection_gradients(parameters, camera, projected.color, cotangents,
+                                            config, active_degree, clusters, True, rgb_only,
+                                            active_sh_only, sh_color_only)
+
+    return projected, pullback
+
+
+# ---------------------------------------------------------------------------
+# Binning (kernels/sorted_binning.py:9-117)
+# ---------------------------------------------------------------------------
+def build_sorted_visibility_table_cute(projected: ProjectedGaussians, camera: DeviceCamera,
+                                       config: CapacityConfig) -> SortedVisibilityTable:
+    """LiteGS count / depth sort / scan / emit / tile sort / ranges."""
+    _require_cuda(projected.mean, "binning")
+    C = config.max_gaussians
+    dev = projected.mean.device
+    tw, th = config.tile_size, config.raster_tile_height
+    tiles = (-(-camera.width // tw)) * (-(-camera.height // th))
+    max_pairs = config.visibility_capacity
+    counts = torch.empty(C, dtype=_i32, device=dev)
+    ids = torch.empty(max_pairs, dtype=_i32, device=dev)
+    offsets = torch.empty(tiles + 1, dtype=_i32, device=dev)
+    pair_count = torch.empty(1, dtype=_i32, device=dev)
+    overflow = torch.empty(1, dtype=_i32, device=dev)
+    p = L.BinParams(C, camera.width, camera.height, tw, th, max_pairs)
+    ws = _workspace(L.lib.gsb_bin_workspace_size(L.ref(p)), dev)
+    L.check(L.lib.gsb_bin(_stream(), L.ref(p), _ptr(ws), ws.numel(),
+                          _ptr(_c(projected.mean, _f32)), _ptr(_c(projected.conic, _f32)),
+                          _ptr(_c(projected.alpha, _f32)), _ptr(_c(projected.depth, _f32)),
+                          _ptr(_c(projected.visible, torch.int8)), _ptr(counts), _ptr(ids),
+                          _ptr(offsets), _ptr(pair_count), _ptr(overflow)), "binning")
+    return SortedVisibilityTable(ids, offsets, counts, pair_count, overflow)
+
+
+build_sorted_visibility_table = build_sorted_visibility_table_cute
+
+
+# ---------------------------------------------------------------------------
+# fp32 rasterization (kernels/sorted_rasterizer.py)
+# ---------------------------------------------------------------------------
+def _tiles(camera: DeviceCamera, config: CapacityConfig) -> int:
+    return (-(-camera.width // config.tile_size)) * (-(-camera.height // config.raster_tile_height))
+
+
+def rasterize_forward(projected: ProjectedGaussians, table: SortedVisibilityTable,
+                      camera: DeviceCamera, config: CapacityConfig, background=None,
+                      want_depth: bool = True, want_alpha: bool = True):
+    """sorted_rasterizer.py:15-70: returns (RenderResult, RasterCache).
+
+    The table may reference only visible Gaussians (others are not staged).
+    """
+    _require_cuda(projected.mean, "rasterization")
+    C = config.max_gaussians
+    dev = projected.mean.device
+    W, H = camera.width, camera.height
+    if background is None:
+        background = torch.zeros(3, dtype=_f32, device=dev)
+    rgb = torch.empty(H, W, 3, dtype=_f32, device=dev)
+    out_depth = torch.empty(H, W, dtype=_f32, device=dev) if want_depth else None
+    out_alpha = torch.empty(H, W, dtype=_f32, device=dev) if want_alpha else None
+    final_t = torch.empty(H * W, dtype=_f32, device=dev)
+    last = torch.empty(H * W, dtype=_i32, device=dev)
+    work = torch.empty(_tiles(camera, config), dtype=_i32, device=dev)
+    splats = torch.empty(C, 12, dtype=_f32, device=dev)
+    p = L.RasterParams(C, W, H, config.tile_size, config.raster_tile_height)
+    ws = _workspace(L.lib.gsb_raster_workspace_size(L.ref(p)), dev)
+    L.check(L.lib.gsb_raster_fwd(
+        _stream(), L.ref(p), _ptr(ws), ws.numel(), _ptr(_c(projected.mean, _f32)),
+        _ptr(_c(projected.conic, _f32)), _ptr(_c(projected.depth, _f32)),
+        _ptr(_c(projected.color, _f32)), _ptr(_c(projected.alpha, _f32)),
+        _ptr(_c(projected.visible, torch.int8)), _ptr(table.gaussian_ids),
+        _ptr(table.tile_offsets), _ptr(_c(background, _f32)), _ptr(rgb), _ptr(out_depth),
+        _ptr(out_alpha), _ptr(final_t), _ptr(last), _ptr(work), _ptr(splats)),
+        "rasterization forward")
+    return RenderResult(rgb, out_depth, out_alpha), RasterCache(splats, final_t, last, work)
+
+
+def rasterize_backward(projected: ProjectedGaussians, table: SortedVisibilityTable,
+                       cache: RasterCache, drgb: torch.Tensor, camera: DeviceCamera,
+                       config: CapacityConfig, background=None, ddepth=None, dalpha=None,
+                       visible_clusters=None) -> ProjectedGaussians:
+    """sorted_rasterize.py:91-236: projected-field cotangents (mean, conic,
+    depth, color, alpha).  With visible_clusters only those clusters' rows
+    are zeroed and defined, and depth cotangents are left undefined."""
+    _require_cuda(drgb, "rasterization backward")
+    C = config.max_gaussians
+    dev = drgb.device
+    if background is None:
+        background = torch.zeros(3, dtype=_f32, device=dev)
+    gmean = torch.empty(C, 2, dtype=_f32, device=dev)
+    gconic = torch.empty(C, 2, 2, dtype=_f32, device=dev)
+    gdepth = torch.empty(C, dtype=_f32, device=dev)
+    gcolor = torch.empty(C, 3, dtype=_f32, device=dev)
+    galpha = torch.empty(C, dtype=_f32, device=dev)
+    ids, count = (None, None) if visible_clusters is None else visible_clusters
+    if ddepth is not None and visible_clusters is not None:
+        raise ValueError("depth cotangents are not defined with visible_clusters")
+    p = L.RasterBwdParams(C, camera.width, camera.height, config.tile_size,
+                          config.raster_tile_height, config.cluster_size)
+    rp = L.RasterParams(C, camera.width, camera.height, config.tile_size, config.raster_tile_height)
+    ws = _workspace(L.lib.gsb_raster_workspace_size(L.ref(rp)), dev)
+    L.check(L.lib.gsb_raster_bwd(
+        _stream(), L.ref(p), _ptr(ws), ws.numel(), _ptr(cache.splats),
+        _ptr(_c(projected.depth, _f32)), _ptr(table.gaussian_ids), _ptr(table.tile_offsets),
+        _ptr(_c(background, _f32)), _ptr(cache.final_t), _ptr(cache.last),
+        _ptr(cache.backward_work), _ptr(_c(drgb, _f32)),
+        _ptr(None if ddepth is None else _c(ddepth, _f32)),
+        _ptr(None if dalpha is None else _c(dalpha, _f32)),
+        _ptr(None if ids is None else _c(ids, _i32)), _ptr(None if count is None else _c(count, _i32)),
+        _ptr(gmean), _ptr(gconic), _ptr(gdepth), _ptr(gcolor), _ptr(galpha)),
+        "rasterization backward")
+    if ddepth is None and visible_clusters is None:
+        pass  # gdepth zeroed by the whole-pool clear
+    return projected.replace(mean=gmean, conic=gconic, depth=gdepth, color=gcolor, alpha=galpha,
+                             radius=torch.zeros_like(projected.radius))
+
+
+# ---------------------------------------------------------------------------
+# Fused loss (kernels/fused_loss.py:333-352)
+# ---------------------------------------------------------------------------
+def _fused_loss(prediction: torch.Tensor, target: torch.Tensor, with_scale: bool,
+                clip_input: bool = False):
+    _require_cuda(prediction, "fused loss")
+    if prediction.ndim != 3 or prediction.shape[2] != 3 or tuple(target.shape) != tuple(prediction.shape):
+        raise ValueError("L1+SSIM expects matching HWC RGB images")
+    H, W, _ = prediction.shape
+    dev = prediction.device
+    u8 = target.dtype == torch.uint8
+    grad = torch.empty(H, W, 3, dtype=_f32, device=dev)
+    loss = torch.empty(1, dtype=_f32, device=dev)
+    scale = torch.empty(1, dtype=_f32, device=dev) if with_scale else None
+    p = L.LossParams(W, H, int(u8), int(clip_input))
+    ws = _workspace(L.lib.gsb_loss_workspace_size(L.ref(p)), dev)
+    L.check(L.lib.gsb_loss(_stream(), L.ref(p), _ptr(ws), ws.numel(),
+                           _ptr(_c(prediction, _f32)), _ptr(_c(target, None if u8 else _f32)),
+                           _ptr(loss), _ptr(grad), _ptr(scale)), "fused loss")
+    return loss[0], grad, scale
+
+
+def fused_loss_and_grad(prediction: torch.Tensor, target: torch.Tensor):
+    """Mean L1(0.8)+SSIM(0.2) and its image gradient; uint8 or float target."""
+    loss, grad, _ = _fused_loss(prediction, target, False)
+    return loss, grad
+
+
+def fused_loss_and_grad_with_scale(prediction: torch.Tensor, target: torch.Tensor):
+    """Also the floored max |grad| (the packed rasterizer's gradient scale)."""
+    return _fused_loss(prediction, target, True)
+
+
+def rasterize_loss_and_grad(projected: ProjectedGaussians, table: SortedVisibilityTable,
+                            camera: DeviceCamera, config: CapacityConfig, target: torch.Tensor,
+                            collect_stats: bool = False, visible_clusters=None):
+    """kernels/sorted_rasterizer.py:165-236: fp32 forward, loss on
+    clip(rgb, 0, 1) with the clip's VJP, fp32 backward.  Returns
+    (loss, cotangents, stats); stats collection is not implemented."""
+    if collect_stats:
+        raise ValueError("fragment statistics are not implemented in this backend")
+    result, cache = rasterize_forward(projected, table, camera, config, want_depth=False,
+                                      want_alpha=False)
+    loss, drgb, _ = _fused_loss(result.rgb, target, False, clip_input=True)
+    cot = rasterize_backward(projected, table, cache, drgb, camera, config,
+                             visible_clusters=visible_clusters)
+    return loss, cot, None

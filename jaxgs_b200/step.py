@@ -1,0 +1,94 @@
+"""The north-star training step: cluster cull -> compact projection -> binning
+-> fp32 raster forward -> fused L1+SSIM (on clip(rgb,0,1)) -> raster backward
+-> projection pullback, on one CUDA stream with no host synchronisation.
+
+Mirrors training/step.py:32-132 (compute_training_step) up to, not including,
+the optimizer: the result is the loss, the parameter gradients in compact
+visible-cluster order and the binning metrics.  The reference dispatches
+8x16 tiles to its half2 rasterizer (step.py:74-80); this backend uses the
+fp32 compositing of kernels/sorted_rasterizer.py:165-236 for every tile
+shape, which is the path whose images and gradients meet the 1e-4 / 1e-3
+parity bars.
+
+Multi-GPU (view sharding): ``ViewShardedStep`` renders each rank's views,
+scatters the compact gradients into pool order and sums them across ranks
+with one NCCL all-reduce per step (torch.distributed).
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from . import kernels as K
+from .scene import CapacityConfig
+from .types import DeviceCamera, GaussianArrays, ProjectedGaussians
+
+
+@dataclass
+class StepOutput:
+    loss: torch.Tensor            # [] float32 (device)
+    gradients: tuple              # (xyz, log_scale, rotation, opacity, sh) compact order
+    visible_clusters: tuple       # (ids, count)
+    pair_count: torch.Tensor      # [1] int32
+    overflow: torch.Tensor        # [1] int32
+    image: torch.Tensor | None = None
+
+
+def compute_training_step(pool: GaussianArrays, bounds, camera: DeviceCamera, target: torch.Tensor,
+                          config: CapacityConfig, active_degree: int, *,
+                          active_sh_only: bool = True, sh_color_only: bool = False,
+                          keep_image: bool = False) -> StepOutput:
+    """training/step.py:32-89 without the optimizer update.
+
+    bounds: world cluster bounds (center, extent, valid) on the device.
+    target: uint8 [H, W, 3] (normalised in the loss kernel) or float [0, 1].
+    The culled pool's alive mask (render/pipeline.py:44, alive & slots) equals
+    the pool's alive mask on every listed cluster, which is all the compact
+    projection reads, so it is not materialised.
+    """
+    clusters, _slots = K.compact_visible_clusters(bounds, camera, config)
+    projected, pullback = K.project_with_compact_pullback(
+        pool, camera, config, active_degree, clusters, rgb_only=True,
+        active_sh_only=active_sh_only, sh_color_only=sh_color_only, visible_color_only=True)
+    table = K.build_sorted_visibility_table_cute(projected, camera, config)
+    result, cache = K.rasterize_forward(projected, table, camera, config, want_depth=False,
+                                        want_alpha=False)
+    loss, drgb, _ = K._fused_loss(result.rgb, target, False, clip_input=True)
+    cot = K.rasterize_backward(projected, table, cache, drgb, camera, config,
+                               visible_clusters=clusters)
+    grads = pullback(cot)
+    return StepOutput(loss, grads, clusters, table.pair_count, table.overflow,
+                      result.rgb if keep_image else None)
+
+
+def render(camera: DeviceCamera, gaussians: GaussianArrays, visible_clusters, active_degree: int,
+           pp: CapacityConfig):
+    """render/pipeline.py:47-93 (fp32 compositing): (image clipped to [0,1],
+    primitive_visible, overflow)."""
+    projected = K.project_cute(gaussians, camera, pp, active_degree, visible_clusters)
+    table = K.build_sorted_visibility_table_cute(projected, camera, pp)
+    result, _ = K.rasterize_forward(projected, table, camera, pp, want_depth=False,
+                                    want_alpha=False)
+    return result.rgb.clamp(0, 1), table.point_counts > 0, table.overflow
+
+
+def scatter_compact(grads, clusters, config: CapacityConfig, out=None):
+    """Compact visible-cluster rows -> pool order (rows of unlisted clusters 0).
+
+    Used by the view-sharded step to make per-view gradients summable.
+    """
+    ids, count = clusters
+    n = int(count.item()) if count.numel() else 0
+    cs = config.cluster_size
+    slots = (ids[:n, None].long() * cs + torch.arange(cs, device=ids.device)).reshape(-1)
+    keep = slots < config.max_gaussians
+    rows = torch.arange(n * cs, device=ids.device)[keep]
+    slots = slots[keep]
+    outs = []
+    for i, g in enumerate(grads):
+        dst = torch.zeros_like(g) if out is None else out[i]
+        dst.index_add_(0, slots, g[rows])
+        outs.append(dst)
+    return outs

@@ -1,0 +1,115 @@
+"""Fixed-shape device data shared by the stages (torch tensors on CUDA).
+
+Mirrors render/types.py:7-63 and scene/types.py:6-31 of the reference:
+field names, shapes and dtypes are the reference's, so values convert
+one-to-one to the JAX pytrees.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass, fields, replace
+
+import numpy as np
+import torch
+
+from .scene import Camera
+
+PARAMETER_NAMES = ("xyz", "log_scale", "rotation", "opacity", "sh")
+
+
+@dataclass
+class GaussianArrays:
+    """scene/point.py:12-23 (free_mask / n_active are not read by the hot path)."""
+
+    xyz: torch.Tensor        # [C, 3]
+    log_scale: torch.Tensor  # [C, 3]
+    rotation: torch.Tensor   # [C, 4] wxyz
+    opacity: torch.Tensor    # [C, 1] logits
+    sh: torch.Tensor         # [C, SH_DIM, 3]
+    alive: torch.Tensor      # [C] bool
+
+    @classmethod
+    def from_numpy(cls, pool: dict, device="cuda") -> "GaussianArrays":
+        return cls(*(torch.as_tensor(np.ascontiguousarray(pool[k]), device=device)
+                     for k in ("xyz", "log_scale", "rotation", "opacity", "sh", "alive")))
+
+    @property
+    def capacity(self) -> int:
+        return int(self.xyz.shape[0])
+
+    def replace(self, **kwargs) -> "GaussianArrays":
+        return replace(self, **kwargs)
+
+
+@dataclass
+class DeviceCamera:
+    """scene/camera.py:6-65 with the traced arrays on the device."""
+
+    world_to_camera: torch.Tensor  # [4, 4] float32
+    intrinsics: torch.Tensor       # [4] fx, fy, cx, cy
+    center: torch.Tensor           # [3]
+    planes: torch.Tensor           # [6, 4] frustum planes of scene/cluster.py:40-63
+    width: int
+    height: int
+    near: float = 0.2
+    far: float = 1000.0
+
+    @classmethod
+    def from_camera(cls, camera: Camera, device="cuda") -> "DeviceCamera":
+        def t(a):
+            return torch.as_tensor(np.ascontiguousarray(a, np.float32), device=device)
+
+        return cls(t(camera.world_to_camera), t(camera.intrinsics), t(camera.center),
+                   t(camera.frustum_planes()), camera.width, camera.height, camera.near,
+                   camera.far)
+
+
+@dataclass
+class ProjectedGaussians:
+    """render/types.py:7-16."""
+
+    mean: torch.Tensor     # [C, 2]
+    depth: torch.Tensor    # [C]
+    conic: torch.Tensor    # [C, 2, 2]
+    radius: torch.Tensor   # [C]
+    color: torch.Tensor    # [C, 3]
+    alpha: torch.Tensor    # [C]
+    visible: torch.Tensor  # [C] int8 (0/1)
+
+    def replace(self, **kwargs) -> "ProjectedGaussians":
+        return replace(self, **kwargs)
+
+
+@dataclass
+class SortedVisibilityTable:
+    """render/types.py:29-37.  gaussian_ids' valid prefix ends at pair_count."""
+
+    gaussian_ids: torch.Tensor  # [P_MAX] int32
+    tile_offsets: torch.Tensor  # [T + 1] int32
+    point_counts: torch.Tensor  # [C] int32
+    pair_count: torch.Tensor    # [1] int32
+    overflow: torch.Tensor      # [1] int32 (bool)
+
+
+@dataclass
+class RenderResult:
+    """render/types.py:40-45."""
+
+    rgb: torch.Tensor    # [H, W, 3]
+    depth: torch.Tensor  # [H, W]
+    alpha: torch.Tensor  # [H, W]
+
+
+@dataclass
+class RasterCache:
+    """State the forward hands to the backward (splat records, per-pixel final
+    transmittance and last pair, per-tile backward work)."""
+
+    splats: torch.Tensor         # [C, 12] float32
+    final_t: torch.Tensor        # [H * W]
+    last: torch.Tensor           # [H * W] int32
+    backward_work: torch.Tensor  # [T] int32
+
+
+def tree_fields(obj):
+    return {f.name: getattr(obj, f.name) for f in fields(obj)}
