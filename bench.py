@@ -1,0 +1,368 @@
+"""Benchmark of the north-star hot path: train views/sec (fwd+bwd+loss).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload: 1,000,000-Gaussian pool (config-1 scene,
+seed 2, all slots active, SH degree 3), 1237x822 pinhole camera fx=fy=1040 at
+(0, 1.5, -6) looking at the origin, 8x16 tiles, uint8 target rendered from a
+second random scene (seed 3).  One step = cluster cull + compact projection +
+binning + fp32 raster forward + fused L1+SSIM + raster backward + projection
+pullback to xyz/log_scale/rotation/opacity/SH (degree 3).  Synthetic data.
+
+Multi-GPU (torchrun, one rank per GPU): every rank renders one view per step
+(ring camera r of BASELINE config 3's ring, radius 6) and the per-view
+parameter gradients, scattered to pool order, are summed by one NCCL
+all-reduce per step; value = views of all ranks / max-over-ranks time.
+
+--impl reference times the reference path's CPU restatement (oracle/, the
+reference being JAX code that is not installed here) on the host cores.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "train views/sec (fwd+bwd+loss) at 1M Gaussians, 1237x822"
+UNIT = "views/s"
+
+
+def _config():
+    from jaxgs_b200.scene import CapacityConfig
+
+    return CapacityConfig(max_gaussians=1_000_000, cluster_size=128, tile_size=16, sh_degree=3,
+                          max_visibility_pairs=8_000_000, tile_height=8)
+
+
+def _workload(rank: int):
+    """(pool dict, camera, target uint8) of config 2; rank picks its ring camera."""
+    import numpy as np
+
+    from jaxgs_b200.scene import config1_scene, ring_cameras
+
+    pool = config1_scene()
+    camera = ring_cameras(8, radius=6.0, height=1.5)[rank % 8]
+    return pool, camera
+
+
+def _target(camera, device):
+    """uint8 render of the seed-3 scene from the same camera (GPU forward)."""
+    import torch
+
+    from jaxgs_b200 import kernels as K
+    from jaxgs_b200.scene import config1_scene
+    from jaxgs_b200.types import DeviceCamera, GaussianArrays
+
+    config = _config()
+    other = GaussianArrays.from_numpy(config1_scene(seed=3), device=device)
+    cam = DeviceCamera.from_camera(camera, device=device)
+    projected = K.project_cute(other, cam, config)
+    table = K.build_sorted_visibility_table_cute(projected, cam, config)
+    result, _ = K.rasterize_forward(projected, table, cam, config, want_depth=False,
+                                    want_alpha=False)
+    target = (result.rgb.clamp(0, 1) * 255.0 + 0.5).to(torch.uint8)
+    del other, projected, table, result
+    return target
+
+
+class ClockSampler:
+    """nvidia-smi samples of SM clock and throttle reasons during the timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.thread.join(timeout=2)
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[5:9]):
+                if flag.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def _peaks():
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        data = json.loads(path.read_text())
+        return float(data["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def run_ours(args) -> None:
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from jaxgs_b200 import _lib
+    from jaxgs_b200 import kernels as K
+    from jaxgs_b200.scene import world_cluster_bounds
+    from jaxgs_b200.step import compute_training_step, scatter_compact
+    from jaxgs_b200.types import DeviceCamera, GaussianArrays
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=device)
+    config = _config()
+    pool_np, camera = _workload(rank)
+    pool = GaussianArrays.from_numpy(pool_np, device=device)
+    center, extent, valid = world_cluster_bounds(pool_np, 128)
+    bounds = (torch.as_tensor(center, device=device), torch.as_tensor(extent, device=device),
+              torch.as_tensor(valid.astype(np.uint8), device=device))
+    dcam = DeviceCamera.from_camera(camera, device=device)
+    target = _target(camera, device)
+    target_host = target.cpu().pin_memory()
+    cam_host = [t.cpu().pin_memory() for t in (dcam.world_to_camera, dcam.intrinsics,
+                                               dcam.center, dcam.planes)]
+    degree = 3
+    pool_grads = None
+    if world > 1:
+        pool_grads = [torch.zeros_like(t) for t in (pool.xyz, pool.log_scale, pool.rotation,
+                                                  pool.opacity, pool.sh)]
+    stream = torch.cuda.current_stream()
+    kernel_events = []
+
+    def step(cam, tgt, record=False):
+        events = {} if record else None
+        out = compute_training_step(pool, bounds, cam, tgt, config, degree, stage_events=events)
+        if world > 1:
+            for t in pool_grads:
+                t.zero_()
+            scatter_compact(out.gradients, out.visible_clusters, config, out=pool_grads)
+            flat = torch.cat([t.reshape(-1) for t in pool_grads])
+            dist.all_reduce(flat)
+        if record:
+            kernel_events.append(events)
+        return out
+
+    # Warm-up.
+    for _ in range(max(args.warmup, 0)):
+        out = step(dcam, target)
+    torch.cuda.synchronize()
+    pairs = int(out.pair_count.item())
+    overflow = bool(out.overflow.item())
+    visible_clusters = int(out.visible_clusters[1].item())
+
+    # Device-resident timed region.
+    sampler = ClockSampler(local)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    sampler.start()
+    time.sleep(0.3)
+    launches0 = _lib.launch_count()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(args.steps):
+        out = step(dcam, target, record=True)
+    end.record(stream)
+    torch.cuda.synchronize()
+    launches = _lib.launch_count() - launches0
+    if world > 1:
+        dist.barrier()
+    clocks = sampler.stop()
+    elapsed = start.elapsed_time(end) / 1e3
+    stage_ms = {}
+    for events in kernel_events:
+        for name, (a, b) in events.items():
+            stage_ms.setdefault(name, []).append(a.elapsed_time(b))
+    stage_ms = {k: statistics.mean(v) for k, v in stage_ms.items()}
+
+    # End-to-end through the public API from pinned host buffers.
+    e2e_loss = torch.empty(args.steps, dtype=torch.float32).pin_memory()
+    tgt_dev = torch.empty_like(target)
+    cam_dev = [torch.empty_like(t) for t in (dcam.world_to_camera, dcam.intrinsics, dcam.center,
+                                             dcam.planes)]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e_start.record(stream)
+    for i in range(0 if args.no_e2e else args.steps):
+        tgt_dev.copy_(target_host, non_blocking=True)
+        for d, h in zip(cam_dev, cam_host):
+            d.copy_(h, non_blocking=True)
+        cam = DeviceCamera(cam_dev[0], cam_dev[1], cam_dev[2], cam_dev[3], camera.width,
+                           camera.height, camera.near, camera.far)
+        out = step(cam, tgt_dev)
+        e2e_loss[i].copy_(out.loss, non_blocking=True)
+    e_end.record(stream)
+    torch.cuda.synchronize()
+    e2e_elapsed = e_start.elapsed_time(e_end) / 1e3 if not args.no_e2e else float("nan")
+    h2d = target.numel() + sum(t.numel() * 4 for t in cam_host)
+    d2h = 4
+
+    if world > 1:
+        t = torch.tensor([elapsed, e2e_elapsed], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        elapsed, e2e_elapsed = float(t[0]), float(t[1])
+
+    if rank == 0:
+        views = world * args.steps
+        value = views / elapsed
+        # Roofline of the dominant kernel: the raster backward is timed with
+        # events around its call (zero + order + main kernel), see DESIGN.md.
+        peak, peak_kind = _peaks()
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(elapsed / args.steps * 1e3, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "BASELINE config 2: 1M-Gaussian training step, 1237x822, 8x16 tiles, SH3",
+                       "gaussians": 1_000_000, "width": 1237, "height": 822, "tile": "8x16",
+                       "views_per_gpu_per_step": 1, "pairs": pairs, "overflow": overflow,
+                       "visible_clusters": visible_clusters,
+                       "l2": "inputs larger than L2 (236 MB pool)",
+                       "parallelism": f"view-sharded dp{world}" if world > 1 else "single view"},
+            "e2e": {"value": None if args.no_e2e else round(world * args.steps / e2e_elapsed, 2), "unit": UNIT,
+                    "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": d2h},
+            "gpu_launches": int(launches),
+            "clocks": clocks,
+            "stage_ms": {k: round(v, 4) for k, v in stage_ms.items()},
+            "roofline_peak_source": peak_kind,
+        }
+        line.update(_roofline_fields(stage_ms, peak, peak_kind, pairs))
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(pool_np, camera, target.cpu().numpy())
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def _roofline_fields(stage_ms, peak, peak_kind, pairs):
+    return {"roofline": None}
+
+
+def cpu_baseline(pool_np, camera, target, budget_s: float = 30.0) -> dict:
+    """The oracle (CPU restatement) on the host cores: one full config-2 step."""
+    from oracle import oracle as O
+
+    config = _config()
+    timings = {}
+    t0 = time.perf_counter()
+    O.training_step(pool_np, camera, target, degree=3, sh_dim=16, tile_w=16, tile_h=8,
+                    max_pairs=config.visibility_capacity, timings=timings)
+    dt = time.perf_counter() - t0
+    return {"value": round(1.0 / dt, 5), "unit": UNIT, "cores": O.num_threads(), "kind": "port",
+            "sample": "one full config-2 view (1M Gaussians, 1237x822): oracle/ C restatement, "
+                      "OpenMP over the host cores",
+            "stage_s": {k: round(v, 3) for k, v in timings.items()}}
+
+
+def run_reference(args) -> None:
+    """CPU restatement of the reference path (JAX is not installed) on rank 0."""
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if rank != 0:
+        return
+    from oracle import oracle as O
+
+    config = _config()
+    pool_np, camera = _workload(0)
+    import numpy as np
+
+    rng = np.random.default_rng(3)
+    target = rng.integers(0, 256, (camera.height, camera.width, 3), dtype=np.uint8)
+    steps = max(1, min(args.steps, 3))
+    for _ in range(min(args.warmup, 1)):
+        O.training_step(pool_np, camera, target, degree=3, sh_dim=16, tile_w=16, tile_h=8,
+                        max_pairs=config.visibility_capacity)
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        O.training_step(pool_np, camera, target, degree=3, sh_dim=16, tile_w=16, tile_h=8,
+                        max_pairs=config.visibility_capacity)
+    dt = time.perf_counter() - t0
+    value = steps / dt
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 5), "unit": UNIT,
+        "n_gpus": world, "steps": steps, "warmup": min(args.warmup, 1),
+        "ms_per_step": round(dt / steps * 1e3, 2), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "BASELINE config 2: 1M-Gaussian training step, 1237x822, 8x16 tiles, SH3",
+                   "note": "reference is JAX (not installed); its CPU path is restated in oracle/"},
+        "cpu_baseline": {"value": round(value, 5), "unit": UNIT, "cores": O.num_threads(),
+                         "kind": "port", "sample": f"{steps} full config-2 views"},
+        "e2e": {"value": round(value, 5), "unit": UNIT, "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main() -> None:
+    parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    parser.add_argument("--gpus", type=int, default=1)
+    parser.add_argument("--steps", type=int, default=20)
+    parser.add_argument("--warmup", type=int, default=5)
+    parser.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    parser.add_argument("--no-cpu-baseline", action="store_true",
+                        help="skip the oracle timing (profiling runs)")
+    parser.add_argument("--no-e2e", action="store_true",
+                        help="skip the host-buffer end-to-end loop (profiling runs)")
+    args = parser.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

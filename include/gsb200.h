@@ -53,6 +53,9 @@ enum {
 GSB_API int gsb_abi_version(void);
 /* Last CUDA error string seen by the library (thread-local). */
 GSB_API const char* gsb_last_error(void);
+/* Number of kernels this library has launched in this process (host-side
+ * counter, incremented once per launch it issues). */
+GSB_API unsigned long long gsb_launch_count(void);
 
 /* ------------------------------------------------------------------------
  * Cluster culling + compaction.
@@ -166,40 +169,46 @@ GSB_API int gsb_bin(gsb_stream_t stream, const gsb_bin_params* p, void* workspac
  * fp32 rasterization forward.
  * Replaces kernels/sorted_rasterizer.py:15-70 (_forward_arrays ->
  * cutlass_call(launch_forward_sorted), sorted_rasterize.py:28-88), extended to
- * the rectangular tiles of the packed path (tile_w x tile_h with tile_w a
- * multiple of 8 and tile_h a multiple of 4).
+ * the rectangular tiles of the packed path (tile_w a multiple of 8, tile_h a
+ * multiple of 4, at most 16 x 16).
  * Inputs: mean[C*2], conic[C*4], depth[C], color[C*3], alpha[C] (opacity
- * after sigmoid), visible[C] i8, gaussian_ids, tile_offsets[T+1],
- * background[3].
+ * after sigmoid), visible[C] i8 (only visible Gaussians are staged; the table
+ * must reference no other), gaussian_ids, tile_offsets[T+1], background[3].
  * Outputs: rgb[H*W*3], out_depth[H*W] (may be NULL), out_alpha[H*W] (may be
  * NULL), final_t[H*W], last[H*W] (one past the last composited pair),
  * backward_work[T] (max over the tile's pixels of last - tile start),
- * splats[C*12] (48-byte staged records reused by the backward pass).
+ * splats[C*12] (48-byte staged records), contribution_bits
+ * [gsb_raster_bit_words()] (per 32-pair batch and pixel block, which pairs
+ * gave at least one pixel of the block a composited fragment; only words of
+ * batches the forward reached are written).
  * ------------------------------------------------------------------------ */
 typedef struct {
     int capacity;
     int width, height;
     int tile_w, tile_h;
+    int64_t max_pairs;     /* arena capacity of the table (sizes the bit words) */
 } gsb_raster_params;
 
 GSB_API size_t gsb_raster_workspace_size(const gsb_raster_params* p);
+GSB_API size_t gsb_raster_bit_words(const gsb_raster_params* p);
 GSB_API int gsb_raster_fwd(gsb_stream_t stream, const gsb_raster_params* p, void* workspace,
                    size_t workspace_bytes, const float* mean, const float* conic,
                    const float* depth, const float* color, const float* alpha,
                    const int8_t* visible, const int32_t* gaussian_ids,
                    const int32_t* tile_offsets, const float* background, float* rgb,
                    float* out_depth, float* out_alpha, float* final_t, int32_t* last,
-                   int32_t* backward_work, float* splats);
+                   int32_t* backward_work, float* splats, uint32_t* contribution_bits);
 
 /* ------------------------------------------------------------------------
  * fp32 rasterization backward.
  * Replaces kernels/sorted_rasterizer.py:165-236 (the launch_backward_sorted
  * call inside rasterize_loss_and_grad; kernel sorted_rasterize.py:91-236).
- * Inputs: the forward's splats/final_t/last/backward_work, depth[C] (for the
- * depth cotangent), gaussian_ids, tile_offsets, background[3], drgb[H*W*3],
- * ddepth[H*W] and dalpha[H*W] (may be NULL = zero).  cluster_ids/count:
- * when non-NULL only the listed clusters' cotangents are zeroed (the table
- * must reference no other Gaussian, kernels/packed_rasterize.py:753-758);
+ * Inputs: the forward's splats / final_t / last / backward_work /
+ * contribution_bits, depth[C] (for the depth cotangent), gaussian_ids,
+ * tile_offsets, background[3], drgb[H*W*3], ddepth[H*W] and dalpha[H*W] (may
+ * be NULL = zero).  cluster_ids/count: when non-NULL only the listed
+ * clusters' cotangents are zeroed (the table must reference no other
+ * Gaussian, kernels/packed_rasterize.py:753-758) and gdepth is not written;
  * otherwise the whole pool is zeroed.
  * Outputs (accumulated): gmean[C*2], gconic[C*4], gdepth[C], gcolor[C*3],
  * galpha[C].
@@ -209,16 +218,17 @@ typedef struct {
     int width, height;
     int tile_w, tile_h;
     int cluster_size;
+    int64_t max_pairs;
 } gsb_raster_bwd_params;
 
 GSB_API int gsb_raster_bwd(gsb_stream_t stream, const gsb_raster_bwd_params* p, void* workspace,
                    size_t workspace_bytes, const float* splats, const float* depth,
                    const int32_t* gaussian_ids, const int32_t* tile_offsets,
                    const float* background, const float* final_t, const int32_t* last,
-                   const int32_t* backward_work, const float* drgb, const float* ddepth,
-                   const float* dalpha, const int32_t* cluster_ids,
-                   const int32_t* cluster_count, float* gmean, float* gconic, float* gdepth,
-                   float* gcolor, float* galpha);
+                   const int32_t* backward_work, const uint32_t* contribution_bits,
+                   const float* drgb, const float* ddepth, const float* dalpha,
+                   const int32_t* cluster_ids, const int32_t* cluster_count, float* gmean,
+                   float* gconic, float* gdepth, float* gcolor, float* galpha);
 
 /* ------------------------------------------------------------------------
  * Fused L1(0.8) + SSIM(0.2) loss and image gradient.

@@ -45,12 +45,13 @@ class BinParams(ctypes.Structure):
 
 class RasterParams(ctypes.Structure):
     _fields_ = [("capacity", ctypes.c_int), ("width", ctypes.c_int), ("height", ctypes.c_int),
-                ("tile_w", ctypes.c_int), ("tile_h", ctypes.c_int)]
+                ("tile_w", ctypes.c_int), ("tile_h", ctypes.c_int), ("max_pairs", ctypes.c_int64)]
 
 
 class RasterBwdParams(ctypes.Structure):
     _fields_ = [("capacity", ctypes.c_int), ("width", ctypes.c_int), ("height", ctypes.c_int),
-                ("tile_w", ctypes.c_int), ("tile_h", ctypes.c_int), ("cluster_size", ctypes.c_int)]
+                ("tile_w", ctypes.c_int), ("tile_h", ctypes.c_int), ("cluster_size", ctypes.c_int),
+                ("max_pairs", ctypes.c_int64)]
 
 
 class LossParams(ctypes.Structure):
@@ -60,11 +61,11 @@ class LossParams(ctypes.Structure):
 
 # Symbols declared by include/gsb200.h.
 SYMBOLS = (
-    "gsb_abi_version", "gsb_last_error",
+    "gsb_abi_version", "gsb_last_error", "gsb_launch_count",
     "gsb_cluster_compact_workspace_size", "gsb_cluster_compact",
     "gsb_project_fwd", "gsb_project_bwd",
     "gsb_bin_workspace_size", "gsb_bin",
-    "gsb_raster_workspace_size", "gsb_raster_fwd", "gsb_raster_bwd",
+    "gsb_raster_workspace_size", "gsb_raster_bit_words", "gsb_raster_fwd", "gsb_raster_bwd",
     "gsb_loss_workspace_size", "gsb_loss",
 )
 
@@ -80,8 +81,10 @@ def _load():
     lib.gsb_abi_version.argtypes = []
     lib.gsb_last_error.restype = ctypes.c_char_p
     lib.gsb_last_error.argtypes = []
+    lib.gsb_launch_count.restype = ctypes.c_ulonglong
+    lib.gsb_launch_count.argtypes = []
     for name in ("gsb_cluster_compact_workspace_size", "gsb_bin_workspace_size",
-                 "gsb_raster_workspace_size", "gsb_loss_workspace_size"):
+                 "gsb_raster_workspace_size", "gsb_raster_bit_words", "gsb_loss_workspace_size"):
         getattr(lib, name).restype = sz
         getattr(lib, name).argtypes = [vp]
     lib.gsb_cluster_compact.restype = ctypes.c_int
@@ -93,9 +96,9 @@ def _load():
     lib.gsb_bin.restype = ctypes.c_int
     lib.gsb_bin.argtypes = [vp, vp, vp, sz] + [vp] * 10
     lib.gsb_raster_fwd.restype = ctypes.c_int
-    lib.gsb_raster_fwd.argtypes = [vp, vp, vp, sz] + [vp] * 16
+    lib.gsb_raster_fwd.argtypes = [vp, vp, vp, sz] + [vp] * 17
     lib.gsb_raster_bwd.restype = ctypes.c_int
-    lib.gsb_raster_bwd.argtypes = [vp, vp, vp, sz] + [vp] * 18
+    lib.gsb_raster_bwd.argtypes = [vp, vp, vp, sz] + [vp] * 19
     lib.gsb_loss.restype = ctypes.c_int
     lib.gsb_loss.argtypes = [vp, vp, vp, sz] + [vp] * 5
     return lib
@@ -118,3 +121,8 @@ def check(code: int, what: str) -> None:
 
 def ref(struct) -> ctypes.c_void_p:
     return ctypes.cast(ctypes.pointer(struct), ctypes.c_void_p)
+
+
+def launch_count() -> int:
+    """Kernels launched by libgsb200.so so far in this process."""
+    return int(lib.gsb_launch_count())

@@ -1,10 +1,14 @@
 // Library-level C ABI: version and last-error reporting.
+#include <atomic>
+
 #include "gsb_common.cuh"
 
 namespace gsb {
 namespace {
 thread_local char g_last_error[256] = "no error";
-}
+std::atomic<unsigned long long> g_launches{0};
+}  // namespace
+void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 void set_error(cudaError_t err)
 {
     const char* msg = cudaGetErrorString(err);
@@ -16,3 +20,4 @@ void set_error(cudaError_t err)
 
 extern "C" int gsb_abi_version(void) { return GSB_ABI_VERSION; }
 extern "C" const char* gsb_last_error(void) { return gsb::g_last_error; }
+extern "C" unsigned long long gsb_launch_count(void) { return gsb::g_launches.load(); }

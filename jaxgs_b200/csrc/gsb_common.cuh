@@ -12,10 +12,14 @@ namespace gsb {
 
 // Records the last CUDA error string for gsb_last_error().
 void set_error(cudaError_t err);
+// Adds to the process-wide count of kernels this library has launched.
+void count_launch();
 
-// Returns GSB_ERR_LAUNCH (and records the error) if the last launch failed.
+// Counts the launch just issued; returns GSB_ERR_LAUNCH (and records the
+// error) if it failed.
 inline int check_launch()
 {
+    count_launch();
     cudaError_t err = cudaGetLastError();
     if (err != cudaSuccess) {
         set_error(err);

@@ -5,19 +5,25 @@
 // power <= 0, early stop once T < 1/8192, backward from the pixel's last
 // composited pair), on rectangular tile_w x tile_h tiles.
 //
-// Work decomposition (B200-first, not the reference's): one CTA per tile,
-// one warp per 8x4 block of the tile, one pixel per lane.  Warps walk the
-// tile's pair list in 32-pair batches; each lane stages one 48-byte splat
-// record and tests the splat's conservative 1/256-level bounding box against
-// its warp's 8x4 block, so a warp skips (with one ballot) every splat that
-// cannot give any of its pixels alpha >= 1/256 — the result is identical to
-// visiting them.  Warps stop independently once all their pixels are
-// saturated.  The backward reduces each splat's nine gradients with a
-// transposed butterfly (8 values in 9 shuffles + 1 in 5) and issues one
-// float atomic per value per warp.
+// Work decomposition (B200-first, not the reference's): one CTA per tile, one
+// warp per 8 x (4*ROWS) pixel block, ROWS vertically adjacent pixels per lane
+// (ROWS = 2 when tile_h is a multiple of 8, else 1).
+//  * Forward: a warp walks the tile's pairs in 32-pair batches; each lane
+//    stages one 48-byte splat record and tests the splat's conservative
+//    1/256-level bounding box against the warp's block, so one ballot skips
+//    every splat that cannot reach the block.  Warps stop independently once
+//    all their pixels are saturated, and record per batch a 32-bit word of
+//    the pairs that composited at least one fragment of the block.
+//  * Backward: a warp reads those words from its top pair down and visits
+//    only the set bits (exact pruning), recomputing each fragment in reverse.
+//    Per splat every lane accumulates moments of its pixels' power gradients
+//    (sum ge, ge*dy, ge*dy^2; the lane's column fixes dx) and colour
+//    gradients; a transposed butterfly reduces eight of them in nine
+//    shuffles, and one predicated RED per warp adds the ten cotangents.
 //
-// The power is computed with the exact operation sequence of the host
-// oracle (pre-scaled conic, fmaf form), so only exp differs between them.
+// The power is evaluated with the host oracle's operation order (the conic
+// scaled by -1/2, shared c00*dx / c10*dx, fused dy terms), so it is
+// bit-identical; only exp differs (__expf here, libm there).
 #include "gsb_common.cuh"
 
 namespace gsb {
@@ -63,8 +69,8 @@ __global__ void pack_kernel(int64_t capacity, const float* __restrict__ mean,
 }
 
 // Heaviest-first tile permutation: counting sort into 256 buckets, eight per
-// octave of (work + 1) (kernels/packed_rasterize.py:38-89 describes the same
-// bucketing); order inside a bucket is unspecified.
+// octave of (work + 1) (the bucketing of kernels/packed_rasterize.py:38-89);
+// order inside a bucket is unspecified.
 constexpr int kOrderThreads = 1024;
 constexpr int kOrderBuckets = 256;
 
@@ -109,81 +115,90 @@ __global__ void __launch_bounds__(kOrderThreads) order_tiles_kernel(const int32_
     }
 }
 
-struct TileGeom {
-    int tile, tx0, ty0;     // tile id and pixel origin
-    int bx0, by0;           // this warp's 8x4 block origin (pixels)
-    int px, py;             // this lane's pixel
-    bool in_image;
+template <int ROWS>
+struct Geom {
+    int tile;
+    int bx0, by0;  // block origin (pixels)
+    int px;        // lane column
+    int py0;       // lane's first row
 };
 
-__device__ __forceinline__ TileGeom tile_geom(const gsb_raster_params& p, int tile, int warp,
-                                              int lane)
+template <int ROWS>
+__device__ __forceinline__ Geom<ROWS> geom(int width, int tile_w, int tile_h, int tile, int warp,
+                                           int lane)
 {
-    TileGeom t;
-    int tiles_x = (p.width + p.tile_w - 1) / p.tile_w;
+    Geom<ROWS> t;
+    int tiles_x = (width + tile_w - 1) / tile_w;
+    int blocks_x = tile_w / 8;
     t.tile = tile;
-    t.tx0 = (tile % tiles_x) * p.tile_w;
-    t.ty0 = (tile / tiles_x) * p.tile_h;
-    int blocks_x = p.tile_w / 8;
-    t.bx0 = t.tx0 + (warp % blocks_x) * 8;
-    t.by0 = t.ty0 + (warp / blocks_x) * 4;
+    t.bx0 = (tile % tiles_x) * tile_w + (warp % blocks_x) * 8;
+    t.by0 = (tile / tiles_x) * tile_h + (warp / blocks_x) * 4 * ROWS;
     t.px = t.bx0 + (lane & 7);
-    t.py = t.by0 + (lane >> 3);
-    t.in_image = t.px < p.width && t.py < p.height;
+    t.py0 = t.by0 + (lane >> 3) * ROWS;
     return t;
 }
 
-// Can the splat reach alpha >= 1/256 at any pixel centre of the 8x4 block?
+// Can the splat reach alpha >= 1/256 at any pixel centre of the block?
+template <int ROWS>
 __device__ __forceinline__ bool block_hit(float4 r0, float bx0, float by0)
 {
-    return r0.x - r0.z <= bx0 + 7.5f && r0.x + r0.z >= bx0 + 0.5f && r0.y - r0.w <= by0 + 3.5f &&
-           r0.y + r0.w >= by0 + 0.5f;
+    return r0.x - r0.z <= bx0 + 7.5f && r0.x + r0.z >= bx0 + 0.5f &&
+           r0.y - r0.w <= by0 + (4 * ROWS - 0.5f) && r0.y + r0.w >= by0 + 0.5f;
 }
 
-// Power (= -q/2) with the oracle's operation sequence.
-__device__ __forceinline__ float power_of(float4 r1, float dx, float dy)
+__device__ __forceinline__ uint32_t bit_word(int32_t start, int tile, int batch, int warps, int warp)
 {
-    float t1 = __fmaf_rn(r1.x, dx, __fmul_rn(r1.y, dy));
-    float t2 = __fmaf_rn(r1.z, dx, __fmul_rn(r1.w, dy));
-    return __fmaf_rn(dx, t1, __fmul_rn(dy, t2));
+    return (uint32_t)(((start >> 5) + tile + batch) * warps + warp);
 }
 
 struct Stash {
     float4 r0[32], r1[32], r2[32];
+    int32_t id[32];
     float depth[32];
 };
 
-template <bool WANT_DEPTH>
+template <int ROWS, bool WANT_DEPTH>
 __global__ void __launch_bounds__(256) raster_fwd_kernel(
     gsb_raster_params p, const float4* __restrict__ splats, const float* __restrict__ depth,
     const int32_t* __restrict__ ids, const int32_t* __restrict__ offsets,
     const int32_t* __restrict__ order, const float* __restrict__ background,
     float* __restrict__ rgb, float* __restrict__ out_depth, float* __restrict__ out_alpha,
     float* __restrict__ final_t, int32_t* __restrict__ last_out,
-    int32_t* __restrict__ backward_work)
+    int32_t* __restrict__ backward_work, uint32_t* __restrict__ bits)
 {
     extern __shared__ Stash stash_all[];
     __shared__ int tile_work;
-    int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, warps = blockDim.x >> 5;
     Stash& st = stash_all[warp];
-    int tile = order[blockIdx.x];
-    TileGeom tg = tile_geom(p, tile, warp, lane);
+    const int tile = order[blockIdx.x];
+    const Geom<ROWS> tg = geom<ROWS>(p.width, p.tile_w, p.tile_h, tile, warp, lane);
     if (threadIdx.x == 0) tile_work = 0;
-    int32_t start = offsets[tile], end = offsets[tile + 1];
-    float pcx = (float)tg.px + 0.5f, pcy = (float)tg.py + 0.5f;
-    float bx0 = (float)tg.bx0, by0 = (float)tg.by0;
-    float T = 1.0f, cr = 0.0f, cg = 0.0f, cb = 0.0f, cd = 0.0f;
-    int32_t last = end;
-    bool done = !tg.in_image;
-    for (int32_t base = start; base < end; base += 32) {
-        if (__all_sync(GSB_FULL_MASK, done)) break;
+    const int32_t start = offsets[tile], end = offsets[tile + 1];
+    const float pcx = (float)tg.px + 0.5f;
+    const float bx0 = (float)tg.bx0, by0 = (float)tg.by0;
+    float pcy[ROWS], T[ROWS], cr[ROWS], cg[ROWS], cb[ROWS], cd[ROWS];
+    int32_t last[ROWS];
+    bool active[ROWS];
+#pragma unroll
+    for (int r = 0; r < ROWS; r++) {
+        pcy[r] = (float)(tg.py0 + r) + 0.5f;
+        T[r] = 1.0f;
+        cr[r] = cg[r] = cb[r] = cd[r] = 0.0f;
+        last[r] = end;
+        active[r] = tg.px < p.width && tg.py0 + r < p.height;
+    }
+    bool any_active = false;
+#pragma unroll
+    for (int r = 0; r < ROWS; r++) any_active |= active[r];
+    for (int32_t base = start, batch = 0; base < end; base += 32, batch++) {
+        if (!__any_sync(GSB_FULL_MASK, any_active)) break;
         int32_t i = base + lane;
         bool hit = false;
         if (i < end) {
             int32_t g = __ldg(ids + i);
             const float4* rec = splats + (int64_t)g * 3;
             float4 r0 = __ldg(rec);
-            hit = block_hit(r0, bx0, by0);
+            hit = block_hit<ROWS>(r0, bx0, by0);
             if (hit) {
                 st.r0[lane] = r0;
                 st.r1[lane] = __ldg(rec + 1);
@@ -192,42 +207,63 @@ __global__ void __launch_bounds__(256) raster_fwd_kernel(
             }
         }
         unsigned mask = __ballot_sync(GSB_FULL_MASK, hit);
+        unsigned contributed = 0;
         __syncwarp();
         while (mask) {
-            int k = __ffs(mask) - 1;
+            const int k = __ffs(mask) - 1;
             mask &= mask - 1;
-            float4 r0 = st.r0[k], r1 = st.r1[k], r2 = st.r2[k];
-            float dx = pcx - r0.x, dy = pcy - r0.y;
-            float power = power_of(r1, dx, dy);
-            float raw = r2.w * __expf(power);
-            if (!done && power <= 0.0f && raw >= kMinAlpha) {
-                float a = fminf(kMaxAlpha, raw);
-                float w = a * T;
-                cr = __fmaf_rn(w, r2.x, cr);
-                cg = __fmaf_rn(w, r2.y, cg);
-                cb = __fmaf_rn(w, r2.z, cb);
-                if (WANT_DEPTH) cd = __fmaf_rn(w, st.depth[k], cd);
-                T = T * (1.0f - a);
-                if (T < kMinT) {
-                    done = true;
-                    last = base + k + 1;
+            const float4 r0 = st.r0[k], r1 = st.r1[k], r2 = st.r2[k];
+            const float dx = pcx - r0.x;
+            const float ax = __fmul_rn(r1.x, dx), bx = __fmul_rn(r1.z, dx);
+            bool valid_any = false;
+#pragma unroll
+            for (int r = 0; r < ROWS; r++) {
+                const float dy = pcy[r] - r0.y;
+                const float t1 = __fmaf_rn(r1.y, dy, ax);
+                const float t2 = __fmaf_rn(r1.w, dy, bx);
+                const float power = __fmaf_rn(dy, t2, __fmul_rn(dx, t1));
+                const float raw = r2.w * __expf(power);
+                const bool valid = active[r] && power <= 0.0f && raw >= kMinAlpha;
+                if (valid) {
+                    const float a = fminf(kMaxAlpha, raw);
+                    const float w = a * T[r];
+                    cr[r] = __fmaf_rn(w, r2.x, cr[r]);
+                    cg[r] = __fmaf_rn(w, r2.y, cg[r]);
+                    cb[r] = __fmaf_rn(w, r2.z, cb[r]);
+                    if (WANT_DEPTH) cd[r] = __fmaf_rn(w, st.depth[k], cd[r]);
+                    T[r] = T[r] * (1.0f - a);
+                    if (T[r] < kMinT) {
+                        active[r] = false;
+                        last[r] = base + k + 1;
+                    }
                 }
+                valid_any |= valid;
             }
-            if (__all_sync(GSB_FULL_MASK, done)) break;
+            if (__ballot_sync(GSB_FULL_MASK, valid_any)) contributed |= 1u << k;
+            any_active = false;
+#pragma unroll
+            for (int r = 0; r < ROWS; r++) any_active |= active[r];
+            if (!__any_sync(GSB_FULL_MASK, any_active)) break;
         }
+        if (lane == 0) bits[bit_word(start, tile, batch, warps, warp)] = contributed;
         __syncwarp();
     }
-    if (tg.in_image) {
-        int64_t pix = (int64_t)tg.py * p.width + tg.px;
-        rgb[pix * 3] = cr + T * __ldg(background);
-        rgb[pix * 3 + 1] = cg + T * __ldg(background + 1);
-        rgb[pix * 3 + 2] = cb + T * __ldg(background + 2);
-        if (out_depth) out_depth[pix] = cd;
-        if (out_alpha) out_alpha[pix] = 1.0f - T;
-        final_t[pix] = T;
-        last_out[pix] = last;
+    int work = 0;
+#pragma unroll
+    for (int r = 0; r < ROWS; r++) {
+        const int y = tg.py0 + r;
+        if (tg.px < p.width && y < p.height) {
+            const int64_t pix = (int64_t)y * p.width + tg.px;
+            rgb[pix * 3] = cr[r] + T[r] * __ldg(background);
+            rgb[pix * 3 + 1] = cg[r] + T[r] * __ldg(background + 1);
+            rgb[pix * 3 + 2] = cb[r] + T[r] * __ldg(background + 2);
+            if (out_depth) out_depth[pix] = cd[r];
+            if (out_alpha) out_alpha[pix] = 1.0f - T[r];
+            final_t[pix] = T[r];
+            last_out[pix] = last[r];
+            work = max(work, last[r] - start);
+        }
     }
-    int work = tg.in_image ? last - start : 0;
 #pragma unroll
     for (int d = 16; d > 0; d >>= 1) work = max(work, __shfl_xor_sync(GSB_FULL_MASK, work, d));
     __syncthreads();
@@ -240,7 +276,7 @@ __global__ void __launch_bounds__(256) raster_fwd_kernel(
 // of value (l >> 2).  9 shuffles instead of 8 x 5.
 __device__ __forceinline__ float warp_sum8(float v[8], int lane)
 {
-    bool b4 = lane & 16, b3 = lane & 8, b2 = lane & 4;
+    const bool b4 = lane & 16, b3 = lane & 8, b2 = lane & 4;
 #pragma unroll
     for (int j = 0; j < 4; j++) {
         float keep = b4 ? v[j + 4] : v[j];
@@ -264,122 +300,139 @@ __device__ __forceinline__ float warp_sum8(float v[8], int lane)
     return s;
 }
 
-template <bool WANT_DEPTH>
+template <int ROWS, bool WANT_DEPTH>
 __global__ void __launch_bounds__(256) raster_bwd_kernel(
     gsb_raster_bwd_params p, const float4* __restrict__ splats, const float* __restrict__ depth,
     const int32_t* __restrict__ ids, const int32_t* __restrict__ offsets,
-    const int32_t* __restrict__ order, const float* __restrict__ background,
-    const float* __restrict__ final_t, const int32_t* __restrict__ last_in,
-    const float* __restrict__ drgb, const float* __restrict__ ddepth,
-    const float* __restrict__ dalpha, float* __restrict__ gmean, float* __restrict__ gconic,
-    float* __restrict__ gdepth, float* __restrict__ gcolor, float* __restrict__ galpha)
+    const int32_t* __restrict__ order, const uint32_t* __restrict__ bits,
+    const float* __restrict__ background, const float* __restrict__ final_t,
+    const int32_t* __restrict__ last_in, const float* __restrict__ drgb,
+    const float* __restrict__ ddepth, const float* __restrict__ dalpha, float* __restrict__ gmean,
+    float* __restrict__ gconic, float* __restrict__ gdepth, float* __restrict__ gcolor,
+    float* __restrict__ galpha)
 {
     extern __shared__ Stash stash_all[];
-    __shared__ int32_t stash_id[8][32];
-    int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, warps = blockDim.x >> 5;
     Stash& st = stash_all[warp];
-    int tile = order[blockIdx.x];
-    gsb_raster_params rp{p.capacity, p.width, p.height, p.tile_w, p.tile_h};
-    TileGeom tg = tile_geom(rp, tile, warp, lane);
-    int32_t start = offsets[tile];
-    float pcx = (float)tg.px + 0.5f, pcy = (float)tg.py + 0.5f;
-    float bx0 = (float)tg.bx0, by0 = (float)tg.by0;
-    float gR = 0.0f, gG = 0.0f, gB = 0.0f, gD = 0.0f, gtrans = 0.0f, T_after = 1.0f;
-    int32_t last = start;
-    if (tg.in_image) {
-        int64_t pix = (int64_t)tg.py * p.width + tg.px;
-        last = last_in[pix];
-        gR = drgb[pix * 3];
-        gG = drgb[pix * 3 + 1];
-        gB = drgb[pix * 3 + 2];
-        if (WANT_DEPTH) gD = ddepth ? ddepth[pix] : 0.0f;
-        gtrans = gR * __ldg(background) + gG * __ldg(background + 1) + gB * __ldg(background + 2) -
-                 (dalpha ? dalpha[pix] : 0.0f);
-        T_after = final_t[pix];
+    const int tile = order[blockIdx.x];
+    const Geom<ROWS> tg = geom<ROWS>(p.width, p.tile_w, p.tile_h, tile, warp, lane);
+    const int32_t start = offsets[tile];
+    const float pcx = (float)tg.px + 0.5f;
+    float pcy[ROWS], gR[ROWS], gG[ROWS], gB[ROWS], gD[ROWS], gtrans[ROWS], T_after[ROWS];
+    int32_t last[ROWS];
+    int32_t top = start;
+#pragma unroll
+    for (int r = 0; r < ROWS; r++) {
+        const int y = tg.py0 + r;
+        pcy[r] = (float)y + 0.5f;
+        gR[r] = gG[r] = gB[r] = gD[r] = gtrans[r] = 0.0f;
+        T_after[r] = 1.0f;
+        last[r] = start;
+        if (tg.px < p.width && y < p.height) {
+            const int64_t pix = (int64_t)y * p.width + tg.px;
+            last[r] = last_in[pix];
+            gR[r] = drgb[pix * 3];
+            gG[r] = drgb[pix * 3 + 1];
+            gB[r] = drgb[pix * 3 + 2];
+            if (WANT_DEPTH) gD[r] = ddepth[pix];
+            gtrans[r] = gR[r] * __ldg(background) + gG[r] * __ldg(background + 1) +
+                        gB[r] * __ldg(background + 2) - (dalpha ? dalpha[pix] : 0.0f);
+            T_after[r] = final_t[pix];
+            top = max(top, last[r]);
+        }
     }
-    int32_t top = last;
 #pragma unroll
     for (int d = 16; d > 0; d >>= 1) top = max(top, __shfl_xor_sync(GSB_FULL_MASK, top, d));
-    // Walk batches [base, chunk_end) from the end back to the tile start.
-    for (int32_t chunk_end = top; chunk_end > start; chunk_end -= 32) {
-        int32_t base = max(start, chunk_end - 32);
-        int32_t i = base + lane;
-        bool hit = false;
-        if (i < chunk_end) {
-            int32_t g = __ldg(ids + i);
-            const float4* rec = splats + (int64_t)g * 3;
-            float4 r0 = __ldg(rec);
-            hit = block_hit(r0, bx0, by0);
-            if (hit) {
-                st.r0[lane] = r0;
-                st.r1[lane] = __ldg(rec + 1);
-                st.r2[lane] = __ldg(rec + 2);
-                stash_id[warp][lane] = g;
-                if (WANT_DEPTH) st.depth[lane] = __ldg(depth + g);
-            }
+    // Per-lane RED target after the reduction: lane 4j holds moment j
+    // (Sx, Sy, Sxx, Sxy, Syy, R, G, B), lane 13 repeats Sxy for conic[2],
+    // lane 1 adds the opacity gradient sum(ge) / o, lane 2 the depth one.
+    const int group = lane >> 2, role = lane & 3;
+    float* target = nullptr;
+    int stride = 0;
+    if (role == 0) {
+        if (group < 2) { target = gmean + group; stride = 2; }
+        else if (group < 5) { target = gconic + (group == 2 ? 0 : group == 3 ? 1 : 3); stride = 4; }
+        else { target = gcolor + (group - 5); stride = 3; }
+    } else if (lane == 13) {
+        target = gconic + 2; stride = 4;
+    } else if (lane == 1) {
+        target = galpha; stride = 1;
+    } else if (WANT_DEPTH && lane == 2) {
+        target = gdepth; stride = 1;
+    }
+    if (top <= start) return;
+    const int32_t top_batch = (top - 1 - start) >> 5;
+    for (int32_t batch = top_batch; batch >= 0; batch--) {
+        uint32_t word = __ldg(bits + bit_word(start, tile, batch, warps, warp));
+        if (batch == top_batch) {
+            const int k_max = (top - 1 - start) & 31;
+            word &= k_max == 31 ? 0xffffffffu : ((2u << k_max) - 1u);
         }
-        unsigned mask = __ballot_sync(GSB_FULL_MASK, hit);
+        if (word == 0) continue;
+        const int32_t base = start + batch * 32;
+        if (word & (1u << lane)) {
+            const int32_t g = __ldg(ids + base + lane);
+            const float4* rec = splats + (int64_t)g * 3;
+            st.r0[lane] = __ldg(rec);
+            st.r1[lane] = __ldg(rec + 1);
+            st.r2[lane] = __ldg(rec + 2);
+            st.id[lane] = g;
+            if (WANT_DEPTH) st.depth[lane] = __ldg(depth + g);
+        }
         __syncwarp();
-        while (mask) {
-            int k = 31 - __clz(mask);
-            mask &= ~(1u << k);
-            int32_t idx = base + k;
-            float4 r0 = st.r0[k], r1 = st.r1[k], r2 = st.r2[k];
-            float dx = pcx - r0.x, dy = pcy - r0.y;
-            float power = power_of(r1, dx, dy);
-            float e = __expf(power);
-            float raw = r2.w * e;
-            bool contrib = idx < last && power <= 0.0f && raw >= kMinAlpha;
-            float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-            float go = 0.0f, gz = 0.0f;
-            if (contrib) {
-                float a = fminf(kMaxAlpha, raw);
-                float one_minus = 1.0f - a;
-                float T_before = __fdividef(T_after, one_minus);
-                float w = T_before * a;
-                float gw = gR * r2.x + gG * r2.y + gB * r2.z;
-                if (WANT_DEPTH) gw += gD * st.depth[k];
-                float ga = T_before * (gw - gtrans);
-                gtrans = a * gw + one_minus * gtrans;
-                v[5] = w * gR;
-                v[6] = w * gG;
-                v[7] = w * gB;
-                if (WANT_DEPTH) gz = w * gD;
-                if (raw < kMaxAlpha) {
-                    float ge = ga * raw;
-                    go = ga * e;
-                    // r1 holds -c/2: c00*dx + cbar*dy = -2 (r1.x dx + rbar dy).
-                    float rbar = 0.5f * (r1.y + r1.z);
-                    float m0 = __fmaf_rn(r1.x, dx, rbar * dy);
-                    float m1 = __fmaf_rn(r1.w, dy, rbar * dx);
-                    v[0] = -2.0f * ge * m0;
-                    v[1] = -2.0f * ge * m1;
-                    float h = -0.5f * ge;
-                    v[2] = h * dx * dx;
-                    v[3] = h * dx * dy;
-                    v[4] = h * dy * dy;
-                }
-                T_after = T_before;
-            }
-            if (__any_sync(GSB_FULL_MASK, contrib)) {
-                int64_t g = stash_id[warp][k];
-                float s = warp_sum8(v, lane);
-                go = warp_sum(go);
-                if (WANT_DEPTH) gz = warp_sum(gz);
-                int which = lane >> 2, role = lane & 3;
-                if (role == 0) {
-                    float* dst = which < 2 ? gmean + g * 2 + which
-                                 : which < 5 ? gconic + g * 4 + (which == 2 ? 0 : which == 3 ? 1 : 3)
-                                             : gcolor + g * 3 + (which - 5);
-                    atomicAdd(dst, s);
-                } else if (role == 1 && which == 3) {
-                    atomicAdd(gconic + g * 4 + 2, s);
-                } else if (lane == 1) {
-                    atomicAdd(galpha + g, go);
-                } else if (WANT_DEPTH && lane == 2) {
-                    atomicAdd(gdepth + g, gz);
+        while (word) {
+            const int k = 31 - __clz(word);
+            word &= ~(1u << k);
+            const int32_t idx = base + k;
+            const float4 r0 = st.r0[k], r1 = st.r1[k], r2 = st.r2[k];
+            const float dx = pcx - r0.x;
+            const float ax = __fmul_rn(r1.x, dx), bx = __fmul_rn(r1.z, dx);
+            float S0 = 0.f, Sy = 0.f, Syy = 0.f, R = 0.f, G = 0.f, B = 0.f, Z = 0.f;
+#pragma unroll
+            for (int r = 0; r < ROWS; r++) {
+                const float dy = pcy[r] - r0.y;
+                const float t1 = __fmaf_rn(r1.y, dy, ax);
+                const float t2 = __fmaf_rn(r1.w, dy, bx);
+                const float power = __fmaf_rn(dy, t2, __fmul_rn(dx, t1));
+                const float raw = r2.w * __expf(power);
+                if (idx < last[r] && power <= 0.0f && raw >= kMinAlpha) {
+                    const float a = fminf(kMaxAlpha, raw);
+                    const float one_minus = 1.0f - a;
+                    const float T_before = __fdividef(T_after[r], one_minus);
+                    const float w = T_before * a;
+                    float gw = gR[r] * r2.x + gG[r] * r2.y + gB[r] * r2.z;
+                    if (WANT_DEPTH) gw += gD[r] * st.depth[k];
+                    const float ga = T_before * (gw - gtrans[r]);
+                    gtrans[r] = a * gw + one_minus * gtrans[r];
+                    R = __fmaf_rn(w, gR[r], R);
+                    G = __fmaf_rn(w, gG[r], G);
+                    B = __fmaf_rn(w, gB[r], B);
+                    if (WANT_DEPTH) Z = __fmaf_rn(w, gD[r], Z);
+                    const float ge = raw < kMaxAlpha ? ga * raw : 0.0f;
+                    const float gedy = ge * dy;
+                    S0 += ge;
+                    Sy += gedy;
+                    Syy = __fmaf_rn(gedy, dy, Syy);
+                    T_after[r] = T_before;
                 }
             }
+            const float Sx = dx * S0;
+            float v[8] = {Sx, Sy, dx * Sx, dx * Sy, Syy, R, G, B};
+            float s = warp_sum8(v, lane);
+            S0 = warp_sum(S0);
+            if (WANT_DEPTH) Z = warp_sum(Z);
+            // gmean.x = c00 Sx + cbar Sy, gmean.y = c11 Sy + cbar Sx with c = -2 r1;
+            // gconic = -Sxx/2, -Sxy/2 (twice), -Syy/2; gcolor = R, G, B.
+            const float other = __shfl_xor_sync(GSB_FULL_MASK, s, 4);
+            const float rbar = r1.y + r1.z;  // = -cbar
+            float value;
+            if (group == 0) value = -2.0f * r1.x * s - rbar * other;
+            else if (group == 1) value = -2.0f * r1.w * s - rbar * other;
+            else if (group < 5) value = -0.5f * s;
+            else value = s;
+            if (lane == 1) value = __fdividef(S0, r2.w);
+            if (WANT_DEPTH && lane == 2) value = Z;
+            if (target) atomicAdd(target + (int64_t)st.id[k] * stride, value);
         }
         __syncwarp();
     }
@@ -415,14 +468,65 @@ __global__ void zero_cluster_cotangents_kernel(int64_t capacity, int cluster_siz
 
 bool tiles_ok(int tile_w, int tile_h)
 {
-    return tile_w > 0 && tile_h > 0 && tile_w % 8 == 0 && tile_h % 4 == 0 &&
-           (tile_w / 8) * (tile_h / 4) <= 8;
+    return tile_w > 0 && tile_h > 0 && tile_w % 8 == 0 && tile_h % 4 == 0 && tile_w <= 16 &&
+           tile_h <= 16;
+}
+
+int rows_per_lane(int tile_h) { return tile_h % 8 == 0 ? 2 : 1; }
+
+int warps_per_tile(int tile_w, int tile_h)
+{
+    return (tile_w / 8) * (tile_h / (4 * rows_per_lane(tile_h)));
+}
+
+int64_t num_tiles(const gsb_raster_params& p)
+{
+    return (int64_t)ceil_div(p.width, p.tile_w) * ceil_div(p.height, p.tile_h);
 }
 
 size_t raster_ws(const gsb_raster_params& p)
 {
-    int64_t tiles = (int64_t)ceil_div(p.width, p.tile_w) * ceil_div(p.height, p.tile_h);
-    return ((size_t)tiles * sizeof(int32_t) + 255) & ~size_t(255);
+    return ((size_t)num_tiles(p) * sizeof(int32_t) + 255) & ~size_t(255);
+}
+
+size_t bit_words(const gsb_raster_params& p)
+{
+    int64_t pairs = p.max_pairs > 0 ? p.max_pairs : 0;
+    return (size_t)(pairs / 32 + num_tiles(p) + 1) * warps_per_tile(p.tile_w, p.tile_h);
+}
+
+template <int ROWS>
+void launch_fwd(cudaStream_t s, int tiles, int warps, bool want_depth, const gsb_raster_params& p,
+                const float4* sp, const float* depth, const int32_t* ids, const int32_t* offsets,
+                const int32_t* order, const float* bg, float* rgb, float* od, float* oa,
+                float* final_t, int32_t* last, int32_t* work, uint32_t* bits)
+{
+    size_t smem = (size_t)warps * sizeof(Stash);
+    if (want_depth)
+        raster_fwd_kernel<ROWS, true><<<tiles, warps * 32, smem, s>>>(
+            p, sp, depth, ids, offsets, order, bg, rgb, od, oa, final_t, last, work, bits);
+    else
+        raster_fwd_kernel<ROWS, false><<<tiles, warps * 32, smem, s>>>(
+            p, sp, depth, ids, offsets, order, bg, rgb, od, oa, final_t, last, work, bits);
+}
+
+template <int ROWS>
+void launch_bwd(cudaStream_t s, int tiles, int warps, bool want_depth,
+                const gsb_raster_bwd_params& p, const float4* sp, const float* depth,
+                const int32_t* ids, const int32_t* offsets, const int32_t* order,
+                const uint32_t* bits, const float* bg, const float* final_t, const int32_t* last,
+                const float* drgb, const float* ddepth, const float* dalpha, float* gmean,
+                float* gconic, float* gdepth, float* gcolor, float* galpha)
+{
+    size_t smem = (size_t)warps * sizeof(Stash);
+    if (want_depth)
+        raster_bwd_kernel<ROWS, true><<<tiles, warps * 32, smem, s>>>(
+            p, sp, depth, ids, offsets, order, bits, bg, final_t, last, drgb, ddepth, dalpha,
+            gmean, gconic, gdepth, gcolor, galpha);
+    else
+        raster_bwd_kernel<ROWS, false><<<tiles, warps * 32, smem, s>>>(
+            p, sp, depth, ids, offsets, order, bits, bg, final_t, last, drgb, ddepth, dalpha,
+            gmean, gconic, gdepth, gcolor, galpha);
 }
 
 }  // namespace
@@ -435,27 +539,34 @@ extern "C" size_t gsb_raster_workspace_size(const gsb_raster_params* p)
     return p ? raster_ws(*p) : 0;
 }
 
+extern "C" size_t gsb_raster_bit_words(const gsb_raster_params* p)
+{
+    if (!p || !tiles_ok(p->tile_w, p->tile_h) || p->width <= 0 || p->height <= 0) return 0;
+    return bit_words(*p);
+}
+
 extern "C" int gsb_raster_fwd(gsb_stream_t stream, const gsb_raster_params* p, void* workspace,
                               size_t workspace_bytes, const float* mean, const float* conic,
                               const float* depth, const float* color, const float* alpha,
                               const int8_t* visible, const int32_t* gaussian_ids,
                               const int32_t* tile_offsets, const float* background, float* rgb,
                               float* out_depth, float* out_alpha, float* final_t, int32_t* last,
-                              int32_t* backward_work, float* splats)
+                              int32_t* backward_work, float* splats, uint32_t* contribution_bits)
 {
     if (!p) return GSB_ERR_NULL;
-    if (p->capacity < 0 || p->width <= 0 || p->height <= 0 || !tiles_ok(p->tile_w, p->tile_h))
+    if (p->capacity < 0 || p->width <= 0 || p->height <= 0 || !tiles_ok(p->tile_w, p->tile_h) ||
+        p->max_pairs < 0 || p->max_pairs >= (int64_t(1) << 31))
         return GSB_ERR_INVALID;
     if (!workspace || workspace_bytes < raster_ws(*p)) return GSB_ERR_WORKSPACE;
     if (!gaussian_ids || !tile_offsets || !background || !rgb || !final_t || !last ||
-        !backward_work || !splats ||
+        !backward_work || !splats || !contribution_bits ||
         (p->capacity > 0 && (!mean || !conic || !color || !alpha || !visible)) ||
         (out_depth && !depth))
         return GSB_ERR_NULL;
     if ((reinterpret_cast<uintptr_t>(splats) | reinterpret_cast<uintptr_t>(conic)) & 15)
         return GSB_ERR_INVALID;
     cudaStream_t s = as_stream(stream);
-    int tiles = ceil_div(p->width, p->tile_w) * ceil_div(p->height, p->tile_h);
+    int tiles = (int)num_tiles(*p);
     int32_t* order = static_cast<int32_t*>(workspace);
     if (p->capacity > 0) {
         pack_kernel<<<ceil_div(p->capacity, 256), 256, 0, s>>>(p->capacity, mean, conic, color,
@@ -465,16 +576,16 @@ extern "C" int gsb_raster_fwd(gsb_stream_t stream, const gsb_raster_params* p, v
     }
     order_tiles_kernel<<<1, kOrderThreads, 0, s>>>(tile_offsets, tiles, 1, order);
     if (int e = check_launch()) return e;
-    int warps = (p->tile_w / 8) * (p->tile_h / 4);
-    size_t smem = (size_t)warps * sizeof(Stash);
-    if (out_depth)
-        raster_fwd_kernel<true><<<tiles, warps * 32, smem, s>>>(
-            *p, reinterpret_cast<const float4*>(splats), depth, gaussian_ids, tile_offsets, order,
-            background, rgb, out_depth, out_alpha, final_t, last, backward_work);
+    int warps = warps_per_tile(p->tile_w, p->tile_h);
+    const float4* sp = reinterpret_cast<const float4*>(splats);
+    if (rows_per_lane(p->tile_h) == 2)
+        launch_fwd<2>(s, tiles, warps, out_depth != nullptr, *p, sp, depth, gaussian_ids,
+                      tile_offsets, order, background, rgb, out_depth, out_alpha, final_t, last,
+                      backward_work, contribution_bits);
     else
-        raster_fwd_kernel<false><<<tiles, warps * 32, smem, s>>>(
-            *p, reinterpret_cast<const float4*>(splats), depth, gaussian_ids, tile_offsets, order,
-            background, rgb, out_depth, out_alpha, final_t, last, backward_work);
+        launch_fwd<1>(s, tiles, warps, out_depth != nullptr, *p, sp, depth, gaussian_ids,
+                      tile_offsets, order, background, rgb, out_depth, out_alpha, final_t, last,
+                      backward_work, contribution_bits);
     return check_launch();
 }
 
@@ -483,27 +594,28 @@ extern "C" int gsb_raster_bwd(gsb_stream_t stream, const gsb_raster_bwd_params* 
                               const float* depth, const int32_t* gaussian_ids,
                               const int32_t* tile_offsets, const float* background,
                               const float* final_t, const int32_t* last,
-                              const int32_t* backward_work, const float* drgb,
-                              const float* ddepth, const float* dalpha,
+                              const int32_t* backward_work, const uint32_t* contribution_bits,
+                              const float* drgb, const float* ddepth, const float* dalpha,
                               const int32_t* cluster_ids, const int32_t* cluster_count,
                               float* gmean, float* gconic, float* gdepth, float* gcolor,
                               float* galpha)
 {
     if (!p) return GSB_ERR_NULL;
-    gsb_raster_params rp{p->capacity, p->width, p->height, p->tile_w, p->tile_h};
+    gsb_raster_params rp{p->capacity, p->width, p->height, p->tile_w, p->tile_h, p->max_pairs};
     if (p->capacity < 0 || p->width <= 0 || p->height <= 0 || !tiles_ok(p->tile_w, p->tile_h))
         return GSB_ERR_INVALID;
     if (!workspace || workspace_bytes < raster_ws(rp)) return GSB_ERR_WORKSPACE;
     if (!splats || !gaussian_ids || !tile_offsets || !background || !final_t || !last ||
-        !backward_work || !drgb || !gmean || !gconic || !gcolor || !galpha)
+        !backward_work || !contribution_bits || !drgb || !gmean || !gconic || !gcolor || !galpha)
         return GSB_ERR_NULL;
     bool want_depth = ddepth != nullptr;
     if (want_depth && (!depth || !gdepth)) return GSB_ERR_NULL;
     if (cluster_ids && (!cluster_count || p->cluster_size <= 0)) return GSB_ERR_INVALID;
+    if (!cluster_ids && !gdepth) return GSB_ERR_NULL;
     if ((reinterpret_cast<uintptr_t>(splats) | reinterpret_cast<uintptr_t>(gconic)) & 15)
         return GSB_ERR_INVALID;
     cudaStream_t s = as_stream(stream);
-    int tiles = ceil_div(p->width, p->tile_w) * ceil_div(p->height, p->tile_h);
+    int tiles = (int)num_tiles(rp);
     int32_t* order = static_cast<int32_t*>(workspace);
     if (p->capacity > 0) {
         if (cluster_ids) {
@@ -518,16 +630,15 @@ extern "C" int gsb_raster_bwd(gsb_stream_t stream, const gsb_raster_bwd_params* 
     }
     order_tiles_kernel<<<1, kOrderThreads, 0, s>>>(backward_work, tiles, 0, order);
     if (int e = check_launch()) return e;
-    int warps = (p->tile_w / 8) * (p->tile_h / 4);
-    size_t smem = (size_t)warps * sizeof(Stash);
+    int warps = warps_per_tile(p->tile_w, p->tile_h);
     const float4* sp = reinterpret_cast<const float4*>(splats);
-    if (want_depth)
-        raster_bwd_kernel<true><<<tiles, warps * 32, smem, s>>>(
-            *p, sp, depth, gaussian_ids, tile_offsets, order, background, final_t, last, drgb,
-            ddepth, dalpha, gmean, gconic, gdepth, gcolor, galpha);
+    if (rows_per_lane(p->tile_h) == 2)
+        launch_bwd<2>(s, tiles, warps, want_depth, *p, sp, depth, gaussian_ids, tile_offsets,
+                      order, contribution_bits, background, final_t, last, drgb, ddepth, dalpha,
+                      gmean, gconic, gdepth, gcolor, galpha);
     else
-        raster_bwd_kernel<false><<<tiles, warps * 32, smem, s>>>(
-            *p, sp, depth, gaussian_ids, tile_offsets, order, background, final_t, last, drgb,
-            ddepth, dalpha, gmean, gconic, gdepth, gcolor, galpha);
+        launch_bwd<1>(s, tiles, warps, want_depth, *p, sp, depth, gaussian_ids, tile_offsets,
+                      order, contribution_bits, background, final_t, last, drgb, ddepth, dalpha,
+                      gmean, gconic, gdepth, gcolor, galpha);
     return check_launch();
 }

@@ -43,6 +43,17 @@ def _workspace(nbytes: int, device) -> torch.Tensor:
     return torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=device)
 
 
+_ZEROS = {}
+
+
+def _zeros(n: int, device) -> torch.Tensor:
+    """Cached read-only zeros (background, absent cotangents)."""
+    key = (str(device), n)
+    if key not in _ZEROS:
+        _ZEROS[key] = torch.zeros(n, dtype=_f32, device=device)
+    return _ZEROS[key]
+
+
 def _c(t: torch.Tensor, dtype=None) -> torch.Tensor:
     if dtype is not None and t.dtype != dtype:
         t = t.to(dtype)
@@ -52,18 +63,20 @@ def _c(t: torch.Tensor, dtype=None) -> torch.Tensor:
 # ---------------------------------------------------------------------------
 # Cluster culling (render/pipeline.py:18-44)
 # ---------------------------------------------------------------------------
-def compact_visible_clusters(bounds, camera: DeviceCamera, config: CapacityConfig):
+def compact_visible_clusters(bounds, camera: DeviceCamera, config: CapacityConfig,
+                             want_slots: bool = True):
     """frustum_cluster_mask + compact_visible_clusters.
 
-    bounds: (center [N,3], extent [N,3], valid [N] bool) device tensors.
-    Returns ((ids [N] int32, count [1] int32), visible_slots [C] bool).
+    bounds: (center [N,3], extent [N,3], valid [N] bool/uint8) device tensors.
+    Returns ((ids [N] int32, count [1] int32), visible_slots [C] bool or None).
     """
     center, extent, valid = bounds
     _require_cuda(center, "compact_visible_clusters")
     n = int(valid.shape[0])
     ids = torch.empty(max(n, 1), dtype=_i32, device=center.device)
     count = torch.empty(1, dtype=_i32, device=center.device)
-    slots = torch.empty(config.max_gaussians, dtype=torch.uint8, device=center.device)
+    slots = (torch.empty(config.max_gaussians, dtype=torch.uint8, device=center.device)
+             if want_slots else None)
     p = L.ClusterParams(n, config.cluster_size, config.max_gaussians)
     ws = _workspace(L.lib.gsb_cluster_compact_workspace_size(L.ref(p)), center.device)
     L.check(L.lib.gsb_cluster_compact(_stream(), L.ref(p), _ptr(ws), ws.numel(),
@@ -71,7 +84,7 @@ def compact_visible_clusters(bounds, camera: DeviceCamera, config: CapacityConfi
                                       _ptr(_c(valid, torch.uint8)), _ptr(_c(camera.planes, _f32)),
                                       _ptr(ids), _ptr(count), _ptr(slots)),
             "compact_visible_clusters")
-    return (ids[:n] if n else ids[:0], count), slots.bool()
+    return (ids[:n] if n else ids[:0], count), (slots.bool() if want_slots else None)
 
 
 def render_preprocess(cluster_bounds, camera: DeviceCamera, gaussians: GaussianArrays,
@@ -233,7 +246,7 @@ def rasterize_forward(projected: ProjectedGaussians, table: SortedVisibilityTabl
     dev = projected.mean.device
     W, H = camera.width, camera.height
     if background is None:
-        background = torch.zeros(3, dtype=_f32, device=dev)
+        background = _zeros(3, dev)
     rgb = torch.empty(H, W, 3, dtype=_f32, device=dev)
     out_depth = torch.empty(H, W, dtype=_f32, device=dev) if want_depth else None
     out_alpha = torch.empty(H, W, dtype=_f32, device=dev) if want_alpha else None
@@ -241,7 +254,9 @@ def rasterize_forward(projected: ProjectedGaussians, table: SortedVisibilityTabl
     last = torch.empty(H * W, dtype=_i32, device=dev)
     work = torch.empty(_tiles(camera, config), dtype=_i32, device=dev)
     splats = torch.empty(C, 12, dtype=_f32, device=dev)
-    p = L.RasterParams(C, W, H, config.tile_size, config.raster_tile_height)
+    p = L.RasterParams(C, W, H, config.tile_size, config.raster_tile_height,
+                       int(table.gaussian_ids.shape[0]))
+    bits = torch.empty(max(int(L.lib.gsb_raster_bit_words(L.ref(p))), 1), dtype=_i32, device=dev)
     ws = _workspace(L.lib.gsb_raster_workspace_size(L.ref(p)), dev)
     L.check(L.lib.gsb_raster_fwd(
         _stream(), L.ref(p), _ptr(ws), ws.numel(), _ptr(_c(projected.mean, _f32)),
@@ -249,9 +264,9 @@ def rasterize_forward(projected: ProjectedGaussians, table: SortedVisibilityTabl
         _ptr(_c(projected.color, _f32)), _ptr(_c(projected.alpha, _f32)),
         _ptr(_c(projected.visible, torch.int8)), _ptr(table.gaussian_ids),
         _ptr(table.tile_offsets), _ptr(_c(background, _f32)), _ptr(rgb), _ptr(out_depth),
-        _ptr(out_alpha), _ptr(final_t), _ptr(last), _ptr(work), _ptr(splats)),
+        _ptr(out_alpha), _ptr(final_t), _ptr(last), _ptr(work), _ptr(splats), _ptr(bits)),
         "rasterization forward")
-    return RenderResult(rgb, out_depth, out_alpha), RasterCache(splats, final_t, last, work)
+    return RenderResult(rgb, out_depth, out_alpha), RasterCache(splats, final_t, last, work, bits)
 
 
 def rasterize_backward(projected: ProjectedGaussians, table: SortedVisibilityTable,
@@ -265,7 +280,7 @@ def rasterize_backward(projected: ProjectedGaussians, table: SortedVisibilityTab
     C = config.max_gaussians
     dev = drgb.device
     if background is None:
-        background = torch.zeros(3, dtype=_f32, device=dev)
+        background = _zeros(3, dev)
     gmean = torch.empty(C, 2, dtype=_f32, device=dev)
     gconic = torch.empty(C, 2, 2, dtype=_f32, device=dev)
     gdepth = torch.empty(C, dtype=_f32, device=dev)
@@ -274,24 +289,26 @@ def rasterize_backward(projected: ProjectedGaussians, table: SortedVisibilityTab
     ids, count = (None, None) if visible_clusters is None else visible_clusters
     if ddepth is not None and visible_clusters is not None:
         raise ValueError("depth cotangents are not defined with visible_clusters")
+    max_pairs = int(table.gaussian_ids.shape[0])
     p = L.RasterBwdParams(C, camera.width, camera.height, config.tile_size,
-                          config.raster_tile_height, config.cluster_size)
-    rp = L.RasterParams(C, camera.width, camera.height, config.tile_size, config.raster_tile_height)
+                          config.raster_tile_height, config.cluster_size, max_pairs)
+    rp = L.RasterParams(C, camera.width, camera.height, config.tile_size,
+                        config.raster_tile_height, max_pairs)
     ws = _workspace(L.lib.gsb_raster_workspace_size(L.ref(rp)), dev)
     L.check(L.lib.gsb_raster_bwd(
         _stream(), L.ref(p), _ptr(ws), ws.numel(), _ptr(cache.splats),
         _ptr(_c(projected.depth, _f32)), _ptr(table.gaussian_ids), _ptr(table.tile_offsets),
         _ptr(_c(background, _f32)), _ptr(cache.final_t), _ptr(cache.last),
-        _ptr(cache.backward_work), _ptr(_c(drgb, _f32)),
+        _ptr(cache.backward_work), _ptr(cache.contribution_bits), _ptr(_c(drgb, _f32)),
         _ptr(None if ddepth is None else _c(ddepth, _f32)),
         _ptr(None if dalpha is None else _c(dalpha, _f32)),
         _ptr(None if ids is None else _c(ids, _i32)), _ptr(None if count is None else _c(count, _i32)),
         _ptr(gmean), _ptr(gconic), _ptr(gdepth), _ptr(gcolor), _ptr(galpha)),
         "rasterization backward")
-    if ddepth is None and visible_clusters is None:
-        pass  # gdepth zeroed by the whole-pool clear
+    # The radius cotangent of a rasterizer is zero (sorted_rasterizer.py:224).
+    radius = _zeros(1, dev).expand(C)
     return projected.replace(mean=gmean, conic=gconic, depth=gdepth, color=gcolor, alpha=galpha,
-                             radius=torch.zeros_like(projected.radius))
+                             radius=radius)
 
 
 # ---------------------------------------------------------------------------

@@ -39,7 +39,7 @@ class StepOutput:
 def compute_training_step(pool: GaussianArrays, bounds, camera: DeviceCamera, target: torch.Tensor,
                           config: CapacityConfig, active_degree: int, *,
                           active_sh_only: bool = True, sh_color_only: bool = False,
-                          keep_image: bool = False) -> StepOutput:
+                          keep_image: bool = False, stage_events: dict | None = None) -> StepOutput:
     """training/step.py:32-89 without the optimizer update.
 
     bounds: world cluster bounds (center, extent, valid) on the device.
@@ -47,18 +47,49 @@ def compute_training_step(pool: GaussianArrays, bounds, camera: DeviceCamera, ta
     The culled pool's alive mask (render/pipeline.py:44, alive & slots) equals
     the pool's alive mask on every listed cluster, which is all the compact
     projection reads, so it is not materialised.
+    stage_events: optional dict; receives (start, end) CUDA events recorded on
+    the current stream around each stage (cull, project, bin, raster_fwd,
+    loss, raster_bwd, project_bwd).
     """
-    clusters, _slots = K.compact_visible_clusters(bounds, camera, config)
+    stream = torch.cuda.current_stream()
+
+    def mark(name):
+        if stage_events is None:
+            return None
+        ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+        ev[0].record(stream)
+        stage_events[name] = ev
+        return ev
+
+    def done(ev):
+        if ev is not None:
+            ev[1].record(stream)
+
+    ev = mark("cull")
+    clusters, _ = K.compact_visible_clusters(bounds, camera, config, want_slots=False)
+    done(ev)
+    ev = mark("project")
     projected, pullback = K.project_with_compact_pullback(
         pool, camera, config, active_degree, clusters, rgb_only=True,
         active_sh_only=active_sh_only, sh_color_only=sh_color_only, visible_color_only=True)
+    done(ev)
+    ev = mark("bin")
     table = K.build_sorted_visibility_table_cute(projected, camera, config)
+    done(ev)
+    ev = mark("raster_fwd")
     result, cache = K.rasterize_forward(projected, table, camera, config, want_depth=False,
                                         want_alpha=False)
+    done(ev)
+    ev = mark("loss")
     loss, drgb, _ = K._fused_loss(result.rgb, target, False, clip_input=True)
+    done(ev)
+    ev = mark("raster_bwd")
     cot = K.rasterize_backward(projected, table, cache, drgb, camera, config,
                                visible_clusters=clusters)
+    done(ev)
+    ev = mark("project_bwd")
     grads = pullback(cot)
+    done(ev)
     return StepOutput(loss, grads, clusters, table.pair_count, table.overflow,
                       result.rgb if keep_image else None)
 

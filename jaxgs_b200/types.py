@@ -26,12 +26,14 @@ class GaussianArrays:
     rotation: torch.Tensor   # [C, 4] wxyz
     opacity: torch.Tensor    # [C, 1] logits
     sh: torch.Tensor         # [C, SH_DIM, 3]
-    alive: torch.Tensor      # [C] bool
+    alive: torch.Tensor      # [C] bool or uint8 (uint8 avoids a per-call conversion)
 
     @classmethod
     def from_numpy(cls, pool: dict, device="cuda") -> "GaussianArrays":
-        return cls(*(torch.as_tensor(np.ascontiguousarray(pool[k]), device=device)
-                     for k in ("xyz", "log_scale", "rotation", "opacity", "sh", "alive")))
+        arrays = [torch.as_tensor(np.ascontiguousarray(pool[k]), device=device)
+                  for k in ("xyz", "log_scale", "rotation", "opacity", "sh")]
+        alive = torch.as_tensor(np.ascontiguousarray(pool["alive"], np.uint8), device=device)
+        return cls(*arrays, alive)
 
     @property
     def capacity(self) -> int:
@@ -105,10 +107,11 @@ class RasterCache:
     """State the forward hands to the backward (splat records, per-pixel final
     transmittance and last pair, per-tile backward work)."""
 
-    splats: torch.Tensor         # [C, 12] float32
-    final_t: torch.Tensor        # [H * W]
-    last: torch.Tensor           # [H * W] int32
-    backward_work: torch.Tensor  # [T] int32
+    splats: torch.Tensor             # [C, 12] float32
+    final_t: torch.Tensor            # [H * W]
+    last: torch.Tensor               # [H * W] int32
+    backward_work: torch.Tensor      # [T] int32
+    contribution_bits: torch.Tensor  # [gsb_raster_bit_words] int32 (uint32 words)
 
 
 def tree_fields(obj):

@@ -688,6 +688,28 @@ EXPORT int64_t orc_bin(const float* mean, const float* conic, const float* alpha
 /* threshold decision lay within a relative 2e-5 of its cut, so an          */
 /* implementation whose exp differs by a few ulp may legitimately differ.    */
 /* ------------------------------------------------------------------------- */
+/* Atomic accumulation for the pixel-parallel backward. */
+#define ACC_ADD(slot, val)                 \
+    do {                                   \
+        double v_ = (val);                 \
+        _Pragma("omp atomic") (slot) += v_; \
+    } while (0)
+
+/*
+ * power = -0.5 * (dx*(c00*dx + c01*dy) + dy*(c10*dx + c11*dy))
+ * (sorted_rasterize.py:67-70) in one fixed operation order: the conic is
+ * scaled by -1/2 (exact), the dx products are rounded first and the dy terms
+ * fused, so an implementation that shares c00*dx and c10*dx between pixels of
+ * one column reproduces these bits.
+ */
+static inline float power_of(const float* c, float dx, float dy)
+{
+    float c00 = -0.5f * c[0], c01 = -0.5f * c[1], c10 = -0.5f * c[2], c11 = -0.5f * c[3];
+    float t1 = fmaf(c01, dy, c00 * dx);
+    float t2 = fmaf(c11, dy, c10 * dx);
+    return fmaf(dy, t2, dx * t1);
+}
+
 static inline int near_cut(float value, float cut, float rel)
 {
     return fabsf(value - cut) <= rel * cut;
@@ -712,8 +734,7 @@ EXPORT void orc_raster_fwd(int width, int height, int tile_w, int tile_h, const 
             int64_t g = ids[index];
             float dx = (float)px + 0.5f - mean[g * 2];
             float dy = (float)py + 0.5f - mean[g * 2 + 1];
-            float exponent = -0.5f * (dx * (conic[g * 4] * dx + conic[g * 4 + 1] * dy)
-                                      + dy * (conic[g * 4 + 2] * dx + conic[g * 4 + 3] * dy));
+            float exponent = power_of(conic + g * 4, dx, dy);
             if (exponent <= 0.0f) {
                 float raw = opacity[g] * expf(exponent);
                 if (near_cut(raw, 1.0f / 256.0f, 2e-5f)) amb = 1;
@@ -757,6 +778,7 @@ EXPORT void orc_raster_bwd(int width, int height, int tile_w, int tile_h, int ca
 {
     int tiles_x = (width + tile_w - 1) / tile_w;
     double* acc = (double*)calloc((size_t)capacity * 11, sizeof(double));
+#pragma omp parallel for schedule(dynamic, 64)
     for (int64_t p = 0; p < (int64_t)width * height; p++) {
         int px = (int)(p % width), py = (int)(p / width);
         int tile = (py / tile_h) * tiles_x + px / tile_w;
@@ -772,7 +794,7 @@ EXPORT void orc_raster_bwd(int width, int height, int tile_w, int tile_h, int ca
             float dy = (float)py + 0.5f - mean[g * 2 + 1];
             float c00 = conic[g * 4], c01 = conic[g * 4 + 1], c10 = conic[g * 4 + 2],
                   c11 = conic[g * 4 + 3];
-            float exponent = -0.5f * (dx * (c00 * dx + c01 * dy) + dy * (c10 * dx + c11 * dy));
+            float exponent = power_of(conic + g * 4, dx, dy);
             if (!(exponent <= 0.0f)) continue;
             float e = expf(exponent);
             float raw = opacity[g] * e;
@@ -785,19 +807,19 @@ EXPORT void orc_raster_bwd(int width, int height, int tile_w, int tile_h, int ca
             float ga = T_before * (gw - gtrans);
             gtrans = a * gw + (1.0f - a) * gtrans;
             double* acc_g = acc + g * 11;
-            acc_g[6] += (double)w * g_d;
-            acc_g[7] += (double)w * g_r;
-            acc_g[8] += (double)w * g_g;
-            acc_g[9] += (double)w * g_b;
+            ACC_ADD(acc_g[6], (double)w * g_d);
+            ACC_ADD(acc_g[7], (double)w * g_r);
+            ACC_ADD(acc_g[8], (double)w * g_g);
+            ACC_ADD(acc_g[9], (double)w * g_b);
             if (raw < 255.0f / 256.0f) {
                 float ge = ga * raw;
-                acc_g[10] += (double)ga * e;
-                acc_g[0] += (double)ge * (c00 * dx + 0.5f * (c01 + c10) * dy);
-                acc_g[1] += (double)ge * (c11 * dy + 0.5f * (c01 + c10) * dx);
-                acc_g[2] += -0.5 * ge * dx * dx;
-                acc_g[3] += -0.5 * ge * dx * dy;
-                acc_g[4] += -0.5 * ge * dy * dx;
-                acc_g[5] += -0.5 * ge * dy * dy;
+                ACC_ADD(acc_g[10], (double)ga * e);
+                ACC_ADD(acc_g[0], (double)ge * (c00 * dx + 0.5f * (c01 + c10) * dy));
+                ACC_ADD(acc_g[1], (double)ge * (c11 * dy + 0.5f * (c01 + c10) * dx));
+                ACC_ADD(acc_g[2], -0.5 * ge * dx * dx);
+                ACC_ADD(acc_g[3], -0.5 * ge * dx * dy);
+                ACC_ADD(acc_g[4], -0.5 * ge * dy * dx);
+                ACC_ADD(acc_g[5], -0.5 * ge * dy * dy);
             }
             T_after = T_before;
         }

@@ -246,3 +246,63 @@ def cluster_compact(center, extent, valid, planes):
                                       _ptr(np.ascontiguousarray(valid, np.uint8)),
                                       _ptr(_f(planes)), _ptr(ids), _ptr(vis))
     return ids[:n], int(count), vis[:n].astype(bool)
+
+
+def clip_grad(image):
+    """d clip(x, 0, 1)/dx with jnp.maximum/minimum tie semantics (1/2 at a bound)."""
+    image = np.asarray(image, np.float32)
+    g = ((image > 0) & (image < 1)).astype(np.float32)
+    g[(image == 0) | (image == 1)] = 0.5
+    return g
+
+
+def training_step(pool, camera, target, *, degree, sh_dim, tile_w, tile_h, max_pairs,
+                  cluster_size=128, bounds=None, timings=None, clusters=None):
+    """Whole hot path of training/step.py:32-89 with the fp32 rasterizer of
+    kernels/sorted_rasterizer.py:165-236 (loss on clip(rgb, 0, 1)):
+    cluster cull -> compact projection -> binning -> raster -> loss -> raster
+    pullback -> projection pullback (compact, rgb_only, active SH only).
+
+    Returns dict(loss, grads (xyz, log_scale, rotation, opacity, sh) in
+    compact order, clusters (ids, count), table, fwd, proj).  timings, if a
+    dict, receives per-stage seconds; clusters overrides the culled list."""
+    import time
+
+    from jaxgs_b200.scene import world_cluster_bounds
+
+    W, H = camera.width, camera.height
+    clock = time.perf_counter
+    t0 = clock()
+    if bounds is None:
+        bounds = world_cluster_bounds(pool, cluster_size)
+    if clusters is None:
+        ids, count, _ = cluster_compact(*bounds, camera.frustum_planes())
+    else:
+        ids, count = np.asarray(clusters[0], np.int32), int(clusters[1])
+    t1 = clock()
+    proj = project_fwd(pool, camera, degree=degree, sh_dim=sh_dim, clusters=(ids, count),
+                       cluster_size=cluster_size, visible_color_only=True)
+    t2 = clock()
+    table = bin(proj, W, H, tile_w, tile_h, max_pairs)
+    t3 = clock()
+    fwd = raster_fwd(proj, table, W, H, tile_w, tile_h)
+    t4 = clock()
+    image = fwd["rgb"].reshape(H, W, 3)
+    value, grad = loss(np.clip(image, 0.0, 1.0), target)
+    grad = grad * clip_grad(image)
+    t5 = clock()
+    cot = raster_bwd(proj, table, fwd, grad.reshape(-1), W, H, tile_w, tile_h)
+    t6 = clock()
+    capacity = pool["xyz"].shape[0]
+    cot_full = dict(cot)
+    cot_full["depth"] = np.zeros(capacity, np.float32)
+    cot_full["radius"] = np.zeros(capacity, np.float32)
+    grads = project_bwd(pool, camera, proj["color"], cot_full, degree=degree, sh_dim=sh_dim,
+                        sh_gradient_dim=(degree + 1) ** 2, clusters=(ids, count),
+                        cluster_size=cluster_size, compact_gradients=True, rgb_only=True)
+    t7 = clock()
+    if timings is not None:
+        timings.update(cull=t1 - t0, project=t2 - t1, bin=t3 - t2, raster_fwd=t4 - t3,
+                       loss=t5 - t4, raster_bwd=t6 - t5, project_bwd=t7 - t6, total=t7 - t0)
+    return {"loss": value, "grads": grads, "clusters": (ids, count), "table": table, "fwd": fwd,
+            "proj": proj}
