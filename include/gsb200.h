@@ -159,6 +159,9 @@ typedef struct {
 } gsb_bin_params;
 
 GSB_API size_t gsb_bin_workspace_size(const gsb_bin_params* p);
+/* Stable tile-sort digit plan (passes, bits per digit) for keys below
+ * num_tiles: replaces kernels/pair_sort.py:33-37 (digit_plan).  Host-only. */
+GSB_API int gsb_tile_sort_plan(int64_t num_tiles, int* passes, int* bits);
 GSB_API int gsb_bin(gsb_stream_t stream, const gsb_bin_params* p, void* workspace,
             size_t workspace_bytes, const float* mean, const float* conic, const float* alpha,
             const float* depth, const int8_t* visible, int32_t* point_counts,

@@ -64,7 +64,7 @@ SYMBOLS = (
     "gsb_abi_version", "gsb_last_error", "gsb_launch_count",
     "gsb_cluster_compact_workspace_size", "gsb_cluster_compact",
     "gsb_project_fwd", "gsb_project_bwd",
-    "gsb_bin_workspace_size", "gsb_bin",
+    "gsb_bin_workspace_size", "gsb_tile_sort_plan", "gsb_bin",
     "gsb_raster_workspace_size", "gsb_raster_bit_words", "gsb_raster_fwd", "gsb_raster_bwd",
     "gsb_loss_workspace_size", "gsb_loss",
 )
@@ -87,6 +87,8 @@ def _load():
                  "gsb_raster_workspace_size", "gsb_raster_bit_words", "gsb_loss_workspace_size"):
         getattr(lib, name).restype = sz
         getattr(lib, name).argtypes = [vp]
+    lib.gsb_tile_sort_plan.restype = ctypes.c_int
+    lib.gsb_tile_sort_plan.argtypes = [ctypes.c_int64, vp, vp]
     lib.gsb_cluster_compact.restype = ctypes.c_int
     lib.gsb_cluster_compact.argtypes = [vp, vp, vp, sz] + [vp] * 7
     lib.gsb_project_fwd.restype = ctypes.c_int
@@ -126,3 +128,10 @@ def ref(struct) -> ctypes.c_void_p:
 def launch_count() -> int:
     """Kernels launched by libgsb200.so so far in this process."""
     return int(lib.gsb_launch_count())
+
+
+def tile_sort_plan(num_tiles: int) -> tuple[int, int]:
+    """(passes, digit bits) of the stable tile sort (kernels/pair_sort.py:33-37)."""
+    passes, bits = ctypes.c_int(0), ctypes.c_int(0)
+    check(lib.gsb_tile_sort_plan(num_tiles, ctypes.byref(passes), ctypes.byref(bits)), "tile_sort_plan")
+    return passes.value, bits.value

@@ -736,6 +736,14 @@ int tile_stage(cudaStream_t s, const gsb_bin_params& p, const BinLayout& L, int 
 
 using namespace gsb;
 
+extern "C" int gsb_tile_sort_plan(int64_t num_tiles, int* passes, int* bits)
+{
+    if (!passes || !bits) return GSB_ERR_NULL;
+    if (num_tiles <= 0) return GSB_ERR_INVALID;
+    digit_plan(num_tiles, *passes, *bits);
+    return GSB_OK;
+}
+
 extern "C" size_t gsb_bin_workspace_size(const gsb_bin_params* p)
 {
     if (!p) return 0;

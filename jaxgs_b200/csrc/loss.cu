@@ -7,14 +7,19 @@
 // blurred once more, grad = blur(p0) + 2x blur(p1) + y blur(p2)
 // + 0.8 sign(x - y) / (3HW).
 //
-// One CTA per 32x16 output tile and channel loop.  The CTA stages a 52x36
-// zero-padded patch of image and target (10-pixel halo), computes the five
-// window statistics over the 42x26 region whose partials the output needs
-// (separable: horizontal then vertical 11-tap passes in shared memory), the
-// partials and the loss there, then blurs the partials back onto the 32x16
-// tile.  The loss map and the partials never reach global memory.  Per-CTA
-// loss sums and |grad| maxima are reduced by a second, single-block kernel in
-// a fixed order, so the scalar results are deterministic.
+// One CTA per 32x16 output tile.  The CTA stages the 52x36 zero-padded patch
+// (10-pixel halo) of all three channels of image and target with coalesced
+// row loads, then per channel runs four separable 11-tap passes in shared
+// memory, each thread producing a run of consecutive outputs from one
+// sliding window held in registers:
+//   1. horizontal window sums of x, x^2, y, y^2, xy    (36 rows x 42 columns)
+//   2. vertical sums -> statistics -> SSIM partials, loss (26 x 42)
+//   3. horizontal blur of the partials                   (26 x 32)
+//   4. vertical blur -> image gradient                   (16 x 32)
+// The gradient tile is written back coalesced after the third channel.  The
+// loss map and the partials never reach global memory.  Per-CTA loss sums
+// and |grad| maxima are reduced by a single-block kernel in a fixed order, so
+// the scalar results are deterministic.
 #include "gsb_common.cuh"
 
 namespace gsb {
@@ -24,6 +29,12 @@ constexpr int kTW = 32, kTH = 16, kR = 5;
 constexpr int kSW = kTW + 2 * kR, kSH = kTH + 2 * kR;  // 42 x 26 statistics region
 constexpr int kPW = kSW + 2 * kR, kPH = kSH + 2 * kR;  // 52 x 36 staged patch
 constexpr int kThreads = 256;
+// Pass shapes: runs of consecutive outputs per thread.
+constexpr int kRunH = 6;   // pass 1: 42 = 7 x 6 columns, 36 rows -> 252 items
+constexpr int kRunV = 5;   // pass 2: 26 rows in 6 runs of 5, 42 columns -> 252 items
+constexpr int kRunHB = 4;  // pass 3: 32 = 8 x 4 columns, 26 rows -> 208 items
+constexpr int kRunVB = 2;  // pass 4: 16 = 8 x 2 rows, 32 columns -> 256 items
+constexpr int kHRows = 6 * kRunV + 2 * kR;  // 40 rows (4 padding rows feed discarded outputs)
 
 // exp(-(d/1.5)^2 / 2) normalised, correctly rounded to float32.
 __constant__ float kTaps[11] = {0.001028380123898387f, 0.0075987582094967365f,
@@ -34,11 +45,11 @@ __constant__ float kTaps[11] = {0.001028380123898387f, 0.0075987582094967365f,
                                 0.001028380123898387f};
 
 struct LossSmem {
-    float x[kPH][kPW];
-    float y[kPH][kPW];
-    float h[5][kPH][kSW];      // horizontal sums of x, x^2, y, y^2, xy
-    float part[3][kSH][kSW];   // p0, p1, p2
-    float hp[3][kSH][kTW + 1]; // horizontally blurred partials
+    float x[kPH][kPW * 3];        // image patch, HWC
+    float y[kPH][kPW * 3];        // target patch, HWC (normalised)
+    float h[5][kHRows][kSW];      // horizontal sums; reused for blurred partials
+    float part[3][kSH + 6][kSW];  // partials p0, p1, p2 (+ padding rows)
+    float g[kTH][kTW * 3];        // gradient tile, HWC
 };
 
 __device__ __forceinline__ float clip01(float v) { return fminf(fmaxf(v, 0.0f), 1.0f); }
@@ -61,124 +72,169 @@ __global__ void __launch_bounds__(kThreads) loss_kernel(int width, int height,
 {
     extern __shared__ float4 smem_raw[];
     LossSmem& S = *reinterpret_cast<LossSmem*>(smem_raw);
+    float(*hp)[kSH + 6][kTW + 1] = reinterpret_cast<float(*)[kSH + 6][kTW + 1]>(&S.h[0][0][0]);
     __shared__ float warp_loss[kThreads / 32];
     __shared__ uint32_t warp_scale[kThreads / 32];
     const int tid = threadIdx.x;
     const int x0 = blockIdx.x * kTW, y0 = blockIdx.y * kTH;
     const float inv_n = 1.0f / (3.0f * (float)width * (float)height);
     const float weight = -0.2f * inv_n;
-    float loss = 0.0f;
-    uint32_t scale_bits = 0;
     const uint8_t* t8 = static_cast<const uint8_t*>(target_raw);
     const float* tf = static_cast<const float*>(target_raw);
+
+    // Stage the zero-padded patch, all channels (rows are contiguous in HWC).
+    for (int k = tid; k < kPH * kPW * 3; k += kThreads) {
+        int r = k / (kPW * 3), q = k % (kPW * 3);
+        int gx = x0 - 2 * kR + q / 3, gy = y0 + r - 2 * kR;
+        float xv = 0.0f, yv = 0.0f;
+        if (gx >= 0 && gx < width && gy >= 0 && gy < height) {
+            int64_t idx = ((int64_t)gy * width + x0 - 2 * kR) * 3 + q;
+            xv = image[idx];
+            if (CLIP) xv = clip01(xv);
+            yv = U8 ? (float)t8[idx] * (float)(1.0 / 255.0) : tf[idx];
+        }
+        S.x[r][q] = xv;
+        S.y[r][q] = yv;
+    }
+    float loss = 0.0f;
     for (int c = 0; c < 3; c++) {
-        // 1. Stage the zero-padded patch.
-        for (int k = tid; k < kPH * kPW; k += kThreads) {
-            int r = k / kPW, q = k % kPW;
-            int gx = x0 + q - 2 * kR, gy = y0 + r - 2 * kR;
-            float xv = 0.0f, yv = 0.0f;
-            if (gx >= 0 && gx < width && gy >= 0 && gy < height) {
-                int64_t idx = ((int64_t)gy * width + gx) * 3 + c;
-                xv = image[idx];
-                if (CLIP) xv = clip01(xv);
-                yv = U8 ? (float)t8[idx] * (float)(1.0 / 255.0) : tf[idx];
-            }
-            S.x[r][q] = xv;
-            S.y[r][q] = yv;
-        }
         __syncthreads();
-        // 2. Horizontal window sums over the statistics columns.
-        for (int k = tid; k < kPH * kSW; k += kThreads) {
-            int r = k / kSW, q = k % kSW;
-            float sx = 0.f, sxx = 0.f, sy = 0.f, syy = 0.f, sxy = 0.f;
+        // 1. Horizontal window sums (run of kRunH columns per thread).
+        if (tid < kPH * (kSW / kRunH)) {
+            const int r = tid / (kSW / kRunH), q0 = (tid % (kSW / kRunH)) * kRunH;
+            float xs[kRunH + 10], ys[kRunH + 10];
 #pragma unroll
-            for (int t = 0; t < 11; t++) {
-                float w = kTaps[t], a = S.x[r][q + t], b = S.y[r][q + t];
-                sx += w * a;
-                sxx += w * a * a;
-                sy += w * b;
-                syy += w * b * b;
-                sxy += w * a * b;
+            for (int t = 0; t < kRunH + 10; t++) {
+                xs[t] = S.x[r][(q0 + t) * 3 + c];
+                ys[t] = S.y[r][(q0 + t) * 3 + c];
             }
-            S.h[0][r][q] = sx;
-            S.h[1][r][q] = sxx;
-            S.h[2][r][q] = sy;
-            S.h[3][r][q] = syy;
-            S.h[4][r][q] = sxy;
-        }
-        __syncthreads();
-        // 3. Vertical sums -> statistics -> SSIM partials and loss.
-        for (int k = tid; k < kSH * kSW; k += kThreads) {
-            int r = k / kSW, q = k % kSW;
-            float m[5] = {0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-            for (int t = 0; t < 11; t++) {
-                float w = kTaps[t];
-#pragma unroll
-                for (int s = 0; s < 5; s++) m[s] += w * S.h[s][r + t][q];
-            }
-            int gx = x0 + q - kR, gy = y0 + r - kR;
-            float p0 = 0.f, p1 = 0.f, p2 = 0.f;
-            if (gx >= 0 && gx < width && gy >= 0 && gy < height) {
-                float mx = m[0], xx = m[1], my = m[2], yy = m[3], xy = m[4];
-                float A = mx * mx + my * my + 1e-4f;
-                float B = (xx - mx * mx) + (yy - my * my) + 9e-4f;
-                float Cc = 2.0f * mx * my + 1e-4f;
-                float D = 2.0f * (xy - mx * my) + 9e-4f;
-                float inv_ab = 1.0f / (A * B);
-                float ssim = Cc * D * inv_ab;
-                p0 = (2.0f * my * (D - Cc) * inv_ab + 2.0f * mx * ssim * (1.0f / B - 1.0f / A)) * weight;
-                p1 = -ssim / B * weight;
-                p2 = 2.0f * Cc * inv_ab * weight;
-                if (r >= kR && r < kR + kTH && q >= kR && q < kR + kTW) {
-                    float xv = S.x[r + kR][q + kR], yv = S.y[r + kR][q + kR];
-                    loss += 0.2f * (1.0f - ssim) + 0.8f * fabsf(xv - yv);
-                }
-            }
-            S.part[0][r][q] = p0;
-            S.part[1][r][q] = p1;
-            S.part[2][r][q] = p2;
-        }
-        __syncthreads();
-        // 4. Horizontal blur of the partials onto the tile columns.
-        for (int k = tid; k < kSH * kTW; k += kThreads) {
-            int r = k / kTW, q = k % kTW;
-            float a = 0.f, b = 0.f, d = 0.f;
-#pragma unroll
-            for (int t = 0; t < 11; t++) {
-                float w = kTaps[t];
-                a += w * S.part[0][r][q + t];
-                b += w * S.part[1][r][q + t];
-                d += w * S.part[2][r][q + t];
-            }
-            S.hp[0][r][q] = a;
-            S.hp[1][r][q] = b;
-            S.hp[2][r][q] = d;
-        }
-        __syncthreads();
-        // 5. Vertical blur -> image gradient.
-        for (int k = tid; k < kTH * kTW; k += kThreads) {
-            int r = k / kTW, q = k % kTW;
-            int px = x0 + q, py = y0 + r;
-            if (px < width && py < height) {
-                float a = 0.f, b = 0.f, d = 0.f;
+            for (int o = 0; o < kRunH; o++) {
+                float sx = 0.f, sxx = 0.f, sy = 0.f, syy = 0.f, sxy = 0.f;
 #pragma unroll
                 for (int t = 0; t < 11; t++) {
-                    float w = kTaps[t];
-                    a += w * S.hp[0][r + t][q];
-                    b += w * S.hp[1][r + t][q];
-                    d += w * S.hp[2][r + t][q];
+                    const float w = kTaps[t], a = xs[o + t], b = ys[o + t];
+                    const float wa = w * a, wb = w * b;
+                    sx += wa;
+                    sxx = fmaf(wa, a, sxx);
+                    sy += wb;
+                    syy = fmaf(wb, b, syy);
+                    sxy = fmaf(wa, b, sxy);
                 }
-                float xv = S.x[r + 2 * kR][q + 2 * kR], yv = S.y[r + 2 * kR][q + 2 * kR];
-                float sign = xv > yv ? 1.0f : (xv < yv ? -1.0f : 0.0f);
-                float value = a + 2.0f * xv * b + yv * d + 0.8f * sign * inv_n;
-                int64_t idx = ((int64_t)py * width + px) * 3 + c;
-                if (CLIP) value *= clip_grad(image[idx]);
-                grad[idx] = value;
-                scale_bits = max(scale_bits, __float_as_uint(value) & 0x7fffffffu);
+                S.h[0][r][q0 + o] = sx;
+                S.h[1][r][q0 + o] = sxx;
+                S.h[2][r][q0 + o] = sy;
+                S.h[3][r][q0 + o] = syy;
+                S.h[4][r][q0 + o] = sxy;
             }
         }
         __syncthreads();
+        // 2. Vertical sums -> statistics -> partials and loss (run of kRunV rows).
+        if (tid < (kSH + kRunV - 1) / kRunV * kSW) {
+            const int q = tid % kSW, r0 = (tid / kSW) * kRunV;
+            float m[5][kRunV];
+#pragma unroll
+            for (int s = 0; s < 5; s++) {
+                float col[kRunV + 10];
+#pragma unroll
+                for (int t = 0; t < kRunV + 10; t++) col[t] = S.h[s][r0 + t][q];
+#pragma unroll
+                for (int o = 0; o < kRunV; o++) {
+                    float acc = 0.f;
+#pragma unroll
+                    for (int t = 0; t < 11; t++) acc = fmaf(kTaps[t], col[o + t], acc);
+                    m[s][o] = acc;
+                }
+            }
+            const int gx = x0 + q - kR;
+#pragma unroll
+            for (int o = 0; o < kRunV; o++) {
+                const int r = r0 + o;
+                const int gy = y0 + r - kR;
+                float p0 = 0.f, p1 = 0.f, p2 = 0.f;
+                if (r < kSH && gx >= 0 && gx < width && gy >= 0 && gy < height) {
+                    const float mx = m[0][o], xx = m[1][o], my = m[2][o], yy = m[3][o], xy = m[4][o];
+                    const float A = mx * mx + my * my + 1e-4f;
+                    const float B = (xx - mx * mx) + (yy - my * my) + 9e-4f;
+                    const float Cc = 2.0f * mx * my + 1e-4f;
+                    const float D = 2.0f * (xy - mx * my) + 9e-4f;
+                    const float inv_a = 1.0f / A, inv_b = 1.0f / B;
+                    const float inv_ab = inv_a * inv_b;
+                    const float ssim = Cc * D * inv_ab;
+                    p0 = (2.0f * my * (D - Cc) * inv_ab + 2.0f * mx * ssim * (inv_b - inv_a)) * weight;
+                    p1 = -ssim * inv_b * weight;
+                    p2 = 2.0f * Cc * inv_ab * weight;
+                    if (r >= kR && r < kR + kTH && q >= kR && q < kR + kTW) {
+                        const float xv = S.x[r + kR][(q + kR) * 3 + c];
+                        const float yv = S.y[r + kR][(q + kR) * 3 + c];
+                        loss += 0.2f * (1.0f - ssim) + 0.8f * fabsf(xv - yv);
+                    }
+                }
+                S.part[0][r][q] = p0;
+                S.part[1][r][q] = p1;
+                S.part[2][r][q] = p2;
+            }
+        }
+        __syncthreads();
+        // 3. Horizontal blur of the partials onto the tile columns.
+        if (tid < kSH * (kTW / kRunHB)) {
+            const int r = tid / (kTW / kRunHB), q0 = (tid % (kTW / kRunHB)) * kRunHB;
+#pragma unroll
+            for (int k = 0; k < 3; k++) {
+                float row[kRunHB + 10];
+#pragma unroll
+                for (int t = 0; t < kRunHB + 10; t++) row[t] = S.part[k][r][q0 + t];
+#pragma unroll
+                for (int o = 0; o < kRunHB; o++) {
+                    float acc = 0.f;
+#pragma unroll
+                    for (int t = 0; t < 11; t++) acc = fmaf(kTaps[t], row[o + t], acc);
+                    hp[k][r][q0 + o] = acc;
+                }
+            }
+        }
+        __syncthreads();
+        // 4. Vertical blur -> image gradient (run of kRunVB rows).
+        {
+            const int q = tid % kTW, r0 = (tid / kTW) * kRunVB;
+            float acc[3][kRunVB];
+#pragma unroll
+            for (int k = 0; k < 3; k++) {
+                float col[kRunVB + 10];
+#pragma unroll
+                for (int t = 0; t < kRunVB + 10; t++) col[t] = hp[k][r0 + t][q];
+#pragma unroll
+                for (int o = 0; o < kRunVB; o++) {
+                    float a = 0.f;
+#pragma unroll
+                    for (int t = 0; t < 11; t++) a = fmaf(kTaps[t], col[o + t], a);
+                    acc[k][o] = a;
+                }
+            }
+#pragma unroll
+            for (int o = 0; o < kRunVB; o++) {
+                const int r = r0 + o;
+                const float xv = S.x[r + 2 * kR][(q + 2 * kR) * 3 + c];
+                const float yv = S.y[r + 2 * kR][(q + 2 * kR) * 3 + c];
+                const float sign = xv > yv ? 1.0f : (xv < yv ? -1.0f : 0.0f);
+                S.g[r][q * 3 + c] = acc[0][o] + 2.0f * xv * acc[1][o] + yv * acc[2][o] +
+                                    0.8f * sign * inv_n;
+            }
+        }
+    }
+    __syncthreads();
+    // Coalesced write of the gradient tile (and its |max| for the scale).
+    uint32_t scale_bits = 0;
+    for (int k = tid; k < kTH * kTW * 3; k += kThreads) {
+        const int r = k / (kTW * 3), q = k % (kTW * 3);
+        const int px = x0 + q / 3, py = y0 + r;
+        if (px < width && py < height) {
+            const int64_t idx = ((int64_t)py * width + x0) * 3 + q;
+            float value = S.g[r][q];
+            if (CLIP) value *= clip_grad(image[idx]);
+            grad[idx] = value;
+            scale_bits = max(scale_bits, __float_as_uint(value) & 0x7fffffffu);
+        }
     }
     loss = warp_sum(loss);
 #pragma unroll
@@ -195,7 +251,7 @@ __global__ void __launch_bounds__(kThreads) loss_kernel(int width, int height,
             total += warp_loss[w];
             sb = max(sb, warp_scale[w]);
         }
-        int b = blockIdx.y * gridDim.x + blockIdx.x;
+        const int b = blockIdx.y * gridDim.x + blockIdx.x;
         block_loss[b] = total;
         block_scale[b] = sb;
     }
@@ -252,8 +308,8 @@ extern "C" size_t gsb_loss_workspace_size(const gsb_loss_params* p)
 }
 
 extern "C" int gsb_loss(gsb_stream_t stream, const gsb_loss_params* p, void* workspace,
-                        size_t workspace_bytes, const float* image, const void* target,
-                        float* loss, float* grad, float* scale)
+                        size_t workspace_bytes, const float* image, const void* target, float* loss,
+                        float* grad, float* scale)
 {
     if (!p) return GSB_ERR_NULL;
     if (p->width <= 0 || p->height <= 0) return GSB_ERR_INVALID;

@@ -3,11 +3,11 @@
 // One thread per compact index (128 per block).  The compact index i maps to
 // pool slot cluster_ids[i / cluster_size] * cluster_size + i % cluster_size
 // (kernels/projection.py:42-47), so a 128-slot cluster is one contiguous run
-// of 128 Gaussians.  The SH block (the bulk of the 236 B/Gaussian that the
-// pass reads) is staged through shared memory with coalesced 16-byte loads
-// and read back per thread; all other fields are per-thread loads whose warps
-// cover contiguous runs.  HBM-bound: 286 B/Gaussian forward, 524 B/Gaussian
-// backward.
+// of 128 Gaussians and every warp reads and writes contiguous runs.  The SH
+// rows (the bulk of the 236 B/Gaussian) move as 16-byte vectors per thread;
+// the SH degree is a template parameter so the basis and its derivatives are
+// straight-line code.  HBM-bound: 286 B/Gaussian forward, 524 B/Gaussian
+// backward (236 B with colour-only SH gradients).
 #include "gsb_common.cuh"
 
 namespace gsb {
@@ -47,54 +47,57 @@ __device__ __forceinline__ int64_t slot_of(int64_t i, int capacity, const int32_
     return s < capacity ? s : -1;
 }
 
-// Stage the SH prefix of the block's Gaussians: floats [0, width) of each
-// point's row, width a multiple of 4, into sh_s[point * (width + 4) + k]
-// (padding keeps 16-byte alignment and spreads banks).
-__device__ __forceinline__ void stage_sh(float* sh_s, const float* sh, int sh_row, int width,
-                                         const int64_t* slots)
+// SH basis values (LiteGS/3DGS real SH order, reference/sh.py:8-36).
+template <int DEGREE>
+__device__ __forceinline__ void sh_basis(float dx, float dy, float dz, float b[16])
 {
-    int vec = width / 4;
-    int stride = width + 4;
-    for (int k = threadIdx.x; k < kProjThreads * vec; k += kProjThreads) {
-        int point = k / vec, part = k % vec;
-        int64_t s = slots[point];
-        float4 val = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (s >= 0) {
-            const float* src = sh + s * sh_row + part * 4;
-            if ((sh_row & 3) == 0) {
-                val = __ldg(reinterpret_cast<const float4*>(src));
-            } else {
-                int valid = min(4, sh_row - part * 4);
-                float t[4] = {0.f, 0.f, 0.f, 0.f};
-                for (int q = 0; q < valid; q++) t[q] = __ldg(src + q);
-                val = make_float4(t[0], t[1], t[2], t[3]);
-            }
-        }
-        *reinterpret_cast<float4*>(sh_s + point * stride + part * 4) = val;
+    float xx = dx * dx, yy = dy * dy, zz = dz * dz;
+    b[0] = kC0;
+    if (DEGREE >= 1) {
+        b[1] = -kC1 * dy;
+        b[2] = kC1 * dz;
+        b[3] = -kC1 * dx;
+    }
+    if (DEGREE >= 2) {
+        b[4] = 1.0925484305920792f * dx * dy;
+        b[5] = -1.0925484305920792f * dy * dz;
+        b[6] = 0.31539156525252005f * (2.0f * zz - xx - yy);
+        b[7] = -1.0925484305920792f * dx * dz;
+        b[8] = 0.5462742152960396f * (xx - yy);
+    }
+    if (DEGREE >= 3) {
+        b[9] = -0.5900435899266435f * dy * (3.0f * xx - yy);
+        b[10] = 2.890611442640554f * dx * dy * dz;
+        b[11] = -0.4570457994644658f * dy * (4.0f * zz - xx - yy);
+        b[12] = 0.3731763325901154f * dz * (2.0f * zz - 3.0f * xx - 3.0f * yy);
+        b[13] = -0.4570457994644658f * dx * (4.0f * zz - xx - yy);
+        b[14] = 1.445305721320277f * dz * (xx - yy);
+        b[15] = -0.5900435899266435f * dx * (xx - 3.0f * yy);
     }
 }
 
-// SH colour, kernels/projection.py:142-171 (reference/sh.py:8-36).
-__device__ __forceinline__ float sh_channel(const float* c, int ch, int degree, float dx,
-                                            float dy, float dz, float xx, float yy, float zz)
+// Loads floats [0, N) of one Gaussian's SH row (row stride `row` floats):
+// 16-byte vector loads when the row and the base are 16-byte aligned.
+template <int N>
+__device__ __forceinline__ void load_sh(const float* __restrict__ sh, int64_t g, int row, bool vec,
+                                        float c[N])
 {
-    float value = kC0 * c[ch];
-    if (degree >= 1)
-        value += (-kC1 * dy * c[ch + 3] + kC1 * dz * c[ch + 6] - kC1 * dx * c[ch + 9]);
-    if (degree >= 2)
-        value += (1.0925484305920792f * dx * dy * c[ch + 12] - 1.0925484305920792f * dy * dz * c[ch + 15]
-                  + 0.31539156525252005f * (2.0f * zz - xx - yy) * c[ch + 18]
-                  - 1.0925484305920792f * dx * dz * c[ch + 21]
-                  + 0.5462742152960396f * (xx - yy) * c[ch + 24]);
-    if (degree >= 3)
-        value += (-0.5900435899266435f * dy * (3.0f * xx - yy) * c[ch + 27]
-                  + 2.890611442640554f * dx * dy * dz * c[ch + 30]
-                  - 0.4570457994644658f * dy * (4.0f * zz - xx - yy) * c[ch + 33]
-                  + 0.3731763325901154f * dz * (2.0f * zz - 3.0f * xx - 3.0f * yy) * c[ch + 36]
-                  - 0.4570457994644658f * dx * (4.0f * zz - xx - yy) * c[ch + 39]
-                  + 1.445305721320277f * dz * (xx - yy) * c[ch + 42]
-                  - 0.5900435899266435f * dx * (xx - 3.0f * yy) * c[ch + 45]);
-    return fmaxf(value + 0.5f, 0.0f);
+    const float* src = sh + g * row;
+    if (vec) {
+#pragma unroll
+        for (int k = 0; k < N / 4; k++) {
+            float4 v = __ldg(reinterpret_cast<const float4*>(src) + k);
+            c[4 * k] = v.x;
+            c[4 * k + 1] = v.y;
+            c[4 * k + 2] = v.z;
+            c[4 * k + 3] = v.w;
+        }
+#pragma unroll
+        for (int k = (N / 4) * 4; k < N; k++) c[k] = __ldg(src + k);
+    } else {
+#pragma unroll
+        for (int k = 0; k < N; k++) c[k] = __ldg(src + k);
+    }
 }
 
 struct Geometry {
@@ -158,6 +161,7 @@ __device__ __forceinline__ void geometry(Geometry& g, const Cam& cam, float wx, 
     g.d = g.b0 * g.b0 + g.b1 * g.b1 + g.b2 * g.b2 + 0.3f;
 }
 
+template <int DEGREE>
 __global__ void __launch_bounds__(kProjThreads) project_fwd_kernel(
     gsb_project_params p, const float* __restrict__ xyz, const float* __restrict__ log_scale,
     const float* __restrict__ rotation, const float* __restrict__ opacity,
@@ -167,27 +171,17 @@ __global__ void __launch_bounds__(kProjThreads) project_fwd_kernel(
     float* __restrict__ out_depth, float* __restrict__ out_conic, float* __restrict__ out_radius,
     float* __restrict__ out_color, float* __restrict__ out_alpha, int8_t* __restrict__ out_visible)
 {
-    extern __shared__ float4 smem4[];
-    float* sh_s = reinterpret_cast<float*>(smem4);
-    __shared__ int64_t slots[kProjThreads];
+    constexpr int NC = (DEGREE + 1) * (DEGREE + 1) * 3;
     int count = p.compacted ? __ldg(cluster_count) : 0;
-    int64_t first = (int64_t)blockIdx.x * kProjThreads;
-    if (p.compacted && first >= (int64_t)count * p.cluster_size) return;  // uniform per block
-    int64_t i = first + threadIdx.x;
+    int64_t i = (int64_t)blockIdx.x * kProjThreads + threadIdx.x;
     int64_t g = slot_of(i, p.capacity, cluster_ids, count, p.cluster_size, p.compacted);
-    slots[threadIdx.x] = g;
-    __syncthreads();
-    int used = (p.degree + 1) * (p.degree + 1) * 3;
-    int width = (used + 3) & ~3;
-    if (width > p.sh_dim * 3) width = (p.sh_dim * 3 + 3) & ~3;
-    stage_sh(sh_s, sh, p.sh_dim * 3, width, slots);
-    __syncthreads();
     if (g < 0) return;
-
+    const int row = p.sh_dim * 3;
+    const bool vec = (row & 3) == 0 && (reinterpret_cast<uintptr_t>(sh) & 15) == 0;
     Cam cam;
     load_cam(cam, view, intr, center);
     float wx = xyz[g * 3], wy = xyz[g * 3 + 1], wz = xyz[g * 3 + 2];
-    float4 q = *reinterpret_cast<const float4*>(rotation + g * 4);
+    float4 q = __ldg(reinterpret_cast<const float4*>(rotation + g * 4));
     Geometry geo;
     geometry(geo, cam, wx, wy, wz, q, log_scale[g * 3], log_scale[g * 3 + 1],
              log_scale[g * 3 + 2], p.near_plane);
@@ -207,22 +201,32 @@ __global__ void __launch_bounds__(kProjThreads) project_fwd_kernel(
                alpha >= (float)(1.0 / 255) && u >= -0.15f * W && u <= 1.15f * W &&
                v >= -0.15f * H && v <= 1.15f * H;
     out_visible[g] = vis ? 1 : 0;
-    float r = 0.0f, gr = 0.0f, bl = 0.0f;
+    float rgb[3] = {0.0f, 0.0f, 0.0f};
     if (!p.visible_color_only || vis) {
         float dx = wx - cam.c[0], dy = wy - cam.c[1], dz = wz - cam.c[2];
         float dn = rsqrtf(fmaxf(dx * dx + dy * dy + dz * dz, 1e-16f));
-        dx *= dn;
-        dy *= dn;
-        dz *= dn;
-        const float* c = sh_s + threadIdx.x * (width + 4);
-        float xx = dx * dx, yy = dy * dy, zz = dz * dz;
-        r = sh_channel(c, 0, p.degree, dx, dy, dz, xx, yy, zz);
-        gr = sh_channel(c, 1, p.degree, dx, dy, dz, xx, yy, zz);
-        bl = sh_channel(c, 2, p.degree, dx, dy, dz, xx, yy, zz);
+        float c[NC];
+        load_sh<NC>(sh, g, row, vec, c);
+        float bas[16];
+        sh_basis<DEGREE>(dx * dn, dy * dn, dz * dn, bas);
+#pragma unroll
+        for (int ch = 0; ch < 3; ch++) {
+            // kernels/projection.py:142-171 adds the bands in this grouping.
+            float value = bas[0] * c[ch];
+            if (DEGREE >= 1) value += (bas[1] * c[ch + 3] + bas[2] * c[ch + 6] + bas[3] * c[ch + 9]);
+            if (DEGREE >= 2)
+                value += (bas[4] * c[ch + 12] + bas[5] * c[ch + 15] + bas[6] * c[ch + 18] +
+                          bas[7] * c[ch + 21] + bas[8] * c[ch + 24]);
+            if (DEGREE >= 3)
+                value += (bas[9] * c[ch + 27] + bas[10] * c[ch + 30] + bas[11] * c[ch + 33] +
+                          bas[12] * c[ch + 36] + bas[13] * c[ch + 39] + bas[14] * c[ch + 42] +
+                          bas[15] * c[ch + 45]);
+            rgb[ch] = fmaxf(value + 0.5f, 0.0f);
+        }
     }
-    out_color[g * 3] = r;
-    out_color[g * 3 + 1] = gr;
-    out_color[g * 3 + 2] = bl;
+    out_color[g * 3] = rgb[0];
+    out_color[g * 3 + 1] = rgb[1];
+    out_color[g * 3 + 2] = rgb[2];
 }
 
 // kernels/projection.py:178-201 (_clear_projected) / :204-210 (_clear_visible).
@@ -244,7 +248,10 @@ __global__ void clear_projected_kernel(int64_t capacity, int clear_all, float* m
 
 // ---------------------------------------------------------------------------
 // Pullback: kernels/projection_backward.py:42-367.
+// SH_MODE: 0 = all sh_gradient_dim coefficients (bands above DEGREE zero),
+//          1 = colour cotangents only (sh_color_only, 3 floats per point).
 // ---------------------------------------------------------------------------
+template <int DEGREE, int SH_MODE>
 __global__ void __launch_bounds__(kProjThreads) project_bwd_kernel(
     gsb_project_bwd_params p, const float* __restrict__ xyz, const float* __restrict__ log_scale,
     const float* __restrict__ rotation, const float* __restrict__ opacity,
@@ -257,215 +264,206 @@ __global__ void __launch_bounds__(kProjThreads) project_bwd_kernel(
     float* __restrict__ out_log_scale, float* __restrict__ out_rotation,
     float* __restrict__ out_opacity, float* __restrict__ out_sh)
 {
-    extern __shared__ float4 smem4[];
-    __shared__ int64_t slots[kProjThreads];
+    constexpr int NB = (DEGREE + 1) * (DEGREE + 1);
     int count = p.compacted ? __ldg(cluster_count) : 0;
-    int64_t first = (int64_t)blockIdx.x * kProjThreads;
-    if (p.compacted && first >= (int64_t)count * p.cluster_size) return;  // uniform per block
-    int64_t i = first + threadIdx.x;
+    int64_t i = (int64_t)blockIdx.x * kProjThreads + threadIdx.x;
     int64_t g = slot_of(i, p.capacity, cluster_ids, count, p.cluster_size, p.compacted);
-    slots[threadIdx.x] = g;
-    __syncthreads();
-    const int used = (p.degree + 1) * (p.degree + 1) * 3;
-    int width = (used + 3) & ~3;
-    if (width > p.sh_dim * 3) width = (p.sh_dim * 3 + 3) & ~3;
-    const int shg = p.sh_gradient_dim * 3;
-    const int gstride = shg + 1;
-    float* sh_s = reinterpret_cast<float*>(smem4);                 // staged coefficients
-    float* gsh_s = sh_s + kProjThreads * (width + 4);               // transposed gradients
-    stage_sh(sh_s, sh, p.sh_dim * 3, width, slots);
-    __syncthreads();
-    int64_t o = p.compact_gradients ? i : g;
-    float* my_gsh = gsh_s + threadIdx.x * gstride;
-    for (int k = 0; k < shg; k++) my_gsh[k] = 0.0f;
+    if (g < 0) return;
+    const int64_t o = p.compact_gradients ? i : g;
+    const int shg = SH_MODE == 1 ? 3 : p.sh_gradient_dim * 3;
+    float* osh = out_sh + o * shg;
+    const bool vec_out = (shg & 3) == 0 && (reinterpret_cast<uintptr_t>(out_sh) & 15) == 0;
 
-    bool has = false;
-    if (g >= 0) {
-        has = galpha[g] != 0.0f;
-        if (!p.rgb_only) has = has || gdepth[g] != 0.0f || gradius[g] != 0.0f;
-        float2 gm = *reinterpret_cast<const float2*>(gmean + g * 2);
-        float4 gc = *reinterpret_cast<const float4*>(gconic + g * 4);
-        has = has || gm.x != 0.0f || gm.y != 0.0f || gc.x != 0.0f || gc.y != 0.0f ||
-              gc.z != 0.0f || gc.w != 0.0f || gcolor[g * 3] != 0.0f ||
-              gcolor[g * 3 + 1] != 0.0f || gcolor[g * 3 + 2] != 0.0f;
-        if (!has) {
-            for (int k = 0; k < 3; k++) out_xyz[o * 3 + k] = out_log_scale[o * 3 + k] = 0.0f;
-            *reinterpret_cast<float4*>(out_rotation + o * 4) = make_float4(0.f, 0.f, 0.f, 0.f);
-            out_opacity[o] = 0.0f;
-        }
-    }
-    if (has) {
-        Cam cam;
-        load_cam(cam, view, intr, center);
-        float wx = xyz[g * 3], wy = xyz[g * 3 + 1], wz = xyz[g * 3 + 2];
-        float4 q = *reinterpret_cast<const float4*>(rotation + g * 4);
-        Geometry geo;
-        geometry(geo, cam, wx, wy, wz, q, log_scale[g * 3], log_scale[g * 3 + 1],
-                 log_scale[g * 3 + 2], p.near_plane);
-        const float* v = cam.v;
-        float fx = cam.fx, fy = cam.fy;
-        float inv_z = 1.0f / geo.safe_z, inv_z2 = inv_z * inv_z;
-        float x = geo.x, y = geo.y;
-        float gmx = gmean[g * 2], gmy = gmean[g * 2 + 1];
-        float gx = gmx * fx * inv_z;
-        float gy = gmy * fy * inv_z;
-        float gz = p.rgb_only ? 0.0f : gdepth[g];
-        float gsafe_z = -gmx * fx * x * inv_z2;
-        gsafe_z -= gmy * fy * y * inv_z2;
-        float a = geo.a, b = geo.b, d = geo.d;
-        float raw_det = a * d - b * b;
-        float det = fmaxf(raw_det, 1e-8f);
-        float4 gcn = *reinterpret_cast<const float4*>(gconic + g * 4);
-        float gdet = 0.0f;
-        if (raw_det > 1e-8f) gdet = -(gcn.x * d - (gcn.y + gcn.z) * b + gcn.w * a) / (det * det);
-        float ga = gcn.w / det + gdet * d;
-        float gb = -(gcn.y + gcn.z) / det - 2.0f * b * gdet;
-        float gd = gcn.x / det + gdet * a;
-        if (!p.rgb_only) {
-            float disc = (a - d) * (a - d) + 4.0f * b * b;
-            float disc_root = sqrtf(fmaxf(disc, 1e-12f));
-            float eigen = 0.5f * (a + d + disc_root);
-            float geigen = gradius[g] * 1.5f / sqrtf(eigen);
-            float gdisc = disc > 1e-12f ? geigen * 0.25f / disc_root : 0.0f;
-            ga += 0.5f * geigen + 2.0f * (a - d) * gdisc;
-            gb += 8.0f * b * gdisc;
-            gd += 0.5f * geigen - 2.0f * (a - d) * gdisc;
-        }
-        const float* m = geo.m;
-        float ga0 = 2 * geo.a0 * ga + geo.b0 * gb, ga1 = 2 * geo.a1 * ga + geo.b1 * gb,
-              ga2 = 2 * geo.a2 * ga + geo.b2 * gb;
-        float gb0 = 2 * geo.b0 * gd + geo.a0 * gb, gb1 = 2 * geo.b1 * gd + geo.a1 * gb,
-              gb2 = 2 * geo.b2 * gd + geo.a2 * gb;
-        float gj0 = ga0 * m[0] + ga1 * m[1] + ga2 * m[2];
-        float gj1 = gb0 * m[3] + gb1 * m[4] + gb2 * m[5];
-        float gj2 = -(ga0 * m[6] + ga1 * m[7] + ga2 * m[8]);
-        float gj3 = -(gb0 * m[6] + gb1 * m[7] + gb2 * m[8]);
-        gx += gj2 * fx * inv_z2;
-        gy += gj3 * fy * inv_z2;
-        gsafe_z -= (gj0 * fx + gj1 * fy) * inv_z2;
-        gsafe_z -= 2.0f * (gj2 * fx * x + gj3 * fy * y) * inv_z2 * inv_z;
-        if (geo.z > p.near_plane) gz += gsafe_z;
-        float j0 = geo.j0, j1 = geo.j1, j2 = geo.j2, j3 = geo.j3;
-        float gm00 = j0 * ga0, gm01 = j0 * ga1, gm02 = j0 * ga2;
-        float gm10 = j1 * gb0, gm11 = j1 * gb1, gm12 = j1 * gb2;
-        float gm20 = -j2 * ga0 - j3 * gb0, gm21 = -j2 * ga1 - j3 * gb1, gm22 = -j2 * ga2 - j3 * gb2;
-        out_log_scale[o * 3] = gm00 * m[0] + gm10 * m[3] + gm20 * m[6];
-        out_log_scale[o * 3 + 1] = gm01 * m[1] + gm11 * m[4] + gm21 * m[7];
-        out_log_scale[o * 3 + 2] = gm02 * m[2] + gm12 * m[5] + gm22 * m[8];
-        float s0 = geo.s0, s1 = geo.s1, s2 = geo.s2;
-        float gr00 = s0 * (v[0] * gm00 + v[4] * gm10 + v[8] * gm20);
-        float gr10 = s0 * (v[1] * gm00 + v[5] * gm10 + v[9] * gm20);
-        float gr20 = s0 * (v[2] * gm00 + v[6] * gm10 + v[10] * gm20);
-        float gr01 = s1 * (v[0] * gm01 + v[4] * gm11 + v[8] * gm21);
-        float gr11 = s1 * (v[1] * gm01 + v[5] * gm11 + v[9] * gm21);
-        float gr21 = s1 * (v[2] * gm01 + v[6] * gm11 + v[10] * gm21);
-        float gr02 = s2 * (v[0] * gm02 + v[4] * gm12 + v[8] * gm22);
-        float gr12 = s2 * (v[1] * gm02 + v[5] * gm12 + v[9] * gm22);
-        float gr22 = s2 * (v[2] * gm02 + v[6] * gm12 + v[10] * gm22);
-        float qw = geo.qw, qx = geo.qx, qy = geo.qy, qz = geo.qz;
-        float gqw = -2 * qz * gr01 + 2 * qy * gr02 + 2 * qz * gr10 - 2 * qx * gr12 - 2 * qy * gr20 + 2 * qx * gr21;
-        float gqx = 2 * qy * (gr01 + gr10) + 2 * qz * (gr02 + gr20) - 4 * qx * (gr11 + gr22) - 2 * qw * gr12 + 2 * qw * gr21;
-        float gqy = -4 * qy * (gr00 + gr22) + 2 * qx * (gr01 + gr10) + 2 * qw * gr02 + 2 * qz * (gr12 + gr21) - 2 * qw * gr20;
-        float gqz = -4 * qz * (gr00 + gr11) - 2 * qw * gr01 + 2 * qx * (gr02 + gr20) + 2 * qw * gr10 + 2 * qy * (gr12 + gr21);
-        float qdenom = geo.qdenom;
-        float qdot = gqw * qw + gqx * qx + gqy * qy + gqz * qz;
-        if (qdenom > 1e-8f) {
-            gqw = (gqw - qdot * qw) / qdenom;
-            gqx = (gqx - qdot * qx) / qdenom;
-            gqy = (gqy - qdot * qy) / qdenom;
-            gqz = (gqz - qdot * qz) / qdenom;
+    const float2 gm = __ldg(reinterpret_cast<const float2*>(gmean + g * 2));
+    const float4 gcn = __ldg(reinterpret_cast<const float4*>(gconic + g * 4));
+    const float gc0 = gcolor[g * 3], gc1 = gcolor[g * 3 + 1], gc2 = gcolor[g * 3 + 2];
+    const float gal = galpha[g];
+    bool has = gal != 0.0f || gm.x != 0.0f || gm.y != 0.0f || gcn.x != 0.0f || gcn.y != 0.0f ||
+               gcn.z != 0.0f || gcn.w != 0.0f || gc0 != 0.0f || gc1 != 0.0f || gc2 != 0.0f;
+    if (!p.rgb_only) has = has || gdepth[g] != 0.0f || gradius[g] != 0.0f;
+    if (!has) {
+        // Occluded or culled splats: zero gradients (projection_backward.py:61-80).
+        out_xyz[o * 3] = out_xyz[o * 3 + 1] = out_xyz[o * 3 + 2] = 0.0f;
+        out_log_scale[o * 3] = out_log_scale[o * 3 + 1] = out_log_scale[o * 3 + 2] = 0.0f;
+        *reinterpret_cast<float4*>(out_rotation + o * 4) = make_float4(0.f, 0.f, 0.f, 0.f);
+        out_opacity[o] = 0.0f;
+        if (vec_out) {
+            for (int k = 0; k < shg / 4; k++)
+                reinterpret_cast<float4*>(osh)[k] = make_float4(0.f, 0.f, 0.f, 0.f);
         } else {
-            gqw /= qdenom;
-            gqx /= qdenom;
-            gqy /= qdenom;
-            gqz /= qdenom;
+            for (int k = 0; k < shg; k++) osh[k] = 0.0f;
         }
-        *reinterpret_cast<float4*>(out_rotation + o * 4) = make_float4(gqw, gqx, gqy, gqz);
-        float alpha = 1.0f / (1.0f + expf(-opacity[g]));
-        out_opacity[o] = galpha[g] * alpha * (1.0f - alpha);
+        return;
+    }
+    Cam cam;
+    load_cam(cam, view, intr, center);
+    const float wx = xyz[g * 3], wy = xyz[g * 3 + 1], wz = xyz[g * 3 + 2];
+    const float4 q = __ldg(reinterpret_cast<const float4*>(rotation + g * 4));
+    Geometry geo;
+    geometry(geo, cam, wx, wy, wz, q, log_scale[g * 3], log_scale[g * 3 + 1],
+             log_scale[g * 3 + 2], p.near_plane);
+    const float* v = cam.v;
+    const float fx = cam.fx, fy = cam.fy;
+    const float inv_z = 1.0f / geo.safe_z, inv_z2 = inv_z * inv_z;
+    const float x = geo.x, y = geo.y;
+    float gx = gm.x * fx * inv_z;
+    float gy = gm.y * fy * inv_z;
+    float gz = p.rgb_only ? 0.0f : gdepth[g];
+    float gsafe_z = -gm.x * fx * x * inv_z2;
+    gsafe_z -= gm.y * fy * y * inv_z2;
+    const float a = geo.a, b = geo.b, d = geo.d;
+    const float raw_det = a * d - b * b;
+    const float det = fmaxf(raw_det, 1e-8f);
+    float gdet = 0.0f;
+    if (raw_det > 1e-8f) gdet = -(gcn.x * d - (gcn.y + gcn.z) * b + gcn.w * a) / (det * det);
+    float ga = gcn.w / det + gdet * d;
+    float gb = -(gcn.y + gcn.z) / det - 2.0f * b * gdet;
+    float gd = gcn.x / det + gdet * a;
+    if (!p.rgb_only) {
+        float disc = (a - d) * (a - d) + 4.0f * b * b;
+        float disc_root = sqrtf(fmaxf(disc, 1e-12f));
+        float eigen = 0.5f * (a + d + disc_root);
+        float geigen = gradius[g] * 1.5f / sqrtf(eigen);
+        float gdisc = disc > 1e-12f ? geigen * 0.25f / disc_root : 0.0f;
+        ga += 0.5f * geigen + 2.0f * (a - d) * gdisc;
+        gb += 8.0f * b * gdisc;
+        gd += 0.5f * geigen - 2.0f * (a - d) * gdisc;
+    }
+    const float* m = geo.m;
+    float ga0 = 2 * geo.a0 * ga + geo.b0 * gb, ga1 = 2 * geo.a1 * ga + geo.b1 * gb,
+          ga2 = 2 * geo.a2 * ga + geo.b2 * gb;
+    float gb0 = 2 * geo.b0 * gd + geo.a0 * gb, gb1 = 2 * geo.b1 * gd + geo.a1 * gb,
+          gb2 = 2 * geo.b2 * gd + geo.a2 * gb;
+    float gj0 = ga0 * m[0] + ga1 * m[1] + ga2 * m[2];
+    float gj1 = gb0 * m[3] + gb1 * m[4] + gb2 * m[5];
+    float gj2 = -(ga0 * m[6] + ga1 * m[7] + ga2 * m[8]);
+    float gj3 = -(gb0 * m[6] + gb1 * m[7] + gb2 * m[8]);
+    gx += gj2 * fx * inv_z2;
+    gy += gj3 * fy * inv_z2;
+    gsafe_z -= (gj0 * fx + gj1 * fy) * inv_z2;
+    gsafe_z -= 2.0f * (gj2 * fx * x + gj3 * fy * y) * inv_z2 * inv_z;
+    if (geo.z > p.near_plane) gz += gsafe_z;
+    const float j0 = geo.j0, j1 = geo.j1, j2 = geo.j2, j3 = geo.j3;
+    float gm00 = j0 * ga0, gm01 = j0 * ga1, gm02 = j0 * ga2;
+    float gm10 = j1 * gb0, gm11 = j1 * gb1, gm12 = j1 * gb2;
+    float gm20 = -j2 * ga0 - j3 * gb0, gm21 = -j2 * ga1 - j3 * gb1, gm22 = -j2 * ga2 - j3 * gb2;
+    out_log_scale[o * 3] = gm00 * m[0] + gm10 * m[3] + gm20 * m[6];
+    out_log_scale[o * 3 + 1] = gm01 * m[1] + gm11 * m[4] + gm21 * m[7];
+    out_log_scale[o * 3 + 2] = gm02 * m[2] + gm12 * m[5] + gm22 * m[8];
+    const float s0 = geo.s0, s1 = geo.s1, s2 = geo.s2;
+    float gr00 = s0 * (v[0] * gm00 + v[4] * gm10 + v[8] * gm20);
+    float gr10 = s0 * (v[1] * gm00 + v[5] * gm10 + v[9] * gm20);
+    float gr20 = s0 * (v[2] * gm00 + v[6] * gm10 + v[10] * gm20);
+    float gr01 = s1 * (v[0] * gm01 + v[4] * gm11 + v[8] * gm21);
+    float gr11 = s1 * (v[1] * gm01 + v[5] * gm11 + v[9] * gm21);
+    float gr21 = s1 * (v[2] * gm01 + v[6] * gm11 + v[10] * gm21);
+    float gr02 = s2 * (v[0] * gm02 + v[4] * gm12 + v[8] * gm22);
+    float gr12 = s2 * (v[1] * gm02 + v[5] * gm12 + v[9] * gm22);
+    float gr22 = s2 * (v[2] * gm02 + v[6] * gm12 + v[10] * gm22);
+    const float qw = geo.qw, qx = geo.qx, qy = geo.qy, qz = geo.qz;
+    float gqw = -2 * qz * gr01 + 2 * qy * gr02 + 2 * qz * gr10 - 2 * qx * gr12 - 2 * qy * gr20 + 2 * qx * gr21;
+    float gqx = 2 * qy * (gr01 + gr10) + 2 * qz * (gr02 + gr20) - 4 * qx * (gr11 + gr22) - 2 * qw * gr12 + 2 * qw * gr21;
+    float gqy = -4 * qy * (gr00 + gr22) + 2 * qx * (gr01 + gr10) + 2 * qw * gr02 + 2 * qz * (gr12 + gr21) - 2 * qw * gr20;
+    float gqz = -4 * qz * (gr00 + gr11) - 2 * qw * gr01 + 2 * qx * (gr02 + gr20) + 2 * qw * gr10 + 2 * qy * (gr12 + gr21);
+    const float qdenom = geo.qdenom;
+    const float qdot = gqw * qw + gqx * qx + gqy * qy + gqz * qz;
+    if (qdenom > 1e-8f) {
+        gqw = (gqw - qdot * qw) / qdenom;
+        gqx = (gqx - qdot * qx) / qdenom;
+        gqy = (gqy - qdot * qy) / qdenom;
+        gqz = (gqz - qdot * qz) / qdenom;
+    } else {
+        gqw /= qdenom;
+        gqx /= qdenom;
+        gqy /= qdenom;
+        gqz /= qdenom;
+    }
+    *reinterpret_cast<float4*>(out_rotation + o * 4) = make_float4(gqw, gqx, gqy, gqz);
+    const float alpha = 1.0f / (1.0f + expf(-opacity[g]));
+    out_opacity[o] = gal * alpha * (1.0f - alpha);
 
-        float vx = wx - cam.c[0], vy = wy - cam.c[1], vz = wz - cam.c[2];
-        float dir_denom = sqrtf(fmaxf(vx * vx + vy * vy + vz * vz, 1e-16f));
-        float dx = vx / dir_denom, dy = vy / dir_denom, dz = vz / dir_denom;
-        float xx = dx * dx, yy = dy * dy, zz = dz * dz;
-        float gdx = 0.0f, gdy = 0.0f, gdz = 0.0f;
-        const float* c = sh_s + threadIdx.x * (width + 4);
-        const int degree = p.degree;
-        for (int ch = 0; ch < 3; ch++) {
-            float gc = color[g * 3 + ch] > 0.0f ? gcolor[g * 3 + ch] : 0.0f;
-            if (p.sh_color_only) {
-                my_gsh[ch] = gc;
-            } else {
-                my_gsh[ch] = gc * kC0;
-            }
-            if (degree >= 1) {
-                if (!p.sh_color_only) {
-                    my_gsh[3 + ch] = -gc * kC1 * dy;
-                    my_gsh[6 + ch] = gc * kC1 * dz;
-                    my_gsh[9 + ch] = -gc * kC1 * dx;
+    // SH: colour cotangents pass only where the colour was not clamped.
+    const float vx = wx - cam.c[0], vy = wy - cam.c[1], vz = wz - cam.c[2];
+    const float dir_denom = sqrtf(fmaxf(vx * vx + vy * vy + vz * vz, 1e-16f));
+    const float dx = vx / dir_denom, dy = vy / dir_denom, dz = vz / dir_denom;
+    float gcc[3];
+    gcc[0] = color[g * 3] > 0.0f ? gc0 : 0.0f;
+    gcc[1] = color[g * 3 + 1] > 0.0f ? gc1 : 0.0f;
+    gcc[2] = color[g * 3 + 2] > 0.0f ? gc2 : 0.0f;
+    if (SH_MODE == 1) {
+        osh[0] = gcc[0];
+        osh[1] = gcc[1];
+        osh[2] = gcc[2];
+    } else {
+        float bas[16];
+        sh_basis<DEGREE>(dx, dy, dz, bas);
+        const int nval = NB * 3;
+        if (vec_out) {
+            constexpr int kChunks = (NB * 3 + 3) / 4;
+#pragma unroll
+            for (int k = 0; k < kChunks; k++) {
+                float e[4];
+#pragma unroll
+                for (int t = 0; t < 4; t++) {
+                    const int c = 4 * k + t;
+                    e[t] = c < NB * 3 ? gcc[c % 3] * bas[c / 3] : 0.0f;
                 }
-                gdx -= gc * kC1 * c[ch + 9];
-                gdy -= gc * kC1 * c[ch + 3];
-                gdz += gc * kC1 * c[ch + 6];
+                reinterpret_cast<float4*>(osh)[k] = make_float4(e[0], e[1], e[2], e[3]);
             }
-            if (degree >= 2) {
-                if (!p.sh_color_only) {
-                    my_gsh[12 + ch] = gc * 1.0925484305920792f * dx * dy;
-                    my_gsh[15 + ch] = -gc * 1.0925484305920792f * dy * dz;
-                    my_gsh[18 + ch] = gc * 0.31539156525252005f * (2 * zz - xx - yy);
-                    my_gsh[21 + ch] = -gc * 1.0925484305920792f * dx * dz;
-                    my_gsh[24 + ch] = gc * 0.5462742152960396f * (xx - yy);
-                }
-                gdx += gc * (1.0925484305920792f * dy * c[ch + 12] - 0.6307831305050401f * dx * c[ch + 18] -
-                             1.0925484305920792f * dz * c[ch + 21] + 1.0925484305920792f * dx * c[ch + 24]);
-                gdy += gc * (1.0925484305920792f * dx * c[ch + 12] - 1.0925484305920792f * dz * c[ch + 15] -
-                             0.6307831305050401f * dy * c[ch + 18] - 1.0925484305920792f * dy * c[ch + 24]);
-                gdz += gc * (-1.0925484305920792f * dy * c[ch + 15] + 1.2615662610100802f * dz * c[ch + 18] -
-                             1.0925484305920792f * dx * c[ch + 21]);
-            }
-            if (degree >= 3) {
-                if (!p.sh_color_only) {
-                    my_gsh[27 + ch] = -gc * 0.5900435899266435f * dy * (3 * xx - yy);
-                    my_gsh[30 + ch] = gc * 2.890611442640554f * dx * dy * dz;
-                    my_gsh[33 + ch] = -gc * 0.4570457994644658f * dy * (4 * zz - xx - yy);
-                    my_gsh[36 + ch] = gc * 0.3731763325901154f * dz * (2 * zz - 3 * xx - 3 * yy);
-                    my_gsh[39 + ch] = -gc * 0.4570457994644658f * dx * (4 * zz - xx - yy);
-                    my_gsh[42 + ch] = gc * 1.445305721320277f * dz * (xx - yy);
-                    my_gsh[45 + ch] = -gc * 0.5900435899266435f * dx * (xx - 3 * yy);
-                }
-                gdx += gc * (-3.540261539559861f * dx * dy * c[ch + 27] + 2.890611442640554f * dy * dz * c[ch + 30] +
-                             0.9140915989289316f * dx * dy * c[ch + 33] - 2.2390579955406924f * dx * dz * c[ch + 36] -
-                             0.4570457994644658f * (4 * zz - 3 * xx - yy) * c[ch + 39] +
-                             2.890611442640554f * dx * dz * c[ch + 42] - 1.7701307697799305f * (xx - yy) * c[ch + 45]);
-                gdy += gc * (-1.7701307697799305f * (xx - yy) * c[ch + 27] + 2.890611442640554f * dx * dz * c[ch + 30] -
-                             0.4570457994644658f * (4 * zz - xx - 3 * yy) * c[ch + 33] -
-                             2.2390579955406924f * dy * dz * c[ch + 36] + 0.9140915989289316f * dx * dy * c[ch + 39] -
-                             2.890611442640554f * dy * dz * c[ch + 42] + 3.540261539559861f * dx * dy * c[ch + 45]);
-                gdz += gc * (2.890611442640554f * dx * dy * c[ch + 30] - 3.6563663957157264f * dy * dz * c[ch + 33] +
-                             0.3731763325901154f * (6 * zz - 3 * xx - 3 * yy) * c[ch + 36] -
-                             3.6563663957157264f * dx * dz * c[ch + 39] + 1.445305721320277f * (xx - yy) * c[ch + 42]);
-            }
+            for (int k = kChunks; k < shg / 4; k++)
+                reinterpret_cast<float4*>(osh)[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+        } else {
+#pragma unroll
+            for (int c = 0; c < nval; c++) osh[c] = gcc[c % 3] * bas[c / 3];
+            for (int c = nval; c < shg; c++) osh[c] = 0.0f;
         }
-        float dir_dot = gdx * dx + gdy * dy + gdz * dz;
-        float gxw = gdx / dir_denom, gyw = gdy / dir_denom, gzw = gdz / dir_denom;
-        if (dir_denom > 1e-8f) {
-            gxw = (gdx - dir_dot * dx) / dir_denom;
-            gyw = (gdy - dir_dot * dy) / dir_denom;
-            gzw = (gdz - dir_dot * dz) / dir_denom;
+    }
+    // Direction gradient: dot_k = sum_ch gc_ch * coef[k][ch], then the basis
+    // derivatives of projection_backward.py:259-330.
+    float gdx = 0.0f, gdy = 0.0f, gdz = 0.0f;
+    if (DEGREE >= 1) {
+        float cf[NB * 3];
+        load_sh<NB * 3>(sh, g, p.sh_dim * 3,
+                        ((p.sh_dim * 3) & 3) == 0 && (reinterpret_cast<uintptr_t>(sh) & 15) == 0, cf);
+        float dot[16];
+#pragma unroll
+        for (int k = 0; k < NB; k++) dot[k] = gcc[0] * cf[3 * k] + gcc[1] * cf[3 * k + 1] + gcc[2] * cf[3 * k + 2];
+        const float xx = dx * dx, yy = dy * dy, zz = dz * dz;
+        gdx -= kC1 * dot[3];
+        gdy -= kC1 * dot[1];
+        gdz += kC1 * dot[2];
+        if (DEGREE >= 2) {
+            gdx += 1.0925484305920792f * dy * dot[4] - 0.6307831305050401f * dx * dot[6] -
+                   1.0925484305920792f * dz * dot[7] + 1.0925484305920792f * dx * dot[8];
+            gdy += 1.0925484305920792f * dx * dot[4] - 1.0925484305920792f * dz * dot[5] -
+                   0.6307831305050401f * dy * dot[6] - 1.0925484305920792f * dy * dot[8];
+            gdz += -1.0925484305920792f * dy * dot[5] + 1.2615662610100802f * dz * dot[6] -
+                   1.0925484305920792f * dx * dot[7];
         }
-        out_xyz[o * 3] = v[0] * gx + v[4] * gy + v[8] * gz + gxw;
-        out_xyz[o * 3 + 1] = v[1] * gx + v[5] * gy + v[9] * gz + gyw;
-        out_xyz[o * 3 + 2] = v[2] * gx + v[6] * gy + v[10] * gz + gzw;
+        if (DEGREE >= 3) {
+            gdx += -3.540261539559861f * dx * dy * dot[9] + 2.890611442640554f * dy * dz * dot[10] +
+                   0.9140915989289316f * dx * dy * dot[11] - 2.2390579955406924f * dx * dz * dot[12] -
+                   0.4570457994644658f * (4 * zz - 3 * xx - yy) * dot[13] +
+                   2.890611442640554f * dx * dz * dot[14] - 1.7701307697799305f * (xx - yy) * dot[15];
+            gdy += -1.7701307697799305f * (xx - yy) * dot[9] + 2.890611442640554f * dx * dz * dot[10] -
+                   0.4570457994644658f * (4 * zz - xx - 3 * yy) * dot[11] -
+                   2.2390579955406924f * dy * dz * dot[12] + 0.9140915989289316f * dx * dy * dot[13] -
+                   2.890611442640554f * dy * dz * dot[14] + 3.540261539559861f * dx * dy * dot[15];
+            gdz += 2.890611442640554f * dx * dy * dot[10] - 3.6563663957157264f * dy * dz * dot[11] +
+                   0.3731763325901154f * (6 * zz - 3 * xx - 3 * yy) * dot[12] -
+                   3.6563663957157264f * dx * dz * dot[13] + 1.445305721320277f * (xx - yy) * dot[14];
+        }
     }
-    // Coalesced write of the transposed SH gradients (projection_backward.py:342-367).
-    __syncthreads();
-    for (int k = threadIdx.x; k < kProjThreads * shg; k += kProjThreads) {
-        int point = k / shg, coef = k % shg;
-        int64_t slot = slots[point];
-        if (slot < 0) continue;
-        int64_t out_point = p.compact_gradients ? first + point : slot;
-        out_sh[out_point * shg + coef] = gsh_s[point * gstride + coef];
+    const float dir_dot = gdx * dx + gdy * dy + gdz * dz;
+    float gxw = gdx / dir_denom, gyw = gdy / dir_denom, gzw = gdz / dir_denom;
+    if (dir_denom > 1e-8f) {
+        gxw = (gdx - dir_dot * dx) / dir_denom;
+        gyw = (gdy - dir_dot * dy) / dir_denom;
+        gzw = (gdz - dir_dot * dz) / dir_denom;
     }
+    out_xyz[o * 3] = v[0] * gx + v[4] * gy + v[8] * gz + gxw;
+    out_xyz[o * 3 + 1] = v[1] * gx + v[5] * gy + v[9] * gz + gyw;
+    out_xyz[o * 3 + 2] = v[2] * gx + v[6] * gy + v[10] * gz + gzw;
 }
 
 // kernels/projection_backward.py:370-390 (_clear_parameter_grads).
@@ -539,11 +537,6 @@ __global__ void expand_slots_kernel(int64_t capacity, int cluster_size, const ui
     if (i < capacity) slots[i] = cluster_vis[i / cluster_size];
 }
 
-size_t project_smem(int width_floats, int shg)
-{
-    return (size_t)kProjThreads * (width_floats + 4) * sizeof(float) +
-           (size_t)kProjThreads * (shg + 1) * sizeof(float);
-}
 
 }  // namespace
 }  // namespace gsb
@@ -575,14 +568,18 @@ extern "C" int gsb_project_fwd(gsb_stream_t stream, const gsb_project_params* p,
             p->capacity, p->clear_invisible, mean, depth, conic, radius, color, alpha, visible);
         if (int e = check_launch()) return e;
     }
-    int used = (p->degree + 1) * (p->degree + 1) * 3;
-    int width = (used + 3) & ~3;
-    if (width > p->sh_dim * 3) width = (p->sh_dim * 3 + 3) & ~3;
-    size_t smem = (size_t)kProjThreads * (width + 4) * sizeof(float);
     int blocks = ceil_div(p->capacity, kProjThreads);
-    project_fwd_kernel<<<blocks, kProjThreads, smem, s>>>(
-        *p, xyz, log_scale, rotation, opacity, sh, alive, view, intrinsics, center, cluster_ids,
-        cluster_count, mean, depth, conic, radius, color, alpha, visible);
+#define GSB_PROJ_FWD(D)                                                                          \
+    project_fwd_kernel<D><<<blocks, kProjThreads, 0, s>>>(                                       \
+        *p, xyz, log_scale, rotation, opacity, sh, alive, view, intrinsics, center, cluster_ids, \
+        cluster_count, mean, depth, conic, radius, color, alpha, visible)
+    switch (p->degree) {
+        case 0: GSB_PROJ_FWD(0); break;
+        case 1: GSB_PROJ_FWD(1); break;
+        case 2: GSB_PROJ_FWD(2); break;
+        default: GSB_PROJ_FWD(3); break;
+    }
+#undef GSB_PROJ_FWD
     return check_launch();
 }
 
@@ -622,20 +619,28 @@ extern "C" int gsb_project_bwd(gsb_stream_t stream, const gsb_project_bwd_params
                                                             grotation, gopacity, gsh);
         if (int e = check_launch()) return e;
     }
-    int used = (p->degree + 1) * (p->degree + 1) * 3;
-    int width = (used + 3) & ~3;
-    if (width > p->sh_dim * 3) width = (p->sh_dim * 3 + 3) & ~3;
-    size_t smem = project_smem(width, shg);
-    static bool configured = false;
-    if (!configured) {
-        cudaFuncSetAttribute(project_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             96 * 1024);
-        configured = true;
+    int blocks = ceil_div(p->capacity, kProjThreads);
+#define GSB_PROJ_BWD(D, M)                                                                        \
+    project_bwd_kernel<D, M><<<blocks, kProjThreads, 0, s>>>(                                     \
+        *p, xyz, log_scale, rotation, opacity, sh, view, intrinsics, center, color, cluster_ids,  \
+        cluster_count, gmean, gdepth, gconic, gradius, gcolor, galpha, gxyz, glog_scale,          \
+        grotation, gopacity, gsh)
+    if (p->sh_color_only) {
+        switch (p->degree) {
+            case 0: GSB_PROJ_BWD(0, 1); break;
+            case 1: GSB_PROJ_BWD(1, 1); break;
+            case 2: GSB_PROJ_BWD(2, 1); break;
+            default: GSB_PROJ_BWD(3, 1); break;
+        }
+    } else {
+        switch (p->degree) {
+            case 0: GSB_PROJ_BWD(0, 0); break;
+            case 1: GSB_PROJ_BWD(1, 0); break;
+            case 2: GSB_PROJ_BWD(2, 0); break;
+            default: GSB_PROJ_BWD(3, 0); break;
+        }
     }
-    project_bwd_kernel<<<ceil_div(p->capacity, kProjThreads), kProjThreads, smem, s>>>(
-        *p, xyz, log_scale, rotation, opacity, sh, view, intrinsics, center, color, cluster_ids,
-        cluster_count, gmean, gdepth, gconic, gradius, gcolor, galpha, gxyz, glog_scale,
-        grotation, gopacity, gsh);
+#undef GSB_PROJ_BWD
     return check_launch();
 }
 

@@ -316,9 +316,9 @@ def rasterize_backward(projected: ProjectedGaussians, table: SortedVisibilityTab
 # ---------------------------------------------------------------------------
 def _fused_loss(prediction: torch.Tensor, target: torch.Tensor, with_scale: bool,
                 clip_input: bool = False):
-    _require_cuda(prediction, "fused loss")
     if prediction.ndim != 3 or prediction.shape[2] != 3 or tuple(target.shape) != tuple(prediction.shape):
         raise ValueError("L1+SSIM expects matching HWC RGB images")
+    _require_cuda(prediction, "fused loss")
     H, W, _ = prediction.shape
     dev = prediction.device
     u8 = target.dtype == torch.uint8

@@ -1,0 +1,74 @@
+"""libgsb200.so loads without a GPU, exports every symbol include/gsb200.h
+declares, and rejects bad parameters before any CUDA call (the reference
+raises ValueError before launch: kernels/projector.py:46-47,
+packed_rasterizer.py:52-53, fused_loss.py:361-362)."""
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+from jaxgs_b200 import _lib as L
+
+HEADER = Path(__file__).resolve().parents[1] / "include" / "gsb200.h"
+
+
+def declared_symbols():
+    text = HEADER.read_text()
+    return sorted(set(re.findall(r"GSB_API\s+[\w\s\*]+?\b(gsb_\w+)\s*\(", text)))
+
+
+def test_every_declared_symbol_is_exported():
+    names = declared_symbols()
+    assert len(names) >= 14
+    for name in names:
+        assert hasattr(L.lib, name), name
+    assert set(names) == set(L.SYMBOLS)
+
+
+def test_abi_version_and_launch_counter():
+    assert L.lib.gsb_abi_version() == 1
+    assert L.launch_count() >= 0
+
+
+def _code(fn, *args):
+    return fn(*args)
+
+
+def test_invalid_parameters_are_rejected_before_launch():
+    vp = None
+    bad_bin = L.BinParams(10, 64, 48, 0, 8, 100)  # tile_w 0
+    assert L.lib.gsb_bin(vp, L.ref(bad_bin), vp, 0, *([vp] * 10)) == 1
+    big = L.BinParams(10, 64, 48, 16, 8, 1 << 31)  # arena >= 2^31
+    assert L.lib.gsb_bin(vp, L.ref(big), vp, 0, *([vp] * 10)) == 1
+    ok = L.BinParams(10, 64, 48, 16, 8, 100)
+    assert L.lib.gsb_bin_workspace_size(L.ref(ok)) > 0
+    assert L.lib.gsb_bin(vp, L.ref(ok), vp, 0, *([vp] * 10)) == 2  # no workspace
+    proj = L.ProjectParams(10, 16, 4, 64, 48, 0.2, 1000.0, 128, 0, 1, 0)  # degree 4
+    assert L.lib.gsb_project_fwd(vp, L.ref(proj), *([vp] * 18)) == 1
+    proj = L.ProjectParams(10, 4, 2, 64, 48, 0.2, 1000.0, 128, 0, 1, 0)  # (2+1)^2 > sh_dim
+    assert L.lib.gsb_project_fwd(vp, L.ref(proj), *([vp] * 18)) == 1
+    proj = L.ProjectParams(10, 16, 3, 64, 48, 0.2, 1000.0, 128, 0, 1, 0)
+    assert L.lib.gsb_project_fwd(vp, L.ref(proj), *([vp] * 18)) == 4  # NULL pointers
+    bwd = L.ProjectBwdParams(10, 16, 2, 3, 0.2, 128, 1, 1, 1, 1)  # colour-only needs 1
+    assert L.lib.gsb_project_bwd(vp, L.ref(bwd), *([vp] * 22)) == 1
+    rast = L.RasterParams(10, 64, 48, 12, 8, 100)  # tile width not a multiple of 8
+    assert L.lib.gsb_raster_fwd(vp, L.ref(rast), vp, 0, *([vp] * 17)) == 1
+    assert L.lib.gsb_raster_bit_words(L.ref(rast)) == 0
+    rast = L.RasterParams(10, 64, 48, 16, 8, 100)
+    assert L.lib.gsb_raster_bit_words(L.ref(rast)) == (100 // 32 + 4 * 6 + 1) * 2
+    loss = L.LossParams(0, 5, 1, 0)
+    assert L.lib.gsb_loss(vp, L.ref(loss), vp, 0, *([vp] * 5)) == 1
+    assert L.lib.gsb_bin(vp, None, vp, 0, *([vp] * 10)) == 4
+
+
+def test_python_bindings_refuse_cpu_tensors():
+    torch = pytest.importorskip("torch")
+    from jaxgs_b200 import kernels as K
+
+    with pytest.raises(RuntimeError, match="no CPU fallback"):
+        K.fused_loss_and_grad(torch.zeros(4, 4, 3), torch.zeros(4, 4, 3))
+    with pytest.raises(ValueError, match="HWC"):
+        # shape errors come first, as in kernels/fused_loss.py:361-362
+        K.fused_loss_and_grad(torch.zeros(4, 4, 2), torch.zeros(4, 4, 2))

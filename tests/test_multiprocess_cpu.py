@@ -1,0 +1,98 @@
+"""View-sharded gradient summation on two CPU ranks (gloo), and failure
+detection on the host: a rank that never joins makes the collective of the
+other rank fail with a timeout instead of hanging."""
+
+import os
+import socket
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+import torch.distributed as dist  # noqa: E402
+import torch.multiprocessing as mp  # noqa: E402
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _sum_worker(rank, world, port, out):
+    from datetime import timedelta
+
+    from jaxgs_b200.scene import CapacityConfig
+    from jaxgs_b200.step import scatter_compact
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=30))
+    config = CapacityConfig(max_gaussians=1000, cluster_size=128, sh_degree=1)
+    rng = np.random.default_rng(rank)
+    ids = np.sort(rng.choice(8, 5, replace=False)).astype(np.int32)
+    clusters = (torch.as_tensor(ids), torch.tensor([5], dtype=torch.int32))
+    grads = [torch.as_tensor(rng.normal(0, 1, (1000, k)).astype(np.float32)) for k in (3, 3, 4, 1, 12)]
+    pool = scatter_compact(grads, clusters, config)
+    flat = torch.cat([t.reshape(-1) for t in pool])
+    dist.all_reduce(flat)
+    out[rank] = flat.numpy()
+    dist.destroy_process_group()
+
+
+def _expected(world):
+    from jaxgs_b200.scene import CapacityConfig
+
+    total = None
+    for rank in range(world):
+        rng = np.random.default_rng(rank)
+        ids = np.sort(rng.choice(8, 5, replace=False))
+        grads = [rng.normal(0, 1, (1000, k)).astype(np.float32) for k in (3, 3, 4, 1, 12)]
+        parts = []
+        for g in grads:
+            dst = np.zeros_like(g)
+            for j, c in enumerate(ids):
+                lo, hi = c * 128, min(c * 128 + 128, 1000)
+                if lo < hi:
+                    dst[lo:hi] += g[j * 128:j * 128 + (hi - lo)]
+            parts.append(dst.reshape(-1))
+        flat = np.concatenate(parts)
+        total = flat if total is None else total + flat
+    return total
+
+
+def test_view_sharded_gradients_sum_across_ranks():
+    world = 2
+    port = _free_port()
+    with mp.Manager() as manager:
+        out = manager.dict()
+        mp.spawn(_sum_worker, args=(world, port, out), nprocs=world, join=True)
+        results = [out[r] for r in range(world)]
+    exp = _expected(world)
+    for r in results:
+        np.testing.assert_allclose(r, exp, rtol=1e-6, atol=1e-6)
+
+
+def _missing_rank_worker(rank, world, port, out):
+    from datetime import timedelta
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=3))
+    if rank == 1:
+        # This rank leaves between steps without entering the collective.
+        out[rank] = "left"
+        return
+    try:
+        dist.all_reduce(torch.ones(4))
+        out[rank] = "completed"
+    except Exception as exc:  # the collective must fail, not hang
+        out[rank] = f"error: {type(exc).__name__}"
+
+
+def test_a_rank_that_never_joins_is_detected_by_timeout():
+    world = 2
+    port = _free_port()
+    with mp.Manager() as manager:
+        out = manager.dict()
+        mp.spawn(_missing_rank_worker, args=(world, port, out), nprocs=world, join=True)
+        assert out[1] == "left"
+        assert out[0].startswith("error"), out[0]

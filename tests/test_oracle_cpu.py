@@ -1,0 +1,318 @@
+"""The CPU oracle, pinned (no GPU needed).
+
+1. Known answers transcribed from the reference's own tests
+   (tests/golden/known_answers.json, cited per case).
+2. The oracle's forward values and analytic gradients against an independent
+   PyTorch-autograd restatement of the reference's JAX numerics
+   (tests/torch_ref.py): projection, compositing, L1+SSIM.
+3. Binning self-consistency properties the reference tests for its GPU
+   binning (tests/test_work_balance.py:89-160, test_cute.py:67-107).
+4. Golden fixtures of the oracle itself (tests/golden/oracle_small.npz,
+   made by tests/golden/make_golden.py) so that an oracle change is noticed.
+"""
+
+import json
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+from jaxgs_b200.scene import (Camera, CapacityConfig, config0_scene, create_gaussians,
+                              seed_gaussians)
+from oracle import oracle as O
+from tests import torch_ref as R
+from tests.helpers import known_answer_three, rel_l2, splats
+
+GOLDEN = Path(__file__).resolve().parent / "golden"
+
+
+# ---------------------------------------------------------------------------
+# 1. Known answers of the reference's tests
+# ---------------------------------------------------------------------------
+def _known():
+    return json.loads((GOLDEN / "known_answers.json").read_text())
+
+
+def test_known_answer_three_gaussians():
+    ka = _known()["three_gaussians"]
+    config, cam, pool = known_answer_three()
+    proj = O.project_fwd(pool, cam, degree=0, sh_dim=1)
+    t = O.bin(proj, 8, 8, 4, 4, 16)
+    np.testing.assert_array_equal(np.diff(t["tile_offsets"]), ka["diff_offsets"])
+    np.testing.assert_array_equal(t["gaussian_ids"][:12].reshape(4, 3), ka["ids_per_tile"])
+    assert t["pair_count"] == ka["pair_count"] and t["overflow"] == ka["overflow"]
+    narrow = O.bin(proj, 8, 8, 4, 4, 4)
+    assert narrow["overflow"] == ka["narrow_overflow"]
+
+
+def test_known_answer_large_ellipse_and_empty():
+    ka = _known()["large_ellipse"]
+    cam = Camera.from_colmap([1, 0, 0, 0], [0, 0, 0], 20, 20, 8, 9, 17, 19)
+    pool = seed_gaussians(create_gaussians(CapacityConfig(1, 1, 1, 16, 0, 4)),
+                          np.array([[0, 0, 2.0]]), np.ones((1, 3)) * 0.5, scale=0.2, opacity=0.5)
+    proj = O.project_fwd(pool, cam, degree=0, sh_dim=1)
+    proj["conic"] = np.array([1e-5, 0, 0, 1e-5], np.float32)
+    t = O.bin(proj, 17, 19, 16, 16, 4)
+    assert t["pair_count"] == ka["pair_count"] and t["overflow"] == ka["overflow"]
+    proj["visible"][:] = 0
+    e = O.bin(proj, 17, 19, 16, 16, 4)
+    assert e["pair_count"] == 0 and (e["tile_offsets"] == 0).all()
+
+
+@pytest.mark.parametrize("tiles_x", [255, 256])
+def test_known_answer_tile_key_width(tiles_x):
+    ka = _known()["tile_key_width"]
+    width, height = tiles_x * 8, 256 * 8
+    cam = Camera.from_colmap([1, 0, 0, 0], [0, 0, 0], 20, 20, width - 4, height - 4, width, height)
+    pool = seed_gaussians(create_gaussians(CapacityConfig(1, 1, 1, 8, 0, 4)),
+                          np.array([[0.0, 0.0, 2.0]]), np.full((1, 3), 0.5), scale=0.02, opacity=0.5)
+    t = O.bin(O.project_fwd(pool, cam, degree=0, sh_dim=1), width, height, 8, 8, 4)
+    assert t["pair_count"] == ka["pair_count"]
+    assert (t["tile_offsets"][:-1] == 0).all() and t["tile_offsets"][-1] == ka["last_offset"]
+    assert t["gaussian_ids"][0] == ka["first_id"]
+
+
+def test_known_answer_digit_plan_of_the_c_library():
+    from jaxgs_b200 import _lib
+
+    for num_tiles, expected in _known()["digit_plan"]:
+        assert _lib.tile_sort_plan(num_tiles) == tuple(expected)
+
+
+def test_identical_images_have_zero_loss():
+    """tests/test_loss.py:9-12."""
+    for value in (0.0, 0.5, 1.0):
+        image = np.full((8, 8, 3), value, np.float32)
+        loss, grad = O.loss(image, image)
+        assert abs(loss) < 1e-7 and np.abs(grad).max() < 1e-7
+
+
+def test_log_is_within_two_ulp_and_monotone():
+    """The binning's project-written log (CUDA's logf is specified to 1 ulp;
+    AccuTile only needs a fixed, shared rounding)."""
+    rng = np.random.default_rng(0)
+    xs = np.concatenate([np.float32(np.exp(rng.uniform(-87, 88, 20000))),
+                         np.float32(2.0) ** np.arange(-126, 127, dtype=np.float32),
+                         np.float32([1.0, 255.0, 1 / 255.0, 0.70710677, 1.4142135, 1e-40, 3e-45])])
+    mine = np.array([O.gs_logf(float(x)) for x in xs], np.float64)
+    ref = np.log(xs.astype(np.float64))
+    ulp = np.abs(mine - ref) / np.spacing(np.abs(ref).astype(np.float32)).astype(np.float64)
+    ulp[ref == 0] = np.abs(mine[ref == 0]) / np.spacing(np.float32(0))
+    assert ulp.max() <= 2.0, ulp.max()
+    grid = np.float32(np.linspace(1 / 255, 255, 5000))
+    vals = np.array([O.gs_logf(float(x)) for x in grid])
+    assert (np.diff(vals) >= 0).all()
+
+
+# ---------------------------------------------------------------------------
+# 2. Oracle vs an independent autograd restatement
+# ---------------------------------------------------------------------------
+def _small_pool(n=300, seed=1):
+    pool_np, cam, target = config0_scene()
+    sel = np.random.default_rng(seed).choice(4096, n, replace=False)
+    return {k: v[sel].copy() for k, v in pool_np.items()}, cam, target
+
+
+@pytest.mark.parametrize("degree", [0, 1, 2, 3])
+def test_oracle_projection_matches_torch_restatement(degree):
+    pool, cam, _ = _small_pool()
+    exp = O.project_fwd(pool, cam, degree=degree, sh_dim=16)
+    t = {k: torch.as_tensor(v, dtype=torch.float64) for k, v in pool.items() if k != "alive"}
+    mean, z, conic, radius, color, alpha, vis = R.project(t["xyz"], t["log_scale"], t["rotation"],
+                                                          t["opacity"], t["sh"],
+                                                          torch.as_tensor(pool["alive"]), cam, degree)
+    np.testing.assert_allclose(exp["mean"], mean.numpy().reshape(-1), rtol=1e-4, atol=1e-4)
+    np.testing.assert_allclose(exp["conic"], conic.numpy().reshape(-1), rtol=1e-3, atol=1e-5)
+    np.testing.assert_allclose(exp["radius"], radius.numpy(), rtol=1e-4, atol=1e-4)
+    np.testing.assert_allclose(exp["color"], color.numpy().reshape(-1), rtol=1e-4, atol=1e-5)
+    np.testing.assert_allclose(exp["alpha"], alpha.numpy(), rtol=1e-5, atol=1e-7)
+    np.testing.assert_array_equal(exp["visible"].astype(bool), vis.numpy())
+
+
+@pytest.mark.parametrize("degree", [1, 3])
+def test_oracle_projection_pullback_matches_autograd(degree):
+    """kernels/projection_backward.py vs autograd of render/projection.py
+    (the reference's own check is tests/test_cute.py:393-435, 3e-3)."""
+    pool, cam, _ = _small_pool(200, seed=4)
+    rng = np.random.default_rng(6)
+    n = pool["xyz"].shape[0]
+    w = {"mean": rng.normal(0, 1, (n, 2)), "depth": rng.normal(0, 1, n),
+         "conic": rng.normal(0, 1, (n, 2, 2)), "radius": rng.normal(0, 0.1, n),
+         "color": rng.normal(0, 1, (n, 3)), "alpha": rng.normal(0, 1, n)}
+    params = [torch.tensor(pool[k], dtype=torch.float64, requires_grad=True)
+              for k in ("xyz", "log_scale", "rotation", "opacity", "sh")]
+    out = R.project(*params, torch.as_tensor(pool["alive"]), cam, degree)
+    names = ("mean", "depth", "conic", "radius", "color", "alpha")
+    total = sum((o * torch.as_tensor(w[k])).sum() for k, o in zip(names, out[:6]))
+    total.backward()
+    proj = O.project_fwd(pool, cam, degree=degree, sh_dim=16)
+    cot = {k: np.asarray(w[k], np.float32).reshape(-1) for k in names}
+    grads = O.project_bwd(pool, cam, proj["color"], cot, degree=degree, sh_dim=16)
+    for name, got, p in zip(("xyz", "log_scale", "rotation", "opacity", "sh"), grads, params):
+        ref = p.grad.numpy().reshape(-1)
+        if name == "sh":
+            ref = ref.reshape(n, 16, 3)
+            ref[:, (degree + 1) ** 2:] = 0
+            ref = ref.reshape(-1)
+        assert rel_l2(got, ref) < 1e-4, (name, rel_l2(got, ref))
+
+
+def _dense_case(seed=0, count=40, width=23, height=19):
+    rng = np.random.default_rng(seed)
+    proj = splats(rng, count, width, height, radius=(1.0, 6.0), alpha=(0.2, 0.99))
+    proj["visible"][:] = 1
+    proj["depth"] = np.arange(count, dtype=np.float32)  # distinct depths -> order by id
+    return proj
+
+
+def _dense_table(count, W, H, tw, th):
+    """Every splat listed in every tile in depth (= id) order, so compositing
+    is compared without the binning's 1/255-level tile selection (the
+    reference's test makes every ellipse cover every tile for the same reason,
+    tests/test_cute.py:237-239)."""
+    tiles = (-(-W // tw)) * (-(-H // th))
+    return {"gaussian_ids": np.tile(np.arange(count, dtype=np.int32), tiles),
+            "tile_offsets": (np.arange(tiles + 1) * count).astype(np.int32)}
+
+
+@pytest.mark.parametrize("tile", [(8, 16), (16, 16), (4, 8)])
+def test_oracle_compositing_matches_dense_reference(tile):
+    """Sorted compositing == dense compositing with the early stop
+    (tests/test_cute.py:216-282 makes the same comparison)."""
+    th, tw = tile
+    W, H = 23, 19
+    proj = _dense_case()
+    table = _dense_table(len(proj["alpha"]), W, H, tw, th)
+    bg = np.array([0.12, 0.24, 0.36], np.float32)
+    fwd = O.raster_fwd(proj, table, W, H, tw, th, bg)
+    t = lambda a, s: torch.as_tensor(a, dtype=torch.float64).reshape(s)
+    c = len(proj["alpha"])
+    rgb, depth, alpha = R.dense_composite(t(proj["mean"], (c, 2)), t(proj["conic"], (c, 2, 2)),
+                                          t(proj["color"], (c, 3)), t(proj["alpha"], (c,)),
+                                          t(proj["depth"], (c,)), torch.arange(c), W, H, bg)
+    ok = fwd["ambiguous"] == 0
+    np.testing.assert_allclose(fwd["rgb"].reshape(-1, 3)[ok], rgb.numpy().reshape(-1, 3)[ok], atol=2e-5, rtol=2e-4)
+    np.testing.assert_allclose(fwd["alpha"][ok], alpha.numpy().reshape(-1)[ok], atol=2e-5)
+    np.testing.assert_allclose(fwd["depth"][ok], depth.numpy().reshape(-1)[ok], atol=2e-4, rtol=2e-4)
+
+
+def test_oracle_compositing_pullback_matches_autograd():
+    W, H = 23, 19
+    proj = _dense_case(seed=2)
+    table = _dense_table(len(proj["alpha"]), W, H, 16, 8)
+    bg = np.array([0.1, 0.2, 0.3], np.float32)
+    fwd = O.raster_fwd(proj, table, W, H, 16, 8, bg)
+    rng = np.random.default_rng(8)
+    drgb = rng.normal(0, 1, (H, W, 3))
+    ddepth = rng.normal(0, 0.1, (H, W))
+    dalpha = rng.normal(0, 0.5, (H, W))
+    c = len(proj["alpha"])
+    leaves = {k: torch.tensor(np.asarray(proj[k], np.float64).reshape(s), requires_grad=True)
+              for k, s in (("mean", (c, 2)), ("conic", (c, 2, 2)), ("color", (c, 3)),
+                           ("alpha", (c,)), ("depth", (c,)))}
+    rgb, depth, alpha = R.dense_composite(leaves["mean"], leaves["conic"], leaves["color"],
+                                          leaves["alpha"], leaves["depth"], torch.arange(c), W, H, bg)
+    total = ((rgb * torch.as_tensor(drgb)).sum() + (depth * torch.as_tensor(ddepth)).sum()
+             + (alpha * torch.as_tensor(dalpha)).sum())
+    total.backward()
+    exp = O.raster_bwd(proj, table, fwd, drgb.reshape(-1), W, H, 16, 8, bg,
+                       ddepth.reshape(-1), dalpha.reshape(-1))
+    for name in ("mean", "conic", "color", "alpha", "depth"):
+        got = exp[name]
+        ref = leaves[name].grad.numpy().reshape(-1)
+        assert rel_l2(got, ref) < 1e-3, (name, rel_l2(got, ref))
+
+
+@pytest.mark.parametrize("shape", [(3, 5), (17, 31), (40, 33)])
+def test_oracle_loss_matches_autograd(shape):
+    """Fused loss value and gradient == autograd of reference/loss.py
+    (tests/test_loss.py:15-32 uses rtol 2e-5 / 2e-4)."""
+    rng = np.random.default_rng(41)
+    pred = rng.uniform(0.02, 0.98, shape + (3,)).astype(np.float32)
+    tgt = rng.uniform(0.02, 0.98, shape + (3,)).astype(np.float32)
+    x = torch.tensor(pred, dtype=torch.float64, requires_grad=True)
+    ref = R.photometric_loss(x, torch.as_tensor(tgt, dtype=torch.float64))
+    ref.backward()
+    loss, grad = O.loss(pred, tgt)
+    np.testing.assert_allclose(loss, float(ref), rtol=2e-6)
+    np.testing.assert_allclose(grad, x.grad.numpy(), rtol=2e-4, atol=1e-7)
+
+
+def test_oracle_loss_uint8_target_equals_normalised_float():
+    rng = np.random.default_rng(42)
+    tgt = rng.integers(0, 256, (9, 11, 3), dtype=np.uint8)
+    pred = rng.uniform(0, 1, (9, 11, 3)).astype(np.float32)
+    a = O.loss(pred, tgt)
+    b = O.loss(pred, tgt.astype(np.float32) * np.float32(1.0 / 255.0))
+    assert a[0] == b[0]
+    np.testing.assert_array_equal(a[1], b[1])
+
+
+# ---------------------------------------------------------------------------
+# 3. Binning properties (reference GPU-binning tests, applied to the oracle)
+# ---------------------------------------------------------------------------
+@pytest.mark.parametrize("tile", [(8, 16), (16, 16)])
+def test_oracle_binning_properties(tile):
+    th, tw = tile
+    rng = np.random.default_rng(3)
+    W, H = 640, 360
+    proj = splats(rng, 2048, W, H, radius=(0.4, 60.0), huge=8)
+    t = O.bin(proj, W, H, tw, th, 1 << 19)
+    counts = t["point_counts"]
+    total = t["pair_count"]
+    assert total == counts.sum() and t["tile_offsets"][-1] == total
+    tiles = (-(-W // tw)) * (-(-H // th))
+    ids = t["gaussian_ids"][:total]
+    tile_of = np.repeat(np.arange(tiles), np.diff(t["tile_offsets"]))
+    # ranges == searchsorted of the sorted tile keys (tests/test_cute.py:102)
+    np.testing.assert_array_equal(t["tile_offsets"], np.searchsorted(tile_of, np.arange(tiles + 1)))
+    # every Gaussian appears exactly point_counts times, pairs unique
+    np.testing.assert_array_equal(np.bincount(ids, minlength=len(counts)), counts)
+    assert np.unique(ids.astype(np.int64) * tiles + tile_of).size == total
+    # (tile, depth, id) order inside each tile
+    same = tile_of[1:] == tile_of[:-1]
+    d = proj["depth"][ids]
+    assert (np.diff(d)[same] >= 0).all()
+    tie = same & (np.diff(d) == 0)
+    assert (np.diff(ids)[tie] > 0).all()
+    # the per-Gaussian tile lists agree with the sequential walk
+    for g in np.flatnonzero(counts)[:200]:
+        keys, n = O.gaussian_tiles(*proj["mean"][2 * g:2 * g + 2], proj["conic"][4 * g],
+                                   proj["conic"][4 * g + 1], proj["conic"][4 * g + 3],
+                                   proj["alpha"][g], tw, th, -(-W // tw), -(-H // th))
+        assert n == counts[g]
+        assert set(keys.tolist()) == set(tile_of[ids == g].tolist())
+
+
+def test_oracle_keeps_the_reference_tile_range_formula():
+    """AccuTile's last tile row/column is int((max + tile - 1) / tile)
+    (kernels/sorted_visibility.py:96-97), an integer ceiling applied to a
+    fractional extent: an ellipse that reaches less than one pixel past a tile
+    boundary does not bin into the next tile even when a pixel centre there
+    has alpha >= 1/255.  Bit-exact binning keeps that behaviour."""
+    rng = np.random.default_rng(5)
+    proj = splats(rng, 300, 96, 64, radius=(0.5, 12.0), alpha=(0.01, 0.99))
+    g = 5
+    m, c, a = proj["mean"][2 * g:2 * g + 2], proj["conic"][4 * g:4 * g + 4], proj["alpha"][g]
+    keys, n = O.gaussian_tiles(m[0], m[1], c[0], c[1], c[3], a, 16, 8, 6, 8)
+    assert sorted(keys.tolist()) == [4, 9, 10] and n == 3
+    ys, xs = np.mgrid[16:24, 48:64]
+    d = np.stack([xs + 0.5 - m[0], ys + 0.5 - m[1]], -1).astype(np.float64)
+    q = np.einsum("...i,ij,...j->...", d, c.astype(np.float64).reshape(2, 2), d)
+    assert (a * np.exp(-0.5 * q)).max() > 1.0 / 255  # tile 15 holds such a pixel
+
+
+# ---------------------------------------------------------------------------
+# 4. Golden fixtures of the oracle
+# ---------------------------------------------------------------------------
+def test_oracle_matches_committed_golden_fixtures():
+    from tests.golden.make_golden import compute
+
+    data = np.load(GOLDEN / "oracle_small.npz")
+    now = compute()
+    for key in data.files:
+        if data[key].dtype.kind in "iub":
+            np.testing.assert_array_equal(now[key], data[key], err_msg=key)
+        else:
+            np.testing.assert_allclose(now[key], data[key], rtol=1e-5, atol=1e-6, err_msg=key)
