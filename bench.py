@@ -91,7 +91,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
-                 "--format=csv,noheader,nounits", "-lms", "100"],
+                 "--format=csv,noheader,nounits", "-lms", "10"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
@@ -146,7 +146,7 @@ def run_ours(args) -> None:
     from jaxgs_b200 import _lib
     from jaxgs_b200 import kernels as K
     from jaxgs_b200.scene import world_cluster_bounds
-    from jaxgs_b200.step import compute_training_step, scatter_compact
+    from jaxgs_b200.step import GraphedTrainingStep, compute_training_step, scatter_compact
     from jaxgs_b200.types import DeviceCamera, GaussianArrays
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -176,28 +176,49 @@ def run_ours(args) -> None:
         pool_grads = [torch.zeros_like(t) for t in (pool.xyz, pool.log_scale, pool.rotation,
                                                   pool.opacity, pool.sh)]
     stream = torch.cuda.current_stream()
-    kernel_events = []
+    stage_events = []
 
-    def step(cam, tgt, record=False):
+    def eager_step(cam, tgt, record=False):
         events = {} if record else None
         out = compute_training_step(pool, bounds, cam, tgt, config, degree, stage_events=events)
+        if record:
+            stage_events.append(events)
+        return out
+
+    def exchange(out):
+        """View-sharded gradient sum (one NCCL all-reduce per step)."""
         if world > 1:
             for t in pool_grads:
                 t.zero_()
             scatter_compact(out.gradients, out.visible_clusters, config, out=pool_grads)
             flat = torch.cat([t.reshape(-1) for t in pool_grads])
             dist.all_reduce(flat)
-        if record:
-            kernel_events.append(events)
-        return out
 
-    # Warm-up.
+    # Eager warm-up and the per-stage breakdown (events around each stage on
+    # the launching stream; the dominant kernel's time comes from here).
     for _ in range(max(args.warmup, 0)):
-        out = step(dcam, target)
+        out = eager_step(dcam, target)
+        exchange(out)
+    for _ in range(args.steps):
+        out = eager_step(dcam, target, record=True)
+        exchange(out)
     torch.cuda.synchronize()
+    stage_ms = {}
+    for events in stage_events:
+        for name, (a, b) in events.items():
+            stage_ms.setdefault(name, []).append(a.elapsed_time(b))
+    stage_ms = {k: statistics.mean(v) for k, v in stage_ms.items()}
     pairs = int(out.pair_count.item())
     overflow = bool(out.overflow.item())
     visible_clusters = int(out.visible_clusters[1].item())
+    binned = int((out.point_counts > 0).sum().item())
+
+    # The product step: captured once as a CUDA graph, replayed per view.
+    graphed = GraphedTrainingStep(pool, bounds, dcam, target, config, degree)
+    for _ in range(max(args.warmup, 0)):
+        out = graphed()
+        exchange(out)
+    torch.cuda.synchronize()
 
     # Device-resident timed region.
     sampler = ClockSampler(local)
@@ -210,37 +231,31 @@ def run_ours(args) -> None:
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     start.record(stream)
     for _ in range(args.steps):
-        out = step(dcam, target, record=True)
+        out = graphed()
+        exchange(out)
     end.record(stream)
     torch.cuda.synchronize()
-    launches = _lib.launch_count() - launches0
+    eager_launches = _lib.launch_count() - launches0
     if world > 1:
         dist.barrier()
     clocks = sampler.stop()
     elapsed = start.elapsed_time(end) / 1e3
-    stage_ms = {}
-    for events in kernel_events:
-        for name, (a, b) in events.items():
-            stage_ms.setdefault(name, []).append(a.elapsed_time(b))
-    stage_ms = {k: statistics.mean(v) for k, v in stage_ms.items()}
+    launches = eager_launches + graphed.launches_per_step * args.steps
 
-    # End-to-end through the public API from pinned host buffers.
-    e2e_loss = torch.empty(args.steps, dtype=torch.float32).pin_memory()
-    tgt_dev = torch.empty_like(target)
-    cam_dev = [torch.empty_like(t) for t in (dcam.world_to_camera, dcam.intrinsics, dcam.center,
-                                             dcam.planes)]
+    # End-to-end through the public API from pinned host buffers: each step
+    # copies the camera arrays and the uint8 target to the device and reads
+    # the loss back.
+    e2e_loss = torch.empty(max(args.steps, 1), dtype=torch.float32).pin_memory()
+    host_cam = DeviceCamera(cam_host[0], cam_host[1], cam_host[2], cam_host[3], camera.width,
+                            camera.height, camera.near, camera.far)
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
     e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e_start.record(stream)
     for i in range(0 if args.no_e2e else args.steps):
-        tgt_dev.copy_(target_host, non_blocking=True)
-        for d, h in zip(cam_dev, cam_host):
-            d.copy_(h, non_blocking=True)
-        cam = DeviceCamera(cam_dev[0], cam_dev[1], cam_dev[2], cam_dev[3], camera.width,
-                           camera.height, camera.near, camera.far)
-        out = step(cam, tgt_dev)
+        out = graphed(host_cam, target_host)
+        exchange(out)
         e2e_loss[i].copy_(out.loss, non_blocking=True)
     e_end.record(stream)
     torch.cuda.synchronize()
@@ -256,8 +271,6 @@ def run_ours(args) -> None:
     if rank == 0:
         views = world * args.steps
         value = views / elapsed
-        # Roofline of the dominant kernel: the raster backward is timed with
-        # events around its call (zero + order + main kernel), see DESIGN.md.
         peak, peak_kind = _peaks()
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world,
@@ -268,26 +281,64 @@ def run_ours(args) -> None:
             "config": {"workload": "BASELINE config 2: 1M-Gaussian training step, 1237x822, 8x16 tiles, SH3",
                        "gaussians": 1_000_000, "width": 1237, "height": 822, "tile": "8x16",
                        "views_per_gpu_per_step": 1, "pairs": pairs, "overflow": overflow,
-                       "visible_clusters": visible_clusters,
+                       "visible_clusters": visible_clusters, "binned_gaussians": binned,
                        "l2": "inputs larger than L2 (236 MB pool)",
+                       "launch": "CUDA graph replay of the whole step",
                        "parallelism": f"view-sharded dp{world}" if world > 1 else "single view"},
-            "e2e": {"value": None if args.no_e2e else round(world * args.steps / e2e_elapsed, 2), "unit": UNIT,
-                    "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": d2h},
+            "e2e": {"value": None if args.no_e2e else round(world * args.steps / e2e_elapsed, 2),
+                    "unit": UNIT, "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": d2h},
             "gpu_launches": int(launches),
             "clocks": clocks,
             "stage_ms": {k: round(v, 4) for k, v in stage_ms.items()},
-            "roofline_peak_source": peak_kind,
         }
-        line.update(_roofline_fields(stage_ms, peak, peak_kind, pairs))
+        line["roofline"] = _roofline(stage_ms, peak, peak_kind, pairs, binned)
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(pool_np, camera, target.cpu().numpy())
         print(json.dumps(line), flush=True)
     if world > 1:
+        del graphed
         dist.destroy_process_group()
 
 
-def _roofline_fields(stage_ms, peak, peak_kind, pairs):
-    return {"roofline": None}
+def _profile_value(name: str, key: str):
+    """A figure recorded in a committed ncu summary (profiles/<name>.md,
+    line `key: value`), or None."""
+    path = ROOT / "profiles" / f"{name}.md"
+    if not path.exists():
+        return None
+    for line in path.read_text().splitlines():
+        if line.strip().startswith(key + ":"):
+            try:
+                return float(line.split(":", 1)[1].strip().split()[0])
+            except ValueError:
+                return None
+    return None
+
+
+def _roofline(stage_ms, peak, peak_kind, pairs, binned):
+    """Roofline of the dominant kernel, the fp32 raster backward.
+
+    Algorithmic bytes per launch (the minimum traffic the pass needs): per
+    pixel final T, last index and dL/drgb (20 B); per pair of the table its
+    id and 48-byte splat record (52 B); per binned Gaussian the ten f32
+    cotangents it accumulates (40 B, read + write via L2 atomics counted
+    once).  The kernel is issue-bound (SIMT), not HBM-bound: the fraction
+    says how far it is from the copy roofline, the `simt` entry gives the
+    issue-slot figures from the committed profile.
+    """
+    ms = stage_ms.get("raster_bwd")
+    if not ms:
+        return None
+    pixels = 1237 * 822
+    algo = pixels * 20 + pairs * 52 + binned * 40
+    achieved = algo / (ms * 1e-3) / 1e9
+    traffic = _profile_value("raster_bwd_config2", "dram_bytes_per_launch")
+    return {"kernel": "raster_bwd (zero + order + main kernel, one call)", "bound": "hbm",
+            "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+            "frac": round(achieved / peak, 4), "traffic": traffic,
+            "algorithmic_bytes": int(algo), "peak_source": peak_kind,
+            "simt": {"issue_active_pct": _profile_value("raster_bwd_config2", "issue_active_pct"),
+                     "fp32_pipe_pct": _profile_value("raster_bwd_config2", "fma_pipe_pct")}}
 
 
 def cpu_baseline(pool_np, camera, target, budget_s: float = 30.0) -> dict:
@@ -348,8 +399,8 @@ def run_reference(args) -> None:
 def main() -> None:
     parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     parser.add_argument("--gpus", type=int, default=1)
-    parser.add_argument("--steps", type=int, default=20)
-    parser.add_argument("--warmup", type=int, default=5)
+    parser.add_argument("--steps", type=int, default=100)
+    parser.add_argument("--warmup", type=int, default=10)
     parser.add_argument("--impl", choices=["ours", "reference"], default="ours")
     parser.add_argument("--no-cpu-baseline", action="store_true",
                         help="skip the oracle timing (profiling runs)")

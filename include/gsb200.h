@@ -149,13 +149,15 @@ GSB_API int gsb_project_bwd(gsb_stream_t stream, const gsb_project_bwd_params* p
  * Inputs: mean[C*2], conic[C*4], alpha[C], depth[C], visible[C] i8.
  * Outputs: point_counts[C], gaussian_ids[max_pairs] (valid prefix ends at
  * min(pair_count, max_pairs)), tile_offsets[T+1], pair_count[1] (unclamped),
- * overflow[1] (pair_count > max_pairs).  T = ceil(W/tile_w)*ceil(H/tile_h).
+ * overflow[1]: bit 0 = pair_count > max_pairs (the reference's overflow);
+ * bit 1 = an internal sort look-back gave up waiting (bounded spin; the table
+ * is then invalid).  T = ceil(W/tile_w)*ceil(H/tile_h).
  * ------------------------------------------------------------------------ */
 typedef struct {
     int capacity;
     int width, height;
     int tile_w, tile_h;    /* reference tile_size (width) and tile_height */
-    int64_t max_pairs;     /* arena capacity, < 2^31 */
+    int64_t max_pairs;     /* arena capacity, < 2^30 */
 } gsb_bin_params;
 
 GSB_API size_t gsb_bin_workspace_size(const gsb_bin_params* p);

@@ -243,7 +243,9 @@ __device__ __forceinline__ uint32_t depth_key(float depth, int32_t count)
     return (bits >> 31) ? ~bits : (bits ^ 0x80000000u);
 }
 
-// _count, sorted_visibility.py:307-370.
+// _count, sorted_visibility.py:307-370.  Also accumulates the four 8-bit
+// digit histograms of the keys of Gaussians with pairs (the depth sort's
+// per-pass histograms), one shared-memory update per distinct digit per warp.
 __global__ void __launch_bounds__(256) count_kernel(int capacity, const float* __restrict__ mean,
                                                     const float* __restrict__ conic,
                                                     const float* __restrict__ alpha,
@@ -251,12 +253,15 @@ __global__ void __launch_bounds__(256) count_kernel(int capacity, const float* _
                                                     const int8_t* __restrict__ visible,
                                                     gsb_bin_params p, int tiles_x, int tiles_y,
                                                     int32_t* __restrict__ counts,
-                                                    uint32_t* __restrict__ keys)
+                                                    uint32_t* __restrict__ keys,
+                                                    uint32_t* __restrict__ depth_hist)
 {
-    int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (g >= capacity) return;
+    __shared__ uint32_t hist[4][256];
+    for (int i = threadIdx.x; i < 4 * 256; i += blockDim.x) (&hist[0][0])[i] = 0;
+    __syncthreads();
+    const int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     int32_t count = 0;
-    if (visible[g] != 0) {
+    if (g < capacity && visible[g] != 0) {
         float2 m = *reinterpret_cast<const float2*>(mean + g * 2);
         float4 c = *reinterpret_cast<const float4*>(conic + g * 4);
         float a = alpha[g];
@@ -266,20 +271,53 @@ __global__ void __launch_bounds__(256) count_kernel(int capacity, const float* _
                                                    0, nullptr, nullptr);
         }
     }
-    counts[g] = count;
-    keys[g] = depth_key(depth[g], count);
+    if (g < capacity) {
+        const uint32_t key = depth_key(depth[g], count);
+        counts[g] = count;
+        keys[g] = key;
+    }
+    const uint32_t key = g < capacity ? depth_key(depth[g], count) : 0xFFFFFFFFu;
+    const unsigned lt = lanemask_lt();
+#pragma unroll
+    for (int pass = 0; pass < 4; pass++) {
+        const int d = count > 0 ? (int)((key >> (8 * pass)) & 255u) : 256;
+        const unsigned peers = __match_any_sync(GSB_FULL_MASK, d);
+        if ((peers & lt) == 0 && d < 256) atomicAdd(&hist[pass][d], (uint32_t)__popc(peers));
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < 4 * 256; i += blockDim.x) {
+        const uint32_t v = (&hist[0][0])[i];
+        if (v) atomicAdd(depth_hist + i, v);
+    }
 }
 
 // ---------------------------------------------------------------------------
-// Stable LSD radix sort pass (reduce-then-scan, no inter-block waits).
-// Block tile: 256 threads x 16 items; warp w owns 512 consecutive items,
-// ranked round by round with match.any so equal digits keep their order.
+// Stable LSD radix sort, onesweep style.
+//  * onesweep_hist_kernel reads the keys once and accumulates the digit
+//    histograms of every pass (a key's digits do not change between passes).
+//  * Each pass is one kernel.  A block takes the next partition index from an
+//    atomic counter, so every lower partition was taken by a block that is
+//    already running; it ranks its 2048 items with bit-ballot multisplit
+//    (stable within the tile), publishes its per-digit counts, then looks
+//    back over the predecessors' published counts until one carries an
+//    inclusive prefix (decoupled look-back), publishes its own inclusive
+//    prefix and scatters.  Items are staged in shared memory in digit order,
+//    so each digit's run leaves the block as consecutive addresses.
+//  * Every look-back spin is bounded; on expiry the block records an error
+//    word (reported as GSB_ERR_LAUNCH by the host on the next call) and uses
+//    what it has, so a fault can never turn into a hang.
+// The first depth-sort pass drops the 0xFFFFFFFF keys of Gaussians without
+// pairs; later passes sort only the survivors.
 // ---------------------------------------------------------------------------
 constexpr int kSortThreads = 256;
-constexpr int kSortItems = 16;
+constexpr int kSortItems = 8;
 constexpr int kSortTile = kSortThreads * kSortItems;
 constexpr int kSortWarps = kSortThreads / 32;
 constexpr int kMaxRadix = 256;
+constexpr uint32_t kFlagAggregate = 1u << 30;
+constexpr uint32_t kFlagPrefix = 2u << 30;
+constexpr uint32_t kValueMask = (1u << 30) - 1;
+constexpr int kSpinLimit = 1 << 22;
 
 __device__ __forceinline__ int64_t read_count(const int32_t* ptr, int64_t cap)
 {
@@ -289,146 +327,266 @@ __device__ __forceinline__ int64_t read_count(const int32_t* ptr, int64_t cap)
 }
 
 template <typename K>
-__global__ void __launch_bounds__(kSortThreads) radix_hist_kernel(
-    const K* __restrict__ keys, const int32_t* n_ptr, int64_t n_cap, int shift, int bits,
-    int max_blocks, bool drop_sentinel, uint32_t* __restrict__ hist)
+__device__ __forceinline__ int item_digit(K key, bool valid, bool drop_sentinel, int shift, int radix)
 {
-    __shared__ uint32_t counters[kMaxRadix];
-    int64_t n = read_count(n_ptr, n_cap);
-    int64_t base = (int64_t)blockIdx.x * kSortTile;
-    if (base >= n) return;
-    int radix = 1 << bits;
-    for (int d = threadIdx.x; d < radix; d += kSortThreads) counters[d] = 0;
+    if (!valid || (drop_sentinel && (uint32_t)key == 0xFFFFFFFFu)) return radix;
+    return (int)(((uint32_t)key >> shift) & (radix - 1));
+}
+
+// Lanes of the warp holding the same digit (bit-ballot multisplit); digit
+// `radix` (invalid items) gets its own class through the extra bit.
+__device__ __forceinline__ unsigned same_digit_mask(int d, int bits)
+{
+    unsigned m = GSB_FULL_MASK;
+    for (int k = 0; k <= bits; k++) {
+        const bool b = (d >> k) & 1;
+        const unsigned bal = __ballot_sync(GSB_FULL_MASK, b);
+        m &= b ? bal : ~bal;
+    }
+    return m;
+}
+
+// Digit histograms of all passes: hist[pass * 256 + digit] (global atomics,
+// one per digit per block).  passes <= 4.
+template <typename K>
+__global__ void __launch_bounds__(kSortThreads) onesweep_hist_kernel(
+    const K* __restrict__ keys, const int32_t* n_ptr, int64_t n_cap, int passes, int bits,
+    bool drop_sentinel, uint32_t* __restrict__ hist)
+{
+    __shared__ uint32_t local[4][kMaxRadix];
+    const int64_t n = read_count(n_ptr, n_cap);
+    const int radix = 1 << bits;
+    for (int i = threadIdx.x; i < 4 * kMaxRadix; i += kSortThreads) (&local[0][0])[i] = 0;
     __syncthreads();
-    for (int k = 0; k < kSortItems; k++) {
-        int64_t i = base + (int64_t)k * kSortThreads + threadIdx.x;
-        if (i < n) {
-            uint32_t key = (uint32_t)keys[i];
-            if (!(drop_sentinel && key == 0xFFFFFFFFu))
-                atomicAdd(&counters[(key >> shift) & (radix - 1)], 1u);
+    const unsigned lt = lanemask_lt();
+    const int64_t stride = (int64_t)gridDim.x * kSortThreads;
+    for (int64_t base = (int64_t)blockIdx.x * kSortThreads; base < n; base += stride) {
+        const int64_t i = base + threadIdx.x;
+        const bool valid = i < n;
+        const K key = valid ? keys[i] : (K)0;
+        for (int pass = 0; pass < passes; pass++) {
+            const int d = item_digit(key, valid, drop_sentinel, pass * bits, radix);
+            const unsigned m = same_digit_mask(d, bits);
+            if ((m & lt) == 0 && d < radix) atomicAdd(&local[pass][d], (uint32_t)__popc(m));
         }
     }
     __syncthreads();
-    for (int d = threadIdx.x; d < radix; d += kSortThreads)
-        hist[(int64_t)d * max_blocks + blockIdx.x] = counters[d];
+    for (int i = threadIdx.x; i < passes * radix; i += kSortThreads) {
+        const uint32_t c = local[i / radix][i % radix];
+        if (c) atomicAdd(hist + (i / radix) * kMaxRadix + (i % radix), c);
+    }
 }
 
-// One block per digit: exclusive scan over the active blocks, digit total.
-__global__ void __launch_bounds__(kSortThreads) radix_scan_kernel(
-    const int32_t* n_ptr, int64_t n_cap, int max_blocks, uint32_t* __restrict__ hist,
-    uint32_t* __restrict__ digit_totals)
+// Exclusive scan of 256 values held one per thread (all threads participate).
+__device__ __forceinline__ uint32_t block_exclusive_scan256(uint32_t v, uint32_t* scratch)
 {
-    __shared__ uint32_t warp_sums[kSortWarps];
-    int64_t n = read_count(n_ptr, n_cap);
-    int blocks = (int)((n + kSortTile - 1) / kSortTile);
-    uint32_t* row = hist + (int64_t)blockIdx.x * max_blocks;
-    int per = (blocks + kSortThreads - 1) / kSortThreads;
-    int lo = threadIdx.x * per, hi = min(blocks, lo + per);
-    uint32_t local = 0;
-    for (int b = lo; b < hi; b++) local += row[b];
-    int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    uint32_t inc = warp_inclusive_scan(local, lane);
-    if (lane == 31) warp_sums[warp] = inc;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const uint32_t inc = warp_inclusive_scan(v, lane);
+    if (lane == 31) scratch[warp] = inc;
     __syncthreads();
-    uint32_t warp_base = 0;
-    for (int w = 0; w < warp; w++) warp_base += warp_sums[w];
-    uint32_t running = warp_base + inc - local;
-    for (int b = lo; b < hi; b++) {
-        uint32_t c = row[b];
-        row[b] = running;
-        running += c;
-    }
-    if (threadIdx.x == kSortThreads - 1) digit_totals[blockIdx.x] = warp_base + inc;
+    uint32_t wb = 0;
+    for (int w = 0; w < warp; w++) wb += scratch[w];
+    __syncthreads();
+    return wb + inc - v;
 }
 
 template <typename K>
-__global__ void __launch_bounds__(kSortThreads) radix_scatter_kernel(
+__global__ void __launch_bounds__(kSortThreads) onesweep_pass_kernel(
     const K* __restrict__ keys_in, const int32_t* __restrict__ vals_in, K* __restrict__ keys_out,
     int32_t* __restrict__ vals_out, const int32_t* n_ptr, int64_t n_cap, int shift, int bits,
-    int max_blocks, bool drop_sentinel, const uint32_t* __restrict__ hist,
-    const uint32_t* __restrict__ digit_totals, int32_t* n_out)
+    bool drop_sentinel, const uint32_t* __restrict__ pass_hist, uint32_t* status,
+    int32_t* part_counter, int32_t* n_out, int32_t* error)
 {
     __shared__ uint32_t warp_hist[kSortWarps][kMaxRadix + 1];
-    __shared__ uint32_t digit_off[kMaxRadix];
-    __shared__ uint32_t scan_tmp[kSortWarps];
-    int64_t n = read_count(n_ptr, n_cap);
-    int64_t base = (int64_t)blockIdx.x * kSortTile;
-    int radix = 1 << bits;
-    int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    if (base >= n) {
-        // Block 0 still reports the surviving count when n == 0.
-        if (blockIdx.x == 0 && threadIdx.x == 0 && n_out) *n_out = 0;
-        return;
-    }
-    // Exclusive scan of the digit totals -> digit base offsets.
-    {
-        uint32_t t = threadIdx.x < radix ? digit_totals[threadIdx.x] : 0u;
-        uint32_t inc = warp_inclusive_scan(t, lane);
-        if (lane == 31) scan_tmp[warp] = inc;
-        __syncthreads();
-        uint32_t wb = 0;
-        for (int w = 0; w < warp; w++) wb += scan_tmp[w];
-        if (threadIdx.x < radix) digit_off[threadIdx.x] = wb + inc - t + hist[(int64_t)threadIdx.x * max_blocks + blockIdx.x];
-        if (blockIdx.x == 0 && threadIdx.x == kSortThreads - 1 && n_out) *n_out = (int32_t)(wb + inc);
-    }
+    __shared__ uint32_t global_off[kMaxRadix];
+    __shared__ uint32_t block_start[kMaxRadix];
+    __shared__ uint32_t scratch[kSortWarps];
+    __shared__ K s_keys[kSortTile];
+    __shared__ int32_t s_vals[kSortTile];
+    __shared__ int s_part;
+    __shared__ uint32_t s_valid;
+    const int radix = 1 << bits;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int64_t n = read_count(n_ptr, n_cap);
+    if (threadIdx.x == 0) s_part = atomicAdd(part_counter, 1);
     for (int d = lane; d <= radix; d += 32) warp_hist[warp][d] = 0;
-    __syncwarp();
+    __syncthreads();
+    const int part = s_part;
+    const int64_t base = (int64_t)part * kSortTile;
+    if (part == 0 && threadIdx.x == 0 && n_out) {
+        uint32_t total = 0;
+        for (int d = 0; d < radix; d++) total += pass_hist[d];
+        *n_out = (int32_t)total;
+    }
+    if (base >= n) return;  // uniform: no later partition waits on this one
     K key[kSortItems];
     int32_t val[kSortItems];
-    uint32_t rank[kSortItems];
     int digit[kSortItems];
-    int64_t wbase = base + (int64_t)warp * 32 * kSortItems;
-    unsigned lt = lanemask_lt();
+    uint32_t rank[kSortItems];
+    const int64_t wbase = base + (int64_t)warp * 32 * kSortItems;
 #pragma unroll
     for (int r = 0; r < kSortItems; r++) {
-        int64_t i = wbase + r * 32 + lane;
-        bool valid = i < n;
+        const int64_t i = wbase + r * 32 + lane;
+        const bool valid = i < n;
         key[r] = valid ? keys_in[i] : (K)0;
         val[r] = valid ? (vals_in ? vals_in[i] : (int32_t)i) : 0;
-        if (valid && drop_sentinel && (uint32_t)key[r] == 0xFFFFFFFFu) valid = false;
-        int d = valid ? (int)(((uint32_t)key[r] >> shift) & (radix - 1)) : radix;
-        digit[r] = d;
-        unsigned peers = __match_any_sync(GSB_FULL_MASK, d);
-        uint32_t before = warp_hist[warp][d];
+        digit[r] = item_digit(key[r], valid, drop_sentinel, shift, radix);
+    }
+    const unsigned lt = lanemask_lt();
+#pragma unroll
+    for (int r = 0; r < kSortItems; r++) {
+        const int d = digit[r];
+        const unsigned m = same_digit_mask(d, bits);
+        const uint32_t before = warp_hist[warp][d];
         __syncwarp();
-        rank[r] = before + __popc(peers & lt);
-        if ((peers & lt) == 0) warp_hist[warp][d] = before + __popc(peers);
+        rank[r] = before + __popc(m & lt);
+        if ((m & lt) == 0) warp_hist[warp][d] = before + __popc(m);
         __syncwarp();
     }
     __syncthreads();
-    for (int d = threadIdx.x; d < radix; d += kSortThreads) {
-        uint32_t running = 0;
+    const int d = threadIdx.x;  // kSortThreads == kMaxRadix
+    uint32_t count = 0;
+    if (d < radix) {
+#pragma unroll
         for (int w = 0; w < kSortWarps; w++) {
-            uint32_t c = warp_hist[w][d];
-            warp_hist[w][d] = running;
-            running += c;
+            const uint32_t c = warp_hist[w][d];
+            warp_hist[w][d] = count;
+            count += c;
+        }
+        // Publish this partition's count, then look back for the prefix.
+        volatile uint32_t* st = status;
+        if (part == 0) {
+            st[d] = kFlagPrefix | count;
+        } else {
+            st[(int64_t)part * kMaxRadix + d] = kFlagAggregate | count;
         }
     }
+    uint32_t excl = 0;
+    if (d < radix && part > 0) {
+        // Windowed look-back: the status words of up to kWindow predecessors
+        // are loaded together, so the walk costs one latency per window.
+        constexpr int kWindow = 8;
+        volatile uint32_t* st = status;
+        int j = part - 1;
+        int spins = 0;
+        bool done = false;
+        while (!done && j >= 0) {
+            uint32_t v[kWindow];
+#pragma unroll
+            for (int k = 0; k < kWindow; k++) v[k] = (j - k >= 0) ? (uint32_t)st[(int64_t)(j - k) * kMaxRadix + d] : (uint32_t)(2u << 30);
+            int k = 0;
+            uint32_t acc = 0;
+            for (; k < kWindow; k++) {
+                const uint32_t flag = v[k] & ~kValueMask;
+                if (flag == 0) break;  // not published yet: wait here
+                acc += v[k] & kValueMask;
+                if (flag == kFlagPrefix) {
+                    done = true;
+                    break;
+                }
+            }
+            if (done) {
+                excl += acc;
+            } else if (k == kWindow) {
+                excl += acc;
+                j -= kWindow;
+            } else {
+                excl += acc;  // consume the published run, retry the first gap
+                j -= k;
+                if (++spins > kSpinLimit) {
+                    atomicExch(error, 1);
+                    done = true;
+                }
+            }
+        }
+        st[(int64_t)part * kMaxRadix + d] = kFlagPrefix | ((excl + count) & kValueMask);
+    }
+    const uint32_t start = block_exclusive_scan256(count, scratch);
+    const uint32_t digit_base = block_exclusive_scan256(d < radix ? pass_hist[d] : 0u, scratch);
+    if (d < radix) {
+        block_start[d] = start;
+        global_off[d] = digit_base + excl;
+    }
+    if (d == radix - 1) s_valid = start + count;
     __syncthreads();
 #pragma unroll
     for (int r = 0; r < kSortItems; r++) {
-        int d = digit[r];
-        if (d < radix) {
-            uint32_t dest = digit_off[d] + warp_hist[warp][d] + rank[r];
-            keys_out[dest] = key[r];
-            vals_out[dest] = val[r];
+        const int dd = digit[r];
+        if (dd < radix) {
+            const uint32_t pos = block_start[dd] + warp_hist[warp][dd] + rank[r];
+            s_keys[pos] = key[r];
+            s_vals[pos] = val[r];
         }
+    }
+    __syncthreads();
+    const uint32_t valid_count = s_valid;
+    for (uint32_t j = threadIdx.x; j < valid_count; j += kSortThreads) {
+        const K k = s_keys[j];
+        const int dd = (int)(((uint32_t)k >> shift) & (radix - 1));
+        const uint32_t dst = global_off[dd] + (j - block_start[dd]);
+        keys_out[dst] = k;
+        vals_out[dst] = s_vals[j];
     }
 }
 
-template <typename K>
-int radix_pass(cudaStream_t s, const K* keys_in, const int32_t* vals_in, K* keys_out,
-               int32_t* vals_out, const int32_t* n_ptr, int64_t n_cap, int shift, int bits,
-               bool drop_sentinel, uint32_t* hist, uint32_t* totals, int32_t* n_out)
+__global__ void zero_u32_kernel(uint32_t* p, int64_t n)
 {
-    int max_blocks = ceil_div(n_cap > 0 ? n_cap : 1, kSortTile);
-    radix_hist_kernel<K><<<max_blocks, kSortThreads, 0, s>>>(keys_in, n_ptr, n_cap, shift, bits,
-                                                             max_blocks, drop_sentinel, hist);
-    radix_scan_kernel<<<1 << bits, kSortThreads, 0, s>>>(n_ptr, n_cap, max_blocks, hist, totals);
-    radix_scatter_kernel<K><<<max_blocks, kSortThreads, 0, s>>>(
-        keys_in, vals_in, keys_out, vals_out, n_ptr, n_cap, shift, bits, max_blocks,
-        drop_sentinel, hist, totals, n_out);
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+         i += (int64_t)gridDim.x * blockDim.x)
+        p[i] = 0;
+}
+
+// Sort scratch: histograms [4][256], status [4][partitions][256], counters.
+struct SortScratch {
+    uint32_t* hist;
+    uint32_t* status;
+    int32_t* counters;
+    int partitions;
+};
+
+// Histograms, look-back status words and partition counters are one
+// contiguous region, zeroed by one launch.
+int zero_sort_scratch(cudaStream_t s, const SortScratch& w)
+{
+    const int64_t words = 4 * kMaxRadix + 4 * (int64_t)w.partitions * kMaxRadix + 8;
+    zero_u32_kernel<<<256, 256, 0, s>>>(w.hist, words);
     return check_launch();
+}
+
+// With hist_ready the caller has zeroed the scratch and accumulated the
+// per-pass digit histograms into w.hist (the producer kernels do it).
+template <typename K>
+int onesweep_sort(cudaStream_t s, const K* keys_in, const int32_t* vals_in, K* key_a, K* key_b,
+                  int32_t* val_a, int32_t* val_b, int32_t* val_out, const K** sorted_keys,
+                  const int32_t** sorted_vals, const int32_t* n_ptr, int64_t n_cap, int passes,
+                  int bits, bool drop_sentinel, const SortScratch& w, int32_t* n_out,
+                  int32_t* error, bool hist_ready)
+{
+    if (!hist_ready) {
+        if (int e = zero_sort_scratch(s, w)) return e;
+        onesweep_hist_kernel<K><<<148 * 4, kSortThreads, 0, s>>>(keys_in, n_ptr, n_cap, passes,
+                                                                 bits, drop_sentinel, w.hist);
+        if (int e = check_launch()) return e;
+    }
+    const K* src_k = keys_in;
+    const int32_t* src_v = vals_in;
+    const int32_t* pass_n = n_ptr;
+    for (int pass = 0; pass < passes; pass++) {
+        const bool last = pass == passes - 1;
+        K* dst_k = (src_k == key_a) ? key_b : key_a;
+        int32_t* dst_v = (last && val_out) ? val_out : ((src_v == val_a) ? val_b : val_a);
+        onesweep_pass_kernel<K><<<w.partitions, kSortThreads, 0, s>>>(
+            src_k, src_v, dst_k, dst_v, pass_n, n_cap, pass * bits, bits, drop_sentinel && pass == 0,
+            w.hist + pass * kMaxRadix, w.status + (int64_t)pass * w.partitions * kMaxRadix,
+            w.counters + pass, (pass == 0 && drop_sentinel) ? n_out : nullptr, error);
+        if (int e = check_launch()) return e;
+        if (pass == 0 && drop_sentinel) pass_n = n_out;
+        src_k = dst_k;
+        src_v = dst_v;
+    }
+    *sorted_keys = src_k;
+    *sorted_vals = src_v;
+    return GSB_OK;
 }
 
 // ---------------------------------------------------------------------------
@@ -616,11 +774,14 @@ __global__ void __launch_bounds__(256) emit_large_kernel(
 // ---------------------------------------------------------------------------
 // Tile ranges (sorted_visibility.py:628-659): offsets[t] = first index with
 // key >= t over the first n sorted keys; empty tiles get contiguous offsets.
+// Also reports an internal sort time-out as bit 1 of overflow.
 // ---------------------------------------------------------------------------
 template <typename K>
 __global__ void ranges_kernel(const K* __restrict__ keys, const int32_t* n_ptr, int64_t n_cap,
-                              int num_tiles, int32_t* __restrict__ offsets)
+                              int num_tiles, int32_t* __restrict__ offsets,
+                              const int32_t* __restrict__ sort_error, int32_t* overflow)
 {
+    if (blockIdx.x == 0 && threadIdx.x == 0 && *sort_error) atomicOr(overflow, 2);
     int64_t n = read_count(n_ptr, n_cap);
     int64_t stride = (int64_t)gridDim.x * blockDim.x;
     int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -657,11 +818,22 @@ struct BinLayout {
     int32_t *order_a, *order_b;
     int64_t* ends;
     int64_t* block_sums;
-    int32_t *queue, *scalars;  // scalars: [0] binned count, [1] queue count, [2] clamped pairs
-    void *pair_keys_a, *pair_keys_b;
-    int32_t *pair_ids_a, *pair_ids_b;
-    uint32_t *hist, *totals;
+    int32_t *queue, *scalars;  // [0] binned, [1] queue count, [2] clamped pairs, [3] sort error
+    void *emit_keys, *pair_keys_a, *pair_keys_b;
+    int32_t *emit_ids, *pair_ids_a, *pair_ids_b;
+    SortScratch depth_sort, pair_sort;
 };
+
+SortScratch carve_sort(Carver& c, int64_t items)
+{
+    SortScratch w;
+    w.partitions = ceil_div(items > 0 ? items : 1, kSortTile);
+    uint32_t* base = c.take<uint32_t>(4 * kMaxRadix + 4 * (int64_t)w.partitions * kMaxRadix + 8);
+    w.hist = base;
+    w.status = base ? base + 4 * kMaxRadix : nullptr;
+    w.counters = base ? reinterpret_cast<int32_t*>(w.status + 4 * (int64_t)w.partitions * kMaxRadix) : nullptr;
+    return w;
+}
 
 BinLayout carve_bin(char* base, const gsb_bin_params& p, size_t& used)
 {
@@ -680,13 +852,14 @@ BinLayout carve_bin(char* base, const gsb_bin_params& p, size_t& used)
     L.block_sums = c.take<int64_t>(ceil_div(C, kScanTile));
     L.queue = c.take<int32_t>(C);
     L.scalars = c.take<int32_t>(8);
+    L.emit_keys = c.take<char>(P * key_bytes);
     L.pair_keys_a = c.take<char>(P * key_bytes);
     L.pair_keys_b = c.take<char>(P * key_bytes);
+    L.emit_ids = c.take<int32_t>(P);
     L.pair_ids_a = c.take<int32_t>(P);
     L.pair_ids_b = c.take<int32_t>(P);
-    int64_t max_items = C > P ? C : P;
-    L.hist = c.take<uint32_t>((int64_t)kMaxRadix * ceil_div(max_items, kSortTile));
-    L.totals = c.take<uint32_t>(kMaxRadix);
+    L.depth_sort = carve_sort(c, C);
+    L.pair_sort = carve_sort(c, P);
     used = c.used;
     return L;
 }
@@ -694,40 +867,32 @@ BinLayout carve_bin(char* base, const gsb_bin_params& p, size_t& used)
 template <typename K>
 int tile_stage(cudaStream_t s, const gsb_bin_params& p, const BinLayout& L, int tiles_x,
                int tiles_y, int64_t num_tiles, const float* mean, const float* conic,
-               const float* alpha, const int32_t* point_counts, int32_t* gaussian_ids,
-               int32_t* tile_offsets)
+               const float* alpha, const int32_t* point_counts, const int32_t* order,
+               int32_t* gaussian_ids, int32_t* tile_offsets, int32_t* overflow)
 {
-    K* keys_a = static_cast<K*>(L.pair_keys_a);
-    K* keys_b = static_cast<K*>(L.pair_keys_b);
-    const int32_t* order = L.order_b;  // depth order after 4 passes
+    K* emit_keys = static_cast<K*>(L.emit_keys);
     const int32_t* n_binned = L.scalars + 0;
     int64_t C = p.capacity;
     emit_kernel<K><<<ceil_div(C, 256), 256, 0, s>>>(order, point_counts, L.ends, n_binned, C, mean,
-                                                    conic, alpha, p, tiles_x, tiles_y, keys_a,
-                                                    L.pair_ids_a, L.queue, L.scalars + 1);
+                                                    conic, alpha, p, tiles_x, tiles_y, emit_keys,
+                                                    L.emit_ids, L.queue, L.scalars + 1);
     if (int e = check_launch()) return e;
     emit_large_kernel<K><<<148 * 8, 256, 0, s>>>(L.queue, L.scalars + 1, order, point_counts,
                                                  L.ends, mean, conic, alpha, p, tiles_x, tiles_y,
-                                                 keys_a, L.pair_ids_a);
+                                                 emit_keys, L.emit_ids);
     if (int e = check_launch()) return e;
     int passes, bits;
     digit_plan(num_tiles, passes, bits);
-    const int32_t* n_pairs = L.scalars + 2;
-    const K* src_k = keys_a;
-    const int32_t* src_v = L.pair_ids_a;
-    // Ping-pong so that the last pass writes the ids into gaussian_ids.
-    for (int pass = 0; pass < passes; pass++) {
-        bool last = pass == passes - 1;
-        K* dst_k = (src_k == keys_a) ? keys_b : keys_a;
-        int32_t* dst_v = last ? gaussian_ids
-                              : (src_v == L.pair_ids_a ? L.pair_ids_b : L.pair_ids_a);
-        if (int e = radix_pass<K>(s, src_k, src_v, dst_k, dst_v, n_pairs, p.max_pairs,
-                                  pass * bits, bits, false, L.hist, L.totals, nullptr))
-            return e;
-        src_k = dst_k;
-        src_v = dst_v;
-    }
-    ranges_kernel<K><<<1024, 256, 0, s>>>(src_k, n_pairs, p.max_pairs, (int)num_tiles, tile_offsets);
+    const K* sorted_keys = nullptr;
+    const int32_t* sorted_ids = nullptr;
+    if (int e = onesweep_sort<K>(s, emit_keys, L.emit_ids, static_cast<K*>(L.pair_keys_a),
+                                 static_cast<K*>(L.pair_keys_b), L.pair_ids_a, L.pair_ids_b,
+                                 gaussian_ids, &sorted_keys, &sorted_ids, L.scalars + 2,
+                                 p.max_pairs, passes, bits, false, L.pair_sort, nullptr,
+                                 L.scalars + 3, false))
+        return e;
+    ranges_kernel<K><<<1024, 256, 0, s>>>(sorted_keys, L.scalars + 2, p.max_pairs, (int)num_tiles,
+                                          tile_offsets, L.scalars + 3, overflow);
     return check_launch();
 }
 
@@ -760,7 +925,7 @@ extern "C" int gsb_bin(gsb_stream_t stream, const gsb_bin_params* p, void* works
 {
     if (!p) return GSB_ERR_NULL;
     if (p->capacity < 0 || p->width <= 0 || p->height <= 0 || p->tile_w <= 0 || p->tile_h <= 0 ||
-        p->max_pairs <= 0 || p->max_pairs >= (int64_t(1) << 31))
+        p->max_pairs <= 0 || p->max_pairs >= (int64_t(1) << 30))
         return GSB_ERR_INVALID;
     int tiles_x = ceil_div(p->width, p->tile_w), tiles_y = ceil_div(p->height, p->tile_h);
     int64_t num_tiles = (int64_t)tiles_x * tiles_y;
@@ -779,36 +944,31 @@ extern "C" int gsb_bin(gsb_stream_t stream, const gsb_bin_params* p, void* works
     zero_i32_kernel<<<1, 32, 0, s>>>(L.scalars, 8);
     if (int e = check_launch()) return e;
     int64_t C = p->capacity;
+    const uint32_t* sorted_depth_keys = nullptr;
+    const int32_t* depth_order = L.order_a;
     if (C > 0) {
+        if (int e = zero_sort_scratch(s, L.depth_sort)) return e;
         count_kernel<<<ceil_div(C, 256), 256, 0, s>>>((int)C, mean, conic, alpha, depth, visible,
                                                       *p, tiles_x, tiles_y, point_counts,
-                                                      L.depth_keys);
+                                                      L.depth_keys, L.depth_sort.hist);
         if (int e = check_launch()) return e;
         // Depth sort: pass 0 drops the Gaussians without pairs.
-        if (int e = radix_pass<uint32_t>(s, L.depth_keys, nullptr, L.keys_a, L.order_a, nullptr, C,
-                                         0, 8, true, L.hist, L.totals, L.scalars + 0))
-            return e;
-        const int32_t* nb = L.scalars + 0;
-        if (int e = radix_pass<uint32_t>(s, L.keys_a, L.order_a, L.keys_b, L.order_b, nb, C, 8, 8,
-                                         false, L.hist, L.totals, nullptr))
-            return e;
-        if (int e = radix_pass<uint32_t>(s, L.keys_b, L.order_b, L.keys_a, L.order_a, nb, C, 16, 8,
-                                         false, L.hist, L.totals, nullptr))
-            return e;
-        if (int e = radix_pass<uint32_t>(s, L.keys_a, L.order_a, L.keys_b, L.order_b, nb, C, 24, 8,
-                                         false, L.hist, L.totals, nullptr))
+        if (int e = onesweep_sort<uint32_t>(s, L.depth_keys, nullptr, L.keys_a, L.keys_b, L.order_a,
+                                            L.order_b, nullptr, &sorted_depth_keys, &depth_order,
+                                            nullptr, C, 4, 8, true, L.depth_sort, L.scalars + 0,
+                                            L.scalars + 3, true))
             return e;
     }
     scan_reduce_kernel<<<ceil_div(C > 0 ? C : 1, kScanTile), kScanThreads, 0, s>>>(
-        L.order_b, point_counts, L.scalars + 0, C, L.block_sums);
+        depth_order, point_counts, L.scalars + 0, C, L.block_sums);
     if (int e = check_launch()) return e;
     scan_kernel<<<ceil_div(C > 0 ? C : 1, kScanTile), kScanThreads, 0, s>>>(
-        L.order_b, point_counts, L.scalars + 0, C, L.block_sums, L.ends, p->max_pairs, pair_count,
+        depth_order, point_counts, L.scalars + 0, C, L.block_sums, L.ends, p->max_pairs, pair_count,
         overflow, L.scalars + 2);
     if (int e = check_launch()) return e;
     if (num_tiles <= 65535)
         return tile_stage<uint16_t>(s, *p, L, tiles_x, tiles_y, num_tiles, mean, conic, alpha,
-                                    point_counts, gaussian_ids, tile_offsets);
+                                    point_counts, depth_order, gaussian_ids, tile_offsets, overflow);
     return tile_stage<uint32_t>(s, *p, L, tiles_x, tiles_y, num_tiles, mean, conic, alpha,
-                                point_counts, gaussian_ids, tile_offsets);
+                                point_counts, depth_order, gaussian_ids, tile_offsets, overflow);
 }

@@ -322,17 +322,23 @@ extern "C" int gsb_loss(gsb_stream_t stream, const gsb_loss_params* p, void* wor
     uint32_t* block_scale = reinterpret_cast<uint32_t*>(static_cast<char*>(workspace) + half);
     dim3 grid(ceil_div(p->width, kTW), ceil_div(p->height, kTH));
     size_t smem = sizeof(LossSmem);
-    auto launch = [&](auto kernel) {
-        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    // The shared-memory opt-in is set once per process (one device per
+    // process); it is a host-side attribute, so graph captures never see it.
+    static bool configured[4] = {false, false, false, false};
+    auto launch = [&](auto kernel, int which) {
+        if (!configured[which]) {
+            cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            configured[which] = true;
+        }
         kernel<<<grid, kThreads, smem, s>>>(p->width, p->height, image, target, grad, block_loss,
                                             block_scale);
     };
     if (p->target_u8) {
-        if (p->clip_input) launch(loss_kernel<true, true>);
-        else launch(loss_kernel<true, false>);
+        if (p->clip_input) launch(loss_kernel<true, true>, 0);
+        else launch(loss_kernel<true, false>, 1);
     } else {
-        if (p->clip_input) launch(loss_kernel<false, true>);
-        else launch(loss_kernel<false, false>);
+        if (p->clip_input) launch(loss_kernel<false, true>, 2);
+        else launch(loss_kernel<false, false>, 3);
     }
     if (int e = check_launch()) return e;
     float inv_n = 1.0f / (3.0f * (float)p->width * (float)p->height);

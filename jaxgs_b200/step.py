@@ -10,9 +10,13 @@ fp32 compositing of kernels/sorted_rasterizer.py:165-236 for every tile
 shape, which is the path whose images and gradients meet the 1e-4 / 1e-3
 parity bars.
 
-Multi-GPU (view sharding): ``ViewShardedStep`` renders each rank's views,
-scatters the compact gradients into pool order and sums them across ranks
-with one NCCL all-reduce per step (torch.distributed).
+``GraphedTrainingStep`` captures the whole step once as a CUDA graph and
+replays it: every size the kernels need is static (device-side counts bound
+the work), so a replay issues the ~40 launches without host involvement.
+
+Multi-GPU (view sharding): each rank renders its views, scatters the
+compact gradients into pool order (``scatter_compact``) and the ranks sum
+them with one NCCL all-reduce per step (torch.distributed).
 """
 
 from __future__ import annotations
@@ -33,6 +37,7 @@ class StepOutput:
     visible_clusters: tuple       # (ids, count)
     pair_count: torch.Tensor      # [1] int32
     overflow: torch.Tensor        # [1] int32
+    point_counts: torch.Tensor | None = None  # [C] int32 pairs per Gaussian
     image: torch.Tensor | None = None
 
 
@@ -91,7 +96,7 @@ def compute_training_step(pool: GaussianArrays, bounds, camera: DeviceCamera, ta
     grads = pullback(cot)
     done(ev)
     return StepOutput(loss, grads, clusters, table.pair_count, table.overflow,
-                      result.rgb if keep_image else None)
+                      table.point_counts, result.rgb if keep_image else None)
 
 
 def render(camera: DeviceCamera, gaussians: GaussianArrays, visible_clusters, active_degree: int,
@@ -123,3 +128,50 @@ def scatter_compact(grads, clusters, config: CapacityConfig, out=None):
         dst.index_add_(0, slots, g[rows])
         outs.append(dst)
     return outs
+
+
+class GraphedTrainingStep:
+    """compute_training_step captured once as a CUDA graph, then replayed.
+
+    The pool, cluster bounds and the returned buffers keep their device
+    addresses across replays (an in-place optimizer update of the pool is
+    seen by the next replay).  Each call copies the camera arrays and the
+    target into the graph's static inputs (host or device tensors; host
+    tensors should be pinned for asynchronous copies) and replays.
+    """
+
+    def __init__(self, pool: GaussianArrays, bounds, camera: DeviceCamera, target: torch.Tensor,
+                 config: CapacityConfig, active_degree: int, *, active_sh_only: bool = True,
+                 sh_color_only: bool = False, warmup: int = 2):
+        dev = pool.xyz.device
+        self.camera = DeviceCamera(camera.world_to_camera.clone(), camera.intrinsics.clone(),
+                                   camera.center.clone(), camera.planes.clone(), camera.width,
+                                   camera.height, camera.near, camera.far)
+        self.target = torch.empty_like(target, device=dev)
+        self.target.copy_(target)
+        args = (pool, bounds, self.camera, self.target, config, active_degree)
+        kwargs = dict(active_sh_only=active_sh_only, sh_color_only=sh_color_only)
+        side = torch.cuda.Stream(device=dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            for _ in range(max(warmup, 1)):
+                compute_training_step(*args, **kwargs)
+        torch.cuda.current_stream(dev).wait_stream(side)
+        self.graph = torch.cuda.CUDAGraph()
+        from . import _lib
+
+        before = _lib.launch_count()
+        with torch.cuda.graph(self.graph):
+            self.out = compute_training_step(*args, **kwargs)
+        self.launches_per_step = _lib.launch_count() - before
+
+    def __call__(self, camera: DeviceCamera | None = None, target: torch.Tensor | None = None) -> StepOutput:
+        if camera is not None:
+            for dst, src in ((self.camera.world_to_camera, camera.world_to_camera),
+                             (self.camera.intrinsics, camera.intrinsics),
+                             (self.camera.center, camera.center), (self.camera.planes, camera.planes)):
+                dst.copy_(src, non_blocking=True)
+        if target is not None:
+            self.target.copy_(target, non_blocking=True)
+        self.graph.replay()
+        return self.out
