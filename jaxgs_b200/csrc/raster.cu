@@ -216,6 +216,7 @@ __global__ void __launch_bounds__(256) raster_fwd_kernel(
             const float dx = pcx - r0.x;
             const float ax = __fmul_rn(r1.x, dx), bx = __fmul_rn(r1.z, dx);
             bool valid_any = false;
+            const int32_t next = base + k + 1;
 #pragma unroll
             for (int r = 0; r < ROWS; r++) {
                 const float dy = pcy[r] - r0.y;
@@ -224,19 +225,17 @@ __global__ void __launch_bounds__(256) raster_fwd_kernel(
                 const float power = __fmaf_rn(dy, t2, __fmul_rn(dx, t1));
                 const float raw = r2.w * __expf(power);
                 const bool valid = active[r] && power <= 0.0f && raw >= kMinAlpha;
-                if (valid) {
-                    const float a = fminf(kMaxAlpha, raw);
-                    const float w = a * T[r];
-                    cr[r] = __fmaf_rn(w, r2.x, cr[r]);
-                    cg[r] = __fmaf_rn(w, r2.y, cg[r]);
-                    cb[r] = __fmaf_rn(w, r2.z, cb[r]);
-                    if (WANT_DEPTH) cd[r] = __fmaf_rn(w, st.depth[k], cd[r]);
-                    T[r] = T[r] * (1.0f - a);
-                    if (T[r] < kMinT) {
-                        active[r] = false;
-                        last[r] = base + k + 1;
-                    }
-                }
+                // Branch-free: with a = 0 every update below is an exact no-op.
+                const float a = valid ? fminf(kMaxAlpha, raw) : 0.0f;
+                const float w = a * T[r];
+                cr[r] = __fmaf_rn(w, r2.x, cr[r]);
+                cg[r] = __fmaf_rn(w, r2.y, cg[r]);
+                cb[r] = __fmaf_rn(w, r2.z, cb[r]);
+                if (WANT_DEPTH) cd[r] = __fmaf_rn(w, st.depth[k], cd[r]);
+                T[r] = T[r] * (1.0f - a);
+                const bool stop = valid && T[r] < kMinT;
+                last[r] = stop ? next : last[r];
+                active[r] = active[r] && !stop;
                 valid_any |= valid;
             }
             if (__ballot_sync(GSB_FULL_MASK, valid_any)) contributed |= 1u << k;
@@ -360,6 +359,8 @@ __global__ void __launch_bounds__(256) raster_bwd_kernel(
     } else if (WANT_DEPTH && lane == 2) {
         target = gdepth; stride = 1;
     }
+    // Constant coefficient of the lane's moment (groups 2-4: -1/2, 5-7: 1).
+    const float kA = group < 5 ? -0.5f : 1.0f;
     if (top <= start) return;
     const int32_t top_batch = (top - 1 - start) >> 5;
     for (int32_t batch = top_batch; batch >= 0; batch--) {
@@ -395,41 +396,40 @@ __global__ void __launch_bounds__(256) raster_bwd_kernel(
                 const float t2 = __fmaf_rn(r1.w, dy, bx);
                 const float power = __fmaf_rn(dy, t2, __fmul_rn(dx, t1));
                 const float raw = r2.w * __expf(power);
-                if (idx < last[r] && power <= 0.0f && raw >= kMinAlpha) {
-                    const float a = fminf(kMaxAlpha, raw);
-                    const float one_minus = 1.0f - a;
-                    const float T_before = __fdividef(T_after[r], one_minus);
-                    const float w = T_before * a;
-                    float gw = gR[r] * r2.x + gG[r] * r2.y + gB[r] * r2.z;
-                    if (WANT_DEPTH) gw += gD[r] * st.depth[k];
-                    const float ga = T_before * (gw - gtrans[r]);
-                    gtrans[r] = a * gw + one_minus * gtrans[r];
-                    R = __fmaf_rn(w, gR[r], R);
-                    G = __fmaf_rn(w, gG[r], G);
-                    B = __fmaf_rn(w, gB[r], B);
-                    if (WANT_DEPTH) Z = __fmaf_rn(w, gD[r], Z);
-                    const float ge = raw < kMaxAlpha ? ga * raw : 0.0f;
-                    const float gedy = ge * dy;
-                    S0 += ge;
-                    Sy += gedy;
-                    Syy = __fmaf_rn(gedy, dy, Syy);
-                    T_after[r] = T_before;
-                }
+                const bool valid = idx < last[r] && power <= 0.0f && raw >= kMinAlpha;
+                // Branch-free: with a = 0 the transmittance, the colour
+                // behind and every accumulated term stay exactly unchanged.
+                const float a = valid ? fminf(kMaxAlpha, raw) : 0.0f;
+                const float one_minus = 1.0f - a;
+                const float T_before = __fdividef(T_after[r], one_minus);
+                const float w = T_before * a;
+                float gw = gR[r] * r2.x + gG[r] * r2.y + gB[r] * r2.z;
+                if (WANT_DEPTH) gw += gD[r] * st.depth[k];
+                const float ga = T_before * (gw - gtrans[r]);
+                gtrans[r] = valid ? a * gw + one_minus * gtrans[r] : gtrans[r];
+                R = __fmaf_rn(w, gR[r], R);
+                G = __fmaf_rn(w, gG[r], G);
+                B = __fmaf_rn(w, gB[r], B);
+                if (WANT_DEPTH) Z = __fmaf_rn(w, gD[r], Z);
+                const float ge = (valid && raw < kMaxAlpha) ? ga * raw : 0.0f;
+                const float gedy = ge * dy;
+                S0 += ge;
+                Sy += gedy;
+                Syy = __fmaf_rn(gedy, dy, Syy);
+                T_after[r] = valid ? T_before : T_after[r];
             }
             const float Sx = dx * S0;
             float v[8] = {Sx, Sy, dx * Sx, dx * Sy, Syy, R, G, B};
-            float s = warp_sum8(v, lane);
+            const float s = warp_sum8(v, lane);
             S0 = warp_sum(S0);
             if (WANT_DEPTH) Z = warp_sum(Z);
             // gmean.x = c00 Sx + cbar Sy, gmean.y = c11 Sy + cbar Sx with c = -2 r1;
-            // gconic = -Sxx/2, -Sxy/2 (twice), -Syy/2; gcolor = R, G, B.
+            // gconic = -Sxx/2, -Sxy/2 (twice), -Syy/2; gcolor = R, G, B;
+            // galpha = sum(ge) / o.
             const float other = __shfl_xor_sync(GSB_FULL_MASK, s, 4);
-            const float rbar = r1.y + r1.z;  // = -cbar
-            float value;
-            if (group == 0) value = -2.0f * r1.x * s - rbar * other;
-            else if (group == 1) value = -2.0f * r1.w * s - rbar * other;
-            else if (group < 5) value = -0.5f * s;
-            else value = s;
+            const float coef_a = group == 0 ? -2.0f * r1.x : (group == 1 ? -2.0f * r1.w : kA);
+            const float coef_b = group < 2 ? -(r1.y + r1.z) : 0.0f;
+            float value = coef_a * s + coef_b * other;
             if (lane == 1) value = __fdividef(S0, r2.w);
             if (WANT_DEPTH && lane == 2) value = Z;
             if (target) atomicAdd(target + (int64_t)st.id[k] * stride, value);
