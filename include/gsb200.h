@@ -257,6 +257,31 @@ GSB_API int gsb_loss(gsb_stream_t stream, const gsb_loss_params* p, void* worksp
              size_t workspace_bytes, const float* image, const void* target, float* loss,
              float* grad, float* scale);
 
+/* ------------------------------------------------------------------------
+ * Allocation-free fused loss.  No counterpart in the reference (jax-gs lets
+ * XLA allocate every temporary of its loss kernel).
+ * For callers that cannot allocate device memory when they need the loss: a
+ * JAX/XLA host whose allocator holds most of the GPU and gives a custom call
+ * only planned buffers, a server with a fixed memory plan, a latency-bound
+ * caller that cannot afford cudaMalloc's device synchronisation, or a plugin
+ * ABI that passes only inputs and outputs.  Same arguments and results as
+ * gsb_loss without the workspace; the per-tile temporaries live in a fixed
+ * 128 KiB device array inside the library, held on every GPU that loads the
+ * library's device code until the process exits.  The call allocates nothing.
+ *  - Size limit: ceil(W/32) * ceil(H/16) <= GSB_LOSS_NOALLOC_MAX_TILES
+ *    (e.g. 4096 x 2048); larger images return GSB_ERR_INVALID and
+ *    gsb_last_error() says why.
+ *  - The first call on a device (with it current) looks up the array's
+ *    address and sets the kernels' shared-memory limit; make it before any
+ *    stream capture begins.
+ *  - All calls on a device share the array (each call overwrites what it
+ *    reads, so no clearing is needed); calls that overlap on the GPU race
+ *    and must be ordered by the caller.
+ * ------------------------------------------------------------------------ */
+#define GSB_LOSS_NOALLOC_MAX_TILES 16384
+GSB_API int gsb_loss_noalloc(gsb_stream_t stream, const gsb_loss_params* p, const float* image,
+                     const void* target, float* loss, float* grad, float* scale);
+
 #ifdef __cplusplus
 }
 #endif

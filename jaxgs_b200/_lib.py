@@ -66,7 +66,7 @@ SYMBOLS = (
     "gsb_project_fwd", "gsb_project_bwd",
     "gsb_bin_workspace_size", "gsb_tile_sort_plan", "gsb_bin",
     "gsb_raster_workspace_size", "gsb_raster_bit_words", "gsb_raster_fwd", "gsb_raster_bwd",
-    "gsb_loss_workspace_size", "gsb_loss",
+    "gsb_loss_workspace_size", "gsb_loss", "gsb_loss_noalloc",
 )
 
 
@@ -103,6 +103,8 @@ def _load():
     lib.gsb_raster_bwd.argtypes = [vp, vp, vp, sz] + [vp] * 19
     lib.gsb_loss.restype = ctypes.c_int
     lib.gsb_loss.argtypes = [vp, vp, vp, sz] + [vp] * 5
+    lib.gsb_loss_noalloc.restype = ctypes.c_int
+    lib.gsb_loss_noalloc.argtypes = [vp, vp] + [vp] * 5
     return lib
 
 

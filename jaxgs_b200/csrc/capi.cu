@@ -16,6 +16,12 @@ void set_error(cudaError_t err)
     for (; msg && msg[i] && i < 255; i++) g_last_error[i] = msg[i];
     g_last_error[i] = '\0';
 }
+void set_error_text(const char* msg)
+{
+    int i = 0;
+    for (; msg && msg[i] && i < 255; i++) g_last_error[i] = msg[i];
+    g_last_error[i] = '\0';
+}
 }  // namespace gsb
 
 extern "C" int gsb_abi_version(void) { return GSB_ABI_VERSION; }

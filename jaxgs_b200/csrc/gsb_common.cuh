@@ -12,6 +12,8 @@ namespace gsb {
 
 // Records the last CUDA error string for gsb_last_error().
 void set_error(cudaError_t err);
+// Records a library message (not a CUDA error) for gsb_last_error().
+void set_error_text(const char* msg);
 // Adds to the process-wide count of kernels this library has launched.
 void count_launch();
 

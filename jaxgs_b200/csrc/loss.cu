@@ -345,3 +345,139 @@ extern "C" int gsb_loss(gsb_stream_t stream, const gsb_loss_params* p, void* wor
     loss_finish_kernel<<<1, 1024, 0, s>>>(blocks, inv_n, block_loss, block_scale, loss, scale);
     return check_launch();
 }
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of gsb_loss.
+//
+// Who needs it: callers that may not allocate device memory at the moment
+// they compute the loss.  A JAX/XLA host preallocates most of the GPU for its
+// own allocator and hands a custom call only the buffers it planned, so a
+// cudaMalloc inside the call competes with that pool (and can fail with
+// memory nominally free); a serving process with a fixed memory plan forbids
+// allocation on its request path; cudaMalloc and cudaFree can synchronise the
+// device, stalling every stream a latency-bound caller keeps busy; and a
+// plugin boundary that passes only input and output pointers gives the
+// callee nowhere to put a workspace.  gsb_loss needs 2 x 4 bytes per 32x16
+// output tile of temporaries (per-tile loss sums and |grad| maxima).  Here
+// they live in the fixed array below, part of this library's device image.
+//
+// Limits and sharing:
+//  * kNoallocMaxTiles tiles of 32x16 pixels (4096 x 2048 pixels, or any
+//    image with ceil(W/32) * ceil(H/16) <= 16384); larger images are
+//    rejected with GSB_ERR_INVALID and a message in gsb_last_error().
+//  * The array takes 128 KiB on every GPU on which this library's device
+//    code is loaded, until the process exits.
+//  * Every call on a device shares the one array.  Nothing in it needs to
+//    start at zero: each CTA overwrites its own slots before the finishing
+//    kernel reads them, so the contents left by the previous call are never
+//    read.  Calls whose kernels overlap on the GPU (different streams with
+//    no ordering between them) race on the array and give wrong results;
+//    order them on one stream or with events.
+//  * The first call on a device, with that device current, looks up the
+//    array's device address (cudaGetSymbolAddress) and sets the kernels'
+//    shared-memory limit on that device; make that first call before any
+//    stream capture begins.  Later calls only read the cached address.
+// ---------------------------------------------------------------------------
+#include <atomic>
+#include <cstdio>
+#include <mutex>
+
+namespace gsb {
+namespace {
+
+constexpr int kNoallocMaxTiles = GSB_LOSS_NOALLOC_MAX_TILES;
+constexpr int kNoallocMaxDevices = 64;
+
+// [0, max) per-tile loss sums (float bits), [max, 2 max) per-tile |grad| maxima.
+static __device__ __align__(256) uint32_t g_loss_scratch[2 * kNoallocMaxTiles];
+
+std::mutex g_noalloc_mutex;
+std::atomic<void*> g_noalloc_scratch[kNoallocMaxDevices];
+
+// Device address of g_loss_scratch on the current device (set up on first
+// use).  The name g_loss_scratch in host code is only a handle for the
+// runtime; the address must come from cudaGetSymbolAddress.
+int noalloc_scratch(void** out)
+{
+    int dev = 0;
+    cudaError_t err = cudaGetDevice(&dev);
+    if (err != cudaSuccess) {
+        set_error(err);
+        return GSB_ERR_LAUNCH;
+    }
+    if (dev < 0 || dev >= kNoallocMaxDevices) {
+        set_error_text("gsb_loss_noalloc: device ordinal above 63 is not supported");
+        return GSB_ERR_INVALID;
+    }
+    void* ptr = g_noalloc_scratch[dev].load(std::memory_order_acquire);
+    if (!ptr) {
+        std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+        ptr = g_noalloc_scratch[dev].load(std::memory_order_acquire);
+        if (!ptr) {
+            err = cudaGetSymbolAddress(&ptr, g_loss_scratch);
+            if (err != cudaSuccess || !ptr) {
+                set_error(err != cudaSuccess ? err : cudaErrorInvalidSymbol);
+                return GSB_ERR_LAUNCH;
+            }
+            const int smem = (int)sizeof(LossSmem);
+            const void* kernels[4] = {(const void*)loss_kernel<true, true>,
+                                      (const void*)loss_kernel<true, false>,
+                                      (const void*)loss_kernel<false, true>,
+                                      (const void*)loss_kernel<false, false>};
+            for (const void* k : kernels) {
+                err = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+                if (err != cudaSuccess) {
+                    set_error(err);
+                    return GSB_ERR_LAUNCH;
+                }
+            }
+            g_noalloc_scratch[dev].store(ptr, std::memory_order_release);
+        }
+    }
+    *out = ptr;
+    return GSB_OK;
+}
+
+}  // namespace
+}  // namespace gsb
+
+extern "C" int gsb_loss_noalloc(gsb_stream_t stream, const gsb_loss_params* p, const float* image,
+                                const void* target, float* loss, float* grad, float* scale)
+{
+    if (!p) return GSB_ERR_NULL;
+    if (p->width <= 0 || p->height <= 0) return GSB_ERR_INVALID;
+    const int64_t tiles = (int64_t)ceil_div(p->width, kTW) * ceil_div(p->height, kTH);
+    if (tiles > kNoallocMaxTiles) {
+        char msg[200];
+        std::snprintf(msg, sizeof(msg),
+                      "gsb_loss_noalloc: a %dx%d image has %lld tiles of 32x16, above the "
+                      "limit of %d (e.g. 4096x2048); use gsb_loss with a workspace",
+                      p->width, p->height, (long long)tiles, kNoallocMaxTiles);
+        set_error_text(msg);
+        return GSB_ERR_INVALID;
+    }
+    if (!image || !target || !loss || !grad) return GSB_ERR_NULL;
+    void* scratch = nullptr;
+    if (int e = noalloc_scratch(&scratch)) return e;
+    float* block_loss = static_cast<float*>(scratch);
+    uint32_t* block_scale = static_cast<uint32_t*>(scratch) + kNoallocMaxTiles;
+    cudaStream_t s = as_stream(stream);
+    const int blocks = (int)tiles;
+    dim3 grid(ceil_div(p->width, kTW), ceil_div(p->height, kTH));
+    const size_t smem = sizeof(LossSmem);
+    auto launch = [&](auto kernel) {
+        kernel<<<grid, kThreads, smem, s>>>(p->width, p->height, image, target, grad, block_loss,
+                                            block_scale);
+    };
+    if (p->target_u8) {
+        if (p->clip_input) launch(loss_kernel<true, true>);
+        else launch(loss_kernel<true, false>);
+    } else {
+        if (p->clip_input) launch(loss_kernel<false, true>);
+        else launch(loss_kernel<false, false>);
+    }
+    if (int e = check_launch()) return e;
+    float inv_n = 1.0f / (3.0f * (float)p->width * (float)p->height);
+    loss_finish_kernel<<<1, 1024, 0, s>>>(blocks, inv_n, block_loss, block_scale, loss, scale);
+    return check_launch();
+}

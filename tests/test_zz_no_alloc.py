@@ -1,0 +1,97 @@
+"""gsb_loss_noalloc: the allocation-free fused loss, called through the C ABI.
+
+Its per-tile temporaries live in a fixed array inside libgsb200.so, so it is
+compared here with gsb_loss (caller workspace) on the same inputs, on two
+calls in a row of different sizes and target types (the second call must not
+see the first call's leftovers).  This file is collected last so the check
+also covers a process where every other test already used the library; it
+passes alone in a fresh process as well (the first call does the per-device
+set-up).
+"""
+
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+from jaxgs_b200 import _lib as L
+
+GSB_ERR_INVALID = 1
+
+
+def _params(width, height, target_u8, clip_input):
+    return L.LossParams(width, height, int(target_u8), int(clip_input))
+
+
+def _stream():
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def _outputs(shape):
+    return (torch.empty(1, device="cuda"), torch.empty(shape, device="cuda"),
+            torch.empty(1, device="cuda"))
+
+
+def _with_workspace(image, target, clip_input):
+    h, w, _ = image.shape
+    p = _params(w, h, target.dtype == torch.uint8, clip_input)
+    ws_bytes = L.lib.gsb_loss_workspace_size(L.ref(p))
+    workspace = torch.empty(ws_bytes, dtype=torch.uint8, device="cuda")
+    loss, grad, scale = _outputs(image.shape)
+    rc = L.lib.gsb_loss(_stream(), L.ref(p), workspace.data_ptr(), ws_bytes, image.data_ptr(),
+                        target.data_ptr(), loss.data_ptr(), grad.data_ptr(), scale.data_ptr())
+    assert rc == 0, L.lib.gsb_last_error()
+    return loss, grad, scale
+
+
+def _without_workspace(image, target, clip_input):
+    h, w, _ = image.shape
+    p = _params(w, h, target.dtype == torch.uint8, clip_input)
+    loss, grad, scale = _outputs(image.shape)
+    rc = L.lib.gsb_loss_noalloc(_stream(), L.ref(p), image.data_ptr(), target.data_ptr(),
+                                loss.data_ptr(), grad.data_ptr(), scale.data_ptr())
+    assert rc == 0, L.lib.gsb_last_error()
+    return loss, grad, scale
+
+
+def _case(seed, height, width, u8_target):
+    rng = np.random.default_rng(seed)
+    # Values outside [0, 1] and exactly on the bounds exercise the clip.
+    image = rng.uniform(-0.1, 1.1, (height, width, 3)).astype(np.float32)
+    image[0, :4, 0] = [0.0, 1.0, -0.5, 1.5]
+    if u8_target:
+        target = rng.integers(0, 256, (height, width, 3), dtype=np.uint8)
+    else:
+        target = rng.uniform(0.0, 1.0, (height, width, 3)).astype(np.float32)
+    return torch.as_tensor(image, device="cuda"), torch.as_tensor(target, device="cuda")
+
+
+@pytest.mark.gpu
+def test_noalloc_loss_matches_workspace_loss_on_two_calls_in_a_row():
+    # Call 1: the benchmark's image size, uint8 target, clipped input.
+    # Call 2: a smaller, ragged image with a float target and no clip, so it
+    # uses fewer tiles of the shared array than call 1 left behind.
+    cases = [(7, 822, 1237, True, True), (8, 203, 301, False, False)]
+    for seed, h, w, u8_target, clip in cases:
+        image, target = _case(seed, h, w, u8_target)
+        ref_loss, ref_grad, ref_scale = _with_workspace(image, target, clip)
+        loss, grad, scale = _without_workspace(image, target, clip)
+        torch.cuda.synchronize()
+        # Tolerances of the loss parity tests (loss 1e-5 relative).
+        np.testing.assert_allclose(float(loss), float(ref_loss), rtol=1e-5, atol=2e-6)
+        np.testing.assert_allclose(grad.cpu().numpy(), ref_grad.cpu().numpy(), rtol=2e-4, atol=2e-7)
+        np.testing.assert_allclose(float(scale), float(ref_scale), rtol=1e-5)
+        assert np.isfinite(float(loss)) and float(scale) > 0
+
+
+def test_noalloc_loss_rejects_images_above_the_tile_limit():
+    # Rejected before any CUDA call, so this runs without a GPU too.
+    limit = 16384
+    for w, h in ((4097, 2048), (4096, 2049), (65536, 129)):
+        tiles = -(-w // 32) * -(-h // 16)
+        assert tiles > limit
+        p = _params(w, h, True, True)
+        rc = L.lib.gsb_loss_noalloc(None, L.ref(p), None, None, None, None, None)
+        assert rc == GSB_ERR_INVALID
+        assert b"limit of 16384" in L.lib.gsb_last_error()
