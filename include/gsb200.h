@@ -266,7 +266,7 @@ GSB_API int gsb_loss(gsb_stream_t stream, const gsb_loss_params* p, void* worksp
  * caller that cannot afford cudaMalloc's device synchronisation, or a plugin
  * ABI that passes only inputs and outputs.  Same arguments and results as
  * gsb_loss without the workspace; the per-tile temporaries live in a fixed
- * 128 KiB device array inside the library, held on every GPU that loads the
+ * 384 KiB device array inside the library, held on every GPU that loads the
  * library's device code until the process exits.  The call allocates nothing.
  *  - Size limit: ceil(W/32) * ceil(H/16) <= GSB_LOSS_NOALLOC_MAX_TILES
  *    (e.g. 4096 x 2048); larger images return GSB_ERR_INVALID and

@@ -7,49 +7,78 @@
 // blurred once more, grad = blur(p0) + 2x blur(p1) + y blur(p2)
 // + 0.8 sign(x - y) / (3HW).
 //
-// One CTA per 32x16 output tile.  The CTA stages the 52x36 zero-padded patch
-// (10-pixel halo) of all three channels of image and target with coalesced
-// row loads, then per channel runs four separable 11-tap passes in shared
-// memory, each thread producing a run of consecutive outputs from one
-// sliding window held in registers:
-//   1. horizontal window sums of x, x^2, y, y^2, xy    (36 rows x 42 columns)
-//   2. vertical sums -> statistics -> SSIM partials, loss (26 x 42)
-//   3. horizontal blur of the partials                   (26 x 32)
-//   4. vertical blur -> image gradient                   (16 x 32)
-// The gradient tile is written back coalesced after the third channel.  The
-// loss map and the partials never reach global memory.  Per-CTA loss sums
-// and |grad| maxima are reduced by a single-block kernel in a fixed order, so
-// the scalar results are deterministic.
+// The SSIM map needs only four blurred statistics per channel: mu_x, mu_y,
+// E[x^2 + y^2] (sigma_x^2 and sigma_y^2 enter only as their sum) and E[xy].
+// They are carried as two float2 pairs, (mu_x, mu_y) and (E[x^2+y^2], E[xy]),
+// so every tap of every separable pass is two packed f32x2 FMAs (sm_100).
+//
+// One CTA per (32x16 output tile, channel).  The CTA stages the 52x36
+// zero-padded (x, y) patch of its channel (10-pixel halo), then runs four
+// separable 11-tap passes in shared memory.  Each thread owns a run of
+// consecutive outputs and accumulates them in registers while it streams
+// the inputs once (scatter form), so only the run's accumulators are live:
+//   1. vertical sums of the statistics      (26 rows x 52 columns)
+//   2. horizontal sums -> SSIM partials, loss (26 x 42)
+//   3. vertical blur of the partials          (16 x 42)
+//   4. horizontal blur -> image gradient      (16 x 32)
+// Row strides are padded to odd multiples so that lanes walking down a
+// column hit distinct banks.  About 54 KB of shared memory per CTA, so four
+// CTAs (32 warps) share an SM.  Per-CTA loss sums and |grad| maxima are
+// reduced by a single-block kernel in a fixed order, so the scalar results
+// are deterministic.
+#include <atomic>
+#include <cstdio>
+#include <mutex>
+
 #include "gsb_common.cuh"
 
 namespace gsb {
 namespace {
 
-constexpr int kTW = 32, kTH = 16, kR = 5;
-constexpr int kSW = kTW + 2 * kR, kSH = kTH + 2 * kR;  // 42 x 26 statistics region
-constexpr int kPW = kSW + 2 * kR, kPH = kSH + 2 * kR;  // 52 x 36 staged patch
+constexpr int kTW = 32, kTH = 16, kR = 5, kTaps = 2 * kR + 1;
 constexpr int kThreads = 256;
-// Pass shapes: runs of consecutive outputs per thread.
-constexpr int kRunH = 6;   // pass 1: 42 = 7 x 6 columns, 36 rows -> 252 items
-constexpr int kRunV = 5;   // pass 2: 26 rows in 6 runs of 5, 42 columns -> 252 items
-constexpr int kRunHB = 4;  // pass 3: 32 = 8 x 4 columns, 26 rows -> 208 items
-constexpr int kRunVB = 2;  // pass 4: 16 = 8 x 2 rows, 32 columns -> 256 items
-constexpr int kHRows = 6 * kRunV + 2 * kR;  // 40 rows (4 padding rows feed discarded outputs)
+constexpr int kSW = kTW + 2 * kR, kSH = kTH + 2 * kR;  // 42 x 26 statistics region
+constexpr int kPW = kTW + 4 * kR, kPH = kTH + 4 * kR;  // 52 x 36 staged patch
+constexpr int kRun1 = 7, kRuns1 = 4;          // pass 1: 26 rows as 4 runs of 7 (2 spare rows)
+constexpr int kRun2 = 6, kRuns2 = kSW / kRun2;  // pass 2: 42 columns as 7 runs of 6
+constexpr int kRun3 = 4, kRuns3 = kTH / kRun3;  // pass 3: 16 rows as 4 runs of 4
+constexpr int kRun4 = 4, kRuns4 = kTW / kRun4;  // pass 4: 32 columns as 8 runs of 4
+constexpr int kPRows = kRuns1 * kRun1 + 2 * kR;  // 38 staged rows (the 2 spare ones feed discarded outputs)
+static_assert(kPRows >= kPH, "patch rows");
+constexpr int kPStride = kPW + 1, kVStride = kPW + 1, kQStride = kSW + 1;
+static_assert(kRuns1 * kRun1 >= kSH && kRuns2 * kRun2 == kSW, "run cover");
+static_assert(kRuns1 * kPW <= kThreads && kRuns2 * kSH <= kThreads, "pass items");
+static_assert(kRuns3 * kSW <= kThreads && kRuns4 * kTH <= kThreads, "pass items");
 
-// exp(-(d/1.5)^2 / 2) normalised, correctly rounded to float32.
-__constant__ float kTaps[11] = {0.001028380123898387f, 0.0075987582094967365f,
-                                0.036000773310661316f, 0.10936068743467331f,
-                                0.21300554275512695f,  0.26601171493530273f,
-                                0.21300554275512695f,  0.10936068743467331f,
-                                0.036000773310661316f, 0.0075987582094967365f,
-                                0.001028380123898387f};
+// exp(-(d/1.5)^2 / 2) normalised, correctly rounded to float32; d = t - 5.
+__host__ __device__ constexpr float tap(int t)
+{
+    return t == 0 || t == 10 ? 0.001028380123898387f
+         : t == 1 || t == 9  ? 0.0075987582094967365f
+         : t == 2 || t == 8  ? 0.036000773310661316f
+         : t == 3 || t == 7  ? 0.10936068743467331f
+         : t == 4 || t == 6  ? 0.21300554275512695f
+                             : 0.26601171493530273f;
+}
+
+__device__ __forceinline__ float2 tap2(int t) { return make_float2(tap(t), tap(t)); }
 
 struct LossSmem {
-    float x[kPH][kPW * 3];        // image patch, HWC
-    float y[kPH][kPW * 3];        // target patch, HWC (normalised)
-    float h[5][kHRows][kSW];      // horizontal sums; reused for blurred partials
-    float part[3][kSH + 6][kSW];  // partials p0, p1, p2 (+ padding rows)
-    float g[kTH][kTW * 3];        // gradient tile, HWC
+    float2 patch[kPRows][kPStride];  // (x, y) of this channel; x clipped when requested
+    union {
+        float4 v[kRuns1 * kRun1][kVStride];  // pass 1: (mu_x, mu_y, E[x^2+y^2], E[xy]) column sums
+        struct {
+            float2 q01[kTH][kQStride];  // pass 3: vertically blurred partials (p0, p1)
+            float q2[kTH][kQStride];    //         and p2
+        } q;
+    } u;
+    union {
+        struct {
+            float2 p01[kSH][kQStride];  // pass 2: partials (p0, p1)
+            float p2[kSH][kQStride];    //         and p2
+        } p;
+        float g[kTH][kTW + 1];  // pass 4: gradient tile
+    } w;
 };
 
 __device__ __forceinline__ float clip01(float v) { return fminf(fmaxf(v, 0.0f), 1.0f); }
@@ -63,175 +92,207 @@ __device__ __forceinline__ float clip_grad(float v)
 }
 
 template <bool U8, bool CLIP>
-__global__ void __launch_bounds__(kThreads) loss_kernel(int width, int height,
-                                                        const float* __restrict__ image,
-                                                        const void* __restrict__ target_raw,
-                                                        float* __restrict__ grad,
-                                                        float* __restrict__ block_loss,
-                                                        uint32_t* __restrict__ block_scale)
+__global__ void __launch_bounds__(kThreads, 4) loss_kernel(int width, int height,
+                                                           const float* __restrict__ image,
+                                                           const void* __restrict__ target_raw,
+                                                           float* __restrict__ grad,
+                                                           float* __restrict__ block_loss,
+                                                           uint32_t* __restrict__ block_scale)
 {
     extern __shared__ float4 smem_raw[];
     LossSmem& S = *reinterpret_cast<LossSmem*>(smem_raw);
-    float(*hp)[kSH + 6][kTW + 1] = reinterpret_cast<float(*)[kSH + 6][kTW + 1]>(&S.h[0][0][0]);
     __shared__ float warp_loss[kThreads / 32];
     __shared__ uint32_t warp_scale[kThreads / 32];
     const int tid = threadIdx.x;
+    const int c = blockIdx.z;
     const int x0 = blockIdx.x * kTW, y0 = blockIdx.y * kTH;
     const float inv_n = 1.0f / (3.0f * (float)width * (float)height);
     const float weight = -0.2f * inv_n;
     const uint8_t* t8 = static_cast<const uint8_t*>(target_raw);
     const float* tf = static_cast<const float*>(target_raw);
 
-    // Stage the zero-padded patch, all channels (rows are contiguous in HWC).
-    for (int k = tid; k < kPH * kPW * 3; k += kThreads) {
-        int r = k / (kPW * 3), q = k % (kPW * 3);
-        int gx = x0 - 2 * kR + q / 3, gy = y0 + r - 2 * kR;
-        float xv = 0.0f, yv = 0.0f;
-        if (gx >= 0 && gx < width && gy >= 0 && gy < height) {
-            int64_t idx = ((int64_t)gy * width + x0 - 2 * kR) * 3 + q;
-            xv = image[idx];
-            if (CLIP) xv = clip01(xv);
-            yv = U8 ? (float)t8[idx] * (float)(1.0 / 255.0) : tf[idx];
-        }
-        S.x[r][q] = xv;
-        S.y[r][q] = yv;
-    }
-    float loss = 0.0f;
-    for (int c = 0; c < 3; c++) {
-        __syncthreads();
-        // 1. Horizontal window sums (run of kRunH columns per thread).
-        if (tid < kPH * (kSW / kRunH)) {
-            const int r = tid / (kSW / kRunH), q0 = (tid % (kSW / kRunH)) * kRunH;
-            float xs[kRunH + 10], ys[kRunH + 10];
+    // Stage the zero-padded (x, y) patch of channel c: 64-lane rows, 4 rows
+    // per sweep.  Every load of the thread is issued before the first use so
+    // the rows' memory latencies overlap.
+    {
+        constexpr int kSweeps = (kPRows + kThreads / 64 - 1) / (kThreads / 64);
+        const int col = tid & 63, row0 = tid >> 6;
+        const int gx = x0 - 2 * kR + col;
+        const bool col_in = col < kPW && gx >= 0 && gx < width;
+        float xv[kSweeps], yv[kSweeps];
 #pragma unroll
-            for (int t = 0; t < kRunH + 10; t++) {
-                xs[t] = S.x[r][(q0 + t) * 3 + c];
-                ys[t] = S.y[r][(q0 + t) * 3 + c];
-            }
-#pragma unroll
-            for (int o = 0; o < kRunH; o++) {
-                float sx = 0.f, sxx = 0.f, sy = 0.f, syy = 0.f, sxy = 0.f;
-#pragma unroll
-                for (int t = 0; t < 11; t++) {
-                    const float w = kTaps[t], a = xs[o + t], b = ys[o + t];
-                    const float wa = w * a, wb = w * b;
-                    sx += wa;
-                    sxx = fmaf(wa, a, sxx);
-                    sy += wb;
-                    syy = fmaf(wb, b, syy);
-                    sxy = fmaf(wa, b, sxy);
-                }
-                S.h[0][r][q0 + o] = sx;
-                S.h[1][r][q0 + o] = sxx;
-                S.h[2][r][q0 + o] = sy;
-                S.h[3][r][q0 + o] = syy;
-                S.h[4][r][q0 + o] = sxy;
+        for (int k = 0; k < kSweeps; k++) {
+            const int pr = row0 + k * (kThreads / 64);
+            const int gy = y0 - 2 * kR + pr;
+            xv[k] = 0.0f;
+            yv[k] = 0.0f;
+            if (col_in && pr < kPRows && gy >= 0 && gy < height) {
+                const int64_t idx = ((int64_t)gy * width + gx) * 3 + c;
+                xv[k] = __ldg(image + idx);
+                yv[k] = U8 ? (float)__ldg(t8 + idx) : __ldg(tf + idx);
             }
         }
-        __syncthreads();
-        // 2. Vertical sums -> statistics -> partials and loss (run of kRunV rows).
-        if (tid < (kSH + kRunV - 1) / kRunV * kSW) {
-            const int q = tid % kSW, r0 = (tid / kSW) * kRunV;
-            float m[5][kRunV];
+        if (col < kPW) {
 #pragma unroll
-            for (int s = 0; s < 5; s++) {
-                float col[kRunV + 10];
-#pragma unroll
-                for (int t = 0; t < kRunV + 10; t++) col[t] = S.h[s][r0 + t][q];
-#pragma unroll
-                for (int o = 0; o < kRunV; o++) {
-                    float acc = 0.f;
-#pragma unroll
-                    for (int t = 0; t < 11; t++) acc = fmaf(kTaps[t], col[o + t], acc);
-                    m[s][o] = acc;
+            for (int k = 0; k < kSweeps; k++) {
+                const int pr = row0 + k * (kThreads / 64);
+                if (pr < kPRows) {
+                    const float x = CLIP ? clip01(xv[k]) : xv[k];
+                    const float y = U8 ? yv[k] * (float)(1.0 / 255.0) : yv[k];
+                    S.patch[pr][col] = make_float2(x, y);
                 }
-            }
-            const int gx = x0 + q - kR;
-#pragma unroll
-            for (int o = 0; o < kRunV; o++) {
-                const int r = r0 + o;
-                const int gy = y0 + r - kR;
-                float p0 = 0.f, p1 = 0.f, p2 = 0.f;
-                if (r < kSH && gx >= 0 && gx < width && gy >= 0 && gy < height) {
-                    const float mx = m[0][o], xx = m[1][o], my = m[2][o], yy = m[3][o], xy = m[4][o];
-                    const float A = mx * mx + my * my + 1e-4f;
-                    const float B = (xx - mx * mx) + (yy - my * my) + 9e-4f;
-                    const float Cc = 2.0f * mx * my + 1e-4f;
-                    const float D = 2.0f * (xy - mx * my) + 9e-4f;
-                    const float inv_a = 1.0f / A, inv_b = 1.0f / B;
-                    const float inv_ab = inv_a * inv_b;
-                    const float ssim = Cc * D * inv_ab;
-                    p0 = (2.0f * my * (D - Cc) * inv_ab + 2.0f * mx * ssim * (inv_b - inv_a)) * weight;
-                    p1 = -ssim * inv_b * weight;
-                    p2 = 2.0f * Cc * inv_ab * weight;
-                    if (r >= kR && r < kR + kTH && q >= kR && q < kR + kTW) {
-                        const float xv = S.x[r + kR][(q + kR) * 3 + c];
-                        const float yv = S.y[r + kR][(q + kR) * 3 + c];
-                        loss += 0.2f * (1.0f - ssim) + 0.8f * fabsf(xv - yv);
-                    }
-                }
-                S.part[0][r][q] = p0;
-                S.part[1][r][q] = p1;
-                S.part[2][r][q] = p2;
-            }
-        }
-        __syncthreads();
-        // 3. Horizontal blur of the partials onto the tile columns.
-        if (tid < kSH * (kTW / kRunHB)) {
-            const int r = tid / (kTW / kRunHB), q0 = (tid % (kTW / kRunHB)) * kRunHB;
-#pragma unroll
-            for (int k = 0; k < 3; k++) {
-                float row[kRunHB + 10];
-#pragma unroll
-                for (int t = 0; t < kRunHB + 10; t++) row[t] = S.part[k][r][q0 + t];
-#pragma unroll
-                for (int o = 0; o < kRunHB; o++) {
-                    float acc = 0.f;
-#pragma unroll
-                    for (int t = 0; t < 11; t++) acc = fmaf(kTaps[t], row[o + t], acc);
-                    hp[k][r][q0 + o] = acc;
-                }
-            }
-        }
-        __syncthreads();
-        // 4. Vertical blur -> image gradient (run of kRunVB rows).
-        {
-            const int q = tid % kTW, r0 = (tid / kTW) * kRunVB;
-            float acc[3][kRunVB];
-#pragma unroll
-            for (int k = 0; k < 3; k++) {
-                float col[kRunVB + 10];
-#pragma unroll
-                for (int t = 0; t < kRunVB + 10; t++) col[t] = hp[k][r0 + t][q];
-#pragma unroll
-                for (int o = 0; o < kRunVB; o++) {
-                    float a = 0.f;
-#pragma unroll
-                    for (int t = 0; t < 11; t++) a = fmaf(kTaps[t], col[o + t], a);
-                    acc[k][o] = a;
-                }
-            }
-#pragma unroll
-            for (int o = 0; o < kRunVB; o++) {
-                const int r = r0 + o;
-                const float xv = S.x[r + 2 * kR][(q + 2 * kR) * 3 + c];
-                const float yv = S.y[r + 2 * kR][(q + 2 * kR) * 3 + c];
-                const float sign = xv > yv ? 1.0f : (xv < yv ? -1.0f : 0.0f);
-                S.g[r][q * 3 + c] = acc[0][o] + 2.0f * xv * acc[1][o] + yv * acc[2][o] +
-                                    0.8f * sign * inv_n;
             }
         }
     }
     __syncthreads();
-    // Coalesced write of the gradient tile (and its |max| for the scale).
+    // 1. Vertical window sums of (x, y) and (x^2 + y^2, xy).
+    if (tid < kRuns1 * kPW) {
+        const int q = tid % kPW, r0 = (tid / kPW) * kRun1;
+        float2 m[kRun1], s[kRun1];
+#pragma unroll
+        for (int o = 0; o < kRun1; o++) m[o] = s[o] = make_float2(0.0f, 0.0f);
+#pragma unroll
+        for (int j = 0; j < kRun1 + 2 * kR; j++) {
+            const float2 v = S.patch[r0 + j][q];
+            const float2 sq = __fmul2_rn(v, v);
+            const float2 u = make_float2(sq.x + sq.y, v.x * v.y);
+#pragma unroll
+            for (int o = 0; o < kRun1; o++) {
+                const int t = j - o;
+                if (t >= 0 && t < kTaps) {
+                    m[o] = __ffma2_rn(tap2(t), v, m[o]);
+                    s[o] = __ffma2_rn(tap2(t), u, s[o]);
+                }
+            }
+        }
+#pragma unroll
+        for (int o = 0; o < kRun1; o++)
+            S.u.v[r0 + o][q] = make_float4(m[o].x, m[o].y, s[o].x, s[o].y);
+    }
+    __syncthreads();
+    // 2. Horizontal sums -> statistics -> SSIM partials (zero outside the
+    // image) and the SSIM part of the loss on the tile's own pixels.
+    float loss = 0.0f;
+    if (tid < kRuns2 * kSH) {
+        const int r = tid % kSH, c0 = (tid / kSH) * kRun2;
+        float2 m[kRun2], s[kRun2];
+#pragma unroll
+        for (int o = 0; o < kRun2; o++) m[o] = s[o] = make_float2(0.0f, 0.0f);
+#pragma unroll
+        for (int j = 0; j < kRun2 + 2 * kR; j++) {
+            const float4 v = S.u.v[r][c0 + j];
+            const float2 a = make_float2(v.x, v.y), b = make_float2(v.z, v.w);
+#pragma unroll
+            for (int o = 0; o < kRun2; o++) {
+                const int t = j - o;
+                if (t >= 0 && t < kTaps) {
+                    m[o] = __ffma2_rn(tap2(t), a, m[o]);
+                    s[o] = __ffma2_rn(tap2(t), b, s[o]);
+                }
+            }
+        }
+        const int gy = y0 - kR + r;
+        const bool row_in = gy >= 0 && gy < height;
+        const bool row_own = r >= kR && r < kR + kTH;
+#pragma unroll
+        for (int o = 0; o < kRun2; o++) {
+            const int cc = c0 + o;
+            const int gx = x0 - kR + cc;
+            float p0 = 0.0f, p1 = 0.0f, p2 = 0.0f;
+            if (row_in && gx >= 0 && gx < width) {
+                const float mx = m[o].x, my = m[o].y;
+                const float mxy = mx * my;
+                const float mm = fmaf(mx, mx, my * my);
+                const float A = mm + 1e-4f;
+                const float B = (s[o].x - mm) + 9e-4f;
+                const float Cc = fmaf(2.0f, mxy, 1e-4f);
+                const float D = fmaf(2.0f, s[o].y - mxy, 9e-4f);
+                const float inv_a = __fdividef(1.0f, A), inv_b = __fdividef(1.0f, B);
+                const float inv_ab = inv_a * inv_b;
+                const float ssim = Cc * D * inv_ab;
+                p0 = (my * (D - Cc) * inv_ab + mx * ssim * (inv_b - inv_a)) * (2.0f * weight);
+                p1 = -ssim * inv_b * weight;
+                p2 = 2.0f * Cc * inv_ab * weight;
+                if (row_own && cc >= kR && cc < kR + kTW) loss += 0.2f * (1.0f - ssim);
+            }
+            S.w.p.p01[r][cc] = make_float2(p0, p1);
+            S.w.p.p2[r][cc] = p2;
+        }
+    }
+    __syncthreads();
+    // 3. Vertical blur of the partials onto the tile rows.
+    if (tid < kRuns3 * kSW) {
+        const int cc = tid % kSW, r0 = (tid / kSW) * kRun3;
+        float2 a[kRun3];
+        float b[kRun3];
+#pragma unroll
+        for (int o = 0; o < kRun3; o++) {
+            a[o] = make_float2(0.0f, 0.0f);
+            b[o] = 0.0f;
+        }
+#pragma unroll
+        for (int j = 0; j < kRun3 + 2 * kR; j++) {
+            const float2 u = S.w.p.p01[r0 + j][cc];
+            const float v = S.w.p.p2[r0 + j][cc];
+#pragma unroll
+            for (int o = 0; o < kRun3; o++) {
+                const int t = j - o;
+                if (t >= 0 && t < kTaps) {
+                    a[o] = __ffma2_rn(tap2(t), u, a[o]);
+                    b[o] = fmaf(tap(t), v, b[o]);
+                }
+            }
+        }
+#pragma unroll
+        for (int o = 0; o < kRun3; o++) {
+            S.u.q.q01[r0 + o][cc] = a[o];
+            S.u.q.q2[r0 + o][cc] = b[o];
+        }
+    }
+    __syncthreads();
+    // 4. Horizontal blur -> image gradient; the L1 part of the loss.
+    if (tid < kRuns4 * kTH) {
+        const int r = tid % kTH, c0 = (tid / kTH) * kRun4;
+        float2 a[kRun4];
+        float b[kRun4];
+#pragma unroll
+        for (int o = 0; o < kRun4; o++) {
+            a[o] = make_float2(0.0f, 0.0f);
+            b[o] = 0.0f;
+        }
+#pragma unroll
+        for (int j = 0; j < kRun4 + 2 * kR; j++) {
+            const float2 u = S.u.q.q01[r][c0 + j];
+            const float v = S.u.q.q2[r][c0 + j];
+#pragma unroll
+            for (int o = 0; o < kRun4; o++) {
+                const int t = j - o;
+                if (t >= 0 && t < kTaps) {
+                    a[o] = __ffma2_rn(tap2(t), u, a[o]);
+                    b[o] = fmaf(tap(t), v, b[o]);
+                }
+            }
+        }
+        const bool row_in = y0 + r < height;
+#pragma unroll
+        for (int o = 0; o < kRun4; o++) {
+            const int col = c0 + o;
+            const float2 xy = S.patch[r + 2 * kR][col + 2 * kR];
+            const float sign = xy.x > xy.y ? 1.0f : (xy.x < xy.y ? -1.0f : 0.0f);
+            S.w.g[r][col] = a[o].x + 2.0f * xy.x * a[o].y + xy.y * b[o] + 0.8f * sign * inv_n;
+            if (row_in && x0 + col < width) loss += 0.8f * fabsf(xy.x - xy.y);
+        }
+    }
+    __syncthreads();
+    // Write the gradient tile (and its |max| for the scale).
     uint32_t scale_bits = 0;
-    for (int k = tid; k < kTH * kTW * 3; k += kThreads) {
-        const int r = k / (kTW * 3), q = k % (kTW * 3);
-        const int px = x0 + q / 3, py = y0 + r;
+    for (int k = tid; k < kTH * kTW; k += kThreads) {
+        const int r = k / kTW, col = k % kTW;
+        const int px = x0 + col, py = y0 + r;
         if (px < width && py < height) {
-            const int64_t idx = ((int64_t)py * width + x0) * 3 + q;
-            float value = S.g[r][q];
-            if (CLIP) value *= clip_grad(image[idx]);
+            const int64_t idx = ((int64_t)py * width + px) * 3 + c;
+            float value = S.w.g[r][col];
+            if (CLIP) value *= clip_grad(__ldg(image + idx));
             grad[idx] = value;
             scale_bits = max(scale_bits, __float_as_uint(value) & 0x7fffffffu);
         }
@@ -251,7 +312,7 @@ __global__ void __launch_bounds__(kThreads) loss_kernel(int width, int height,
             total += warp_loss[w];
             sb = max(sb, warp_scale[w]);
         }
-        const int b = blockIdx.y * gridDim.x + blockIdx.x;
+        const int b = (blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x;
         block_loss[b] = total;
         block_scale[b] = sb;
     }
@@ -294,7 +355,75 @@ __global__ void __launch_bounds__(1024) loss_finish_kernel(int blocks, float inv
     }
 }
 
-int loss_blocks(const gsb_loss_params& p) { return ceil_div(p.width, kTW) * ceil_div(p.height, kTH); }
+
+// 32x16 output tiles of one channel; the kernel runs one CTA per tile and channel.
+int64_t loss_tiles(const gsb_loss_params& p)
+{
+    return (int64_t)ceil_div(p.width, kTW) * ceil_div(p.height, kTH);
+}
+
+bool loss_shape_ok(const gsb_loss_params& p)
+{
+    return p.width > 0 && p.height > 0 && ceil_div(p.height, kTH) <= 65535 &&
+           loss_tiles(p) <= (int64_t)1 << 28;
+}
+
+// The kernels need more than 48 KB of dynamic shared memory: opt in once per
+// device (a host-side function attribute; it never enters a graph capture).
+std::atomic<uint64_t> g_loss_configured{0};
+
+int configure_loss_kernels()
+{
+    int dev = 0;
+    cudaError_t err = cudaGetDevice(&dev);
+    if (err != cudaSuccess) {
+        set_error(err);
+        return GSB_ERR_LAUNCH;
+    }
+    const uint64_t bit = dev >= 0 && dev < 64 ? (uint64_t)1 << dev : 0;
+    if (bit && (g_loss_configured.load(std::memory_order_acquire) & bit)) return GSB_OK;
+    const int smem = (int)sizeof(LossSmem);
+    const void* kernels[4] = {(const void*)loss_kernel<true, true>,
+                              (const void*)loss_kernel<true, false>,
+                              (const void*)loss_kernel<false, true>,
+                              (const void*)loss_kernel<false, false>};
+    for (const void* k : kernels) {
+        err = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (err != cudaSuccess) {
+            set_error(err);
+            return GSB_ERR_LAUNCH;
+        }
+    }
+    g_loss_configured.fetch_or(bit, std::memory_order_acq_rel);
+    return GSB_OK;
+}
+
+// Loss kernel + fixed-order finish.  block_loss / block_scale hold one slot
+// per (tile, channel).
+int launch_loss(cudaStream_t s, const gsb_loss_params& p, const float* image, const void* target,
+                float* loss, float* grad, float* scale, float* block_loss, uint32_t* block_scale)
+{
+    dim3 grid(ceil_div(p.width, kTW), ceil_div(p.height, kTH), 3);
+    const size_t smem = sizeof(LossSmem);
+    auto launch = [&](auto kernel) {
+        kernel<<<grid, kThreads, smem, s>>>(p.width, p.height, image, target, grad, block_loss,
+                                            block_scale);
+    };
+    if (p.target_u8) {
+        if (p.clip_input) launch(loss_kernel<true, true>);
+        else launch(loss_kernel<true, false>);
+    } else {
+        if (p.clip_input) launch(loss_kernel<false, true>);
+        else launch(loss_kernel<false, false>);
+    }
+    if (int e = check_launch()) return e;
+    const float inv_n = 1.0f / (3.0f * (float)p.width * (float)p.height);
+    loss_finish_kernel<<<1, 1024, 0, s>>>((int)(3 * loss_tiles(p)), inv_n, block_loss, block_scale,
+                                          loss, scale);
+    return check_launch();
+}
+
+size_t slot_bytes(const gsb_loss_params& p) { return ((size_t)(3 * loss_tiles(p)) * 4 + 255) & ~size_t(255); }
 
 }  // namespace
 }  // namespace gsb
@@ -303,8 +432,8 @@ using namespace gsb;
 
 extern "C" size_t gsb_loss_workspace_size(const gsb_loss_params* p)
 {
-    if (!p || p->width <= 0 || p->height <= 0) return 0;
-    return 2 * (((size_t)loss_blocks(*p) * 4 + 255) & ~size_t(255));
+    if (!p || !loss_shape_ok(*p)) return 0;
+    return 2 * slot_bytes(*p);
 }
 
 extern "C" int gsb_loss(gsb_stream_t stream, const gsb_loss_params* p, void* workspace,
@@ -312,38 +441,15 @@ extern "C" int gsb_loss(gsb_stream_t stream, const gsb_loss_params* p, void* wor
                         float* grad, float* scale)
 {
     if (!p) return GSB_ERR_NULL;
-    if (p->width <= 0 || p->height <= 0) return GSB_ERR_INVALID;
+    if (!loss_shape_ok(*p)) return GSB_ERR_INVALID;
     if (!workspace || workspace_bytes < gsb_loss_workspace_size(p)) return GSB_ERR_WORKSPACE;
     if (!image || !target || !loss || !grad) return GSB_ERR_NULL;
-    cudaStream_t s = as_stream(stream);
-    int blocks = loss_blocks(*p);
-    size_t half = ((size_t)blocks * 4 + 255) & ~size_t(255);
+    if (int e = configure_loss_kernels()) return e;
     float* block_loss = static_cast<float*>(workspace);
-    uint32_t* block_scale = reinterpret_cast<uint32_t*>(static_cast<char*>(workspace) + half);
-    dim3 grid(ceil_div(p->width, kTW), ceil_div(p->height, kTH));
-    size_t smem = sizeof(LossSmem);
-    // The shared-memory opt-in is set once per process (one device per
-    // process); it is a host-side attribute, so graph captures never see it.
-    static bool configured[4] = {false, false, false, false};
-    auto launch = [&](auto kernel, int which) {
-        if (!configured[which]) {
-            cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-            configured[which] = true;
-        }
-        kernel<<<grid, kThreads, smem, s>>>(p->width, p->height, image, target, grad, block_loss,
-                                            block_scale);
-    };
-    if (p->target_u8) {
-        if (p->clip_input) launch(loss_kernel<true, true>, 0);
-        else launch(loss_kernel<true, false>, 1);
-    } else {
-        if (p->clip_input) launch(loss_kernel<false, true>, 2);
-        else launch(loss_kernel<false, false>, 3);
-    }
-    if (int e = check_launch()) return e;
-    float inv_n = 1.0f / (3.0f * (float)p->width * (float)p->height);
-    loss_finish_kernel<<<1, 1024, 0, s>>>(blocks, inv_n, block_loss, block_scale, loss, scale);
-    return check_launch();
+    uint32_t* block_scale =
+        reinterpret_cast<uint32_t*>(static_cast<char*>(workspace) + slot_bytes(*p));
+    return launch_loss(as_stream(stream), *p, image, target, loss, grad, scale, block_loss,
+                       block_scale);
 }
 
 // ---------------------------------------------------------------------------
@@ -358,14 +464,14 @@ extern "C" int gsb_loss(gsb_stream_t stream, const gsb_loss_params* p, void* wor
 // device, stalling every stream a latency-bound caller keeps busy; and a
 // plugin boundary that passes only input and output pointers gives the
 // callee nowhere to put a workspace.  gsb_loss needs 2 x 4 bytes per 32x16
-// output tile of temporaries (per-tile loss sums and |grad| maxima).  Here
-// they live in the fixed array below, part of this library's device image.
+// tile and channel of temporaries (loss sums and |grad| maxima).  Here they
+// live in the fixed array below, part of this library's device image.
 //
 // Limits and sharing:
-//  * kNoallocMaxTiles tiles of 32x16 pixels (4096 x 2048 pixels, or any
-//    image with ceil(W/32) * ceil(H/16) <= 16384); larger images are
+//  * GSB_LOSS_NOALLOC_MAX_TILES tiles of 32x16 pixels (4096 x 2048 pixels,
+//    or any image with ceil(W/32) * ceil(H/16) <= 16384); larger images are
 //    rejected with GSB_ERR_INVALID and a message in gsb_last_error().
-//  * The array takes 128 KiB on every GPU on which this library's device
+//  * The array takes 384 KiB on every GPU on which this library's device
 //    code is loaded, until the process exits.
 //  * Every call on a device shares the one array.  Nothing in it needs to
 //    start at zero: each CTA overwrites its own slots before the finishing
@@ -378,18 +484,15 @@ extern "C" int gsb_loss(gsb_stream_t stream, const gsb_loss_params* p, void* wor
 //    shared-memory limit on that device; make that first call before any
 //    stream capture begins.  Later calls only read the cached address.
 // ---------------------------------------------------------------------------
-#include <atomic>
-#include <cstdio>
-#include <mutex>
-
 namespace gsb {
 namespace {
 
 constexpr int kNoallocMaxTiles = GSB_LOSS_NOALLOC_MAX_TILES;
+constexpr int kNoallocSlots = 3 * kNoallocMaxTiles;  // one per tile and channel
 constexpr int kNoallocMaxDevices = 64;
 
-// [0, max) per-tile loss sums (float bits), [max, 2 max) per-tile |grad| maxima.
-static __device__ __align__(256) uint32_t g_loss_scratch[2 * kNoallocMaxTiles];
+// [0, slots) loss sums (float bits), [slots, 2 slots) |grad| maxima.
+static __device__ __align__(256) uint32_t g_loss_scratch[2 * kNoallocSlots];
 
 std::mutex g_noalloc_mutex;
 std::atomic<void*> g_noalloc_scratch[kNoallocMaxDevices];
@@ -419,18 +522,6 @@ int noalloc_scratch(void** out)
                 set_error(err != cudaSuccess ? err : cudaErrorInvalidSymbol);
                 return GSB_ERR_LAUNCH;
             }
-            const int smem = (int)sizeof(LossSmem);
-            const void* kernels[4] = {(const void*)loss_kernel<true, true>,
-                                      (const void*)loss_kernel<true, false>,
-                                      (const void*)loss_kernel<false, true>,
-                                      (const void*)loss_kernel<false, false>};
-            for (const void* k : kernels) {
-                err = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-                if (err != cudaSuccess) {
-                    set_error(err);
-                    return GSB_ERR_LAUNCH;
-                }
-            }
             g_noalloc_scratch[dev].store(ptr, std::memory_order_release);
         }
     }
@@ -446,7 +537,7 @@ extern "C" int gsb_loss_noalloc(gsb_stream_t stream, const gsb_loss_params* p, c
 {
     if (!p) return GSB_ERR_NULL;
     if (p->width <= 0 || p->height <= 0) return GSB_ERR_INVALID;
-    const int64_t tiles = (int64_t)ceil_div(p->width, kTW) * ceil_div(p->height, kTH);
+    const int64_t tiles = loss_tiles(*p);
     if (tiles > kNoallocMaxTiles) {
         char msg[200];
         std::snprintf(msg, sizeof(msg),
@@ -459,25 +550,9 @@ extern "C" int gsb_loss_noalloc(gsb_stream_t stream, const gsb_loss_params* p, c
     if (!image || !target || !loss || !grad) return GSB_ERR_NULL;
     void* scratch = nullptr;
     if (int e = noalloc_scratch(&scratch)) return e;
+    if (int e = configure_loss_kernels()) return e;
     float* block_loss = static_cast<float*>(scratch);
-    uint32_t* block_scale = static_cast<uint32_t*>(scratch) + kNoallocMaxTiles;
-    cudaStream_t s = as_stream(stream);
-    const int blocks = (int)tiles;
-    dim3 grid(ceil_div(p->width, kTW), ceil_div(p->height, kTH));
-    const size_t smem = sizeof(LossSmem);
-    auto launch = [&](auto kernel) {
-        kernel<<<grid, kThreads, smem, s>>>(p->width, p->height, image, target, grad, block_loss,
-                                            block_scale);
-    };
-    if (p->target_u8) {
-        if (p->clip_input) launch(loss_kernel<true, true>);
-        else launch(loss_kernel<true, false>);
-    } else {
-        if (p->clip_input) launch(loss_kernel<false, true>);
-        else launch(loss_kernel<false, false>);
-    }
-    if (int e = check_launch()) return e;
-    float inv_n = 1.0f / (3.0f * (float)p->width * (float)p->height);
-    loss_finish_kernel<<<1, 1024, 0, s>>>(blocks, inv_n, block_loss, block_scale, loss, scale);
-    return check_launch();
+    uint32_t* block_scale = static_cast<uint32_t*>(scratch) + kNoallocSlots;
+    return launch_loss(as_stream(stream), *p, image, target, loss, grad, scale, block_loss,
+                       block_scale);
 }

@@ -151,11 +151,86 @@ __device__ __forceinline__ uint32_t bit_word(int32_t start, int tile, int batch,
     return (uint32_t)(((start >> 5) + tile + batch) * warps + warp);
 }
 
-struct Stash {
-    float4 r0[32], r1[32], r2[32];
-    int32_t id[32];
-    float depth[32];
+// Lane arithmetic over the lane's ROWS pixels: with two rows every add, mul
+// and fma is one packed f32x2 instruction (sm_100), rounded exactly like its
+// scalar form, so one- and two-row kernels produce identical fragments.
+template <int ROWS>
+struct Vec;
+
+template <>
+struct Vec<2> {
+    using T = float2;
+    static __device__ __forceinline__ T add(T a, T b) { return __fadd2_rn(a, b); }
+    static __device__ __forceinline__ T mul(T a, T b) { return __fmul2_rn(a, b); }
+    static __device__ __forceinline__ T fma(T a, T b, T c) { return __ffma2_rn(a, b, c); }
+    static __device__ __forceinline__ T lo(float4 v) { return make_float2(v.x, v.y); }
+    static __device__ __forceinline__ T hi(float4 v) { return make_float2(v.z, v.w); }
+    static __device__ __forceinline__ T splat(float x) { return make_float2(x, x); }
+    static __device__ __forceinline__ float get(T v, int r) { return r ? v.y : v.x; }
+    static __device__ __forceinline__ void set(T& v, int r, float x)
+    {
+        if (r) v.y = x;
+        else v.x = x;
+    }
 };
+
+template <>
+struct Vec<1> {
+    using T = float;
+    static __device__ __forceinline__ T add(T a, T b) { return __fadd_rn(a, b); }
+    static __device__ __forceinline__ T mul(T a, T b) { return __fmul_rn(a, b); }
+    static __device__ __forceinline__ T fma(T a, T b, T c) { return __fmaf_rn(a, b, c); }
+    static __device__ __forceinline__ T lo(float4 v) { return v.x; }
+    static __device__ __forceinline__ T hi(float4 v) { return v.z; }
+    static __device__ __forceinline__ T splat(float x) { return x; }
+    static __device__ __forceinline__ float get(T v, int) { return v; }
+    static __device__ __forceinline__ void set(T& v, int, float x) { v = x; }
+};
+
+// Per-warp stash of up to 32 staged splats, every scalar duplicated so that
+// one broadcast shared load yields the (value, value) operand of a packed
+// instruction.
+struct Stash {
+    float4 q0[32];     // (-mean_x, -mean_x, -mean_y, -mean_y)
+    float4 q1[32];     // (c00', c00', c10', c10')   c' = -c / 2
+    float4 q2[32];     // (c01', c01', c11', c11')
+    float4 q3[32];     // (opacity, opacity, red, red)
+    float4 q4[32];     // (green, green, blue, blue)
+    float2 depth[32];  // (depth, depth)
+    int32_t id[32];
+};
+
+__device__ __forceinline__ void stash_splat(Stash& st, int lane, float4 r0, float4 r1, float4 r2)
+{
+    st.q0[lane] = make_float4(-r0.x, -r0.x, -r0.y, -r0.y);
+    st.q1[lane] = make_float4(r1.x, r1.x, r1.z, r1.z);
+    st.q2[lane] = make_float4(r1.y, r1.y, r1.w, r1.w);
+    st.q3[lane] = make_float4(r2.w, r2.w, r2.x, r2.x);
+    st.q4[lane] = make_float4(r2.y, r2.y, r2.z, r2.z);
+}
+
+// Offsets and power of splat k at the lane's pixels, in the oracle's order:
+// power = dy * (c11' dy + c10' dx) + dx * (c01' dy + c00' dx), fused.
+template <int ROWS>
+struct Fragment {
+    typename Vec<ROWS>::T dx, dy, power;
+};
+
+template <int ROWS>
+__device__ __forceinline__ Fragment<ROWS> fragment(const Stash& st, int k,
+                                                   typename Vec<ROWS>::T pcx,
+                                                   typename Vec<ROWS>::T pcy)
+{
+    using V = Vec<ROWS>;
+    const float4 q0 = st.q0[k], q1 = st.q1[k], q2 = st.q2[k];
+    Fragment<ROWS> f;
+    f.dx = V::add(pcx, V::lo(q0));
+    f.dy = V::add(pcy, V::hi(q0));
+    const auto t1 = V::fma(V::lo(q2), f.dy, V::mul(V::lo(q1), f.dx));
+    const auto t2 = V::fma(V::hi(q2), f.dy, V::mul(V::hi(q1), f.dx));
+    f.power = V::fma(f.dy, t2, V::mul(f.dx, t1));
+    return f;
+}
 
 template <int ROWS, bool WANT_DEPTH>
 __global__ void __launch_bounds__(256) raster_fwd_kernel(
@@ -166,6 +241,8 @@ __global__ void __launch_bounds__(256) raster_fwd_kernel(
     float* __restrict__ final_t, int32_t* __restrict__ last_out,
     int32_t* __restrict__ backward_work, uint32_t* __restrict__ bits)
 {
+    using V = Vec<ROWS>;
+    using T = typename V::T;
     extern __shared__ Stash stash_all[];
     __shared__ int tile_work;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, warps = blockDim.x >> 5;
@@ -174,16 +251,14 @@ __global__ void __launch_bounds__(256) raster_fwd_kernel(
     const Geom<ROWS> tg = geom<ROWS>(p.width, p.tile_w, p.tile_h, tile, warp, lane);
     if (threadIdx.x == 0) tile_work = 0;
     const int32_t start = offsets[tile], end = offsets[tile + 1];
-    const float pcx = (float)tg.px + 0.5f;
+    const T pcx = V::splat((float)tg.px + 0.5f);
     const float bx0 = (float)tg.bx0, by0 = (float)tg.by0;
-    float pcy[ROWS], T[ROWS], cr[ROWS], cg[ROWS], cb[ROWS], cd[ROWS];
+    T pcy, trans = V::splat(1.0f), cr = V::splat(0.0f), cg = cr, cb = cr, cd = cr;
     int32_t last[ROWS];
     bool active[ROWS];
 #pragma unroll
     for (int r = 0; r < ROWS; r++) {
-        pcy[r] = (float)(tg.py0 + r) + 0.5f;
-        T[r] = 1.0f;
-        cr[r] = cg[r] = cb[r] = cd[r] = 0.0f;
+        V::set(pcy, r, (float)(tg.py0 + r) + 0.5f);
         last[r] = end;
         active[r] = tg.px < p.width && tg.py0 + r < p.height;
     }
@@ -200,10 +275,11 @@ __global__ void __launch_bounds__(256) raster_fwd_kernel(
             float4 r0 = __ldg(rec);
             hit = block_hit<ROWS>(r0, bx0, by0);
             if (hit) {
-                st.r0[lane] = r0;
-                st.r1[lane] = __ldg(rec + 1);
-                st.r2[lane] = __ldg(rec + 2);
-                if (WANT_DEPTH) st.depth[lane] = __ldg(depth + g);
+                stash_splat(st, lane, r0, __ldg(rec + 1), __ldg(rec + 2));
+                if (WANT_DEPTH) {
+                    const float d = __ldg(depth + g);
+                    st.depth[lane] = make_float2(d, d);
+                }
             }
         }
         unsigned mask = __ballot_sync(GSB_FULL_MASK, hit);
@@ -212,36 +288,43 @@ __global__ void __launch_bounds__(256) raster_fwd_kernel(
         while (mask) {
             const int k = __ffs(mask) - 1;
             mask &= mask - 1;
-            const float4 r0 = st.r0[k], r1 = st.r1[k], r2 = st.r2[k];
-            const float dx = pcx - r0.x;
-            const float ax = __fmul_rn(r1.x, dx), bx = __fmul_rn(r1.z, dx);
+            const Fragment<ROWS> f = fragment<ROWS>(st, k, pcx, pcy);
+            const float4 q3 = st.q3[k], q4 = st.q4[k];
+            T e;
+#pragma unroll
+            for (int r = 0; r < ROWS; r++) V::set(e, r, __expf(V::get(f.power, r)));
+            const T raw = V::mul(V::lo(q3), e);
+            T a;
             bool valid_any = false;
-            const int32_t next = base + k + 1;
+            bool valid[ROWS];
 #pragma unroll
             for (int r = 0; r < ROWS; r++) {
-                const float dy = pcy[r] - r0.y;
-                const float t1 = __fmaf_rn(r1.y, dy, ax);
-                const float t2 = __fmaf_rn(r1.w, dy, bx);
-                const float power = __fmaf_rn(dy, t2, __fmul_rn(dx, t1));
-                const float raw = r2.w * __expf(power);
-                const bool valid = active[r] && power <= 0.0f && raw >= kMinAlpha;
+                const float rr = V::get(raw, r);
+                valid[r] = active[r] && V::get(f.power, r) <= 0.0f && rr >= kMinAlpha;
                 // Branch-free: with a = 0 every update below is an exact no-op.
-                const float a = valid ? fminf(kMaxAlpha, raw) : 0.0f;
-                const float w = a * T[r];
-                cr[r] = __fmaf_rn(w, r2.x, cr[r]);
-                cg[r] = __fmaf_rn(w, r2.y, cg[r]);
-                cb[r] = __fmaf_rn(w, r2.z, cb[r]);
-                if (WANT_DEPTH) cd[r] = __fmaf_rn(w, st.depth[k], cd[r]);
-                T[r] = T[r] * (1.0f - a);
-                const bool stop = valid && T[r] < kMinT;
-                last[r] = stop ? next : last[r];
-                active[r] = active[r] && !stop;
-                valid_any |= valid;
+                V::set(a, r, valid[r] ? fminf(kMaxAlpha, rr) : 0.0f);
+                valid_any |= valid[r];
             }
-            if (__ballot_sync(GSB_FULL_MASK, valid_any)) contributed |= 1u << k;
+            const T w = V::mul(a, trans);
+            cr = V::fma(w, V::hi(q3), cr);
+            cg = V::fma(w, V::lo(q4), cg);
+            cb = V::fma(w, V::hi(q4), cb);
+            if (WANT_DEPTH) {
+                const float2 d = st.depth[k];
+                cd = V::fma(w, V::lo(make_float4(d.x, d.y, d.x, d.y)), cd);
+            }
+            // T (1 - a), with 1 - a formed as fma(a, -1, 1) (exact same rounding).
+            trans = V::mul(trans, V::fma(a, V::splat(-1.0f), V::splat(1.0f)));
+            const int32_t next = base + k + 1;
             any_active = false;
 #pragma unroll
-            for (int r = 0; r < ROWS; r++) any_active |= active[r];
+            for (int r = 0; r < ROWS; r++) {
+                const bool stop = valid[r] && V::get(trans, r) < kMinT;
+                last[r] = stop ? next : last[r];
+                active[r] = active[r] && !stop;
+                any_active |= active[r];
+            }
+            if (__ballot_sync(GSB_FULL_MASK, valid_any)) contributed |= 1u << k;
             if (!__any_sync(GSB_FULL_MASK, any_active)) break;
         }
         if (lane == 0) bits[bit_word(start, tile, batch, warps, warp)] = contributed;
@@ -253,12 +336,13 @@ __global__ void __launch_bounds__(256) raster_fwd_kernel(
         const int y = tg.py0 + r;
         if (tg.px < p.width && y < p.height) {
             const int64_t pix = (int64_t)y * p.width + tg.px;
-            rgb[pix * 3] = cr[r] + T[r] * __ldg(background);
-            rgb[pix * 3 + 1] = cg[r] + T[r] * __ldg(background + 1);
-            rgb[pix * 3 + 2] = cb[r] + T[r] * __ldg(background + 2);
-            if (out_depth) out_depth[pix] = cd[r];
-            if (out_alpha) out_alpha[pix] = 1.0f - T[r];
-            final_t[pix] = T[r];
+            const float t = V::get(trans, r);
+            rgb[pix * 3] = V::get(cr, r) + t * __ldg(background);
+            rgb[pix * 3 + 1] = V::get(cg, r) + t * __ldg(background + 1);
+            rgb[pix * 3 + 2] = V::get(cb, r) + t * __ldg(background + 2);
+            if (out_depth) out_depth[pix] = V::get(cd, r);
+            if (out_alpha) out_alpha[pix] = 1.0f - t;
+            final_t[pix] = t;
             last_out[pix] = last[r];
             work = max(work, last[r] - start);
         }
@@ -299,6 +383,15 @@ __device__ __forceinline__ float warp_sum8(float v[8], int lane)
     return s;
 }
 
+template <int ROWS>
+__device__ __forceinline__ float row_sum(typename Vec<ROWS>::T v)
+{
+    float s = Vec<ROWS>::get(v, 0);
+#pragma unroll
+    for (int r = 1; r < ROWS; r++) s += Vec<ROWS>::get(v, r);
+    return s;
+}
+
 template <int ROWS, bool WANT_DEPTH>
 __global__ void __launch_bounds__(256) raster_bwd_kernel(
     gsb_raster_bwd_params p, const float4* __restrict__ splats, const float* __restrict__ depth,
@@ -310,33 +403,34 @@ __global__ void __launch_bounds__(256) raster_bwd_kernel(
     float* __restrict__ gconic, float* __restrict__ gdepth, float* __restrict__ gcolor,
     float* __restrict__ galpha)
 {
+    using V = Vec<ROWS>;
+    using T = typename V::T;
     extern __shared__ Stash stash_all[];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, warps = blockDim.x >> 5;
     Stash& st = stash_all[warp];
     const int tile = order[blockIdx.x];
     const Geom<ROWS> tg = geom<ROWS>(p.width, p.tile_w, p.tile_h, tile, warp, lane);
     const int32_t start = offsets[tile];
-    const float pcx = (float)tg.px + 0.5f;
-    float pcy[ROWS], gR[ROWS], gG[ROWS], gB[ROWS], gD[ROWS], gtrans[ROWS], T_after[ROWS];
+    const T pcx = V::splat((float)tg.px + 0.5f);
+    T pcy, gR = V::splat(0.0f), gG = gR, gB = gR, gD = gR, gtrans = gR, T_after = V::splat(1.0f);
     int32_t last[ROWS];
     int32_t top = start;
 #pragma unroll
     for (int r = 0; r < ROWS; r++) {
         const int y = tg.py0 + r;
-        pcy[r] = (float)y + 0.5f;
-        gR[r] = gG[r] = gB[r] = gD[r] = gtrans[r] = 0.0f;
-        T_after[r] = 1.0f;
+        V::set(pcy, r, (float)y + 0.5f);
         last[r] = start;
         if (tg.px < p.width && y < p.height) {
             const int64_t pix = (int64_t)y * p.width + tg.px;
             last[r] = last_in[pix];
-            gR[r] = drgb[pix * 3];
-            gG[r] = drgb[pix * 3 + 1];
-            gB[r] = drgb[pix * 3 + 2];
-            if (WANT_DEPTH) gD[r] = ddepth[pix];
-            gtrans[r] = gR[r] * __ldg(background) + gG[r] * __ldg(background + 1) +
-                        gB[r] * __ldg(background + 2) - (dalpha ? dalpha[pix] : 0.0f);
-            T_after[r] = final_t[pix];
+            const float r_ = drgb[pix * 3], g_ = drgb[pix * 3 + 1], b_ = drgb[pix * 3 + 2];
+            V::set(gR, r, r_);
+            V::set(gG, r, g_);
+            V::set(gB, r, b_);
+            if (WANT_DEPTH) V::set(gD, r, ddepth[pix]);
+            V::set(gtrans, r, r_ * __ldg(background) + g_ * __ldg(background + 1) +
+                                  b_ * __ldg(background + 2) - (dalpha ? dalpha[pix] : 0.0f));
+            V::set(T_after, r, final_t[pix]);
             top = max(top, last[r]);
         }
     }
@@ -374,63 +468,79 @@ __global__ void __launch_bounds__(256) raster_bwd_kernel(
         if (word & (1u << lane)) {
             const int32_t g = __ldg(ids + base + lane);
             const float4* rec = splats + (int64_t)g * 3;
-            st.r0[lane] = __ldg(rec);
-            st.r1[lane] = __ldg(rec + 1);
-            st.r2[lane] = __ldg(rec + 2);
+            stash_splat(st, lane, __ldg(rec), __ldg(rec + 1), __ldg(rec + 2));
             st.id[lane] = g;
-            if (WANT_DEPTH) st.depth[lane] = __ldg(depth + g);
+            if (WANT_DEPTH) {
+                const float d = __ldg(depth + g);
+                st.depth[lane] = make_float2(d, d);
+            }
         }
         __syncwarp();
         while (word) {
             const int k = 31 - __clz(word);
             word &= ~(1u << k);
             const int32_t idx = base + k;
-            const float4 r0 = st.r0[k], r1 = st.r1[k], r2 = st.r2[k];
-            const float dx = pcx - r0.x;
-            const float ax = __fmul_rn(r1.x, dx), bx = __fmul_rn(r1.z, dx);
-            float S0 = 0.f, Sy = 0.f, Syy = 0.f, R = 0.f, G = 0.f, B = 0.f, Z = 0.f;
+            const Fragment<ROWS> f = fragment<ROWS>(st, k, pcx, pcy);
+            const float4 q3 = st.q3[k], q4 = st.q4[k];
+            T e;
+#pragma unroll
+            for (int r = 0; r < ROWS; r++) V::set(e, r, __expf(V::get(f.power, r)));
+            const T raw = V::mul(V::lo(q3), e);
+            T a, inv;
+            bool valid[ROWS];
 #pragma unroll
             for (int r = 0; r < ROWS; r++) {
-                const float dy = pcy[r] - r0.y;
-                const float t1 = __fmaf_rn(r1.y, dy, ax);
-                const float t2 = __fmaf_rn(r1.w, dy, bx);
-                const float power = __fmaf_rn(dy, t2, __fmul_rn(dx, t1));
-                const float raw = r2.w * __expf(power);
-                const bool valid = idx < last[r] && power <= 0.0f && raw >= kMinAlpha;
+                const float rr = V::get(raw, r);
+                valid[r] = idx < last[r] && V::get(f.power, r) <= 0.0f && rr >= kMinAlpha;
                 // Branch-free: with a = 0 the transmittance, the colour
                 // behind and every accumulated term stay exactly unchanged.
-                const float a = valid ? fminf(kMaxAlpha, raw) : 0.0f;
-                const float one_minus = 1.0f - a;
-                const float T_before = __fdividef(T_after[r], one_minus);
-                const float w = T_before * a;
-                float gw = gR[r] * r2.x + gG[r] * r2.y + gB[r] * r2.z;
-                if (WANT_DEPTH) gw += gD[r] * st.depth[k];
-                const float ga = T_before * (gw - gtrans[r]);
-                gtrans[r] = valid ? a * gw + one_minus * gtrans[r] : gtrans[r];
-                R = __fmaf_rn(w, gR[r], R);
-                G = __fmaf_rn(w, gG[r], G);
-                B = __fmaf_rn(w, gB[r], B);
-                if (WANT_DEPTH) Z = __fmaf_rn(w, gD[r], Z);
-                const float ge = (valid && raw < kMaxAlpha) ? ga * raw : 0.0f;
-                const float gedy = ge * dy;
-                S0 += ge;
-                Sy += gedy;
-                Syy = __fmaf_rn(gedy, dy, Syy);
-                T_after[r] = valid ? T_before : T_after[r];
+                V::set(a, r, valid[r] ? fminf(kMaxAlpha, rr) : 0.0f);
             }
+            const T one_minus = V::fma(a, V::splat(-1.0f), V::splat(1.0f));
+#pragma unroll
+            for (int r = 0; r < ROWS; r++) V::set(inv, r, __fdividef(1.0f, V::get(one_minus, r)));
+            const T T_before = V::mul(T_after, inv);
+            const T w = V::mul(T_before, a);
+            T gw = V::fma(gB, V::hi(q4), V::fma(gG, V::lo(q4), V::mul(gR, V::hi(q3))));
+            if (WANT_DEPTH) {
+                const float2 d = st.depth[k];
+                gw = V::fma(gD, V::lo(make_float4(d.x, d.y, d.x, d.y)), gw);
+            }
+            // ga = T_before (gw - gtrans); gtrans' = a gw + (1 - a) gtrans
+            // (an exact no-op when a = 0).
+            const T ga = V::mul(T_before, V::fma(gtrans, V::splat(-1.0f), gw));
+            gtrans = V::fma(a, gw, V::mul(one_minus, gtrans));
+            const float R = row_sum<ROWS>(V::mul(w, gR));
+            const float G = row_sum<ROWS>(V::mul(w, gG));
+            const float B = row_sum<ROWS>(V::mul(w, gB));
+            float Z = 0.0f;
+            if (WANT_DEPTH) Z = row_sum<ROWS>(V::mul(w, gD));
+            T ge = V::mul(ga, raw);
+#pragma unroll
+            for (int r = 0; r < ROWS; r++) {
+                const bool live = valid[r] && V::get(raw, r) < kMaxAlpha;
+                V::set(ge, r, live ? V::get(ge, r) : 0.0f);
+                V::set(T_after, r, valid[r] ? V::get(T_before, r) : V::get(T_after, r));
+            }
+            const T gedy = V::mul(ge, f.dy);
+            float S0 = row_sum<ROWS>(ge);
+            const float Sy = row_sum<ROWS>(gedy);
+            const float Syy = row_sum<ROWS>(V::mul(gedy, f.dy));
+            const float dx = V::get(f.dx, 0);
             const float Sx = dx * S0;
             float v[8] = {Sx, Sy, dx * Sx, dx * Sy, Syy, R, G, B};
             const float s = warp_sum8(v, lane);
             S0 = warp_sum(S0);
             if (WANT_DEPTH) Z = warp_sum(Z);
-            // gmean.x = c00 Sx + cbar Sy, gmean.y = c11 Sy + cbar Sx with c = -2 r1;
+            // gmean.x = c00 Sx + cbar Sy, gmean.y = c11 Sy + cbar Sx with c = -2 c';
             // gconic = -Sxx/2, -Sxy/2 (twice), -Syy/2; gcolor = R, G, B;
             // galpha = sum(ge) / o.
+            const float4 q1 = st.q1[k], q2 = st.q2[k];
             const float other = __shfl_xor_sync(GSB_FULL_MASK, s, 4);
-            const float coef_a = group == 0 ? -2.0f * r1.x : (group == 1 ? -2.0f * r1.w : kA);
-            const float coef_b = group < 2 ? -(r1.y + r1.z) : 0.0f;
+            const float coef_a = group == 0 ? -2.0f * q1.x : (group == 1 ? -2.0f * q2.z : kA);
+            const float coef_b = group < 2 ? -(q2.x + q1.z) : 0.0f;
             float value = coef_a * s + coef_b * other;
-            if (lane == 1) value = __fdividef(S0, r2.w);
+            if (lane == 1) value = __fdividef(S0, q3.x);
             if (WANT_DEPTH && lane == 2) value = Z;
             if (target) atomicAdd(target + (int64_t)st.id[k] * stride, value);
         }
