@@ -47,7 +47,7 @@ enum {
     GSB_ERR_NULL = 4        /* required pointer is NULL */
 };
 
-#define GSB_ABI_VERSION 1
+#define GSB_ABI_VERSION 2
 
 /* Library ABI version (GSB_ABI_VERSION). */
 GSB_API int gsb_abi_version(void);
@@ -192,7 +192,10 @@ typedef struct {
     int width, height;
     int tile_w, tile_h;
     int64_t max_pairs;     /* arena capacity of the table (sizes the bit words) */
+    int flags;             /* GSB_RASTER_SPLATS_READY: splats already written by gsb_raster_pack */
 } gsb_raster_params;
+
+#define GSB_RASTER_SPLATS_READY 1
 
 GSB_API size_t gsb_raster_workspace_size(const gsb_raster_params* p);
 GSB_API size_t gsb_raster_bit_words(const gsb_raster_params* p);
@@ -203,6 +206,16 @@ GSB_API int gsb_raster_fwd(gsb_stream_t stream, const gsb_raster_params* p, void
                    const int32_t* tile_offsets, const float* background, float* rgb,
                    float* out_depth, float* out_alpha, float* final_t, int32_t* last,
                    int32_t* backward_work, float* splats, uint32_t* contribution_bits);
+
+/* The first stage of gsb_raster_fwd on its own: write the splat records of
+ * every visible Gaussian.  It depends on the projection only, so a caller
+ * can run it on a second stream while the table is built, then call
+ * gsb_raster_fwd with GSB_RASTER_SPLATS_READY in p->flags (that call then
+ * skips the stage and its mean/conic/color/alpha/visible may be NULL).
+ * Splitting of the launcher inside kernels/sorted_rasterizer.py:15-70. */
+GSB_API int gsb_raster_pack(gsb_stream_t stream, const gsb_raster_params* p, const float* mean,
+                    const float* conic, const float* color, const float* alpha,
+                    const int8_t* visible, float* splats);
 
 /* ------------------------------------------------------------------------
  * fp32 rasterization backward.
@@ -224,7 +237,10 @@ typedef struct {
     int tile_w, tile_h;
     int cluster_size;
     int64_t max_pairs;
+    int flags;             /* GSB_RASTER_BWD_PREPARED: gsb_raster_bwd_prepare already ran */
 } gsb_raster_bwd_params;
+
+#define GSB_RASTER_BWD_PREPARED 1
 
 GSB_API int gsb_raster_bwd(gsb_stream_t stream, const gsb_raster_bwd_params* p, void* workspace,
                    size_t workspace_bytes, const float* splats, const float* depth,
@@ -234,6 +250,19 @@ GSB_API int gsb_raster_bwd(gsb_stream_t stream, const gsb_raster_bwd_params* p, 
                    const float* drgb, const float* ddepth, const float* dalpha,
                    const int32_t* cluster_ids, const int32_t* cluster_count, float* gmean,
                    float* gconic, float* gdepth, float* gcolor, float* galpha);
+
+/* The preparation stages of gsb_raster_bwd on their own: zero the cotangents
+ * (the listed clusters' slots, or the whole pool) and order the tiles by
+ * backward_work into the workspace.  They need only the forward's
+ * backward_work, so a caller can run them on a second stream during the
+ * loss, then call gsb_raster_bwd with the same workspace and
+ * GSB_RASTER_BWD_PREPARED in p->flags.
+ * Splitting of the backward launch inside kernels/sorted_rasterizer.py:165-236. */
+GSB_API int gsb_raster_bwd_prepare(gsb_stream_t stream, const gsb_raster_bwd_params* p,
+                           void* workspace, size_t workspace_bytes,
+                           const int32_t* backward_work, const int32_t* cluster_ids,
+                           const int32_t* cluster_count, float* gmean, float* gconic,
+                           float* gdepth, float* gcolor, float* galpha);
 
 /* ------------------------------------------------------------------------
  * Fused L1(0.8) + SSIM(0.2) loss and image gradient.

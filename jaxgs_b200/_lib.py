@@ -45,13 +45,18 @@ class BinParams(ctypes.Structure):
 
 class RasterParams(ctypes.Structure):
     _fields_ = [("capacity", ctypes.c_int), ("width", ctypes.c_int), ("height", ctypes.c_int),
-                ("tile_w", ctypes.c_int), ("tile_h", ctypes.c_int), ("max_pairs", ctypes.c_int64)]
+                ("tile_w", ctypes.c_int), ("tile_h", ctypes.c_int), ("max_pairs", ctypes.c_int64),
+                ("flags", ctypes.c_int)]
+
+
+RASTER_SPLATS_READY = 1
+RASTER_BWD_PREPARED = 1
 
 
 class RasterBwdParams(ctypes.Structure):
     _fields_ = [("capacity", ctypes.c_int), ("width", ctypes.c_int), ("height", ctypes.c_int),
                 ("tile_w", ctypes.c_int), ("tile_h", ctypes.c_int), ("cluster_size", ctypes.c_int),
-                ("max_pairs", ctypes.c_int64)]
+                ("max_pairs", ctypes.c_int64), ("flags", ctypes.c_int)]
 
 
 class LossParams(ctypes.Structure):
@@ -66,6 +71,7 @@ SYMBOLS = (
     "gsb_project_fwd", "gsb_project_bwd",
     "gsb_bin_workspace_size", "gsb_tile_sort_plan", "gsb_bin",
     "gsb_raster_workspace_size", "gsb_raster_bit_words", "gsb_raster_fwd", "gsb_raster_bwd",
+    "gsb_raster_pack", "gsb_raster_bwd_prepare",
     "gsb_loss_workspace_size", "gsb_loss", "gsb_loss_noalloc",
 )
 
@@ -101,6 +107,10 @@ def _load():
     lib.gsb_raster_fwd.argtypes = [vp, vp, vp, sz] + [vp] * 17
     lib.gsb_raster_bwd.restype = ctypes.c_int
     lib.gsb_raster_bwd.argtypes = [vp, vp, vp, sz] + [vp] * 19
+    lib.gsb_raster_pack.restype = ctypes.c_int
+    lib.gsb_raster_pack.argtypes = [vp, vp] + [vp] * 6
+    lib.gsb_raster_bwd_prepare.restype = ctypes.c_int
+    lib.gsb_raster_bwd_prepare.argtypes = [vp, vp, vp, sz] + [vp] * 8
     lib.gsb_loss.restype = ctypes.c_int
     lib.gsb_loss.argtypes = [vp, vp, vp, sz] + [vp] * 5
     lib.gsb_loss_noalloc.restype = ctypes.c_int
@@ -109,7 +119,7 @@ def _load():
 
 
 lib = _load()
-if lib.gsb_abi_version() != 1:
+if lib.gsb_abi_version() != 2:
     raise RuntimeError("libgsb200.so ABI version mismatch; rebuild with `python -m jaxgs_b200.build`")
 
 

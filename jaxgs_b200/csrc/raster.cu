@@ -655,6 +655,73 @@ extern "C" size_t gsb_raster_bit_words(const gsb_raster_params* p)
     return bit_words(*p);
 }
 
+namespace gsb {
+namespace {
+
+int launch_pack(cudaStream_t s, const gsb_raster_params& p, const float* mean, const float* conic,
+                const float* color, const float* alpha, const int8_t* visible, float* splats)
+{
+    if (p.capacity == 0) return GSB_OK;
+    pack_kernel<<<ceil_div(p.capacity, 256), 256, 0, s>>>(p.capacity, mean, conic, color, alpha,
+                                                          visible,
+                                                          reinterpret_cast<float4*>(splats));
+    return check_launch();
+}
+
+// Zero the cotangents and order the tiles by backward work (into workspace).
+int launch_bwd_prepare(cudaStream_t s, const gsb_raster_bwd_params& p, int tiles,
+                       const int32_t* backward_work, const int32_t* cluster_ids,
+                       const int32_t* cluster_count, int32_t* order, float* gmean, float* gconic,
+                       float* gdepth, float* gcolor, float* galpha)
+{
+    if (p.capacity > 0) {
+        if (cluster_ids) {
+            zero_cluster_cotangents_kernel<<<ceil_div(p.capacity, 256), 256, 0, s>>>(
+                p.capacity, p.cluster_size, cluster_ids, cluster_count, gmean, gconic, gcolor,
+                galpha);
+        } else {
+            zero_cotangents_kernel<<<ceil_div(p.capacity, 256), 256, 0, s>>>(
+                p.capacity, gmean, gconic, gdepth, gcolor, galpha);
+        }
+        if (int e = check_launch()) return e;
+    }
+    order_tiles_kernel<<<1, kOrderThreads, 0, s>>>(backward_work, tiles, 0, order);
+    return check_launch();
+}
+
+bool raster_shape_ok(const gsb_raster_params& p)
+{
+    return p.capacity >= 0 && p.width > 0 && p.height > 0 && tiles_ok(p.tile_w, p.tile_h) &&
+           p.max_pairs >= 0 && p.max_pairs < (int64_t(1) << 31) &&
+           (p.flags & ~GSB_RASTER_SPLATS_READY) == 0;
+}
+
+bool raster_bwd_shape_ok(const gsb_raster_bwd_params& p)
+{
+    return p.capacity >= 0 && p.width > 0 && p.height > 0 && tiles_ok(p.tile_w, p.tile_h) &&
+           (p.flags & ~GSB_RASTER_BWD_PREPARED) == 0;
+}
+
+bool misaligned16(const void* a, const void* b)
+{
+    return ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b)) & 15) != 0;
+}
+
+}  // namespace
+}  // namespace gsb
+
+extern "C" int gsb_raster_pack(gsb_stream_t stream, const gsb_raster_params* p, const float* mean,
+                               const float* conic, const float* color, const float* alpha,
+                               const int8_t* visible, float* splats)
+{
+    if (!p) return GSB_ERR_NULL;
+    if (!raster_shape_ok(*p)) return GSB_ERR_INVALID;
+    if (!splats || (p->capacity > 0 && (!mean || !conic || !color || !alpha || !visible)))
+        return GSB_ERR_NULL;
+    if (misaligned16(splats, conic)) return GSB_ERR_INVALID;
+    return launch_pack(as_stream(stream), *p, mean, conic, color, alpha, visible, splats);
+}
+
 extern "C" int gsb_raster_fwd(gsb_stream_t stream, const gsb_raster_params* p, void* workspace,
                               size_t workspace_bytes, const float* mean, const float* conic,
                               const float* depth, const float* color, const float* alpha,
@@ -664,25 +731,20 @@ extern "C" int gsb_raster_fwd(gsb_stream_t stream, const gsb_raster_params* p, v
                               int32_t* backward_work, float* splats, uint32_t* contribution_bits)
 {
     if (!p) return GSB_ERR_NULL;
-    if (p->capacity < 0 || p->width <= 0 || p->height <= 0 || !tiles_ok(p->tile_w, p->tile_h) ||
-        p->max_pairs < 0 || p->max_pairs >= (int64_t(1) << 31))
-        return GSB_ERR_INVALID;
+    if (!raster_shape_ok(*p)) return GSB_ERR_INVALID;
     if (!workspace || workspace_bytes < raster_ws(*p)) return GSB_ERR_WORKSPACE;
+    const bool packed = (p->flags & GSB_RASTER_SPLATS_READY) != 0;
     if (!gaussian_ids || !tile_offsets || !background || !rgb || !final_t || !last ||
         !backward_work || !splats || !contribution_bits ||
-        (p->capacity > 0 && (!mean || !conic || !color || !alpha || !visible)) ||
+        (p->capacity > 0 && !packed && (!mean || !conic || !color || !alpha || !visible)) ||
         (out_depth && !depth))
         return GSB_ERR_NULL;
-    if ((reinterpret_cast<uintptr_t>(splats) | reinterpret_cast<uintptr_t>(conic)) & 15)
-        return GSB_ERR_INVALID;
+    if (misaligned16(splats, packed ? nullptr : conic)) return GSB_ERR_INVALID;
     cudaStream_t s = as_stream(stream);
     int tiles = (int)num_tiles(*p);
     int32_t* order = static_cast<int32_t*>(workspace);
-    if (p->capacity > 0) {
-        pack_kernel<<<ceil_div(p->capacity, 256), 256, 0, s>>>(p->capacity, mean, conic, color,
-                                                               alpha, visible,
-                                                               reinterpret_cast<float4*>(splats));
-        if (int e = check_launch()) return e;
+    if (!packed) {
+        if (int e = launch_pack(s, *p, mean, conic, color, alpha, visible, splats)) return e;
     }
     order_tiles_kernel<<<1, kOrderThreads, 0, s>>>(tile_offsets, tiles, 1, order);
     if (int e = check_launch()) return e;
@@ -699,6 +761,25 @@ extern "C" int gsb_raster_fwd(gsb_stream_t stream, const gsb_raster_params* p, v
     return check_launch();
 }
 
+extern "C" int gsb_raster_bwd_prepare(gsb_stream_t stream, const gsb_raster_bwd_params* p,
+                                      void* workspace, size_t workspace_bytes,
+                                      const int32_t* backward_work, const int32_t* cluster_ids,
+                                      const int32_t* cluster_count, float* gmean, float* gconic,
+                                      float* gdepth, float* gcolor, float* galpha)
+{
+    if (!p) return GSB_ERR_NULL;
+    gsb_raster_params rp{p->capacity, p->width, p->height, p->tile_w, p->tile_h, p->max_pairs, 0};
+    if (!raster_bwd_shape_ok(*p)) return GSB_ERR_INVALID;
+    if (!workspace || workspace_bytes < raster_ws(rp)) return GSB_ERR_WORKSPACE;
+    if (!backward_work || !gmean || !gconic || !gcolor || !galpha) return GSB_ERR_NULL;
+    if (cluster_ids && (!cluster_count || p->cluster_size <= 0)) return GSB_ERR_INVALID;
+    if (!cluster_ids && !gdepth) return GSB_ERR_NULL;
+    if (misaligned16(gconic, nullptr)) return GSB_ERR_INVALID;
+    return launch_bwd_prepare(as_stream(stream), *p, (int)num_tiles(rp), backward_work,
+                              cluster_ids, cluster_count, static_cast<int32_t*>(workspace), gmean,
+                              gconic, gdepth, gcolor, galpha);
+}
+
 extern "C" int gsb_raster_bwd(gsb_stream_t stream, const gsb_raster_bwd_params* p,
                               void* workspace, size_t workspace_bytes, const float* splats,
                               const float* depth, const int32_t* gaussian_ids,
@@ -711,9 +792,8 @@ extern "C" int gsb_raster_bwd(gsb_stream_t stream, const gsb_raster_bwd_params* 
                               float* galpha)
 {
     if (!p) return GSB_ERR_NULL;
-    gsb_raster_params rp{p->capacity, p->width, p->height, p->tile_w, p->tile_h, p->max_pairs};
-    if (p->capacity < 0 || p->width <= 0 || p->height <= 0 || !tiles_ok(p->tile_w, p->tile_h))
-        return GSB_ERR_INVALID;
+    gsb_raster_params rp{p->capacity, p->width, p->height, p->tile_w, p->tile_h, p->max_pairs, 0};
+    if (!raster_bwd_shape_ok(*p)) return GSB_ERR_INVALID;
     if (!workspace || workspace_bytes < raster_ws(rp)) return GSB_ERR_WORKSPACE;
     if (!splats || !gaussian_ids || !tile_offsets || !background || !final_t || !last ||
         !backward_work || !contribution_bits || !drgb || !gmean || !gconic || !gcolor || !galpha)
@@ -722,24 +802,15 @@ extern "C" int gsb_raster_bwd(gsb_stream_t stream, const gsb_raster_bwd_params* 
     if (want_depth && (!depth || !gdepth)) return GSB_ERR_NULL;
     if (cluster_ids && (!cluster_count || p->cluster_size <= 0)) return GSB_ERR_INVALID;
     if (!cluster_ids && !gdepth) return GSB_ERR_NULL;
-    if ((reinterpret_cast<uintptr_t>(splats) | reinterpret_cast<uintptr_t>(gconic)) & 15)
-        return GSB_ERR_INVALID;
+    if (misaligned16(splats, gconic)) return GSB_ERR_INVALID;
     cudaStream_t s = as_stream(stream);
     int tiles = (int)num_tiles(rp);
     int32_t* order = static_cast<int32_t*>(workspace);
-    if (p->capacity > 0) {
-        if (cluster_ids) {
-            zero_cluster_cotangents_kernel<<<ceil_div(p->capacity, 256), 256, 0, s>>>(
-                p->capacity, p->cluster_size, cluster_ids, cluster_count, gmean, gconic, gcolor,
-                galpha);
-        } else {
-            zero_cotangents_kernel<<<ceil_div(p->capacity, 256), 256, 0, s>>>(
-                p->capacity, gmean, gconic, gdepth, gcolor, galpha);
-        }
-        if (int e = check_launch()) return e;
+    if (!(p->flags & GSB_RASTER_BWD_PREPARED)) {
+        if (int e = launch_bwd_prepare(s, *p, tiles, backward_work, cluster_ids, cluster_count,
+                                       order, gmean, gconic, gdepth, gcolor, galpha))
+            return e;
     }
-    order_tiles_kernel<<<1, kOrderThreads, 0, s>>>(backward_work, tiles, 0, order);
-    if (int e = check_launch()) return e;
     int warps = warps_per_tile(p->tile_w, p->tile_h);
     const float4* sp = reinterpret_cast<const float4*>(splats);
     if (rows_per_lane(p->tile_h) == 2)

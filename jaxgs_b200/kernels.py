@@ -234,12 +234,37 @@ def _tiles(camera: DeviceCamera, config: CapacityConfig) -> int:
     return (-(-camera.width // config.tile_size)) * (-(-camera.height // config.raster_tile_height))
 
 
+def _raster_params(camera: DeviceCamera, config: CapacityConfig, max_pairs: int, flags: int = 0):
+    return L.RasterParams(config.max_gaussians, camera.width, camera.height, config.tile_size,
+                          config.raster_tile_height, int(max_pairs), flags)
+
+
+def pack_splats(projected: ProjectedGaussians, camera: DeviceCamera, config: CapacityConfig,
+                out: torch.Tensor | None = None) -> torch.Tensor:
+    """The first stage of rasterize_forward on its own (gsb_raster_pack): the
+    48-byte splat records of the visible Gaussians.  It needs only the
+    projection, so it can run on a second stream while the table is built;
+    pass the result to rasterize_forward(splats=...)."""
+    _require_cuda(projected.mean, "splat packing")
+    dev = projected.mean.device
+    splats = torch.empty(config.max_gaussians, 12, dtype=_f32, device=dev) if out is None else out
+    p = _raster_params(camera, config, 0)
+    L.check(L.lib.gsb_raster_pack(
+        _stream(), L.ref(p), _ptr(_c(projected.mean, _f32)), _ptr(_c(projected.conic, _f32)),
+        _ptr(_c(projected.color, _f32)), _ptr(_c(projected.alpha, _f32)),
+        _ptr(_c(projected.visible, torch.int8)), _ptr(splats)), "splat packing")
+    return splats
+
+
 def rasterize_forward(projected: ProjectedGaussians, table: SortedVisibilityTable,
                       camera: DeviceCamera, config: CapacityConfig, background=None,
-                      want_depth: bool = True, want_alpha: bool = True):
+                      want_depth: bool = True, want_alpha: bool = True,
+                      splats: torch.Tensor | None = None):
     """sorted_rasterizer.py:15-70: returns (RenderResult, RasterCache).
 
     The table may reference only visible Gaussians (others are not staged).
+    splats: records already written by pack_splats (the packing stage is
+    then skipped).
     """
     _require_cuda(projected.mean, "rasterization")
     C = config.max_gaussians
@@ -253,9 +278,11 @@ def rasterize_forward(projected: ProjectedGaussians, table: SortedVisibilityTabl
     final_t = torch.empty(H * W, dtype=_f32, device=dev)
     last = torch.empty(H * W, dtype=_i32, device=dev)
     work = torch.empty(_tiles(camera, config), dtype=_i32, device=dev)
-    splats = torch.empty(C, 12, dtype=_f32, device=dev)
-    p = L.RasterParams(C, W, H, config.tile_size, config.raster_tile_height,
-                       int(table.gaussian_ids.shape[0]))
+    packed = splats is not None
+    if not packed:
+        splats = torch.empty(C, 12, dtype=_f32, device=dev)
+    p = _raster_params(camera, config, table.gaussian_ids.shape[0],
+                       L.RASTER_SPLATS_READY if packed else 0)
     bits = torch.empty(max(int(L.lib.gsb_raster_bit_words(L.ref(p))), 1), dtype=_i32, device=dev)
     ws = _workspace(L.lib.gsb_raster_workspace_size(L.ref(p)), dev)
     L.check(L.lib.gsb_raster_fwd(
@@ -269,46 +296,88 @@ def rasterize_forward(projected: ProjectedGaussians, table: SortedVisibilityTabl
     return RenderResult(rgb, out_depth, out_alpha), RasterCache(splats, final_t, last, work, bits)
 
 
+class BackwardBuffers:
+    """Outputs and workspace of one rasterize_backward call, allocated up
+    front so that prepare_rasterize_backward can fill them on another stream."""
+
+    def __init__(self, table: SortedVisibilityTable, camera: DeviceCamera, config: CapacityConfig,
+                 visible_clusters=None):
+        C = config.max_gaussians
+        dev = table.gaussian_ids.device
+        self.gmean = torch.empty(C, 2, dtype=_f32, device=dev)
+        self.gconic = torch.empty(C, 2, 2, dtype=_f32, device=dev)
+        self.gdepth = torch.empty(C, dtype=_f32, device=dev)
+        self.gcolor = torch.empty(C, 3, dtype=_f32, device=dev)
+        self.galpha = torch.empty(C, dtype=_f32, device=dev)
+        self.visible_clusters = visible_clusters
+        self.max_pairs = int(table.gaussian_ids.shape[0])
+        rp = _raster_params(camera, config, self.max_pairs)
+        self.workspace = _workspace(L.lib.gsb_raster_workspace_size(L.ref(rp)), dev)
+        self.prepared = False
+
+    def params(self, camera: DeviceCamera, config: CapacityConfig, flags: int = 0):
+        return L.RasterBwdParams(config.max_gaussians, camera.width, camera.height,
+                                 config.tile_size, config.raster_tile_height, config.cluster_size,
+                                 self.max_pairs, flags)
+
+    def clusters(self):
+        ids, count = (None, None) if self.visible_clusters is None else self.visible_clusters
+        return (_ptr(None if ids is None else _c(ids, _i32)),
+                _ptr(None if count is None else _c(count, _i32)))
+
+
+def prepare_rasterize_backward(cache: RasterCache, camera: DeviceCamera, config: CapacityConfig,
+                               buffers: BackwardBuffers) -> BackwardBuffers:
+    """The preparation stages of rasterize_backward on their own
+    (gsb_raster_bwd_prepare): zero the cotangents and order the tiles by the
+    forward's backward work.  Needs only the forward, so it can overlap the
+    loss on a second stream."""
+    p = buffers.params(camera, config)
+    ids, count = buffers.clusters()
+    L.check(L.lib.gsb_raster_bwd_prepare(
+        _stream(), L.ref(p), _ptr(buffers.workspace), buffers.workspace.numel(),
+        _ptr(cache.backward_work), ids, count, _ptr(buffers.gmean), _ptr(buffers.gconic),
+        _ptr(buffers.gdepth), _ptr(buffers.gcolor), _ptr(buffers.galpha)),
+        "rasterization backward preparation")
+    buffers.prepared = True
+    return buffers
+
+
 def rasterize_backward(projected: ProjectedGaussians, table: SortedVisibilityTable,
                        cache: RasterCache, drgb: torch.Tensor, camera: DeviceCamera,
                        config: CapacityConfig, background=None, ddepth=None, dalpha=None,
-                       visible_clusters=None) -> ProjectedGaussians:
+                       visible_clusters=None,
+                       buffers: BackwardBuffers | None = None) -> ProjectedGaussians:
     """sorted_rasterize.py:91-236: projected-field cotangents (mean, conic,
     depth, color, alpha).  With visible_clusters only those clusters' rows
-    are zeroed and defined, and depth cotangents are left undefined."""
+    are zeroed and defined, and depth cotangents are left undefined.
+    buffers: from BackwardBuffers (and prepare_rasterize_backward, which then
+    replaces the zeroing and ordering stages); its visible_clusters is used."""
     _require_cuda(drgb, "rasterization backward")
     C = config.max_gaussians
     dev = drgb.device
     if background is None:
         background = _zeros(3, dev)
-    gmean = torch.empty(C, 2, dtype=_f32, device=dev)
-    gconic = torch.empty(C, 2, 2, dtype=_f32, device=dev)
-    gdepth = torch.empty(C, dtype=_f32, device=dev)
-    gcolor = torch.empty(C, 3, dtype=_f32, device=dev)
-    galpha = torch.empty(C, dtype=_f32, device=dev)
-    ids, count = (None, None) if visible_clusters is None else visible_clusters
-    if ddepth is not None and visible_clusters is not None:
+    if buffers is None:
+        buffers = BackwardBuffers(table, camera, config, visible_clusters)
+    if ddepth is not None and buffers.visible_clusters is not None:
         raise ValueError("depth cotangents are not defined with visible_clusters")
-    max_pairs = int(table.gaussian_ids.shape[0])
-    p = L.RasterBwdParams(C, camera.width, camera.height, config.tile_size,
-                          config.raster_tile_height, config.cluster_size, max_pairs)
-    rp = L.RasterParams(C, camera.width, camera.height, config.tile_size,
-                        config.raster_tile_height, max_pairs)
-    ws = _workspace(L.lib.gsb_raster_workspace_size(L.ref(rp)), dev)
+    p = buffers.params(camera, config, L.RASTER_BWD_PREPARED if buffers.prepared else 0)
+    ids, count = buffers.clusters()
     L.check(L.lib.gsb_raster_bwd(
-        _stream(), L.ref(p), _ptr(ws), ws.numel(), _ptr(cache.splats),
-        _ptr(_c(projected.depth, _f32)), _ptr(table.gaussian_ids), _ptr(table.tile_offsets),
-        _ptr(_c(background, _f32)), _ptr(cache.final_t), _ptr(cache.last),
-        _ptr(cache.backward_work), _ptr(cache.contribution_bits), _ptr(_c(drgb, _f32)),
-        _ptr(None if ddepth is None else _c(ddepth, _f32)),
-        _ptr(None if dalpha is None else _c(dalpha, _f32)),
-        _ptr(None if ids is None else _c(ids, _i32)), _ptr(None if count is None else _c(count, _i32)),
-        _ptr(gmean), _ptr(gconic), _ptr(gdepth), _ptr(gcolor), _ptr(galpha)),
+        _stream(), L.ref(p), _ptr(buffers.workspace), buffers.workspace.numel(),
+        _ptr(cache.splats), _ptr(_c(projected.depth, _f32)), _ptr(table.gaussian_ids),
+        _ptr(table.tile_offsets), _ptr(_c(background, _f32)), _ptr(cache.final_t),
+        _ptr(cache.last), _ptr(cache.backward_work), _ptr(cache.contribution_bits),
+        _ptr(_c(drgb, _f32)), _ptr(None if ddepth is None else _c(ddepth, _f32)),
+        _ptr(None if dalpha is None else _c(dalpha, _f32)), ids, count,
+        _ptr(buffers.gmean), _ptr(buffers.gconic), _ptr(buffers.gdepth), _ptr(buffers.gcolor),
+        _ptr(buffers.galpha)),
         "rasterization backward")
     # The radius cotangent of a rasterizer is zero (sorted_rasterizer.py:224).
     radius = _zeros(1, dev).expand(C)
-    return projected.replace(mean=gmean, conic=gconic, depth=gdepth, color=gcolor, alpha=galpha,
-                             radius=radius)
+    return projected.replace(mean=buffers.gmean, conic=buffers.gconic, depth=buffers.gdepth,
+                             color=buffers.gcolor, alpha=buffers.galpha, radius=radius)
 
 
 # ---------------------------------------------------------------------------

@@ -1,6 +1,7 @@
 """The north-star training step: cluster cull -> compact projection -> binning
 -> fp32 raster forward -> fused L1+SSIM (on clip(rgb,0,1)) -> raster backward
--> projection pullback, on one CUDA stream with no host synchronisation.
+-> projection pullback, with no host synchronisation (one stream, plus a
+second one for the stages that can overlap).
 
 Mirrors training/step.py:32-132 (compute_training_step) up to, not including,
 the optimizer: the result is the loss, the parameter gradients in compact
@@ -30,6 +31,16 @@ from .scene import CapacityConfig
 from .types import DeviceCamera, GaussianArrays, ProjectedGaussians
 
 
+_SIDE_STREAMS: dict = {}
+
+
+def _side_stream(device) -> torch.cuda.Stream:
+    key = torch.device(device).index
+    if key not in _SIDE_STREAMS:
+        _SIDE_STREAMS[key] = torch.cuda.Stream(device=device)
+    return _SIDE_STREAMS[key]
+
+
 @dataclass
 class StepOutput:
     loss: torch.Tensor            # [] float32 (device)
@@ -44,7 +55,8 @@ class StepOutput:
 def compute_training_step(pool: GaussianArrays, bounds, camera: DeviceCamera, target: torch.Tensor,
                           config: CapacityConfig, active_degree: int, *,
                           active_sh_only: bool = True, sh_color_only: bool = False,
-                          keep_image: bool = False, stage_events: dict | None = None) -> StepOutput:
+                          keep_image: bool = False, stage_events: dict | None = None,
+                          overlap: bool = True) -> StepOutput:
     """training/step.py:32-89 without the optimizer update.
 
     bounds: world cluster bounds (center, extent, valid) on the device.
@@ -55,6 +67,8 @@ def compute_training_step(pool: GaussianArrays, bounds, camera: DeviceCamera, ta
     stage_events: optional dict; receives (start, end) CUDA events recorded on
     the current stream around each stage (cull, project, bin, raster_fwd,
     loss, raster_bwd, project_bwd).
+    overlap: run the splat packing and the backward preparation on a second
+    stream (joined back before their consumers); False keeps one stream.
     """
     stream = torch.cuda.current_stream()
 
@@ -70,6 +84,11 @@ def compute_training_step(pool: GaussianArrays, bounds, camera: DeviceCamera, ta
         if ev is not None:
             ev[1].record(stream)
 
+    # Work that depends on fewer inputs than its position in the chain runs on
+    # a second stream, joined back before its consumer: the splat records
+    # (need the projection) overlap the binning, and the cotangent zeroing and
+    # backward tile order (need the forward) overlap the loss.
+    side = _side_stream(stream.device) if overlap else None
     ev = mark("cull")
     clusters, _ = K.compact_visible_clusters(bounds, camera, config, want_slots=False)
     done(ev)
@@ -78,19 +97,33 @@ def compute_training_step(pool: GaussianArrays, bounds, camera: DeviceCamera, ta
         pool, camera, config, active_degree, clusters, rgb_only=True,
         active_sh_only=active_sh_only, sh_color_only=sh_color_only, visible_color_only=True)
     done(ev)
+    splats = None
+    if side is not None:
+        splats = torch.empty(config.max_gaussians, 12, dtype=torch.float32, device=stream.device)
+        side.wait_stream(stream)
+        with torch.cuda.stream(side):
+            K.pack_splats(projected, camera, config, out=splats)
     ev = mark("bin")
     table = K.build_sorted_visibility_table_cute(projected, camera, config)
     done(ev)
+    if side is not None:
+        stream.wait_stream(side)
     ev = mark("raster_fwd")
     result, cache = K.rasterize_forward(projected, table, camera, config, want_depth=False,
-                                        want_alpha=False)
+                                        want_alpha=False, splats=splats)
     done(ev)
+    buffers = K.BackwardBuffers(table, camera, config, visible_clusters=clusters)
+    if side is not None:
+        side.wait_stream(stream)
+        with torch.cuda.stream(side):
+            K.prepare_rasterize_backward(cache, camera, config, buffers)
     ev = mark("loss")
     loss, drgb, _ = K._fused_loss(result.rgb, target, False, clip_input=True)
     done(ev)
+    if side is not None:
+        stream.wait_stream(side)
     ev = mark("raster_bwd")
-    cot = K.rasterize_backward(projected, table, cache, drgb, camera, config,
-                               visible_clusters=clusters)
+    cot = K.rasterize_backward(projected, table, cache, drgb, camera, config, buffers=buffers)
     done(ev)
     ev = mark("project_bwd")
     grads = pullback(cot)

@@ -343,6 +343,61 @@ def test_raster_backward_matches_oracle(tile_h, tile_w):
         assert rel_l2(got, exp[name]) < 1e-3, (name, rel_l2(got, exp[name]))
 
 
+@pytest.mark.parametrize("tile_h,tile_w", [(16, 8), (12, 16)])
+def test_raster_split_stages_match_single_calls(tile_h, tile_w):
+    """gsb_raster_pack + gsb_raster_fwd(SPLATS_READY) and gsb_raster_bwd_prepare
+    + gsb_raster_bwd(PREPARED), each stage on a second stream, give the
+    single calls' forward bit for bit and their cotangents up to the order of
+    the atomic additions."""
+    from jaxgs_b200.scene import CapacityConfig
+    from jaxgs_b200.types import DeviceCamera, SortedVisibilityTable
+
+    K = _kernels()
+    W, H = 67, 45
+    proj, table = _raster_case(21, W, H, tw=tile_w, th=tile_h)
+    c = len(proj["alpha"])
+    config = CapacityConfig(c, 128, 1, tile_w, 0, len(table["gaussian_ids"]), tile_height=tile_h)
+    t_table = SortedVisibilityTable(*(torch.as_tensor(table[k], device="cuda") for k in
+                                      ("gaussian_ids", "tile_offsets", "point_counts")),
+                                    torch.tensor([table["pair_count"]], device="cuda"),
+                                    torch.tensor([0], device="cuda"))
+    cam = DeviceCamera(None, None, None, None, W, H)
+    projected = torch_proj(proj)
+    drgb = torch.as_tensor(np.random.default_rng(5).normal(0, 1, (H, W, 3)).astype(np.float32),
+                           device="cuda")
+    ids = torch.arange(-(-c // 128), dtype=torch.int32, device="cuda")
+    clusters = (ids, torch.tensor([ids.numel()], dtype=torch.int32, device="cuda"))
+    r1, c1 = K.rasterize_forward(projected, t_table, cam, config, want_depth=False, want_alpha=False)
+    g1 = K.rasterize_backward(projected, t_table, c1, r1.rgb * 0 + drgb, cam, config,
+                              visible_clusters=clusters)
+    main, side = torch.cuda.current_stream(), torch.cuda.Stream()
+    splats = torch.full((c, 12), float("nan"), device="cuda")
+    side.wait_stream(main)
+    with torch.cuda.stream(side):
+        K.pack_splats(projected, cam, config, out=splats)
+    main.wait_stream(side)
+    r2, c2 = K.rasterize_forward(projected, t_table, cam, config, want_depth=False,
+                                 want_alpha=False, splats=splats)
+    buffers = K.BackwardBuffers(t_table, cam, config, visible_clusters=clusters)
+    for t in (buffers.gmean, buffers.gconic, buffers.gcolor, buffers.galpha):
+        t.fill_(float("nan"))
+    side.wait_stream(main)
+    with torch.cuda.stream(side):
+        K.prepare_rasterize_backward(c2, cam, config, buffers)
+    main.wait_stream(side)
+    g2 = K.rasterize_backward(projected, t_table, c2, drgb, cam, config, buffers=buffers)
+    torch.cuda.synchronize()
+    vis = projected.visible != 0
+    for a, b in ((r1.rgb, r2.rgb), (c1.final_t, c2.final_t), (c1.last, c2.last),
+                 (c1.backward_work, c2.backward_work), (c1.splats[vis], c2.splats[vis])):
+        assert torch.equal(a, b)
+    # Cotangents accumulate with float atomics, whose order varies per run.
+    for name in ("mean", "conic", "color", "alpha"):
+        a, b = getattr(g1, name).cpu().numpy(), getattr(g2, name).cpu().numpy()
+        assert np.isfinite(b).all(), name
+        assert rel_l2(b.reshape(-1), a.reshape(-1)) < 1e-6, name
+
+
 # ---------------------------------------------------------------------------
 # Loss
 # ---------------------------------------------------------------------------
