@@ -10,9 +10,11 @@ binning + fp32 raster forward + fused L1+SSIM + raster backward + projection
 pullback to xyz/log_scale/rotation/opacity/SH (degree 3).  Synthetic data.
 
 Multi-GPU (torchrun, one rank per GPU): every rank renders one view per step
-(ring camera r of BASELINE config 3's ring, radius 6) and the per-view
-parameter gradients, scattered to pool order, are summed by one NCCL
-all-reduce per step; value = views of all ranks / max-over-ranks time.
+(ring camera r of BASELINE config 3's ring, radius 6) and the ranks sum the
+per-view gradients (jaxgs_b200.step.ViewShardedExchange: all-reduce of the
+geometric gradients, all-gather of the 3-float colour cotangents, SH
+expansion of all views on every rank); value = views of all ranks /
+max-over-ranks time.
 
 --impl reference times the reference path's CPU restatement (oracle/, the
 reference being JAX code that is not installed here) on the host cores.
@@ -146,7 +148,7 @@ def run_ours(args) -> None:
     from jaxgs_b200 import _lib
     from jaxgs_b200 import kernels as K
     from jaxgs_b200.scene import world_cluster_bounds
-    from jaxgs_b200.step import GraphedTrainingStep, compute_training_step, scatter_compact
+    from jaxgs_b200.step import GraphedTrainingStep, ViewShardedExchange, compute_training_step
     from jaxgs_b200.types import DeviceCamera, GaussianArrays
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -171,28 +173,27 @@ def run_ours(args) -> None:
     cam_host = [t.cpu().pin_memory() for t in (dcam.world_to_camera, dcam.intrinsics,
                                                dcam.center, dcam.planes)]
     degree = 3
-    pool_grads = None
-    if world > 1:
-        pool_grads = [torch.zeros_like(t) for t in (pool.xyz, pool.log_scale, pool.rotation,
-                                                  pool.opacity, pool.sh)]
+    exch = ViewShardedExchange(pool, config, degree) if world > 1 else None
+    pool_grads = exch.pool_grads if exch is not None else None
+    sharded = dict(pool_grads=pool_grads, sh_color_only=exch is not None)
     stream = torch.cuda.current_stream()
     stage_events = []
+    current_center = [dcam.center]
 
     def eager_step(cam, tgt, record=False):
         events = {} if record else None
-        out = compute_training_step(pool, bounds, cam, tgt, config, degree, stage_events=events)
+        out = compute_training_step(pool, bounds, cam, tgt, config, degree, stage_events=events,
+                                    **sharded)
         if record:
             stage_events.append(events)
         return out
 
     def exchange(out):
-        """View-sharded gradient sum (one NCCL all-reduce per step)."""
-        if world > 1:
-            for t in pool_grads:
-                t.zero_()
-            scatter_compact(out.gradients, out.visible_clusters, config, out=pool_grads)
-            flat = torch.cat([t.reshape(-1) for t in pool_grads])
-            dist.all_reduce(flat)
+        """View-sharded gradient sum (ViewShardedExchange: one all-reduce of
+        the geometric gradients, all-gathers of the colour cotangents and
+        camera centres, SH expansion)."""
+        if exch is not None:
+            exch.exchange(current_center[0])
 
     # Eager warm-up and the per-stage breakdown (events around each stage on
     # the launching stream; the dominant kernel's time comes from here).
@@ -214,7 +215,8 @@ def run_ours(args) -> None:
     binned = int((out.point_counts > 0).sum().item())
 
     # The product step: captured once as a CUDA graph, replayed per view.
-    graphed = GraphedTrainingStep(pool, bounds, dcam, target, config, degree)
+    graphed = GraphedTrainingStep(pool, bounds, dcam, target, config, degree, **sharded)
+    current_center[0] = graphed.camera.center
     for _ in range(max(args.warmup, 0)):
         out = graphed()
         exchange(out)
@@ -284,7 +286,11 @@ def run_ours(args) -> None:
                        "visible_clusters": visible_clusters, "binned_gaussians": binned,
                        "l2": "inputs larger than L2 (236 MB pool)",
                        "launch": "CUDA graph replay of the whole step",
-                       "parallelism": f"view-sharded dp{world}" if world > 1 else "single view"},
+                       "parallelism": f"view-sharded dp{world}" if world > 1 else "single view",
+                       "exchange": (f"per step: NCCL all-reduce of {exch.geometric.numel() * 4 / 1e6:.0f} MB "
+                                    f"geometric gradients, all-gather of {exch.colors.numel() * 4 / 1e6:.0f} MB "
+                                    "colour cotangents per rank, SH expansion of all views")
+                                   if exch is not None else None},
             "e2e": {"value": None if args.no_e2e else round(world * args.steps / e2e_elapsed, 2),
                     "unit": UNIT, "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": d2h},
             "gpu_launches": int(launches),

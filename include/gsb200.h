@@ -115,7 +115,8 @@ GSB_API int gsb_project_fwd(gsb_stream_t stream, const gsb_project_params* p, co
  * Cotangents: gmean[C*2], gdepth[C] (unused if rgb_only), gconic[C*4],
  * gradius[C] (unused if rgb_only), gcolor[C*3], galpha[C].
  * Outputs (compact visible-cluster order when compact_gradients, else pool
- * order): gxyz[C*3], glog_scale[C*3], grotation[C*4], gopacity[C],
+ * order, where every slot is written and unlisted clusters' rows are zero):
+ * gxyz[C*3], glog_scale[C*3], grotation[C*4], gopacity[C],
  * gsh[C*sh_gradient_dim*3].
  * ------------------------------------------------------------------------ */
 typedef struct {
@@ -139,6 +140,26 @@ GSB_API int gsb_project_bwd(gsb_stream_t stream, const gsb_project_bwd_params* p
                     const float* gconic, const float* gradius, const float* gcolor,
                     const float* galpha, float* gxyz, float* glog_scale, float* grotation,
                     float* gopacity, float* gsh);
+
+/* ------------------------------------------------------------------------
+ * SH coefficient cotangents from colour cotangents, summed over views.
+ * Replaces training/sh_pullback.py:18-53 (with_sh_pullback: one view's
+ * masked colour cotangent expanded on the SH basis of its direction from
+ * the camera centre), summed over `views` cameras so that view-sharded ranks
+ * can exchange 3 floats per Gaussian and view instead of sh_dim * 3.
+ * Inputs: xyz[C*3], centers[views*3], colors[views*C*3] (view-major; each the
+ * sh_color_only output of gsb_project_bwd in pool order).
+ * Output: gsh[C*sh_dim*3] (bands above degree zero).
+ * ------------------------------------------------------------------------ */
+typedef struct {
+    int capacity;
+    int sh_dim;
+    int degree;
+    int views;
+} gsb_sh_params;
+
+GSB_API int gsb_sh_from_colors(gsb_stream_t stream, const gsb_sh_params* p, const float* xyz,
+                       const float* centers, const float* colors, float* gsh);
 
 /* ------------------------------------------------------------------------
  * Tile binning (AccuTile count, depth sort, scan, emission, stable tile sort,

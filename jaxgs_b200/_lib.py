@@ -38,6 +38,11 @@ class ProjectBwdParams(ctypes.Structure):
                 ("rgb_only", ctypes.c_int), ("sh_color_only", ctypes.c_int)]
 
 
+class ShParams(ctypes.Structure):
+    _fields_ = [("capacity", ctypes.c_int), ("sh_dim", ctypes.c_int), ("degree", ctypes.c_int),
+                ("views", ctypes.c_int)]
+
+
 class BinParams(ctypes.Structure):
     _fields_ = [("capacity", ctypes.c_int), ("width", ctypes.c_int), ("height", ctypes.c_int),
                 ("tile_w", ctypes.c_int), ("tile_h", ctypes.c_int), ("max_pairs", ctypes.c_int64)]
@@ -68,7 +73,7 @@ class LossParams(ctypes.Structure):
 SYMBOLS = (
     "gsb_abi_version", "gsb_last_error", "gsb_launch_count",
     "gsb_cluster_compact_workspace_size", "gsb_cluster_compact",
-    "gsb_project_fwd", "gsb_project_bwd",
+    "gsb_project_fwd", "gsb_project_bwd", "gsb_sh_from_colors",
     "gsb_bin_workspace_size", "gsb_tile_sort_plan", "gsb_bin",
     "gsb_raster_workspace_size", "gsb_raster_bit_words", "gsb_raster_fwd", "gsb_raster_bwd",
     "gsb_raster_pack", "gsb_raster_bwd_prepare",
@@ -101,6 +106,8 @@ def _load():
     lib.gsb_project_fwd.argtypes = [vp, vp] + [vp] * 18
     lib.gsb_project_bwd.restype = ctypes.c_int
     lib.gsb_project_bwd.argtypes = [vp, vp] + [vp] * 22
+    lib.gsb_sh_from_colors.restype = ctypes.c_int
+    lib.gsb_sh_from_colors.argtypes = [vp, vp] + [vp] * 4
     lib.gsb_bin.restype = ctypes.c_int
     lib.gsb_bin.argtypes = [vp, vp, vp, sz] + [vp] * 10
     lib.gsb_raster_fwd.restype = ctypes.c_int

@@ -47,6 +47,18 @@ __device__ __forceinline__ int64_t slot_of(int64_t i, int capacity, const int32_
     return s < capacity ? s : -1;
 }
 
+// Is cluster c among the ascending visible-cluster ids[0:count]?
+__device__ __forceinline__ bool cluster_listed(const int32_t* ids, int count, int64_t c)
+{
+    int lo = 0, hi = count;
+    while (lo < hi) {
+        const int mid = (lo + hi) >> 1;
+        if (__ldg(ids + mid) < c) lo = mid + 1;
+        else hi = mid;
+    }
+    return lo < count && __ldg(ids + lo) == c;
+}
+
 // SH basis values (LiteGS/3DGS real SH order, reference/sh.py:8-36).
 template <int DEGREE>
 __device__ __forceinline__ void sh_basis(float dx, float dy, float dz, float b[16])
@@ -267,20 +279,39 @@ __global__ void __launch_bounds__(kProjThreads) project_bwd_kernel(
     constexpr int NB = (DEGREE + 1) * (DEGREE + 1);
     int count = p.compacted ? __ldg(cluster_count) : 0;
     int64_t i = (int64_t)blockIdx.x * kProjThreads + threadIdx.x;
-    int64_t g = slot_of(i, p.capacity, cluster_ids, count, p.cluster_size, p.compacted);
-    if (g < 0) return;
+    // Pool-order output of a compacted pullback covers every slot: the rows of
+    // unlisted clusters are written as zeros (their cotangents are not read).
+    const bool pool_order = p.compacted && !p.compact_gradients;
+    int64_t g;
+    bool listed = true;
+    if (pool_order) {
+        if (i >= p.capacity) return;
+        g = i;
+        listed = cluster_listed(cluster_ids, count, g / p.cluster_size);
+    } else {
+        g = slot_of(i, p.capacity, cluster_ids, count, p.cluster_size, p.compacted);
+        if (g < 0) return;
+    }
     const int64_t o = p.compact_gradients ? i : g;
     const int shg = SH_MODE == 1 ? 3 : p.sh_gradient_dim * 3;
     float* osh = out_sh + o * shg;
     const bool vec_out = (shg & 3) == 0 && (reinterpret_cast<uintptr_t>(out_sh) & 15) == 0;
 
-    const float2 gm = __ldg(reinterpret_cast<const float2*>(gmean + g * 2));
-    const float4 gcn = __ldg(reinterpret_cast<const float4*>(gconic + g * 4));
-    const float gc0 = gcolor[g * 3], gc1 = gcolor[g * 3 + 1], gc2 = gcolor[g * 3 + 2];
-    const float gal = galpha[g];
-    bool has = gal != 0.0f || gm.x != 0.0f || gm.y != 0.0f || gcn.x != 0.0f || gcn.y != 0.0f ||
-               gcn.z != 0.0f || gcn.w != 0.0f || gc0 != 0.0f || gc1 != 0.0f || gc2 != 0.0f;
-    if (!p.rgb_only) has = has || gdepth[g] != 0.0f || gradius[g] != 0.0f;
+    float2 gm = make_float2(0.f, 0.f);
+    float4 gcn = make_float4(0.f, 0.f, 0.f, 0.f);
+    float gc0 = 0.f, gc1 = 0.f, gc2 = 0.f, gal = 0.f;
+    bool has = false;
+    if (listed) {
+        gm = __ldg(reinterpret_cast<const float2*>(gmean + g * 2));
+        gcn = __ldg(reinterpret_cast<const float4*>(gconic + g * 4));
+        gc0 = gcolor[g * 3];
+        gc1 = gcolor[g * 3 + 1];
+        gc2 = gcolor[g * 3 + 2];
+        gal = galpha[g];
+        has = gal != 0.0f || gm.x != 0.0f || gm.y != 0.0f || gcn.x != 0.0f || gcn.y != 0.0f ||
+              gcn.z != 0.0f || gcn.w != 0.0f || gc0 != 0.0f || gc1 != 0.0f || gc2 != 0.0f;
+        if (!p.rgb_only) has = has || gdepth[g] != 0.0f || gradius[g] != 0.0f;
+    }
     if (!has) {
         // Occluded or culled splats: zero gradients (projection_backward.py:61-80).
         out_xyz[o * 3] = out_xyz[o * 3 + 1] = out_xyz[o * 3 + 2] = 0.0f;
@@ -466,15 +497,60 @@ __global__ void __launch_bounds__(kProjThreads) project_bwd_kernel(
     out_xyz[o * 3 + 2] = v[2] * gx + v[6] * gy + v[10] * gz + gzw;
 }
 
-// kernels/projection_backward.py:370-390 (_clear_parameter_grads).
-__global__ void clear_grads_kernel(int64_t capacity, int shg, float* gxyz, float* gscale,
-                                   float* grot, float* gop, float* gsh)
+// training/sh_pullback.py:18-53 summed over views: the SH coefficient
+// cotangents of colour cotangents that were masked where the colour clamped
+// (the sh_color_only pullback output),
+//   gsh[g][k][c] = sum_v B_k(dir_gv) colors[v][g][c],
+// with dir_gv normalised exactly as the pullback does; bands above DEGREE and
+// coefficients past (DEGREE+1)^2 are zero.  A view whose three cotangents
+// are zero (the Gaussian was culled or occluded there) adds nothing.
+template <int DEGREE>
+__global__ void __launch_bounds__(kProjThreads) sh_from_colors_kernel(
+    int64_t capacity, int sh_dim, int views, const float* __restrict__ xyz,
+    const float* __restrict__ centers, const float* __restrict__ colors, float* __restrict__ gsh)
 {
-    int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i < capacity * shg) gsh[i] = 0.0f;
-    if (i < capacity * 4) grot[i] = 0.0f;
-    if (i < capacity * 3) gxyz[i] = gscale[i] = 0.0f;
-    if (i < capacity) gop[i] = 0.0f;
+    constexpr int NB = (DEGREE + 1) * (DEGREE + 1);
+    const int64_t g = (int64_t)blockIdx.x * kProjThreads + threadIdx.x;
+    if (g >= capacity) return;
+    const float wx = xyz[g * 3], wy = xyz[g * 3 + 1], wz = xyz[g * 3 + 2];
+    float acc[NB * 3];
+#pragma unroll
+    for (int c = 0; c < NB * 3; c++) acc[c] = 0.0f;
+    for (int v = 0; v < views; v++) {
+        const float* col = colors + ((int64_t)v * capacity + g) * 3;
+        const float c0 = col[0], c1 = col[1], c2 = col[2];
+        if (c0 == 0.0f && c1 == 0.0f && c2 == 0.0f) continue;
+        const float vx = wx - __ldg(centers + v * 3), vy = wy - __ldg(centers + v * 3 + 1),
+                    vz = wz - __ldg(centers + v * 3 + 2);
+        const float dir_denom = sqrtf(fmaxf(vx * vx + vy * vy + vz * vz, 1e-16f));
+        const float dx = vx / dir_denom, dy = vy / dir_denom, dz = vz / dir_denom;
+        float bas[16];
+        sh_basis<DEGREE>(dx, dy, dz, bas);
+#pragma unroll
+        for (int k = 0; k < NB; k++) {
+            acc[k * 3] = fmaf(bas[k], c0, acc[k * 3]);
+            acc[k * 3 + 1] = fmaf(bas[k], c1, acc[k * 3 + 1]);
+            acc[k * 3 + 2] = fmaf(bas[k], c2, acc[k * 3 + 2]);
+        }
+    }
+    float* out = gsh + g * (int64_t)sh_dim * 3;
+    const int n = sh_dim * 3;
+    if ((n & 3) == 0 && (reinterpret_cast<uintptr_t>(gsh) & 15) == 0) {
+        constexpr int kChunks = (NB * 3 + 3) / 4;
+#pragma unroll
+        for (int k = 0; k < kChunks; k++) {
+            float e[4];
+#pragma unroll
+            for (int t = 0; t < 4; t++) e[t] = 4 * k + t < NB * 3 ? acc[4 * k + t] : 0.0f;
+            reinterpret_cast<float4*>(out)[k] = make_float4(e[0], e[1], e[2], e[3]);
+        }
+        for (int k = kChunks; k < n / 4; k++)
+            reinterpret_cast<float4*>(out)[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+    } else {
+#pragma unroll
+        for (int c = 0; c < NB * 3; c++) out[c] = acc[c];
+        for (int c = NB * 3; c < n; c++) out[c] = 0.0f;
+    }
 }
 
 // ---------------------------------------------------------------------------
@@ -613,12 +689,6 @@ extern "C" int gsb_project_bwd(gsb_stream_t stream, const gsb_project_bwd_params
         return GSB_ERR_INVALID;
     cudaStream_t s = as_stream(stream);
     int shg = p->sh_gradient_dim * 3;
-    if (p->compacted && !p->compact_gradients) {
-        int64_t n = (int64_t)p->capacity * (shg > 4 ? shg : 4);
-        clear_grads_kernel<<<ceil_div(n, 256), 256, 0, s>>>(p->capacity, shg, gxyz, glog_scale,
-                                                            grotation, gopacity, gsh);
-        if (int e = check_launch()) return e;
-    }
     int blocks = ceil_div(p->capacity, kProjThreads);
 #define GSB_PROJ_BWD(D, M)                                                                        \
     project_bwd_kernel<D, M><<<blocks, kProjThreads, 0, s>>>(                                     \
@@ -673,4 +743,28 @@ extern "C" int gsb_cluster_compact(gsb_stream_t stream, const gsb_cluster_params
         return check_launch();
     }
     return GSB_OK;
+}
+
+extern "C" int gsb_sh_from_colors(gsb_stream_t stream, const gsb_sh_params* p, const float* xyz,
+                                  const float* centers, const float* colors, float* gsh)
+{
+    if (!p) return GSB_ERR_NULL;
+    if (p->capacity < 0 || p->sh_dim < 1 || p->degree < 0 || p->degree > 3 ||
+        (p->degree + 1) * (p->degree + 1) > p->sh_dim || p->views < 0)
+        return GSB_ERR_INVALID;
+    if (p->capacity == 0) return GSB_OK;
+    if (!xyz || !gsh || (p->views > 0 && (!centers || !colors))) return GSB_ERR_NULL;
+    cudaStream_t s = as_stream(stream);
+    const int blocks = ceil_div(p->capacity, kProjThreads);
+#define GSB_SH_FROM_COLORS(D)                                                                  \
+    sh_from_colors_kernel<D><<<blocks, kProjThreads, 0, s>>>(p->capacity, p->sh_dim, p->views, \
+                                                             xyz, centers, colors, gsh)
+    switch (p->degree) {
+        case 0: GSB_SH_FROM_COLORS(0); break;
+        case 1: GSB_SH_FROM_COLORS(1); break;
+        case 2: GSB_SH_FROM_COLORS(2); break;
+        default: GSB_SH_FROM_COLORS(3); break;
+    }
+#undef GSB_SH_FROM_COLORS
+    return check_launch();
 }

@@ -144,8 +144,13 @@ def compute_projection_gradients(parameters, camera: DeviceCamera, projected_col
                                  cotangents: ProjectedGaussians, config: CapacityConfig,
                                  active_degree: int | None, visible_clusters,
                                  compact_gradients: bool, rgb_only: bool = False,
-                                 active_sh_only: bool = False, sh_color_only: bool = False):
-    """kernels/projector.py:240-307: parameter gradients from cotangents."""
+                                 active_sh_only: bool = False, sh_color_only: bool = False,
+                                 out=None):
+    """kernels/projector.py:240-307: parameter gradients from cotangents.
+
+    out: optional (xyz, log_scale, rotation, opacity, sh) gradient tensors to
+    write (contiguous float32 of the output shapes), e.g. views of one flat
+    buffer that a collective reduces in place."""
     xyz, log_scale, rotation, opacity, sh = parameters
     _require_cuda(xyz, "projection pullback")
     C = config.max_gaussians
@@ -153,9 +158,14 @@ def compute_projection_gradients(parameters, camera: DeviceCamera, projected_col
     sh_dim = int(sh.shape[1])
     shg = 1 if sh_color_only else ((degree + 1) ** 2 if active_sh_only else sh_dim)
     dev = xyz.device
-    out = [torch.empty(C, 3, dtype=_f32, device=dev), torch.empty(C, 3, dtype=_f32, device=dev),
-           torch.empty(C, 4, dtype=_f32, device=dev), torch.empty(C, 1, dtype=_f32, device=dev),
-           torch.empty(C, shg, 3, dtype=_f32, device=dev)]
+    shapes = ((C, 3), (C, 3), (C, 4), (C, 1), (C, shg, 3))
+    if out is None:
+        out = [torch.empty(shape, dtype=_f32, device=dev) for shape in shapes]
+    else:
+        out = list(out)
+        for o, shape in zip(out, shapes):
+            if tuple(o.shape) != shape or o.dtype != _f32 or not o.is_contiguous():
+                raise ValueError(f"gradient output must be contiguous float32 {shape}")
     ids, count = (None, None) if visible_clusters is None else visible_clusters
     p = L.ProjectBwdParams(C, sh_dim, shg, degree, camera.near, config.cluster_size,
                            int(visible_clusters is not None), int(compact_gradients),
@@ -178,6 +188,26 @@ def compute_projection_gradients(parameters, camera: DeviceCamera, projected_col
     return tuple(out)
 
 
+def sh_from_colors(xyz: torch.Tensor, centers: torch.Tensor, colors: torch.Tensor,
+                   degree: int, sh_dim: int, out: torch.Tensor | None = None) -> torch.Tensor:
+    """training/sh_pullback.py:18-53 summed over views: SH coefficient
+    cotangents [C, sh_dim, 3] from per-view masked colour cotangents
+    colors [V, C, 3] (the sh_color_only pullback output of each view, pool
+    order) and the views' camera centres [V, 3]."""
+    _require_cuda(xyz, "SH reconstruction")
+    C = int(xyz.shape[0])
+    views = int(centers.shape[0])
+    if tuple(colors.shape) != (views, C, 3) and tuple(colors.shape) != (views, C, 1, 3):
+        raise ValueError("colors must be [views, C, 3]")
+    if out is None:
+        out = torch.empty(C, sh_dim, 3, dtype=_f32, device=xyz.device)
+    p = L.ShParams(C, sh_dim, degree, views)
+    L.check(L.lib.gsb_sh_from_colors(_stream(), L.ref(p), _ptr(_c(xyz, _f32)),
+                                     _ptr(_c(centers, _f32)), _ptr(_c(colors, _f32)), _ptr(out)),
+            "SH reconstruction")
+    return out
+
+
 def project_with_compact_pullback(pool: GaussianArrays, camera: DeviceCamera,
                                   config: CapacityConfig, active_degree: int, clusters, *,
                                   rgb_only: bool = False, active_sh_only: bool = False,
@@ -189,10 +219,13 @@ def project_with_compact_pullback(pool: GaussianArrays, camera: DeviceCamera,
     parameters = (pool.xyz, pool.log_scale, pool.rotation, pool.opacity, pool.sh)
     projected = _project(pool, camera, config, active_degree, clusters, False, visible_color_only)
 
-    def pullback(cotangents: ProjectedGaussians):
+    def pullback(cotangents: ProjectedGaussians, out=None, compact: bool = True):
+        """Gradients in visible-cluster order, or (compact=False) in pool
+        order with the unlisted clusters' rows zeroed; out as in
+        compute_projection_gradients."""
         return compute_projection_gradients(parameters, camera, projected.color, cotangents,
-                                            config, active_degree, clusters, True, rgb_only,
-                                            active_sh_only, sh_color_only)
+                                            config, active_degree, clusters, compact, rgb_only,
+                                            active_sh_only, sh_color_only, out=out)
 
     return projected, pullback
 

@@ -69,3 +69,130 @@ def test_training_step_inactive_and_culled_gaussians():
     for got, ref in zip(out.gradients, exp["grads"]):
         g = got.cpu().numpy().reshape(4096, -1)[:rows]
         assert rel_l2(g, ref.reshape(4096, -1)[:rows]) < 1e-3
+
+
+def test_pool_order_gradients_for_the_view_sharded_exchange():
+    """pool_grads: the step writes pool-order gradients (culled clusters' rows
+    zero, stale contents overwritten) into views of one flat buffer, equal to
+    the compact gradients scattered to pool order; the graphed step does the
+    same on every replay."""
+    from jaxgs_b200.scene import Camera, CapacityConfig, config0_scene, world_cluster_bounds
+    from jaxgs_b200.step import (GraphedTrainingStep, compute_training_step, pool_gradient_buffer,
+                                 scatter_compact)
+    from jaxgs_b200.types import DeviceCamera, GaussianArrays
+
+    pool_np, _, target = config0_scene()
+    # Clusters as x slabs, camera on the +x side: the low-x clusters are culled.
+    order = np.argsort(pool_np["xyz"][:, 0], kind="stable")
+    pool_np = {k: np.ascontiguousarray(v[order]) for k, v in pool_np.items()}
+    cam = Camera.look_at((1.8, 0.0, -2.5), (1.8, 0.0, 0.0), 110.0, 110.0, 128, 96, near=0.01,
+                         far=100.0)
+    n = pool_np["xyz"].shape[0]
+    config = CapacityConfig(n, 128, 16, 16, 3, n * 64, tile_height=8)
+    center, extent, valid = world_cluster_bounds(pool_np, 128)
+    bounds = (torch.as_tensor(center, device="cuda"), torch.as_tensor(extent, device="cuda"),
+              torch.as_tensor(valid.astype(np.uint8), device="cuda"))
+    pool = GaussianArrays.from_numpy(pool_np)
+    dcam = DeviceCamera.from_camera(cam)
+    tgt = torch.as_tensor(target, device="cuda")
+    ref = compute_training_step(pool, bounds, dcam, tgt, config, 3)
+    count = int(ref.visible_clusters[1].item())
+    assert 0 < count < n // 128  # some clusters culled
+    expected = scatter_compact(ref.gradients, ref.visible_clusters, config)
+    flat, views = pool_gradient_buffer(pool, config, 3)
+    flat.fill_(float("nan"))
+    out = compute_training_step(pool, bounds, dcam, tgt, config, 3, pool_grads=views)
+    torch.cuda.synchronize()
+    assert abs(float(out.loss) - float(ref.loss)) <= 1e-6 * abs(float(ref.loss))
+    for got, exp in zip(views, expected):
+        g, e = got.cpu().numpy().reshape(-1), exp.cpu().numpy().reshape(-1)
+        assert np.isfinite(g).all()
+        assert rel_l2(g, e) < 1e-5
+    graphed = GraphedTrainingStep(pool, bounds, dcam, tgt, config, 3, pool_grads=views)
+    flat.fill_(float("nan"))
+    graphed()
+    torch.cuda.synchronize()
+    for got, exp in zip(views, expected):
+        assert rel_l2(got.cpu().numpy().reshape(-1), exp.cpu().numpy().reshape(-1)) < 1e-5
+
+
+def _np_sh_from_colors(xyz, centers, colors, degree, sh_dim):
+    """training/sh_pullback.py:18-53 in numpy (float64), summed over views."""
+    out = np.zeros((xyz.shape[0], sh_dim, 3))
+    for center, gc in zip(centers, colors):
+        delta = xyz.astype(np.float64) - center
+        norm = np.sqrt(np.maximum((delta * delta).sum(1, keepdims=True), 1e-16))
+        dx, dy, dz = (delta / norm).T
+        xx, yy, zz = dx * dx, dy * dy, dz * dz
+        basis = [np.full_like(dx, 0.28209479177387814), -0.4886025119029199 * dy,
+                 0.4886025119029199 * dz, -0.4886025119029199 * dx,
+                 1.0925484305920792 * dx * dy, -1.0925484305920792 * dy * dz,
+                 0.31539156525252005 * (2 * zz - xx - yy), -1.0925484305920792 * dx * dz,
+                 0.5462742152960396 * (xx - yy), -0.5900435899266435 * dy * (3 * xx - yy),
+                 2.890611442640554 * dx * dy * dz, -0.4570457994644658 * dy * (4 * zz - xx - yy),
+                 0.3731763325901154 * dz * (2 * zz - 3 * xx - 3 * yy),
+                 -0.4570457994644658 * dx * (4 * zz - xx - yy), 1.445305721320277 * dz * (xx - yy),
+                 -0.5900435899266435 * dx * (xx - 3 * yy)]
+        for k in range((degree + 1) ** 2):
+            out[:, k, :] += basis[k][:, None] * gc.reshape(-1, 3)
+    return out
+
+
+@pytest.mark.parametrize("degree,sh_dim", [(0, 1), (1, 4), (2, 16), (3, 16)])
+def test_sh_from_colors_matches_sh_pullback(degree, sh_dim):
+    from jaxgs_b200 import kernels as K
+
+    rng = np.random.default_rng(degree)
+    C, V = 1000, 3
+    xyz = rng.normal(0, 2, (C, 3)).astype(np.float32)
+    centers = rng.normal(0, 5, (V, 3)).astype(np.float32)
+    colors = rng.normal(0, 1, (V, C, 3)).astype(np.float32)
+    colors[:, ::7] = 0.0  # culled in some views
+    xyz[5] = centers[1]   # direction floor (|delta| = 0)
+    got = K.sh_from_colors(torch.as_tensor(xyz, device="cuda"), torch.as_tensor(centers, device="cuda"),
+                           torch.as_tensor(colors, device="cuda"), degree, sh_dim)
+    exp = _np_sh_from_colors(xyz, centers, colors, degree, sh_dim)
+    np.testing.assert_allclose(got.cpu().numpy(), exp, rtol=1e-5, atol=1e-6)
+
+
+def test_view_sharded_exchange_math_equals_summed_per_view_gradients():
+    """The exchange's decomposition (summed geometric gradients + per-view
+    colour cotangents expanded on each view's SH basis) equals the sum of
+    the per-view full gradients, here for three views on one GPU."""
+    from jaxgs_b200 import kernels as K
+    from jaxgs_b200.scene import CapacityConfig, config0_scene, ring_cameras, world_cluster_bounds
+    from jaxgs_b200.step import compute_training_step, pool_gradient_buffer
+    from jaxgs_b200.types import DeviceCamera, GaussianArrays
+
+    pool_np, _, target = config0_scene()
+    n = pool_np["xyz"].shape[0]
+    config = CapacityConfig(n, 128, 16, 16, 3, n * 64, tile_height=8)
+    center, extent, valid = world_cluster_bounds(pool_np, 128)
+    bounds = (torch.as_tensor(center, device="cuda"), torch.as_tensor(extent, device="cuda"),
+              torch.as_tensor(valid.astype(np.uint8), device="cuda"))
+    pool = GaussianArrays.from_numpy(pool_np)
+    tgt = torch.as_tensor(target, device="cuda")
+    cams = [DeviceCamera.from_camera(c) for c in ring_cameras(3, radius=4.0, height=0.5, width=128,
+                                                                height_px=96, focal=110.0)]
+    expected = None
+    for cam in cams:
+        flat, views = pool_gradient_buffer(pool, config, 3)
+        compute_training_step(pool, bounds, cam, tgt, config, 3, pool_grads=views)
+        expected = [v.clone() for v in views] if expected is None else [
+            e + v for e, v in zip(expected, views)]
+    geometric = [torch.zeros_like(e) for e in expected[:4]]
+    colors = []
+    for cam in cams:
+        bufs = tuple(torch.empty_like(e) for e in expected[:4]) + (
+            torch.empty(n, 1, 3, device="cuda"),)
+        compute_training_step(pool, bounds, cam, tgt, config, 3, pool_grads=bufs,
+                              sh_color_only=True)
+        geometric = [a + b for a, b in zip(geometric, bufs[:4])]
+        colors.append(bufs[4].view(n, 3))
+    centers = torch.stack([c.center.reshape(3) for c in cams])
+    sh = K.sh_from_colors(pool.xyz, centers, torch.stack(colors), 3, 16)
+    torch.cuda.synchronize()
+    for got, exp in zip((*geometric, sh), expected):
+        g, e = got.cpu().numpy().reshape(-1), exp.cpu().numpy().reshape(-1)
+        assert np.abs(e).max() > 0
+        assert rel_l2(g, e) < 1e-5
