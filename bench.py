@@ -159,8 +159,18 @@ def run_ours(args) -> None:
     if world > 1:
         import datetime
 
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=device)
+        # NCCL may print its version banner on stdout; keep stdout for the
+        # one JSON line.
+        saved = os.dup(1)
+        os.dup2(2, 1)
+        try:
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                    device_id=device)
+            dist.barrier()
+        finally:
+            sys.stdout.flush()
+            os.dup2(saved, 1)
+            os.close(saved)
     config = _config()
     pool_np, camera = _workload(rank)
     pool = GaussianArrays.from_numpy(pool_np, device=device)

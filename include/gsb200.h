@@ -147,8 +147,11 @@ GSB_API int gsb_project_bwd(gsb_stream_t stream, const gsb_project_bwd_params* p
  * masked colour cotangent expanded on the SH basis of its direction from
  * the camera centre), summed over `views` cameras so that view-sharded ranks
  * can exchange 3 floats per Gaussian and view instead of sh_dim * 3.
- * Inputs: xyz[C*3], centers[views*3], colors[views*C*3] (view-major; each the
- * sh_color_only output of gsb_project_bwd in pool order).
+ * Inputs: xyz[C*3]; view v's centre at centers + v * center_stride (3
+ * floats) and its colour cotangents at colors + v * view_stride (C*3 floats,
+ * the sh_color_only output of gsb_project_bwd in pool order); strides in
+ * floats, 0 = dense (3 and C*3), so one gathered buffer of [colours | centre]
+ * rows can be read in place.
  * Output: gsh[C*sh_dim*3] (bands above degree zero).
  * ------------------------------------------------------------------------ */
 typedef struct {
@@ -156,6 +159,8 @@ typedef struct {
     int sh_dim;
     int degree;
     int views;
+    int64_t view_stride;
+    int64_t center_stride;
 } gsb_sh_params;
 
 GSB_API int gsb_sh_from_colors(gsb_stream_t stream, const gsb_sh_params* p, const float* xyz,

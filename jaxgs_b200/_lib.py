@@ -40,7 +40,8 @@ class ProjectBwdParams(ctypes.Structure):
 
 class ShParams(ctypes.Structure):
     _fields_ = [("capacity", ctypes.c_int), ("sh_dim", ctypes.c_int), ("degree", ctypes.c_int),
-                ("views", ctypes.c_int)]
+                ("views", ctypes.c_int), ("view_stride", ctypes.c_int64),
+                ("center_stride", ctypes.c_int64)]
 
 
 class BinParams(ctypes.Structure):

@@ -506,8 +506,9 @@ __global__ void __launch_bounds__(kProjThreads) project_bwd_kernel(
 // are zero (the Gaussian was culled or occluded there) adds nothing.
 template <int DEGREE>
 __global__ void __launch_bounds__(kProjThreads) sh_from_colors_kernel(
-    int64_t capacity, int sh_dim, int views, const float* __restrict__ xyz,
-    const float* __restrict__ centers, const float* __restrict__ colors, float* __restrict__ gsh)
+    int64_t capacity, int sh_dim, int views, int64_t view_stride, int64_t center_stride,
+    const float* __restrict__ xyz, const float* __restrict__ centers,
+    const float* __restrict__ colors, float* __restrict__ gsh)
 {
     constexpr int NB = (DEGREE + 1) * (DEGREE + 1);
     const int64_t g = (int64_t)blockIdx.x * kProjThreads + threadIdx.x;
@@ -517,11 +518,11 @@ __global__ void __launch_bounds__(kProjThreads) sh_from_colors_kernel(
 #pragma unroll
     for (int c = 0; c < NB * 3; c++) acc[c] = 0.0f;
     for (int v = 0; v < views; v++) {
-        const float* col = colors + ((int64_t)v * capacity + g) * 3;
+        const float* col = colors + v * view_stride + g * 3;
         const float c0 = col[0], c1 = col[1], c2 = col[2];
         if (c0 == 0.0f && c1 == 0.0f && c2 == 0.0f) continue;
-        const float vx = wx - __ldg(centers + v * 3), vy = wy - __ldg(centers + v * 3 + 1),
-                    vz = wz - __ldg(centers + v * 3 + 2);
+        const float* cv = centers + v * center_stride;
+        const float vx = wx - __ldg(cv), vy = wy - __ldg(cv + 1), vz = wz - __ldg(cv + 2);
         const float dir_denom = sqrtf(fmaxf(vx * vx + vy * vy + vz * vz, 1e-16f));
         const float dx = vx / dir_denom, dy = vy / dir_denom, dz = vz / dir_denom;
         float bas[16];
@@ -749,16 +750,20 @@ extern "C" int gsb_sh_from_colors(gsb_stream_t stream, const gsb_sh_params* p, c
                                   const float* centers, const float* colors, float* gsh)
 {
     if (!p) return GSB_ERR_NULL;
+    const int64_t view_stride = p->view_stride ? p->view_stride : (int64_t)p->capacity * 3;
+    const int64_t center_stride = p->center_stride ? p->center_stride : 3;
     if (p->capacity < 0 || p->sh_dim < 1 || p->degree < 0 || p->degree > 3 ||
-        (p->degree + 1) * (p->degree + 1) > p->sh_dim || p->views < 0)
+        (p->degree + 1) * (p->degree + 1) > p->sh_dim || p->views < 0 ||
+        view_stride < (int64_t)p->capacity * 3 || center_stride < 3)
         return GSB_ERR_INVALID;
     if (p->capacity == 0) return GSB_OK;
     if (!xyz || !gsh || (p->views > 0 && (!centers || !colors))) return GSB_ERR_NULL;
     cudaStream_t s = as_stream(stream);
     const int blocks = ceil_div(p->capacity, kProjThreads);
-#define GSB_SH_FROM_COLORS(D)                                                                  \
-    sh_from_colors_kernel<D><<<blocks, kProjThreads, 0, s>>>(p->capacity, p->sh_dim, p->views, \
-                                                             xyz, centers, colors, gsh)
+#define GSB_SH_FROM_COLORS(D)                                                               \
+    sh_from_colors_kernel<D><<<blocks, kProjThreads, 0, s>>>(                               \
+        p->capacity, p->sh_dim, p->views, view_stride, center_stride, xyz, centers, colors, \
+        gsh)
     switch (p->degree) {
         case 0: GSB_SH_FROM_COLORS(0); break;
         case 1: GSB_SH_FROM_COLORS(1); break;

@@ -15,6 +15,8 @@ Reference bindings mirrored (src/jaxgs/...):
 
 from __future__ import annotations
 
+import ctypes
+
 import torch
 
 from . import _lib as L
@@ -191,19 +193,30 @@ def compute_projection_gradients(parameters, camera: DeviceCamera, projected_col
 def sh_from_colors(xyz: torch.Tensor, centers: torch.Tensor, colors: torch.Tensor,
                    degree: int, sh_dim: int, out: torch.Tensor | None = None) -> torch.Tensor:
     """training/sh_pullback.py:18-53 summed over views: SH coefficient
-    cotangents [C, sh_dim, 3] from per-view masked colour cotangents
-    colors [V, C, 3] (the sh_color_only pullback output of each view, pool
-    order) and the views' camera centres [V, 3]."""
+    cotangents [C, sh_dim, 3] from per-view masked colour cotangents (the
+    sh_color_only pullback output of each view, pool order) and the views'
+    camera centres.  colors: [V, C, 3], or [V, >= C*3 + 3] rows holding a
+    view's C*3 cotangents followed by its centre (then centers is None)."""
     _require_cuda(xyz, "SH reconstruction")
     C = int(xyz.shape[0])
-    views = int(centers.shape[0])
-    if tuple(colors.shape) != (views, C, 3) and tuple(colors.shape) != (views, C, 1, 3):
-        raise ValueError("colors must be [views, C, 3]")
+    views = int(colors.shape[0])
+    if centers is None:
+        if colors.ndim != 2 or colors.shape[1] < C * 3 + 3 or not colors.is_contiguous():
+            raise ValueError("packed colour rows must be [V, >= C*3 + 3] contiguous")
+        row = int(colors.shape[1])
+        p = L.ShParams(C, sh_dim, degree, views, row, row)
+        centers_ptr = colors.data_ptr() + C * 3 * 4
+    else:
+        if tuple(colors.reshape(views, -1).shape) != (views, C * 3) or tuple(centers.shape) != (views, 3):
+            raise ValueError("colors must be [V, C, 3] with centers [V, 3]")
+        centers = _c(centers, _f32)
+        colors = _c(colors, _f32)
+        p = L.ShParams(C, sh_dim, degree, views, 0, 0)
+        centers_ptr = centers.data_ptr()
     if out is None:
         out = torch.empty(C, sh_dim, 3, dtype=_f32, device=xyz.device)
-    p = L.ShParams(C, sh_dim, degree, views)
     L.check(L.lib.gsb_sh_from_colors(_stream(), L.ref(p), _ptr(_c(xyz, _f32)),
-                                     _ptr(_c(centers, _f32)), _ptr(_c(colors, _f32)), _ptr(out)),
+                                     ctypes.c_void_p(centers_ptr), _ptr(colors), _ptr(out)),
             "SH reconstruction")
     return out
 

@@ -168,12 +168,12 @@ class ViewShardedExchange:
     Each rank's step writes, in pool order, its geometric gradients (xyz,
     log_scale, rotation, opacity: 11 floats per Gaussian) into one flat buffer
     and its masked colour cotangents (3 floats, the sh_color_only pullback)
-    into another.  exchange() sums the geometric buffer with one all-reduce,
-    all-gathers the colour cotangents and the views' camera centres, and
-    expands them into the summed SH gradients (training/sh_pullback.py:18-53
-    summed over the views).  The result equals the all-reduced per-view
-    gradients with SH, while 12 instead of 192 bytes per Gaussian and view
-    cross NVLink for the SH part.
+    into a row that also carries its camera centre.  exchange() all-gathers
+    the rows, sums the geometric buffer with one all-reduce and, while that
+    runs, expands every view's colour cotangents into the summed SH gradients
+    (training/sh_pullback.py:18-53 summed over the views).  The result equals
+    the all-reduced per-view gradients with SH, while 12 instead of 192
+    bytes per Gaussian and view cross NVLink for the SH part.
     """
 
     def __init__(self, pool: GaussianArrays, config: CapacityConfig, active_degree: int,
@@ -193,10 +193,11 @@ class ViewShardedExchange:
         for n, shape in ((C * 3, (C, 3)), (C * 3, (C, 3)), (C * 4, (C, 4)), (C, (C, 1))):
             views.append(self.geometric[at:at + n].view(shape))
             at += n
-        self.colors = torch.empty(C, 1, 3, dtype=torch.float32, device=dev)
-        self.center = torch.empty(3, dtype=torch.float32, device=dev)
-        self.all_colors = torch.empty(self.world, C, 3, dtype=torch.float32, device=dev)
-        self.all_centers = torch.empty(self.world, 3, dtype=torch.float32, device=dev)
+        # [colour cotangents C*3 | camera centre 3 | pad 1] per rank.
+        self.row = torch.zeros(C * 3 + 4, dtype=torch.float32, device=dev)
+        self.colors = self.row[:C * 3].view(C, 1, 3)
+        self.center = self.row[C * 3:C * 3 + 3]
+        self.rows = torch.empty(self.world, C * 3 + 4, dtype=torch.float32, device=dev)
         self.sh = torch.empty(C, self.sh_dim, 3, dtype=torch.float32, device=dev)
         self.pool_grads = (*views, self.colors)
 
@@ -204,12 +205,10 @@ class ViewShardedExchange:
         """Sum the ranks' gradients; returns (xyz, log_scale, rotation,
         opacity, sh) in pool order, identical on every rank."""
         self.center.copy_(camera_center.reshape(3))
-        self.dist.all_reduce(self.geometric, group=self.group)
-        self.dist.all_gather_into_tensor(self.all_colors, self.colors.view(-1, 3),
-                                         group=self.group)
-        self.dist.all_gather_into_tensor(self.all_centers, self.center, group=self.group)
-        K.sh_from_colors(self.xyz, self.all_centers, self.all_colors, self.degree, self.sh_dim,
-                         out=self.sh)
+        self.dist.all_gather_into_tensor(self.rows, self.row, group=self.group)
+        work = self.dist.all_reduce(self.geometric, group=self.group, async_op=True)
+        K.sh_from_colors(self.xyz, None, self.rows, self.degree, self.sh_dim, out=self.sh)
+        work.wait()
         return (*self.pool_grads[:4], self.sh)
 
 
