@@ -148,7 +148,8 @@ def run_ours(args) -> None:
     from jaxgs_b200 import _lib
     from jaxgs_b200 import kernels as K
     from jaxgs_b200.scene import world_cluster_bounds
-    from jaxgs_b200.step import GraphedTrainingStep, ViewShardedExchange, compute_training_step
+    from jaxgs_b200.step import (GraphedTrainingStep, NvlsExchange, ViewShardedExchange,
+                                 compute_training_step)
     from jaxgs_b200.types import DeviceCamera, GaussianArrays
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -183,9 +184,11 @@ def run_ours(args) -> None:
     cam_host = [t.cpu().pin_memory() for t in (dcam.world_to_camera, dcam.intrinsics,
                                                dcam.center, dcam.planes)]
     degree = 3
-    exch = ViewShardedExchange(pool, config, degree) if world > 1 else None
-    pool_grads = exch.pool_grads if exch is not None else None
-    sharded = dict(pool_grads=pool_grads, sh_color_only=exch is not None)
+    exch = None
+    if world > 1:
+        use_nvls = os.environ.get("GSB_EXCHANGE", "nvls") == "nvls" and NvlsExchange.available()
+        exch = (NvlsExchange if use_nvls else ViewShardedExchange)(pool, config, degree)
+    sharded = exch.step_kwargs if exch is not None else {}
     stream = torch.cuda.current_stream()
     stage_events = []
     current_center = [dcam.center]
@@ -297,8 +300,9 @@ def run_ours(args) -> None:
                        "l2": "inputs larger than L2 (236 MB pool)",
                        "launch": "CUDA graph replay of the whole step",
                        "parallelism": f"view-sharded dp{world}" if world > 1 else "single view",
-                       "exchange": (f"per step: NCCL all-reduce of {exch.geometric.numel() * 4 / 1e6:.0f} MB "
-                                    f"geometric gradients, all-gather of {exch.colors.numel() * 4 / 1e6:.0f} MB "
+                       "exchange": (f"per step: {'NVLS multicast (own kernels)' if isinstance(exch, NvlsExchange) else 'NCCL'} "
+                                    f"all-reduce of {exch.geometric.numel() * 4 / 1e6:.0f} MB "
+                                    f"geometric gradients, all-gather of {config.max_gaussians * 12 / 1e6:.0f} MB "
                                     "colour cotangents per rank, SH expansion of all views")
                                    if exch is not None else None},
             "e2e": {"value": None if args.no_e2e else round(world * args.steps / e2e_elapsed, 2),

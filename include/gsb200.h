@@ -141,6 +141,25 @@ GSB_API int gsb_project_bwd(gsb_stream_t stream, const gsb_project_bwd_params* p
                     const float* galpha, float* gxyz, float* glog_scale, float* grotation,
                     float* gopacity, float* gsh);
 
+/* The colour-only, pool-order pullback (sh_color_only = 1, compacted = 1,
+ * compact_gradients = 0) fused with the all-gather of its colour
+ * cotangents: instead of gsh, the colours and the camera centre are stored
+ * through an NVLS multicast address into this rank's row of a symmetric row
+ * table, row = [centre x, y, z, 0 | colours C*3 | pad], row_floats >= 4 + C*3
+ * rounded up to a multiple of 4, row_multicast 16-byte aligned.  Every GPU's
+ * copy of the row is written; a gsb_exchange_barrier afterwards publishes
+ * it.  The geometric gradients are written locally as by gsb_project_bwd.
+ * No counterpart in the reference (its step sums per-view gradients with
+ * one collective after the pullback). */
+GSB_API int gsb_project_bwd_colors_multicast(
+    gsb_stream_t stream, const gsb_project_bwd_params* p, const float* xyz,
+    const float* log_scale, const float* rotation, const float* opacity, const float* sh,
+    const float* view, const float* intrinsics, const float* center, const float* color,
+    const int32_t* cluster_ids, const int32_t* cluster_count, const float* gmean,
+    const float* gdepth, const float* gconic, const float* gradius, const float* gcolor,
+    const float* galpha, float* gxyz, float* glog_scale, float* grotation, float* gopacity,
+    float* row_multicast, int64_t row_floats);
+
 /* ------------------------------------------------------------------------
  * SH coefficient cotangents from colour cotangents, summed over views.
  * Replaces training/sh_pullback.py:18-53 (with_sh_pullback: one view's
@@ -336,6 +355,37 @@ GSB_API int gsb_loss(gsb_stream_t stream, const gsb_loss_params* p, void* worksp
 #define GSB_LOSS_NOALLOC_MAX_TILES 16384
 GSB_API int gsb_loss_noalloc(gsb_stream_t stream, const gsb_loss_params* p, const float* image,
                      const void* target, float* loss, float* grad, float* scale);
+
+/* ------------------------------------------------------------------------
+ * View-sharded gradient exchange over NVLink / NVSwitch (NVLS multicast).
+ * No single counterpart in the reference: it replaces the NCCL all-reduce of
+ * the per-view gradients before the shared Adam update that the view-
+ * sharded training step performs with collectives
+ * written for symmetric memory (one allocation per GPU, mapped into an NVLS
+ * multicast object and into every peer).  One process per GPU; every rank
+ * makes the same calls in the same order.
+ *  - gsb_exchange_barrier: every rank stores an epoch into slot `rank` of
+ *    every peer's flags (peer_flags[q] = rank q's flags, a device array of
+ *    world pointers) and waits for all world slots of its own flags to reach
+ *    it.  epoch[1] and flags[world] start at zero on every rank.  A wait that
+ *    gives up (a peer missing for seconds) sets error[0] = 1 and returns.
+ *  - gsb_nvls_allreduce: sums count floats (a multiple of 4, 16-byte
+ *    aligned) over all ranks' copies through the multicast address: rank r
+ *    reduces and stores shard r.  Put a barrier before (inputs written) and
+ *    after (sum complete everywhere).
+ *  The all-gather of the colour cotangents is fused into the pullback
+ *  (gsb_project_bwd_colors_multicast).
+ * ------------------------------------------------------------------------ */
+typedef struct {
+    int world;
+    int rank;
+} gsb_exchange_params;
+
+GSB_API int gsb_exchange_barrier(gsb_stream_t stream, const gsb_exchange_params* p,
+                         uint32_t* const* peer_flags, const uint32_t* flags, uint32_t* epoch,
+                         int32_t* error);
+GSB_API int gsb_nvls_allreduce(gsb_stream_t stream, const gsb_exchange_params* p, float* multicast,
+                       int64_t count);
 
 #ifdef __cplusplus
 }

@@ -44,6 +44,10 @@ class ShParams(ctypes.Structure):
                 ("center_stride", ctypes.c_int64)]
 
 
+class ExchangeParams(ctypes.Structure):
+    _fields_ = [("world", ctypes.c_int), ("rank", ctypes.c_int)]
+
+
 class BinParams(ctypes.Structure):
     _fields_ = [("capacity", ctypes.c_int), ("width", ctypes.c_int), ("height", ctypes.c_int),
                 ("tile_w", ctypes.c_int), ("tile_h", ctypes.c_int), ("max_pairs", ctypes.c_int64)]
@@ -79,6 +83,7 @@ SYMBOLS = (
     "gsb_raster_workspace_size", "gsb_raster_bit_words", "gsb_raster_fwd", "gsb_raster_bwd",
     "gsb_raster_pack", "gsb_raster_bwd_prepare",
     "gsb_loss_workspace_size", "gsb_loss", "gsb_loss_noalloc",
+    "gsb_exchange_barrier", "gsb_nvls_allreduce", "gsb_project_bwd_colors_multicast",
 )
 
 
@@ -121,6 +126,13 @@ def _load():
     lib.gsb_raster_bwd_prepare.argtypes = [vp, vp, vp, sz] + [vp] * 8
     lib.gsb_loss.restype = ctypes.c_int
     lib.gsb_loss.argtypes = [vp, vp, vp, sz] + [vp] * 5
+    for name, n in (("gsb_exchange_barrier", 4),):
+        getattr(lib, name).restype = ctypes.c_int
+        getattr(lib, name).argtypes = [vp, vp] + [vp] * n
+    lib.gsb_nvls_allreduce.restype = ctypes.c_int
+    lib.gsb_nvls_allreduce.argtypes = [vp, vp, vp, ctypes.c_int64]
+    lib.gsb_project_bwd_colors_multicast.restype = ctypes.c_int
+    lib.gsb_project_bwd_colors_multicast.argtypes = [vp, vp] + [vp] * 22 + [ctypes.c_int64]
     lib.gsb_loss_noalloc.restype = ctypes.c_int
     lib.gsb_loss_noalloc.argtypes = [vp, vp] + [vp] * 5
     return lib

@@ -1,0 +1,127 @@
+// View-sharded gradient exchange over NVLink 5 / NVSwitch (sm_100a).
+//
+// The ranks of the view-sharded step (one process per GPU) hold their
+// gradient buffers in symmetric memory: the same allocation on every GPU,
+// mapped into one NVLS multicast object and into each peer's address space.
+//   * gsb_exchange_barrier: every rank stores an epoch into every peer's flag
+//     slot (release, system scope) and waits until all ranks' flags reach the
+//     epoch (acquire).  Each wait is bounded; on expiry the kernel records an
+//     error word and returns, so a missing peer can never hang the GPU.
+//   * gsb_nvls_allreduce: rank r owns the r-th shard of the buffer; for each
+//     16-byte chunk of it, multimem.ld_reduce makes the switch fetch and sum
+//     the chunk of every GPU, and multimem.st writes the sum into every GPU's
+//     copy.  Each GPU sends and receives about one buffer's worth of bytes.
+//   * The all-gather of the colour rows is fused into the pullback that
+//     produces them (project.cu, project_bwd_colors_multicast_kernel): each
+//     row is stored through the multicast address into every GPU's copy.
+// Callers put a barrier between a producer and these collectives and after
+// them (the sum is complete on every GPU only once every shard is stored).
+// No TMA and no cluster-multicast loads are used: peers' memory is touched
+// only by multimem.* and plain st/ld with system-scope ordering.
+#include "gsb_common.cuh"
+
+namespace gsb {
+namespace {
+
+constexpr int kBarrierSpinLimit = 1 << 22;  // about a second of local polls
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v)
+{
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p)
+{
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// One block, one thread per rank.  flags: this rank's slots [world] (each
+// peer writes slot `rank` of it); peer_flags[q]: rank q's slots.
+__global__ void exchange_barrier_kernel(int world, int rank, uint32_t* const* peer_flags,
+                                        const uint32_t* flags, uint32_t* epoch, int32_t* error)
+{
+    __shared__ uint32_t next;
+    if (threadIdx.x == 0) {
+        __threadfence_system();  // this rank's earlier writes precede its signal
+        next = *epoch + 1;
+    }
+    __syncthreads();
+    const int q = threadIdx.x;
+    if (q < world) {
+        st_release_sys(peer_flags[q] + rank, next);
+        int spins = 0;
+        while ((int32_t)(ld_acquire_sys(flags + q) - next) < 0) {
+            if (++spins > kBarrierSpinLimit) {
+                atomicExch(error, 1);
+                break;
+            }
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        *epoch = next;
+        __threadfence_system();
+    }
+}
+
+constexpr int kUnroll = 4;  // independent 16-byte chunks in flight per thread
+
+// Shard [begin, end) of the multicast buffer, in float4 chunks.
+__global__ void nvls_allreduce_kernel(float* mc, int64_t begin4, int64_t end4)
+{
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i = begin4 + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < end4;
+         i += stride * kUnroll) {
+        float4 v[kUnroll];
+#pragma unroll
+        for (int u = 0; u < kUnroll; u++)
+            if (i + u * stride < end4) v[u] = multimem_ld_reduce_add_v4(mc + (i + u * stride) * 4);
+#pragma unroll
+        for (int u = 0; u < kUnroll; u++)
+            if (i + u * stride < end4) multimem_st_v4(mc + (i + u * stride) * 4, v[u]);
+    }
+    // The stores precede the barrier that follows: one system-scope fence per
+    // block, cumulative over the block's stores through the block barrier.
+    __syncthreads();
+    if (threadIdx.x == 0) __threadfence_system();
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+}  // namespace
+}  // namespace gsb
+
+using namespace gsb;
+
+extern "C" int gsb_exchange_barrier(gsb_stream_t stream, const gsb_exchange_params* p,
+                                    uint32_t* const* peer_flags, const uint32_t* flags,
+                                    uint32_t* epoch, int32_t* error)
+{
+    if (!p) return GSB_ERR_NULL;
+    if (p->world < 1 || p->world > 1024 || p->rank < 0 || p->rank >= p->world)
+        return GSB_ERR_INVALID;
+    if (!peer_flags || !flags || !epoch || !error) return GSB_ERR_NULL;
+    exchange_barrier_kernel<<<1, ((p->world + 31) / 32) * 32, 0, as_stream(stream)>>>(
+        p->world, p->rank, peer_flags, flags, epoch, error);
+    return check_launch();
+}
+
+extern "C" int gsb_nvls_allreduce(gsb_stream_t stream, const gsb_exchange_params* p,
+                                  float* multicast, int64_t count)
+{
+    if (!p) return GSB_ERR_NULL;
+    if (p->world < 1 || p->rank < 0 || p->rank >= p->world || count < 0 || (count & 3) != 0)
+        return GSB_ERR_INVALID;
+    if (!multicast) return GSB_ERR_NULL;
+    if (!aligned16(multicast)) return GSB_ERR_INVALID;
+    const int64_t n4 = count / 4;
+    const int64_t per = (n4 + p->world - 1) / p->world;
+    const int64_t begin = per * p->rank, end = begin + per < n4 ? begin + per : n4;
+    if (begin >= end) return GSB_OK;
+    const int64_t want = (end - begin + 256 * kUnroll - 1) / (256 * kUnroll);
+    const int blocks = (int)(want < 148 * 8 ? want : 148 * 8);
+    nvls_allreduce_kernel<<<blocks, 256, 0, as_stream(stream)>>>(multicast, begin, end);
+    return check_launch();
+}

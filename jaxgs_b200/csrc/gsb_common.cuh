@@ -49,6 +49,26 @@ struct Carver {
 
 inline int ceil_div(int64_t a, int64_t b) { return (int)((a + b - 1) / b); }
 
+// NVLS multicast access (symmetric memory bound to a multicast object):
+// the switch sums one 16-byte chunk over every GPU's copy, or writes it to
+// every copy.
+__device__ __forceinline__ float4 multimem_ld_reduce_add_v4(const float* mc)
+{
+    float4 v;
+    asm volatile("multimem.ld_reduce.relaxed.sys.global.add.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "l"(mc)
+                 : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void multimem_st_v4(float* mc, float4 v)
+{
+    asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(mc),
+                 "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w)
+                 : "memory");
+}
+
 // ---------------------------------------------------------------------------
 // Explicitly rounded float32 arithmetic.  These never contract into a
 // neighbouring FMA, so the binning's fixed roundings are identical to the

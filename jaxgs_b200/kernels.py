@@ -147,12 +147,16 @@ def compute_projection_gradients(parameters, camera: DeviceCamera, projected_col
                                  active_degree: int | None, visible_clusters,
                                  compact_gradients: bool, rgb_only: bool = False,
                                  active_sh_only: bool = False, sh_color_only: bool = False,
-                                 out=None):
+                                 out=None, color_multicast=None):
     """kernels/projector.py:240-307: parameter gradients from cotangents.
 
     out: optional (xyz, log_scale, rotation, opacity, sh) gradient tensors to
     write (contiguous float32 of the output shapes), e.g. views of one flat
-    buffer that a collective reduces in place."""
+    buffer that a collective reduces in place.
+    color_multicast: (multicast address, row floats) of this rank's row of a
+    symmetric row table; the colour-only pool-order cotangents and the camera
+    centre are then stored there, into every GPU's copy
+    (gsb_project_bwd_colors_multicast), and out's sh entry is unused."""
     xyz, log_scale, rotation, opacity, sh = parameters
     _require_cuda(xyz, "projection pullback")
     C = config.max_gaussians
@@ -161,10 +165,14 @@ def compute_projection_gradients(parameters, camera: DeviceCamera, projected_col
     shg = 1 if sh_color_only else ((degree + 1) ** 2 if active_sh_only else sh_dim)
     dev = xyz.device
     shapes = ((C, 3), (C, 3), (C, 4), (C, 1), (C, shg, 3))
+    if color_multicast is not None:
+        if not (sh_color_only and visible_clusters is not None and not compact_gradients):
+            raise ValueError("color_multicast needs the colour-only, pool-order pullback")
+        shapes = shapes[:4]
     if out is None:
         out = [torch.empty(shape, dtype=_f32, device=dev) for shape in shapes]
     else:
-        out = list(out)
+        out = list(out)[:len(shapes)]
         for o, shape in zip(out, shapes):
             if tuple(o.shape) != shape or o.dtype != _f32 or not o.is_contiguous():
                 raise ValueError(f"gradient output must be contiguous float32 {shape}")
@@ -176,16 +184,23 @@ def compute_projection_gradients(parameters, camera: DeviceCamera, projected_col
     gdepth, gradius = cotangents.depth, cotangents.radius
     if rgb_only:
         gdepth = gradius = None
-    L.check(L.lib.gsb_project_bwd(
-        _stream(), L.ref(p), _ptr(_c(xyz, _f32)), _ptr(_c(log_scale, _f32)),
-        _ptr(_c(rotation, _f32)), _ptr(_c(opacity, _f32)), _ptr(_c(sh, _f32)),
-        _ptr(_c(camera.world_to_camera, _f32)), _ptr(_c(camera.intrinsics, _f32)),
-        _ptr(_c(camera.center, _f32)), _ptr(_c(projected_color, _f32)),
-        _ptr(None if ids is None else _c(ids, _i32)), _ptr(None if count is None else _c(count, _i32)),
-        _ptr(_c(cotangents.mean, _f32)), _ptr(None if gdepth is None else _c(gdepth, _f32)),
-        _ptr(_c(cotangents.conic, _f32)), _ptr(None if gradius is None else _c(gradius, _f32)),
-        _ptr(_c(cotangents.color, _f32)), _ptr(_c(cotangents.alpha, _f32)),
-        *[_ptr(o) for o in out]), "projection pullback")
+    args = (_stream(), L.ref(p), _ptr(_c(xyz, _f32)), _ptr(_c(log_scale, _f32)),
+            _ptr(_c(rotation, _f32)), _ptr(_c(opacity, _f32)), _ptr(_c(sh, _f32)),
+            _ptr(_c(camera.world_to_camera, _f32)), _ptr(_c(camera.intrinsics, _f32)),
+            _ptr(_c(camera.center, _f32)), _ptr(_c(projected_color, _f32)),
+            _ptr(None if ids is None else _c(ids, _i32)),
+            _ptr(None if count is None else _c(count, _i32)),
+            _ptr(_c(cotangents.mean, _f32)), _ptr(None if gdepth is None else _c(gdepth, _f32)),
+            _ptr(_c(cotangents.conic, _f32)), _ptr(None if gradius is None else _c(gradius, _f32)),
+            _ptr(_c(cotangents.color, _f32)), _ptr(_c(cotangents.alpha, _f32)),
+            *[_ptr(o) for o in out])
+    if color_multicast is not None:
+        address, row_floats = color_multicast
+        L.check(L.lib.gsb_project_bwd_colors_multicast(*args, ctypes.c_void_p(address),
+                                                       int(row_floats)),
+                "projection pullback (colour multicast)")
+        return tuple(out) + (None,)
+    L.check(L.lib.gsb_project_bwd(*args), "projection pullback")
     del zeros
     return tuple(out)
 
@@ -195,17 +210,19 @@ def sh_from_colors(xyz: torch.Tensor, centers: torch.Tensor, colors: torch.Tenso
     """training/sh_pullback.py:18-53 summed over views: SH coefficient
     cotangents [C, sh_dim, 3] from per-view masked colour cotangents (the
     sh_color_only pullback output of each view, pool order) and the views'
-    camera centres.  colors: [V, C, 3], or [V, >= C*3 + 3] rows holding a
-    view's C*3 cotangents followed by its centre (then centers is None)."""
+    camera centres.  colors: [V, C, 3], or [V, >= 4 + C*3] rows holding a
+    view's centre (3 floats and a pad) followed by its C*3 cotangents (then
+    centers is None)."""
     _require_cuda(xyz, "SH reconstruction")
     C = int(xyz.shape[0])
     views = int(colors.shape[0])
     if centers is None:
-        if colors.ndim != 2 or colors.shape[1] < C * 3 + 3 or not colors.is_contiguous():
-            raise ValueError("packed colour rows must be [V, >= C*3 + 3] contiguous")
+        if colors.ndim != 2 or colors.shape[1] < C * 3 + 4 or not colors.is_contiguous():
+            raise ValueError("packed colour rows must be [V, >= 4 + C*3] contiguous")
         row = int(colors.shape[1])
         p = L.ShParams(C, sh_dim, degree, views, row, row)
-        centers_ptr = colors.data_ptr() + C * 3 * 4
+        centers_ptr = colors.data_ptr()
+        colors_ptr = colors.data_ptr() + 4 * 4
     else:
         if tuple(colors.reshape(views, -1).shape) != (views, C * 3) or tuple(centers.shape) != (views, 3):
             raise ValueError("colors must be [V, C, 3] with centers [V, 3]")
@@ -213,10 +230,12 @@ def sh_from_colors(xyz: torch.Tensor, centers: torch.Tensor, colors: torch.Tenso
         colors = _c(colors, _f32)
         p = L.ShParams(C, sh_dim, degree, views, 0, 0)
         centers_ptr = centers.data_ptr()
+        colors_ptr = colors.data_ptr()
     if out is None:
         out = torch.empty(C, sh_dim, 3, dtype=_f32, device=xyz.device)
     L.check(L.lib.gsb_sh_from_colors(_stream(), L.ref(p), _ptr(_c(xyz, _f32)),
-                                     ctypes.c_void_p(centers_ptr), _ptr(colors), _ptr(out)),
+                                     ctypes.c_void_p(centers_ptr), ctypes.c_void_p(colors_ptr),
+                                     _ptr(out)),
             "SH reconstruction")
     return out
 
@@ -232,13 +251,15 @@ def project_with_compact_pullback(pool: GaussianArrays, camera: DeviceCamera,
     parameters = (pool.xyz, pool.log_scale, pool.rotation, pool.opacity, pool.sh)
     projected = _project(pool, camera, config, active_degree, clusters, False, visible_color_only)
 
-    def pullback(cotangents: ProjectedGaussians, out=None, compact: bool = True):
+    def pullback(cotangents: ProjectedGaussians, out=None, compact: bool = True,
+                 color_multicast=None):
         """Gradients in visible-cluster order, or (compact=False) in pool
-        order with the unlisted clusters' rows zeroed; out as in
-        compute_projection_gradients."""
+        order with the unlisted clusters' rows zeroed; out and
+        color_multicast as in compute_projection_gradients."""
         return compute_projection_gradients(parameters, camera, projected.color, cotangents,
                                             config, active_degree, clusters, compact, rgb_only,
-                                            active_sh_only, sh_color_only, out=out)
+                                            active_sh_only, sh_color_only, out=out,
+                                            color_multicast=color_multicast)
 
     return projected, pullback
 

@@ -56,7 +56,8 @@ def compute_training_step(pool: GaussianArrays, bounds, camera: DeviceCamera, ta
                           config: CapacityConfig, active_degree: int, *,
                           active_sh_only: bool = True, sh_color_only: bool = False,
                           keep_image: bool = False, stage_events: dict | None = None,
-                          overlap: bool = True, pool_grads=None) -> StepOutput:
+                          overlap: bool = True, pool_grads=None,
+                          color_multicast=None) -> StepOutput:
     """training/step.py:32-89 without the optimizer update.
 
     bounds: world cluster bounds (center, extent, valid) on the device.
@@ -72,6 +73,9 @@ def compute_training_step(pool: GaussianArrays, bounds, camera: DeviceCamera, ta
     pool_grads: optional (xyz, log_scale, rotation, opacity, sh) tensors; the
     gradients are then written there in pool order (rows of culled clusters
     zero), ready to be summed across view-sharded ranks in place.
+    color_multicast: with sh_color_only and pool_grads, the colour cotangents
+    (and the camera centre) go to this (multicast address, row floats) row
+    instead (NvlsExchange).
     """
     stream = torch.cuda.current_stream()
 
@@ -129,7 +133,8 @@ def compute_training_step(pool: GaussianArrays, bounds, camera: DeviceCamera, ta
     cot = K.rasterize_backward(projected, table, cache, drgb, camera, config, buffers=buffers)
     done(ev)
     ev = mark("project_bwd")
-    grads = pullback(cot) if pool_grads is None else pullback(cot, out=pool_grads, compact=False)
+    grads = (pullback(cot) if pool_grads is None else
+             pullback(cot, out=pool_grads, compact=False, color_multicast=color_multicast))
     done(ev)
     return StepOutput(loss, grads, clusters, table.pair_count, table.overflow,
                       table.point_counts, result.rgb if keep_image else None)
@@ -193,13 +198,14 @@ class ViewShardedExchange:
         for n, shape in ((C * 3, (C, 3)), (C * 3, (C, 3)), (C * 4, (C, 4)), (C, (C, 1))):
             views.append(self.geometric[at:at + n].view(shape))
             at += n
-        # [colour cotangents C*3 | camera centre 3 | pad 1] per rank.
-        self.row = torch.zeros(C * 3 + 4, dtype=torch.float32, device=dev)
-        self.colors = self.row[:C * 3].view(C, 1, 3)
-        self.center = self.row[C * 3:C * 3 + 3]
-        self.rows = torch.empty(self.world, C * 3 + 4, dtype=torch.float32, device=dev)
+        # [camera centre 3 | pad 1 | colour cotangents C*3] per rank.
+        self.row = torch.zeros(4 + C * 3, dtype=torch.float32, device=dev)
+        self.center = self.row[:3]
+        self.colors = self.row[4:].view(C, 1, 3)
+        self.rows = torch.empty(self.world, 4 + C * 3, dtype=torch.float32, device=dev)
         self.sh = torch.empty(C, self.sh_dim, 3, dtype=torch.float32, device=dev)
         self.pool_grads = (*views, self.colors)
+        self.step_kwargs = dict(pool_grads=self.pool_grads, sh_color_only=True)
 
     def exchange(self, camera_center: torch.Tensor):
         """Sum the ranks' gradients; returns (xyz, log_scale, rotation,
@@ -210,6 +216,120 @@ class ViewShardedExchange:
         K.sh_from_colors(self.xyz, None, self.rows, self.degree, self.sh_dim, out=self.sh)
         work.wait()
         return (*self.pool_grads[:4], self.sh)
+
+
+class NvlsExchange:
+    """ViewShardedExchange's sum with collectives written for NVLink /
+    NVSwitch multicast (include/gsb200.h, gsb_exchange_barrier,
+    gsb_nvls_allreduce, gsb_project_bwd_colors_multicast).
+
+    The geometric gradients live in symmetric memory.  The step's pullback
+    stores each rank's colour cotangents and camera centre straight into row
+    r of every GPU's copy of a symmetric row table (the all-gather is part of
+    the kernel that produces them).  exchange() then passes a cross-GPU
+    barrier, sums shard r of the geometric gradients in the switch
+    (multimem.ld_reduce) and stores the sum into every copy (multimem.st)
+    while a second stream expands the gathered colours into the summed SH
+    gradients, and passes a second barrier.  No NCCL call is made per step
+    and every launch can be captured in a CUDA graph.  Build it only when
+    NvlsExchange.available(group) says the GPUs share multicast.
+    """
+
+    @staticmethod
+    def available(group=None) -> bool:
+        try:
+            import torch.distributed as dist
+            import torch.distributed._symmetric_memory as symm_mem
+
+            probe = symm_mem.empty(4, dtype=torch.float32, device=torch.cuda.current_device())
+            handle = symm_mem.rendezvous(probe, group or dist.group.WORLD)
+            return int(handle.multicast_ptr) != 0
+        except Exception:
+            return False
+
+    def __init__(self, pool: GaussianArrays, config: CapacityConfig, active_degree: int,
+                 group=None, active_sh_only: bool = True):
+        import torch.distributed as dist
+        import torch.distributed._symmetric_memory as symm_mem
+
+        from . import _lib
+
+        self.L = _lib
+        group = group or dist.group.WORLD
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.degree = active_degree
+        self.sh_dim = (active_degree + 1) ** 2 if active_sh_only else int(pool.sh.shape[1])
+        self.xyz = pool.xyz
+        C = config.max_gaussians
+        dev = pool.xyz.device
+        self.params = _lib.ExchangeParams(self.world, self.rank)
+        self.geo_count = -(-(C * 11) // 4) * 4
+        self.geometric = symm_mem.empty(self.geo_count, dtype=torch.float32, device=dev)
+        # Row r = [camera centre 3 | pad 1 | colour cotangents C*3 | pad].
+        self.row_floats = 4 + -(-(C * 3) // 4) * 4
+        self.table = symm_mem.empty(self.world * self.row_floats, dtype=torch.float32, device=dev)
+        self.flags = symm_mem.empty(self.world, dtype=torch.int32, device=dev)
+        self.flags.zero_()
+        self.geometric.zero_()
+        self.table.zero_()
+        h_geo = symm_mem.rendezvous(self.geometric, group)
+        h_tab = symm_mem.rendezvous(self.table, group)
+        h_flags = symm_mem.rendezvous(self.flags, group)
+        if not (int(h_geo.multicast_ptr) and int(h_tab.multicast_ptr)):
+            raise RuntimeError("NVLS multicast is not available for this group")
+        self._handles = (h_geo, h_tab, h_flags)
+        self.mc_geo = int(h_geo.multicast_ptr)
+        self.mc_row = int(h_tab.multicast_ptr) + self.rank * self.row_floats * 4
+        self.peer_flags = torch.tensor(list(h_flags.buffer_ptrs), dtype=torch.int64, device=dev)
+        self.epoch = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.error = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.rows = self.table.view(self.world, self.row_floats)
+        self.sh = torch.empty(C, self.sh_dim, 3, dtype=torch.float32, device=dev)
+        at, views = 0, []
+        for n, shape in ((C * 3, (C, 3)), (C * 3, (C, 3)), (C * 4, (C, 4)), (C, (C, 1))):
+            views.append(self.geometric[at:at + n].view(shape))
+            at += n
+        self.pool_grads = (*views, None)
+        self.step_kwargs = dict(pool_grads=self.pool_grads, sh_color_only=True,
+                                color_multicast=(self.mc_row, self.row_floats))
+        self.side = torch.cuda.Stream(device=dev)
+        torch.cuda.synchronize(dev)
+        dist.barrier(group)
+
+    def _barrier(self):
+        import ctypes
+
+        L = self.L
+        L.check(L.lib.gsb_exchange_barrier(
+            ctypes.c_void_p(torch.cuda.current_stream().cuda_stream), L.ref(self.params),
+            ctypes.c_void_p(self.peer_flags.data_ptr()), ctypes.c_void_p(self.flags.data_ptr()),
+            ctypes.c_void_p(self.epoch.data_ptr()), ctypes.c_void_p(self.error.data_ptr())),
+            "exchange barrier")
+
+    def exchange(self, camera_center: torch.Tensor | None = None):
+        """Sum the ranks' gradients after a step run with step_kwargs;
+        returns (xyz, log_scale, rotation, opacity, sh) in pool order,
+        identical on every rank.  (The camera centre travels with the
+        colour row, so camera_center is not needed.)"""
+        import ctypes
+
+        L = self.L
+        main = torch.cuda.current_stream()
+        self._barrier()
+        self.side.wait_stream(main)
+        L.check(L.lib.gsb_nvls_allreduce(ctypes.c_void_p(main.cuda_stream), L.ref(self.params),
+                                         ctypes.c_void_p(self.mc_geo), self.geo_count),
+                "NVLS all-reduce")
+        with torch.cuda.stream(self.side):
+            K.sh_from_colors(self.xyz, None, self.rows, self.degree, self.sh_dim, out=self.sh)
+        main.wait_stream(self.side)
+        self._barrier()
+        return (*self.pool_grads[:4], self.sh)
+
+    def failed(self) -> bool:
+        """Did a barrier give up waiting for a peer (host read, synchronises)?"""
+        return bool(self.error.item())
 
 
 def scatter_compact(grads, clusters, config: CapacityConfig, out=None):
@@ -245,7 +365,8 @@ class GraphedTrainingStep:
 
     def __init__(self, pool: GaussianArrays, bounds, camera: DeviceCamera, target: torch.Tensor,
                  config: CapacityConfig, active_degree: int, *, active_sh_only: bool = True,
-                 sh_color_only: bool = False, warmup: int = 2, pool_grads=None):
+                 sh_color_only: bool = False, warmup: int = 2, pool_grads=None,
+                 color_multicast=None):
         dev = pool.xyz.device
         self.camera = DeviceCamera(camera.world_to_camera.clone(), camera.intrinsics.clone(),
                                    camera.center.clone(), camera.planes.clone(), camera.width,
@@ -254,7 +375,7 @@ class GraphedTrainingStep:
         self.target.copy_(target)
         args = (pool, bounds, self.camera, self.target, config, active_degree)
         kwargs = dict(active_sh_only=active_sh_only, sh_color_only=sh_color_only,
-                      pool_grads=pool_grads)
+                      pool_grads=pool_grads, color_multicast=color_multicast)
         side = torch.cuda.Stream(device=dev)
         side.wait_stream(torch.cuda.current_stream(dev))
         with torch.cuda.stream(side):

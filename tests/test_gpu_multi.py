@@ -1,6 +1,8 @@
-"""View-sharded step on two GPUs (one NCCL rank per GPU): the gradients that
-ViewShardedExchange leaves on every rank equal the single-process sum of the
-two views' full gradients.  Skipped with fewer than two GPUs."""
+"""View-sharded step on two GPUs (one rank per GPU): the gradients that the
+exchange (ViewShardedExchange over NCCL, or NvlsExchange with this library's
+NVLS multicast collectives) leaves on every rank equal the single-process
+sum of the two views' full gradients, over several steps in a row.  Skipped
+with fewer than two GPUs (NvlsExchange also without multicast support)."""
 
 import os
 import socket
@@ -30,12 +32,12 @@ def _setup(device):
     return pool, bounds, cams, torch.as_tensor(target, device=device), config
 
 
-def _rank(rank, world, port, path):
+def _rank(rank, world, port, path, kind):
     import datetime
 
     import torch.distributed as dist
 
-    from jaxgs_b200.step import GraphedTrainingStep, ViewShardedExchange
+    from jaxgs_b200.step import GraphedTrainingStep, NvlsExchange, ViewShardedExchange
 
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     torch.cuda.set_device(rank)
@@ -44,12 +46,19 @@ def _rank(rank, world, port, path):
                             timeout=datetime.timedelta(seconds=60), device_id=device)
     try:
         pool, bounds, cams, target, config = _setup(device)
-        exch = ViewShardedExchange(pool, config, 3)
+        if kind == "nvls" and not NvlsExchange.available():
+            if rank == 0:
+                np.savez(path, skipped=np.ones(1))
+            return
+        exch = (NvlsExchange if kind == "nvls" else ViewShardedExchange)(pool, config, 3)
         step = GraphedTrainingStep(pool, bounds, cams[rank], target, config, 3,
-                                   pool_grads=exch.pool_grads, sh_color_only=True)
-        step()
-        grads = exch.exchange(step.camera.center)
+                                   **exch.step_kwargs)
+        for _ in range(3):  # reused buffers: every step must give the same sum
+            step()
+            grads = exch.exchange(step.camera.center)
         torch.cuda.synchronize()
+        if kind == "nvls":
+            assert not exch.failed()
         if rank == 0:
             np.savez(path, *[g.cpu().numpy() for g in grads])
         dist.barrier()
@@ -59,7 +68,8 @@ def _rank(rank, world, port, path):
 
 
 @pytest.mark.timeout(600)
-def test_two_rank_view_sharded_gradients():
+@pytest.mark.parametrize("kind", ["nccl", "nvls"])
+def test_two_rank_view_sharded_gradients(kind):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     import torch.multiprocessing as mp
@@ -71,8 +81,11 @@ def test_two_rank_view_sharded_gradients():
         port = s.getsockname()[1]
     with tempfile.TemporaryDirectory() as tmp:
         path = os.path.join(tmp, "grads.npz")
-        mp.start_processes(_rank, args=(2, port, path), nprocs=2, join=True, start_method="spawn")
+        mp.start_processes(_rank, args=(2, port, path, kind), nprocs=2, join=True,
+                           start_method="spawn")
         got = np.load(path)
+        if "skipped" in got:
+            pytest.skip("no NVLS multicast between the GPUs")
         got = [got[f"arr_{i}"] for i in range(5)]
     pool, bounds, cams, target, config = _setup(torch.device("cuda", 0))
     expected = None
