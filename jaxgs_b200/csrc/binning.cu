@@ -155,10 +155,22 @@ __device__ __forceinline__ Splat load_splat(const float* mean, const float* coni
 }
 
 // sorted_visibility.py:178-224: sequential row walk; EMIT writes the pairs.
+// Per-block digit histograms of the emitted tile keys (the tile sort's
+// per-pass histograms), accumulated in shared memory during emission.
+struct KeyHist {
+    uint32_t* local;  // [passes][256] in shared memory, or nullptr
+    int passes, bits;
+    __device__ __forceinline__ void add(uint32_t key) const
+    {
+        for (int pass = 0; pass < passes; pass++)
+            atomicAdd(local + pass * 256 + ((key >> (pass * bits)) & ((1u << bits) - 1)), 1u);
+    }
+};
+
 template <bool EMIT, typename K>
 __device__ int32_t process_tiles(const Splat& s, int tile_w, int tile_h, int tiles_x, int tiles_y,
                                  int32_t gid, int64_t offset, int64_t max_pairs, K* keys,
-                                 int32_t* values)
+                                 int32_t* values, KeyHist hist = KeyHist{nullptr, 0, 0})
 {
     Ellipse e = ellipse_bounds(s.px, s.py, s.c00, s.c01, s.c11, s.alpha, tile_w, tile_h, tiles_x,
                                tiles_y);
@@ -181,8 +193,10 @@ __device__ int32_t process_tiles(const Splat& s, int tile_w, int tile_h, int til
                 for (int32_t v = first; v < end; v++) {
                     int64_t slot = offset + count + v - first;
                     if (slot < max_pairs) {
-                        keys[slot] = (K)tile_key(e.is_y, u, v, tiles_x);
+                        const uint32_t key = tile_key(e.is_y, u, v, tiles_x);
+                        keys[slot] = (K)key;
                         values[slot] = gid;
+                        if (hist.local) hist.add(key);
                     }
                 }
             }
@@ -536,6 +550,18 @@ __global__ void zero_u32_kernel(uint32_t* p, int64_t n)
         p[i] = 0;
 }
 
+// Zeroes up to three word ranges in one launch.
+__global__ void zero_ranges_kernel(uint32_t* a, int64_t na, uint32_t* b, int64_t nb, uint32_t* c,
+                                   int64_t nc)
+{
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < na + nb + nc; i += stride) {
+        if (i < na) a[i] = 0;
+        else if (i < na + nb) b[i - na] = 0;
+        else c[i - na - nb] = 0;
+    }
+}
+
 // Sort scratch: histograms [4][256], status [4][partitions][256], counters.
 struct SortScratch {
     uint32_t* hist;
@@ -546,10 +572,14 @@ struct SortScratch {
 
 // Histograms, look-back status words and partition counters are one
 // contiguous region, zeroed by one launch.
+int64_t sort_scratch_words(const SortScratch& w)
+{
+    return 4 * kMaxRadix + 4 * (int64_t)w.partitions * kMaxRadix + 8;
+}
+
 int zero_sort_scratch(cudaStream_t s, const SortScratch& w)
 {
-    const int64_t words = 4 * kMaxRadix + 4 * (int64_t)w.partitions * kMaxRadix + 8;
-    zero_u32_kernel<<<256, 256, 0, s>>>(w.hist, words);
+    zero_u32_kernel<<<256, 256, 0, s>>>(w.hist, sort_scratch_words(w));
     return check_launch();
 }
 
@@ -681,6 +711,18 @@ __global__ void __launch_bounds__(kScanThreads) scan_kernel(
 // ---------------------------------------------------------------------------
 constexpr int kLanePairs = 16;
 
+// Adds the block's digit counts to the tile sort's global histograms
+// (hist[pass * 256 + digit], the layout onesweep_sort reads).
+__device__ __forceinline__ void flush_key_hist(const uint32_t* local, int passes,
+                                               uint32_t* key_hist)
+{
+    __syncthreads();
+    for (int i = threadIdx.x; i < passes * 256; i += blockDim.x) {
+        const uint32_t c = local[i];
+        if (c) atomicAdd(key_hist + i, c);
+    }
+}
+
 template <typename K>
 __global__ void __launch_bounds__(256) emit_kernel(
     const int32_t* __restrict__ order, const int32_t* __restrict__ counts,
@@ -688,8 +730,12 @@ __global__ void __launch_bounds__(256) emit_kernel(
     const float* __restrict__ mean, const float* __restrict__ conic,
     const float* __restrict__ alpha, gsb_bin_params p, int tiles_x, int tiles_y,
     K* __restrict__ keys, int32_t* __restrict__ values, int32_t* __restrict__ queue,
-    int32_t* __restrict__ queue_count)
+    int32_t* __restrict__ queue_count, int passes, int bits, uint32_t* __restrict__ key_hist)
 {
+    __shared__ uint32_t local[4 * 256];
+    for (int i = threadIdx.x; i < passes * 256; i += blockDim.x) local[i] = 0;
+    __syncthreads();
+    const KeyHist hist{local, passes, bits};
     int64_t n = read_count(n_ptr, n_cap);
     int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     int32_t count = 0, gid = 0;
@@ -702,7 +748,7 @@ __global__ void __launch_bounds__(256) emit_kernel(
     if (count > 0 && count <= kLanePairs && offset < p.max_pairs) {
         Splat s = load_splat(mean, conic, alpha, gid);
         process_tiles<true, K>(s, p.tile_w, p.tile_h, tiles_x, tiles_y, gid, offset, p.max_pairs,
-                               keys, values);
+                               keys, values, hist);
     }
     bool large = count > kLanePairs && offset < p.max_pairs;
     unsigned queued = __ballot_sync(GSB_FULL_MASK, large);
@@ -714,6 +760,7 @@ __global__ void __launch_bounds__(256) emit_kernel(
         first = __shfl_sync(GSB_FULL_MASK, first, leader);
         if (large) queue[first + __popc(queued & lanemask_lt())] = (int32_t)r;
     }
+    flush_key_hist(local, passes, key_hist);
 }
 
 // One warp per queued Gaussian: lanes take 32 rows at a time, then write the
@@ -725,8 +772,13 @@ __global__ void __launch_bounds__(256) emit_large_kernel(
     const int32_t* __restrict__ order, const int32_t* __restrict__ counts,
     const int64_t* __restrict__ ends, const float* __restrict__ mean,
     const float* __restrict__ conic, const float* __restrict__ alpha, gsb_bin_params p,
-    int tiles_x, int tiles_y, K* __restrict__ keys, int32_t* __restrict__ values)
+    int tiles_x, int tiles_y, K* __restrict__ keys, int32_t* __restrict__ values, int passes,
+    int bits, uint32_t* __restrict__ key_hist)
 {
+    __shared__ uint32_t local[4 * 256];
+    for (int i = threadIdx.x; i < passes * 256; i += blockDim.x) local[i] = 0;
+    __syncthreads();
+    const KeyHist hist{local, passes, bits};
     int lane = threadIdx.x & 31;
     int warps = gridDim.x * (blockDim.x / 32);
     int total = *queue_count;
@@ -761,14 +813,17 @@ __global__ void __launch_bounds__(256) emit_large_kernel(
                 int32_t row_before = __shfl_sync(GSB_FULL_MASK, before, row);
                 int64_t slot = offset + pair;
                 if (pair < rows_total && slot < p.max_pairs) {
-                    keys[slot] = (K)tile_key(e.is_y, base + row, row_first + pair - row_before,
-                                             tiles_x);
+                    const uint32_t key =
+                        tile_key(e.is_y, base + row, row_first + pair - row_before, tiles_x);
+                    keys[slot] = (K)key;
                     values[slot] = gid;
+                    hist.add(key);
                 }
             }
             offset += rows_total;
         }
     }
+    flush_key_hist(local, passes, key_hist);
 }
 
 // ---------------------------------------------------------------------------
@@ -795,12 +850,6 @@ __global__ void ranges_kernel(const K* __restrict__ keys, const int32_t* n_ptr, 
         if (current > num_tiles) current = num_tiles;
         for (int64_t t = previous + 1; t <= current; t++) offsets[t] = (int32_t)i;
     }
-}
-
-__global__ void zero_i32_kernel(int32_t* p, int n)
-{
-    int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i < n) p[i] = 0;
 }
 
 // digit_plan, kernels/pair_sort.py:33-37.
@@ -873,23 +922,26 @@ int tile_stage(cudaStream_t s, const gsb_bin_params& p, const BinLayout& L, int 
     K* emit_keys = static_cast<K*>(L.emit_keys);
     const int32_t* n_binned = L.scalars + 0;
     int64_t C = p.capacity;
-    emit_kernel<K><<<ceil_div(C, 256), 256, 0, s>>>(order, point_counts, L.ends, n_binned, C, mean,
-                                                    conic, alpha, p, tiles_x, tiles_y, emit_keys,
-                                                    L.emit_ids, L.queue, L.scalars + 1);
+    int passes, bits;
+    digit_plan(num_tiles, passes, bits);
+    // The emission kernels also accumulate the tile sort's digit histograms
+    // (its scratch was zeroed at the start of gsb_bin).
+    emit_kernel<K><<<ceil_div(C > 0 ? C : 1, 256), 256, 0, s>>>(
+        order, point_counts, L.ends, n_binned, C, mean, conic, alpha, p, tiles_x, tiles_y,
+        emit_keys, L.emit_ids, L.queue, L.scalars + 1, passes, bits, L.pair_sort.hist);
     if (int e = check_launch()) return e;
     emit_large_kernel<K><<<148 * 8, 256, 0, s>>>(L.queue, L.scalars + 1, order, point_counts,
                                                  L.ends, mean, conic, alpha, p, tiles_x, tiles_y,
-                                                 emit_keys, L.emit_ids);
+                                                 emit_keys, L.emit_ids, passes, bits,
+                                                 L.pair_sort.hist);
     if (int e = check_launch()) return e;
-    int passes, bits;
-    digit_plan(num_tiles, passes, bits);
     const K* sorted_keys = nullptr;
     const int32_t* sorted_ids = nullptr;
     if (int e = onesweep_sort<K>(s, emit_keys, L.emit_ids, static_cast<K*>(L.pair_keys_a),
                                  static_cast<K*>(L.pair_keys_b), L.pair_ids_a, L.pair_ids_b,
                                  gaussian_ids, &sorted_keys, &sorted_ids, L.scalars + 2,
                                  p.max_pairs, passes, bits, false, L.pair_sort, nullptr,
-                                 L.scalars + 3, false))
+                                 L.scalars + 3, true))
         return e;
     ranges_kernel<K><<<1024, 256, 0, s>>>(sorted_keys, L.scalars + 2, p.max_pairs, (int)num_tiles,
                                           tile_offsets, L.scalars + 3, overflow);
@@ -941,13 +993,15 @@ extern "C" int gsb_bin(gsb_stream_t stream, const gsb_bin_params* p, void* works
     cudaStream_t s = as_stream(stream);
     size_t used = 0;
     BinLayout L = carve_bin(static_cast<char*>(workspace), *p, used);
-    zero_i32_kernel<<<1, 32, 0, s>>>(L.scalars, 8);
+    // Scalars, the depth sort's and the tile sort's scratch: one launch.
+    zero_ranges_kernel<<<296, 256, 0, s>>>(reinterpret_cast<uint32_t*>(L.scalars), 8,
+                                           L.depth_sort.hist, sort_scratch_words(L.depth_sort),
+                                           L.pair_sort.hist, sort_scratch_words(L.pair_sort));
     if (int e = check_launch()) return e;
     int64_t C = p->capacity;
     const uint32_t* sorted_depth_keys = nullptr;
     const int32_t* depth_order = L.order_a;
     if (C > 0) {
-        if (int e = zero_sort_scratch(s, L.depth_sort)) return e;
         count_kernel<<<ceil_div(C, 256), 256, 0, s>>>((int)C, mean, conic, alpha, depth, visible,
                                                       *p, tiles_x, tiles_y, point_counts,
                                                       L.depth_keys, L.depth_sort.hist);

@@ -754,7 +754,6 @@ extern "C" int gsb_project_bwd(gsb_stream_t stream, const gsb_project_bwd_params
          reinterpret_cast<uintptr_t>(grotation) | reinterpret_cast<uintptr_t>(gmean)) & 15)
         return GSB_ERR_INVALID;
     cudaStream_t s = as_stream(stream);
-    int shg = p->sh_gradient_dim * 3;
     int blocks = ceil_div(p->capacity, kProjThreads);
 #define GSB_PROJ_BWD(D, M)                                                                        \
     project_bwd_kernel<D, M><<<blocks, kProjThreads, 0, s>>>(                                     \
