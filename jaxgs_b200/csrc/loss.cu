@@ -328,9 +328,22 @@ __global__ void __launch_bounds__(1024) loss_finish_kernel(int blocks, float inv
     __shared__ uint32_t pscale[32];
     double s = 0.0;
     uint32_t m = 0;
-    for (int b = threadIdx.x; b < blocks; b += blockDim.x) {
-        s += (double)block_loss[b];
-        m = max(m, block_scale[b]);
+    // Eight loads per thread in flight before they are summed (fixed order).
+    constexpr int kBatch = 8;
+    for (int base = threadIdx.x; base < blocks; base += blockDim.x * kBatch) {
+        float lv[kBatch];
+        uint32_t sv[kBatch];
+#pragma unroll
+        for (int k = 0; k < kBatch; k++) {
+            const int b = base + k * (int)blockDim.x;
+            lv[k] = b < blocks ? block_loss[b] : 0.0f;
+            sv[k] = b < blocks ? block_scale[b] : 0u;
+        }
+#pragma unroll
+        for (int k = 0; k < kBatch; k++) {
+            s += (double)lv[k];
+            m = max(m, sv[k]);
+        }
     }
     s = warp_sum(s);
 #pragma unroll

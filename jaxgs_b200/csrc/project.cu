@@ -59,6 +59,32 @@ __device__ __forceinline__ bool cluster_listed(const int32_t* ids, int count, in
     return lo < count && __ldg(ids + lo) == c;
 }
 
+// cluster_listed for a whole warp: when all lanes ask about the same
+// cluster, the warp narrows the search 32-way per round (3 rounds of loads
+// for 8k clusters instead of 13 dependent ones); otherwise each lane
+// searches alone.  Every lane of the warp must call it.
+__device__ __forceinline__ bool cluster_listed_warp(const int32_t* ids, int count, int64_t c)
+{
+    const int lane = threadIdx.x & 31;
+    const int64_t c0 = __shfl_sync(GSB_FULL_MASK, c, 0);
+    if (!__all_sync(GSB_FULL_MASK, c == c0)) return cluster_listed(ids, count, c);
+    int lo = 0, hi = count;  // lower bound of c0 lies in [lo, hi]
+    while (hi - lo > 32) {
+        const int step = (hi - lo + 31) / 32;
+        const int pos = lo + lane * step;
+        const bool below = pos < hi && __ldg(ids + pos) < c0;
+        const int k = __popc(__ballot_sync(GSB_FULL_MASK, below));  // lanes 0..k-1 below
+        const int new_lo = k > 0 ? lo + (k - 1) * step + 1 : lo;
+        const int new_hi = k < 32 && lo + k * step < hi ? lo + k * step : hi;
+        lo = new_lo;
+        hi = new_hi;
+    }
+    const int pos = lo + lane;
+    const bool below = pos < hi && __ldg(ids + pos) < c0;
+    const int first = lo + __popc(__ballot_sync(GSB_FULL_MASK, below));
+    return first < count && __ldg(ids + first) == c0;
+}
+
 // SH basis values (LiteGS/3DGS real SH order, reference/sh.py:8-36).
 template <int DEGREE>
 __device__ __forceinline__ void sh_basis(float dx, float dy, float dz, float b[16])
@@ -185,9 +211,25 @@ __global__ void __launch_bounds__(kProjThreads) project_fwd_kernel(
 {
     constexpr int NC = (DEGREE + 1) * (DEGREE + 1) * 3;
     int count = p.compacted ? __ldg(cluster_count) : 0;
-    int64_t i = (int64_t)blockIdx.x * kProjThreads + threadIdx.x;
-    int64_t g = slot_of(i, p.capacity, cluster_ids, count, p.cluster_size, p.compacted);
-    if (g < 0) return;
+    // One thread per pool slot.  With a cluster list, slots of unlisted
+    // clusters are cleared here (kernels/projection.py:178-210: visible = 0,
+    // and with clear_invisible every field), so no separate clear pass runs.
+    const int64_t g = (int64_t)blockIdx.x * kProjThreads + threadIdx.x;
+    const bool listed = !p.compacted ||
+        cluster_listed_warp(cluster_ids, count, (g < p.capacity ? g : p.capacity - 1) / p.cluster_size);
+    if (g >= p.capacity) return;
+    if (!listed) {
+        out_visible[g] = 0;
+        if (p.clear_invisible) {
+            *reinterpret_cast<float2*>(out_mean + g * 2) = make_float2(0.f, 0.f);
+            *reinterpret_cast<float4*>(out_conic + g * 4) = make_float4(0.f, 0.f, 0.f, 0.f);
+            out_color[g * 3] = out_color[g * 3 + 1] = out_color[g * 3 + 2] = 0.0f;
+            out_depth[g] = __int_as_float(0x7f800000);
+            out_radius[g] = 0.0f;
+            out_alpha[g] = 0.0f;
+        }
+        return;
+    }
     const int row = p.sh_dim * 3;
     const bool vec = (row & 3) == 0 && (reinterpret_cast<uintptr_t>(sh) & 15) == 0;
     Cam cam;
@@ -241,23 +283,6 @@ __global__ void __launch_bounds__(kProjThreads) project_fwd_kernel(
     out_color[g * 3 + 2] = rgb[2];
 }
 
-// kernels/projection.py:178-201 (_clear_projected) / :204-210 (_clear_visible).
-__global__ void clear_projected_kernel(int64_t capacity, int clear_all, float* mean, float* depth,
-                                       float* conic, float* radius, float* color, float* alpha,
-                                       int8_t* visible)
-{
-    int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= capacity) return;
-    visible[i] = 0;
-    if (!clear_all) return;
-    *reinterpret_cast<float2*>(mean + i * 2) = make_float2(0.f, 0.f);
-    *reinterpret_cast<float4*>(conic + i * 4) = make_float4(0.f, 0.f, 0.f, 0.f);
-    color[i * 3] = color[i * 3 + 1] = color[i * 3 + 2] = 0.0f;
-    depth[i] = __int_as_float(0x7f800000);
-    radius[i] = 0.0f;
-    alpha[i] = 0.0f;
-}
-
 // ---------------------------------------------------------------------------
 // Pullback: kernels/projection_backward.py:42-367.
 // SH_MODE: 0 = all sh_gradient_dim coefficients (bands above DEGREE zero),
@@ -288,9 +313,10 @@ __device__ __forceinline__ void project_bwd_body(
     int64_t g;
     bool listed = true;
     if (pool_order) {
+        listed = cluster_listed_warp(cluster_ids, count,
+                                     (i < p.capacity ? i : p.capacity - 1) / p.cluster_size);
         if (i >= p.capacity) return;
         g = i;
-        listed = cluster_listed(cluster_ids, count, g / p.cluster_size);
     } else {
         g = slot_of(i, p.capacity, cluster_ids, count, p.cluster_size, p.compacted);
         if (g < 0) return;
@@ -621,11 +647,15 @@ __global__ void __launch_bounds__(kProjThreads) sh_from_colors_kernel(
 
 // ---------------------------------------------------------------------------
 // Cluster frustum test + stable compaction (scene/cluster.py:40-67,
-// kernels/cluster_compact.py:31-44).  One block of 1024 threads handles up to
-// 1024 clusters per chunk with a block scan, so the ids come out in ascending
-// order without atomics.
+// kernels/cluster_compact.py:31-44).  One block of 1024 threads per round of
+// 8192 clusters: the tests read the bounds coalesced (cluster j*1024 + t) and
+// leave one visibility byte per cluster in shared memory; then thread t
+// takes clusters 8t..8t+7, and one block scan of the per-thread counts
+// writes the ids in ascending order without atomics.
 // ---------------------------------------------------------------------------
 constexpr int kClusterThreads = 1024;
+constexpr int kClustersPerThread = 8;
+constexpr int kClusterRound = kClusterThreads * kClustersPerThread;
 
 __global__ void __launch_bounds__(kClusterThreads) cluster_compact_kernel(
     int num_clusters, const float* __restrict__ center, const float* __restrict__ extent,
@@ -635,38 +665,64 @@ __global__ void __launch_bounds__(kClusterThreads) cluster_compact_kernel(
     __shared__ float pl[24];
     __shared__ int warp_totals[32];
     __shared__ int running;
+    __shared__ __align__(8) uint8_t vis_s[kClusterRound];
     if (threadIdx.x < 24) pl[threadIdx.x] = planes[threadIdx.x];
     if (threadIdx.x == 0) running = 0;
     __syncthreads();
-    int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    for (int base = 0; base < num_clusters; base += kClusterThreads) {
-        int c = base + threadIdx.x;
-        int vis = 0;
-        if (c < num_clusters) {
-            vis = valid[c] != 0;
-            float cx = center[c * 3], cy = center[c * 3 + 1], cz = center[c * 3 + 2];
-            float ex = extent[c * 3], ey = extent[c * 3 + 1], ez = extent[c * 3 + 2];
-            for (int k = 0; k < 6 && vis; k++) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    for (int base = 0; base < num_clusters; base += kClusterRound) {
+        // All eight clusters' bounds are loaded before any test, so their
+        // memory latencies overlap.
+        float b[kClustersPerThread][6];
+        int ok[kClustersPerThread];
+#pragma unroll
+        for (int j = 0; j < kClustersPerThread; j++) {
+            const int c = base + j * kClusterThreads + threadIdx.x;
+            ok[j] = c < num_clusters ? valid[c] != 0 : 0;
+#pragma unroll
+            for (int k = 0; k < 3; k++) {
+                b[j][k] = c < num_clusters ? center[c * 3 + k] : 0.0f;
+                b[j][3 + k] = c < num_clusters ? extent[c * 3 + k] : 0.0f;
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < kClustersPerThread; j++) {
+            const int local = j * kClusterThreads + threadIdx.x;
+            const int c = base + local;
+            int vis = ok[j];
+#pragma unroll
+            for (int k = 0; k < 6; k++) {
                 const float* q = pl + k * 4;
-                float dist = cx * q[0] + cy * q[1] + cz * q[2] + q[3];
-                float rad = ex * fabsf(q[0]) + ey * fabsf(q[1]) + ez * fabsf(q[2]);
+                const float dist = b[j][0] * q[0] + b[j][1] * q[1] + b[j][2] * q[2] + q[3];
+                const float rad = b[j][3] * fabsf(q[0]) + b[j][4] * fabsf(q[1]) + b[j][5] * fabsf(q[2]);
                 if (!(dist + rad >= 0.0f)) vis = 0;
             }
-            cluster_vis[c] = (uint8_t)vis;
+            if (c < num_clusters) cluster_vis[c] = (uint8_t)vis;
+            vis_s[local] = (uint8_t)vis;
         }
-        unsigned ballot = __ballot_sync(GSB_FULL_MASK, vis);
-        if (lane == 0) warp_totals[warp] = __popc(ballot);
+        __syncthreads();
+        const uint2 packed = reinterpret_cast<const uint2*>(vis_s)[threadIdx.x];
+        unsigned bits = 0;
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            bits |= ((packed.x >> (8 * j)) & 1u) << j;
+            bits |= ((packed.y >> (8 * j)) & 1u) << (j + 4);
+        }
+        const int first = base + threadIdx.x * kClustersPerThread;
+        const int cnt = __popc(bits);
+        const int inc = warp_inclusive_scan(cnt, lane);
+        if (lane == 31) warp_totals[warp] = inc;
         __syncthreads();
         if (warp == 0) {
-            int t = warp_totals[lane];
-            int inc = warp_inclusive_scan(t, lane);
-            warp_totals[lane] = inc - t;
+            const int t = warp_totals[lane];
+            warp_totals[lane] = warp_inclusive_scan(t, lane) - t;
         }
         __syncthreads();
-        int pos = running + warp_totals[warp] + __popc(ballot & lanemask_lt());
-        if (vis) ids[pos] = c;
+        int pos = running + warp_totals[warp] + inc - cnt;
+        for (int j = 0; j < kClustersPerThread; j++)
+            if ((bits >> j) & 1u) ids[pos++] = first + j;
         __syncthreads();
-        if (threadIdx.x == kClusterThreads - 1) running = pos + vis;
+        if (threadIdx.x == kClusterThreads - 1) running = pos;
         __syncthreads();
     }
     if (threadIdx.x == 0) *count_out = running;
@@ -705,11 +761,6 @@ extern "C" int gsb_project_fwd(gsb_stream_t stream, const gsb_project_params* p,
     if ((reinterpret_cast<uintptr_t>(rotation) | reinterpret_cast<uintptr_t>(conic)) & 15)
         return GSB_ERR_INVALID;
     cudaStream_t s = as_stream(stream);
-    if (p->compacted) {
-        clear_projected_kernel<<<ceil_div(p->capacity, 256), 256, 0, s>>>(
-            p->capacity, p->clear_invisible, mean, depth, conic, radius, color, alpha, visible);
-        if (int e = check_launch()) return e;
-    }
     int blocks = ceil_div(p->capacity, kProjThreads);
 #define GSB_PROJ_FWD(D)                                                                          \
     project_fwd_kernel<D><<<blocks, kProjThreads, 0, s>>>(                                       \

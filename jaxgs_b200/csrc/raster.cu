@@ -82,17 +82,43 @@ __device__ __forceinline__ int work_bucket(int64_t work)
     return kOrderBuckets - 1 - b;
 }
 
+// Tiles are taken 8 per thread per round (round r, thread t: tiles
+// r*8192 + j*1024 + t); a round's loads are issued before its atomics so
+// their latencies overlap, and one round's buckets stay in registers for the
+// scatter (larger images reload theirs).
+constexpr int kOrderPerThread = 8;
+
+__device__ __forceinline__ void order_round_buckets(const int32_t* __restrict__ work, int tiles,
+                                                    int from_offsets, int round, int bucket[])
+{
+    int64_t w[kOrderPerThread];
+#pragma unroll
+    for (int j = 0; j < kOrderPerThread; j++) {
+        const int t = round * kOrderThreads * kOrderPerThread + j * kOrderThreads + threadIdx.x;
+        w[j] = t < tiles ? (from_offsets ? (int64_t)work[t + 1] - work[t] : (int64_t)work[t]) : 0;
+    }
+#pragma unroll
+    for (int j = 0; j < kOrderPerThread; j++) {
+        const int t = round * kOrderThreads * kOrderPerThread + j * kOrderThreads + threadIdx.x;
+        bucket[j] = t < tiles ? work_bucket(w[j]) : -1;
+    }
+}
+
 __global__ void __launch_bounds__(kOrderThreads) order_tiles_kernel(const int32_t* __restrict__ work,
                                                                     int tiles, int from_offsets,
                                                                     int32_t* __restrict__ order)
 {
     __shared__ int starts[kOrderBuckets];
-    int tid = threadIdx.x;
+    const int tid = threadIdx.x;
+    const int rounds = (tiles + kOrderThreads * kOrderPerThread - 1) / (kOrderThreads * kOrderPerThread);
     if (tid < kOrderBuckets) starts[tid] = 0;
     __syncthreads();
-    for (int t = tid; t < tiles; t += kOrderThreads) {
-        int64_t w = from_offsets ? (int64_t)work[t + 1] - work[t] : work[t];
-        atomicAdd(&starts[work_bucket(w)], 1);
+    int bucket[kOrderPerThread];
+    for (int r = 0; r < rounds; r++) {
+        order_round_buckets(work, tiles, from_offsets, r, bucket);
+#pragma unroll
+        for (int j = 0; j < kOrderPerThread; j++)
+            if (bucket[j] >= 0) atomicAdd(&starts[bucket[j]], 1);
     }
     __syncthreads();
     if (tid < 32) {
@@ -108,10 +134,14 @@ __global__ void __launch_bounds__(kOrderThreads) order_tiles_kernel(const int32_
         }
     }
     __syncthreads();
-    for (int t = tid; t < tiles; t += kOrderThreads) {
-        int64_t w = from_offsets ? (int64_t)work[t + 1] - work[t] : work[t];
-        int pos = atomicAdd(&starts[work_bucket(w)], 1);
-        order[pos] = t;
+    for (int r = 0; r < rounds; r++) {
+        if (rounds > 1) order_round_buckets(work, tiles, from_offsets, r, bucket);
+#pragma unroll
+        for (int j = 0; j < kOrderPerThread; j++) {
+            if (bucket[j] < 0) continue;
+            const int t = r * kOrderThreads * kOrderPerThread + j * kOrderThreads + tid;
+            order[atomicAdd(&starts[bucket[j]], 1)] = t;
+        }
     }
 }
 
