@@ -270,6 +270,7 @@ __global__ void __launch_bounds__(256) count_kernel(int capacity, const float* _
                                                     uint32_t* __restrict__ keys,
                                                     uint32_t* __restrict__ depth_hist)
 {
+    pdl_begin();
     __shared__ uint32_t hist[4][256];
     for (int i = threadIdx.x; i < 4 * 256; i += blockDim.x) (&hist[0][0])[i] = 0;
     __syncthreads();
@@ -367,6 +368,7 @@ __global__ void __launch_bounds__(kSortThreads) onesweep_hist_kernel(
     const K* __restrict__ keys, const int32_t* n_ptr, int64_t n_cap, int passes, int bits,
     bool drop_sentinel, uint32_t* __restrict__ hist)
 {
+    pdl_begin();
     __shared__ uint32_t local[4][kMaxRadix];
     const int64_t n = read_count(n_ptr, n_cap);
     const int radix = 1 << bits;
@@ -411,6 +413,7 @@ __global__ void __launch_bounds__(kSortThreads) onesweep_pass_kernel(
     bool drop_sentinel, const uint32_t* __restrict__ pass_hist, uint32_t* status,
     int32_t* part_counter, int32_t* n_out, int32_t* error)
 {
+    pdl_begin();
     __shared__ uint32_t warp_hist[kSortWarps][kMaxRadix + 1];
     __shared__ uint32_t global_off[kMaxRadix];
     __shared__ uint32_t block_start[kMaxRadix];
@@ -545,6 +548,7 @@ __global__ void __launch_bounds__(kSortThreads) onesweep_pass_kernel(
 
 __global__ void zero_u32_kernel(uint32_t* p, int64_t n)
 {
+    pdl_begin();
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
          i += (int64_t)gridDim.x * blockDim.x)
         p[i] = 0;
@@ -554,6 +558,7 @@ __global__ void zero_u32_kernel(uint32_t* p, int64_t n)
 __global__ void zero_ranges_kernel(uint32_t* a, int64_t na, uint32_t* b, int64_t nb, uint32_t* c,
                                    int64_t nc)
 {
+    pdl_begin();
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < na + nb + nc; i += stride) {
         if (i < na) a[i] = 0;
@@ -579,7 +584,7 @@ int64_t sort_scratch_words(const SortScratch& w)
 
 int zero_sort_scratch(cudaStream_t s, const SortScratch& w)
 {
-    zero_u32_kernel<<<256, 256, 0, s>>>(w.hist, sort_scratch_words(w));
+    gsb::launch(zero_u32_kernel, 256, 256, 0, s, w.hist, sort_scratch_words(w));
     return check_launch();
 }
 
@@ -594,7 +599,7 @@ int onesweep_sort(cudaStream_t s, const K* keys_in, const int32_t* vals_in, K* k
 {
     if (!hist_ready) {
         if (int e = zero_sort_scratch(s, w)) return e;
-        onesweep_hist_kernel<K><<<148 * 4, kSortThreads, 0, s>>>(keys_in, n_ptr, n_cap, passes,
+        gsb::launch(onesweep_hist_kernel<K>, 148 * 4, kSortThreads, 0, s, keys_in, n_ptr, n_cap, passes,
                                                                  bits, drop_sentinel, w.hist);
         if (int e = check_launch()) return e;
     }
@@ -605,7 +610,7 @@ int onesweep_sort(cudaStream_t s, const K* keys_in, const int32_t* vals_in, K* k
         const bool last = pass == passes - 1;
         K* dst_k = (src_k == key_a) ? key_b : key_a;
         int32_t* dst_v = (last && val_out) ? val_out : ((src_v == val_a) ? val_b : val_a);
-        onesweep_pass_kernel<K><<<w.partitions, kSortThreads, 0, s>>>(
+        gsb::launch(onesweep_pass_kernel<K>, w.partitions, kSortThreads, 0, s, 
             src_k, src_v, dst_k, dst_v, pass_n, n_cap, pass * bits, bits, drop_sentinel && pass == 0,
             w.hist + pass * kMaxRadix, w.status + (int64_t)pass * w.partitions * kMaxRadix,
             w.counters + pass, (pass == 0 && drop_sentinel) ? n_out : nullptr, error);
@@ -643,6 +648,7 @@ __global__ void __launch_bounds__(kScanThreads) scan_reduce_kernel(
     const int32_t* __restrict__ order, const int32_t* __restrict__ counts, const int32_t* n_ptr,
     int64_t n_cap, int64_t* __restrict__ block_sums)
 {
+    pdl_begin();
     __shared__ int64_t shared[kScanThreads / 32];
     int64_t n = read_count(n_ptr, n_cap);
     int64_t base = (int64_t)blockIdx.x * kScanTile;
@@ -661,6 +667,7 @@ __global__ void __launch_bounds__(kScanThreads) scan_kernel(
     int64_t n_cap, const int64_t* __restrict__ block_sums, int64_t* __restrict__ ends,
     int64_t max_pairs, int32_t* pair_count, int32_t* overflow, int32_t* n_pairs_clamped)
 {
+    pdl_begin();
     __shared__ int64_t shared[kScanThreads / 32];
     __shared__ int64_t warp_inc[kScanThreads / 32];
     int64_t n = read_count(n_ptr, n_cap);
@@ -732,6 +739,7 @@ __global__ void __launch_bounds__(256) emit_kernel(
     K* __restrict__ keys, int32_t* __restrict__ values, int32_t* __restrict__ queue,
     int32_t* __restrict__ queue_count, int passes, int bits, uint32_t* __restrict__ key_hist)
 {
+    pdl_begin();
     __shared__ uint32_t local[4 * 256];
     for (int i = threadIdx.x; i < passes * 256; i += blockDim.x) local[i] = 0;
     __syncthreads();
@@ -775,6 +783,7 @@ __global__ void __launch_bounds__(256) emit_large_kernel(
     int tiles_x, int tiles_y, K* __restrict__ keys, int32_t* __restrict__ values, int passes,
     int bits, uint32_t* __restrict__ key_hist)
 {
+    pdl_begin();
     __shared__ uint32_t local[4 * 256];
     for (int i = threadIdx.x; i < passes * 256; i += blockDim.x) local[i] = 0;
     __syncthreads();
@@ -836,6 +845,7 @@ __global__ void ranges_kernel(const K* __restrict__ keys, const int32_t* n_ptr, 
                               int num_tiles, int32_t* __restrict__ offsets,
                               const int32_t* __restrict__ sort_error, int32_t* overflow)
 {
+    pdl_begin();
     if (blockIdx.x == 0 && threadIdx.x == 0 && *sort_error) atomicOr(overflow, 2);
     int64_t n = read_count(n_ptr, n_cap);
     int64_t stride = (int64_t)gridDim.x * blockDim.x;
@@ -926,11 +936,11 @@ int tile_stage(cudaStream_t s, const gsb_bin_params& p, const BinLayout& L, int 
     digit_plan(num_tiles, passes, bits);
     // The emission kernels also accumulate the tile sort's digit histograms
     // (its scratch was zeroed at the start of gsb_bin).
-    emit_kernel<K><<<ceil_div(C > 0 ? C : 1, 256), 256, 0, s>>>(
+    gsb::launch(emit_kernel<K>, ceil_div(C > 0 ? C : 1, 256), 256, 0, s, 
         order, point_counts, L.ends, n_binned, C, mean, conic, alpha, p, tiles_x, tiles_y,
         emit_keys, L.emit_ids, L.queue, L.scalars + 1, passes, bits, L.pair_sort.hist);
     if (int e = check_launch()) return e;
-    emit_large_kernel<K><<<148 * 8, 256, 0, s>>>(L.queue, L.scalars + 1, order, point_counts,
+    gsb::launch(emit_large_kernel<K>, 148 * 8, 256, 0, s, L.queue, L.scalars + 1, order, point_counts,
                                                  L.ends, mean, conic, alpha, p, tiles_x, tiles_y,
                                                  emit_keys, L.emit_ids, passes, bits,
                                                  L.pair_sort.hist);
@@ -943,7 +953,7 @@ int tile_stage(cudaStream_t s, const gsb_bin_params& p, const BinLayout& L, int 
                                  p.max_pairs, passes, bits, false, L.pair_sort, nullptr,
                                  L.scalars + 3, true))
         return e;
-    ranges_kernel<K><<<1024, 256, 0, s>>>(sorted_keys, L.scalars + 2, p.max_pairs, (int)num_tiles,
+    gsb::launch(ranges_kernel<K>, 1024, 256, 0, s, sorted_keys, L.scalars + 2, p.max_pairs, (int)num_tiles,
                                           tile_offsets, L.scalars + 3, overflow);
     return check_launch();
 }
@@ -994,7 +1004,7 @@ extern "C" int gsb_bin(gsb_stream_t stream, const gsb_bin_params* p, void* works
     size_t used = 0;
     BinLayout L = carve_bin(static_cast<char*>(workspace), *p, used);
     // Scalars, the depth sort's and the tile sort's scratch: one launch.
-    zero_ranges_kernel<<<296, 256, 0, s>>>(reinterpret_cast<uint32_t*>(L.scalars), 8,
+    gsb::launch(zero_ranges_kernel, 296, 256, 0, s, reinterpret_cast<uint32_t*>(L.scalars), 8,
                                            L.depth_sort.hist, sort_scratch_words(L.depth_sort),
                                            L.pair_sort.hist, sort_scratch_words(L.pair_sort));
     if (int e = check_launch()) return e;
@@ -1002,7 +1012,7 @@ extern "C" int gsb_bin(gsb_stream_t stream, const gsb_bin_params* p, void* works
     const uint32_t* sorted_depth_keys = nullptr;
     const int32_t* depth_order = L.order_a;
     if (C > 0) {
-        count_kernel<<<ceil_div(C, 256), 256, 0, s>>>((int)C, mean, conic, alpha, depth, visible,
+        gsb::launch(count_kernel, ceil_div(C, 256), 256, 0, s, (int)C, mean, conic, alpha, depth, visible,
                                                       *p, tiles_x, tiles_y, point_counts,
                                                       L.depth_keys, L.depth_sort.hist);
         if (int e = check_launch()) return e;
@@ -1013,10 +1023,10 @@ extern "C" int gsb_bin(gsb_stream_t stream, const gsb_bin_params* p, void* works
                                             L.scalars + 3, true))
             return e;
     }
-    scan_reduce_kernel<<<ceil_div(C > 0 ? C : 1, kScanTile), kScanThreads, 0, s>>>(
+    gsb::launch(scan_reduce_kernel, ceil_div(C > 0 ? C : 1, kScanTile), kScanThreads, 0, s, 
         depth_order, point_counts, L.scalars + 0, C, L.block_sums);
     if (int e = check_launch()) return e;
-    scan_kernel<<<ceil_div(C > 0 ? C : 1, kScanTile), kScanThreads, 0, s>>>(
+    gsb::launch(scan_kernel, ceil_div(C > 0 ? C : 1, kScanTile), kScanThreads, 0, s, 
         depth_order, point_counts, L.scalars + 0, C, L.block_sums, L.ends, p->max_pairs, pair_count,
         overflow, L.scalars + 2);
     if (int e = check_launch()) return e;

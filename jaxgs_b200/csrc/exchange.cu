@@ -42,6 +42,7 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p)
 __global__ void exchange_barrier_kernel(int world, int rank, uint32_t* const* peer_flags,
                                         const uint32_t* flags, uint32_t* epoch, int32_t* error)
 {
+    pdl_begin();
     __shared__ uint32_t next;
     if (threadIdx.x == 0) {
         __threadfence_system();  // this rank's earlier writes precede its signal
@@ -71,6 +72,7 @@ constexpr int kUnroll = 4;  // independent 16-byte chunks in flight per thread
 // Shard [begin, end) of the multicast buffer, in float4 chunks.
 __global__ void nvls_allreduce_kernel(float* mc, int64_t begin4, int64_t end4)
 {
+    pdl_begin();
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     for (int64_t i = begin4 + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < end4;
          i += stride * kUnroll) {
@@ -103,7 +105,7 @@ extern "C" int gsb_exchange_barrier(gsb_stream_t stream, const gsb_exchange_para
     if (p->world < 1 || p->world > 1024 || p->rank < 0 || p->rank >= p->world)
         return GSB_ERR_INVALID;
     if (!peer_flags || !flags || !epoch || !error) return GSB_ERR_NULL;
-    exchange_barrier_kernel<<<1, ((p->world + 31) / 32) * 32, 0, as_stream(stream)>>>(
+    gsb::launch(exchange_barrier_kernel, 1, ((p->world + 31) / 32) * 32, 0, as_stream(stream), 
         p->world, p->rank, peer_flags, flags, epoch, error);
     return check_launch();
 }
@@ -122,6 +124,6 @@ extern "C" int gsb_nvls_allreduce(gsb_stream_t stream, const gsb_exchange_params
     if (begin >= end) return GSB_OK;
     const int64_t want = (end - begin + 256 * kUnroll - 1) / (256 * kUnroll);
     const int blocks = (int)(want < 148 * 8 ? want : 148 * 8);
-    nvls_allreduce_kernel<<<blocks, 256, 0, as_stream(stream)>>>(multicast, begin, end);
+    gsb::launch(nvls_allreduce_kernel, blocks, 256, 0, as_stream(stream), multicast, begin, end);
     return check_launch();
 }

@@ -32,6 +32,40 @@ inline int check_launch()
 
 inline cudaStream_t as_stream(gsb_stream_t s) { return reinterpret_cast<cudaStream_t>(s); }
 
+// Programmatic dependent launch.  Every kernel of this library is launched
+// with programmatic stream serialization and starts with pdl_begin(): it
+// waits until the previous kernel on the stream has completed and its
+// memory is visible (griddepcontrol.wait; a no-op without a programmatic
+// predecessor), then lets the next kernel's blocks be scheduled as soon as
+// all of its own blocks have started (griddepcontrol.launch_dependents).  The
+// next kernel's blocks thus take the SMs that this kernel's last blocks
+// leave idle, and launch latency overlaps the tail; no kernel reads another
+// kernel's output before that kernel has finished.
+__device__ __forceinline__ void pdl_begin()
+{
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// kernel<<<grid, block, smem, stream>>>(args...) with the programmatic
+// serialization attribute; errors surface through check_launch().
+template <typename... Params, typename... Args>
+inline void launch(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                   Args... args)
+{
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaLaunchKernelEx(&cfg, kernel, static_cast<Params>(args)...);
+}
+
 // Workspace carving: 256-byte aligned sub-buffers.
 struct Carver {
     char* base;

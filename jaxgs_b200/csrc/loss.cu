@@ -99,6 +99,7 @@ __global__ void __launch_bounds__(kThreads, 4) loss_kernel(int width, int height
                                                            float* __restrict__ block_loss,
                                                            uint32_t* __restrict__ block_scale)
 {
+    pdl_begin();
     extern __shared__ float4 smem_raw[];
     LossSmem& S = *reinterpret_cast<LossSmem*>(smem_raw);
     __shared__ float warp_loss[kThreads / 32];
@@ -324,6 +325,7 @@ __global__ void __launch_bounds__(1024) loss_finish_kernel(int blocks, float inv
                                                            const uint32_t* __restrict__ block_scale,
                                                            float* loss, float* scale)
 {
+    pdl_begin();
     __shared__ double partial[32];
     __shared__ uint32_t pscale[32];
     double s = 0.0;
@@ -419,7 +421,7 @@ int launch_loss(cudaStream_t s, const gsb_loss_params& p, const float* image, co
     dim3 grid(ceil_div(p.width, kTW), ceil_div(p.height, kTH), 3);
     const size_t smem = sizeof(LossSmem);
     auto launch = [&](auto kernel) {
-        kernel<<<grid, kThreads, smem, s>>>(p.width, p.height, image, target, grad, block_loss,
+        gsb::launch(kernel, grid, kThreads, smem, s, p.width, p.height, image, target, grad, block_loss,
                                             block_scale);
     };
     if (p.target_u8) {
@@ -431,7 +433,7 @@ int launch_loss(cudaStream_t s, const gsb_loss_params& p, const float* image, co
     }
     if (int e = check_launch()) return e;
     const float inv_n = 1.0f / (3.0f * (float)p.width * (float)p.height);
-    loss_finish_kernel<<<1, 1024, 0, s>>>((int)(3 * loss_tiles(p)), inv_n, block_loss, block_scale,
+    gsb::launch(loss_finish_kernel, 1, 1024, 0, s, (int)(3 * loss_tiles(p)), inv_n, block_loss, block_scale,
                                           loss, scale);
     return check_launch();
 }

@@ -209,6 +209,7 @@ __global__ void __launch_bounds__(kProjThreads) project_fwd_kernel(
     float* __restrict__ out_depth, float* __restrict__ out_conic, float* __restrict__ out_radius,
     float* __restrict__ out_color, float* __restrict__ out_alpha, int8_t* __restrict__ out_visible)
 {
+    pdl_begin();
     constexpr int NC = (DEGREE + 1) * (DEGREE + 1) * 3;
     int count = p.compacted ? __ldg(cluster_count) : 0;
     // One thread per pool slot.  With a cluster list, slots of unlisted
@@ -539,6 +540,7 @@ __global__ void __launch_bounds__(kProjThreads) project_bwd_kernel(
     float* __restrict__ out_log_scale, float* __restrict__ out_rotation,
     float* __restrict__ out_opacity, float* __restrict__ out_sh)
 {
+    pdl_begin();
     project_bwd_body<DEGREE, SH_MODE>(p, xyz, log_scale, rotation, opacity, sh, view, intr, center,
                                       color, cluster_ids, cluster_count, gmean, gdepth, gconic,
                                       gradius, gcolor, galpha, out_xyz, out_log_scale,
@@ -565,6 +567,7 @@ __global__ void __launch_bounds__(kProjThreads) project_bwd_colors_multicast_ker
     float* __restrict__ out_log_scale, float* __restrict__ out_rotation,
     float* __restrict__ out_opacity, float* row_multicast, int64_t row_floats)
 {
+    pdl_begin();
     __shared__ __align__(16) float stage[kProjThreads * 3];
     stage[threadIdx.x * 3] = stage[threadIdx.x * 3 + 1] = stage[threadIdx.x * 3 + 2] = 0.0f;
     project_bwd_body<DEGREE, 1>(p, xyz, log_scale, rotation, opacity, sh, view, intr, center,
@@ -601,6 +604,7 @@ __global__ void __launch_bounds__(kProjThreads) sh_from_colors_kernel(
     const float* __restrict__ xyz, const float* __restrict__ centers,
     const float* __restrict__ colors, float* __restrict__ gsh)
 {
+    pdl_begin();
     constexpr int NB = (DEGREE + 1) * (DEGREE + 1);
     const int64_t g = (int64_t)blockIdx.x * kProjThreads + threadIdx.x;
     if (g >= capacity) return;
@@ -662,6 +666,7 @@ __global__ void __launch_bounds__(kClusterThreads) cluster_compact_kernel(
     const uint8_t* __restrict__ valid, const float* __restrict__ planes, int32_t* ids,
     int32_t* count_out, uint8_t* cluster_vis)
 {
+    pdl_begin();
     __shared__ float pl[24];
     __shared__ int warp_totals[32];
     __shared__ int running;
@@ -731,6 +736,7 @@ __global__ void __launch_bounds__(kClusterThreads) cluster_compact_kernel(
 __global__ void expand_slots_kernel(int64_t capacity, int cluster_size, const uint8_t* cluster_vis,
                                     uint8_t* slots)
 {
+    pdl_begin();
     int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i < capacity) slots[i] = cluster_vis[i / cluster_size];
 }
@@ -763,7 +769,7 @@ extern "C" int gsb_project_fwd(gsb_stream_t stream, const gsb_project_params* p,
     cudaStream_t s = as_stream(stream);
     int blocks = ceil_div(p->capacity, kProjThreads);
 #define GSB_PROJ_FWD(D)                                                                          \
-    project_fwd_kernel<D><<<blocks, kProjThreads, 0, s>>>(                                       \
+    gsb::launch(project_fwd_kernel<D>, blocks, kProjThreads, 0, s,                                        \
         *p, xyz, log_scale, rotation, opacity, sh, alive, view, intrinsics, center, cluster_ids, \
         cluster_count, mean, depth, conic, radius, color, alpha, visible)
     switch (p->degree) {
@@ -807,7 +813,7 @@ extern "C" int gsb_project_bwd(gsb_stream_t stream, const gsb_project_bwd_params
     cudaStream_t s = as_stream(stream);
     int blocks = ceil_div(p->capacity, kProjThreads);
 #define GSB_PROJ_BWD(D, M)                                                                        \
-    project_bwd_kernel<D, M><<<blocks, kProjThreads, 0, s>>>(                                     \
+    gsb::launch(project_bwd_kernel<D, M>, blocks, kProjThreads, 0, s,                                      \
         *p, xyz, log_scale, rotation, opacity, sh, view, intrinsics, center, color, cluster_ids,  \
         cluster_count, gmean, gdepth, gconic, gradius, gcolor, galpha, gxyz, glog_scale,          \
         grotation, gopacity, gsh)
@@ -850,11 +856,11 @@ extern "C" int gsb_cluster_compact(gsb_stream_t stream, const gsb_cluster_params
         return GSB_ERR_NULL;
     cudaStream_t s = as_stream(stream);
     uint8_t* cluster_vis = static_cast<uint8_t*>(workspace);
-    cluster_compact_kernel<<<1, kClusterThreads, 0, s>>>(p->num_clusters, center, extent, valid,
+    gsb::launch(cluster_compact_kernel, 1, kClusterThreads, 0, s, p->num_clusters, center, extent, valid,
                                                          planes, ids, count, cluster_vis);
     if (int e = check_launch()) return e;
     if (visible_slots && p->capacity > 0) {
-        expand_slots_kernel<<<ceil_div(p->capacity, 256), 256, 0, s>>>(
+        gsb::launch(expand_slots_kernel, ceil_div(p->capacity, 256), 256, 0, s, 
             p->capacity, p->cluster_size, cluster_vis, visible_slots);
         return check_launch();
     }
@@ -876,7 +882,7 @@ extern "C" int gsb_sh_from_colors(gsb_stream_t stream, const gsb_sh_params* p, c
     cudaStream_t s = as_stream(stream);
     const int blocks = ceil_div(p->capacity, kProjThreads);
 #define GSB_SH_FROM_COLORS(D)                                                               \
-    sh_from_colors_kernel<D><<<blocks, kProjThreads, 0, s>>>(                               \
+    gsb::launch(sh_from_colors_kernel<D>, blocks, kProjThreads, 0, s,                                \
         p->capacity, p->sh_dim, p->views, view_stride, center_stride, xyz, centers, colors, \
         gsh)
     switch (p->degree) {
@@ -917,7 +923,7 @@ extern "C" int gsb_project_bwd_colors_multicast(
     cudaStream_t s = as_stream(stream);
     const int blocks = ceil_div(p->capacity, kProjThreads);
 #define GSB_PROJ_BWD_MC(D)                                                                         \
-    project_bwd_colors_multicast_kernel<D><<<blocks, kProjThreads, 0, s>>>(                        \
+    gsb::launch(project_bwd_colors_multicast_kernel<D>, blocks, kProjThreads, 0, s,                         \
         *p, xyz, log_scale, rotation, opacity, sh, view, intrinsics, center, color, cluster_ids,   \
         cluster_count, gmean, gdepth, gconic, gradius, gcolor, galpha, gxyz, glog_scale,           \
         grotation, gopacity, row_multicast, row_floats)

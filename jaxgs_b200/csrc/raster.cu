@@ -44,6 +44,7 @@ __global__ void pack_kernel(int64_t capacity, const float* __restrict__ mean,
                             const float* __restrict__ alpha, const int8_t* __restrict__ visible,
                             float4* __restrict__ splats)
 {
+    pdl_begin();
     int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (g >= capacity || visible[g] == 0) return;
     float2 m = *reinterpret_cast<const float2*>(mean + g * 2);
@@ -108,6 +109,7 @@ __global__ void __launch_bounds__(kOrderThreads) order_tiles_kernel(const int32_
                                                                     int tiles, int from_offsets,
                                                                     int32_t* __restrict__ order)
 {
+    pdl_begin();
     __shared__ int starts[kOrderBuckets];
     const int tid = threadIdx.x;
     const int rounds = (tiles + kOrderThreads * kOrderPerThread - 1) / (kOrderThreads * kOrderPerThread);
@@ -271,6 +273,7 @@ __global__ void __launch_bounds__(256) raster_fwd_kernel(
     float* __restrict__ final_t, int32_t* __restrict__ last_out,
     int32_t* __restrict__ backward_work, uint32_t* __restrict__ bits)
 {
+    pdl_begin();
     using V = Vec<ROWS>;
     using T = typename V::T;
     extern __shared__ Stash stash_all[];
@@ -433,6 +436,7 @@ __global__ void __launch_bounds__(256) raster_bwd_kernel(
     float* __restrict__ gconic, float* __restrict__ gdepth, float* __restrict__ gcolor,
     float* __restrict__ galpha)
 {
+    pdl_begin();
     using V = Vec<ROWS>;
     using T = typename V::T;
     extern __shared__ Stash stash_all[];
@@ -581,6 +585,7 @@ __global__ void __launch_bounds__(256) raster_bwd_kernel(
 __global__ void zero_cotangents_kernel(int64_t capacity, float* gmean, float* gconic, float* gdepth,
                                        float* gcolor, float* galpha)
 {
+    pdl_begin();
     int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= capacity) return;
     *reinterpret_cast<float2*>(gmean + i * 2) = make_float2(0.f, 0.f);
@@ -596,6 +601,7 @@ __global__ void zero_cluster_cotangents_kernel(int64_t capacity, int cluster_siz
                                                const int32_t* __restrict__ count, float* gmean,
                                                float* gconic, float* gcolor, float* galpha)
 {
+    pdl_begin();
     int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= (int64_t)(*count) * cluster_size) return;
     int64_t g = (int64_t)ids[i / cluster_size] * cluster_size + i % cluster_size;
@@ -643,10 +649,10 @@ void launch_fwd(cudaStream_t s, int tiles, int warps, bool want_depth, const gsb
 {
     size_t smem = (size_t)warps * sizeof(Stash);
     if (want_depth)
-        raster_fwd_kernel<ROWS, true><<<tiles, warps * 32, smem, s>>>(
+        gsb::launch(raster_fwd_kernel<ROWS, true>, tiles, warps * 32, smem, s, 
             p, sp, depth, ids, offsets, order, bg, rgb, od, oa, final_t, last, work, bits);
     else
-        raster_fwd_kernel<ROWS, false><<<tiles, warps * 32, smem, s>>>(
+        gsb::launch(raster_fwd_kernel<ROWS, false>, tiles, warps * 32, smem, s, 
             p, sp, depth, ids, offsets, order, bg, rgb, od, oa, final_t, last, work, bits);
 }
 
@@ -660,11 +666,11 @@ void launch_bwd(cudaStream_t s, int tiles, int warps, bool want_depth,
 {
     size_t smem = (size_t)warps * sizeof(Stash);
     if (want_depth)
-        raster_bwd_kernel<ROWS, true><<<tiles, warps * 32, smem, s>>>(
+        gsb::launch(raster_bwd_kernel<ROWS, true>, tiles, warps * 32, smem, s, 
             p, sp, depth, ids, offsets, order, bits, bg, final_t, last, drgb, ddepth, dalpha,
             gmean, gconic, gdepth, gcolor, galpha);
     else
-        raster_bwd_kernel<ROWS, false><<<tiles, warps * 32, smem, s>>>(
+        gsb::launch(raster_bwd_kernel<ROWS, false>, tiles, warps * 32, smem, s, 
             p, sp, depth, ids, offsets, order, bits, bg, final_t, last, drgb, ddepth, dalpha,
             gmean, gconic, gdepth, gcolor, galpha);
 }
@@ -692,7 +698,7 @@ int launch_pack(cudaStream_t s, const gsb_raster_params& p, const float* mean, c
                 const float* color, const float* alpha, const int8_t* visible, float* splats)
 {
     if (p.capacity == 0) return GSB_OK;
-    pack_kernel<<<ceil_div(p.capacity, 256), 256, 0, s>>>(p.capacity, mean, conic, color, alpha,
+    gsb::launch(pack_kernel, ceil_div(p.capacity, 256), 256, 0, s, p.capacity, mean, conic, color, alpha,
                                                           visible,
                                                           reinterpret_cast<float4*>(splats));
     return check_launch();
@@ -706,16 +712,16 @@ int launch_bwd_prepare(cudaStream_t s, const gsb_raster_bwd_params& p, int tiles
 {
     if (p.capacity > 0) {
         if (cluster_ids) {
-            zero_cluster_cotangents_kernel<<<ceil_div(p.capacity, 256), 256, 0, s>>>(
+            gsb::launch(zero_cluster_cotangents_kernel, ceil_div(p.capacity, 256), 256, 0, s, 
                 p.capacity, p.cluster_size, cluster_ids, cluster_count, gmean, gconic, gcolor,
                 galpha);
         } else {
-            zero_cotangents_kernel<<<ceil_div(p.capacity, 256), 256, 0, s>>>(
+            gsb::launch(zero_cotangents_kernel, ceil_div(p.capacity, 256), 256, 0, s, 
                 p.capacity, gmean, gconic, gdepth, gcolor, galpha);
         }
         if (int e = check_launch()) return e;
     }
-    order_tiles_kernel<<<1, kOrderThreads, 0, s>>>(backward_work, tiles, 0, order);
+    gsb::launch(order_tiles_kernel, 1, kOrderThreads, 0, s, backward_work, tiles, 0, order);
     return check_launch();
 }
 
@@ -776,7 +782,7 @@ extern "C" int gsb_raster_fwd(gsb_stream_t stream, const gsb_raster_params* p, v
     if (!packed) {
         if (int e = launch_pack(s, *p, mean, conic, color, alpha, visible, splats)) return e;
     }
-    order_tiles_kernel<<<1, kOrderThreads, 0, s>>>(tile_offsets, tiles, 1, order);
+    gsb::launch(order_tiles_kernel, 1, kOrderThreads, 0, s, tile_offsets, tiles, 1, order);
     if (int e = check_launch()) return e;
     int warps = warps_per_tile(p->tile_w, p->tile_h);
     const float4* sp = reinterpret_cast<const float4*>(splats);
