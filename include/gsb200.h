@@ -147,8 +147,9 @@ GSB_API int gsb_project_bwd(gsb_stream_t stream, const gsb_project_bwd_params* p
  * through an NVLS multicast address into this rank's row of a symmetric row
  * table, row = [centre x, y, z, 0 | colours C*3 | pad], row_floats >= 4 + C*3
  * rounded up to a multiple of 4, row_multicast 16-byte aligned.  Every GPU's
- * copy of the row is written; a gsb_exchange_barrier afterwards publishes
- * it.  The geometric gradients are written locally as by gsb_project_bwd.
+ * copy of the row is written, except 16-byte chunks that are all zero (the
+ * receiving copies must hold zeros there: clear them after each use); a
+ * gsb_exchange_barrier afterwards publishes it.  The geometric gradients are written locally as by gsb_project_bwd.
  * No counterpart in the reference (its step sums per-view gradients with
  * one collective after the pullback). */
 GSB_API int gsb_project_bwd_colors_multicast(

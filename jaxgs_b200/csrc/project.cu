@@ -575,12 +575,14 @@ __global__ void __launch_bounds__(kProjThreads) project_bwd_colors_multicast_ker
                                 gcolor, galpha, out_xyz, out_log_scale, out_rotation, out_opacity,
                                 nullptr, stage);
     __syncthreads();
+    // Chunks of zeros are not sent: the receiving tables are zeroed after
+    // every exchange, and most Gaussians of a view have no colour cotangent.
     constexpr int kVec = kProjThreads * 3 / 4;
     if (threadIdx.x < kVec) {
         const int64_t off = 4 + (int64_t)blockIdx.x * kProjThreads * 3 + threadIdx.x * 4;
-        if (off + 4 <= row_floats)
-            multimem_st_v4(row_multicast + off,
-                           reinterpret_cast<const float4*>(stage)[threadIdx.x]);
+        const float4 v = reinterpret_cast<const float4*>(stage)[threadIdx.x];
+        if (off + 4 <= row_floats && (v.x != 0.0f || v.y != 0.0f || v.z != 0.0f || v.w != 0.0f))
+            multimem_st_v4(row_multicast + off, v);
     }
     if (blockIdx.x == 0 && threadIdx.x == 0)
         multimem_st_v4(row_multicast, make_float4(__ldg(center), __ldg(center + 1),

@@ -226,7 +226,8 @@ class NvlsExchange:
     The geometric gradients live in symmetric memory.  The step's pullback
     stores each rank's colour cotangents and camera centre straight into row
     r of every GPU's copy of a symmetric row table (the all-gather is part of
-    the kernel that produces them).  exchange() then passes a cross-GPU
+    the kernel that produces them; all-zero chunks, most of a view, are not
+    sent, and each rank clears its table after use).  exchange() then passes a cross-GPU
     barrier, sums shard r of the geometric gradients in the switch
     (multimem.ld_reduce) and stores the sum into every copy (multimem.st)
     while a second stream expands the gathered colours into the summed SH
@@ -323,6 +324,10 @@ class NvlsExchange:
                 "NVLS all-reduce")
         with torch.cuda.stream(self.side):
             K.sh_from_colors(self.xyz, None, self.rows, self.degree, self.sh_dim, out=self.sh)
+            # The pullback skips all-zero chunks, so the table must be zero
+            # before the next step's rows arrive (they come after the next
+            # barrier, which this rank reaches only after clearing).
+            self.table.zero_()
         main.wait_stream(self.side)
         self._barrier()
         return (*self.pool_grads[:4], self.sh)
