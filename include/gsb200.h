@@ -47,7 +47,7 @@ enum {
     GSB_ERR_NULL = 4        /* required pointer is NULL */
 };
 
-#define GSB_ABI_VERSION 2
+#define GSB_ABI_VERSION 3
 
 /* Library ABI version (GSB_ABI_VERSION). */
 GSB_API int gsb_abi_version(void);
@@ -276,6 +276,14 @@ GSB_API int gsb_raster_pack(gsb_stream_t stream, const gsb_raster_params* p, con
  * otherwise the whole pool is zeroed.
  * Outputs (accumulated): gmean[C*2], gconic[C*4], gdepth[C], gcolor[C*3],
  * galpha[C].
+ * fragment_stats[C*3] (may be NULL = not collected; collect_stats of
+ * kernels/sorted_rasterize.py:155-203): per Gaussian the number of
+ * composited fragments (alpha >= 1/256, before the pixel's last index), the
+ * sum of their compositing weights T*alpha, and the sum over fragments of
+ * the squared per-pixel opacity cotangent (zero where alpha saturates at
+ * 255/256).  With it galpha is zeroed over the whole pool, also when
+ * cluster_ids is given, so that galpha is the fourth statistic everywhere
+ * (kernels/packed_rasterize.py:753-766).
  * ------------------------------------------------------------------------ */
 typedef struct {
     int capacity;
@@ -295,10 +303,12 @@ GSB_API int gsb_raster_bwd(gsb_stream_t stream, const gsb_raster_bwd_params* p, 
                    const int32_t* backward_work, const uint32_t* contribution_bits,
                    const float* drgb, const float* ddepth, const float* dalpha,
                    const int32_t* cluster_ids, const int32_t* cluster_count, float* gmean,
-                   float* gconic, float* gdepth, float* gcolor, float* galpha);
+                   float* gconic, float* gdepth, float* gcolor, float* galpha,
+                   float* fragment_stats);
 
 /* The preparation stages of gsb_raster_bwd on their own: zero the cotangents
- * (the listed clusters' slots, or the whole pool) and order the tiles by
+ * (the listed clusters' slots, or the whole pool; fragment_stats and galpha
+ * over the whole pool when fragment_stats is non-NULL) and order the tiles by
  * backward_work into the workspace.  They need only the forward's
  * backward_work, so a caller can run them on a second stream during the
  * loss, then call gsb_raster_bwd with the same workspace and
@@ -308,7 +318,7 @@ GSB_API int gsb_raster_bwd_prepare(gsb_stream_t stream, const gsb_raster_bwd_par
                            void* workspace, size_t workspace_bytes,
                            const int32_t* backward_work, const int32_t* cluster_ids,
                            const int32_t* cluster_count, float* gmean, float* gconic,
-                           float* gdepth, float* gcolor, float* galpha);
+                           float* gdepth, float* gcolor, float* galpha, float* fragment_stats);
 
 /* ------------------------------------------------------------------------
  * Fused L1(0.8) + SSIM(0.2) loss and image gradient.

@@ -119,11 +119,11 @@ def _load():
     lib.gsb_raster_fwd.restype = ctypes.c_int
     lib.gsb_raster_fwd.argtypes = [vp, vp, vp, sz] + [vp] * 17
     lib.gsb_raster_bwd.restype = ctypes.c_int
-    lib.gsb_raster_bwd.argtypes = [vp, vp, vp, sz] + [vp] * 19
+    lib.gsb_raster_bwd.argtypes = [vp, vp, vp, sz] + [vp] * 20
     lib.gsb_raster_pack.restype = ctypes.c_int
     lib.gsb_raster_pack.argtypes = [vp, vp] + [vp] * 6
     lib.gsb_raster_bwd_prepare.restype = ctypes.c_int
-    lib.gsb_raster_bwd_prepare.argtypes = [vp, vp, vp, sz] + [vp] * 8
+    lib.gsb_raster_bwd_prepare.argtypes = [vp, vp, vp, sz] + [vp] * 9
     lib.gsb_loss.restype = ctypes.c_int
     lib.gsb_loss.argtypes = [vp, vp, vp, sz] + [vp] * 5
     for name, n in (("gsb_exchange_barrier", 4),):
@@ -139,7 +139,7 @@ def _load():
 
 
 lib = _load()
-if lib.gsb_abi_version() != 2:
+if lib.gsb_abi_version() != 3:
     raise RuntimeError("libgsb200.so ABI version mismatch; rebuild with `python -m jaxgs_b200.build`")
 
 

@@ -425,7 +425,7 @@ __device__ __forceinline__ float row_sum(typename Vec<ROWS>::T v)
     return s;
 }
 
-template <int ROWS, bool WANT_DEPTH>
+template <int ROWS, bool WANT_DEPTH, bool STATS>
 __global__ void __launch_bounds__(256) raster_bwd_kernel(
     gsb_raster_bwd_params p, const float4* __restrict__ splats, const float* __restrict__ depth,
     const int32_t* __restrict__ ids, const int32_t* __restrict__ offsets,
@@ -434,7 +434,7 @@ __global__ void __launch_bounds__(256) raster_bwd_kernel(
     const int32_t* __restrict__ last_in, const float* __restrict__ drgb,
     const float* __restrict__ ddepth, const float* __restrict__ dalpha, float* __restrict__ gmean,
     float* __restrict__ gconic, float* __restrict__ gdepth, float* __restrict__ gcolor,
-    float* __restrict__ galpha)
+    float* __restrict__ galpha, float* __restrict__ stats)
 {
     pdl_begin();
     using V = Vec<ROWS>;
@@ -550,11 +550,32 @@ __global__ void __launch_bounds__(256) raster_bwd_kernel(
             float Z = 0.0f;
             if (WANT_DEPTH) Z = row_sum<ROWS>(V::mul(w, gD));
             T ge = V::mul(ga, raw);
+            float count = 0.0f, square = 0.0f;
 #pragma unroll
             for (int r = 0; r < ROWS; r++) {
                 const bool live = valid[r] && V::get(raw, r) < kMaxAlpha;
                 V::set(ge, r, live ? V::get(ge, r) : 0.0f);
                 V::set(T_after, r, valid[r] ? V::get(T_before, r) : V::get(T_after, r));
+                if (STATS) {
+                    // Fragment statistics (sorted_rasterize.py:155-203): one
+                    // count per composited fragment, and the squared opacity
+                    // cotangent ga * e of each unsaturated one.
+                    const float go = live ? V::get(ga, r) * V::get(e, r) : 0.0f;
+                    count += valid[r] ? 1.0f : 0.0f;
+                    square = fmaf(go, go, square);
+                }
+            }
+            if (STATS) {
+                // w is exactly zero where the fragment is not composited.
+                const float weight = warp_sum(row_sum<ROWS>(w));
+                count = warp_sum(count);
+                square = warp_sum(square);
+                if (lane == 0 && count != 0.0f) {
+                    float* st_g = stats + (int64_t)st.id[k] * 3;
+                    atomicAdd(st_g, count);
+                    atomicAdd(st_g + 1, weight);
+                    atomicAdd(st_g + 2, square);
+                }
             }
             const T gedy = V::mul(ge, f.dy);
             float S0 = row_sum<ROWS>(ge);
@@ -612,6 +633,17 @@ __global__ void zero_cluster_cotangents_kernel(int64_t capacity, int cluster_siz
     galpha[g] = 0.0f;
 }
 
+// Fragment statistics start from zero over the whole pool, and so does the
+// opacity cotangent, their fourth column (kernels/packed_rasterize.py:759-766).
+__global__ void zero_stats_kernel(int64_t capacity, float* stats, float* galpha)
+{
+    pdl_begin();
+    int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= capacity * 3) return;
+    stats[i] = 0.0f;
+    if (i < capacity) galpha[i] = 0.0f;
+}
+
 bool tiles_ok(int tile_w, int tile_h)
 {
     return tile_w > 0 && tile_h > 0 && tile_w % 8 == 0 && tile_h % 4 == 0 && tile_w <= 16 &&
@@ -662,17 +694,21 @@ void launch_bwd(cudaStream_t s, int tiles, int warps, bool want_depth,
                 const int32_t* ids, const int32_t* offsets, const int32_t* order,
                 const uint32_t* bits, const float* bg, const float* final_t, const int32_t* last,
                 const float* drgb, const float* ddepth, const float* dalpha, float* gmean,
-                float* gconic, float* gdepth, float* gcolor, float* galpha)
+                float* gconic, float* gdepth, float* gcolor, float* galpha, float* stats)
 {
     size_t smem = (size_t)warps * sizeof(Stash);
-    if (want_depth)
-        gsb::launch(raster_bwd_kernel<ROWS, true>, tiles, warps * 32, smem, s, 
-            p, sp, depth, ids, offsets, order, bits, bg, final_t, last, drgb, ddepth, dalpha,
-            gmean, gconic, gdepth, gcolor, galpha);
-    else
-        gsb::launch(raster_bwd_kernel<ROWS, false>, tiles, warps * 32, smem, s, 
-            p, sp, depth, ids, offsets, order, bits, bg, final_t, last, drgb, ddepth, dalpha,
-            gmean, gconic, gdepth, gcolor, galpha);
+    auto go = [&](auto kernel) {
+        gsb::launch(kernel, tiles, warps * 32, smem, s, p, sp, depth, ids, offsets, order, bits,
+                    bg, final_t, last, drgb, ddepth, dalpha, gmean, gconic, gdepth, gcolor,
+                    galpha, stats);
+    };
+    if (stats) {
+        if (want_depth) go(raster_bwd_kernel<ROWS, true, true>);
+        else go(raster_bwd_kernel<ROWS, false, true>);
+    } else {
+        if (want_depth) go(raster_bwd_kernel<ROWS, true, false>);
+        else go(raster_bwd_kernel<ROWS, false, false>);
+    }
 }
 
 }  // namespace
@@ -708,8 +744,13 @@ int launch_pack(cudaStream_t s, const gsb_raster_params& p, const float* mean, c
 int launch_bwd_prepare(cudaStream_t s, const gsb_raster_bwd_params& p, int tiles,
                        const int32_t* backward_work, const int32_t* cluster_ids,
                        const int32_t* cluster_count, int32_t* order, float* gmean, float* gconic,
-                       float* gdepth, float* gcolor, float* galpha)
+                       float* gdepth, float* gcolor, float* galpha, float* stats)
 {
+    if (p.capacity > 0 && stats) {
+        gsb::launch(zero_stats_kernel, ceil_div((int64_t)p.capacity * 3, 256), 256, 0, s,
+                    (int64_t)p.capacity, stats, galpha);
+        if (int e = check_launch()) return e;
+    }
     if (p.capacity > 0) {
         if (cluster_ids) {
             gsb::launch(zero_cluster_cotangents_kernel, ceil_div(p.capacity, 256), 256, 0, s, 
@@ -801,7 +842,8 @@ extern "C" int gsb_raster_bwd_prepare(gsb_stream_t stream, const gsb_raster_bwd_
                                       void* workspace, size_t workspace_bytes,
                                       const int32_t* backward_work, const int32_t* cluster_ids,
                                       const int32_t* cluster_count, float* gmean, float* gconic,
-                                      float* gdepth, float* gcolor, float* galpha)
+                                      float* gdepth, float* gcolor, float* galpha,
+                                      float* fragment_stats)
 {
     if (!p) return GSB_ERR_NULL;
     gsb_raster_params rp{p->capacity, p->width, p->height, p->tile_w, p->tile_h, p->max_pairs, 0};
@@ -813,7 +855,7 @@ extern "C" int gsb_raster_bwd_prepare(gsb_stream_t stream, const gsb_raster_bwd_
     if (misaligned16(gconic, nullptr)) return GSB_ERR_INVALID;
     return launch_bwd_prepare(as_stream(stream), *p, (int)num_tiles(rp), backward_work,
                               cluster_ids, cluster_count, static_cast<int32_t*>(workspace), gmean,
-                              gconic, gdepth, gcolor, galpha);
+                              gconic, gdepth, gcolor, galpha, fragment_stats);
 }
 
 extern "C" int gsb_raster_bwd(gsb_stream_t stream, const gsb_raster_bwd_params* p,
@@ -825,7 +867,7 @@ extern "C" int gsb_raster_bwd(gsb_stream_t stream, const gsb_raster_bwd_params* 
                               const float* drgb, const float* ddepth, const float* dalpha,
                               const int32_t* cluster_ids, const int32_t* cluster_count,
                               float* gmean, float* gconic, float* gdepth, float* gcolor,
-                              float* galpha)
+                              float* galpha, float* fragment_stats)
 {
     if (!p) return GSB_ERR_NULL;
     gsb_raster_params rp{p->capacity, p->width, p->height, p->tile_w, p->tile_h, p->max_pairs, 0};
@@ -844,7 +886,8 @@ extern "C" int gsb_raster_bwd(gsb_stream_t stream, const gsb_raster_bwd_params* 
     int32_t* order = static_cast<int32_t*>(workspace);
     if (!(p->flags & GSB_RASTER_BWD_PREPARED)) {
         if (int e = launch_bwd_prepare(s, *p, tiles, backward_work, cluster_ids, cluster_count,
-                                       order, gmean, gconic, gdepth, gcolor, galpha))
+                                       order, gmean, gconic, gdepth, gcolor, galpha,
+                                       fragment_stats))
             return e;
     }
     int warps = warps_per_tile(p->tile_w, p->tile_h);
@@ -852,10 +895,10 @@ extern "C" int gsb_raster_bwd(gsb_stream_t stream, const gsb_raster_bwd_params* 
     if (rows_per_lane(p->tile_h) == 2)
         launch_bwd<2>(s, tiles, warps, want_depth, *p, sp, depth, gaussian_ids, tile_offsets,
                       order, contribution_bits, background, final_t, last, drgb, ddepth, dalpha,
-                      gmean, gconic, gdepth, gcolor, galpha);
+                      gmean, gconic, gdepth, gcolor, galpha, fragment_stats);
     else
         launch_bwd<1>(s, tiles, warps, want_depth, *p, sp, depth, gaussian_ids, tile_offsets,
                       order, contribution_bits, background, final_t, last, drgb, ddepth, dalpha,
-                      gmean, gconic, gdepth, gcolor, galpha);
+                      gmean, gconic, gdepth, gcolor, galpha, fragment_stats);
     return check_launch();
 }

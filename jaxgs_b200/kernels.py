@@ -365,10 +365,11 @@ def rasterize_forward(projected: ProjectedGaussians, table: SortedVisibilityTabl
 
 class BackwardBuffers:
     """Outputs and workspace of one rasterize_backward call, allocated up
-    front so that prepare_rasterize_backward can fill them on another stream."""
+    front so that prepare_rasterize_backward can fill them on another stream.
+    collect_stats: also gather the fragment statistics (statistics())."""
 
     def __init__(self, table: SortedVisibilityTable, camera: DeviceCamera, config: CapacityConfig,
-                 visible_clusters=None):
+                 visible_clusters=None, collect_stats: bool = False):
         C = config.max_gaussians
         dev = table.gaussian_ids.device
         self.gmean = torch.empty(C, 2, dtype=_f32, device=dev)
@@ -376,6 +377,7 @@ class BackwardBuffers:
         self.gdepth = torch.empty(C, dtype=_f32, device=dev)
         self.gcolor = torch.empty(C, 3, dtype=_f32, device=dev)
         self.galpha = torch.empty(C, dtype=_f32, device=dev)
+        self.fragments = torch.empty(C * 3, dtype=_f32, device=dev) if collect_stats else None
         self.visible_clusters = visible_clusters
         self.max_pairs = int(table.gaussian_ids.shape[0])
         rp = _raster_params(camera, config, self.max_pairs)
@@ -386,6 +388,15 @@ class BackwardBuffers:
         return L.RasterBwdParams(config.max_gaussians, camera.width, camera.height,
                                  config.tile_size, config.raster_tile_height, config.cluster_size,
                                  self.max_pairs, flags)
+
+    def statistics(self) -> torch.Tensor:
+        """[C, 4] fragment statistics of the backward: composited fragment
+        count, compositing weight sum, alpha cotangent, squared opacity
+        cotangent sum (kernels/sorted_rasterizer.py:227-235)."""
+        if self.fragments is None:
+            raise ValueError("these backward buffers do not collect fragment statistics")
+        f = self.fragments.view(-1, 3)
+        return torch.stack((f[:, 0], f[:, 1], self.galpha, f[:, 2]), dim=1)
 
     def clusters(self):
         ids, count = (None, None) if self.visible_clusters is None else self.visible_clusters
@@ -404,7 +415,8 @@ def prepare_rasterize_backward(cache: RasterCache, camera: DeviceCamera, config:
     L.check(L.lib.gsb_raster_bwd_prepare(
         _stream(), L.ref(p), _ptr(buffers.workspace), buffers.workspace.numel(),
         _ptr(cache.backward_work), ids, count, _ptr(buffers.gmean), _ptr(buffers.gconic),
-        _ptr(buffers.gdepth), _ptr(buffers.gcolor), _ptr(buffers.galpha)),
+        _ptr(buffers.gdepth), _ptr(buffers.gcolor), _ptr(buffers.galpha),
+        _ptr(buffers.fragments)),
         "rasterization backward preparation")
     buffers.prepared = True
     return buffers
@@ -413,20 +425,25 @@ def prepare_rasterize_backward(cache: RasterCache, camera: DeviceCamera, config:
 def rasterize_backward(projected: ProjectedGaussians, table: SortedVisibilityTable,
                        cache: RasterCache, drgb: torch.Tensor, camera: DeviceCamera,
                        config: CapacityConfig, background=None, ddepth=None, dalpha=None,
-                       visible_clusters=None,
-                       buffers: BackwardBuffers | None = None) -> ProjectedGaussians:
+                       visible_clusters=None, buffers: BackwardBuffers | None = None,
+                       collect_stats: bool = False) -> ProjectedGaussians:
     """sorted_rasterize.py:91-236: projected-field cotangents (mean, conic,
     depth, color, alpha).  With visible_clusters only those clusters' rows
     are zeroed and defined, and depth cotangents are left undefined.
     buffers: from BackwardBuffers (and prepare_rasterize_backward, which then
-    replaces the zeroing and ordering stages); its visible_clusters is used."""
+    replaces the zeroing and ordering stages); its visible_clusters and
+    collect_stats are used.  With fragment statistics (collect_stats, or
+    buffers made with it) the result is (cotangents, [C, 4] statistics), as
+    kernels/packed_rasterizer.py:96-175 returns a pair."""
     _require_cuda(drgb, "rasterization backward")
     C = config.max_gaussians
     dev = drgb.device
     if background is None:
         background = _zeros(3, dev)
     if buffers is None:
-        buffers = BackwardBuffers(table, camera, config, visible_clusters)
+        buffers = BackwardBuffers(table, camera, config, visible_clusters, collect_stats)
+    elif collect_stats and buffers.fragments is None:
+        raise ValueError("collect_stats needs BackwardBuffers made with collect_stats")
     if ddepth is not None and buffers.visible_clusters is not None:
         raise ValueError("depth cotangents are not defined with visible_clusters")
     p = buffers.params(camera, config, L.RASTER_BWD_PREPARED if buffers.prepared else 0)
@@ -439,12 +456,15 @@ def rasterize_backward(projected: ProjectedGaussians, table: SortedVisibilityTab
         _ptr(_c(drgb, _f32)), _ptr(None if ddepth is None else _c(ddepth, _f32)),
         _ptr(None if dalpha is None else _c(dalpha, _f32)), ids, count,
         _ptr(buffers.gmean), _ptr(buffers.gconic), _ptr(buffers.gdepth), _ptr(buffers.gcolor),
-        _ptr(buffers.galpha)),
+        _ptr(buffers.galpha), _ptr(buffers.fragments)),
         "rasterization backward")
     # The radius cotangent of a rasterizer is zero (sorted_rasterizer.py:224).
     radius = _zeros(1, dev).expand(C)
-    return projected.replace(mean=buffers.gmean, conic=buffers.gconic, depth=buffers.gdepth,
-                             color=buffers.gcolor, alpha=buffers.galpha, radius=radius)
+    cot = projected.replace(mean=buffers.gmean, conic=buffers.gconic, depth=buffers.gdepth,
+                            color=buffers.gcolor, alpha=buffers.galpha, radius=radius)
+    if buffers.fragments is not None:
+        return cot, buffers.statistics()
+    return cot
 
 
 # ---------------------------------------------------------------------------
@@ -485,12 +505,14 @@ def rasterize_loss_and_grad(projected: ProjectedGaussians, table: SortedVisibili
                             collect_stats: bool = False, visible_clusters=None):
     """kernels/sorted_rasterizer.py:165-236: fp32 forward, loss on
     clip(rgb, 0, 1) with the clip's VJP, fp32 backward.  Returns
-    (loss, cotangents, stats); stats collection is not implemented."""
-    if collect_stats:
-        raise ValueError("fragment statistics are not implemented in this backend")
+    (loss, cotangents, stats): stats is the [C, 4] fragment statistics
+    (count, weight, alpha cotangent, squared opacity cotangent) with
+    collect_stats, else zeros, as sorted_rasterizer.py:227-235 returns."""
     result, cache = rasterize_forward(projected, table, camera, config, want_depth=False,
                                       want_alpha=False)
     loss, drgb, _ = _fused_loss(result.rgb, target, False, clip_input=True)
     cot = rasterize_backward(projected, table, cache, drgb, camera, config,
-                             visible_clusters=visible_clusters)
-    return loss, cot, None
+                             visible_clusters=visible_clusters, collect_stats=collect_stats)
+    if collect_stats:
+        return loss, cot[0], cot[1]
+    return loss, cot, torch.zeros(config.max_gaussians, 4, dtype=_f32, device=drgb.device)

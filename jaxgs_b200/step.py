@@ -50,6 +50,7 @@ class StepOutput:
     overflow: torch.Tensor        # [1] int32
     point_counts: torch.Tensor | None = None  # [C] int32 pairs per Gaussian
     image: torch.Tensor | None = None
+    stats: torch.Tensor | None = None  # [C, 4] fragment statistics (collect_stats)
 
 
 def compute_training_step(pool: GaussianArrays, bounds, camera: DeviceCamera, target: torch.Tensor,
@@ -57,7 +58,8 @@ def compute_training_step(pool: GaussianArrays, bounds, camera: DeviceCamera, ta
                           active_sh_only: bool = True, sh_color_only: bool = False,
                           keep_image: bool = False, stage_events: dict | None = None,
                           overlap: bool = True, pool_grads=None,
-                          color_multicast=None) -> StepOutput:
+                          color_multicast=None, collect_stats: bool = False,
+                          stats: torch.Tensor | None = None) -> StepOutput:
     """training/step.py:32-89 without the optimizer update.
 
     bounds: world cluster bounds (center, extent, valid) on the device.
@@ -76,6 +78,10 @@ def compute_training_step(pool: GaussianArrays, bounds, camera: DeviceCamera, ta
     color_multicast: with sh_color_only and pool_grads, the colour cotangents
     (and the camera centre) go to this (multicast address, row floats) row
     instead (NvlsExchange).
+    collect_stats: also gather this view's [C, 4] fragment statistics (count,
+    compositing weight, alpha cotangent, squared opacity cotangent); with
+    stats given they are added into it in place (step.py:125-126,
+    stats = stats + fragment_stats), and StepOutput.stats is that tensor.
     """
     stream = torch.cuda.current_stream()
 
@@ -119,7 +125,8 @@ def compute_training_step(pool: GaussianArrays, bounds, camera: DeviceCamera, ta
     result, cache = K.rasterize_forward(projected, table, camera, config, want_depth=False,
                                         want_alpha=False, splats=splats)
     done(ev)
-    buffers = K.BackwardBuffers(table, camera, config, visible_clusters=clusters)
+    buffers = K.BackwardBuffers(table, camera, config, visible_clusters=clusters,
+                                collect_stats=collect_stats)
     if side is not None:
         side.wait_stream(stream)
         with torch.cuda.stream(side):
@@ -131,13 +138,18 @@ def compute_training_step(pool: GaussianArrays, bounds, camera: DeviceCamera, ta
         stream.wait_stream(side)
     ev = mark("raster_bwd")
     cot = K.rasterize_backward(projected, table, cache, drgb, camera, config, buffers=buffers)
+    fragment_stats = None
+    if collect_stats:
+        cot, fragment_stats = cot
+        if stats is not None:
+            fragment_stats = stats.add_(fragment_stats)
     done(ev)
     ev = mark("project_bwd")
     grads = (pullback(cot) if pool_grads is None else
              pullback(cot, out=pool_grads, compact=False, color_multicast=color_multicast))
     done(ev)
     return StepOutput(loss, grads, clusters, table.pair_count, table.overflow,
-                      table.point_counts, result.rgb if keep_image else None)
+                      table.point_counts, result.rgb if keep_image else None, fragment_stats)
 
 
 def render(camera: DeviceCamera, gaussians: GaussianArrays, visible_clusters, active_degree: int,
@@ -371,7 +383,8 @@ class GraphedTrainingStep:
     def __init__(self, pool: GaussianArrays, bounds, camera: DeviceCamera, target: torch.Tensor,
                  config: CapacityConfig, active_degree: int, *, active_sh_only: bool = True,
                  sh_color_only: bool = False, warmup: int = 2, pool_grads=None,
-                 color_multicast=None):
+                 color_multicast=None, collect_stats: bool = False,
+                 stats: torch.Tensor | None = None):
         dev = pool.xyz.device
         self.camera = DeviceCamera(camera.world_to_camera.clone(), camera.intrinsics.clone(),
                                    camera.center.clone(), camera.planes.clone(), camera.width,
@@ -380,13 +393,19 @@ class GraphedTrainingStep:
         self.target.copy_(target)
         args = (pool, bounds, self.camera, self.target, config, active_degree)
         kwargs = dict(active_sh_only=active_sh_only, sh_color_only=sh_color_only,
-                      pool_grads=pool_grads, color_multicast=color_multicast)
+                      pool_grads=pool_grads, color_multicast=color_multicast,
+                      collect_stats=collect_stats)
         side = torch.cuda.Stream(device=dev)
         side.wait_stream(torch.cuda.current_stream(dev))
         with torch.cuda.stream(side):
             for _ in range(max(warmup, 1)):
                 compute_training_step(*args, **kwargs)
         torch.cuda.current_stream(dev).wait_stream(side)
+        # Statistics accumulate across replays into `stats` (the warm-up steps
+        # above do not touch it): the captured step adds into it in place.
+        if collect_stats:
+            kwargs["stats"] = stats if stats is not None else torch.zeros(
+                config.max_gaussians, 4, dtype=torch.float32, device=dev)
         self.graph = torch.cuda.CUDAGraph()
         from . import _lib
 

@@ -774,10 +774,14 @@ EXPORT void orc_raster_bwd(int width, int height, int tile_w, int tile_h, int ca
                            const int32_t* tile_offsets, const float* background,
                            const float* final_t, const int32_t* last, const float* drgb,
                            const float* ddepth, const float* dalpha, float* gmean,
-                           float* gconic, float* gdepth, float* gcolor, float* gopacity)
+                           float* gconic, float* gdepth, float* gcolor, float* gopacity,
+                           float* stats)
 {
+    /* stats (may be NULL): per Gaussian (fragment count, sum of compositing
+     * weights, sum of squared per-pixel opacity gradients), the fragment
+     * statistics of kernels/sorted_rasterize.py:155-203. */
     int tiles_x = (width + tile_w - 1) / tile_w;
-    double* acc = (double*)calloc((size_t)capacity * 11, sizeof(double));
+    double* acc = (double*)calloc((size_t)capacity * 14, sizeof(double));
 #pragma omp parallel for schedule(dynamic, 64)
     for (int64_t p = 0; p < (int64_t)width * height; p++) {
         int px = (int)(p % width), py = (int)(p / width);
@@ -806,7 +810,9 @@ EXPORT void orc_raster_bwd(int width, int height, int tile_w, int tile_h, int ca
                        + g_d * depth[g];
             float ga = T_before * (gw - gtrans);
             gtrans = a * gw + (1.0f - a) * gtrans;
-            double* acc_g = acc + g * 11;
+            double* acc_g = acc + g * 14;
+            ACC_ADD(acc_g[11], 1.0);
+            ACC_ADD(acc_g[12], (double)w);
             ACC_ADD(acc_g[6], (double)w * g_d);
             ACC_ADD(acc_g[7], (double)w * g_r);
             ACC_ADD(acc_g[8], (double)w * g_g);
@@ -814,6 +820,7 @@ EXPORT void orc_raster_bwd(int width, int height, int tile_w, int tile_h, int ca
             if (raw < 255.0f / 256.0f) {
                 float ge = ga * raw;
                 ACC_ADD(acc_g[10], (double)ga * e);
+                ACC_ADD(acc_g[13], (double)(ga * e) * (double)(ga * e));
                 ACC_ADD(acc_g[0], (double)ge * (c00 * dx + 0.5f * (c01 + c10) * dy));
                 ACC_ADD(acc_g[1], (double)ge * (c11 * dy + 0.5f * (c01 + c10) * dx));
                 ACC_ADD(acc_g[2], -0.5 * ge * dx * dx);
@@ -825,7 +832,9 @@ EXPORT void orc_raster_bwd(int width, int height, int tile_w, int tile_h, int ca
         }
     }
     for (int64_t g = 0; g < capacity; g++) {
-        double* acc_g = acc + g * 11;
+        double* acc_g = acc + g * 14;
+        if (stats)
+            for (int k = 0; k < 3; k++) stats[g * 3 + k] = (float)acc_g[11 + k];
         gmean[g * 2] = (float)acc_g[0];
         gmean[g * 2 + 1] = (float)acc_g[1];
         for (int k = 0; k < 4; k++) gconic[g * 4 + k] = (float)acc_g[2 + k];

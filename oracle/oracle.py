@@ -202,12 +202,16 @@ def raster_bwd(proj, table, fwd, drgb, width, height, tile_w, tile_h, background
                ddepth=None, dalpha=None):
     """fp32 compositing pullback, kernels/sorted_rasterize.py:91-236.
 
-    Returns dict of flat cotangents mean[C*2], conic[C*4], depth, color, alpha.
+    Returns dict of flat cotangents mean[C*2], conic[C*4], depth, color, alpha,
+    and "stats" [C, 4]: the fragment statistics (count, compositing weight,
+    alpha cotangent, squared opacity cotangent) that
+    kernels/sorted_rasterizer.py:227-235 stacks from the collect_stats outputs.
     """
     capacity = proj["alpha"].shape[0]
     out = {"mean": np.zeros(capacity * 2, np.float32), "conic": np.zeros(capacity * 4, np.float32),
            "depth": np.zeros(capacity, np.float32), "color": np.zeros(capacity * 3, np.float32),
            "alpha": np.zeros(capacity, np.float32)}
+    fragments = np.zeros(capacity * 3, np.float32)
     lib().orc_raster_bwd(
         _int(width), _int(height), _int(tile_w), _int(tile_h), _int(capacity),
         _ptr(_f(proj["mean"])), _ptr(_f(proj["conic"])), _ptr(_f(proj["depth"])),
@@ -217,7 +221,9 @@ def raster_bwd(proj, table, fwd, drgb, width, height, tile_w, tile_h, background
         _ptr(_f(np.asarray(background))), _ptr(_f(fwd["final_t"])),
         _ptr(np.ascontiguousarray(fwd["last"], np.int32)), _ptr(_f(drgb)),
         _ptr(None if ddepth is None else _f(ddepth)), _ptr(None if dalpha is None else _f(dalpha)),
-        *[_ptr(out[k]) for k in ("mean", "conic", "depth", "color", "alpha")])
+        *[_ptr(out[k]) for k in ("mean", "conic", "depth", "color", "alpha")], _ptr(fragments))
+    out["stats"] = np.stack((fragments[0::3], fragments[1::3], out["alpha"], fragments[2::3]),
+                            axis=1)
     return out
 
 
@@ -264,7 +270,8 @@ def training_step(pool, camera, target, *, degree, sh_dim, tile_w, tile_h, max_p
     pullback -> projection pullback (compact, rgb_only, active SH only).
 
     Returns dict(loss, grads (xyz, log_scale, rotation, opacity, sh) in
-    compact order, clusters (ids, count), table, fwd, proj).  timings, if a
+    compact order, clusters (ids, count), table, fwd, proj, stats (the [C, 4]
+    fragment statistics of this view)).  timings, if a
     dict, receives per-stage seconds; clusters overrides the culled list."""
     import time
 
@@ -305,4 +312,4 @@ def training_step(pool, camera, target, *, degree, sh_dim, tile_w, tile_h, max_p
         timings.update(cull=t1 - t0, project=t2 - t1, bin=t3 - t2, raster_fwd=t4 - t3,
                        loss=t5 - t4, raster_bwd=t6 - t5, project_bwd=t7 - t6, total=t7 - t0)
     return {"loss": value, "grads": grads, "clusters": (ids, count), "table": table, "fwd": fwd,
-            "proj": proj}
+            "proj": proj, "stats": cot["stats"]}

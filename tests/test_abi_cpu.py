@@ -28,7 +28,7 @@ def test_every_declared_symbol_is_exported():
 
 
 def test_abi_version_and_launch_counter():
-    assert L.lib.gsb_abi_version() == 2
+    assert L.lib.gsb_abi_version() == 3
     assert L.launch_count() >= 0
 
 
@@ -64,9 +64,9 @@ def test_invalid_parameters_are_rejected_before_launch():
     rast = L.RasterParams(10, 64, 48, 16, 8, 100, L.RASTER_SPLATS_READY)
     assert L.lib.gsb_raster_pack(vp, L.ref(rast), *([vp] * 6)) == 4  # NULL pointers
     rbwd = L.RasterBwdParams(10, 64, 48, 16, 8, 128, 100, 4)  # unknown flag
-    assert L.lib.gsb_raster_bwd_prepare(vp, L.ref(rbwd), vp, 0, *([vp] * 8)) == 1
+    assert L.lib.gsb_raster_bwd_prepare(vp, L.ref(rbwd), vp, 0, *([vp] * 9)) == 1
     rbwd = L.RasterBwdParams(10, 64, 48, 16, 8, 128, 100, L.RASTER_BWD_PREPARED)
-    assert L.lib.gsb_raster_bwd_prepare(vp, L.ref(rbwd), vp, 0, *([vp] * 8)) == 2  # no workspace
+    assert L.lib.gsb_raster_bwd_prepare(vp, L.ref(rbwd), vp, 0, *([vp] * 9)) == 2  # no workspace
     loss = L.LossParams(0, 5, 1, 0)
     assert L.lib.gsb_loss(vp, L.ref(loss), vp, 0, *([vp] * 5)) == 1
     assert L.lib.gsb_bin(vp, None, vp, 0, *([vp] * 10)) == 4

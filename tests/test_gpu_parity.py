@@ -343,6 +343,111 @@ def test_raster_backward_matches_oracle(tile_h, tile_w):
         assert rel_l2(got, exp[name]) < 1e-3, (name, rel_l2(got, exp[name]))
 
 
+def _assert_stats_close(got, exp):
+    """[C, 4] fragment statistics: counts equal for all but threshold-borderline
+    Gaussians, every column within 1e-3 relative L2."""
+    assert got.shape == exp.shape
+    assert np.isfinite(got).all()
+    assert exp[:, 0].sum() > 0
+    assert np.mean(got[:, 0] == exp[:, 0]) >= 0.99
+    for col in range(4):
+        assert rel_l2(got[:, col], exp[:, col]) < 1e-3, (col, rel_l2(got[:, col], exp[:, col]))
+
+
+@pytest.mark.parametrize("tile_h,tile_w,split", [(8, 16, False), (12, 16, True), (16, 16, True)])
+def test_fragment_statistics_match_oracle(tile_h, tile_w, split):
+    """collect_stats (sorted_rasterize.py:155-203): per Gaussian the composited
+    fragment count, the compositing weight sum and the squared opacity
+    cotangent sum, stacked with the alpha cotangent as
+    sorted_rasterizer.py:227-235 does.  split: the preparation runs on its
+    own over NaN-filled buffers with a cluster list, so the statistics and
+    the alpha cotangent must be zeroed over the whole pool."""
+    from jaxgs_b200.scene import CapacityConfig
+    from jaxgs_b200.types import DeviceCamera, SortedVisibilityTable
+
+    K = _kernels()
+    W, H = 67, 45
+    proj, table = _raster_case(31, W, H, tw=tile_w, th=tile_h)
+    c = len(proj["alpha"])
+    config = CapacityConfig(c, 128, 1, tile_w, 0, len(table["gaussian_ids"]), tile_height=tile_h)
+    t_table = SortedVisibilityTable(*(torch.as_tensor(table[k], device="cuda") for k in
+                                      ("gaussian_ids", "tile_offsets", "point_counts")),
+                                    torch.tensor([table["pair_count"]], device="cuda"),
+                                    torch.tensor([0], device="cuda"))
+    cam = DeviceCamera(None, None, None, None, W, H)
+    projected = torch_proj(proj)
+    rng = np.random.default_rng(8)
+    drgb = rng.normal(0, 1, (H, W, 3)).astype(np.float32)
+    ddepth = None if split else rng.normal(0, 0.1, (H, W)).astype(np.float32)
+    result, cache = K.rasterize_forward(projected, t_table, cam, config)
+    drgb_t = torch.as_tensor(drgb, device="cuda")
+    if split:
+        ids = torch.arange(-(-c // 128), dtype=torch.int32, device="cuda")
+        clusters = (ids, torch.tensor([ids.numel()], dtype=torch.int32, device="cuda"))
+        buffers = K.BackwardBuffers(t_table, cam, config, visible_clusters=clusters,
+                                    collect_stats=True)
+        for t in (buffers.gmean, buffers.gconic, buffers.gcolor, buffers.galpha,
+                  buffers.fragments):
+            t.fill_(float("nan"))
+        K.prepare_rasterize_backward(cache, cam, config, buffers)
+        cot, stats = K.rasterize_backward(projected, t_table, cache, drgb_t, cam, config,
+                                          buffers=buffers)
+    else:
+        cot, stats = K.rasterize_backward(projected, t_table, cache, drgb_t, cam, config,
+                                          ddepth=torch.as_tensor(ddepth, device="cuda"),
+                                          collect_stats=True)
+    torch.cuda.synchronize()
+    fwd = O.raster_fwd(proj, table, W, H, tile_w, tile_h)
+    exp = O.raster_bwd(proj, table, fwd, drgb.reshape(-1), W, H, tile_w, tile_h,
+                       ddepth=None if ddepth is None else ddepth.reshape(-1))
+    _assert_stats_close(stats.cpu().numpy(), exp["stats"])
+    for name in ("mean", "conic", "color", "alpha"):
+        got = getattr(cot, name).cpu().numpy().reshape(-1)
+        assert rel_l2(got, exp[name]) < 1e-3, (name, rel_l2(got, exp[name]))
+    # Without statistics the same call returns the cotangents alone.
+    plain = K.rasterize_backward(projected, t_table, cache, drgb_t, cam, config,
+                                 ddepth=None if ddepth is None else torch.as_tensor(ddepth,
+                                                                                   device="cuda"))
+    torch.cuda.synchronize()
+    assert rel_l2(plain.alpha.cpu().numpy(), exp["alpha"]) < 1e-3
+
+
+def test_known_answer_early_termination_statistics_on_gpu():
+    """tests/test_packed.py:240-273 on the CUDA path: black right half, 0.5
+    left half, the fourth splat on collects nothing, and the statistics
+    equal the oracle's."""
+    from jaxgs_b200.scene import CapacityConfig
+    from jaxgs_b200.types import DeviceCamera, SortedVisibilityTable
+    from tests.test_oracle_cpu import early_termination_case
+
+    K = _kernels()
+    proj, table = early_termination_case()
+    config = CapacityConfig(12, 1, 12, 16, 0, 12, tile_height=8)
+    t_table = SortedVisibilityTable(torch.as_tensor(table["gaussian_ids"], device="cuda"),
+                                    torch.as_tensor(table["tile_offsets"], device="cuda"),
+                                    torch.ones(12, dtype=torch.int32, device="cuda"),
+                                    torch.tensor([12], device="cuda"),
+                                    torch.tensor([0], device="cuda"))
+    cam = DeviceCamera(None, None, None, None, 32, 8)
+    projected = torch_proj(proj)
+    result, cache = K.rasterize_forward(projected, t_table, cam, config)
+    drgb = torch.ones(8, 32, 3, device="cuda")
+    cot, stats = K.rasterize_backward(projected, t_table, cache, drgb, cam, config,
+                                      collect_stats=True)
+    torch.cuda.synchronize()
+    image = result.rgb.cpu().numpy()
+    np.testing.assert_array_equal(image[:, 16:], 0)
+    np.testing.assert_allclose(image[:, :16], 0.5, atol=1e-3)
+    assert cache.last.cpu().numpy().reshape(8, 32)[:, :16].max() < 12
+    np.testing.assert_array_equal(cot.color.cpu().numpy()[3:], 0)
+    stats = stats.cpu().numpy()
+    np.testing.assert_array_equal(stats[3:, :2], 0)
+    fwd = O.raster_fwd(proj, table, 32, 8, 16, 8)
+    exp = O.raster_bwd(proj, table, fwd, np.ones(8 * 32 * 3, np.float32), 32, 8, 16, 8)
+    np.testing.assert_array_equal(stats[:, 0], exp["stats"][:, 0])
+    np.testing.assert_allclose(stats, exp["stats"], rtol=1e-4, atol=1e-6)
+
+
 @pytest.mark.parametrize("tile_h,tile_w", [(16, 8), (12, 16)])
 def test_raster_split_stages_match_single_calls(tile_h, tile_w):
     """gsb_raster_pack + gsb_raster_fwd(SPLATS_READY) and gsb_raster_bwd_prepare

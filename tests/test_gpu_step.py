@@ -116,6 +116,48 @@ def test_pool_order_gradients_for_the_view_sharded_exchange():
         assert rel_l2(got.cpu().numpy().reshape(-1), exp.cpu().numpy().reshape(-1)) < 1e-5
 
 
+def test_training_step_fragment_statistics():
+    """collect_stats: the step's [C, 4] fragment statistics equal the oracle's
+    for the view; with `stats` they are added into it in place
+    (training/step.py:125-126), and a graphed step adds one view's worth on
+    every replay."""
+    from jaxgs_b200.scene import CapacityConfig, config0_scene, world_cluster_bounds
+    from jaxgs_b200.step import GraphedTrainingStep, compute_training_step
+    from jaxgs_b200.types import DeviceCamera, GaussianArrays
+
+    pool_np, cam, target = config0_scene()
+    n = pool_np["xyz"].shape[0]
+    config = CapacityConfig(n, 128, 16, 16, 3, n * 64, tile_height=8)
+    center, extent, valid = world_cluster_bounds(pool_np, 128)
+    bounds = (torch.as_tensor(center, device="cuda"), torch.as_tensor(extent, device="cuda"),
+              torch.as_tensor(valid.astype(np.uint8), device="cuda"))
+    pool = GaussianArrays.from_numpy(pool_np)
+    dcam = DeviceCamera.from_camera(cam)
+    tgt = torch.as_tensor(target, device="cuda")
+    out = compute_training_step(pool, bounds, dcam, tgt, config, 3, collect_stats=True)
+    torch.cuda.synchronize()
+    ids = out.visible_clusters[0].cpu().numpy()
+    count = int(out.visible_clusters[1].item())
+    exp = O.training_step(pool_np, cam, target, degree=3, sh_dim=16, tile_w=16, tile_h=8,
+                          max_pairs=n * 64, clusters=(ids, count))
+    single = out.stats.cpu().numpy()
+    assert single.shape == (n, 4) and exp["stats"][:, 0].sum() > 0
+    assert np.mean(single[:, 0] == exp["stats"][:, 0]) >= 0.99
+    for col in range(4):
+        assert rel_l2(single[:, col], exp["stats"][:, col]) < 1e-3, col
+    acc = torch.ones(n, 4, device="cuda")
+    again = compute_training_step(pool, bounds, dcam, tgt, config, 3, collect_stats=True,
+                                  stats=acc)
+    assert again.stats is acc
+    torch.cuda.synchronize()
+    assert rel_l2(acc.cpu().numpy() - 1.0, single) < 1e-5
+    graphed = GraphedTrainingStep(pool, bounds, dcam, tgt, config, 3, collect_stats=True)
+    for _ in range(3):
+        graphed()
+    torch.cuda.synchronize()
+    assert rel_l2(graphed.out.stats.cpu().numpy(), 3 * single) < 1e-5
+
+
 def _np_sh_from_colors(xyz, centers, colors, degree, sh_dim):
     """training/sh_pullback.py:18-53 in numpy (float64), summed over views."""
     out = np.zeros((xyz.shape[0], sh_dim, 3))

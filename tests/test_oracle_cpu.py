@@ -224,6 +224,62 @@ def test_oracle_compositing_pullback_matches_autograd():
         assert rel_l2(got, ref) < 1e-3, (name, rel_l2(got, ref))
 
 
+def test_oracle_fragment_statistics_match_dense_autograd():
+    """collect_stats (sorted_rasterize.py:155-203) against the dense float64
+    restatement: counts exact, the other columns within 1e-4 relative L2."""
+    W, H = 23, 19
+    proj = _dense_case(seed=4)
+    table = _dense_table(len(proj["alpha"]), W, H, 16, 8)
+    bg = np.array([0.1, 0.2, 0.3], np.float32)
+    fwd = O.raster_fwd(proj, table, W, H, 16, 8, bg)
+    drgb = np.random.default_rng(9).normal(0, 1, (H, W, 3))
+    exp = O.raster_bwd(proj, table, fwd, drgb.reshape(-1), W, H, 16, 8, bg)
+    c = len(proj["alpha"])
+    t = lambda a, s: torch.as_tensor(np.asarray(a, np.float64)).reshape(s)
+    ref = R.dense_fragment_statistics(t(proj["mean"], (c, 2)), t(proj["conic"], (c, 2, 2)),
+                                      t(proj["color"], (c, 3)), t(proj["alpha"], (c,)), W, H,
+                                      torch.as_tensor(drgb), bg).numpy()
+    stats = exp["stats"]
+    assert stats.shape == (c, 4) and ref[:, 0].sum() > 0
+    np.testing.assert_array_equal(stats[:, 0], ref[:, 0])
+    for col in (1, 2, 3):
+        assert rel_l2(stats[:, col], ref[:, col]) < 1e-4, (col, rel_l2(stats[:, col], ref[:, col]))
+
+
+def early_termination_case():
+    """tests/test_packed.py:240-271: twelve coincident near-opaque splats
+    (opacity 0.99) over the left 16x8 tile of a 32x8 image; the right tile
+    is empty."""
+    c = 12
+    proj = {"mean": np.full(c * 2, 4.0, np.float32), "depth": np.ones(c, np.float32),
+            "conic": np.tile(np.eye(2, dtype=np.float32).reshape(-1) * 1e-4, c),
+            "radius": np.ones(c, np.float32), "color": np.full(c * 3, 0.5, np.float32),
+            "alpha": np.full(c, 0.99, np.float32), "visible": np.ones(c, np.int8)}
+    table = {"gaussian_ids": np.arange(c, dtype=np.int32),
+             "tile_offsets": np.array([0, c, c], np.int32)}
+    return proj, table
+
+
+def test_known_answer_early_termination_statistics():
+    """tests/test_packed.py:262-273: the right half stays black, the left is
+    0.5, no pixel composites all twelve splats, the splats from the fourth
+    on collect no statistics and get no colour cotangent, and the squared
+    opacity cotangents are finite."""
+    proj, table = early_termination_case()
+    fwd = O.raster_fwd(proj, table, 32, 8, 16, 8)
+    image = fwd["rgb"].reshape(8, 32, 3)
+    np.testing.assert_array_equal(image[:, 16:], 0)
+    np.testing.assert_allclose(image[:, :16], 0.5, atol=1e-3)
+    assert fwd["last"].reshape(8, 32)[:, :16].max() < 12
+    bwd = O.raster_bwd(proj, table, fwd, np.ones(8 * 32 * 3, np.float32), 32, 8, 16, 8)
+    np.testing.assert_array_equal(bwd["color"].reshape(12, 3)[3:], 0)
+    stats = bwd["stats"]
+    np.testing.assert_array_equal(stats[3:, :2], 0)
+    assert np.isfinite(stats).all()
+    # Every pixel of the left tile composites the first two splats.
+    np.testing.assert_array_equal(stats[:2, 0], 128)
+
+
 @pytest.mark.parametrize("shape", [(3, 5), (17, 31), (40, 33)])
 def test_oracle_loss_matches_autograd(shape):
     """Fused loss value and gradient == autograd of reference/loss.py

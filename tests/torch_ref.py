@@ -6,6 +6,8 @@ its analytic gradients.  Each function restates one reference function:
   project          render/projection.py:33-74 (+ reference/sh.py:8-36)
   dense_composite  tests/test_cute.py:244-264 (front-to-back compositing with
                    the T >= 1/8192 early stop, over every splat in depth order)
+  dense_fragment_statistics  kernels/sorted_rasterize.py:155-203 on the
+                   same dense compositing
   photometric_loss reference/loss.py:6-43
 """
 
@@ -112,6 +114,36 @@ def dense_composite(mean, conic, color, alpha, depth, order, width, height, back
     if background is not None:
         rgb = rgb + final_t[:, :, None] * torch.as_tensor(background, dtype=dt)
     return rgb, (weight * dep).sum(-1), 1 - final_t
+
+
+def dense_fragment_statistics(mean, conic, color, opacity, width, height, drgb, background=None):
+    """The fragment statistics of kernels/sorted_rasterize.py:155-203 from the
+    dense compositing above (splats in index order), float64: per Gaussian
+    the composited fragment count, the compositing weight sum, the opacity
+    cotangent of sum(rgb * drgb) and the sum over pixels of its squared
+    per-pixel part.  The per-pixel part comes from autograd through one
+    opacity leaf per (pixel, Gaussian).  Returns [C, 4]."""
+    dt = mean.dtype
+    ys, xs = torch.meshgrid(torch.arange(height, dtype=dt), torch.arange(width, dtype=dt), indexing="ij")
+    pix = torch.stack([xs + 0.5, ys + 0.5], -1)
+    delta = pix[:, :, None, :] - mean
+    power = -0.5 * torch.einsum("hwgi,gij,hwgj->hwg", delta, conic, delta)
+    per_pixel = opacity.detach().expand(height, width, -1).clone().requires_grad_(True)
+    raw = per_pixel * torch.exp(power)
+    keep = (power <= 0) & (raw >= 1.0 / 256)
+    al = torch.where(keep, torch.clamp(raw, max=255.0 / 256), torch.zeros_like(raw))
+    prefix = torch.cumprod(1 - al, -1)
+    before = torch.cat([torch.ones_like(prefix[..., :1]), prefix[..., :-1]], -1)
+    active = (before >= 1.0 / 8192).detach()
+    al = torch.where(active, al, torch.zeros_like(al))
+    weight = before * al
+    rgb = torch.einsum("hwg,gc->hwc", weight, color)
+    if background is not None:
+        rgb = rgb + torch.prod(1 - al, -1)[:, :, None] * torch.as_tensor(background, dtype=dt)
+    (rgb * drgb).sum().backward()
+    go = per_pixel.grad
+    count = (keep & active).to(dt).sum((0, 1))
+    return torch.stack([count, weight.detach().sum((0, 1)), go.sum((0, 1)), (go * go).sum((0, 1))], 1)
 
 
 def _gauss_window(dt):
