@@ -290,9 +290,12 @@ __global__ void __launch_bounds__(kProjThreads) project_fwd_kernel(
 //          1 = colour cotangents only (sh_color_only, 3 floats per point).
 // ---------------------------------------------------------------------------
 // color_stage (colour-only mode): write the thread's 3 colour cotangents to
-// color_stage[threadIdx.x * 3] instead of out_sh.
+// color_stage[threadIdx.x * 3] instead of out_sh.  sh_stage (all-coefficient
+// mode): write the thread's SH gradient row to sh_stage[threadIdx.x *
+// sh_stage_stride] (16-byte aligned, shg a multiple of 4) for the block to
+// store coalesced.  Returns whether the thread's output row was produced.
 template <int DEGREE, int SH_MODE>
-__device__ __forceinline__ void project_bwd_body(
+__device__ __forceinline__ bool project_bwd_body(
     const gsb_project_bwd_params& p, const float* __restrict__ xyz,
     const float* __restrict__ log_scale, const float* __restrict__ rotation,
     const float* __restrict__ opacity, const float* __restrict__ sh, const float* view,
@@ -303,7 +306,7 @@ __device__ __forceinline__ void project_bwd_body(
     const float* __restrict__ gcolor, const float* __restrict__ galpha,
     float* __restrict__ out_xyz, float* __restrict__ out_log_scale,
     float* __restrict__ out_rotation, float* __restrict__ out_opacity, float* __restrict__ out_sh,
-    float* color_stage)
+    float* color_stage, float* sh_stage = nullptr, int sh_stage_stride = 0)
 {
     constexpr int NB = (DEGREE + 1) * (DEGREE + 1);
     int count = p.compacted ? __ldg(cluster_count) : 0;
@@ -316,16 +319,19 @@ __device__ __forceinline__ void project_bwd_body(
     if (pool_order) {
         listed = cluster_listed_warp(cluster_ids, count,
                                      (i < p.capacity ? i : p.capacity - 1) / p.cluster_size);
-        if (i >= p.capacity) return;
+        if (i >= p.capacity) return false;
         g = i;
     } else {
         g = slot_of(i, p.capacity, cluster_ids, count, p.cluster_size, p.compacted);
-        if (g < 0) return;
+        if (g < 0) return false;
     }
     const int64_t o = p.compact_gradients ? i : g;
     const int shg = SH_MODE == 1 ? 3 : p.sh_gradient_dim * 3;
-    float* osh = (SH_MODE == 1 && color_stage) ? color_stage + threadIdx.x * 3 : out_sh + o * shg;
-    const bool vec_out = (shg & 3) == 0 && (reinterpret_cast<uintptr_t>(out_sh) & 15) == 0;
+    float* osh = (SH_MODE == 1 && color_stage) ? color_stage + threadIdx.x * 3
+                 : (SH_MODE == 0 && sh_stage) ? sh_stage + threadIdx.x * sh_stage_stride
+                                              : out_sh + o * shg;
+    const bool vec_out = (SH_MODE == 0 && sh_stage) ||
+                         ((shg & 3) == 0 && (reinterpret_cast<uintptr_t>(out_sh) & 15) == 0);
 
     float2 gm = make_float2(0.f, 0.f);
     float4 gcn = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -354,7 +360,7 @@ __device__ __forceinline__ void project_bwd_body(
         } else {
             for (int k = 0; k < shg; k++) osh[k] = 0.0f;
         }
-        return;
+        return true;
     }
     Cam cam;
     load_cam(cam, view, intr, center);
@@ -525,7 +531,15 @@ __device__ __forceinline__ void project_bwd_body(
     out_xyz[o * 3] = v[0] * gx + v[4] * gy + v[8] * gz + gxw;
     out_xyz[o * 3 + 1] = v[1] * gx + v[5] * gy + v[9] * gz + gyw;
     out_xyz[o * 3 + 2] = v[2] * gx + v[6] * gy + v[10] * gz + gzw;
+    return true;
 }
+
+// Rows of SH gradients are 4 * chunks floats (chunks <= kStageChunks); a
+// block's rows are staged in shared memory with an odd float4 stride (no
+// bank conflicts for the per-thread float4 writes) and leave as consecutive
+// float4 stores of the whole block.
+constexpr int kStageChunks = 12;
+constexpr int kStageStride4 = kStageChunks + 1;
 
 template <int DEGREE, int SH_MODE>
 __global__ void __launch_bounds__(kProjThreads) project_bwd_kernel(
@@ -541,10 +555,42 @@ __global__ void __launch_bounds__(kProjThreads) project_bwd_kernel(
     float* __restrict__ out_opacity, float* __restrict__ out_sh)
 {
     pdl_begin();
-    project_bwd_body<DEGREE, SH_MODE>(p, xyz, log_scale, rotation, opacity, sh, view, intr, center,
-                                      color, cluster_ids, cluster_count, gmean, gdepth, gconic,
-                                      gradius, gcolor, galpha, out_xyz, out_log_scale,
-                                      out_rotation, out_opacity, out_sh, nullptr);
+    const int shg = p.sh_gradient_dim * 3;
+    const int chunks = shg >> 2;
+    const bool staged = SH_MODE == 0 && (shg & 3) == 0 && chunks <= kStageChunks &&
+                        (reinterpret_cast<uintptr_t>(out_sh) & 15) == 0;
+    if (!staged) {
+        project_bwd_body<DEGREE, SH_MODE>(p, xyz, log_scale, rotation, opacity, sh, view, intr,
+                                          center, color, cluster_ids, cluster_count, gmean, gdepth,
+                                          gconic, gradius, gcolor, galpha, out_xyz, out_log_scale,
+                                          out_rotation, out_opacity, out_sh, nullptr);
+        return;
+    }
+    __shared__ __align__(16) float4 stage[kProjThreads * kStageStride4];
+    __shared__ int row_count;
+    const bool wrote = project_bwd_body<DEGREE, SH_MODE>(
+        p, xyz, log_scale, rotation, opacity, sh, view, intr, center, color, cluster_ids,
+        cluster_count, gmean, gdepth, gconic, gradius, gcolor, galpha, out_xyz, out_log_scale,
+        out_rotation, out_opacity, nullptr, nullptr, reinterpret_cast<float*>(stage),
+        kStageStride4 * 4);
+    // The rows produced form a prefix of the block's slots (validity only
+    // ends at the last listed slot or the capacity).
+    if (threadIdx.x == 0) row_count = 0;
+    __syncthreads();
+    const unsigned ballot = __ballot_sync(GSB_FULL_MASK, wrote);
+    if ((threadIdx.x & 31) == 0 && ballot) atomicAdd(&row_count, __popc(ballot));
+    __syncthreads();
+    const int rows = row_count;
+    // Row r of the block is output row blockIdx.x * kProjThreads + r (the
+    // compact index, or the pool slot in pool order).
+    float4* out4 = reinterpret_cast<float4*>(out_sh) +
+                   (int64_t)blockIdx.x * kProjThreads * chunks;
+    const uint32_t magic = ((1u << 20) + chunks - 1) / chunks;  // exact for idx < 2^16
+    for (int idx = threadIdx.x; idx < rows * chunks; idx += kProjThreads) {
+        const int r = (int)(((uint32_t)idx * magic) >> 20);
+        const int k = idx - r * chunks;
+        out4[idx] = stage[r * kStageStride4 + k];
+    }
 }
 
 // Colour-only pool-order pullback fused with its all-gather: the block's 128
