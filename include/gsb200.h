@@ -47,7 +47,7 @@ enum {
     GSB_ERR_NULL = 4        /* required pointer is NULL */
 };
 
-#define GSB_ABI_VERSION 3
+#define GSB_ABI_VERSION 4
 
 /* Library ABI version (GSB_ABI_VERSION). */
 GSB_API int gsb_abi_version(void);
@@ -140,26 +140,6 @@ GSB_API int gsb_project_bwd(gsb_stream_t stream, const gsb_project_bwd_params* p
                     const float* gconic, const float* gradius, const float* gcolor,
                     const float* galpha, float* gxyz, float* glog_scale, float* grotation,
                     float* gopacity, float* gsh);
-
-/* The colour-only, pool-order pullback (sh_color_only = 1, compacted = 1,
- * compact_gradients = 0) fused with the all-gather of its colour
- * cotangents: instead of gsh, the colours and the camera centre are stored
- * through an NVLS multicast address into this rank's row of a symmetric row
- * table, row = [centre x, y, z, 0 | colours C*3 | pad], row_floats >= 4 + C*3
- * rounded up to a multiple of 4, row_multicast 16-byte aligned.  Every GPU's
- * copy of the row is written, except 16-byte chunks that are all zero (the
- * receiving copies must hold zeros there: clear them after each use); a
- * gsb_exchange_barrier afterwards publishes it.  The geometric gradients are written locally as by gsb_project_bwd.
- * No counterpart in the reference (its step sums per-view gradients with
- * one collective after the pullback). */
-GSB_API int gsb_project_bwd_colors_multicast(
-    gsb_stream_t stream, const gsb_project_bwd_params* p, const float* xyz,
-    const float* log_scale, const float* rotation, const float* opacity, const float* sh,
-    const float* view, const float* intrinsics, const float* center, const float* color,
-    const int32_t* cluster_ids, const int32_t* cluster_count, const float* gmean,
-    const float* gdepth, const float* gconic, const float* gradius, const float* gcolor,
-    const float* galpha, float* gxyz, float* glog_scale, float* grotation, float* gopacity,
-    float* row_multicast, int64_t row_floats);
 
 /* ------------------------------------------------------------------------
  * SH coefficient cotangents from colour cotangents, summed over views.
@@ -384,8 +364,14 @@ GSB_API int gsb_loss_noalloc(gsb_stream_t stream, const gsb_loss_params* p, cons
  *    aligned) over all ranks' copies through the multicast address: rank r
  *    reduces and stores shard r.  Put a barrier before (inputs written) and
  *    after (sum complete everywhere).
- *  The all-gather of the colour cotangents is fused into the pullback
- *  (gsb_project_bwd_colors_multicast).
+ *  - gsb_multicast_nonzero: the all-gather of the colour cotangents.  Each
+ *    rank's pullback (gsb_project_bwd, colour-only, pool order) writes its
+ *    row of a symmetric row table locally, row = [centre x, y, z, 0 |
+ *    colours C*3 | pad]; this call stores the row's non-zero 16-byte chunks
+ *    (count floats, a multiple of 4, both addresses 16-byte aligned)
+ *    through the multicast address of that row into every GPU's copy.  The
+ *    receiving copies must hold zeros where nothing is sent: clear them
+ *    after each use.  A gsb_exchange_barrier afterwards publishes the rows.
  * ------------------------------------------------------------------------ */
 typedef struct {
     int world;
@@ -397,6 +383,8 @@ GSB_API int gsb_exchange_barrier(gsb_stream_t stream, const gsb_exchange_params*
                          int32_t* error);
 GSB_API int gsb_nvls_allreduce(gsb_stream_t stream, const gsb_exchange_params* p, float* multicast,
                        int64_t count);
+GSB_API int gsb_multicast_nonzero(gsb_stream_t stream, const float* src, float* multicast,
+                          int64_t count);
 
 #ifdef __cplusplus
 }

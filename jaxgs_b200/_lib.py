@@ -83,7 +83,7 @@ SYMBOLS = (
     "gsb_raster_workspace_size", "gsb_raster_bit_words", "gsb_raster_fwd", "gsb_raster_bwd",
     "gsb_raster_pack", "gsb_raster_bwd_prepare",
     "gsb_loss_workspace_size", "gsb_loss", "gsb_loss_noalloc",
-    "gsb_exchange_barrier", "gsb_nvls_allreduce", "gsb_project_bwd_colors_multicast",
+    "gsb_exchange_barrier", "gsb_nvls_allreduce", "gsb_multicast_nonzero",
 )
 
 
@@ -131,15 +131,15 @@ def _load():
         getattr(lib, name).argtypes = [vp, vp] + [vp] * n
     lib.gsb_nvls_allreduce.restype = ctypes.c_int
     lib.gsb_nvls_allreduce.argtypes = [vp, vp, vp, ctypes.c_int64]
-    lib.gsb_project_bwd_colors_multicast.restype = ctypes.c_int
-    lib.gsb_project_bwd_colors_multicast.argtypes = [vp, vp] + [vp] * 22 + [ctypes.c_int64]
+    lib.gsb_multicast_nonzero.restype = ctypes.c_int
+    lib.gsb_multicast_nonzero.argtypes = [vp, vp, vp, ctypes.c_int64]
     lib.gsb_loss_noalloc.restype = ctypes.c_int
     lib.gsb_loss_noalloc.argtypes = [vp, vp] + [vp] * 5
     return lib
 
 
 lib = _load()
-if lib.gsb_abi_version() != 3:
+if lib.gsb_abi_version() != 4:
     raise RuntimeError("libgsb200.so ABI version mismatch; rebuild with `python -m jaxgs_b200.build`")
 
 

@@ -11,9 +11,11 @@
 //     16-byte chunk of it, multimem.ld_reduce makes the switch fetch and sum
 //     the chunk of every GPU, and multimem.st writes the sum into every GPU's
 //     copy.  Each GPU sends and receives about one buffer's worth of bytes.
-//   * The all-gather of the colour rows is fused into the pullback that
-//     produces them (project.cu, project_bwd_colors_multicast_kernel): each
-//     row is stored through the multicast address into every GPU's copy.
+//   * gsb_multicast_nonzero is the all-gather of the colour rows: each rank
+//     stores the non-zero 16-byte chunks of its own row (written locally by
+//     the pullback) through the multicast address into every GPU's copy.
+//     A few hundred blocks do it, each with one system-scope fence at its
+//     end, so the pullback itself never waits for NVLink acknowledgements.
 // Callers put a barrier between a producer and these collectives and after
 // them (the sum is complete on every GPU only once every shard is stored).
 // No TMA and no cluster-multicast loads are used: peers' memory is touched
@@ -90,6 +92,29 @@ __global__ void nvls_allreduce_kernel(float* mc, int64_t begin4, int64_t end4)
     if (threadIdx.x == 0) __threadfence_system();
 }
 
+// Chunks that are all zero are not sent: the receiving copies hold zeros
+// there (they are cleared after each use), and most of a view's colour
+// cotangents are zero.
+__global__ void multicast_nonzero_kernel(const float4* __restrict__ src, float* mc, int64_t n4)
+{
+    pdl_begin();
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += stride * kUnroll) {
+        float4 v[kUnroll];
+#pragma unroll
+        for (int u = 0; u < kUnroll; u++)
+            v[u] = i + u * stride < n4 ? src[i + u * stride] : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int u = 0; u < kUnroll; u++)
+            if (v[u].x != 0.0f || v[u].y != 0.0f || v[u].z != 0.0f || v[u].w != 0.0f)
+                multimem_st_v4(mc + (i + u * stride) * 4, v[u]);
+    }
+    // The stores precede the barrier that follows: one system-scope fence per
+    // block, cumulative over the block's stores through the block barrier.
+    __syncthreads();
+    if (threadIdx.x == 0) __threadfence_system();
+}
+
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 }  // namespace
@@ -125,5 +150,20 @@ extern "C" int gsb_nvls_allreduce(gsb_stream_t stream, const gsb_exchange_params
     const int64_t want = (end - begin + 256 * kUnroll - 1) / (256 * kUnroll);
     const int blocks = (int)(want < 148 * 8 ? want : 148 * 8);
     gsb::launch(nvls_allreduce_kernel, blocks, 256, 0, as_stream(stream), multicast, begin, end);
+    return check_launch();
+}
+
+extern "C" int gsb_multicast_nonzero(gsb_stream_t stream, const float* src, float* multicast,
+                                     int64_t count)
+{
+    if (count < 0 || (count & 3) != 0) return GSB_ERR_INVALID;
+    if (count == 0) return GSB_OK;
+    if (!src || !multicast) return GSB_ERR_NULL;
+    if (!aligned16(src) || !aligned16(multicast)) return GSB_ERR_INVALID;
+    const int64_t n4 = count / 4;
+    const int64_t want = (n4 + 256 * kUnroll - 1) / (256 * kUnroll);
+    const int blocks = (int)(want < 148 * 2 ? want : 148 * 2);
+    gsb::launch(multicast_nonzero_kernel, blocks, 256, 0, as_stream(stream),
+                reinterpret_cast<const float4*>(src), multicast, n4);
     return check_launch();
 }

@@ -289,9 +289,7 @@ __global__ void __launch_bounds__(kProjThreads) project_fwd_kernel(
 // SH_MODE: 0 = all sh_gradient_dim coefficients (bands above DEGREE zero),
 //          1 = colour cotangents only (sh_color_only, 3 floats per point).
 // ---------------------------------------------------------------------------
-// color_stage (colour-only mode): write the thread's 3 colour cotangents to
-// color_stage[threadIdx.x * 3] instead of out_sh.  sh_stage (all-coefficient
-// mode): write the thread's SH gradient row to sh_stage[threadIdx.x *
+// sh_stage (all-coefficient mode): write the thread's SH gradient row to sh_stage[threadIdx.x *
 // sh_stage_stride] (16-byte aligned, shg a multiple of 4) for the block to
 // store coalesced.  Returns whether the thread's output row was produced.
 template <int DEGREE, int SH_MODE>
@@ -306,7 +304,7 @@ __device__ __forceinline__ bool project_bwd_body(
     const float* __restrict__ gcolor, const float* __restrict__ galpha,
     float* __restrict__ out_xyz, float* __restrict__ out_log_scale,
     float* __restrict__ out_rotation, float* __restrict__ out_opacity, float* __restrict__ out_sh,
-    float* color_stage, float* sh_stage = nullptr, int sh_stage_stride = 0)
+    float* sh_stage = nullptr, int sh_stage_stride = 0)
 {
     constexpr int NB = (DEGREE + 1) * (DEGREE + 1);
     int count = p.compacted ? __ldg(cluster_count) : 0;
@@ -327,9 +325,8 @@ __device__ __forceinline__ bool project_bwd_body(
     }
     const int64_t o = p.compact_gradients ? i : g;
     const int shg = SH_MODE == 1 ? 3 : p.sh_gradient_dim * 3;
-    float* osh = (SH_MODE == 1 && color_stage) ? color_stage + threadIdx.x * 3
-                 : (SH_MODE == 0 && sh_stage) ? sh_stage + threadIdx.x * sh_stage_stride
-                                              : out_sh + o * shg;
+    float* osh = (SH_MODE == 0 && sh_stage) ? sh_stage + threadIdx.x * sh_stage_stride
+                                            : out_sh + o * shg;
     const bool vec_out = (SH_MODE == 0 && sh_stage) ||
                          ((shg & 3) == 0 && (reinterpret_cast<uintptr_t>(out_sh) & 15) == 0);
 
@@ -563,7 +560,7 @@ __global__ void __launch_bounds__(kProjThreads) project_bwd_kernel(
         project_bwd_body<DEGREE, SH_MODE>(p, xyz, log_scale, rotation, opacity, sh, view, intr,
                                           center, color, cluster_ids, cluster_count, gmean, gdepth,
                                           gconic, gradius, gcolor, galpha, out_xyz, out_log_scale,
-                                          out_rotation, out_opacity, out_sh, nullptr);
+                                          out_rotation, out_opacity, out_sh);
         return;
     }
     __shared__ __align__(16) float4 stage[kProjThreads * kStageStride4];
@@ -571,7 +568,7 @@ __global__ void __launch_bounds__(kProjThreads) project_bwd_kernel(
     const bool wrote = project_bwd_body<DEGREE, SH_MODE>(
         p, xyz, log_scale, rotation, opacity, sh, view, intr, center, color, cluster_ids,
         cluster_count, gmean, gdepth, gconic, gradius, gcolor, galpha, out_xyz, out_log_scale,
-        out_rotation, out_opacity, nullptr, nullptr, reinterpret_cast<float*>(stage),
+        out_rotation, out_opacity, nullptr, reinterpret_cast<float*>(stage),
         kStageStride4 * 4);
     // The rows produced form a prefix of the block's slots (validity only
     // ends at the last listed slot or the capacity).
@@ -591,52 +588,6 @@ __global__ void __launch_bounds__(kProjThreads) project_bwd_kernel(
         const int k = idx - r * chunks;
         out4[idx] = stage[r * kStageStride4 + k];
     }
-}
-
-// Colour-only pool-order pullback fused with its all-gather: the block's 128
-// consecutive slots' colour cotangents are staged in shared memory and
-// stored, 16 bytes per store, through the multicast address of this rank's
-// row of the symmetric row table (row = [centre x, y, z, 0 | colours C*3 |
-// pad]); block 0 also stores the camera centre.  Every GPU's copy of the row
-// is written while the block's other work proceeds; a cross-GPU barrier
-// after the kernel publishes it.
-template <int DEGREE>
-__global__ void __launch_bounds__(kProjThreads) project_bwd_colors_multicast_kernel(
-    gsb_project_bwd_params p, const float* __restrict__ xyz, const float* __restrict__ log_scale,
-    const float* __restrict__ rotation, const float* __restrict__ opacity,
-    const float* __restrict__ sh, const float* view, const float* intr, const float* center,
-    const float* __restrict__ color, const int32_t* __restrict__ cluster_ids,
-    const int32_t* __restrict__ cluster_count, const float* __restrict__ gmean,
-    const float* __restrict__ gdepth, const float* __restrict__ gconic,
-    const float* __restrict__ gradius, const float* __restrict__ gcolor,
-    const float* __restrict__ galpha, float* __restrict__ out_xyz,
-    float* __restrict__ out_log_scale, float* __restrict__ out_rotation,
-    float* __restrict__ out_opacity, float* row_multicast, int64_t row_floats)
-{
-    pdl_begin();
-    __shared__ __align__(16) float stage[kProjThreads * 3];
-    stage[threadIdx.x * 3] = stage[threadIdx.x * 3 + 1] = stage[threadIdx.x * 3 + 2] = 0.0f;
-    project_bwd_body<DEGREE, 1>(p, xyz, log_scale, rotation, opacity, sh, view, intr, center,
-                                color, cluster_ids, cluster_count, gmean, gdepth, gconic, gradius,
-                                gcolor, galpha, out_xyz, out_log_scale, out_rotation, out_opacity,
-                                nullptr, stage);
-    __syncthreads();
-    // Chunks of zeros are not sent: the receiving tables are zeroed after
-    // every exchange, and most Gaussians of a view have no colour cotangent.
-    constexpr int kVec = kProjThreads * 3 / 4;
-    if (threadIdx.x < kVec) {
-        const int64_t off = 4 + (int64_t)blockIdx.x * kProjThreads * 3 + threadIdx.x * 4;
-        const float4 v = reinterpret_cast<const float4*>(stage)[threadIdx.x];
-        if (off + 4 <= row_floats && (v.x != 0.0f || v.y != 0.0f || v.z != 0.0f || v.w != 0.0f))
-            multimem_st_v4(row_multicast + off, v);
-    }
-    if (blockIdx.x == 0 && threadIdx.x == 0)
-        multimem_st_v4(row_multicast, make_float4(__ldg(center), __ldg(center + 1),
-                                                  __ldg(center + 2), 0.0f));
-    // One system-scope fence per block, after the block's stores (the block
-    // barrier makes the fence cumulative over them).
-    __syncthreads();
-    if (threadIdx.x == 0) __threadfence_system();
 }
 
 // training/sh_pullback.py:18-53 summed over views: the SH coefficient
@@ -940,47 +891,5 @@ extern "C" int gsb_sh_from_colors(gsb_stream_t stream, const gsb_sh_params* p, c
         default: GSB_SH_FROM_COLORS(3); break;
     }
 #undef GSB_SH_FROM_COLORS
-    return check_launch();
-}
-
-extern "C" int gsb_project_bwd_colors_multicast(
-    gsb_stream_t stream, const gsb_project_bwd_params* p, const float* xyz,
-    const float* log_scale, const float* rotation, const float* opacity, const float* sh,
-    const float* view, const float* intrinsics, const float* center, const float* color,
-    const int32_t* cluster_ids, const int32_t* cluster_count, const float* gmean,
-    const float* gdepth, const float* gconic, const float* gradius, const float* gcolor,
-    const float* galpha, float* gxyz, float* glog_scale, float* grotation, float* gopacity,
-    float* row_multicast, int64_t row_floats)
-{
-    if (!p) return GSB_ERR_NULL;
-    if (p->capacity < 0 || p->sh_dim < 1 || p->degree < 0 || p->degree > 3 ||
-        (p->degree + 1) * (p->degree + 1) > p->sh_dim || p->cluster_size <= 0 ||
-        !p->sh_color_only || p->sh_gradient_dim != 1 || !p->compacted || p->compact_gradients ||
-        row_floats < 4 + 3 * (int64_t)p->capacity || (row_floats & 3) != 0)
-        return GSB_ERR_INVALID;
-    if (p->capacity == 0) return GSB_OK;
-    if (!xyz || !log_scale || !rotation || !opacity || !sh || !view || !intrinsics || !center ||
-        !color || !gmean || !gconic || !gcolor || !galpha || !gxyz || !glog_scale ||
-        !grotation || !gopacity || !row_multicast || !cluster_ids || !cluster_count)
-        return GSB_ERR_NULL;
-    if (!p->rgb_only && (!gdepth || !gradius)) return GSB_ERR_NULL;
-    if ((reinterpret_cast<uintptr_t>(rotation) | reinterpret_cast<uintptr_t>(gconic) |
-         reinterpret_cast<uintptr_t>(grotation) | reinterpret_cast<uintptr_t>(gmean) |
-         reinterpret_cast<uintptr_t>(row_multicast)) & 15)
-        return GSB_ERR_INVALID;
-    cudaStream_t s = as_stream(stream);
-    const int blocks = ceil_div(p->capacity, kProjThreads);
-#define GSB_PROJ_BWD_MC(D)                                                                         \
-    gsb::launch(project_bwd_colors_multicast_kernel<D>, blocks, kProjThreads, 0, s,                         \
-        *p, xyz, log_scale, rotation, opacity, sh, view, intrinsics, center, color, cluster_ids,   \
-        cluster_count, gmean, gdepth, gconic, gradius, gcolor, galpha, gxyz, glog_scale,           \
-        grotation, gopacity, row_multicast, row_floats)
-    switch (p->degree) {
-        case 0: GSB_PROJ_BWD_MC(0); break;
-        case 1: GSB_PROJ_BWD_MC(1); break;
-        case 2: GSB_PROJ_BWD_MC(2); break;
-        default: GSB_PROJ_BWD_MC(3); break;
-    }
-#undef GSB_PROJ_BWD_MC
     return check_launch();
 }

@@ -147,16 +147,12 @@ def compute_projection_gradients(parameters, camera: DeviceCamera, projected_col
                                  active_degree: int | None, visible_clusters,
                                  compact_gradients: bool, rgb_only: bool = False,
                                  active_sh_only: bool = False, sh_color_only: bool = False,
-                                 out=None, color_multicast=None):
+                                 out=None):
     """kernels/projector.py:240-307: parameter gradients from cotangents.
 
     out: optional (xyz, log_scale, rotation, opacity, sh) gradient tensors to
     write (contiguous float32 of the output shapes), e.g. views of one flat
-    buffer that a collective reduces in place.
-    color_multicast: (multicast address, row floats) of this rank's row of a
-    symmetric row table; the colour-only pool-order cotangents and the camera
-    centre are then stored there, into every GPU's copy
-    (gsb_project_bwd_colors_multicast), and out's sh entry is unused."""
+    buffer that a collective reduces in place."""
     xyz, log_scale, rotation, opacity, sh = parameters
     _require_cuda(xyz, "projection pullback")
     C = config.max_gaussians
@@ -165,10 +161,6 @@ def compute_projection_gradients(parameters, camera: DeviceCamera, projected_col
     shg = 1 if sh_color_only else ((degree + 1) ** 2 if active_sh_only else sh_dim)
     dev = xyz.device
     shapes = ((C, 3), (C, 3), (C, 4), (C, 1), (C, shg, 3))
-    if color_multicast is not None:
-        if not (sh_color_only and visible_clusters is not None and not compact_gradients):
-            raise ValueError("color_multicast needs the colour-only, pool-order pullback")
-        shapes = shapes[:4]
     if out is None:
         out = [torch.empty(shape, dtype=_f32, device=dev) for shape in shapes]
     else:
@@ -180,7 +172,6 @@ def compute_projection_gradients(parameters, camera: DeviceCamera, projected_col
     p = L.ProjectBwdParams(C, sh_dim, shg, degree, camera.near, config.cluster_size,
                            int(visible_clusters is not None), int(compact_gradients),
                            int(rgb_only), int(sh_color_only))
-    zeros = None
     gdepth, gradius = cotangents.depth, cotangents.radius
     if rgb_only:
         gdepth = gradius = None
@@ -194,14 +185,7 @@ def compute_projection_gradients(parameters, camera: DeviceCamera, projected_col
             _ptr(_c(cotangents.conic, _f32)), _ptr(None if gradius is None else _c(gradius, _f32)),
             _ptr(_c(cotangents.color, _f32)), _ptr(_c(cotangents.alpha, _f32)),
             *[_ptr(o) for o in out])
-    if color_multicast is not None:
-        address, row_floats = color_multicast
-        L.check(L.lib.gsb_project_bwd_colors_multicast(*args, ctypes.c_void_p(address),
-                                                       int(row_floats)),
-                "projection pullback (colour multicast)")
-        return tuple(out) + (None,)
     L.check(L.lib.gsb_project_bwd(*args), "projection pullback")
-    del zeros
     return tuple(out)
 
 
@@ -251,15 +235,13 @@ def project_with_compact_pullback(pool: GaussianArrays, camera: DeviceCamera,
     parameters = (pool.xyz, pool.log_scale, pool.rotation, pool.opacity, pool.sh)
     projected = _project(pool, camera, config, active_degree, clusters, False, visible_color_only)
 
-    def pullback(cotangents: ProjectedGaussians, out=None, compact: bool = True,
-                 color_multicast=None):
+    def pullback(cotangents: ProjectedGaussians, out=None, compact: bool = True):
         """Gradients in visible-cluster order, or (compact=False) in pool
-        order with the unlisted clusters' rows zeroed; out and
-        color_multicast as in compute_projection_gradients."""
+        order with the unlisted clusters' rows zeroed; out as in
+        compute_projection_gradients."""
         return compute_projection_gradients(parameters, camera, projected.color, cotangents,
                                             config, active_degree, clusters, compact, rgb_only,
-                                            active_sh_only, sh_color_only, out=out,
-                                            color_multicast=color_multicast)
+                                            active_sh_only, sh_color_only, out=out)
 
     return projected, pullback
 

@@ -57,8 +57,7 @@ def compute_training_step(pool: GaussianArrays, bounds, camera: DeviceCamera, ta
                           config: CapacityConfig, active_degree: int, *,
                           active_sh_only: bool = True, sh_color_only: bool = False,
                           keep_image: bool = False, stage_events: dict | None = None,
-                          overlap: bool = True, pool_grads=None,
-                          color_multicast=None, collect_stats: bool = False,
+                          overlap: bool = True, pool_grads=None, collect_stats: bool = False,
                           stats: torch.Tensor | None = None) -> StepOutput:
     """training/step.py:32-89 without the optimizer update.
 
@@ -75,9 +74,6 @@ def compute_training_step(pool: GaussianArrays, bounds, camera: DeviceCamera, ta
     pool_grads: optional (xyz, log_scale, rotation, opacity, sh) tensors; the
     gradients are then written there in pool order (rows of culled clusters
     zero), ready to be summed across view-sharded ranks in place.
-    color_multicast: with sh_color_only and pool_grads, the colour cotangents
-    (and the camera centre) go to this (multicast address, row floats) row
-    instead (NvlsExchange).
     collect_stats: also gather this view's [C, 4] fragment statistics (count,
     compositing weight, alpha cotangent, squared opacity cotangent); with
     stats given they are added into it in place (step.py:125-126,
@@ -145,8 +141,7 @@ def compute_training_step(pool: GaussianArrays, bounds, camera: DeviceCamera, ta
             fragment_stats = stats.add_(fragment_stats)
     done(ev)
     ev = mark("project_bwd")
-    grads = (pullback(cot) if pool_grads is None else
-             pullback(cot, out=pool_grads, compact=False, color_multicast=color_multicast))
+    grads = pullback(cot) if pool_grads is None else pullback(cot, out=pool_grads, compact=False)
     done(ev)
     return StepOutput(loss, grads, clusters, table.pair_count, table.overflow,
                       table.point_counts, result.rgb if keep_image else None, fragment_stats)
@@ -233,19 +228,21 @@ class ViewShardedExchange:
 class NvlsExchange:
     """ViewShardedExchange's sum with collectives written for NVLink /
     NVSwitch multicast (include/gsb200.h, gsb_exchange_barrier,
-    gsb_nvls_allreduce, gsb_project_bwd_colors_multicast).
+    gsb_nvls_allreduce, gsb_multicast_nonzero).
 
-    The geometric gradients live in symmetric memory.  The step's pullback
-    stores each rank's colour cotangents and camera centre straight into row
-    r of every GPU's copy of a symmetric row table (the all-gather is part of
-    the kernel that produces them; all-zero chunks, most of a view, are not
-    sent, and each rank clears its table after use).  exchange() then passes a cross-GPU
+    The geometric gradients and a table of colour rows live in symmetric
+    memory.  The step's pullback writes the geometric gradients and this
+    rank's colour cotangents (row r of the table: [camera centre | pad |
+    colours]) locally.  exchange() stores the camera centre into the row,
+    pushes the row's non-zero 16-byte chunks (most of a view is zero)
+    through the multicast address into every GPU's copy, passes a cross-GPU
     barrier, sums shard r of the geometric gradients in the switch
     (multimem.ld_reduce) and stores the sum into every copy (multimem.st)
     while a second stream expands the gathered colours into the summed SH
-    gradients, and passes a second barrier.  No NCCL call is made per step
-    and every launch can be captured in a CUDA graph.  Build it only when
-    NvlsExchange.available(group) says the GPUs share multicast.
+    gradients and clears the table, and passes a second barrier.  No NCCL
+    call is made per step and every launch can be captured in a CUDA graph.
+    Build it only when NvlsExchange.available(group) says the GPUs share
+    multicast.
     """
 
     @staticmethod
@@ -303,9 +300,11 @@ class NvlsExchange:
         for n, shape in ((C * 3, (C, 3)), (C * 3, (C, 3)), (C * 4, (C, 4)), (C, (C, 1))):
             views.append(self.geometric[at:at + n].view(shape))
             at += n
-        self.pool_grads = (*views, None)
-        self.step_kwargs = dict(pool_grads=self.pool_grads, sh_color_only=True,
-                                color_multicast=(self.mc_row, self.row_floats))
+        # The pullback's colour-only output [C, 1, 3] is this rank's row.
+        self.own_row = self.rows[self.rank]
+        colours = self.own_row[4:4 + C * 3].view(C, 1, 3)
+        self.pool_grads = (*views, colours)
+        self.step_kwargs = dict(pool_grads=self.pool_grads, sh_color_only=True)
         self.side = torch.cuda.Stream(device=dev)
         torch.cuda.synchronize(dev)
         dist.barrier(group)
@@ -323,12 +322,19 @@ class NvlsExchange:
     def exchange(self, camera_center: torch.Tensor | None = None):
         """Sum the ranks' gradients after a step run with step_kwargs;
         returns (xyz, log_scale, rotation, opacity, sh) in pool order,
-        identical on every rank.  (The camera centre travels with the
-        colour row, so camera_center is not needed.)"""
+        identical on every rank.  camera_center: this rank's camera centre
+        [3] on the device (it travels with the colour row)."""
         import ctypes
 
         L = self.L
         main = torch.cuda.current_stream()
+        if camera_center is None:
+            raise ValueError("NvlsExchange.exchange needs this rank's camera centre")
+        self.own_row[:3].copy_(camera_center.reshape(3))
+        L.check(L.lib.gsb_multicast_nonzero(ctypes.c_void_p(main.cuda_stream),
+                                            ctypes.c_void_p(self.own_row.data_ptr()),
+                                            ctypes.c_void_p(self.mc_row), self.row_floats),
+                "colour row all-gather")
         self._barrier()
         self.side.wait_stream(main)
         L.check(L.lib.gsb_nvls_allreduce(ctypes.c_void_p(main.cuda_stream), L.ref(self.params),
@@ -383,7 +389,7 @@ class GraphedTrainingStep:
     def __init__(self, pool: GaussianArrays, bounds, camera: DeviceCamera, target: torch.Tensor,
                  config: CapacityConfig, active_degree: int, *, active_sh_only: bool = True,
                  sh_color_only: bool = False, warmup: int = 2, pool_grads=None,
-                 color_multicast=None, collect_stats: bool = False,
+                 collect_stats: bool = False,
                  stats: torch.Tensor | None = None):
         dev = pool.xyz.device
         self.camera = DeviceCamera(camera.world_to_camera.clone(), camera.intrinsics.clone(),
@@ -393,8 +399,7 @@ class GraphedTrainingStep:
         self.target.copy_(target)
         args = (pool, bounds, self.camera, self.target, config, active_degree)
         kwargs = dict(active_sh_only=active_sh_only, sh_color_only=sh_color_only,
-                      pool_grads=pool_grads, color_multicast=color_multicast,
-                      collect_stats=collect_stats)
+                      pool_grads=pool_grads, collect_stats=collect_stats)
         side = torch.cuda.Stream(device=dev)
         side.wait_stream(torch.cuda.current_stream(dev))
         with torch.cuda.stream(side):
