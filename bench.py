@@ -187,7 +187,12 @@ def run_ours(args) -> None:
     exch = None
     if world > 1:
         use_nvls = os.environ.get("GSB_EXCHANGE", "nvls") == "nvls" and NvlsExchange.available()
-        exch = (NvlsExchange if use_nvls else ViewShardedExchange)(pool, config, degree)
+        if use_nvls:
+            # GSB_ALLREDUCE: "p2p" (default) or "nvls" sum of the geometric gradients.
+            exch = NvlsExchange(pool, config, degree,
+                                allreduce=os.environ.get("GSB_ALLREDUCE", "p2p"))
+        else:
+            exch = ViewShardedExchange(pool, config, degree)
     sharded = exch.step_kwargs if exch is not None else {}
     stream = torch.cuda.current_stream()
     stage_events = []
@@ -300,7 +305,7 @@ def run_ours(args) -> None:
                        "l2": "inputs larger than L2 (236 MB pool)",
                        "launch": "CUDA graph replay of the whole step",
                        "parallelism": f"view-sharded dp{world}" if world > 1 else "single view",
-                       "exchange": (f"per step: {'NVLS multicast (own kernels)' if isinstance(exch, NvlsExchange) else 'NCCL'} "
+                       "exchange": (f"per step: {('own kernels: %s all-reduce, NVLS multicast all-gather' % exch.allreduce.upper()) if isinstance(exch, NvlsExchange) else 'NCCL'} "
                                     f"all-reduce of {exch.geometric.numel() * 4 / 1e6:.0f} MB "
                                     f"geometric gradients, all-gather of {config.max_gaussians * 12 / 1e6:.0f} MB "
                                     "colour cotangents per rank, SH expansion of all views")

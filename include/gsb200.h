@@ -364,6 +364,11 @@ GSB_API int gsb_loss_noalloc(gsb_stream_t stream, const gsb_loss_params* p, cons
  *    aligned) over all ranks' copies through the multicast address: rank r
  *    reduces and stores shard r.  Put a barrier before (inputs written) and
  *    after (sum complete everywhere).
+ *  - gsb_p2p_allreduce: gsb_nvls_allreduce with plain peer loads and
+ *    stores instead of the multicast object: buffers[q] is rank q's copy
+ *    (host array of world <= 8 device pointers, each 16-byte aligned); rank
+ *    r reads shard r of every copy, adds them in rank order and stores the
+ *    sum into shard r of every copy.  Same barriers before and after.
  *  - gsb_multicast_nonzero: the all-gather of the colour cotangents.  Each
  *    rank's pullback (gsb_project_bwd, colour-only, pool order) writes its
  *    row of a symmetric row table locally, row = [centre x, y, z, 0 |
@@ -385,6 +390,8 @@ GSB_API int gsb_nvls_allreduce(gsb_stream_t stream, const gsb_exchange_params* p
                        int64_t count);
 GSB_API int gsb_multicast_nonzero(gsb_stream_t stream, const float* src, float* multicast,
                           int64_t count);
+GSB_API int gsb_p2p_allreduce(gsb_stream_t stream, const gsb_exchange_params* p,
+                      float* const* buffers, int64_t count);
 
 #ifdef __cplusplus
 }

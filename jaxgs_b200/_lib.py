@@ -83,7 +83,7 @@ SYMBOLS = (
     "gsb_raster_workspace_size", "gsb_raster_bit_words", "gsb_raster_fwd", "gsb_raster_bwd",
     "gsb_raster_pack", "gsb_raster_bwd_prepare",
     "gsb_loss_workspace_size", "gsb_loss", "gsb_loss_noalloc",
-    "gsb_exchange_barrier", "gsb_nvls_allreduce", "gsb_multicast_nonzero",
+    "gsb_exchange_barrier", "gsb_nvls_allreduce", "gsb_multicast_nonzero", "gsb_p2p_allreduce",
 )
 
 
@@ -133,6 +133,8 @@ def _load():
     lib.gsb_nvls_allreduce.argtypes = [vp, vp, vp, ctypes.c_int64]
     lib.gsb_multicast_nonzero.restype = ctypes.c_int
     lib.gsb_multicast_nonzero.argtypes = [vp, vp, vp, ctypes.c_int64]
+    lib.gsb_p2p_allreduce.restype = ctypes.c_int
+    lib.gsb_p2p_allreduce.argtypes = [vp, vp, vp, ctypes.c_int64]
     lib.gsb_loss_noalloc.restype = ctypes.c_int
     lib.gsb_loss_noalloc.argtypes = [vp, vp] + [vp] * 5
     return lib

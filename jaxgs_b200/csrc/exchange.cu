@@ -16,6 +16,12 @@
 //     the pullback) through the multicast address into every GPU's copy.
 //     A few hundred blocks do it, each with one system-scope fence at its
 //     end, so the pullback itself never waits for NVLink acknowledgements.
+//   * gsb_p2p_allreduce: the same sum with plain peer loads and stores: rank
+//     r reads shard r of every rank's buffer (its own locally), adds them in
+//     rank order and stores the sum into shard r of every buffer.  Each GPU
+//     moves (world - 1) / world of the buffer in each direction, about what
+//     the switch-reduced form moves, with ordinary loads that keep many
+//     requests in flight.
 // Callers put a barrier between a producer and these collectives and after
 // them (the sum is complete on every GPU only once every shard is stored).
 // No TMA and no cluster-multicast loads are used: peers' memory is touched
@@ -115,6 +121,50 @@ __global__ void multicast_nonzero_kernel(const float4* __restrict__ src, float* 
     if (threadIdx.x == 0) __threadfence_system();
 }
 
+constexpr int kMaxPeers = 8;
+struct PeerBuffers {
+    float* p[kMaxPeers];
+};
+constexpr int kP2PUnroll = 2;
+
+__global__ void p2p_allreduce_kernel(PeerBuffers peers, int world, int64_t begin4, int64_t end4)
+{
+    pdl_begin();
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i = begin4 + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < end4;
+         i += stride * kP2PUnroll) {
+        float4 v[kMaxPeers][kP2PUnroll];
+        // Every load of the chunk is issued before the first add; .cv loads
+        // fetch the peers' data afresh (written before the barrier).
+#pragma unroll
+        for (int q = 0; q < kMaxPeers; q++)
+#pragma unroll
+            for (int u = 0; u < kP2PUnroll; u++)
+                if (q < world && i + u * stride < end4)
+                    v[q][u] = __ldcv(reinterpret_cast<const float4*>(peers.p[q]) + i + u * stride);
+#pragma unroll
+        for (int u = 0; u < kP2PUnroll; u++) {
+            if (i + u * stride >= end4) continue;
+            float4 acc = v[0][u];
+#pragma unroll
+            for (int q = 1; q < kMaxPeers; q++) {
+                if (q < world) {
+                    acc.x += v[q][u].x;
+                    acc.y += v[q][u].y;
+                    acc.z += v[q][u].z;
+                    acc.w += v[q][u].w;
+                }
+            }
+#pragma unroll
+            for (int q = 0; q < kMaxPeers; q++)
+                if (q < world) reinterpret_cast<float4*>(peers.p[q])[i + u * stride] = acc;
+        }
+    }
+    // The remote stores precede the barrier that follows.
+    __syncthreads();
+    if (threadIdx.x == 0) __threadfence_system();
+}
+
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 }  // namespace
@@ -165,5 +215,30 @@ extern "C" int gsb_multicast_nonzero(gsb_stream_t stream, const float* src, floa
     const int blocks = (int)(want < 148 * 2 ? want : 148 * 2);
     gsb::launch(multicast_nonzero_kernel, blocks, 256, 0, as_stream(stream),
                 reinterpret_cast<const float4*>(src), multicast, n4);
+    return check_launch();
+}
+
+extern "C" int gsb_p2p_allreduce(gsb_stream_t stream, const gsb_exchange_params* p,
+                                 float* const* buffers, int64_t count)
+{
+    if (!p) return GSB_ERR_NULL;
+    if (p->world < 1 || p->world > kMaxPeers || p->rank < 0 || p->rank >= p->world || count < 0 ||
+        (count & 3) != 0)
+        return GSB_ERR_INVALID;
+    if (!buffers) return GSB_ERR_NULL;
+    PeerBuffers peers{};
+    for (int q = 0; q < p->world; q++) {
+        if (!buffers[q]) return GSB_ERR_NULL;
+        if (!aligned16(buffers[q])) return GSB_ERR_INVALID;
+        peers.p[q] = buffers[q];
+    }
+    const int64_t n4 = count / 4;
+    const int64_t per = (n4 + p->world - 1) / p->world;
+    const int64_t begin = per * p->rank, end = begin + per < n4 ? begin + per : n4;
+    if (begin >= end) return GSB_OK;
+    const int64_t want = (end - begin + 256 * kP2PUnroll - 1) / (256 * kP2PUnroll);
+    const int blocks = (int)(want < 148 * 4 ? want : 148 * 4);
+    gsb::launch(p2p_allreduce_kernel, blocks, 256, 0, as_stream(stream), peers, p->world, begin,
+                end);
     return check_launch();
 }

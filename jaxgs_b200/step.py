@@ -236,9 +236,10 @@ class NvlsExchange:
     colours]) locally.  exchange() stores the camera centre into the row,
     pushes the row's non-zero 16-byte chunks (most of a view is zero)
     through the multicast address into every GPU's copy, passes a cross-GPU
-    barrier, sums shard r of the geometric gradients in the switch
-    (multimem.ld_reduce) and stores the sum into every copy (multimem.st)
-    while a second stream expands the gathered colours into the summed SH
+    barrier, sums shard r of the geometric gradients (allreduce="p2p": peer
+    loads of every copy's shard r, added in rank order, stored into every
+    copy; "nvls": multimem.ld_reduce in the switch and multimem.st) while a
+    second stream expands the gathered colours into the summed SH
     gradients and clears the table, and passes a second barrier.  No NCCL
     call is made per step and every launch can be captured in a CUDA graph.
     Build it only when NvlsExchange.available(group) says the GPUs share
@@ -258,7 +259,9 @@ class NvlsExchange:
             return False
 
     def __init__(self, pool: GaussianArrays, config: CapacityConfig, active_degree: int,
-                 group=None, active_sh_only: bool = True):
+                 group=None, active_sh_only: bool = True, allreduce: str = "p2p"):
+        import ctypes
+
         import torch.distributed as dist
         import torch.distributed._symmetric_memory as symm_mem
 
@@ -290,6 +293,12 @@ class NvlsExchange:
             raise RuntimeError("NVLS multicast is not available for this group")
         self._handles = (h_geo, h_tab, h_flags)
         self.mc_geo = int(h_geo.multicast_ptr)
+        # allreduce: "p2p" (plain peer loads/stores, up to 8 ranks) or "nvls"
+        # (multimem reduction in the switch).
+        if allreduce not in ("p2p", "nvls"):
+            raise ValueError("allreduce must be 'p2p' or 'nvls'")
+        self.allreduce = "nvls" if self.world > 8 else allreduce
+        self.geo_peers = (ctypes.c_void_p * self.world)(*[int(x) for x in h_geo.buffer_ptrs])
         self.mc_row = int(h_tab.multicast_ptr) + self.rank * self.row_floats * 4
         self.peer_flags = torch.tensor(list(h_flags.buffer_ptrs), dtype=torch.int64, device=dev)
         self.epoch = torch.zeros(1, dtype=torch.int32, device=dev)
@@ -337,12 +346,16 @@ class NvlsExchange:
                 "colour row all-gather")
         self._barrier()
         self.side.wait_stream(main)
-        L.check(L.lib.gsb_nvls_allreduce(ctypes.c_void_p(main.cuda_stream), L.ref(self.params),
-                                         ctypes.c_void_p(self.mc_geo), self.geo_count),
-                "NVLS all-reduce")
+        if self.allreduce == "p2p":
+            L.check(L.lib.gsb_p2p_allreduce(ctypes.c_void_p(main.cuda_stream), L.ref(self.params),
+                                            self.geo_peers, self.geo_count), "P2P all-reduce")
+        else:
+            L.check(L.lib.gsb_nvls_allreduce(ctypes.c_void_p(main.cuda_stream),
+                                             L.ref(self.params), ctypes.c_void_p(self.mc_geo),
+                                             self.geo_count), "NVLS all-reduce")
         with torch.cuda.stream(self.side):
             K.sh_from_colors(self.xyz, None, self.rows, self.degree, self.sh_dim, out=self.sh)
-            # The pullback skips all-zero chunks, so the table must be zero
+            # The all-gather skips all-zero chunks, so the table must be zero
             # before the next step's rows arrive (they come after the next
             # barrier, which this rank reaches only after clearing).
             self.table.zero_()

@@ -1,6 +1,6 @@
 """View-sharded step on two GPUs (one rank per GPU): the gradients that the
 exchange (ViewShardedExchange over NCCL, or NvlsExchange with this library's
-NVLS multicast collectives) leaves on every rank equal the single-process
+collectives, its all-reduce in the switch or by peer loads and stores) leaves on every rank equal the single-process
 sum of the two views' full gradients, over several steps in a row.  Skipped
 with fewer than two GPUs (NvlsExchange also without multicast support)."""
 
@@ -46,18 +46,22 @@ def _rank(rank, world, port, path, kind):
                             timeout=datetime.timedelta(seconds=60), device_id=device)
     try:
         pool, bounds, cams, target, config = _setup(device)
-        if kind == "nvls" and not NvlsExchange.available():
+        nvls = kind != "nccl"
+        if nvls and not NvlsExchange.available():
             if rank == 0:
                 np.savez(path, skipped=np.ones(1))
             return
-        exch = (NvlsExchange if kind == "nvls" else ViewShardedExchange)(pool, config, 3)
+        if nvls:
+            exch = NvlsExchange(pool, config, 3, allreduce=kind)
+        else:
+            exch = ViewShardedExchange(pool, config, 3)
         step = GraphedTrainingStep(pool, bounds, cams[rank], target, config, 3,
                                    **exch.step_kwargs)
         for _ in range(3):  # reused buffers: every step must give the same sum
             step()
             grads = exch.exchange(step.camera.center)
         torch.cuda.synchronize()
-        if kind == "nvls":
+        if nvls:
             assert not exch.failed()
         if rank == 0:
             np.savez(path, *[g.cpu().numpy() for g in grads])
@@ -68,7 +72,7 @@ def _rank(rank, world, port, path, kind):
 
 
 @pytest.mark.timeout(600)
-@pytest.mark.parametrize("kind", ["nccl", "nvls"])
+@pytest.mark.parametrize("kind", ["nccl", "nvls", "p2p"])
 def test_two_rank_view_sharded_gradients(kind):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
