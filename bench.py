@@ -188,9 +188,9 @@ def run_ours(args) -> None:
     if world > 1:
         use_nvls = os.environ.get("GSB_EXCHANGE", "nvls") == "nvls" and NvlsExchange.available()
         if use_nvls:
-            # GSB_ALLREDUCE: "p2p" (default) or "nvls" sum of the geometric gradients.
+            # GSB_ALLREDUCE: "auto" (default), "p2p" or "nvls" sum of the geometric gradients.
             exch = NvlsExchange(pool, config, degree,
-                                allreduce=os.environ.get("GSB_ALLREDUCE", "p2p"))
+                                allreduce=os.environ.get("GSB_ALLREDUCE", "auto"))
         else:
             exch = ViewShardedExchange(pool, config, degree)
     sharded = exch.step_kwargs if exch is not None else {}
@@ -233,8 +233,14 @@ def run_ours(args) -> None:
     binned = int((out.point_counts > 0).sum().item())
 
     # The product step: captured once as a CUDA graph, replayed per view.
-    graphed = GraphedTrainingStep(pool, bounds, dcam, target, config, degree, **sharded)
+    # NvlsExchange's launches are captured into the step's graph as well.
+    captured = isinstance(exch, NvlsExchange)
+    graphed = GraphedTrainingStep(pool, bounds, dcam, target, config, degree, **sharded,
+                                  exchange=exch if captured else None)
     current_center[0] = graphed.camera.center
+    if captured:
+        def exchange(out):
+            return None
     for _ in range(max(args.warmup, 0)):
         out = graphed()
         exchange(out)

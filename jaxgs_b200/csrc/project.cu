@@ -606,45 +606,61 @@ __global__ void __launch_bounds__(kProjThreads) sh_from_colors_kernel(
     pdl_begin();
     constexpr int NB = (DEGREE + 1) * (DEGREE + 1);
     const int64_t g = (int64_t)blockIdx.x * kProjThreads + threadIdx.x;
-    if (g >= capacity) return;
-    const float wx = xyz[g * 3], wy = xyz[g * 3 + 1], wz = xyz[g * 3 + 2];
+    const bool active = g < capacity;
     float acc[NB * 3];
 #pragma unroll
     for (int c = 0; c < NB * 3; c++) acc[c] = 0.0f;
-    for (int v = 0; v < views; v++) {
-        const float* col = colors + v * view_stride + g * 3;
-        const float c0 = col[0], c1 = col[1], c2 = col[2];
-        if (c0 == 0.0f && c1 == 0.0f && c2 == 0.0f) continue;
-        const float* cv = centers + v * center_stride;
-        const float vx = wx - __ldg(cv), vy = wy - __ldg(cv + 1), vz = wz - __ldg(cv + 2);
-        const float dir_denom = sqrtf(fmaxf(vx * vx + vy * vy + vz * vz, 1e-16f));
-        const float dx = vx / dir_denom, dy = vy / dir_denom, dz = vz / dir_denom;
-        float bas[16];
-        sh_basis<DEGREE>(dx, dy, dz, bas);
+    if (active) {
+        const float wx = xyz[g * 3], wy = xyz[g * 3 + 1], wz = xyz[g * 3 + 2];
+        for (int v = 0; v < views; v++) {
+            const float* col = colors + v * view_stride + g * 3;
+            const float c0 = col[0], c1 = col[1], c2 = col[2];
+            if (c0 == 0.0f && c1 == 0.0f && c2 == 0.0f) continue;
+            const float* cv = centers + v * center_stride;
+            const float vx = wx - __ldg(cv), vy = wy - __ldg(cv + 1), vz = wz - __ldg(cv + 2);
+            const float dir_denom = sqrtf(fmaxf(vx * vx + vy * vy + vz * vz, 1e-16f));
+            const float dx = vx / dir_denom, dy = vy / dir_denom, dz = vz / dir_denom;
+            float bas[16];
+            sh_basis<DEGREE>(dx, dy, dz, bas);
 #pragma unroll
-        for (int k = 0; k < NB; k++) {
-            acc[k * 3] = fmaf(bas[k], c0, acc[k * 3]);
-            acc[k * 3 + 1] = fmaf(bas[k], c1, acc[k * 3 + 1]);
-            acc[k * 3 + 2] = fmaf(bas[k], c2, acc[k * 3 + 2]);
+            for (int k = 0; k < NB; k++) {
+                acc[k * 3] = fmaf(bas[k], c0, acc[k * 3]);
+                acc[k * 3 + 1] = fmaf(bas[k], c1, acc[k * 3 + 1]);
+                acc[k * 3 + 2] = fmaf(bas[k], c2, acc[k * 3 + 2]);
+            }
         }
     }
-    float* out = gsh + g * (int64_t)sh_dim * 3;
     const int n = sh_dim * 3;
-    if ((n & 3) == 0 && (reinterpret_cast<uintptr_t>(gsh) & 15) == 0) {
-        constexpr int kChunks = (NB * 3 + 3) / 4;
-#pragma unroll
-        for (int k = 0; k < kChunks; k++) {
-            float e[4];
-#pragma unroll
-            for (int t = 0; t < 4; t++) e[t] = 4 * k + t < NB * 3 ? acc[4 * k + t] : 0.0f;
-            reinterpret_cast<float4*>(out)[k] = make_float4(e[0], e[1], e[2], e[3]);
-        }
-        for (int k = kChunks; k < n / 4; k++)
-            reinterpret_cast<float4*>(out)[k] = make_float4(0.f, 0.f, 0.f, 0.f);
-    } else {
+    const int chunks = n >> 2;
+    constexpr int kChunks = (NB * 3 + 3) / 4;
+    // Uniform over the block: rows staged in shared memory and stored as
+    // whole-block coalesced float4 runs when they are float4 rows.
+    if ((n & 3) != 0 || chunks > kStageChunks || (reinterpret_cast<uintptr_t>(gsh) & 15) != 0) {
+        if (!active) return;
+        float* out = gsh + g * (int64_t)n;
 #pragma unroll
         for (int c = 0; c < NB * 3; c++) out[c] = acc[c];
         for (int c = NB * 3; c < n; c++) out[c] = 0.0f;
+        return;
+    }
+    __shared__ __align__(16) float4 stage[kProjThreads * kStageStride4];
+    float4* row = stage + threadIdx.x * kStageStride4;
+#pragma unroll
+    for (int k = 0; k < kChunks; k++) {
+        float e[4];
+#pragma unroll
+        for (int t = 0; t < 4; t++) e[t] = 4 * k + t < NB * 3 ? acc[4 * k + t] : 0.0f;
+        row[k] = make_float4(e[0], e[1], e[2], e[3]);
+    }
+    for (int k = kChunks; k < chunks; k++) row[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+    __syncthreads();
+    const int64_t first = (int64_t)blockIdx.x * kProjThreads;
+    const int rows = (int)(capacity - first < kProjThreads ? capacity - first : kProjThreads);
+    float4* out4 = reinterpret_cast<float4*>(gsh) + first * chunks;
+    const uint32_t magic = ((1u << 20) + chunks - 1) / chunks;  // exact for idx < 2^16
+    for (int idx = threadIdx.x; idx < rows * chunks; idx += kProjThreads) {
+        const int r = (int)(((uint32_t)idx * magic) >> 20);
+        out4[idx] = stage[r * kStageStride4 + (idx - r * chunks)];
     }
 }
 

@@ -259,7 +259,7 @@ class NvlsExchange:
             return False
 
     def __init__(self, pool: GaussianArrays, config: CapacityConfig, active_degree: int,
-                 group=None, active_sh_only: bool = True, allreduce: str = "p2p"):
+                 group=None, active_sh_only: bool = True, allreduce: str = "auto"):
         import ctypes
 
         import torch.distributed as dist
@@ -293,10 +293,15 @@ class NvlsExchange:
             raise RuntimeError("NVLS multicast is not available for this group")
         self._handles = (h_geo, h_tab, h_flags)
         self.mc_geo = int(h_geo.multicast_ptr)
-        # allreduce: "p2p" (plain peer loads/stores, up to 8 ranks) or "nvls"
-        # (multimem reduction in the switch).
-        if allreduce not in ("p2p", "nvls"):
-            raise ValueError("allreduce must be 'p2p' or 'nvls'")
+        # allreduce: "p2p" (plain peer loads/stores, up to 8 ranks), "nvls"
+        # (multimem reduction in the switch) or "auto".  Per GPU and direction
+        # P2P moves 2 (N-1)/N of the buffer over NVLink and the switch form
+        # about (N+1)/N of it, so P2P is chosen for up to 3 ranks (at 2 it
+        # took 77 us against 131 us for the 44 MB buffer).
+        if allreduce not in ("p2p", "nvls", "auto"):
+            raise ValueError("allreduce must be 'p2p', 'nvls' or 'auto'")
+        if allreduce == "auto":
+            allreduce = "p2p" if self.world <= 3 else "nvls"
         self.allreduce = "nvls" if self.world > 8 else allreduce
         self.geo_peers = (ctypes.c_void_p * self.world)(*[int(x) for x in h_geo.buffer_ptrs])
         self.mc_row = int(h_tab.multicast_ptr) + self.rank * self.row_floats * 4
@@ -397,13 +402,17 @@ class GraphedTrainingStep:
     target into the graph's static inputs (host or device tensors; host
     tensors should be pinned for asynchronous copies) and replays.  With
     pool_grads the gradients land there in pool order on every replay.
+    exchange: an NvlsExchange built for this step (its step_kwargs passed
+    here too); its exchange() is captured after the step, so each replay
+    also sums the ranks' gradients with no host launch (every rank must
+    replay in step).  The sums are self.gradients.
     """
 
     def __init__(self, pool: GaussianArrays, bounds, camera: DeviceCamera, target: torch.Tensor,
                  config: CapacityConfig, active_degree: int, *, active_sh_only: bool = True,
                  sh_color_only: bool = False, warmup: int = 2, pool_grads=None,
                  collect_stats: bool = False,
-                 stats: torch.Tensor | None = None):
+                 stats: torch.Tensor | None = None, exchange=None):
         dev = pool.xyz.device
         self.camera = DeviceCamera(camera.world_to_camera.clone(), camera.intrinsics.clone(),
                                    camera.center.clone(), camera.planes.clone(), camera.width,
@@ -415,9 +424,13 @@ class GraphedTrainingStep:
                       pool_grads=pool_grads, collect_stats=collect_stats)
         side = torch.cuda.Stream(device=dev)
         side.wait_stream(torch.cuda.current_stream(dev))
+        self.exchange = exchange
+        self.gradients = None
         with torch.cuda.stream(side):
             for _ in range(max(warmup, 1)):
                 compute_training_step(*args, **kwargs)
+                if exchange is not None:
+                    exchange.exchange(self.camera.center)
         torch.cuda.current_stream(dev).wait_stream(side)
         # Statistics accumulate across replays into `stats` (the warm-up steps
         # above do not touch it): the captured step adds into it in place.
@@ -430,6 +443,8 @@ class GraphedTrainingStep:
         before = _lib.launch_count()
         with torch.cuda.graph(self.graph):
             self.out = compute_training_step(*args, **kwargs)
+            if exchange is not None:
+                self.gradients = exchange.exchange(self.camera.center)
         self.launches_per_step = _lib.launch_count() - before
 
     def __call__(self, camera: DeviceCamera | None = None, target: torch.Tensor | None = None) -> StepOutput:

@@ -55,11 +55,12 @@ def _rank(rank, world, port, path, kind):
             exch = NvlsExchange(pool, config, 3, allreduce=kind)
         else:
             exch = ViewShardedExchange(pool, config, 3)
+        # NvlsExchange: the exchange is captured into the step's graph.
         step = GraphedTrainingStep(pool, bounds, cams[rank], target, config, 3,
-                                   **exch.step_kwargs)
+                                   **exch.step_kwargs, exchange=exch if nvls else None)
         for _ in range(3):  # reused buffers: every step must give the same sum
             step()
-            grads = exch.exchange(step.camera.center)
+            grads = step.gradients if nvls else exch.exchange(step.camera.center)
         torch.cuda.synchronize()
         if nvls:
             assert not exch.failed()
