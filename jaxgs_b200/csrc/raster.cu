@@ -316,7 +316,9 @@ __global__ void __launch_bounds__(256) raster_fwd_kernel(
             }
         }
         unsigned mask = __ballot_sync(GSB_FULL_MASK, hit);
-        unsigned contributed = 0;
+        // Bit k: this lane composited splat k of the batch (OR-reduced over
+        // the warp once per batch).
+        unsigned mine = 0;
         __syncwarp();
         while (mask) {
             const int k = __ffs(mask) - 1;
@@ -349,17 +351,20 @@ __global__ void __launch_bounds__(256) raster_fwd_kernel(
             // T (1 - a), with 1 - a formed as fma(a, -1, 1) (exact same rounding).
             trans = V::mul(trans, V::fma(a, V::splat(-1.0f), V::splat(1.0f)));
             const int32_t next = base + k + 1;
-            any_active = false;
 #pragma unroll
             for (int r = 0; r < ROWS; r++) {
                 const bool stop = valid[r] && V::get(trans, r) < kMinT;
                 last[r] = stop ? next : last[r];
                 active[r] = active[r] && !stop;
-                any_active |= active[r];
             }
-            if (__ballot_sync(GSB_FULL_MASK, valid_any)) contributed |= 1u << k;
-            if (!__any_sync(GSB_FULL_MASK, any_active)) break;
+            if (valid_any) mine |= 1u << k;
         }
+        // Saturated lanes composite nothing more, so the warp's exit is
+        // tested once per batch.
+        any_active = false;
+#pragma unroll
+        for (int r = 0; r < ROWS; r++) any_active |= active[r];
+        const unsigned contributed = __reduce_or_sync(GSB_FULL_MASK, mine);
         if (lane == 0) bits[bit_word(start, tile, batch, warps, warp)] = contributed;
         __syncwarp();
     }
