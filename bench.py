@@ -287,6 +287,9 @@ def run_ours(args) -> None:
     torch.cuda.synchronize()
     e2e_elapsed = e_start.elapsed_time(e_end) / 1e3 if not args.no_e2e else float("nan")
     h2d = target.numel() + sum(t.numel() * 4 for t in cam_host)
+    # The consumer of the gradients, timed after the step (it updates the pool
+    # in place): visible-cluster sparse Adam over the step's compact gradients.
+    optimizer = _time_optimizer(pool, graphed.out, stream) if world == 1 else None
     d2h = 4
 
     if world > 1:
@@ -323,6 +326,10 @@ def run_ours(args) -> None:
             "stage_ms": {k: round(v, 4) for k, v in stage_ms.items()},
         }
         line["roofline"] = _roofline(stage_ms, peak, peak_kind, pairs, binned)
+        if optimizer is not None:
+            optimizer["frac"] = round(optimizer["achieved_gbs"] / peak, 4)
+            optimizer["peak_gbs"] = peak
+            line["optimizer"] = optimizer
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(pool_np, camera, target.cpu().numpy())
         print(json.dumps(line), flush=True)
@@ -344,6 +351,49 @@ def _profile_value(name: str, key: str):
             except ValueError:
                 return None
     return None
+
+
+def _time_optimizer(pool, out, stream, iters: int = 20) -> dict:
+    """sparse_adam_update's five field launches (gsb_sparse_adam) over the
+    step's compact gradients, CUDA events on the launching stream.
+    Algorithmic bytes: per element of an alive listed slot, value, both
+    moments and the gradient read (16 B) and value and moments written
+    (12 B); 59 elements per Gaussian at SH degree 3."""
+    import torch
+
+    from jaxgs_b200.optimizer import (PARAMETER_NAMES, create_adam_state,
+                                      parameter_learning_rates, update_field)
+
+    state = create_adam_state(pool)
+    rates = torch.tensor(parameter_learning_rates(100, 1.0), dtype=torch.float32,
+                         device=pool.xyz.device)
+
+    def update():
+        for i, name in enumerate(PARAMETER_NAMES):
+            update_field(getattr(pool, name), state.m[i], state.v[i], out.gradients[i],
+                         pool.alive, out.visible_clusters, rates[i:i + 1], 128, name == "sh",
+                         True)
+
+    for _ in range(3):
+        update()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(iters):
+        update()
+    b.record(stream)
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / iters
+    count = int(out.visible_clusters[1].item())
+    ids = out.visible_clusters[0][:count].long()
+    slots = (ids[:, None] * 128 + torch.arange(128, device=ids.device)).reshape(-1)
+    slots = slots[slots < pool.alive.shape[0]]
+    alive = int(pool.alive[slots].to(torch.int64).sum().item())
+    elements = alive * sum(getattr(pool, n)[0].numel() for n in PARAMETER_NAMES)
+    nbytes = elements * 28
+    return {"kernel": "sparse Adam, 5 fields (gsb_sparse_adam)", "ms": round(ms, 4),
+            "slots": alive, "bytes": nbytes, "achieved_gbs": round(nbytes / ms / 1e6, 1),
+            "unit": "GB/s"}
 
 
 def _roofline(stage_ms, peak, peak_kind, pairs, binned):

@@ -47,7 +47,7 @@ enum {
     GSB_ERR_NULL = 4        /* required pointer is NULL */
 };
 
-#define GSB_ABI_VERSION 4
+#define GSB_ABI_VERSION 5
 
 /* Library ABI version (GSB_ABI_VERSION). */
 GSB_API int gsb_abi_version(void);
@@ -140,6 +140,34 @@ GSB_API int gsb_project_bwd(gsb_stream_t stream, const gsb_project_bwd_params* p
                     const float* gconic, const float* gradius, const float* gcolor,
                     const float* galpha, float* gxyz, float* glog_scale, float* grotation,
                     float* gopacity, float* gsh);
+
+/* ------------------------------------------------------------------------
+ * Visible-cluster sparse Adam, one parameter field per call.
+ * Replaces kernels/sparse_adam.py:98-136 (update_field -> cutlass_call of
+ * _launch/_update, used by training/optimizer.py:276-341 sparse_adam_update
+ * with compacted clusters): LiteGS Adam without bias correction,
+ *   m = 0.9 m + 0.1 g;  v = 0.999 v + 0.001 g^2;
+ *   value -= lr * m / (sqrt(v) + 1e-15),  lr = rate[0] (x10 for the first
+ *   three channels of each row when is_sh, the SH DC coefficient),
+ * on every channel of every alive slot of the listed clusters; every other
+ * element is left as it was.  value/mean/variance[capacity * channels] are
+ * updated in place (pool order); gradient is [capacity * channels] in pool
+ * order, or (compact_gradients) the visible-cluster prefix
+ * [count * cluster_size * channels].  rate is a device scalar, so a
+ * schedule needs no new launch parameters.
+ * ------------------------------------------------------------------------ */
+typedef struct {
+    int capacity;
+    int channels;          /* floats per slot of this field (3, 3, 4, 1, sh_dim * 3) */
+    int cluster_size;
+    int is_sh;
+    int compact_gradients;
+} gsb_adam_params;
+
+GSB_API int gsb_sparse_adam(gsb_stream_t stream, const gsb_adam_params* p, float* value,
+                    float* mean, float* variance, const float* gradient, const int8_t* alive,
+                    const int32_t* cluster_ids, const int32_t* cluster_count,
+                    const float* rate);
 
 /* ------------------------------------------------------------------------
  * SH coefficient cotangents from colour cotangents, summed over views.

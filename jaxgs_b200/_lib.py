@@ -69,6 +69,12 @@ class RasterBwdParams(ctypes.Structure):
                 ("max_pairs", ctypes.c_int64), ("flags", ctypes.c_int)]
 
 
+class AdamParams(ctypes.Structure):
+    _fields_ = [("capacity", ctypes.c_int), ("channels", ctypes.c_int),
+                ("cluster_size", ctypes.c_int), ("is_sh", ctypes.c_int),
+                ("compact_gradients", ctypes.c_int)]
+
+
 class LossParams(ctypes.Structure):
     _fields_ = [("width", ctypes.c_int), ("height", ctypes.c_int), ("target_u8", ctypes.c_int),
                 ("clip_input", ctypes.c_int)]
@@ -84,6 +90,7 @@ SYMBOLS = (
     "gsb_raster_pack", "gsb_raster_bwd_prepare",
     "gsb_loss_workspace_size", "gsb_loss", "gsb_loss_noalloc",
     "gsb_exchange_barrier", "gsb_nvls_allreduce", "gsb_multicast_nonzero", "gsb_p2p_allreduce",
+    "gsb_sparse_adam",
 )
 
 
@@ -135,13 +142,15 @@ def _load():
     lib.gsb_multicast_nonzero.argtypes = [vp, vp, vp, ctypes.c_int64]
     lib.gsb_p2p_allreduce.restype = ctypes.c_int
     lib.gsb_p2p_allreduce.argtypes = [vp, vp, vp, ctypes.c_int64]
+    lib.gsb_sparse_adam.restype = ctypes.c_int
+    lib.gsb_sparse_adam.argtypes = [vp, vp] + [vp] * 8
     lib.gsb_loss_noalloc.restype = ctypes.c_int
     lib.gsb_loss_noalloc.argtypes = [vp, vp] + [vp] * 5
     return lib
 
 
 lib = _load()
-if lib.gsb_abi_version() != 4:
+if lib.gsb_abi_version() != 5:
     raise RuntimeError("libgsb200.so ABI version mismatch; rebuild with `python -m jaxgs_b200.build`")
 
 

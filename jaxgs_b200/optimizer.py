@@ -1,0 +1,134 @@
+"""Visible-cluster sparse Adam, the consumer of the step's gradients.
+
+Mirrors training/optimizer.py:18-27 (AdamState, create_adam_state),
+:93-120 (the per-field learning rates) and :276-341 (sparse_adam_update
+with compacted clusters), each field updated in place by one
+gsb_sparse_adam launch (kernels/sparse_adam.py:16-136).  LiteGS Adam: no
+bias correction, eps 1e-15, moments frozen in slots that are not updated.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+
+from . import _lib as L
+from .types import GaussianArrays
+
+PARAMETER_NAMES = ("xyz", "log_scale", "rotation", "opacity", "sh")
+
+
+@dataclass(frozen=True)
+class OptimizationConfig:
+    """The optimisation rates of config/training.py:33-44 with the values of
+    config/default.toml:24-30."""
+
+    position_lr_init: float = 0.00016
+    position_lr_final: float = 0.0000016
+    position_lr_max_steps: int = 30000
+    feature_lr: float = 0.0025
+    opacity_lr: float = 0.025
+    scaling_lr: float = 0.005
+    rotation_lr: float = 0.001
+
+
+@dataclass
+class AdamState:
+    """training/optimizer.py:18-21: first and second moments per field and
+    the per-slot count of updates."""
+
+    m: tuple
+    v: tuple
+    step: torch.Tensor  # [C] int32
+
+
+def create_adam_state(pool: GaussianArrays) -> AdamState:
+    """Zero moments shaped like the pool's fields (training/optimizer.py:24-27)."""
+    fields = [getattr(pool, name) for name in PARAMETER_NAMES]
+    return AdamState(tuple(torch.zeros_like(f) for f in fields),
+                     tuple(torch.zeros_like(f) for f in fields),
+                     torch.zeros(pool.xyz.shape[0], dtype=torch.int32, device=pool.xyz.device))
+
+
+def parameter_learning_rates(step: float, spatial_scale: float, max_steps: int | None = None,
+                             optimization: OptimizationConfig = OptimizationConfig()):
+    """training/optimizer.py:93-120: rates of (xyz, log_scale, rotation,
+    opacity, sh).  The position rate decays log-linearly from init to final
+    over max_steps (position_lr_max_steps by default), scaled by the scene's
+    spatial scale; the SH rate is feature_lr / 10, the DC coefficient's x10
+    being applied per channel by the update."""
+    o = optimization
+    frac = min(max(float(step) / float(max_steps or o.position_lr_max_steps), 0.0), 1.0)
+    if o.position_lr_init == o.position_lr_final == 0:
+        position = 0.0
+    else:
+        position = float(spatial_scale) * math.exp(math.log(o.position_lr_init) * (1 - frac)
+                                                   + math.log(o.position_lr_final) * frac)
+    return position, o.scaling_lr, o.rotation_lr, o.opacity_lr, o.feature_lr / 10
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def update_field(value: torch.Tensor, mean: torch.Tensor, variance: torch.Tensor,
+                 gradient: torch.Tensor, alive: torch.Tensor, clusters, rate,
+                 cluster_size: int, is_sh: bool, compact_gradients: bool):
+    """kernels/sparse_adam.py:98-136: one field's update, in place on value,
+    mean and variance (contiguous float32 on the GPU).  rate: a float or a
+    device float tensor of one element; clusters: (ids, count) on the device.
+    Returns (value, mean, variance)."""
+    for t in (value, mean, variance, gradient):
+        if not t.is_cuda or t.dtype != torch.float32 or not t.is_contiguous():
+            raise ValueError("sparse Adam needs contiguous float32 CUDA tensors")
+    if value.shape != mean.shape or value.shape != variance.shape:
+        raise ValueError("value and moments must have one shape")
+    capacity = int(alive.shape[0])
+    channels = value.numel() // max(capacity, 1)
+    if channels * capacity != value.numel():
+        raise ValueError("field size must be capacity x channels")
+    ids, count = clusters
+    if not torch.is_tensor(rate):
+        rate = torch.full((1,), float(rate), dtype=torch.float32, device=value.device)
+    if alive.dtype == torch.int8:
+        alive8 = alive
+    elif alive.dtype == torch.uint8:
+        alive8 = alive.view(torch.int8)
+    else:
+        alive8 = alive.to(torch.int8)
+    p = L.AdamParams(capacity, channels, int(cluster_size), int(is_sh), int(compact_gradients))
+    ptr = lambda t: t.data_ptr()
+    L.check(L.lib.gsb_sparse_adam(_stream(), L.ref(p), ptr(value), ptr(mean), ptr(variance),
+                                  ptr(gradient), ptr(alive8.contiguous()),
+                                  ptr(ids.to(torch.int32).contiguous()),
+                                  ptr(count.to(torch.int32).contiguous()),
+                                  ptr(rate.to(torch.float32).contiguous())),
+            "sparse Adam")
+    return value, mean, variance
+
+
+def sparse_adam_update(pool: GaussianArrays, state: AdamState, gradients, visible: torch.Tensor,
+                       step: float, spatial_scale: float, max_steps: int | None = None, *,
+                       compacted_clusters, cluster_size: int = 128,
+                       compact_gradients: bool = False,
+                       optimization: OptimizationConfig = OptimizationConfig()):
+    """training/optimizer.py:276-341 with compacted clusters: LiteGS Adam on
+    every field of the listed clusters' alive slots, in place on the pool and
+    the state; state.step counts the update in every slot of `visible` that
+    is alive.  gradients: (xyz, log_scale, rotation, opacity, sh) in pool
+    order, or the visible-cluster prefix with compact_gradients; the SH
+    gradient carries every coefficient of the pool.  Returns (pool, state)."""
+    rates = parameter_learning_rates(step, spatial_scale, max_steps, optimization)
+    dev = pool.xyz.device
+    rate_t = torch.tensor(rates, dtype=torch.float32, device=dev)
+    for i, (name, gradient) in enumerate(zip(PARAMETER_NAMES, gradients)):
+        value = getattr(pool, name)
+        if gradient.numel() != value.numel() and not compact_gradients:
+            raise ValueError(f"{name} gradient must cover every coefficient of the pool")
+        update_field(value, state.m[i], state.v[i], gradient.contiguous(), pool.alive,
+                     compacted_clusters, rate_t[i:i + 1], cluster_size, name == "sh",
+                     compact_gradients)
+    state.step += (visible.to(torch.bool) & pool.alive.to(torch.bool)).to(torch.int32)
+    return pool, state

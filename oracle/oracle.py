@@ -313,3 +313,59 @@ def training_step(pool, camera, target, *, degree, sh_dim, tile_w, tile_h, max_p
                        loss=t5 - t4, raster_bwd=t6 - t5, project_bwd=t7 - t6, total=t7 - t0)
     return {"loss": value, "grads": grads, "clusters": (ids, count), "table": table, "fwd": fwd,
             "proj": proj, "stats": cot["stats"]}
+
+
+def sparse_adam(value, mean, variance, gradient, alive, ids, count, rate, *, cluster_size,
+                is_sh, compact_gradients):
+    """Visible-cluster LiteGS Adam on one field, kernels/sparse_adam.py:16-54
+    (as called by training/optimizer.py:310-325): for every channel of every
+    alive slot of the first `count` listed clusters,
+        m = 0.9 m + 0.1 g;  v = 0.999 v + 0.001 g g;  x -= lr m / (sqrt(v) + 1e-15)
+    with lr = rate (times 10 for the first three channels of an SH row), each
+    operation rounded to float32 in that order.  gradient is in pool order,
+    or (compact_gradients) the visible-cluster prefix.  Returns new
+    (value, mean, variance) flat float32 arrays; other elements unchanged."""
+    f = np.float32
+    x = np.array(value, np.float32).reshape(-1)
+    m = np.array(mean, np.float32).reshape(-1)
+    v = np.array(variance, np.float32).reshape(-1)
+    g_all = np.asarray(gradient, np.float32).reshape(-1)
+    alive = np.asarray(alive).reshape(-1).astype(bool)
+    capacity = alive.size
+    ch = x.size // capacity
+    lr0 = f(rate)
+    channel_rate = np.full(ch, lr0, np.float32)
+    if is_sh:
+        channel_rate[:3] = lr0 * f(10.0)
+    for c in range(int(count)):
+        slots = int(ids[c]) * cluster_size + np.arange(cluster_size)
+        in_pool = slots < capacity
+        keep = np.zeros(cluster_size, bool)
+        keep[in_pool] = alive[slots[in_pool]]
+        elems = (slots[:, None] * ch + np.arange(ch)).reshape(-1)
+        gidx = (c * cluster_size * ch + np.arange(cluster_size * ch)) if compact_gradients else elems
+        mask = np.repeat(keep, ch)
+        e, gi = elems[mask], gidx[mask]
+        g = g_all[gi]
+        lr = np.tile(channel_rate, cluster_size)[mask]
+        mm = f(0.9) * m[e] + f(0.1) * g
+        vv = f(0.999) * v[e] + (f(0.001) * g) * g
+        x[e] = x[e] - (lr * mm) / (np.sqrt(vv) + f(1e-15))
+        m[e], v[e] = mm, vv
+    return x, m, v
+
+
+def parameter_learning_rates(step, spatial_scale, max_steps, position_lr_init,
+                             position_lr_final, feature_lr, opacity_lr, scaling_lr, rotation_lr):
+    """training/optimizer.py:93-120: (xyz, log_scale, rotation, opacity, sh)
+    rates of sparse_adam_update, the SH one being feature_lr / 10 (the DC
+    coefficient's x10 is applied per channel).  float64 host arithmetic."""
+    import math
+
+    frac = min(max(step / max_steps, 0.0), 1.0)
+    if position_lr_init == position_lr_final == 0:
+        position = 0.0
+    else:
+        position = spatial_scale * math.exp(math.log(position_lr_init) * (1 - frac)
+                                            + math.log(position_lr_final) * frac)
+    return position, scaling_lr, rotation_lr, opacity_lr, feature_lr / 10

@@ -280,6 +280,70 @@ def test_known_answer_early_termination_statistics():
     np.testing.assert_array_equal(stats[:2, 0], 128)
 
 
+ADAM_RATES = dict(position_lr_init=0.00016, position_lr_final=0.0000016, feature_lr=0.0025,
+                  opacity_lr=0.025, scaling_lr=0.005, rotation_lr=0.001)
+
+
+def _adam_all_fields(pool, m, v, grads, ids, count, rates, cluster_size, compact):
+    out = {}
+    for i, name in enumerate(("xyz", "log_scale", "rotation", "opacity", "sh")):
+        out[name] = O.sparse_adam(pool[name], m[name], v[name], grads[i], pool["alive"], ids,
+                                  count, rates[i], cluster_size=cluster_size,
+                                  is_sh=name == "sh", compact_gradients=compact)
+    return out
+
+
+def test_known_answer_sparse_adam_rates_and_mask():
+    """tests/test_training_protocol.py:201-224: unit gradients, zero moments,
+    step 0, spatial scale 2: each active field moves by rate * 0.1 /
+    sqrt(0.001) (rates 0.00032, 0.005, 0.001, 0.025; SH DC 0.0025, the other
+    coefficients 0.00025), the inactive slot not at all."""
+    config = CapacityConfig(2, 1, 2, 4, 1)
+    pool = seed_gaussians(create_gaussians(config), np.ones((2, 3)), np.ones((2, 3)))
+    rates = O.parameter_learning_rates(0, 2.0, 30000, **ADAM_RATES)
+    zeros = {k: np.zeros_like(pool[k]) for k in ("xyz", "log_scale", "rotation", "opacity", "sh")}
+    grads = [np.ones_like(pool[k]) for k in ("xyz", "log_scale", "rotation", "opacity", "sh")]
+    # visible = [True, False] with clusters of one slot: cluster 0 listed.
+    out = _adam_all_fields(pool, zeros, zeros, grads, np.array([0, 1], np.int32), 1, rates, 1,
+                           False)
+    for name, rate in zip(("xyz", "log_scale", "rotation", "opacity"), (0.00032, 0.005, 0.001, 0.025)):
+        got = out[name][0].reshape(pool[name].shape)
+        np.testing.assert_allclose(got[0], pool[name][0] - rate * 0.1 / np.sqrt(0.001), atol=1e-6)
+        np.testing.assert_array_equal(got[1], pool[name][1])
+    sh = out["sh"][0].reshape(pool["sh"].shape)
+    np.testing.assert_allclose(sh[0, 0], pool["sh"][0, 0] - 0.0025 * np.sqrt(10), atol=1e-6)
+    np.testing.assert_allclose(sh[0, 1], pool["sh"][0, 1] - 0.00025 * np.sqrt(10), atol=1e-6)
+    np.testing.assert_array_equal(sh[1], pool["sh"][1])
+
+
+def test_oracle_sparse_adam_compact_gradients_and_untouched_slots():
+    """tests/test_packed.py:275-330: moments 0.2 / 0.1, gradients 0.3, step
+    123, spatial scale 2, clusters of two slots with 1, 3 and 4 listed: the
+    compact-gradient update equals the pool-order one, and slots outside the
+    listed clusters keep their values and moments."""
+    config = CapacityConfig(10, 2, 16, 16, 2, 128, tile_height=8)
+    pool = seed_gaussians(create_gaussians(config), np.ones((9, 3)) * 2.0, np.ones((9, 3)) * 0.4)
+    names = ("xyz", "log_scale", "rotation", "opacity", "sh")
+    visible = np.repeat(np.array([False, True, False, True, True]), 2)
+    ids, count = np.array([1, 3, 4, 0, 0], np.int32), 3
+    m = {k: np.full_like(pool[k], 0.2) for k in names}
+    v = {k: np.full_like(pool[k], 0.1) for k in names}
+    grads = [np.full_like(pool[k], 0.3) for k in names]
+    rates = O.parameter_learning_rates(123, 2.0, 30000, **ADAM_RATES)
+    full = _adam_all_fields(pool, m, v, grads, ids, count, rates, 2, False)
+    slots = (ids[:count, None] * 2 + np.arange(2)).reshape(-1)
+    compact = [g.reshape(10, -1)[slots].reshape(-1) for g in grads]
+    comp = _adam_all_fields(pool, m, v, compact, ids, count, rates, 2, True)
+    for name in names:
+        for a, b in zip(full[name], comp[name]):
+            np.testing.assert_array_equal(a, b)
+        x = full[name][0].reshape(10, -1)
+        assert np.all(x[visible & pool["alive"]] != pool[name].reshape(10, -1)[visible & pool["alive"]])
+        np.testing.assert_array_equal(x[~visible], pool[name].reshape(10, -1)[~visible])
+        np.testing.assert_array_equal(full[name][1].reshape(10, -1)[~visible],
+                                      m[name].reshape(10, -1)[~visible])
+
+
 @pytest.mark.parametrize("shape", [(3, 5), (17, 31), (40, 33)])
 def test_oracle_loss_matches_autograd(shape):
     """Fused loss value and gradient == autograd of reference/loss.py
