@@ -63,11 +63,19 @@ __global__ void __launch_bounds__(kAdamThreads) sparse_adam_kernel(
         g[0] = gv.x; g[1] = gv.y; g[2] = gv.z; g[3] = gv.w;
     }
     bool any = false;
+    // Slot and channel of the first element with one 32-bit division (a run
+    // holds fewer than 2^26 elements); the next three follow by carrying.
+    int rel = (int)local / p.channels;
+    int chan = (int)local - rel * p.channels;
 #pragma unroll
     for (int k = 0; k < kAdamVec; k++) {
+        if (k > 0 && ++chan == p.channels) {
+            chan = 0;
+            rel++;
+        }
         if (k >= n) break;
         const int64_t e = local + k;
-        const int64_t slot = first_slot + e / p.channels;
+        const int64_t slot = first_slot + rel;
         if (slot >= p.capacity || __ldg(alive + slot) == 0) continue;
         if (!vec) {
             x[k] = value[base + e];
@@ -75,7 +83,7 @@ __global__ void __launch_bounds__(kAdamThreads) sparse_adam_kernel(
             v[k] = variance[base + e];
             g[k] = __ldg(gradient + gbase + e);
         }
-        const float lr = p.is_sh && (e % p.channels) < 3 ? lr0 * 10.0f : lr0;
+        const float lr = p.is_sh && chan < 3 ? lr0 * 10.0f : lr0;
         adam_element(x[k], m[k], v[k], g[k], lr);
         any = true;
         if (!vec) {
