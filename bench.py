@@ -287,8 +287,10 @@ def run_ours(args) -> None:
     torch.cuda.synchronize()
     e2e_elapsed = e_start.elapsed_time(e_end) / 1e3 if not args.no_e2e else float("nan")
     h2d = target.numel() + sum(t.numel() * 4 for t in cam_host)
-    # The consumer of the gradients, timed after the step (it updates the pool
-    # in place): visible-cluster sparse Adam over the step's compact gradients.
+    # Inference of the same view (RGB-only forward, uint8 frame), then the
+    # consumer of the gradients (it updates the pool in place): visible-
+    # cluster sparse Adam over the step's compact gradients.
+    inference = _time_inference(pool, camera, stream) if world == 1 else None
     optimizer = _time_optimizer(pool, graphed.out, stream) if world == 1 else None
     d2h = 4
 
@@ -326,6 +328,8 @@ def run_ours(args) -> None:
             "stage_ms": {k: round(v, 4) for k, v in stage_ms.items()},
         }
         line["roofline"] = _roofline(stage_ms, peak, peak_kind, pairs, binned)
+        if inference is not None:
+            line["inference"] = inference
         if optimizer is not None:
             optimizer["frac"] = round(optimizer["achieved_gbs"] / peak, 4)
             optimizer["peak_gbs"] = peak
@@ -351,6 +355,29 @@ def _profile_value(name: str, key: str):
             except ValueError:
                 return None
     return None
+
+
+def _time_inference(pool, camera, stream, iters: int = 30) -> dict:
+    """ViewRenderer frames (cull, project, bin, RGB-only raster, uint8) of
+    the bench view, graph replays timed with CUDA events."""
+    import torch
+
+    from jaxgs_b200.view import ViewRenderer
+
+    renderer = ViewRenderer(pool)
+    for _ in range(3):
+        renderer(camera, copy=False)
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(iters):
+        image, overflow = renderer(camera, copy=False)
+    b.record(stream)
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / iters
+    return {"what": "ViewRenderer frame (uint8 1237x822, CUDA graph replay)",
+            "ms_per_frame": round(ms, 4), "frames_per_s": round(1e3 / ms, 1),
+            "overflow": bool(overflow.item())}
 
 
 def _time_optimizer(pool, out, stream, iters: int = 20) -> dict:

@@ -246,10 +246,16 @@ typedef struct {
     int width, height;
     int tile_w, tile_h;
     int64_t max_pairs;     /* arena capacity of the table (sizes the bit words) */
-    int flags;             /* GSB_RASTER_SPLATS_READY: splats already written by gsb_raster_pack */
+    int flags;             /* GSB_RASTER_SPLATS_READY: splats already written by gsb_raster_pack;
+                              GSB_RASTER_RGB_ONLY: the inference forward, which
+                              writes no final_t / last / backward_work /
+                              contribution_bits (they may be NULL); the
+                              reference's record_contributions = False,
+                              kernels/packed_rasterizer.py:219-232 */
 } gsb_raster_params;
 
 #define GSB_RASTER_SPLATS_READY 1
+#define GSB_RASTER_RGB_ONLY 2
 
 GSB_API size_t gsb_raster_workspace_size(const gsb_raster_params* p);
 GSB_API size_t gsb_raster_bit_words(const gsb_raster_params* p);

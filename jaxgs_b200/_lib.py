@@ -60,6 +60,7 @@ class RasterParams(ctypes.Structure):
 
 
 RASTER_SPLATS_READY = 1
+RASTER_RGB_ONLY = 2
 RASTER_BWD_PREPARED = 1
 
 

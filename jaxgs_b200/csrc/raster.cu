@@ -264,7 +264,11 @@ __device__ __forceinline__ Fragment<ROWS> fragment(const Stash& st, int k,
     return f;
 }
 
-template <int ROWS, bool WANT_DEPTH>
+// RECORD = false is the RGB-only forward of inference (the reference's
+// record_contributions = False, packed_rasterizer.py:219-232): the same
+// compositing, without final T, last index, backward work or contribution
+// bits.
+template <int ROWS, bool WANT_DEPTH, bool RECORD>
 __global__ void __launch_bounds__(256) raster_fwd_kernel(
     gsb_raster_params p, const float4* __restrict__ splats, const float* __restrict__ depth,
     const int32_t* __restrict__ ids, const int32_t* __restrict__ offsets,
@@ -282,7 +286,7 @@ __global__ void __launch_bounds__(256) raster_fwd_kernel(
     Stash& st = stash_all[warp];
     const int tile = order[blockIdx.x];
     const Geom<ROWS> tg = geom<ROWS>(p.width, p.tile_w, p.tile_h, tile, warp, lane);
-    if (threadIdx.x == 0) tile_work = 0;
+    if (RECORD && threadIdx.x == 0) tile_work = 0;
     const int32_t start = offsets[tile], end = offsets[tile + 1];
     const T pcx = V::splat((float)tg.px + 0.5f);
     const float bx0 = (float)tg.bx0, by0 = (float)tg.by0;
@@ -357,15 +361,17 @@ __global__ void __launch_bounds__(256) raster_fwd_kernel(
                 last[r] = stop ? next : last[r];
                 active[r] = active[r] && !stop;
             }
-            if (valid_any) mine |= 1u << k;
+            if (RECORD && valid_any) mine |= 1u << k;
         }
         // Saturated lanes composite nothing more, so the warp's exit is
         // tested once per batch.
         any_active = false;
 #pragma unroll
         for (int r = 0; r < ROWS; r++) any_active |= active[r];
-        const unsigned contributed = __reduce_or_sync(GSB_FULL_MASK, mine);
-        if (lane == 0) bits[bit_word(start, tile, batch, warps, warp)] = contributed;
+        if (RECORD) {
+            const unsigned contributed = __reduce_or_sync(GSB_FULL_MASK, mine);
+            if (lane == 0) bits[bit_word(start, tile, batch, warps, warp)] = contributed;
+        }
         __syncwarp();
     }
     int work = 0;
@@ -380,11 +386,14 @@ __global__ void __launch_bounds__(256) raster_fwd_kernel(
             rgb[pix * 3 + 2] = V::get(cb, r) + t * __ldg(background + 2);
             if (out_depth) out_depth[pix] = V::get(cd, r);
             if (out_alpha) out_alpha[pix] = 1.0f - t;
-            final_t[pix] = t;
-            last_out[pix] = last[r];
-            work = max(work, last[r] - start);
+            if (RECORD) {
+                final_t[pix] = t;
+                last_out[pix] = last[r];
+                work = max(work, last[r] - start);
+            }
         }
     }
+    if (!RECORD) return;
 #pragma unroll
     for (int d = 16; d > 0; d >>= 1) work = max(work, __shfl_xor_sync(GSB_FULL_MASK, work, d));
     __syncthreads();
@@ -679,18 +688,24 @@ size_t bit_words(const gsb_raster_params& p)
 }
 
 template <int ROWS>
-void launch_fwd(cudaStream_t s, int tiles, int warps, bool want_depth, const gsb_raster_params& p,
-                const float4* sp, const float* depth, const int32_t* ids, const int32_t* offsets,
-                const int32_t* order, const float* bg, float* rgb, float* od, float* oa,
-                float* final_t, int32_t* last, int32_t* work, uint32_t* bits)
+void launch_fwd(cudaStream_t s, int tiles, int warps, bool want_depth, bool record,
+                const gsb_raster_params& p, const float4* sp, const float* depth,
+                const int32_t* ids, const int32_t* offsets, const int32_t* order, const float* bg,
+                float* rgb, float* od, float* oa, float* final_t, int32_t* last, int32_t* work,
+                uint32_t* bits)
 {
     size_t smem = (size_t)warps * sizeof(Stash);
-    if (want_depth)
-        gsb::launch(raster_fwd_kernel<ROWS, true>, tiles, warps * 32, smem, s, 
-            p, sp, depth, ids, offsets, order, bg, rgb, od, oa, final_t, last, work, bits);
-    else
-        gsb::launch(raster_fwd_kernel<ROWS, false>, tiles, warps * 32, smem, s, 
-            p, sp, depth, ids, offsets, order, bg, rgb, od, oa, final_t, last, work, bits);
+    auto go = [&](auto kernel) {
+        gsb::launch(kernel, tiles, warps * 32, smem, s, p, sp, depth, ids, offsets, order, bg, rgb,
+                    od, oa, final_t, last, work, bits);
+    };
+    if (record) {
+        if (want_depth) go(raster_fwd_kernel<ROWS, true, true>);
+        else go(raster_fwd_kernel<ROWS, false, true>);
+    } else {
+        if (want_depth) go(raster_fwd_kernel<ROWS, true, false>);
+        else go(raster_fwd_kernel<ROWS, false, false>);
+    }
 }
 
 template <int ROWS>
@@ -775,7 +790,7 @@ bool raster_shape_ok(const gsb_raster_params& p)
 {
     return p.capacity >= 0 && p.width > 0 && p.height > 0 && tiles_ok(p.tile_w, p.tile_h) &&
            p.max_pairs >= 0 && p.max_pairs < (int64_t(1) << 31) &&
-           (p.flags & ~GSB_RASTER_SPLATS_READY) == 0;
+           (p.flags & ~(GSB_RASTER_SPLATS_READY | GSB_RASTER_RGB_ONLY)) == 0;
 }
 
 bool raster_bwd_shape_ok(const gsb_raster_bwd_params& p)
@@ -816,8 +831,9 @@ extern "C" int gsb_raster_fwd(gsb_stream_t stream, const gsb_raster_params* p, v
     if (!raster_shape_ok(*p)) return GSB_ERR_INVALID;
     if (!workspace || workspace_bytes < raster_ws(*p)) return GSB_ERR_WORKSPACE;
     const bool packed = (p->flags & GSB_RASTER_SPLATS_READY) != 0;
-    if (!gaussian_ids || !tile_offsets || !background || !rgb || !final_t || !last ||
-        !backward_work || !splats || !contribution_bits ||
+    const bool record = (p->flags & GSB_RASTER_RGB_ONLY) == 0;
+    if (!gaussian_ids || !tile_offsets || !background || !rgb || !splats ||
+        (record && (!final_t || !last || !backward_work || !contribution_bits)) ||
         (p->capacity > 0 && !packed && (!mean || !conic || !color || !alpha || !visible)) ||
         (out_depth && !depth))
         return GSB_ERR_NULL;
@@ -833,11 +849,11 @@ extern "C" int gsb_raster_fwd(gsb_stream_t stream, const gsb_raster_params* p, v
     int warps = warps_per_tile(p->tile_w, p->tile_h);
     const float4* sp = reinterpret_cast<const float4*>(splats);
     if (rows_per_lane(p->tile_h) == 2)
-        launch_fwd<2>(s, tiles, warps, out_depth != nullptr, *p, sp, depth, gaussian_ids,
+        launch_fwd<2>(s, tiles, warps, out_depth != nullptr, record, *p, sp, depth, gaussian_ids,
                       tile_offsets, order, background, rgb, out_depth, out_alpha, final_t, last,
                       backward_work, contribution_bits);
     else
-        launch_fwd<1>(s, tiles, warps, out_depth != nullptr, *p, sp, depth, gaussian_ids,
+        launch_fwd<1>(s, tiles, warps, out_depth != nullptr, record, *p, sp, depth, gaussian_ids,
                       tile_offsets, order, background, rgb, out_depth, out_alpha, final_t, last,
                       backward_work, contribution_bits);
     return check_launch();

@@ -308,12 +308,14 @@ def pack_splats(projected: ProjectedGaussians, camera: DeviceCamera, config: Cap
 def rasterize_forward(projected: ProjectedGaussians, table: SortedVisibilityTable,
                       camera: DeviceCamera, config: CapacityConfig, background=None,
                       want_depth: bool = True, want_alpha: bool = True,
-                      splats: torch.Tensor | None = None):
+                      splats: torch.Tensor | None = None, record: bool = True):
     """sorted_rasterizer.py:15-70: returns (RenderResult, RasterCache).
 
     The table may reference only visible Gaussians (others are not staged).
     splats: records already written by pack_splats (the packing stage is
-    then skipped).
+    then skipped).  record=False is the inference forward
+    (packed_rasterizer.py:219-232, record_contributions=False): the same
+    image with no backward state, and the cache is None.
     """
     _require_cuda(projected.mean, "rasterization")
     C = config.max_gaussians
@@ -324,15 +326,16 @@ def rasterize_forward(projected: ProjectedGaussians, table: SortedVisibilityTabl
     rgb = torch.empty(H, W, 3, dtype=_f32, device=dev)
     out_depth = torch.empty(H, W, dtype=_f32, device=dev) if want_depth else None
     out_alpha = torch.empty(H, W, dtype=_f32, device=dev) if want_alpha else None
-    final_t = torch.empty(H * W, dtype=_f32, device=dev)
-    last = torch.empty(H * W, dtype=_i32, device=dev)
-    work = torch.empty(_tiles(camera, config), dtype=_i32, device=dev)
+    final_t = torch.empty(H * W, dtype=_f32, device=dev) if record else None
+    last = torch.empty(H * W, dtype=_i32, device=dev) if record else None
+    work = torch.empty(_tiles(camera, config), dtype=_i32, device=dev) if record else None
     packed = splats is not None
     if not packed:
         splats = torch.empty(C, 12, dtype=_f32, device=dev)
     p = _raster_params(camera, config, table.gaussian_ids.shape[0],
-                       L.RASTER_SPLATS_READY if packed else 0)
-    bits = torch.empty(max(int(L.lib.gsb_raster_bit_words(L.ref(p))), 1), dtype=_i32, device=dev)
+                       (L.RASTER_SPLATS_READY if packed else 0) | (0 if record else L.RASTER_RGB_ONLY))
+    bits = (torch.empty(max(int(L.lib.gsb_raster_bit_words(L.ref(p))), 1), dtype=_i32, device=dev)
+            if record else None)
     ws = _workspace(L.lib.gsb_raster_workspace_size(L.ref(p)), dev)
     L.check(L.lib.gsb_raster_fwd(
         _stream(), L.ref(p), _ptr(ws), ws.numel(), _ptr(_c(projected.mean, _f32)),
@@ -342,7 +345,8 @@ def rasterize_forward(projected: ProjectedGaussians, table: SortedVisibilityTabl
         _ptr(table.tile_offsets), _ptr(_c(background, _f32)), _ptr(rgb), _ptr(out_depth),
         _ptr(out_alpha), _ptr(final_t), _ptr(last), _ptr(work), _ptr(splats), _ptr(bits)),
         "rasterization forward")
-    return RenderResult(rgb, out_depth, out_alpha), RasterCache(splats, final_t, last, work, bits)
+    cache = RasterCache(splats, final_t, last, work, bits) if record else None
+    return RenderResult(rgb, out_depth, out_alpha), cache
 
 
 class BackwardBuffers:

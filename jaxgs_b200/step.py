@@ -149,12 +149,12 @@ def compute_training_step(pool: GaussianArrays, bounds, camera: DeviceCamera, ta
 
 def render(camera: DeviceCamera, gaussians: GaussianArrays, visible_clusters, active_degree: int,
            pp: CapacityConfig):
-    """render/pipeline.py:47-93 (fp32 compositing): (image clipped to [0,1],
-    primitive_visible, overflow)."""
+    """render/pipeline.py:47-93 (fp32 compositing, the RGB-only forward):
+    (image clipped to [0,1], primitive_visible, overflow)."""
     projected = K.project_cute(gaussians, camera, pp, active_degree, visible_clusters)
     table = K.build_sorted_visibility_table_cute(projected, camera, pp)
     result, _ = K.rasterize_forward(projected, table, camera, pp, want_depth=False,
-                                    want_alpha=False)
+                                    want_alpha=False, record=False)
     return result.rgb.clamp(0, 1), table.point_counts > 0, table.overflow
 
 

@@ -58,7 +58,7 @@ def test_invalid_parameters_are_rejected_before_launch():
     assert L.lib.gsb_raster_bit_words(L.ref(rast)) == 0
     rast = L.RasterParams(10, 64, 48, 16, 8, 100)
     assert L.lib.gsb_raster_bit_words(L.ref(rast)) == (100 // 32 + 4 * 6 + 1) * 2
-    rast = L.RasterParams(10, 64, 48, 16, 8, 100, 2)  # unknown flag
+    rast = L.RasterParams(10, 64, 48, 16, 8, 100, 4)  # unknown flag
     assert L.lib.gsb_raster_fwd(vp, L.ref(rast), vp, 0, *([vp] * 17)) == 1
     assert L.lib.gsb_raster_pack(vp, L.ref(rast), *([vp] * 6)) == 1
     rast = L.RasterParams(10, 64, 48, 16, 8, 100, L.RASTER_SPLATS_READY)
