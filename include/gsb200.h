@@ -47,7 +47,7 @@ enum {
     GSB_ERR_NULL = 4        /* required pointer is NULL */
 };
 
-#define GSB_ABI_VERSION 5
+#define GSB_ABI_VERSION 6
 
 /* Library ABI version (GSB_ABI_VERSION). */
 GSB_API int gsb_abi_version(void);
@@ -168,6 +168,24 @@ GSB_API int gsb_sparse_adam(gsb_stream_t stream, const gsb_adam_params* p, float
                     float* mean, float* variance, const float* gradient, const int8_t* alive,
                     const int32_t* cluster_ids, const int32_t* cluster_count,
                     const float* rate);
+
+/* ------------------------------------------------------------------------
+ * Density-control consumers of the fragment statistics.
+ * gsb_densify_scores replaces training/densify.py:20-35
+ * (compute_densification_scores): stats[C*4] = (count, weight, alpha
+ * cotangent sum, squared sum) per slot (16-byte aligned), opacity[C] logits,
+ * alive[C] -> scores[C] = max(sq/(n+1) - (sum/(n+1))^2, 0) * n *
+ * sigmoid(opacity)^2 (0 for dead slots and non-finite values), prune[C] =
+ * alive & weight == 0.
+ * gsb_decay_opacity replaces the pool half of training/densify.py:158-165
+ * (decay_opacity): alive slots' logits become logit(max(sigmoid / 2,
+ * 1/128)); the caller clears the Adam moments.
+ * ------------------------------------------------------------------------ */
+GSB_API int gsb_densify_scores(gsb_stream_t stream, int64_t capacity, const float* stats,
+                       const float* opacity, const int8_t* alive, float* scores,
+                       int8_t* prune);
+GSB_API int gsb_decay_opacity(gsb_stream_t stream, int64_t capacity, float* opacity,
+                      const int8_t* alive);
 
 /* ------------------------------------------------------------------------
  * SH coefficient cotangents from colour cotangents, summed over views.

@@ -91,7 +91,7 @@ SYMBOLS = (
     "gsb_raster_pack", "gsb_raster_bwd_prepare",
     "gsb_loss_workspace_size", "gsb_loss", "gsb_loss_noalloc",
     "gsb_exchange_barrier", "gsb_nvls_allreduce", "gsb_multicast_nonzero", "gsb_p2p_allreduce",
-    "gsb_sparse_adam",
+    "gsb_sparse_adam", "gsb_densify_scores", "gsb_decay_opacity",
 )
 
 
@@ -145,13 +145,17 @@ def _load():
     lib.gsb_p2p_allreduce.argtypes = [vp, vp, vp, ctypes.c_int64]
     lib.gsb_sparse_adam.restype = ctypes.c_int
     lib.gsb_sparse_adam.argtypes = [vp, vp] + [vp] * 8
+    lib.gsb_densify_scores.restype = ctypes.c_int
+    lib.gsb_densify_scores.argtypes = [vp, ctypes.c_int64] + [vp] * 5
+    lib.gsb_decay_opacity.restype = ctypes.c_int
+    lib.gsb_decay_opacity.argtypes = [vp, ctypes.c_int64, vp, vp]
     lib.gsb_loss_noalloc.restype = ctypes.c_int
     lib.gsb_loss_noalloc.argtypes = [vp, vp] + [vp] * 5
     return lib
 
 
 lib = _load()
-if lib.gsb_abi_version() != 5:
+if lib.gsb_abi_version() != 6:
     raise RuntimeError("libgsb200.so ABI version mismatch; rebuild with `python -m jaxgs_b200.build`")
 
 

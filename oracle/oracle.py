@@ -369,3 +369,23 @@ def parameter_learning_rates(step, spatial_scale, max_steps, position_lr_init,
         position = spatial_scale * math.exp(math.log(position_lr_init) * (1 - frac)
                                             + math.log(position_lr_final) * frac)
     return position, scaling_lr, rotation_lr, opacity_lr, feature_lr / 10
+
+
+def densification_scores(opacity, alive, stats):
+    """training/densify.py:20-35 in float64: opacity-weighted variance of the
+    per-fragment opacity gradient, zero for dead slots and non-finite values,
+    and the prune mask alive & (compositing weight == 0)."""
+    n, w, s, q = np.asarray(stats, np.float64).T
+    alive = np.asarray(alive).astype(bool)
+    variance = np.maximum(q / (n + 1) - (s / (n + 1)) ** 2, 0)
+    a = 1.0 / (1.0 + np.exp(-np.asarray(opacity, np.float64).reshape(-1)))
+    with np.errstate(all="ignore"):
+        scores = np.nan_to_num(variance * n * a ** 2, nan=0, posinf=0, neginf=0)
+    return np.where(alive, scores, 0), alive & (w == 0)
+
+
+def decay_opacity(opacity, alive):
+    """training/densify.py:158-165 (float64): alive logits -> logit(max(sigmoid/2, 1/128))."""
+    o = np.asarray(opacity, np.float64).reshape(-1)
+    a = np.maximum(0.5 / (1.0 + np.exp(-o)), 1 / 128)
+    return np.where(np.asarray(alive).astype(bool), np.log(a / (1 - a)), o)

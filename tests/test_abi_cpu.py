@@ -28,7 +28,7 @@ def test_every_declared_symbol_is_exported():
 
 
 def test_abi_version_and_launch_counter():
-    assert L.lib.gsb_abi_version() == 5
+    assert L.lib.gsb_abi_version() == 6
     assert L.launch_count() >= 0
 
 

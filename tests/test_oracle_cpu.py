@@ -344,6 +344,23 @@ def test_oracle_sparse_adam_compact_gradients_and_untouched_slots():
                                       m[name].reshape(10, -1)[~visible])
 
 
+def test_known_answer_densification_scores():
+    """tests/test_training_protocol.py:14-29: the first parent's score is
+    (4/4 - (2/4)^2) * 3 * sigmoid(0.5 logit)^2, the zero-weight second is
+    pruned, dead slots score 0 and are not pruned."""
+    config = CapacityConfig(4, 1, 2, 4, 1)
+    pool = seed_gaussians(create_gaussians(config), np.array([[1.0, 2.0, 3.0], [4.0, 5.0, 6.0]]),
+                          np.ones((2, 3)), scale=0.2, opacity=0.5)
+    stats = np.array([[3.0, 1.0, 2.0, 4.0], [0.0] * 4, [0.0] * 4, [0.0] * 4])
+    score, prune = O.densification_scores(pool["opacity"], pool["alive"], stats)
+    np.testing.assert_allclose(score[0], (4 / 4 - (2 / 4) ** 2) * 3 * 0.5 ** 2, rtol=1e-6)
+    np.testing.assert_array_equal(prune, [False, True, False, False])
+    decayed = O.decay_opacity(pool["opacity"], pool["alive"])
+    a = 1 / (1 + np.exp(-decayed))
+    np.testing.assert_allclose(a[:2], 0.25, rtol=1e-6)
+    np.testing.assert_array_equal(decayed[2:], pool["opacity"].reshape(-1)[2:])
+
+
 @pytest.mark.parametrize("shape", [(3, 5), (17, 31), (40, 33)])
 def test_oracle_loss_matches_autograd(shape):
     """Fused loss value and gradient == autograd of reference/loss.py
