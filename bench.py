@@ -279,8 +279,15 @@ def run_ours(args) -> None:
     torch.cuda.synchronize()
     e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e_start.record(stream)
-    for i in range(0 if args.no_e2e else args.steps):
-        out = graphed(host_cam, target_host)
+    n_e2e = 0 if args.no_e2e else args.steps
+    if n_e2e:
+        graphed.upload(host_cam, target_host)
+    for i in range(n_e2e):
+        # Each step's inputs are uploaded from pinned host memory while the
+        # previous step runs (a loader's prefetch); every step moves its own.
+        out = graphed()
+        if i + 1 < n_e2e:
+            graphed.upload(host_cam, target_host)
         exchange(out)
         e2e_loss[i].copy_(out.loss, non_blocking=True)
     e_end.record(stream)

@@ -447,13 +447,59 @@ class GraphedTrainingStep:
                 self.gradients = exchange.exchange(self.camera.center)
         self.launches_per_step = _lib.launch_count() - before
 
+    def _camera_pairs(self, camera: DeviceCamera, into):
+        return zip(into, (camera.world_to_camera, camera.intrinsics, camera.center,
+                          camera.planes))
+
+    def upload(self, camera: DeviceCamera | None = None, target: torch.Tensor | None = None):
+        """Stage the next step's inputs (pinned host tensors, not modified
+        until that step has run) on a copy stream, so that their transfer
+        overlaps the step in flight; the next call without arguments
+        consumes them.  A data loader's prefetch: each step still moves its
+        own inputs."""
+        dev = self.target.device
+        if not hasattr(self, "_copy"):
+            self._copy = torch.cuda.Stream(device=dev)
+            self._stage_camera = [t.clone() for t in (self.camera.world_to_camera,
+                                                      self.camera.intrinsics, self.camera.center,
+                                                      self.camera.planes)]
+            self._stage_target = torch.empty_like(self.target)
+            self._consumed = torch.cuda.Event()
+        # The staging buffers are free once the previous staged step took them.
+        self._copy.wait_event(self._consumed)
+        with torch.cuda.stream(self._copy):
+            if camera is not None:
+                for dst, src in self._camera_pairs(camera, self._stage_camera):
+                    dst.copy_(src, non_blocking=True)
+            if target is not None:
+                self._stage_target.copy_(target, non_blocking=True)
+        ready = torch.cuda.Event()
+        ready.record(self._copy)
+        self._staged = (ready, camera is not None, target is not None)
+
     def __call__(self, camera: DeviceCamera | None = None, target: torch.Tensor | None = None) -> StepOutput:
-        if camera is not None:
-            for dst, src in ((self.camera.world_to_camera, camera.world_to_camera),
-                             (self.camera.intrinsics, camera.intrinsics),
-                             (self.camera.center, camera.center), (self.camera.planes, camera.planes)):
-                dst.copy_(src, non_blocking=True)
-        if target is not None:
-            self.target.copy_(target, non_blocking=True)
+        staged = getattr(self, "_staged", None)
+        if staged is not None and camera is None and target is None:
+            # Device-to-device copies of the staged inputs (microseconds).
+            ready, has_camera, has_target = staged
+            current = torch.cuda.current_stream(self.target.device)
+            current.wait_event(ready)
+            if has_camera:
+                for dst, src in zip((self.camera.world_to_camera, self.camera.intrinsics,
+                                     self.camera.center, self.camera.planes), self._stage_camera):
+                    dst.copy_(src, non_blocking=True)
+            if has_target:
+                self.target.copy_(self._stage_target, non_blocking=True)
+            self._consumed.record(current)
+            self._staged = None
+        else:
+            if camera is not None:
+                for dst, src in ((self.camera.world_to_camera, camera.world_to_camera),
+                                 (self.camera.intrinsics, camera.intrinsics),
+                                 (self.camera.center, camera.center),
+                                 (self.camera.planes, camera.planes)):
+                    dst.copy_(src, non_blocking=True)
+            if target is not None:
+                self.target.copy_(target, non_blocking=True)
         self.graph.replay()
         return self.out

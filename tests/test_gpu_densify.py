@@ -29,7 +29,9 @@ def test_densification_scores_and_decay_match_oracle():
     scores, prune = compute_densification_scores(pool, torch.as_tensor(stats, device="cuda"))
     torch.cuda.synchronize()
     exp_scores, exp_prune = O.densification_scores(pool_np["opacity"], pool_np["alive"], stats)
-    np.testing.assert_allclose(scores.cpu().numpy(), exp_scores, rtol=2e-6, atol=1e-12)
+    # float32 against float64: the variance cancels, so the bound is absolute
+    # at the scores' scale as well as relative.
+    np.testing.assert_allclose(scores.cpu().numpy(), exp_scores, rtol=1e-5, atol=1e-7)
     np.testing.assert_array_equal(prune.cpu().numpy(), exp_prune)
     assert scores[7].item() == 0.0 and exp_prune.sum() > 0
     _, state = decay_opacity(pool)

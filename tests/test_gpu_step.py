@@ -158,6 +158,43 @@ def test_training_step_fragment_statistics():
     assert rel_l2(graphed.out.stats.cpu().numpy(), 3 * single) < 1e-5
 
 
+def test_graphed_step_staged_upload_equals_direct_inputs():
+    """GraphedTrainingStep.upload stages pinned host inputs on a copy stream;
+    the next call consumes them and gives the same loss and gradients as a
+    call that passes the same inputs directly."""
+    from jaxgs_b200.scene import Camera, CapacityConfig, config0_scene, world_cluster_bounds
+    from jaxgs_b200.step import GraphedTrainingStep
+    from jaxgs_b200.types import DeviceCamera, GaussianArrays
+
+    pool_np, cam, target = config0_scene()
+    n = pool_np["xyz"].shape[0]
+    config = CapacityConfig(n, 128, 16, 16, 3, n * 64, tile_height=8)
+    center, extent, valid = world_cluster_bounds(pool_np, 128)
+    bounds = (torch.as_tensor(center, device="cuda"), torch.as_tensor(extent, device="cuda"),
+              torch.as_tensor(valid.astype(np.uint8), device="cuda"))
+    pool = GaussianArrays.from_numpy(pool_np)
+    step = GraphedTrainingStep(pool, bounds, DeviceCamera.from_camera(cam),
+                               torch.as_tensor(target, device="cuda"), config, 3)
+    other = Camera.look_at((1.0, 0.3, -3.2), (0.2, 0.0, 0.0), cam.fx, cam.fy, cam.width,
+                           cam.height, near=cam.near, far=cam.far)
+    other_target = np.ascontiguousarray(target[::-1])
+    direct = step(DeviceCamera.from_camera(other), torch.as_tensor(other_target, device="cuda"))
+    loss_direct = float(direct.loss)
+    grads_direct = [g.clone() for g in direct.gradients]
+    step(DeviceCamera.from_camera(cam), torch.as_tensor(target, device="cuda"))
+    host_cam = DeviceCamera.from_camera(other, device="cpu")
+    host_cam = DeviceCamera(*(t.pin_memory() for t in (host_cam.world_to_camera,
+                                                        host_cam.intrinsics, host_cam.center,
+                                                        host_cam.planes)),
+                            other.width, other.height, other.near, other.far)
+    step.upload(host_cam, torch.as_tensor(other_target).pin_memory())
+    staged = step()
+    torch.cuda.synchronize()
+    assert float(staged.loss) == loss_direct
+    for a, b in zip(staged.gradients, grads_direct):
+        assert rel_l2(a.cpu().numpy(), b.cpu().numpy()) < 1e-6
+
+
 def _np_sh_from_colors(xyz, centers, colors, degree, sh_dim):
     """training/sh_pullback.py:18-53 in numpy (float64), summed over views."""
     out = np.zeros((xyz.shape[0], sh_dim, 3))
