@@ -71,6 +71,27 @@ def test_training_step_inactive_and_culled_gaussians():
         assert rel_l2(g, ref.reshape(4096, -1)[:rows]) < 1e-3
 
 
+def test_training_step_partial_cluster_and_empty_view():
+    """A pool of 1000 slots (its last cluster partial) against the oracle,
+    and a camera that sees no cluster at all: the step runs with zero pairs,
+    the loss is that of the background image and every gradient is zero."""
+    from jaxgs_b200.scene import Camera, config0_scene
+
+    pool_np, cam, target = config0_scene()
+    small = {k: np.ascontiguousarray(v[:1000]) for k, v in pool_np.items()}
+    out, exp, count = _run(small, cam, target)
+    assert count == 8
+    assert abs(float(out.loss) - exp["loss"]) <= 1e-5 * abs(exp["loss"])
+    for got, ref in zip(out.gradients, exp["grads"]):
+        g = got.cpu().numpy().reshape(1000, -1)
+        assert rel_l2(g, ref.reshape(1000, -1)) < 1e-3
+    away = Camera.look_at((0.0, 0.0, -4.0), (0.0, 0.0, -8.0), 110.0, 110.0, 128, 96,
+                          near=0.01, far=100.0)
+    out, exp, count = _run(pool_np, away, target)
+    assert count == 0 and int(out.pair_count.item()) == 0
+    assert abs(float(out.loss) - exp["loss"]) <= 1e-5 * abs(exp["loss"])
+
+
 def test_pool_order_gradients_for_the_view_sharded_exchange():
     """pool_grads: the step writes pool-order gradients (culled clusters' rows
     zero, stale contents overwritten) into views of one flat buffer, equal to
