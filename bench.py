@@ -280,20 +280,22 @@ def run_ours(args) -> None:
     e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e_start.record(stream)
     n_e2e = 0 if args.no_e2e else args.steps
+    # The camera in its packed form (one 192-byte copy per step).
+    cam_packed = host_cam.pack().pin_memory()
     if n_e2e:
-        graphed.upload(host_cam, target_host)
+        graphed.upload(cam_packed, target_host)
     for i in range(n_e2e):
         # Each step's inputs are uploaded from pinned host memory while the
         # previous step runs (a loader's prefetch); every step moves its own.
         out = graphed()
         if i + 1 < n_e2e:
-            graphed.upload(host_cam, target_host)
+            graphed.upload(cam_packed, target_host)
         exchange(out)
         e2e_loss[i].copy_(out.loss, non_blocking=True)
     e_end.record(stream)
     torch.cuda.synchronize()
     e2e_elapsed = e_start.elapsed_time(e_end) / 1e3 if not args.no_e2e else float("nan")
-    h2d = target.numel() + sum(t.numel() * 4 for t in cam_host)
+    h2d = target.numel() + DeviceCamera.PACKED_FLOATS * 4
     # Inference of the same view (RGB-only forward, uint8 frame), then the
     # consumer of the gradients (it updates the pool in place): visible-
     # cluster sparse Adam over the step's compact gradients.

@@ -414,9 +414,11 @@ class GraphedTrainingStep:
                  collect_stats: bool = False,
                  stats: torch.Tensor | None = None, exchange=None):
         dev = pool.xyz.device
-        self.camera = DeviceCamera(camera.world_to_camera.clone(), camera.intrinsics.clone(),
-                                   camera.center.clone(), camera.planes.clone(), camera.width,
-                                   camera.height, camera.near, camera.far)
+        # The graph's camera arrays are views of one packed buffer, so a new
+        # camera arrives in one copy (DeviceCamera.pack).
+        self.camera_flat = camera.pack().to(dev)
+        self.camera = DeviceCamera.packed_views(self.camera_flat, camera.width, camera.height,
+                                                camera.near, camera.far)
         self.target = torch.empty_like(target, device=dev)
         self.target.copy_(target)
         args = (pool, bounds, self.camera, self.target, config, active_degree)
@@ -447,30 +449,32 @@ class GraphedTrainingStep:
                 self.gradients = exchange.exchange(self.camera.center)
         self.launches_per_step = _lib.launch_count() - before
 
-    def _camera_pairs(self, camera: DeviceCamera, into):
-        return zip(into, (camera.world_to_camera, camera.intrinsics, camera.center,
-                          camera.planes))
-
-    def upload(self, camera: DeviceCamera | None = None, target: torch.Tensor | None = None):
+    def upload(self, camera=None, target: torch.Tensor | None = None):
         """Stage the next step's inputs (pinned host tensors, not modified
         until that step has run) on a copy stream, so that their transfer
         overlaps the step in flight; the next call without arguments
         consumes them.  A data loader's prefetch: each step still moves its
-        own inputs."""
+        own inputs.  camera: a DeviceCamera or its packed [48] form
+        (DeviceCamera.pack), which moves in one copy."""
         dev = self.target.device
         if not hasattr(self, "_copy"):
             self._copy = torch.cuda.Stream(device=dev)
-            self._stage_camera = [t.clone() for t in (self.camera.world_to_camera,
-                                                      self.camera.intrinsics, self.camera.center,
-                                                      self.camera.planes)]
+            self._stage_camera = torch.empty_like(self.camera_flat)
             self._stage_target = torch.empty_like(self.target)
             self._consumed = torch.cuda.Event()
         # The staging buffers are free once the previous staged step took them.
         self._copy.wait_event(self._consumed)
         with torch.cuda.stream(self._copy):
-            if camera is not None:
-                for dst, src in self._camera_pairs(camera, self._stage_camera):
-                    dst.copy_(src, non_blocking=True)
+            if isinstance(camera, DeviceCamera):
+                staged = DeviceCamera.packed_views(self._stage_camera, camera.width,
+                                                   camera.height)
+                for dst, src in ((staged.planes, camera.planes),
+                                 (staged.world_to_camera, camera.world_to_camera),
+                                 (staged.intrinsics, camera.intrinsics),
+                                 (staged.center, camera.center)):
+                    dst.copy_(src.reshape(dst.shape), non_blocking=True)
+            elif camera is not None:
+                self._stage_camera.copy_(camera.reshape(-1), non_blocking=True)
             if target is not None:
                 self._stage_target.copy_(target, non_blocking=True)
         ready = torch.cuda.Event()
@@ -485,9 +489,7 @@ class GraphedTrainingStep:
             current = torch.cuda.current_stream(self.target.device)
             current.wait_event(ready)
             if has_camera:
-                for dst, src in zip((self.camera.world_to_camera, self.camera.intrinsics,
-                                     self.camera.center, self.camera.planes), self._stage_camera):
-                    dst.copy_(src, non_blocking=True)
+                self.camera_flat.copy_(self._stage_camera, non_blocking=True)
             if has_target:
                 self.target.copy_(self._stage_target, non_blocking=True)
             self._consumed.record(current)

@@ -65,6 +65,31 @@ class DeviceCamera:
                    t(camera.frustum_planes()), camera.width, camera.height, camera.near,
                    camera.far)
 
+    # Packed layout (floats): planes [0, 24), world_to_camera [24, 40),
+    # intrinsics [40, 44), center [44, 47), one pad; every field starts on a
+    # 16-byte boundary, so the arrays of one camera move in one copy.
+    PACKED_FLOATS = 48
+
+    @classmethod
+    def packed_views(cls, flat: torch.Tensor, width: int, height: int, near: float = 0.2,
+                     far: float = 1000.0) -> "DeviceCamera":
+        """A DeviceCamera whose arrays are views of one packed [48] buffer."""
+        if flat.numel() != cls.PACKED_FLOATS or flat.dtype != torch.float32:
+            raise ValueError("a packed camera is 48 float32 values")
+        return cls(flat[24:40].view(4, 4), flat[40:44], flat[44:47], flat[0:24].view(6, 4),
+                   width, height, near, far)
+
+    def pack(self, out: torch.Tensor | None = None) -> torch.Tensor:
+        """This camera's arrays in the packed layout (a new tensor on the
+        arrays' device, or copied into `out`)."""
+        flat = torch.zeros(self.PACKED_FLOATS, dtype=torch.float32,
+                           device=self.world_to_camera.device) if out is None else out
+        view = DeviceCamera.packed_views(flat, self.width, self.height, self.near, self.far)
+        for dst, src in ((view.planes, self.planes), (view.world_to_camera, self.world_to_camera),
+                         (view.intrinsics, self.intrinsics), (view.center, self.center)):
+            dst.copy_(src.reshape(dst.shape))
+        return flat
+
 
 @dataclass
 class ProjectedGaussians:

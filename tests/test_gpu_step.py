@@ -214,6 +214,12 @@ def test_graphed_step_staged_upload_equals_direct_inputs():
     assert float(staged.loss) == loss_direct
     for a, b in zip(staged.gradients, grads_direct):
         assert rel_l2(a.cpu().numpy(), b.cpu().numpy()) < 1e-6
+    # The packed camera (one copy) gives the same step again.
+    step(DeviceCamera.from_camera(cam), torch.as_tensor(target, device="cuda"))
+    step.upload(host_cam.pack().pin_memory(), torch.as_tensor(other_target).pin_memory())
+    packed = step()
+    torch.cuda.synchronize()
+    assert float(packed.loss) == loss_direct
 
 
 def _np_sh_from_colors(xyz, centers, colors, degree, sh_dim):
