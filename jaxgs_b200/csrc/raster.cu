@@ -393,13 +393,15 @@ __global__ void __launch_bounds__(256) raster_fwd_kernel(
             }
         }
     }
-    if (!RECORD) return;
+    if constexpr (RECORD) {
 #pragma unroll
-    for (int d = 16; d > 0; d >>= 1) work = max(work, __shfl_xor_sync(GSB_FULL_MASK, work, d));
-    __syncthreads();
-    if (lane == 0) atomicMax(&tile_work, work);
-    __syncthreads();
-    if (threadIdx.x == 0) backward_work[tile] = tile_work;
+        for (int d = 16; d > 0; d >>= 1)
+            work = max(work, __shfl_xor_sync(GSB_FULL_MASK, work, d));
+        __syncthreads();
+        if (lane == 0) atomicMax(&tile_work, work);
+        __syncthreads();
+        if (threadIdx.x == 0) backward_work[tile] = tile_work;
+    }
 }
 
 // Transposed butterfly over 8 values: afterwards lane l holds the warp sum
