@@ -325,11 +325,7 @@ def run_ours(args) -> None:
                        "l2": "inputs larger than L2 (236 MB pool)",
                        "launch": "CUDA graph replay of the whole step",
                        "parallelism": f"view-sharded dp{world}" if world > 1 else "single view",
-                       "exchange": (f"per step: {('own kernels: %s all-reduce, NVLS multicast all-gather' % exch.allreduce.upper()) if isinstance(exch, NvlsExchange) else 'NCCL'} "
-                                    f"all-reduce of {exch.geometric.numel() * 4 / 1e6:.0f} MB "
-                                    f"geometric gradients, all-gather of {config.max_gaussians * 12 / 1e6:.0f} MB "
-                                    "colour cotangents per rank, SH expansion of all views")
-                                   if exch is not None else None},
+                       "exchange": _exchange_text(exch, config) if exch is not None else None},
             "e2e": {"value": None if args.no_e2e else round(world * args.steps / e2e_elapsed, 2),
                     "unit": UNIT, "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": d2h},
             "gpu_launches": int(launches),
@@ -364,6 +360,21 @@ def _profile_value(name: str, key: str):
             except ValueError:
                 return None
     return None
+
+
+def _exchange_text(exch, config) -> str:
+    """What the view-sharded exchange moves per step, for the JSON line."""
+    from jaxgs_b200.step import NvlsExchange
+
+    geo = exch.geometric.numel() * 4 / 1e6
+    colours = config.max_gaussians * 12 / 1e6
+    if isinstance(exch, NvlsExchange):
+        return (f"per step, own kernels in the step's CUDA graph: {exch.allreduce.upper()} "
+                f"all-reduce of {geo:.0f} MB geometric gradients, NVLS multicast all-gather of "
+                f"the non-zero part of {colours:.0f} MB colour cotangents per rank, SH "
+                "expansion of all views")
+    return (f"per step, NCCL: all-reduce of {geo:.0f} MB geometric gradients, all-gather of "
+            f"{colours:.0f} MB colour cotangents per rank, SH expansion of all views")
 
 
 def _time_inference(pool, camera, stream, iters: int = 30) -> dict:
