@@ -81,3 +81,32 @@ def test_python_bindings_refuse_cpu_tensors():
     with pytest.raises(ValueError, match="HWC"):
         # shape errors come first, as in kernels/fused_loss.py:361-362
         K.fused_loss_and_grad(torch.zeros(4, 4, 2), torch.zeros(4, 4, 2))
+
+
+def test_optimizer_density_and_exchange_entry_points_validate_before_launch():
+    """The newer entry points refuse bad shapes (1), NULL pointers (4) and
+    misaligned buffers (1) on the host, before any launch."""
+    import ctypes
+
+    vp = None
+    adam = L.AdamParams(10, 0, 128, 0, 0)  # zero channels
+    assert L.lib.gsb_sparse_adam(vp, L.ref(adam), *([vp] * 8)) == 1
+    adam = L.AdamParams(10, 48, 1 << 21, 1, 0)  # run past the grid's reach
+    assert L.lib.gsb_sparse_adam(vp, L.ref(adam), *([vp] * 8)) == 1
+    adam = L.AdamParams(10, 3, 128, 0, 0)
+    assert L.lib.gsb_sparse_adam(vp, L.ref(adam), *([vp] * 8)) == 4
+    assert L.lib.gsb_sparse_adam(vp, L.ref(L.AdamParams(0, 3, 128, 0, 0)), *([vp] * 8)) == 0
+    assert L.lib.gsb_densify_scores(vp, -1, *([vp] * 5)) == 1
+    assert L.lib.gsb_densify_scores(vp, 10, *([vp] * 5)) == 4
+    assert L.lib.gsb_densify_scores(vp, 0, *([vp] * 5)) == 0
+    assert L.lib.gsb_decay_opacity(vp, 10, vp, vp) == 4
+    assert L.lib.gsb_multicast_nonzero(vp, vp, vp, 6) == 1  # not a multiple of 4
+    assert L.lib.gsb_multicast_nonzero(vp, ctypes.c_void_p(8), ctypes.c_void_p(16), 8) == 1
+    assert L.lib.gsb_multicast_nonzero(vp, vp, vp, 0) == 0
+    nine = L.ExchangeParams(9, 0)  # more ranks than the P2P form takes
+    buffers = (ctypes.c_void_p * 9)(*([16] * 9))
+    assert L.lib.gsb_p2p_allreduce(vp, L.ref(nine), buffers, 8) == 1
+    two = L.ExchangeParams(2, 0)
+    assert L.lib.gsb_p2p_allreduce(vp, L.ref(two), (ctypes.c_void_p * 2)(16, 24), 8) == 1
+    assert L.lib.gsb_p2p_allreduce(vp, L.ref(two), (ctypes.c_void_p * 2)(16, None), 8) == 4
+    assert L.lib.gsb_p2p_allreduce(vp, L.ref(L.ExchangeParams(2, 2)), buffers, 8) == 1
