@@ -80,15 +80,19 @@ def update_field(value: torch.Tensor, mean: torch.Tensor, variance: torch.Tensor
     mean and variance (contiguous float32 on the GPU).  rate: a float or a
     device float tensor of one element; clusters: (ids, count) on the device.
     Returns (value, mean, variance)."""
+    if value.shape != mean.shape or value.shape != variance.shape:
+        raise ValueError("value and moments must have one shape")
+    if gradient.dim() > 1 and tuple(gradient.shape[1:]) != tuple(value.shape[1:]):
+        raise ValueError("gradient rows must have the field's shape (every SH coefficient)")
+    capacity = int(alive.shape[0])
+    if capacity == 0:
+        return value, mean, variance
+    channels = value.numel() // capacity
+    if channels * capacity != value.numel():
+        raise ValueError("field size must be capacity x channels")
     for t in (value, mean, variance, gradient):
         if not t.is_cuda or t.dtype != torch.float32 or not t.is_contiguous():
             raise ValueError("sparse Adam needs contiguous float32 CUDA tensors")
-    if value.shape != mean.shape or value.shape != variance.shape:
-        raise ValueError("value and moments must have one shape")
-    capacity = int(alive.shape[0])
-    channels = value.numel() // max(capacity, 1)
-    if channels * capacity != value.numel():
-        raise ValueError("field size must be capacity x channels")
     ids, count = clusters
     if not torch.is_tensor(rate):
         rate = torch.full((1,), float(rate), dtype=torch.float32, device=value.device)

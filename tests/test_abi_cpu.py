@@ -110,3 +110,18 @@ def test_optimizer_density_and_exchange_entry_points_validate_before_launch():
     assert L.lib.gsb_p2p_allreduce(vp, L.ref(two), (ctypes.c_void_p * 2)(16, 24), 8) == 1
     assert L.lib.gsb_p2p_allreduce(vp, L.ref(two), (ctypes.c_void_p * 2)(16, None), 8) == 4
     assert L.lib.gsb_p2p_allreduce(vp, L.ref(L.ExchangeParams(2, 2)), buffers, 8) == 1
+
+
+def test_sparse_adam_python_checks_refuse_mismatched_rows():
+    """update_field refuses SH gradients narrower than the field (an
+    active-bands gradient), on the host."""
+    import torch
+
+    from jaxgs_b200.optimizer import update_field
+
+    sh = torch.zeros(4, 16, 3)
+    narrow = torch.zeros(4, 4, 3)
+    with pytest.raises(ValueError, match="every SH coefficient"):
+        update_field(sh, sh.clone(), sh.clone(), narrow, torch.ones(4, dtype=torch.uint8),
+                     (torch.zeros(1, dtype=torch.int32), torch.ones(1, dtype=torch.int32)),
+                     0.1, 1, True, False)
