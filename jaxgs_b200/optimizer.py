@@ -52,6 +52,17 @@ def create_adam_state(pool: GaussianArrays) -> AdamState:
                      torch.zeros(pool.xyz.shape[0], dtype=torch.int32, device=pool.xyz.device))
 
 
+def reset_adam_slots(state: AdamState, slot_mask: torch.Tensor) -> AdamState:
+    """training/optimizer.py:78-90: zero both moments and the update count
+    of the masked slots, in place."""
+    mask = slot_mask.to(torch.bool)
+    for moments in (state.m, state.v):
+        for t in moments:
+            t[mask] = 0
+    state.step[mask] = 0
+    return state
+
+
 def parameter_learning_rates(step: float, spatial_scale: float, max_steps: int | None = None,
                              optimization: OptimizationConfig = OptimizationConfig()):
     """training/optimizer.py:93-120: rates of (xyz, log_scale, rotation,
