@@ -22,6 +22,7 @@ them with one NCCL all-reduce per step (torch.distributed).
 
 from __future__ import annotations
 
+import math
 from dataclasses import dataclass
 
 import torch
@@ -371,6 +372,44 @@ class NvlsExchange:
     def failed(self) -> bool:
         """Did a barrier give up waiting for a peer (host read, synchronises)?"""
         return bool(self.error.item())
+
+
+class StepMonitor:
+    """The trainer's failure checks (training/trainer.py:175-231) without a
+    host synchronisation per step: record(out) folds each step's overflow
+    word and pair count into device accumulators and keeps its loss;
+    check(epoch) reads them once and raises RuntimeError, in the trainer's
+    order, when a step overflowed the pair arena (bit 0 of the overflow
+    word), when a binning look-back wait gave up (bit 1), or when the last
+    recorded loss is not finite.  Returns {"epoch", "loss", "peak_pairs"}
+    and clears the accumulators."""
+
+    def __init__(self, pair_capacity: int, device=None):
+        self.capacity = int(pair_capacity)
+        self.overflow = torch.zeros(1, dtype=torch.int32, device=device)
+        self.peak_pairs = torch.zeros(1, dtype=torch.int32, device=device)
+        self.loss = torch.zeros((), dtype=torch.float32, device=device)
+
+    def record(self, out: StepOutput) -> None:
+        torch.bitwise_or(self.overflow, out.overflow.view(1), out=self.overflow)
+        torch.maximum(self.peak_pairs, out.pair_count.view(1), out=self.peak_pairs)
+        self.loss.copy_(out.loss.reshape(()))
+
+    def check(self, epoch: int = 0) -> dict:
+        overflow = int(self.overflow.item())
+        peak = int(self.peak_pairs.item())
+        loss = float(self.loss.item())
+        self.overflow.zero_()
+        self.peak_pairs.zero_()
+        self.loss.zero_()
+        if overflow & 2:
+            raise RuntimeError(f"epoch {epoch}: a binning scan gave up waiting for its "
+                               "predecessor; the table is incomplete")
+        if overflow & 1:
+            raise RuntimeError(f"epoch {epoch}: {peak} pairs exceed {self.capacity}")
+        if not math.isfinite(loss):
+            raise RuntimeError("non-finite training loss")
+        return {"epoch": epoch, "loss": loss, "peak_pairs": peak}
 
 
 def scatter_compact(grads, clusters, config: CapacityConfig, out=None):

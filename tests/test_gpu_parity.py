@@ -206,6 +206,49 @@ def test_binning_overflow_truncates_like_reference():
     _assert_tables_equal(table, exp)
 
 
+@pytest.mark.parametrize("arena_scale", [1.0, 0.5])
+def test_binning_poisoned_outputs_are_written_exactly(arena_scale):
+    """Poisoned output buffers (the reference pads its arena with
+    fill_padding, sorted_visibility.py:757-766): every counts, offsets and
+    arena slot below min(pair_count, arena) is written and equals the
+    oracle; no arena slot past it is touched, with and without overflow."""
+    from jaxgs_b200 import _lib as L
+
+    K = _kernels()
+    rng = np.random.default_rng(21)
+    width, height = 320, 200
+    proj = splats(rng, 1500, width, height, radius=(0.5, 40.0), huge=4)
+    full = O.bin(proj, width, height, 16, 8, 1 << 20)["pair_count"]
+    max_pairs = int(full * arena_scale) + 37
+    exp = O.bin(proj, width, height, 16, 8, max_pairs)
+    assert exp["overflow"] == (arena_scale < 1)
+    c = len(proj["alpha"])
+    tiles = (-(-width // 16)) * (-(-height // 8))
+    poison = -0x5A5A5A5B
+    projected = torch_proj(proj)
+    counts = torch.full((c,), poison, dtype=torch.int32, device="cuda")
+    ids = torch.full((max_pairs,), poison, dtype=torch.int32, device="cuda")
+    offsets = torch.full((tiles + 1,), poison, dtype=torch.int32, device="cuda")
+    pair_count = torch.full((1,), poison, dtype=torch.int32, device="cuda")
+    overflow = torch.full((1,), poison, dtype=torch.int32, device="cuda")
+    p = L.BinParams(c, width, height, 16, 8, max_pairs)
+    ws = K._workspace(L.lib.gsb_bin_workspace_size(L.ref(p)), "cuda")
+    L.check(L.lib.gsb_bin(K._stream(), L.ref(p), K._ptr(ws), ws.numel(),
+                          *(K._ptr(t) for t in (projected.mean, projected.conic, projected.alpha,
+                                                projected.depth, projected.visible, counts, ids,
+                                                offsets, pair_count, overflow))), "binning")
+    torch.cuda.synchronize()
+    assert int(pair_count.item()) == exp["pair_count"]
+    assert bool(overflow.item()) == exp["overflow"]
+    np.testing.assert_array_equal(counts.cpu().numpy(), exp["point_counts"])
+    np.testing.assert_array_equal(offsets.cpu().numpy(), exp["tile_offsets"])
+    used = min(exp["pair_count"], max_pairs)
+    got = ids.cpu().numpy()
+    np.testing.assert_array_equal(got[:used], exp["gaussian_ids"][:used])
+    assert (got[used:] == poison).all()
+    assert arena_scale < 1 or used < max_pairs
+
+
 def test_binning_config1_scene_bit_exact():
     """Full-size BASELINE config 1 (1M Gaussians, 1237x822, 8x16 tiles):
     GPU projection feeds both binnings."""

@@ -96,3 +96,67 @@ def test_a_rank_that_never_joins_is_detected_by_timeout():
         mp.spawn(_missing_rank_worker, args=(world, port, out), nprocs=world, join=True)
         assert out[1] == "left"
         assert out[0].startswith("error"), out[0]
+
+
+def _outputs(losses, overflows, pairs):
+    from jaxgs_b200.step import StepOutput
+
+    for loss, overflow, count in zip(losses, overflows, pairs):
+        yield StepOutput(torch.tensor(loss), (), (), torch.tensor([count], dtype=torch.int32),
+                         torch.tensor([overflow], dtype=torch.int32))
+
+
+def test_step_monitor_raises_like_the_trainer():
+    """training/trainer.py:190-191 (overflow raises at epoch end with the
+    peak pair count) and :230-231 (a non-finite loss raises); a healthy
+    epoch reports its last loss and peak pairs and clears the record."""
+    from jaxgs_b200.step import StepMonitor
+
+    monitor = StepMonitor(100)
+    for out in _outputs([0.5, 0.25], [0, 0], [40, 70]):
+        monitor.record(out)
+    assert monitor.check(3) == {"epoch": 3, "loss": 0.25, "peak_pairs": 70}
+    for out in _outputs([0.5, 0.4], [1, 0], [130, 20]):
+        monitor.record(out)
+    with pytest.raises(RuntimeError, match="epoch 4: 130 pairs exceed 100"):
+        monitor.check(4)
+    for out in _outputs([0.5], [2], [10]):
+        monitor.record(out)
+    with pytest.raises(RuntimeError, match="gave up waiting"):
+        monitor.check(5)
+    for out in _outputs([float("nan")], [0], [10]):
+        monitor.record(out)
+    with pytest.raises(RuntimeError, match="non-finite training loss"):
+        monitor.check(6)
+    assert monitor.check(7)["peak_pairs"] == 0
+
+
+def _raising_rank_worker(rank, world, port):
+    from datetime import timedelta
+
+    from jaxgs_b200.step import StepMonitor
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=5))
+    monitor = StepMonitor(100)
+    try:
+        for step in range(3):
+            grads = torch.ones(8)
+            dist.all_reduce(grads)
+            loss = float("nan") if (rank == 1 and step == 1) else 1.0 / (step + 1)
+            for out in _outputs([loss], [0], [10]):
+                monitor.record(out)
+            # Checked between steps, with no collective in flight.
+            monitor.check(step)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_a_rank_that_raises_between_steps_fails_the_job():
+    """A rank whose step check raises (a non-finite loss) leaves between
+    collectives; the launcher surfaces its error and the job ends instead
+    of the other rank waiting at its next all-reduce."""
+    world = 2
+    port = _free_port()
+    with pytest.raises(mp.ProcessRaisedException, match="non-finite training loss"):
+        mp.spawn(_raising_rank_worker, args=(world, port), nprocs=world, join=True)
