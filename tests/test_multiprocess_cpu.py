@@ -131,7 +131,7 @@ def test_step_monitor_raises_like_the_trainer():
     assert monitor.check(7)["peak_pairs"] == 0
 
 
-def _raising_rank_worker(rank, world, port):
+def _raising_rank_worker(rank, world, port, out):
     from datetime import timedelta
 
     from jaxgs_b200.step import StepMonitor
@@ -139,24 +139,31 @@ def _raising_rank_worker(rank, world, port):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=5))
     monitor = StepMonitor(100)
+    step = 0
     try:
         for step in range(3):
             grads = torch.ones(8)
             dist.all_reduce(grads)
             loss = float("nan") if (rank == 1 and step == 1) else 1.0 / (step + 1)
-            for out in _outputs([loss], [0], [10]):
-                monitor.record(out)
+            for result in _outputs([loss], [0], [10]):
+                monitor.record(result)
             # Checked between steps, with no collective in flight.
             monitor.check(step)
+        out[rank] = "completed"
+    except RuntimeError as exc:
+        out[rank] = (step, str(exc).splitlines()[0])
     finally:
         dist.destroy_process_group()
 
 
 def test_a_rank_that_raises_between_steps_fails_the_job():
     """A rank whose step check raises (a non-finite loss) leaves between
-    collectives; the launcher surfaces its error and the job ends instead
-    of the other rank waiting at its next all-reduce."""
+    collectives; the other rank's next all-reduce then fails (peer gone or
+    time-out) instead of waiting for good."""
     world = 2
     port = _free_port()
-    with pytest.raises(mp.ProcessRaisedException, match="non-finite training loss"):
-        mp.spawn(_raising_rank_worker, args=(world, port), nprocs=world, join=True)
+    with mp.Manager() as manager:
+        out = manager.dict()
+        mp.spawn(_raising_rank_worker, args=(world, port, out), nprocs=world, join=True)
+        assert out[1] == (1, "non-finite training loss")
+        assert out[0] != "completed" and out[0][0] == 2, out[0]
