@@ -12,22 +12,34 @@
 // They are carried as two float2 pairs, (mu_x, mu_y) and (E[x^2+y^2], E[xy]),
 // so every tap of every separable pass is two packed f32x2 FMAs (sm_100).
 //
-// One CTA per (32x16 output tile, channel).  The CTA stages the 52x36
-// zero-padded (x, y) patch of its channel (10-pixel halo), then runs four
-// separable 11-tap passes in shared memory.  Each thread owns a run of
-// consecutive outputs and accumulates them in registers while it streams
-// the inputs once (scatter form), so only the run's accumulators are live:
-//   1. vertical sums of the statistics      (26 rows x 52 columns)
-//   2. horizontal sums -> SSIM partials, loss (26 x 42)
-//   3. vertical blur of the partials          (16 x 42)
-//   4. horizontal blur -> image gradient      (16 x 32)
-// Row strides are padded to odd multiples so that lanes walking down a
-// column hit distinct banks.  About 54 KB of shared memory per CTA, so four
-// CTAs (32 warps) share an SM.  Per-CTA loss sums and |grad| maxima are
-// reduced by a single-block kernel in a fixed order, so the scalar results
-// are deterministic.
+// Row streaming.  One CTA per (32-column strip, segment of rows, channel)
+// walks down its segment 16 rows at a time.  The two vertical windows (the
+// statistics' and the partials') live in 32-row ring buffers in shared
+// memory, so a row is staged and its partials are formed once per strip
+// rather than once per tile: only the 10-column (statistics) and 5-column
+// (partials) horizontal halos are computed twice.  Per 16-row chunk k, with
+// statistics rows S_k = ys - 11 + 16k .. +15 and output rows S_k - 5 .. +10:
+//   stage   16 new (x, y) rows (52 columns) into the patch ring
+//   pass 1  vertical window sums of the statistics      (16 x 52)
+//   pass 2  horizontal sums -> SSIM partials, SSIM loss (16 x 42) -> ring
+//   pass 3  vertical blur of the partials               (16 x 42)
+//   pass 4  horizontal blur -> image gradient, L1 loss  (16 x 32)
+// Chunk 0 only fills the rings (its outputs precede the segment).  Each
+// thread of a pass owns a run of consecutive outputs and accumulates them in
+// registers while it streams the inputs once (scatter form).  Row strides
+// are padded to odd multiples so that lanes walking down a column hit
+// distinct banks.  About 43 KB of shared memory per CTA, four CTAs (32
+// warps) per SM.  Per-CTA loss sums and |grad| maxima are reduced by a
+// single-block kernel in a fixed order, so the scalar results are
+// deterministic.
+//
+// The stage and pass bodies are __host__ __device__ functions of (thread
+// index, shared state): the kernel runs them between barriers, and a host
+// build can run the same bodies thread by thread with checked indexing.
 #include <atomic>
+#include <cmath>
 #include <cstdio>
+#include <cstring>
 #include <mutex>
 
 #include "gsb_common.cuh"
@@ -35,20 +47,29 @@
 namespace gsb {
 namespace {
 
-constexpr int kTW = 32, kTH = 16, kR = 5, kTaps = 2 * kR + 1;
+constexpr int kTW = 32, kR = 5, kTaps = 2 * kR + 1;
+constexpr int kCH = 16;    // rows per chunk
+constexpr int kRing = 32;  // rows held by each ring buffer (a power of two)
 constexpr int kThreads = 256;
-constexpr int kSW = kTW + 2 * kR, kSH = kTH + 2 * kR;  // 42 x 26 statistics region
-constexpr int kPW = kTW + 4 * kR, kPH = kTH + 4 * kR;  // 52 x 36 staged patch
-constexpr int kRun1 = 7, kRuns1 = 4;          // pass 1: 26 rows as 4 runs of 7 (2 spare rows)
-constexpr int kRun2 = 6, kRuns2 = kSW / kRun2;  // pass 2: 42 columns as 7 runs of 6
-constexpr int kRun3 = 4, kRuns3 = kTH / kRun3;  // pass 3: 16 rows as 4 runs of 4
-constexpr int kRun4 = 4, kRuns4 = kTW / kRun4;  // pass 4: 32 columns as 8 runs of 4
-constexpr int kPRows = kRuns1 * kRun1 + 2 * kR;  // 38 staged rows (the 2 spare ones feed discarded outputs)
-static_assert(kPRows >= kPH, "patch rows");
-constexpr int kPStride = kPW + 1, kVStride = kPW + 1, kQStride = kSW + 1;
-static_assert(kRuns1 * kRun1 >= kSH && kRuns2 * kRun2 == kSW, "run cover");
-static_assert(kRuns1 * kPW <= kThreads && kRuns2 * kSH <= kThreads, "pass items");
-static_assert(kRuns3 * kSW <= kThreads && kRuns4 * kTH <= kThreads, "pass items");
+constexpr int kSW = kTW + 2 * kR;  // 42 statistics / partials columns
+constexpr int kPW = kTW + 4 * kR;  // 52 staged columns
+constexpr int kPStride = kPW + 1, kQStride = kSW + 1;
+constexpr int kRun1 = 4, kRuns1 = kCH / kRun1;  // pass 1: 16 rows as 4 runs of 4, x 52 columns
+constexpr int kRun2 = 3, kRuns2 = kSW / kRun2;  // pass 2: 42 columns as 14 runs of 3, x 16 rows
+constexpr int kRun3 = 4, kRuns3 = kCH / kRun3;  // pass 3: 16 rows as 4 runs of 4, x 42 columns
+constexpr int kRun4 = 4, kRuns4 = kTW / kRun4;  // pass 4: 32 columns as 8 runs of 4, x 16 rows
+static_assert(kRuns1 * kRun1 == kCH && kRuns2 * kRun2 == kSW, "run cover");
+static_assert(kRuns3 * kRun3 == kCH && kRuns4 * kRun4 == kTW, "run cover");
+static_assert(kRuns1 * kPW <= kThreads && kRuns2 * kCH <= kThreads, "pass items");
+static_assert(kRuns3 * kSW <= kThreads && kRuns4 * kCH <= kThreads, "pass items");
+static_assert(kPW <= 64 && kThreads % 64 == 0 && kCH % (kThreads / 64) == 0, "staging lanes");
+// Each ring holds two chunks of rows: the 26-row windows a chunk reads
+// (5 rows above its first row to 5 below its last, twice over for the
+// patch) stay inside the chunk and its neighbour when 2 kR <= kCH.
+static_assert(2 * kR <= kCH && kRing == 2 * kCH, "ring rows");
+// Statistics rows run kCH - kR rows ahead of the output rows, and the patch
+// rows another kCH - kR ahead of those (so chunk 1's outputs start at ys).
+constexpr int kPartLead = kCH - kR, kPatchLead = 2 * (kCH - kR);
 
 // exp(-(d/1.5)^2 / 2) normalised, correctly rounded to float32; d = t - 5.
 __host__ __device__ constexpr float tap(int t)
@@ -61,38 +82,310 @@ __host__ __device__ constexpr float tap(int t)
                              : 0.26601171493530273f;
 }
 
-__device__ __forceinline__ float2 tap2(int t) { return make_float2(tap(t), tap(t)); }
+// Packed f32x2 arithmetic on the device (each lane rounded like its scalar
+// form), the same lane by lane on the host.
+__host__ __device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c)
+{
+#ifdef __CUDA_ARCH__
+    return __ffma2_rn(a, b, c);
+#else
+    return make_float2(std::fmaf(a.x, b.x, c.x), std::fmaf(a.y, b.y, c.y));
+#endif
+}
 
-struct LossSmem {
-    float2 patch[kPRows][kPStride];  // (x, y) of this channel; x clipped when requested
-    union {
-        float4 v[kRuns1 * kRun1][kVStride];  // pass 1: (mu_x, mu_y, E[x^2+y^2], E[xy]) column sums
-        struct {
-            float2 q01[kTH][kQStride];  // pass 3: vertically blurred partials (p0, p1)
-            float q2[kTH][kQStride];    //         and p2
-        } q;
-    } u;
-    union {
-        struct {
-            float2 p01[kSH][kQStride];  // pass 2: partials (p0, p1)
-            float p2[kSH][kQStride];    //         and p2
-        } p;
-        float g[kTH][kTW + 1];  // pass 4: gradient tile
-    } w;
-};
+__host__ __device__ __forceinline__ float2 mul2(float2 a, float2 b)
+{
+#ifdef __CUDA_ARCH__
+    return __fmul2_rn(a, b);
+#else
+    return make_float2(a.x * b.x, a.y * b.y);
+#endif
+}
 
-__device__ __forceinline__ float clip01(float v) { return fminf(fmaxf(v, 0.0f), 1.0f); }
+__host__ __device__ __forceinline__ float2 tap2(int t) { return make_float2(tap(t), tap(t)); }
+
+// 1/x for the SSIM denominators (both >= 1e-4): the fast reciprocal on the
+// device, an IEEE divide on the host.
+__host__ __device__ __forceinline__ float recip(float x)
+{
+#ifdef __CUDA_ARCH__
+    return __fdividef(1.0f, x);
+#else
+    return 1.0f / x;
+#endif
+}
+
+template <typename T>
+__host__ __device__ __forceinline__ T load_ro(const T* p)
+{
+#ifdef __CUDA_ARCH__
+    return __ldg(p);
+#else
+    return *p;
+#endif
+}
+
+__host__ __device__ __forceinline__ float clip01(float v) { return fminf(fmaxf(v, 0.0f), 1.0f); }
 
 // d clip(v, 0, 1) / dv with jnp.maximum/minimum tie semantics (1/2 at a bound).
-__device__ __forceinline__ float clip_grad(float v)
+__host__ __device__ __forceinline__ float clip_grad(float v)
 {
     if (v > 0.0f && v < 1.0f) return 1.0f;
     if (v == 0.0f || v == 1.0f) return 0.5f;
     return 0.0f;
 }
 
+struct LossSmem {
+    float2 patch[kRing][kPStride];  // (x, y) rows of the channel, ring; x clipped when requested
+    union {
+        float4 v[kCH][kPStride];  // pass 1 -> 2: (mu_x, mu_y, E[x^2+y^2], E[xy]) column sums
+        struct {
+            float2 q01[kCH][kQStride];  // pass 3 -> 4: vertically blurred partials (p0, p1)
+            float q2[kCH][kQStride];    //              and p2
+        } r;
+    } u;
+    float2 p01[kRing][kQStride];  // SSIM partials (p0, p1), ring
+    float p2[kRing][kQStride];    //               and p2
+};
+
+// One CTA's strip: output columns [x0, x0 + 32), output rows [ys, ye) of
+// channel c.  Patch row y sits in ring row (y - ys + 22) & 31, partials row
+// y in (y - ys + 11) & 31 (both offsets are >= 0 for every row touched).
+struct Strip {
+    int width, height, x0, ys, ye, c;
+    float inv_n;
+};
+
+__host__ __device__ __forceinline__ int patch_ring(const Strip& g, int y) { return (y - g.ys + kPatchLead) & (kRing - 1); }
+__host__ __device__ __forceinline__ int part_ring(const Strip& g, int y) { return (y - g.ys + kPartLead) & (kRing - 1); }
+__host__ __device__ __forceinline__ int stats_row0(const Strip& g, int k) { return g.ys - kPartLead + kCH * k; }
+
+// Stage block j: image rows [ys - 22 + 16 j, +16) of the 52 columns from
+// x0 - 10, zero outside the image.  Every load of the thread is issued
+// before the first store so their latencies overlap.
 template <bool U8, bool CLIP>
-__global__ void __launch_bounds__(kThreads, 4) loss_kernel(int width, int height,
+__host__ __device__ __forceinline__ void stage_rows(int tid, LossSmem& S, const Strip& g, int j,
+                                                    const float* image, const void* target_raw)
+{
+    constexpr int kSweeps = kCH / (kThreads / 64);
+    const int col = tid & 63, row0 = tid >> 6;
+    const int gx = g.x0 - 2 * kR + col;
+    const bool col_in = col < kPW && gx >= 0 && gx < g.width;
+    const uint8_t* t8 = static_cast<const uint8_t*>(target_raw);
+    const float* tf = static_cast<const float*>(target_raw);
+    float xv[kSweeps], yv[kSweeps];
+#pragma unroll
+    for (int k = 0; k < kSweeps; k++) {
+        const int gy = g.ys - kPatchLead + kCH * j + row0 + k * (kThreads / 64);
+        xv[k] = 0.0f;
+        yv[k] = 0.0f;
+        if (col_in && gy >= 0 && gy < g.height) {
+            const int64_t idx = ((int64_t)gy * g.width + gx) * 3 + g.c;
+            xv[k] = load_ro(image + idx);
+            yv[k] = U8 ? (float)load_ro(t8 + idx) : load_ro(tf + idx);
+        }
+    }
+    if (col < kPW) {
+#pragma unroll
+        for (int k = 0; k < kSweeps; k++) {
+            const int gy = g.ys - kPatchLead + kCH * j + row0 + k * (kThreads / 64);
+            const float x = CLIP ? clip01(xv[k]) : xv[k];
+            const float y = U8 ? yv[k] * (float)(1.0 / 255.0) : yv[k];
+            S.patch[patch_ring(g, gy)][col] = make_float2(x, y);
+        }
+    }
+}
+
+// Pass 1: vertical window sums of (x, y) and (x^2 + y^2, xy) for the
+// chunk's 16 statistics rows, all 52 staged columns.
+__host__ __device__ __forceinline__ void pass1(int tid, LossSmem& S, const Strip& g, int k)
+{
+    if (tid >= kRuns1 * kPW) return;
+    const int q = tid % kPW, r0 = (tid / kPW) * kRun1;
+    const int y0 = stats_row0(g, k) + r0 - kR;  // first patch row of the run's windows
+    float2 m[kRun1], s[kRun1];
+#pragma unroll
+    for (int o = 0; o < kRun1; o++) m[o] = s[o] = make_float2(0.0f, 0.0f);
+#pragma unroll
+    for (int j = 0; j < kRun1 + 2 * kR; j++) {
+        const float2 v = S.patch[patch_ring(g, y0 + j)][q];
+        const float2 sq = mul2(v, v);
+        const float2 u = make_float2(sq.x + sq.y, v.x * v.y);
+#pragma unroll
+        for (int o = 0; o < kRun1; o++) {
+            const int t = j - o;
+            if (t >= 0 && t < kTaps) {
+                m[o] = fma2(tap2(t), v, m[o]);
+                s[o] = fma2(tap2(t), u, s[o]);
+            }
+        }
+    }
+#pragma unroll
+    for (int o = 0; o < kRun1; o++) S.u.v[r0 + o][q] = make_float4(m[o].x, m[o].y, s[o].x, s[o].y);
+}
+
+// Pass 2: horizontal sums -> statistics -> SSIM partials (zero outside the
+// image) into the partials ring, and the SSIM part of the loss on the
+// strip's own pixels.
+__host__ __device__ __forceinline__ void pass2(int tid, LossSmem& S, const Strip& g, int k, float& loss)
+{
+    if (tid >= kRuns2 * kCH) return;
+    const int r = tid % kCH, c0 = (tid / kCH) * kRun2;
+    const float weight = -0.2f * g.inv_n;
+    float2 m[kRun2], s[kRun2];
+#pragma unroll
+    for (int o = 0; o < kRun2; o++) m[o] = s[o] = make_float2(0.0f, 0.0f);
+#pragma unroll
+    for (int j = 0; j < kRun2 + 2 * kR; j++) {
+        const float4 v = S.u.v[r][c0 + j];
+        const float2 a = make_float2(v.x, v.y), b = make_float2(v.z, v.w);
+#pragma unroll
+        for (int o = 0; o < kRun2; o++) {
+            const int t = j - o;
+            if (t >= 0 && t < kTaps) {
+                m[o] = fma2(tap2(t), a, m[o]);
+                s[o] = fma2(tap2(t), b, s[o]);
+            }
+        }
+    }
+    const int gy = stats_row0(g, k) + r;
+    const bool row_in = gy >= 0 && gy < g.height;
+    const bool row_own = gy >= g.ys && gy < g.ye;
+    const int ring = part_ring(g, gy);
+#pragma unroll
+    for (int o = 0; o < kRun2; o++) {
+        const int cc = c0 + o;
+        const int gx = g.x0 - kR + cc;
+        float p0 = 0.0f, p1 = 0.0f, p2 = 0.0f;
+        if (row_in && gx >= 0 && gx < g.width) {
+            const float mx = m[o].x, my = m[o].y;
+            const float mxy = mx * my;
+            const float mm = fmaf(mx, mx, my * my);
+            const float A = mm + 1e-4f;
+            const float B = (s[o].x - mm) + 9e-4f;
+            const float Cc = fmaf(2.0f, mxy, 1e-4f);
+            const float D = fmaf(2.0f, s[o].y - mxy, 9e-4f);
+            const float inv_a = recip(A), inv_b = recip(B);
+            const float inv_ab = inv_a * inv_b;
+            const float ssim = Cc * D * inv_ab;
+            p0 = (my * (D - Cc) * inv_ab + mx * ssim * (inv_b - inv_a)) * (2.0f * weight);
+            p1 = -ssim * inv_b * weight;
+            p2 = 2.0f * Cc * inv_ab * weight;
+            if (row_own && cc >= kR && cc < kR + kTW) loss += 0.2f * (1.0f - ssim);
+        }
+        S.p01[ring][cc] = make_float2(p0, p1);
+        S.p2[ring][cc] = p2;
+    }
+}
+
+// Pass 3: vertical blur of the partials onto the chunk's 16 output rows.
+__host__ __device__ __forceinline__ void pass3(int tid, LossSmem& S, const Strip& g, int k)
+{
+    if (tid >= kRuns3 * kSW) return;
+    const int cc = tid % kSW, r0 = (tid / kSW) * kRun3;
+    const int y0 = stats_row0(g, k) - 2 * kR + r0;  // first partials row of the run's windows
+    float2 a[kRun3];
+    float b[kRun3];
+#pragma unroll
+    for (int o = 0; o < kRun3; o++) {
+        a[o] = make_float2(0.0f, 0.0f);
+        b[o] = 0.0f;
+    }
+#pragma unroll
+    for (int j = 0; j < kRun3 + 2 * kR; j++) {
+        const int ring = part_ring(g, y0 + j);
+        const float2 u = S.p01[ring][cc];
+        const float v = S.p2[ring][cc];
+#pragma unroll
+        for (int o = 0; o < kRun3; o++) {
+            const int t = j - o;
+            if (t >= 0 && t < kTaps) {
+                a[o] = fma2(tap2(t), u, a[o]);
+                b[o] = fmaf(tap(t), v, b[o]);
+            }
+        }
+    }
+#pragma unroll
+    for (int o = 0; o < kRun3; o++) {
+        S.u.r.q01[r0 + o][cc] = a[o];
+        S.u.r.q2[r0 + o][cc] = b[o];
+    }
+}
+
+// Pass 4: horizontal blur -> image gradient of the chunk's output rows
+// (written straight to global memory), the L1 part of the loss, |grad| max.
+template <bool CLIP>
+__host__ __device__ __forceinline__ void pass4(int tid, LossSmem& S, const Strip& g, int k,
+                                               const float* image, float* grad, float& loss,
+                                               uint32_t& scale_bits)
+{
+    if (tid >= kRuns4 * kCH) return;
+    const int r = tid % kCH, c0 = (tid / kCH) * kRun4;
+    float2 a[kRun4];
+    float b[kRun4];
+#pragma unroll
+    for (int o = 0; o < kRun4; o++) {
+        a[o] = make_float2(0.0f, 0.0f);
+        b[o] = 0.0f;
+    }
+#pragma unroll
+    for (int j = 0; j < kRun4 + 2 * kR; j++) {
+        const float2 u = S.u.r.q01[r][c0 + j];
+        const float v = S.u.r.q2[r][c0 + j];
+#pragma unroll
+        for (int o = 0; o < kRun4; o++) {
+            const int t = j - o;
+            if (t >= 0 && t < kTaps) {
+                a[o] = fma2(tap2(t), u, a[o]);
+                b[o] = fmaf(tap(t), v, b[o]);
+            }
+        }
+    }
+    const int gy = stats_row0(g, k) - kR + r;
+    if (gy < g.ys || gy >= g.ye) return;
+    const int ring = patch_ring(g, gy);
+#pragma unroll
+    for (int o = 0; o < kRun4; o++) {
+        const int col = c0 + o;
+        const int gx = g.x0 + col;
+        if (gx < g.width) {
+            const float2 xy = S.patch[ring][col + 2 * kR];
+            const float sign = xy.x > xy.y ? 1.0f : (xy.x < xy.y ? -1.0f : 0.0f);
+            float value = a[o].x + 2.0f * xy.x * a[o].y + xy.y * b[o] + 0.8f * sign * g.inv_n;
+            const int64_t idx = ((int64_t)gy * g.width + gx) * 3 + g.c;
+            if (CLIP) value *= clip_grad(load_ro(image + idx));
+            grad[idx] = value;
+            uint32_t bits;
+            memcpy(&bits, &value, sizeof(bits));
+            scale_bits = scale_bits > (bits & 0x7fffffffu) ? scale_bits : (bits & 0x7fffffffu);
+            loss += 0.8f * fabsf(xy.x - xy.y);
+        }
+    }
+}
+
+// Rows of the segment a CTA covers and the strip geometry of block (bx, by, c).
+__host__ __device__ __forceinline__ Strip strip_of(int width, int height, int seg_rows, int bx, int by,
+                                                   int c)
+{
+    Strip g;
+    g.width = width;
+    g.height = height;
+    g.x0 = bx * kTW;
+    g.ys = by * seg_rows;
+    g.ye = g.ys + seg_rows < height ? g.ys + seg_rows : height;
+    g.c = c;
+    g.inv_n = 1.0f / (3.0f * (float)width * (float)height);
+    return g;
+}
+
+// Chunks a CTA runs: one to fill the rings, then one per 16 output rows.
+__host__ __device__ __forceinline__ int strip_chunks(const Strip& g)
+{
+    return 1 + (g.ye - g.ys + kCH - 1) / kCH;
+}
+
+template <bool U8, bool CLIP>
+__global__ void __launch_bounds__(kThreads, 4) loss_kernel(int width, int height, int seg_rows,
                                                            const float* __restrict__ image,
                                                            const void* __restrict__ target_raw,
                                                            float* __restrict__ grad,
@@ -105,197 +398,23 @@ __global__ void __launch_bounds__(kThreads, 4) loss_kernel(int width, int height
     __shared__ float warp_loss[kThreads / 32];
     __shared__ uint32_t warp_scale[kThreads / 32];
     const int tid = threadIdx.x;
-    const int c = blockIdx.z;
-    const int x0 = blockIdx.x * kTW, y0 = blockIdx.y * kTH;
-    const float inv_n = 1.0f / (3.0f * (float)width * (float)height);
-    const float weight = -0.2f * inv_n;
-    const uint8_t* t8 = static_cast<const uint8_t*>(target_raw);
-    const float* tf = static_cast<const float*>(target_raw);
-
-    // Stage the zero-padded (x, y) patch of channel c: 64-lane rows, 4 rows
-    // per sweep.  Every load of the thread is issued before the first use so
-    // the rows' memory latencies overlap.
-    {
-        constexpr int kSweeps = (kPRows + kThreads / 64 - 1) / (kThreads / 64);
-        const int col = tid & 63, row0 = tid >> 6;
-        const int gx = x0 - 2 * kR + col;
-        const bool col_in = col < kPW && gx >= 0 && gx < width;
-        float xv[kSweeps], yv[kSweeps];
-#pragma unroll
-        for (int k = 0; k < kSweeps; k++) {
-            const int pr = row0 + k * (kThreads / 64);
-            const int gy = y0 - 2 * kR + pr;
-            xv[k] = 0.0f;
-            yv[k] = 0.0f;
-            if (col_in && pr < kPRows && gy >= 0 && gy < height) {
-                const int64_t idx = ((int64_t)gy * width + gx) * 3 + c;
-                xv[k] = __ldg(image + idx);
-                yv[k] = U8 ? (float)__ldg(t8 + idx) : __ldg(tf + idx);
-            }
-        }
-        if (col < kPW) {
-#pragma unroll
-            for (int k = 0; k < kSweeps; k++) {
-                const int pr = row0 + k * (kThreads / 64);
-                if (pr < kPRows) {
-                    const float x = CLIP ? clip01(xv[k]) : xv[k];
-                    const float y = U8 ? yv[k] * (float)(1.0 / 255.0) : yv[k];
-                    S.patch[pr][col] = make_float2(x, y);
-                }
-            }
-        }
-    }
-    __syncthreads();
-    // 1. Vertical window sums of (x, y) and (x^2 + y^2, xy).
-    if (tid < kRuns1 * kPW) {
-        const int q = tid % kPW, r0 = (tid / kPW) * kRun1;
-        float2 m[kRun1], s[kRun1];
-#pragma unroll
-        for (int o = 0; o < kRun1; o++) m[o] = s[o] = make_float2(0.0f, 0.0f);
-#pragma unroll
-        for (int j = 0; j < kRun1 + 2 * kR; j++) {
-            const float2 v = S.patch[r0 + j][q];
-            const float2 sq = __fmul2_rn(v, v);
-            const float2 u = make_float2(sq.x + sq.y, v.x * v.y);
-#pragma unroll
-            for (int o = 0; o < kRun1; o++) {
-                const int t = j - o;
-                if (t >= 0 && t < kTaps) {
-                    m[o] = __ffma2_rn(tap2(t), v, m[o]);
-                    s[o] = __ffma2_rn(tap2(t), u, s[o]);
-                }
-            }
-        }
-#pragma unroll
-        for (int o = 0; o < kRun1; o++)
-            S.u.v[r0 + o][q] = make_float4(m[o].x, m[o].y, s[o].x, s[o].y);
-    }
-    __syncthreads();
-    // 2. Horizontal sums -> statistics -> SSIM partials (zero outside the
-    // image) and the SSIM part of the loss on the tile's own pixels.
+    const Strip g = strip_of(width, height, seg_rows, blockIdx.x, blockIdx.y, blockIdx.z);
+    const int chunks = strip_chunks(g);
     float loss = 0.0f;
-    if (tid < kRuns2 * kSH) {
-        const int r = tid % kSH, c0 = (tid / kSH) * kRun2;
-        float2 m[kRun2], s[kRun2];
-#pragma unroll
-        for (int o = 0; o < kRun2; o++) m[o] = s[o] = make_float2(0.0f, 0.0f);
-#pragma unroll
-        for (int j = 0; j < kRun2 + 2 * kR; j++) {
-            const float4 v = S.u.v[r][c0 + j];
-            const float2 a = make_float2(v.x, v.y), b = make_float2(v.z, v.w);
-#pragma unroll
-            for (int o = 0; o < kRun2; o++) {
-                const int t = j - o;
-                if (t >= 0 && t < kTaps) {
-                    m[o] = __ffma2_rn(tap2(t), a, m[o]);
-                    s[o] = __ffma2_rn(tap2(t), b, s[o]);
-                }
-            }
-        }
-        const int gy = y0 - kR + r;
-        const bool row_in = gy >= 0 && gy < height;
-        const bool row_own = r >= kR && r < kR + kTH;
-#pragma unroll
-        for (int o = 0; o < kRun2; o++) {
-            const int cc = c0 + o;
-            const int gx = x0 - kR + cc;
-            float p0 = 0.0f, p1 = 0.0f, p2 = 0.0f;
-            if (row_in && gx >= 0 && gx < width) {
-                const float mx = m[o].x, my = m[o].y;
-                const float mxy = mx * my;
-                const float mm = fmaf(mx, mx, my * my);
-                const float A = mm + 1e-4f;
-                const float B = (s[o].x - mm) + 9e-4f;
-                const float Cc = fmaf(2.0f, mxy, 1e-4f);
-                const float D = fmaf(2.0f, s[o].y - mxy, 9e-4f);
-                const float inv_a = __fdividef(1.0f, A), inv_b = __fdividef(1.0f, B);
-                const float inv_ab = inv_a * inv_b;
-                const float ssim = Cc * D * inv_ab;
-                p0 = (my * (D - Cc) * inv_ab + mx * ssim * (inv_b - inv_a)) * (2.0f * weight);
-                p1 = -ssim * inv_b * weight;
-                p2 = 2.0f * Cc * inv_ab * weight;
-                if (row_own && cc >= kR && cc < kR + kTW) loss += 0.2f * (1.0f - ssim);
-            }
-            S.w.p.p01[r][cc] = make_float2(p0, p1);
-            S.w.p.p2[r][cc] = p2;
-        }
-    }
-    __syncthreads();
-    // 3. Vertical blur of the partials onto the tile rows.
-    if (tid < kRuns3 * kSW) {
-        const int cc = tid % kSW, r0 = (tid / kSW) * kRun3;
-        float2 a[kRun3];
-        float b[kRun3];
-#pragma unroll
-        for (int o = 0; o < kRun3; o++) {
-            a[o] = make_float2(0.0f, 0.0f);
-            b[o] = 0.0f;
-        }
-#pragma unroll
-        for (int j = 0; j < kRun3 + 2 * kR; j++) {
-            const float2 u = S.w.p.p01[r0 + j][cc];
-            const float v = S.w.p.p2[r0 + j][cc];
-#pragma unroll
-            for (int o = 0; o < kRun3; o++) {
-                const int t = j - o;
-                if (t >= 0 && t < kTaps) {
-                    a[o] = __ffma2_rn(tap2(t), u, a[o]);
-                    b[o] = fmaf(tap(t), v, b[o]);
-                }
-            }
-        }
-#pragma unroll
-        for (int o = 0; o < kRun3; o++) {
-            S.u.q.q01[r0 + o][cc] = a[o];
-            S.u.q.q2[r0 + o][cc] = b[o];
-        }
-    }
-    __syncthreads();
-    // 4. Horizontal blur -> image gradient; the L1 part of the loss.
-    if (tid < kRuns4 * kTH) {
-        const int r = tid % kTH, c0 = (tid / kTH) * kRun4;
-        float2 a[kRun4];
-        float b[kRun4];
-#pragma unroll
-        for (int o = 0; o < kRun4; o++) {
-            a[o] = make_float2(0.0f, 0.0f);
-            b[o] = 0.0f;
-        }
-#pragma unroll
-        for (int j = 0; j < kRun4 + 2 * kR; j++) {
-            const float2 u = S.u.q.q01[r][c0 + j];
-            const float v = S.u.q.q2[r][c0 + j];
-#pragma unroll
-            for (int o = 0; o < kRun4; o++) {
-                const int t = j - o;
-                if (t >= 0 && t < kTaps) {
-                    a[o] = __ffma2_rn(tap2(t), u, a[o]);
-                    b[o] = fmaf(tap(t), v, b[o]);
-                }
-            }
-        }
-        const bool row_in = y0 + r < height;
-#pragma unroll
-        for (int o = 0; o < kRun4; o++) {
-            const int col = c0 + o;
-            const float2 xy = S.patch[r + 2 * kR][col + 2 * kR];
-            const float sign = xy.x > xy.y ? 1.0f : (xy.x < xy.y ? -1.0f : 0.0f);
-            S.w.g[r][col] = a[o].x + 2.0f * xy.x * a[o].y + xy.y * b[o] + 0.8f * sign * inv_n;
-            if (row_in && x0 + col < width) loss += 0.8f * fabsf(xy.x - xy.y);
-        }
-    }
-    __syncthreads();
-    // Write the gradient tile (and its |max| for the scale).
     uint32_t scale_bits = 0;
-    for (int k = tid; k < kTH * kTW; k += kThreads) {
-        const int r = k / kTW, col = k % kTW;
-        const int px = x0 + col, py = y0 + r;
-        if (px < width && py < height) {
-            const int64_t idx = ((int64_t)py * width + px) * 3 + c;
-            float value = S.w.g[r][col];
-            if (CLIP) value *= clip_grad(__ldg(image + idx));
-            grad[idx] = value;
-            scale_bits = max(scale_bits, __float_as_uint(value) & 0x7fffffffu);
+    for (int k = 0; k < chunks; k++) {
+        if (k == 0) stage_rows<U8, CLIP>(tid, S, g, 0, image, target_raw);
+        stage_rows<U8, CLIP>(tid, S, g, k + 1, image, target_raw);
+        __syncthreads();
+        pass1(tid, S, g, k);
+        __syncthreads();
+        pass2(tid, S, g, k, loss);
+        __syncthreads();
+        if (k > 0) {
+            pass3(tid, S, g, k);
+            __syncthreads();
+            pass4<CLIP>(tid, S, g, k, image, grad, loss, scale_bits);
+            __syncthreads();
         }
     }
     loss = warp_sum(loss);
@@ -371,20 +490,37 @@ __global__ void __launch_bounds__(1024) loss_finish_kernel(int blocks, float inv
 }
 
 
-// 32x16 output tiles of one channel; the kernel runs one CTA per tile and channel.
+// Per-CTA slots: at most one per 32x16 block of pixels and channel (the
+// strips' segments are whole multiples of 16 rows).
+constexpr int kSlotRows = 16;
+
 int64_t loss_tiles(const gsb_loss_params& p)
 {
-    return (int64_t)ceil_div(p.width, kTW) * ceil_div(p.height, kTH);
+    return (int64_t)ceil_div(p.width, kTW) * ceil_div(p.height, kSlotRows);
 }
 
 bool loss_shape_ok(const gsb_loss_params& p)
 {
-    return p.width > 0 && p.height > 0 && ceil_div(p.height, kTH) <= 65535 &&
+    return p.width > 0 && p.height > 0 && ceil_div(p.height, kSlotRows) <= 65535 &&
            loss_tiles(p) <= (int64_t)1 << 28;
 }
 
-// The kernels need more than 48 KB of dynamic shared memory: opt in once per
-// device (a host-side function attribute; it never enters a graph capture).
+// Rows per segment: enough segments that the strips x segments x channels
+// CTAs fill about four per SM of a 148-SM B200 in one wave, each a whole
+// number of 16-row chunks.
+int loss_segment_rows(const gsb_loss_params& p)
+{
+    constexpr double kTargetCtas = 4.0 * 148.0;
+    const int strips = ceil_div(p.width, kTW);
+    const int chunks = ceil_div(p.height, kCH);
+    int segments = (int)std::lround(kTargetCtas / (3.0 * strips));
+    segments = segments < 1 ? 1 : (segments > chunks ? chunks : segments);
+    return ceil_div(ceil_div(p.height, segments), kCH) * kCH;
+}
+
+// The kernels need more than 48 KB of dynamic shared memory on some builds:
+// opt in once per device (a host-side function attribute; it never enters a
+// graph capture).
 std::atomic<uint64_t> g_loss_configured{0};
 
 int configure_loss_kernels()
@@ -414,15 +550,16 @@ int configure_loss_kernels()
 }
 
 // Loss kernel + fixed-order finish.  block_loss / block_scale hold one slot
-// per (tile, channel).
+// per CTA (strip, segment, channel).
 int launch_loss(cudaStream_t s, const gsb_loss_params& p, const float* image, const void* target,
                 float* loss, float* grad, float* scale, float* block_loss, uint32_t* block_scale)
 {
-    dim3 grid(ceil_div(p.width, kTW), ceil_div(p.height, kTH), 3);
+    const int seg_rows = loss_segment_rows(p);
+    dim3 grid(ceil_div(p.width, kTW), ceil_div(p.height, seg_rows), 3);
     const size_t smem = sizeof(LossSmem);
     auto launch = [&](auto kernel) {
-        gsb::launch(kernel, grid, kThreads, smem, s, p.width, p.height, image, target, grad, block_loss,
-                                            block_scale);
+        gsb::launch(kernel, grid, kThreads, smem, s, p.width, p.height, seg_rows, image, target, grad,
+                    block_loss, block_scale);
     };
     if (p.target_u8) {
         if (p.clip_input) launch(loss_kernel<true, true>);
@@ -433,8 +570,8 @@ int launch_loss(cudaStream_t s, const gsb_loss_params& p, const float* image, co
     }
     if (int e = check_launch()) return e;
     const float inv_n = 1.0f / (3.0f * (float)p.width * (float)p.height);
-    gsb::launch(loss_finish_kernel, 1, 1024, 0, s, (int)(3 * loss_tiles(p)), inv_n, block_loss, block_scale,
-                                          loss, scale);
+    const int blocks = (int)(grid.x * grid.y * grid.z);
+    gsb::launch(loss_finish_kernel, 1, 1024, 0, s, blocks, inv_n, block_loss, block_scale, loss, scale);
     return check_launch();
 }
 
