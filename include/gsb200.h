@@ -382,7 +382,7 @@ GSB_API int gsb_loss(gsb_stream_t stream, const gsb_loss_params* p, void* worksp
  * only planned buffers, a server with a fixed memory plan, a latency-bound
  * caller that cannot afford cudaMalloc's device synchronisation, or a plugin
  * ABI that passes only inputs and outputs.  Same arguments and results as
- * gsb_loss without the workspace; the per-tile temporaries live in a fixed
+ * gsb_loss without the workspace; the per-CTA temporaries live in a fixed
  * 384 KiB device array inside the library, held on every GPU that loads the
  * library's device code until the process exits.  The call allocates nothing.
  *  - Size limit: ceil(W/32) * ceil(H/16) <= GSB_LOSS_NOALLOC_MAX_TILES

@@ -615,8 +615,9 @@ extern "C" int gsb_loss(gsb_stream_t stream, const gsb_loss_params* p, void* wor
 // allocation on its request path; cudaMalloc and cudaFree can synchronise the
 // device, stalling every stream a latency-bound caller keeps busy; and a
 // plugin boundary that passes only input and output pointers gives the
-// callee nowhere to put a workspace.  gsb_loss needs 2 x 4 bytes per 32x16
-// tile and channel of temporaries (loss sums and |grad| maxima).  Here they
+// callee nowhere to put a workspace.  gsb_loss needs at most 2 x 4 bytes
+// per 32x16 block of pixels and channel of temporaries (one loss sum and
+// one |grad| maximum per CTA).  Here they
 // live in the fixed array below, part of this library's device image.
 //
 // Limits and sharing:
@@ -640,7 +641,7 @@ namespace gsb {
 namespace {
 
 constexpr int kNoallocMaxTiles = GSB_LOSS_NOALLOC_MAX_TILES;
-constexpr int kNoallocSlots = 3 * kNoallocMaxTiles;  // one per tile and channel
+constexpr int kNoallocSlots = 3 * kNoallocMaxTiles;  // one per 32x16 block and channel
 constexpr int kNoallocMaxDevices = 64;
 
 // [0, slots) loss sums (float bits), [slots, 2 slots) |grad| maxima.
