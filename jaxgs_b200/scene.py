@@ -17,7 +17,7 @@ distributions are the ones BASELINE.json's configs state, seeded with
 from __future__ import annotations
 
 import math
-from dataclasses import dataclass, field
+from dataclasses import dataclass
 
 import numpy as np
 

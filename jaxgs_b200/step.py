@@ -29,7 +29,7 @@ import torch
 
 from . import kernels as K
 from .scene import CapacityConfig
-from .types import DeviceCamera, GaussianArrays, ProjectedGaussians
+from .types import DeviceCamera, GaussianArrays
 
 
 _SIDE_STREAMS: dict = {}

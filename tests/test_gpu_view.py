@@ -49,7 +49,7 @@ def test_view_renderer_frames():
     forward for that view; a graph replay with another camera of the same
     resolution equals an eager frame of that camera; presets render."""
     from jaxgs_b200 import kernels as K
-    from jaxgs_b200.scene import Camera, CapacityConfig, config0_scene, world_cluster_bounds
+    from jaxgs_b200.scene import Camera, CapacityConfig, config0_scene
     from jaxgs_b200.types import DeviceCamera, GaussianArrays
     from jaxgs_b200.view import ViewRenderer, resize_camera
 

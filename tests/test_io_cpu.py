@@ -6,7 +6,6 @@ an NPZ keeps the whole fixed-capacity pool."""
 
 import numpy as np
 import pytest
-import torch
 
 from jaxgs_b200.io import _read_vertices, load_gaussians, save_gaussians
 from jaxgs_b200.types import GaussianArrays
