@@ -493,6 +493,10 @@ def run_reference(args) -> None:
         return
     from oracle import oracle as O
 
+    # A launcher sets OMP_NUM_THREADS=1 per rank; this rank is the only one
+    # working, so it takes every host thread it may run on.
+    O.set_num_threads(len(os.sched_getaffinity(0)))
+
     config = _config()
     pool_np, camera = _workload(0)
     import numpy as np

@@ -968,3 +968,15 @@ EXPORT int orc_num_threads(void)
     return 1;
 #endif
 }
+
+/* Threads of the parallel loops from here on (n >= 1; ignored without
+ * OpenMP).  A launcher may have set OMP_NUM_THREADS=1 for every rank; the
+ * one rank that runs the oracle takes the host's threads back with this. */
+EXPORT void orc_set_num_threads(int n)
+{
+#ifdef _OPENMP
+    if (n >= 1) omp_set_num_threads(n);
+#else
+    (void)n;
+#endif
+}

@@ -60,6 +60,8 @@ def lib():
         _lib.orc_loss.restype = ctypes.c_double
         _lib.orc_cluster_compact.restype = _int
         _lib.orc_num_threads.restype = _int
+        _lib.orc_set_num_threads.argtypes = [_int]
+        _lib.orc_set_num_threads.restype = None
     return _lib
 
 
@@ -77,6 +79,11 @@ def gs_logf(x: float) -> float:
 
 def num_threads() -> int:
     return int(lib().orc_num_threads())
+
+
+def set_num_threads(n: int) -> None:
+    """Threads of the oracle's parallel loops from here on."""
+    lib().orc_set_num_threads(_int(int(n)))
 
 
 def project_fwd(pool, camera, *, degree, sh_dim, clusters=None, cluster_size=128,
