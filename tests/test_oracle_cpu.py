@@ -453,3 +453,50 @@ def test_oracle_matches_committed_golden_fixtures():
             np.testing.assert_array_equal(now[key], data[key], err_msg=key)
         else:
             np.testing.assert_allclose(now[key], data[key], rtol=1e-5, atol=1e-6, err_msg=key)
+
+
+def test_oracle_whole_chain_matches_finite_differences():
+    """tests/test_cute.py:328-355: the gradient of a weighted sum of the
+    rendered image (weights arange(size) / size) through projection,
+    binning and fp32 compositing, against central differences, within
+    rtol 0.04 / atol 0.003 as there.  For the 12 Gaussians with the largest
+    opacity gradient, log_scale, rotation, opacity and an SH coefficient
+    all match with a step of 1e-4.  Positions use a 2e-5 step and at least
+    90% of them match: a 1e-3 move carries some pixel's alpha across the
+    1/256 cut, or a tile across the binning level, and no difference quotient
+    sees past that jump; a smaller step makes such a crossing rare, while
+    float32 rounding still leaves the quotient accurate."""
+    pool, cam, _ = _small_pool(300, seed=1)
+    W, H = cam.width, cam.height
+    weights = (np.arange(H * W * 3, dtype=np.float64) / (H * W * 3)).astype(np.float32)
+
+    def render(p):
+        proj = O.project_fwd(p, cam, degree=3, sh_dim=16)
+        table = O.bin(proj, W, H, 16, 8, 300 * 96)
+        return proj, table, O.raster_fwd(proj, table, W, H, 16, 8)
+
+    def loss(p):
+        return float(np.sum(render(p)[2]["rgb"].astype(np.float64) * weights))
+
+    proj, table, fwd = render(pool)
+    cot = O.raster_bwd(proj, table, fwd, weights, W, H, 16, 8)
+    cot["radius"] = np.zeros(300, np.float32)
+    grads = O.project_bwd(pool, cam, proj["color"], cot, degree=3, sh_dim=16)
+    names = ("xyz", "log_scale", "rotation", "opacity", "sh")
+
+    def check(name, index, h):
+        analytic = grads[names.index(name)].reshape(pool[name].shape)[index]
+        plus = {k: v.copy() for k, v in pool.items()}
+        minus = {k: v.copy() for k, v in pool.items()}
+        plus[name][index] += h
+        minus[name][index] -= h
+        numeric = (loss(plus) - loss(minus)) / (2 * h)
+        return abs(analytic - numeric) <= 0.003 + 0.04 * abs(numeric)
+
+    top = np.argsort(-np.abs(grads[3]))[:12]
+    for g in top:
+        for name, index in (("log_scale", (g, 1)), ("rotation", (g, 2)), ("opacity", (g, 0)),
+                            ("sh", (g, 1, 0))):
+            assert check(name, index, 1e-4), (name, index)
+    positions = [check("xyz", (g, c), 2e-5) for g in top for c in range(3)]
+    assert np.mean(positions) >= 0.9, positions
