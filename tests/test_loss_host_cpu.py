@@ -64,3 +64,38 @@ def test_host_run_of_the_loss_kernel_matches_oracle(harness, tmp_path, shape, u8
     assert scale == float(np.abs(grad).max())
     if shape[0] == 480:
         assert seg_rows > 16  # several chunks per CTA: the rings wrap
+
+
+@pytest.mark.parametrize("shape", [(1, 1, 3), (3, 5, 3), (17, 31, 3), (64, 49, 3)])
+def test_host_run_uint8_target_equals_normalised_float(harness, tmp_path, shape):
+    """tests/test_loss.py:35-51: a uint8 target and the same target divided
+    by 255 in float32 give bit-identical loss, gradient and |grad| maximum,
+    for a random prediction and for the normalised target itself (where the
+    L1 subgradient is zero and the loss vanishes)."""
+    rng = np.random.default_rng(42 + shape[0])
+    target = rng.integers(0, 256, shape, dtype=np.uint8)
+    target[0, 0] = [0, 128, 255]
+    normalised = target.astype(np.float32) * np.float32(1.0 / 255.0)
+    for prediction in (rng.uniform(0, 1, shape).astype(np.float32), normalised):
+        a = _run(harness, tmp_path, prediction, target, False)
+        b = _run(harness, tmp_path, prediction, normalised, False)
+        assert a[0] == b[0] and a[2] == b[2]
+        np.testing.assert_array_equal(a[1], b[1])
+    loss, grad, _, _ = _run(harness, tmp_path, normalised, target, False)
+    assert abs(loss) < 2e-6 and float(np.abs(grad).max()) < 2e-7
+
+
+@pytest.mark.parametrize("value", [0.0, np.nan, np.inf])
+def test_host_run_gradient_maximum_propagates_nan(harness, tmp_path, value):
+    """tests/test_loss.py:70-77: the |grad| maximum is taken over the float
+    bits, so a NaN anywhere in the gradient (from a NaN or infinite
+    prediction) makes it NaN, and it equals max |grad| otherwise."""
+    prediction = np.zeros((17, 31, 3), np.float32)
+    prediction[0, 0, 0] = value
+    _, grad, scale, _ = _run(harness, tmp_path, prediction, np.zeros_like(prediction), False)
+    expected = float(np.max(np.abs(grad)))
+    if np.isnan(expected):
+        assert np.isnan(scale)
+    else:
+        assert scale == expected
+    assert np.isnan(scale) == (not np.isfinite(value))
