@@ -1,6 +1,7 @@
-"""The oracle against the reference's own edge, bounds, cutoff and
-visible-colour cases (CPU): tests/test_edge_support.py:15-93,
-tests/test_pipeline.py:200-228 and tests/test_projection_visibility.py."""
+"""The oracle against the reference's own edge, bounds, cutoff,
+rectangular-tile, infinite-depth and visible-colour cases (CPU):
+tests/test_edge_support.py:15-93, tests/test_pipeline.py:136-228 and
+tests/test_projection_visibility.py."""
 
 import numpy as np
 import pytest
@@ -153,3 +154,59 @@ def test_oracle_visible_color_only_preserves_render_and_pullback(degree, empty):
     for got, ref, width in zip(grads[0], grads[1], (3, 3, 4, 1, (degree + 1) ** 2 * 3)):
         np.testing.assert_array_equal(got.reshape(capacity, width)[:rows],
                                       ref.reshape(capacity, width)[:rows])
+
+
+def _splats(mean, depth, conic, radius, color, alpha, visible):
+    return {"mean": np.asarray(mean, np.float32).reshape(-1),
+            "depth": np.asarray(depth, np.float32),
+            "conic": np.asarray(conic, np.float32).reshape(-1),
+            "radius": np.asarray(radius, np.float32),
+            "color": np.asarray(color, np.float32).reshape(-1),
+            "alpha": np.asarray(alpha, np.float32),
+            "visible": np.asarray(visible, np.int8)}
+
+
+@pytest.mark.parametrize("tile_height", [8, 12])
+def test_oracle_rectangular_tiles_keep_rows_apart(tile_height):
+    """tests/test_pipeline.py:136-167: two splats in separate tile rows of
+    16 x tile_height tiles are binned into their own tiles only, each pixel
+    under a splat shows only that splat, and the pixel's gradient reaches
+    only its own splat's opacity."""
+    W, H = 17, 2 * tile_height + 1
+    proj = _splats([[8.0, 4.0], [8.0, tile_height + 4.0]], [1.0, 2.0],
+                   np.broadcast_to(np.eye(2) * 2, (2, 2, 2)), [3 / np.sqrt(2)] * 2,
+                   [[1.0, 0.0, 0.0], [0.0, 1.0, 0.0]], [0.5, 0.5], [1, 1])
+    table = O.bin(proj, W, H, 16, tile_height, 8)
+    np.testing.assert_array_equal(np.diff(table["tile_offsets"]), [1, 0, 1, 0, 0, 0])
+    assert not table["overflow"]
+    fwd = O.raster_fwd(proj, table, W, H, 16, tile_height)
+    image = fwd["rgb"].reshape(H, W, 3)
+    expected = 0.5 * np.exp(-0.5)
+    np.testing.assert_allclose(image[4, 8], [expected, 0, 0], atol=1e-7)
+    np.testing.assert_allclose(image[tile_height + 4, 8], [0, expected, 0], atol=1e-7)
+    np.testing.assert_array_equal(image[-1, -1], 0)
+    drgb = np.zeros((H, W, 3), np.float32)
+    drgb[tile_height + 4, 8, 1] = 1
+    cot = O.raster_bwd(proj, table, fwd, drgb.reshape(-1), W, H, 16, tile_height)
+    np.testing.assert_allclose(cot["alpha"], [0, np.exp(-0.5)], atol=1e-7)
+
+
+@pytest.mark.parametrize("has_visible", [False, True])
+def test_oracle_culled_slots_keep_infinite_depth_out_of_the_gradients(has_visible):
+    """tests/test_pipeline.py:170-197: culled slots carry depth = inf; the
+    rendered depth (sum of w d) and its gradients stay finite, with
+    d depth / d alpha = d and d depth / d d = w for the visible splat."""
+    proj = _splats(np.full((2, 2), 0.5), [2.0 if has_visible else np.inf, np.inf],
+                   np.broadcast_to(np.eye(2), (2, 2, 2)), [3.0, 3.0], np.full((2, 3), 0.4),
+                   [0.5, 0.0], [has_visible, False])
+    table = O.bin(proj, 1, 1, 16, 16, 4)
+    fwd = O.raster_fwd(proj, table, 1, 1, 16, 16)
+    np.testing.assert_allclose(fwd["depth"].sum(), 1.0 if has_visible else 0.0)
+    np.testing.assert_allclose(fwd["rgb"], 0.2 if has_visible else 0.0, rtol=1e-6)
+    np.testing.assert_allclose(fwd["alpha"], 0.5 if has_visible else 0.0)
+    cot = O.raster_bwd(proj, table, fwd, np.zeros(3, np.float32), 1, 1, 16, 16,
+                       ddepth=np.ones(1, np.float32))
+    for name in ("mean", "depth", "conic", "color", "alpha"):
+        assert np.isfinite(cot[name]).all(), name
+    np.testing.assert_allclose(cot["alpha"], [2.0 if has_visible else 0.0, 0.0])
+    np.testing.assert_allclose(cot["depth"], [0.5 if has_visible else 0.0, 0.0])
