@@ -500,3 +500,86 @@ def test_oracle_whole_chain_matches_finite_differences():
             assert check(name, index, 1e-4), (name, index)
     positions = [check("xyz", (g, c), 2e-5) for g in top for c in range(3)]
     assert np.mean(positions) >= 0.9, positions
+
+
+def _autograd_projection(pool, cam, degree, weights_fn):
+    """Gradients of weights_fn(projected fields) through the torch
+    restatement of render/projection.py, in float64."""
+    params = [torch.tensor(pool[k], dtype=torch.float64, requires_grad=True)
+              for k in ("xyz", "log_scale", "rotation", "opacity", "sh")]
+    out = R.project(*params, torch.as_tensor(pool["alive"]), cam, degree)
+    weights_fn(*out[:6]).backward()
+    return [p.grad.numpy() for p in params]
+
+
+def test_oracle_projection_pullback_zero_and_individual_cotangents():
+    """tests/test_cute.py:356-390: one cotangent per Gaussian (depth, radius,
+    mean, conic, colour, alpha on Gaussians 1-6) reaches only its own
+    Gaussian's parameters, matching autodiff of the reference projection;
+    Gaussians 0, 7 and 8 get exact zeros."""
+    from jaxgs_b200.scene import Camera, CapacityConfig, create_gaussians, seed_gaussians
+
+    config = CapacityConfig(9, 1, 16, 16, 3)
+    cam = Camera.from_colmap([1, 0, 0, 0], [0, 0, 0], 20, 20, 16, 16, 32, 32)
+    pool = seed_gaussians(create_gaussians(config), np.tile([[0.1, 0.2, 2.0]], (9, 1)),
+                          np.full((9, 3), 0.4), scale=np.tile([[0.1, 0.2, 0.3]], (9, 1)),
+                          opacity=0.3)
+    pool["sh"][:, 1:] = 0.02
+
+    def weighted(mean, depth, conic, radius, color, alpha):
+        return (depth[1] + radius[2] * 0.01 + mean[3].sum() + conic[4].sum() + color[5].sum()
+                + alpha[6])
+
+    expected = _autograd_projection(pool, cam, 3, weighted)
+    cot = {"mean": np.zeros((9, 2), np.float32), "depth": np.zeros(9, np.float32),
+           "conic": np.zeros((9, 4), np.float32), "radius": np.zeros(9, np.float32),
+           "color": np.zeros((9, 3), np.float32), "alpha": np.zeros(9, np.float32)}
+    cot["depth"][1] = 1
+    cot["radius"][2] = 0.01
+    cot["mean"][3] = 1
+    cot["conic"][4] = 1
+    cot["color"][5] = 1
+    cot["alpha"][6] = 1
+    proj = O.project_fwd(pool, cam, degree=3, sh_dim=16)
+    grads = O.project_bwd(pool, cam, proj["color"], {k: v.reshape(-1) for k, v in cot.items()},
+                          degree=3, sh_dim=16)
+    for name, got, ref in zip(("xyz", "log_scale", "rotation", "opacity", "sh"), grads, expected):
+        got = got.reshape(ref.shape)
+        np.testing.assert_allclose(got, ref, rtol=2e-4, atol=2e-5, err_msg=name)
+        np.testing.assert_array_equal(got[[0, 7, 8]], 0)
+
+
+@pytest.mark.parametrize("degree", [0, 2])
+def test_oracle_projection_pullback_clipped_color_and_near_plane(degree):
+    """tests/test_cute.py:439-476: a Gaussian in front of the near plane
+    (depth clamped in the Jacobian) whose colour is clipped to zero, beside
+    an ordinary one; the pullback of squared means and conics plus radii,
+    depths, colours and alphas matches autodiff (rtol 3e-3, atol 3e-4)."""
+    from jaxgs_b200.scene import Camera, CapacityConfig, create_gaussians
+
+    config = CapacityConfig(2, 2, 2, 4, degree)
+    cam = Camera.from_colmap([1, 0, 0, 0], [0, 0, 0], 8, 8, 4, 4, 8, 8)
+    pool = create_gaussians(config)
+    pool["xyz"][:] = [[0.005, -0.003, 0.1], [0.1, 0.2, 2.0]]
+    pool["log_scale"][:] = np.log([[0.1, 0.2, 0.3], [0.2, 0.15, 0.1]])
+    pool["rotation"][:] = [[0.9, 0.2, -0.1, 0.15], [0.8, -0.1, 0.25, 0.2]]
+    pool["opacity"][:] = [[0.1], [-0.2]]
+    pool["sh"][:] = 0.1
+    pool["sh"][0, 0, 0] = -3.0
+    pool["alive"][:] = True
+    sh_dim = (degree + 1) ** 2
+    proj = O.project_fwd(pool, cam, degree=degree, sh_dim=sh_dim)
+    assert proj["color"][0] == 0.0
+
+    def weighted(mean, depth, conic, radius, color, alpha):
+        return ((mean ** 2).sum() + (conic ** 2).sum() + radius.sum() + depth.sum()
+                + color.sum() + alpha.sum())
+
+    expected = _autograd_projection(pool, cam, degree, weighted)
+    cot = {"mean": 2 * proj["mean"], "depth": np.ones(2, np.float32),
+           "conic": 2 * proj["conic"], "radius": np.ones(2, np.float32),
+           "color": np.ones(6, np.float32), "alpha": np.ones(2, np.float32)}
+    grads = O.project_bwd(pool, cam, proj["color"], cot, degree=degree, sh_dim=sh_dim)
+    for name, got, ref in zip(("xyz", "log_scale", "rotation", "opacity", "sh"), grads, expected):
+        np.testing.assert_allclose(got.reshape(ref.shape), ref, rtol=3e-3, atol=3e-4,
+                                   err_msg=name)
