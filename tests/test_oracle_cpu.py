@@ -583,3 +583,53 @@ def test_oracle_projection_pullback_clipped_color_and_near_plane(degree):
     for name, got, ref in zip(("xyz", "log_scale", "rotation", "opacity", "sh"), grads, expected):
         np.testing.assert_allclose(got.reshape(ref.shape), ref, rtol=3e-3, atol=3e-4,
                                    err_msg=name)
+
+
+@pytest.mark.parametrize("degree", [0, 1, 3])
+@pytest.mark.parametrize("empty", [False, True])
+@pytest.mark.parametrize("cluster_size", [65, 128])
+def test_oracle_active_sh_and_color_only_pullbacks_match_the_full_one(degree, empty,
+                                                                       cluster_size):
+    """tests/test_packed.py:14-78: in compact order, the active-bands SH
+    gradient is the prefix of the full one and every other field is the
+    same; the colour-only pullback's [C, 1, 3] cotangent times the SH DC
+    constant is the full DC gradient."""
+    from jaxgs_b200.scene import Camera, CapacityConfig, create_gaussians, seed_gaussians
+
+    capacity = 257
+    config = CapacityConfig(capacity, cluster_size, 16, 16, 3, 4096, tile_height=8)
+    cam = Camera.from_colmap([1, 0, 0, 0], [0, 0, 0], 20, 20, 9, 8, 19, 17)
+    visible = (np.zeros(capacity, bool) if empty
+               else (np.arange(capacity) // cluster_size) % 2 == 0)
+    pool = seed_gaussians(create_gaussians(config), np.tile([[0.1, -0.2, 2.0]], (capacity, 1)),
+                          np.full((capacity, 3), 0.4), scale=0.1)
+    pool["alive"] = visible.copy()
+    pool["sh"] = (np.random.default_rng(5).normal(0, 0.2, pool["sh"].shape)).astype(np.float32)
+    listed = np.unique(np.nonzero(visible)[0] // cluster_size).astype(np.int32)
+    n_clusters = -(-capacity // cluster_size)
+    clusters = (np.pad(listed, (0, n_clusters - len(listed))), len(listed))
+    proj = O.project_fwd(pool, cam, degree=degree, sh_dim=16, clusters=clusters,
+                         cluster_size=cluster_size)
+    cot = {"mean": np.ones(capacity * 2, np.float32), "conic": np.full(capacity * 4, 0.01, np.float32),
+           "color": np.ones(capacity * 3, np.float32), "alpha": np.ones(capacity, np.float32),
+           "depth": np.zeros(capacity, np.float32), "radius": np.zeros(capacity, np.float32)}
+    common = dict(degree=degree, sh_dim=16, clusters=clusters, cluster_size=cluster_size,
+                  compact_gradients=True, rgb_only=True)
+    full = O.project_bwd(pool, cam, proj["color"], cot, **common)
+    sh_dim = (degree + 1) ** 2
+    narrow = O.project_bwd(pool, cam, proj["color"], cot, sh_gradient_dim=sh_dim, **common)
+    color = O.project_bwd(pool, cam, proj["color"], cot, sh_color_only=True, **common)
+    rows = int(visible.sum())
+    widths = (3, 3, 4, 1)
+    for a, b, c, w in zip(narrow[:4], full[:4], color[:4], widths):
+        np.testing.assert_allclose(a.reshape(capacity, w)[:rows], b.reshape(capacity, w)[:rows],
+                                   rtol=2e-5, atol=2e-6)
+        np.testing.assert_allclose(c.reshape(capacity, w)[:rows], b.reshape(capacity, w)[:rows],
+                                   rtol=2e-5, atol=2e-6)
+    full_sh = full[4].reshape(capacity, 16, 3)[:rows]
+    np.testing.assert_allclose(narrow[4].reshape(capacity, sh_dim, 3)[:rows], full_sh[:, :sh_dim],
+                               rtol=2e-5, atol=2e-6)
+    np.testing.assert_allclose(color[4].reshape(capacity, 1, 3)[:rows] * 0.28209479177387814,
+                               full_sh[:, :1], rtol=2e-5, atol=2e-6)
+    if not empty:
+        assert np.abs(full_sh[:, 0]).max() > 0
