@@ -2,7 +2,9 @@
 compute_densification_scores (:20-35) and decay_opacity (:158-165), one
 elementwise kernel each, and densify_step (:38-155), the pool management
 around them (prune, weighted sampling of parents, split/clone children into
-free slots), written with torch operations on the pool's device."""
+free slots), written with torch operations on the pool's device, and
+refresh_cluster_bounds (scene/cluster.py:15-37), which recomputes the
+culling bounds of the changed pool in place."""
 
 from __future__ import annotations
 
@@ -96,7 +98,7 @@ def densify_step(pool: GaussianArrays, state: AdamState, fragment_stats: torch.T
     comes from `generator` (on the pool's device), so the draws differ from
     the reference's JAX key stream; the budget arithmetic, ordering and
     child formulas are the reference's.  Returns (pool, state, born,
-    pruned)."""
+    pruned); the cluster bounds are stale afterwards (refresh_cluster_bounds)."""
     capacity = int(pool.xyz.shape[0])
     dev = pool.xyz.device
     scores, prune_mask = compute_densification_scores(pool, fragment_stats)
@@ -147,3 +149,38 @@ def densify_step(pool: GaussianArrays, state: AdamState, fragment_stats: torch.T
     pool.alive.copy_((pool.alive.to(torch.bool) | newborn).to(pool.alive.dtype))
     reset_adam_slots(state, newborn)
     return pool, state, int(newborn.sum().item()), prune_count
+
+
+def refresh_cluster_bounds(pool: GaussianArrays, bounds, cluster_size: int = 128):
+    """scene/cluster.py:15-37 on the pool's device, written in place into
+    the (center [N, 3], extent [N, 3], valid [N]) tensors of `bounds`: the
+    axis-aligned box of every cluster's alive Gaussians, each grown by its
+    rotated and scaled 1/255-level half extents (sqrt(2 ln 255) sigma).
+    Call it after densify_step, prune_step or an optimizer step that moved
+    Gaussians; updating in place keeps the tensors a captured
+    GraphedTrainingStep reads.  Same formulas as
+    scene.world_cluster_bounds, in float64."""
+    center, extent, valid = bounds
+    capacity = int(pool.xyz.shape[0])
+    n_clusters = -(-capacity // cluster_size)
+    if tuple(center.shape) != (n_clusters, 3) or tuple(extent.shape) != (n_clusters, 3) \
+            or tuple(valid.shape) != (n_clusters,):
+        raise ValueError(f"bounds must hold {n_clusters} clusters of {cluster_size} slots")
+    f64 = torch.float64
+    transform = _rotation_matrices(pool.rotation.to(f64)) * torch.exp(pool.log_scale.to(f64))[:, None, :]
+    half = transform.abs().sum(-1) * math.sqrt(2 * math.log(255.0))
+    alive = pool.alive.to(torch.bool)[:, None]
+    xyz = pool.xyz.to(f64)
+    pad = n_clusters * cluster_size - capacity
+    lower = torch.nn.functional.pad(torch.where(alive, xyz - half, math.inf), (0, 0, 0, pad),
+                                    value=math.inf)
+    upper = torch.nn.functional.pad(torch.where(alive, xyz + half, -math.inf), (0, 0, 0, pad),
+                                    value=-math.inf)
+    lower = lower.reshape(n_clusters, cluster_size, 3).amin(dim=1)
+    upper = upper.reshape(n_clusters, cluster_size, 3).amax(dim=1)
+    ok = torch.isfinite(lower[:, 0])
+    zero = torch.zeros((), dtype=f64, device=xyz.device)
+    center.copy_(torch.where(ok[:, None], (lower + upper) / 2, zero).to(center.dtype))
+    extent.copy_(torch.where(ok[:, None], (upper - lower) / 2, zero).to(extent.dtype))
+    valid.copy_(ok.to(valid.dtype))
+    return bounds
