@@ -198,8 +198,9 @@ def world_cluster_bounds(pool: dict, cluster_size: int):
     lower = lower.reshape(-1, cluster_size, 3).min(axis=1)
     upper = upper.reshape(-1, cluster_size, 3).max(axis=1)
     valid = np.isfinite(lower[:, 0])
-    center = np.where(valid[:, None], (lower + upper) / 2, 0).astype(np.float32)
-    half = np.where(valid[:, None], (upper - lower) / 2, 0).astype(np.float32)
+    with np.errstate(invalid="ignore"):  # empty clusters: inf + -inf, replaced below
+        center = np.where(valid[:, None], (lower + upper) / 2, 0).astype(np.float32)
+        half = np.where(valid[:, None], (upper - lower) / 2, 0).astype(np.float32)
     return center, half, valid
 
 

@@ -169,6 +169,6 @@ def test_fused_loss_scales_its_saved_gradient(oracle_bindings):
     loss = fused_loss(image, target, clip_input=True)
     (3 * loss).backward()
     value, grad = O.loss(np.clip(image.detach().numpy(), 0, 1), target.numpy())
-    np.testing.assert_allclose(float(loss), value, rtol=1e-6)
+    np.testing.assert_allclose(float(loss.detach()), value, rtol=1e-6)
     np.testing.assert_array_equal(image.grad.numpy(),
                                   (3 * torch.as_tensor(grad * O.clip_grad(image.detach().numpy()))).numpy())

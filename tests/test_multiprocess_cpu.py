@@ -63,7 +63,7 @@ def _expected(world):
 def test_view_sharded_gradients_sum_across_ranks():
     world = 2
     port = _free_port()
-    with mp.Manager() as manager:
+    with mp.get_context("spawn").Manager() as manager:
         out = manager.dict()
         mp.spawn(_sum_worker, args=(world, port, out), nprocs=world, join=True)
         results = [out[r] for r in range(world)]
@@ -91,7 +91,7 @@ def _missing_rank_worker(rank, world, port, out):
 def test_a_rank_that_never_joins_is_detected_by_timeout():
     world = 2
     port = _free_port()
-    with mp.Manager() as manager:
+    with mp.get_context("spawn").Manager() as manager:
         out = manager.dict()
         mp.spawn(_missing_rank_worker, args=(world, port, out), nprocs=world, join=True)
         assert out[1] == "left"
@@ -162,7 +162,7 @@ def test_a_rank_that_raises_between_steps_fails_the_job():
     time-out) instead of waiting for good."""
     world = 2
     port = _free_port()
-    with mp.Manager() as manager:
+    with mp.get_context("spawn").Manager() as manager:
         out = manager.dict()
         mp.spawn(_raising_rank_worker, args=(world, port, out), nprocs=world, join=True)
         assert out[1] == (1, "non-finite training loss")

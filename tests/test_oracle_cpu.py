@@ -372,7 +372,7 @@ def test_oracle_loss_matches_autograd(shape):
     ref = R.photometric_loss(x, torch.as_tensor(tgt, dtype=torch.float64))
     ref.backward()
     loss, grad = O.loss(pred, tgt)
-    np.testing.assert_allclose(loss, float(ref), rtol=2e-6)
+    np.testing.assert_allclose(loss, float(ref.detach()), rtol=2e-6)
     np.testing.assert_allclose(grad, x.grad.numpy(), rtol=2e-4, atol=1e-7)
 
 
