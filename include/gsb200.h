@@ -49,7 +49,12 @@ enum {
 
 #define GSB_ABI_VERSION 6
 
-/* Library ABI version (GSB_ABI_VERSION). */
+/* Library utilities.  No counterpart in the reference, whose boundary
+ * (cutlass.jax.cutlass_call) reports errors by raising in Python before
+ * launch; here the same checks return the codes above, and these three
+ * calls expose the version, the last CUDA error and a launch counter.
+ *
+ * Library ABI version (GSB_ABI_VERSION). */
 GSB_API int gsb_abi_version(void);
 /* Last CUDA error string seen by the library (thread-local). */
 GSB_API const char* gsb_last_error(void);
