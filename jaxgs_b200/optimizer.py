@@ -134,14 +134,32 @@ def sparse_adam_update(pool: GaussianArrays, state: AdamState, gradients, visibl
     the state; state.step counts the update in every slot of `visible` that
     is alive.  gradients: (xyz, log_scale, rotation, opacity, sh) in pool
     order, or the visible-cluster prefix with compact_gradients; the SH
-    gradient carries every coefficient of the pool.  Returns (pool, state)."""
+    gradient carries every coefficient of the pool.  Every field, moment and
+    gradient is checked before the first launch, so a rejected call leaves
+    the pool and the state untouched (the reference's trace-time checks,
+    tests/test_chex_contracts.py:57-76).  Returns (pool, state)."""
+    capacity = int(pool.alive.shape[0])
+    if tuple(visible.shape) != (capacity,):
+        raise ValueError("visible must hold one flag per pool slot")
+    if len(gradients) != len(PARAMETER_NAMES):
+        raise ValueError("gradients must be (xyz, log_scale, rotation, opacity, sh)")
+    for i, (name, gradient) in enumerate(zip(PARAMETER_NAMES, gradients)):
+        value = getattr(pool, name)
+        if tuple(state.m[i].shape) != tuple(value.shape) or \
+                tuple(state.v[i].shape) != tuple(value.shape):
+            raise ValueError(f"{name} moments must have the field's shape")
+        if gradient.dtype != torch.float32:
+            raise ValueError(f"{name} gradient must be float32")
+        if gradient.numel() != value.numel() and not compact_gradients:
+            raise ValueError(f"{name} gradient must cover every coefficient of the pool")
+        if gradient.dim() > 1 and tuple(gradient.shape[1:]) != tuple(value.shape[1:]):
+            raise ValueError(f"{name} gradient rows must have the field's shape "
+                             "(every SH coefficient)")
     rates = parameter_learning_rates(step, spatial_scale, max_steps, optimization)
     dev = pool.xyz.device
     rate_t = torch.tensor(rates, dtype=torch.float32, device=dev)
     for i, (name, gradient) in enumerate(zip(PARAMETER_NAMES, gradients)):
         value = getattr(pool, name)
-        if gradient.numel() != value.numel() and not compact_gradients:
-            raise ValueError(f"{name} gradient must cover every coefficient of the pool")
         update_field(value, state.m[i], state.v[i], gradient.contiguous(), pool.alive,
                      compacted_clusters, rate_t[i:i + 1], cluster_size, name == "sh",
                      compact_gradients)

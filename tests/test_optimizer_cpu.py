@@ -1,0 +1,44 @@
+"""sparse_adam_update refuses an incompatible call before any launch
+(tests/test_chex_contracts.py:57-76): a mask that is not one flag per
+slot, moments of another shape, a gradient of another dtype; the pool and
+the state stay as they were."""
+
+import dataclasses
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+
+@pytest.mark.parametrize("invalid", ["mask", "moment_shape", "gradient_dtype", "gradient_rows"])
+def test_sparse_adam_update_rejects_incompatible_state(invalid):
+    from jaxgs_b200.optimizer import create_adam_state, sparse_adam_update
+    from jaxgs_b200.scene import CapacityConfig, create_gaussians, seed_gaussians
+    from jaxgs_b200.types import GaussianArrays
+
+    pool_np = seed_gaussians(create_gaussians(CapacityConfig(2, sh_degree=1)), np.ones((1, 3)),
+                             np.full((1, 3), 0.5))
+    pool = GaussianArrays.from_numpy(pool_np, device="cpu")
+    state = create_adam_state(pool)
+    names = ("xyz", "log_scale", "rotation", "opacity", "sh")
+    gradients = [torch.ones_like(getattr(pool, n)) for n in names]
+    visible = pool.alive.to(torch.bool)
+    message = {"mask": "one flag per pool slot", "moment_shape": "moments",
+               "gradient_dtype": "float32", "gradient_rows": "coefficient"}[invalid]
+    if invalid == "mask":
+        visible = visible[:, None]
+    elif invalid == "moment_shape":
+        state = dataclasses.replace(state, m=(torch.zeros(1, 3), *state.m[1:]))
+    elif invalid == "gradient_dtype":
+        gradients[4] = gradients[4].double()
+    else:
+        gradients[4] = torch.ones(2, 1, 3)
+    before = [getattr(pool, n).clone() for n in names]
+    clusters = (torch.zeros(2, dtype=torch.int32), torch.ones(1, dtype=torch.int32))
+    with pytest.raises(ValueError, match=message):
+        sparse_adam_update(pool, state, gradients, visible, 0, 1.0, compacted_clusters=clusters,
+                           cluster_size=1)
+    for n, b in zip(names, before):
+        assert torch.equal(getattr(pool, n), b)
+    assert int(state.step.sum()) == 0
