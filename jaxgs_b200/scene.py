@@ -96,6 +96,8 @@ class Camera:
     def from_colmap(cls, qvec, tvec, fx, fy, cx, cy, width, height, near=0.2, far=1000.0):
         """scene/camera.py:19-56 (quaternion normalised in float32)."""
         q = np.asarray(qvec, np.float32)
+        if q.shape != (4,) or np.asarray(tvec).shape != (3,):
+            raise ValueError("COLMAP extrinsics are a wxyz quaternion [4] and a translation [3]")
         q = q / np.linalg.norm(q)
         w, x, y, z = q
         rotation = np.array(

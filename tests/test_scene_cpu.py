@@ -75,3 +75,10 @@ def test_ring_cameras_look_at_the_origin(radius):
         assert (cam.width, cam.height, cam.fx) == (1237, 822, 1040)
         origin = cam.world_to_camera @ np.array([0, 0, 0, 1.0])
         assert origin[2] > 0 and np.allclose(origin[:2], 0, atol=1e-4)
+
+
+@pytest.mark.parametrize("qvec,tvec", [([1, 0, 0], [0, 0, 0]), ([1, 0, 0, 0], [0, 0])])
+def test_camera_rejects_malformed_extrinsics(qvec, tvec):
+    """tests/test_chex_contracts.py:31-34."""
+    with pytest.raises(ValueError, match="quaternion"):
+        S.Camera.from_colmap(qvec, tvec, 4, 4, 2, 2, 4, 4)
