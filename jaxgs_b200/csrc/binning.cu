@@ -7,17 +7,24 @@
 //   1. count_kernel      — per Gaussian pair count and 32-bit depth key.
 //   2. depth sort        — 4 stable 8-bit LSD passes; the first pass drops the
 //                          0xFFFFFFFF keys of Gaussians without pairs, so the
-//                          remaining passes sort only binned Gaussians.
-//   3. scan              — inclusive scan of the counts in depth order.
-//   4. emission          — each Gaussian writes its pairs to its segment; one
-//                          thread per small Gaussian, one warp per large one.
-//   5. tile sort         — stable LSD passes over the tile key (digit plan of
+//                          remaining passes sort only binned Gaussians.  The
+//                          last pass also writes the counts in depth order and
+//                          sums them per block of 256 depth ranks.
+//   3. emission          — each block adds up the earlier blocks' sums and
+//                          scans its own counts (the inclusive scan of counts
+//                          in depth order), then each Gaussian writes its pairs
+//                          to its segment; one thread per small Gaussian, one
+//                          warp per large one.
+//   4. tile sort         — stable LSD passes over the tile key (digit plan of
 //                          kernels/pair_sort.py:33-37) of the emitted pairs.
-//   6. tile ranges       — offsets[t] = first pair with tile >= t.
-// Every stage is a plain kernel launch on one stream: no inter-block waits,
-// no host synchronisation; counts that only the device knows (binned
-// Gaussians, pairs) are read by the kernels, whose grids are sized for the
-// capacity and whose surplus blocks exit at once.
+//   5. tile ranges       — offsets[t] = first pair with tile >= t.
+// Every stage is a plain kernel launch on one stream, with no host
+// synchronisation; the only inter-block waits are the sort passes' bounded
+// look-backs.  Counts that only the device knows (binned Gaussians, pairs)
+// are read by the kernels, whose grids are sized for the capacity and whose
+// surplus blocks exit at once.
+#include <atomic>
+
 #include "gsb_common.cuh"
 
 namespace gsb {
@@ -30,7 +37,7 @@ namespace {
 struct Ellipse {
     float disc, level;
     int is_y;
-    float block_u, block_v;
+    float block_u, block_v, inv_block_v;
     int32_t u0, u1, v0, v1;
     float bbox_u_min, bbox_u_max, bbox_v_min, bbox_v_max, arg_min, arg_max;
 };
@@ -61,6 +68,20 @@ __device__ __forceinline__ void intersection(float px, float py, float c00, floa
     out_high = fadd(fdiv(high, coeff), pv);
 }
 
+// x / d for a tile dimension d.  When d is a power of two (inv = 1/d, else
+// inv = 0), x * inv is the same correctly rounded quotient -- the product
+// x * 2^-k is exact before its one rounding, as the quotient is -- so the
+// IEEE division becomes one multiply without changing a bit.
+__device__ __forceinline__ float div_dim(float x, float d, float inv)
+{
+    return inv != 0.0f ? fmul(x, inv) : fdiv(x, d);
+}
+
+__host__ __device__ inline float pow2_reciprocal(int d)
+{
+    return (d > 0 && (d & (d - 1)) == 0) ? 1.0f / (float)d : 0.0f;
+}
+
 // sorted_visibility.py:77-126
 __device__ __forceinline__ Ellipse ellipse_bounds(float px, float py, float c00, float c01,
                                                   float c11, float alpha, int tile_w, int tile_h,
@@ -85,20 +106,21 @@ __device__ __forceinline__ Ellipse ellipse_bounds(float px, float py, float c00,
     intersection(px, py, c00, c01, c11, disc, level, 1, argmax_x, 1, false, unused, xmax);
     intersection(px, py, c00, c01, c11, disc, level, 0, argmax_y, 1, false, unused, ymax);
     float tw = (float)tile_w, th = (float)tile_h;
-    int32_t x0 = max(0, min(tiles_x, trunc_i32(fdiv(xmin, tw))));
-    int32_t y0 = max(0, min(tiles_y, trunc_i32(fdiv(ymin, th))));
-    int32_t x1 = max(0, min(tiles_x, trunc_i32(fdiv(fsub(fadd(xmax, tw), 1.0f), tw))));
-    int32_t y1 = max(0, min(tiles_y, trunc_i32(fdiv(fsub(fadd(ymax, th), 1.0f), th))));
+    const float inv_tw = pow2_reciprocal(tile_w), inv_th = pow2_reciprocal(tile_h);
+    int32_t x0 = max(0, min(tiles_x, trunc_i32(div_dim(xmin, tw, inv_tw))));
+    int32_t y0 = max(0, min(tiles_y, trunc_i32(div_dim(ymin, th, inv_th))));
+    int32_t x1 = max(0, min(tiles_x, trunc_i32(div_dim(fsub(fadd(xmax, tw), 1.0f), tw, inv_tw))));
+    int32_t y1 = max(0, min(tiles_y, trunc_i32(div_dim(fsub(fadd(ymax, th), 1.0f), th, inv_th))));
     e.disc = disc;
     e.level = level;
     e.is_y = (y1 - y0) < (x1 - x0);
     if (e.is_y) {
-        e.block_u = th; e.block_v = tw;
+        e.block_u = th; e.block_v = tw; e.inv_block_v = inv_tw;
         e.u0 = y0; e.u1 = y1; e.v0 = x0; e.v1 = x1;
         e.bbox_u_min = ymin; e.bbox_u_max = ymax; e.bbox_v_min = xmin; e.bbox_v_max = xmax;
         e.arg_min = argmin_x; e.arg_max = argmax_x;
     } else {
-        e.block_u = tw; e.block_v = th;
+        e.block_u = tw; e.block_v = th; e.inv_block_v = inv_th;
         e.u0 = x0; e.u1 = x1; e.v0 = y0; e.v1 = y1;
         e.bbox_u_min = xmin; e.bbox_u_max = xmax; e.bbox_v_min = ymin; e.bbox_v_max = ymax;
         e.arg_min = argmin_y; e.arg_max = argmax_y;
@@ -116,8 +138,8 @@ __device__ __forceinline__ void span(const Ellipse& e, float line, float next_li
     float emax = fmaxf(lower_max, upper_max);
     if (line <= e.arg_min && e.arg_min < next_line) emin = e.bbox_v_min;
     if (line <= e.arg_max && e.arg_max < next_line) emax = e.bbox_v_max;
-    first = max(e.v0, min(e.v1, trunc_i32(fdiv(emin, e.block_v))));
-    end = min(e.v1, max(e.v0, trunc_i32(fadd(fdiv(emax, e.block_v), 1.0f))));
+    first = max(e.v0, min(e.v1, trunc_i32(div_dim(emin, e.block_v, e.inv_block_v))));
+    end = min(e.v1, max(e.v0, trunc_i32(fadd(div_dim(emax, e.block_v, e.inv_block_v), 1.0f))));
 }
 
 __device__ __forceinline__ uint32_t tile_key(int is_y, int32_t u, int32_t v, int tiles_x)
@@ -257,47 +279,79 @@ __device__ __forceinline__ uint32_t depth_key(float depth, int32_t count)
     return (bits >> 31) ? ~bits : (bits ^ 0x80000000u);
 }
 
-// _count, sorted_visibility.py:307-370.  Also accumulates the four 8-bit
-// digit histograms of the keys of Gaussians with pairs (the depth sort's
-// per-pass histograms), one shared-memory update per distinct digit per warp.
-__global__ void __launch_bounds__(256) count_kernel(int capacity, const float* __restrict__ mean,
-                                                    const float* __restrict__ conic,
-                                                    const float* __restrict__ alpha,
-                                                    const float* __restrict__ depth,
-                                                    const int8_t* __restrict__ visible,
-                                                    gsb_bin_params p, int tiles_x, int tiles_y,
-                                                    int32_t* __restrict__ counts,
-                                                    uint32_t* __restrict__ keys,
-                                                    uint32_t* __restrict__ depth_hist)
+// _count, sorted_visibility.py:307-370.  A block covers kCountSlots slots.
+// The cheap gate (visible, alpha, conic, screen bounds) runs first; the slots
+// that pass it are queued in shared memory and walked with full warps (the
+// AccuTile ellipse and row walk are the costly part, and about a third of the
+// slots pass).  The kernel also accumulates the four 8-bit digit histograms
+// of the keys of Gaussians with pairs (the depth sort's per-pass
+// histograms) in shared memory, and
+// zeroes this call's sort look-back words and per-block pair sums (`bulk`),
+// which only later kernels of the call read.
+constexpr int kCountThreads = 256;
+constexpr int kCountPerThread = 4;
+constexpr int kCountSlots = kCountThreads * kCountPerThread;
+
+__global__ void __launch_bounds__(kCountThreads) count_kernel(
+    int capacity, const float* __restrict__ mean, const float* __restrict__ conic,
+    const float* __restrict__ alpha, const float* __restrict__ depth,
+    const int8_t* __restrict__ visible, gsb_bin_params p, int tiles_x, int tiles_y,
+    int32_t* __restrict__ counts, uint32_t* __restrict__ keys, uint32_t* __restrict__ depth_hist,
+    uint4* __restrict__ bulk, int64_t bulk_vec4)
 {
     pdl_begin();
     __shared__ uint32_t hist[4][256];
+    __shared__ int32_t queue[kCountSlots];
+    __shared__ int queued;
     for (int i = threadIdx.x; i < 4 * 256; i += blockDim.x) (&hist[0][0])[i] = 0;
+    if (threadIdx.x == 0) queued = 0;
+    {
+        const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+        for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < bulk_vec4; i += stride)
+            bulk[i] = make_uint4(0u, 0u, 0u, 0u);
+    }
     __syncthreads();
-    const int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    int32_t count = 0;
-    if (g < capacity && visible[g] != 0) {
-        float2 m = *reinterpret_cast<const float2*>(mean + g * 2);
-        float4 c = *reinterpret_cast<const float4*>(conic + g * 4);
-        float a = alpha[g];
-        if (count_gate(m.x, m.y, c.x, c.y, c.w, a, p.width, p.height)) {
-            Splat s{fsub(m.x, 0.5f), fsub(m.y, 0.5f), c.x, c.y, c.w, a};
-            count = process_tiles<false, uint32_t>(s, p.tile_w, p.tile_h, tiles_x, tiles_y, 0, 0,
-                                                   0, nullptr, nullptr);
-        }
-    }
-    if (g < capacity) {
-        const uint32_t key = depth_key(depth[g], count);
-        counts[g] = count;
-        keys[g] = key;
-    }
-    const uint32_t key = g < capacity ? depth_key(depth[g], count) : 0xFFFFFFFFu;
+    const int lane = threadIdx.x & 31;
     const unsigned lt = lanemask_lt();
+    const int64_t first = (int64_t)blockIdx.x * kCountSlots;
 #pragma unroll
-    for (int pass = 0; pass < 4; pass++) {
-        const int d = count > 0 ? (int)((key >> (8 * pass)) & 255u) : 256;
-        const unsigned peers = __match_any_sync(GSB_FULL_MASK, d);
-        if ((peers & lt) == 0 && d < 256) atomicAdd(&hist[pass][d], (uint32_t)__popc(peers));
+    for (int k = 0; k < kCountPerThread; k++) {
+        const int64_t g = first + k * kCountThreads + threadIdx.x;
+        bool gated = false;
+        if (g < capacity && visible[g] != 0) {
+            const float2 m = *reinterpret_cast<const float2*>(mean + g * 2);
+            const float4 c = *reinterpret_cast<const float4*>(conic + g * 4);
+            gated = count_gate(m.x, m.y, c.x, c.y, c.w, alpha[g], p.width, p.height);
+        }
+        if (g < capacity && !gated) {
+            counts[g] = 0;
+            keys[g] = 0xFFFFFFFFu;
+        }
+        const unsigned mask = __ballot_sync(GSB_FULL_MASK, gated);
+        int at = 0;
+        if (lane == 0 && mask) at = atomicAdd(&queued, __popc(mask));
+        at = __shfl_sync(GSB_FULL_MASK, at, 0);
+        if (gated) queue[at + __popc(mask & lt)] = (int32_t)(g - first);
+    }
+    __syncthreads();
+    const int total = queued;
+    for (int base = 0; base < total; base += kCountThreads) {
+        const int q = base + threadIdx.x;
+        int32_t count = 0;
+        uint32_t key = 0xFFFFFFFFu;
+        if (q < total) {
+            const int64_t g = first + queue[q];
+            const Splat sp = load_splat(mean, conic, alpha, g);
+            count = process_tiles<false, uint32_t>(sp, p.tile_w, p.tile_h, tiles_x, tiles_y, 0, 0,
+                                                   0, nullptr, nullptr);
+            key = depth_key(depth[g], count);
+            counts[g] = count;
+            keys[g] = key;
+        }
+        if (count > 0) {
+#pragma unroll
+            for (int pass = 0; pass < 4; pass++) atomicAdd(&hist[pass][(key >> (8 * pass)) & 255u], 1u);
+        }
     }
     __syncthreads();
     for (int i = threadIdx.x; i < 4 * 256; i += blockDim.x) {
@@ -307,24 +361,36 @@ __global__ void __launch_bounds__(256) count_kernel(int capacity, const float* _
 }
 
 // ---------------------------------------------------------------------------
-// Stable LSD radix sort, onesweep style.
-//  * onesweep_hist_kernel reads the keys once and accumulates the digit
-//    histograms of every pass (a key's digits do not change between passes).
-//  * Each pass is one kernel.  A block takes the next partition index from an
-//    atomic counter, so every lower partition was taken by a block that is
-//    already running; it ranks its 2048 items with bit-ballot multisplit
-//    (stable within the tile), publishes its per-digit counts, then looks
-//    back over the predecessors' published counts until one carries an
-//    inclusive prefix (decoupled look-back), publishes its own inclusive
-//    prefix and scatters.  Items are staged in shared memory in digit order,
-//    so each digit's run leaves the block as consecutive addresses.
-//  * Every look-back spin is bounded; on expiry the block records an error
-//    word (reported as GSB_ERR_LAUNCH by the host on the next call) and uses
-//    what it has, so a fault can never turn into a hang.
-// The first depth-sort pass drops the 0xFFFFFFFF keys of Gaussians without
-// pairs; later passes sort only the survivors.
+// Stable LSD radix sort, onesweep style: one kernel per digit pass.
+//  * The digit histograms of every pass come from the kernels that produce
+//    the keys (count_kernel for the depth keys, the emission kernels for the
+//    tile keys; a key's digits do not change between passes), so no pass
+//    reads its input twice.
+//  * Partitions are large (512 threads x 8 items), so the binning's small
+//    sorts (a few hundred thousand to a few million items) have few of them
+//    and the look-back chain stays short.
+//  * Only the blocks a partition needs take one (blocks past the
+//    device-side item count exit at once); each takes the next partition
+//    index from an atomic counter, so every lower partition belongs to a
+//    block that is already running.  It ranks its items stably (bit-ballot
+//    multisplit: bits + 1 ballots per item, which measured faster here than
+//    __match_any_sync, whose throughput falls with many distinct digits;
+//    items are ordered by index, lane-major inside a warp's 256-item run,
+//    warps in order), publishes its per-digit counts at once, stages the
+//    items in shared memory in digit order and only then looks back over its
+//    predecessors' published counts until one carries an inclusive prefix
+//    (decoupled look-back), 32 predecessors per round trip.
+//  * Each digit's run leaves the block as consecutive addresses.
+//  * Every look-back wait is bounded; on expiry the block records an error
+//    word (reported as overflow bit 1) and uses what it has, so a fault can
+//    never turn into a hang.
+// The first depth pass drops the 0xFFFFFFFF keys of Gaussians without pairs;
+// later passes sort only the survivors.  The last depth pass also writes the
+// pair counts in depth order and adds them up per emission block, which is
+// the depth-ordered scan of sorted_visibility.py:511-603 minus its last step
+// (the emission kernel finishes it).
 // ---------------------------------------------------------------------------
-constexpr int kSortThreads = 256;
+constexpr int kSortThreads = 512;
 constexpr int kSortItems = 8;
 constexpr int kSortTile = kSortThreads * kSortItems;
 constexpr int kSortWarps = kSortThreads / 32;
@@ -333,6 +399,9 @@ constexpr uint32_t kFlagAggregate = 1u << 30;
 constexpr uint32_t kFlagPrefix = 2u << 30;
 constexpr uint32_t kValueMask = (1u << 30) - 1;
 constexpr int kSpinLimit = 1 << 22;
+constexpr int kLookBack = 32;
+// Emission: depth ranks per block.
+constexpr int kEmitThreads = 256;
 
 __device__ __forceinline__ int64_t read_count(const int32_t* ptr, int64_t cap)
 {
@@ -361,188 +430,210 @@ __device__ __forceinline__ unsigned same_digit_mask(int d, int bits)
     return m;
 }
 
-// Digit histograms of all passes: hist[pass * 256 + digit] (global atomics,
-// one per digit per block).  passes <= 4.
-template <typename K>
-__global__ void __launch_bounds__(kSortThreads) onesweep_hist_kernel(
-    const K* __restrict__ keys, const int32_t* n_ptr, int64_t n_cap, int passes, int bits,
-    bool drop_sentinel, uint32_t* __restrict__ hist)
+// Exclusive scan of one value per thread over a block of n_warps warps (all
+// threads participate); scratch holds n_warps words.
+__device__ __forceinline__ uint32_t block_exclusive_scan(uint32_t v, uint32_t* scratch)
 {
-    pdl_begin();
-    __shared__ uint32_t local[4][kMaxRadix];
-    const int64_t n = read_count(n_ptr, n_cap);
-    const int radix = 1 << bits;
-    for (int i = threadIdx.x; i < 4 * kMaxRadix; i += kSortThreads) (&local[0][0])[i] = 0;
-    __syncthreads();
-    const unsigned lt = lanemask_lt();
-    const int64_t stride = (int64_t)gridDim.x * kSortThreads;
-    for (int64_t base = (int64_t)blockIdx.x * kSortThreads; base < n; base += stride) {
-        const int64_t i = base + threadIdx.x;
-        const bool valid = i < n;
-        const K key = valid ? keys[i] : (K)0;
-        for (int pass = 0; pass < passes; pass++) {
-            const int d = item_digit(key, valid, drop_sentinel, pass * bits, radix);
-            const unsigned m = same_digit_mask(d, bits);
-            if ((m & lt) == 0 && d < radix) atomicAdd(&local[pass][d], (uint32_t)__popc(m));
-        }
-    }
-    __syncthreads();
-    for (int i = threadIdx.x; i < passes * radix; i += kSortThreads) {
-        const uint32_t c = local[i / radix][i % radix];
-        if (c) atomicAdd(hist + (i / radix) * kMaxRadix + (i % radix), c);
-    }
-}
-
-// Exclusive scan of 256 values held one per thread (all threads participate).
-__device__ __forceinline__ uint32_t block_exclusive_scan256(uint32_t v, uint32_t* scratch)
-{
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, warps = blockDim.x >> 5;
     const uint32_t inc = warp_inclusive_scan(v, lane);
     if (lane == 31) scratch[warp] = inc;
     __syncthreads();
-    uint32_t wb = 0;
-    for (int w = 0; w < warp; w++) wb += scratch[w];
+    if (warp == 0) {
+        const uint32_t t = lane < warps ? scratch[lane] : 0u;
+        const uint32_t ti = warp_inclusive_scan(t, lane);
+        __syncwarp();
+        if (lane < warps) scratch[lane] = ti - t;
+    }
     __syncthreads();
-    return wb + inc - v;
+    const uint32_t out = scratch[warp] + inc - v;
+    __syncthreads();
+    return out;
 }
 
+// The last depth pass's extra outputs: pair counts in depth order and their
+// sums per emission block.
+struct DepthTail {
+    const int32_t* counts;           // per Gaussian id
+    int32_t* sorted_counts;          // per depth rank
+    unsigned long long* block_sums;  // per kEmitThreads ranks
+};
+
+// Sum of the published counts of partitions part-1, part-2, ... down to the
+// first one that carries an inclusive prefix (that prefix included).  Words
+// are read 32 predecessors at a time; at a predecessor that has not
+// published yet, only that one word is polled (with a growing sleep).
+__device__ __forceinline__ uint32_t look_back(const uint32_t* status, int part, int radix, int d,
+                                              int32_t* error)
+{
+    volatile const uint32_t* st = status;
+    uint32_t excl = 0;
+    int j = part - 1;
+    int spins = 0;
+    while (true) {
+        uint32_t v[kLookBack];
+#pragma unroll
+        for (int k = 0; k < kLookBack; k++)
+            v[k] = (j - k >= 0) ? st[(int64_t)(j - k) * radix + d] : kFlagPrefix;
+        int k = 0;
+#pragma unroll
+        for (; k < kLookBack; k++) {
+            const uint32_t flag = v[k] & ~kValueMask;
+            if (flag == 0) break;  // not published yet
+            excl += v[k] & kValueMask;
+            if (flag == kFlagPrefix) return excl;
+        }
+        j -= k;
+        if (k == kLookBack) continue;
+        unsigned sleep_ns = 32;
+        while ((st[(int64_t)j * radix + d] & ~kValueMask) == 0) {
+            if (++spins > kSpinLimit) {
+                atomicExch(error, 1);
+                return excl;
+            }
+            __nanosleep(sleep_ns);
+            sleep_ns = sleep_ns < 256 ? sleep_ns * 2 : 256;
+        }
+    }
+}
+
+// Shared memory of one pass block (dynamic: above the 48 KB static limit).
 template <typename K>
+struct SortSmem {
+    uint16_t warp_hist[kSortWarps][kMaxRadix + 2];  // per-warp counts, then offsets
+    uint32_t global_off[kMaxRadix];
+    uint32_t block_start[kMaxRadix];
+    uint32_t scratch[kSortWarps];
+    K keys[kSortTile];
+    int32_t vals[kSortTile];
+    int part;
+    uint32_t valid;
+};
+
+template <typename K, bool TAIL>
 __global__ void __launch_bounds__(kSortThreads) onesweep_pass_kernel(
     const K* __restrict__ keys_in, const int32_t* __restrict__ vals_in, K* __restrict__ keys_out,
     int32_t* __restrict__ vals_out, const int32_t* n_ptr, int64_t n_cap, int shift, int bits,
     bool drop_sentinel, const uint32_t* __restrict__ pass_hist, uint32_t* status,
-    int32_t* part_counter, int32_t* n_out, int32_t* error)
+    int32_t* part_counter, int32_t* n_out, int32_t* error, DepthTail tail)
 {
     pdl_begin();
-    __shared__ uint32_t warp_hist[kSortWarps][kMaxRadix + 1];
-    __shared__ uint32_t global_off[kMaxRadix];
-    __shared__ uint32_t block_start[kMaxRadix];
-    __shared__ uint32_t scratch[kSortWarps];
-    __shared__ K s_keys[kSortTile];
-    __shared__ int32_t s_vals[kSortTile];
-    __shared__ int s_part;
-    __shared__ uint32_t s_valid;
+    extern __shared__ __align__(16) unsigned char sort_smem_raw[];
+    SortSmem<K>& sm = *reinterpret_cast<SortSmem<K>*>(sort_smem_raw);
     const int radix = 1 << bits;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int64_t n = read_count(n_ptr, n_cap);
-    if (threadIdx.x == 0) s_part = atomicAdd(part_counter, 1);
-    for (int d = lane; d <= radix; d += 32) warp_hist[warp][d] = 0;
-    __syncthreads();
-    const int part = s_part;
-    const int64_t base = (int64_t)part * kSortTile;
-    if (part == 0 && threadIdx.x == 0 && n_out) {
+    if (blockIdx.x == 0 && threadIdx.x == 0 && n_out) {
         uint32_t total = 0;
         for (int d = 0; d < radix; d++) total += pass_hist[d];
         *n_out = (int32_t)total;
     }
-    if (base >= n) return;  // uniform: no later partition waits on this one
-    K key[kSortItems];
-    int32_t val[kSortItems];
-    int digit[kSortItems];
-    uint32_t rank[kSortItems];
-    const int64_t wbase = base + (int64_t)warp * 32 * kSortItems;
-#pragma unroll
-    for (int r = 0; r < kSortItems; r++) {
-        const int64_t i = wbase + r * 32 + lane;
-        const bool valid = i < n;
-        key[r] = valid ? keys_in[i] : (K)0;
-        val[r] = valid ? (vals_in ? vals_in[i] : (int32_t)i) : 0;
-        digit[r] = item_digit(key[r], valid, drop_sentinel, shift, radix);
-    }
+    // Exactly ceil(n / kSortTile) blocks take a partition index.
+    if ((int64_t)blockIdx.x * kSortTile >= n) return;
+    if (threadIdx.x == 0) sm.part = atomicAdd(part_counter, 1);
+    for (int d = lane; d <= radix; d += 32) sm.warp_hist[warp][d] = 0;
+    __syncthreads();
+    const int part = sm.part;
+    const int64_t base = (int64_t)part * kSortTile;
+    uint32_t* my_status = status + (int64_t)part * radix;
+    const int d = threadIdx.x;
     const unsigned lt = lanemask_lt();
+    {
+        K key[kSortItems];
+        int32_t val[kSortItems];
+        int digit[kSortItems];
+        uint32_t rank[kSortItems];
+        const int64_t wbase = base + (int64_t)warp * 32 * kSortItems;
 #pragma unroll
-    for (int r = 0; r < kSortItems; r++) {
-        const int d = digit[r];
-        const unsigned m = same_digit_mask(d, bits);
-        const uint32_t before = warp_hist[warp][d];
-        __syncwarp();
-        rank[r] = before + __popc(m & lt);
-        if ((m & lt) == 0) warp_hist[warp][d] = before + __popc(m);
-        __syncwarp();
-    }
-    __syncthreads();
-    const int d = threadIdx.x;  // kSortThreads == kMaxRadix
-    uint32_t count = 0;
-    if (d < radix) {
-#pragma unroll
-        for (int w = 0; w < kSortWarps; w++) {
-            const uint32_t c = warp_hist[w][d];
-            warp_hist[w][d] = count;
-            count += c;
+        for (int r = 0; r < kSortItems; r++) {
+            const int64_t i = wbase + r * 32 + lane;
+            const bool valid = i < n;
+            key[r] = valid ? keys_in[i] : (K)0;
+            val[r] = valid ? (vals_in ? vals_in[i] : (int32_t)i) : 0;
+            digit[r] = item_digit(key[r], valid, drop_sentinel, shift, radix);
         }
-        // Publish this partition's count, then look back for the prefix.
-        volatile uint32_t* st = status;
-        if (part == 0) {
-            st[d] = kFlagPrefix | count;
-        } else {
-            st[(int64_t)part * kMaxRadix + d] = kFlagAggregate | count;
-        }
-    }
-    uint32_t excl = 0;
-    if (d < radix && part > 0) {
-        // Windowed look-back: the status words of up to kWindow predecessors
-        // are loaded together, so the walk costs one latency per window.
-        constexpr int kWindow = 8;
-        volatile uint32_t* st = status;
-        int j = part - 1;
-        int spins = 0;
-        bool done = false;
-        while (!done && j >= 0) {
-            uint32_t v[kWindow];
 #pragma unroll
-            for (int k = 0; k < kWindow; k++) v[k] = (j - k >= 0) ? (uint32_t)st[(int64_t)(j - k) * kMaxRadix + d] : (uint32_t)(2u << 30);
-            int k = 0;
-            uint32_t acc = 0;
-            for (; k < kWindow; k++) {
-                const uint32_t flag = v[k] & ~kValueMask;
-                if (flag == 0) break;  // not published yet: wait here
-                acc += v[k] & kValueMask;
-                if (flag == kFlagPrefix) {
-                    done = true;
-                    break;
-                }
+        for (int r = 0; r < kSortItems; r++) {
+            const int dr = digit[r];
+            const unsigned peers = same_digit_mask(dr, bits);
+            const uint32_t before = sm.warp_hist[warp][dr];
+            __syncwarp();
+            rank[r] = before + __popc(peers & lt);
+            if ((peers & lt) == 0) sm.warp_hist[warp][dr] = (uint16_t)(before + __popc(peers));
+            __syncwarp();
+        }
+        __syncthreads();
+        uint32_t count = 0;
+        if (d < radix) {
+            for (int w = 0; w < kSortWarps; w++) {
+                const uint32_t c = sm.warp_hist[w][d];
+                sm.warp_hist[w][d] = (uint16_t)count;
+                count += c;
             }
-            if (done) {
-                excl += acc;
-            } else if (k == kWindow) {
-                excl += acc;
-                j -= kWindow;
-            } else {
-                excl += acc;  // consume the published run, retry the first gap
-                j -= k;
-                if (++spins > kSpinLimit) {
-                    atomicExch(error, 1);
-                    done = true;
-                }
+            // Publish this partition's count before anything else, so that
+            // successors looking back find it early.
+            volatile uint32_t* st = my_status;
+            st[d] = (part == 0 ? kFlagPrefix : kFlagAggregate) | count;
+        }
+        const uint32_t start = block_exclusive_scan(d < radix ? count : 0u, sm.scratch);
+        if (d < radix) sm.block_start[d] = start;
+        if (d == radix - 1) sm.valid = start + count;
+        __syncthreads();
+        // Stage the items in digit order (registers are free afterwards).
+#pragma unroll
+        for (int r = 0; r < kSortItems; r++) {
+            const int dd = digit[r];
+            if (dd < radix) {
+                const uint32_t pos = sm.block_start[dd] + sm.warp_hist[warp][dd] + rank[r];
+                sm.keys[pos] = key[r];
+                sm.vals[pos] = val[r];
             }
         }
-        st[(int64_t)part * kMaxRadix + d] = kFlagPrefix | ((excl + count) & kValueMask);
     }
-    const uint32_t start = block_exclusive_scan256(count, scratch);
-    const uint32_t digit_base = block_exclusive_scan256(d < radix ? pass_hist[d] : 0u, scratch);
+    const uint32_t digit_base = block_exclusive_scan(d < radix ? pass_hist[d] : 0u, sm.scratch);
     if (d < radix) {
-        block_start[d] = start;
-        global_off[d] = digit_base + excl;
-    }
-    if (d == radix - 1) s_valid = start + count;
-    __syncthreads();
-#pragma unroll
-    for (int r = 0; r < kSortItems; r++) {
-        const int dd = digit[r];
-        if (dd < radix) {
-            const uint32_t pos = block_start[dd] + warp_hist[warp][dd] + rank[r];
-            s_keys[pos] = key[r];
-            s_vals[pos] = val[r];
+        uint32_t excl = 0;
+        if (part > 0) {
+            const uint32_t count =
+                (d == radix - 1 ? sm.valid : sm.block_start[d + 1]) - sm.block_start[d];
+            excl = look_back(status, part, radix, d, error);
+            volatile uint32_t* st = my_status;
+            st[d] = kFlagPrefix | ((excl + count) & kValueMask);
         }
+        sm.global_off[d] = digit_base + excl;
     }
     __syncthreads();
-    const uint32_t valid_count = s_valid;
-    for (uint32_t j = threadIdx.x; j < valid_count; j += kSortThreads) {
-        const K k = s_keys[j];
-        const int dd = (int)(((uint32_t)k >> shift) & (radix - 1));
-        const uint32_t dst = global_off[dd] + (j - block_start[dd]);
-        keys_out[dst] = k;
-        vals_out[dst] = s_vals[j];
+    const uint32_t valid_count = sm.valid;
+    if constexpr (!TAIL) {
+        for (uint32_t j = threadIdx.x; j < valid_count; j += kSortThreads) {
+            const K k = sm.keys[j];
+            const int dd = (int)(((uint32_t)k >> shift) & (radix - 1));
+            const uint32_t dst = sm.global_off[dd] + (j - sm.block_start[dd]);
+            keys_out[dst] = k;
+            vals_out[dst] = sm.vals[j];
+        }
+    } else {
+        // Whole warps iterate so that each warp can add up the counts of the
+        // ranks it wrote per emission block before one atomic per block.
+        for (uint32_t j0 = (uint32_t)warp * 32; j0 < valid_count; j0 += kSortThreads) {
+            const uint32_t j = j0 + lane;
+            uint32_t blk = 0xFFFFFFFFu, cnt = 0;
+            if (j < valid_count) {
+                const K k = sm.keys[j];
+                const int dd = (int)(((uint32_t)k >> shift) & (radix - 1));
+                const uint32_t dst = sm.global_off[dd] + (j - sm.block_start[dd]);
+                const int32_t v = sm.vals[j];
+                keys_out[dst] = k;
+                vals_out[dst] = v;
+                cnt = (uint32_t)tail.counts[v];
+                tail.sorted_counts[dst] = (int32_t)cnt;
+                blk = dst / kEmitThreads;
+            }
+            const unsigned peers = __match_any_sync(GSB_FULL_MASK, blk);
+            const uint32_t lo = __reduce_add_sync(peers, cnt & 0xFFFFu);
+            const uint32_t hi = __reduce_add_sync(peers, cnt >> 16);
+            if (blk != 0xFFFFFFFFu && (peers & lt) == 0)
+                atomicAdd(tail.block_sums + blk, ((unsigned long long)hi << 16) + lo);
+        }
     }
 }
 
@@ -554,68 +645,83 @@ __global__ void zero_u32_kernel(uint32_t* p, int64_t n)
         p[i] = 0;
 }
 
-// Zeroes up to three word ranges in one launch.
-__global__ void zero_ranges_kernel(uint32_t* a, int64_t na, uint32_t* b, int64_t nb, uint32_t* c,
-                                   int64_t nc)
+// The pass kernels' shared memory is above the static limit: raise each
+// instance's dynamic limit once per device.
+std::atomic<uint64_t> g_sort_configured{0};
+
+int configure_sort_kernels()
 {
-    pdl_begin();
-    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < na + nb + nc; i += stride) {
-        if (i < na) a[i] = 0;
-        else if (i < na + nb) b[i - na] = 0;
-        else c[i - na - nb] = 0;
+    int dev = 0;
+    cudaError_t err = cudaGetDevice(&dev);
+    if (err != cudaSuccess) {
+        set_error(err);
+        return GSB_ERR_LAUNCH;
     }
+    const uint64_t bit = dev >= 0 && dev < 64 ? (uint64_t)1 << dev : 0;
+    if (bit && (g_sort_configured.load(std::memory_order_acquire) & bit)) return GSB_OK;
+    const struct {
+        const void* fn;
+        int smem;
+    } kernels[] = {
+        {(const void*)onesweep_pass_kernel<uint32_t, false>, (int)sizeof(SortSmem<uint32_t>)},
+        {(const void*)onesweep_pass_kernel<uint32_t, true>, (int)sizeof(SortSmem<uint32_t>)},
+        {(const void*)onesweep_pass_kernel<uint16_t, false>, (int)sizeof(SortSmem<uint16_t>)},
+    };
+    for (const auto& k : kernels) {
+        err = cudaFuncSetAttribute(k.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, k.smem);
+        if (err != cudaSuccess) {
+            set_error(err);
+            return GSB_ERR_LAUNCH;
+        }
+    }
+    g_sort_configured.fetch_or(bit, std::memory_order_acq_rel);
+    return GSB_OK;
 }
 
-// Sort scratch: histograms [4][256], status [4][partitions][256], counters.
+// Sort scratch.  hist ([4][256] digit totals per pass) and counters (one
+// partition counter per pass) sit in the call's head region, zeroed first;
+// status ([passes][partitions][radix] look-back words) in the bulk region,
+// zeroed by count_kernel.
 struct SortScratch {
     uint32_t* hist;
     uint32_t* status;
     int32_t* counters;
     int partitions;
+    int radix;
 };
 
-// Histograms, look-back status words and partition counters are one
-// contiguous region, zeroed by one launch.
-int64_t sort_scratch_words(const SortScratch& w)
-{
-    return 4 * kMaxRadix + 4 * (int64_t)w.partitions * kMaxRadix + 8;
-}
-
-int zero_sort_scratch(cudaStream_t s, const SortScratch& w)
-{
-    gsb::launch(zero_u32_kernel, 256, 256, 0, s, w.hist, sort_scratch_words(w));
-    return check_launch();
-}
-
-// With hist_ready the caller has zeroed the scratch and accumulated the
-// per-pass digit histograms into w.hist (the producer kernels do it).
 template <typename K>
 int onesweep_sort(cudaStream_t s, const K* keys_in, const int32_t* vals_in, K* key_a, K* key_b,
                   int32_t* val_a, int32_t* val_b, int32_t* val_out, const K** sorted_keys,
                   const int32_t** sorted_vals, const int32_t* n_ptr, int64_t n_cap, int passes,
                   int bits, bool drop_sentinel, const SortScratch& w, int32_t* n_out,
-                  int32_t* error, bool hist_ready)
+                  int32_t* error, const DepthTail* tail)
 {
-    if (!hist_ready) {
-        if (int e = zero_sort_scratch(s, w)) return e;
-        gsb::launch(onesweep_hist_kernel<K>, 148 * 4, kSortThreads, 0, s, keys_in, n_ptr, n_cap, passes,
-                                                                 bits, drop_sentinel, w.hist);
-        if (int e = check_launch()) return e;
-    }
     const K* src_k = keys_in;
     const int32_t* src_v = vals_in;
     const int32_t* pass_n = n_ptr;
+    const int radix = 1 << bits;
+    const size_t smem = sizeof(SortSmem<K>);
     for (int pass = 0; pass < passes; pass++) {
         const bool last = pass == passes - 1;
         K* dst_k = (src_k == key_a) ? key_b : key_a;
         int32_t* dst_v = (last && val_out) ? val_out : ((src_v == val_a) ? val_b : val_a);
-        gsb::launch(onesweep_pass_kernel<K>, w.partitions, kSortThreads, 0, s, 
-            src_k, src_v, dst_k, dst_v, pass_n, n_cap, pass * bits, bits, drop_sentinel && pass == 0,
-            w.hist + pass * kMaxRadix, w.status + (int64_t)pass * w.partitions * kMaxRadix,
-            w.counters + pass, (pass == 0 && drop_sentinel) ? n_out : nullptr, error);
+        uint32_t* status = w.status + (int64_t)pass * w.partitions * radix;
+        const bool drop = drop_sentinel && pass == 0;
+        int32_t* count_out = drop ? n_out : nullptr;
+        if (last && tail) {
+            gsb::launch(onesweep_pass_kernel<K, true>, w.partitions, kSortThreads, smem, s, src_k,
+                        src_v, dst_k, dst_v, pass_n, n_cap, pass * bits, bits, drop,
+                        w.hist + pass * kMaxRadix, status, w.counters + pass, count_out, error,
+                        *tail);
+        } else {
+            gsb::launch(onesweep_pass_kernel<K, false>, w.partitions, kSortThreads, smem, s,
+                        src_k, src_v, dst_k, dst_v, pass_n, n_cap, pass * bits, bits, drop,
+                        w.hist + pass * kMaxRadix, status, w.counters + pass, count_out, error,
+                        DepthTail{});
+        }
         if (int e = check_launch()) return e;
-        if (pass == 0 && drop_sentinel) pass_n = n_out;
+        if (drop) pass_n = n_out;
         src_k = dst_k;
         src_v = dst_v;
     }
@@ -625,96 +731,11 @@ int onesweep_sort(cudaStream_t s, const K* keys_in, const int32_t* vals_in, K* k
 }
 
 // ---------------------------------------------------------------------------
-// Depth-ordered scan (sorted_visibility.py:511-603): ends[r] = sum of the
-// counts of ranks <= r; pair_count = ends[n-1]; overflow = pair_count > cap.
-// ---------------------------------------------------------------------------
-constexpr int kScanThreads = 256;
-constexpr int kScanItems = 4;
-constexpr int kScanTile = kScanThreads * kScanItems;
-
-__device__ __forceinline__ int64_t block_reduce_i64(int64_t v, int64_t* shared)
-{
-    int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    v = warp_sum(v);
-    if (lane == 0) shared[warp] = v;
-    __syncthreads();
-    int64_t total = 0;
-    for (int w = 0; w < kScanThreads / 32; w++) total += shared[w];
-    __syncthreads();
-    return total;
-}
-
-__global__ void __launch_bounds__(kScanThreads) scan_reduce_kernel(
-    const int32_t* __restrict__ order, const int32_t* __restrict__ counts, const int32_t* n_ptr,
-    int64_t n_cap, int64_t* __restrict__ block_sums)
-{
-    pdl_begin();
-    __shared__ int64_t shared[kScanThreads / 32];
-    int64_t n = read_count(n_ptr, n_cap);
-    int64_t base = (int64_t)blockIdx.x * kScanTile;
-    if (base >= n) return;
-    int64_t sum = 0;
-    for (int k = 0; k < kScanItems; k++) {
-        int64_t i = base + threadIdx.x * kScanItems + k;
-        if (i < n) sum += counts[order[i]];
-    }
-    sum = block_reduce_i64(sum, shared);
-    if (threadIdx.x == 0) block_sums[blockIdx.x] = sum;
-}
-
-__global__ void __launch_bounds__(kScanThreads) scan_kernel(
-    const int32_t* __restrict__ order, const int32_t* __restrict__ counts, const int32_t* n_ptr,
-    int64_t n_cap, const int64_t* __restrict__ block_sums, int64_t* __restrict__ ends,
-    int64_t max_pairs, int32_t* pair_count, int32_t* overflow, int32_t* n_pairs_clamped)
-{
-    pdl_begin();
-    __shared__ int64_t shared[kScanThreads / 32];
-    __shared__ int64_t warp_inc[kScanThreads / 32];
-    int64_t n = read_count(n_ptr, n_cap);
-    int64_t base = (int64_t)blockIdx.x * kScanTile;
-    if (n == 0) {
-        if (blockIdx.x == 0 && threadIdx.x == 0) {
-            *pair_count = 0;
-            *overflow = 0;
-            *n_pairs_clamped = 0;
-        }
-        return;
-    }
-    if (base >= n) return;
-    int64_t earlier = 0;
-    for (int64_t b = threadIdx.x; b < blockIdx.x; b += kScanThreads) earlier += block_sums[b];
-    earlier = block_reduce_i64(earlier, shared);
-    int64_t v[kScanItems];
-    int64_t running = 0;
-    for (int k = 0; k < kScanItems; k++) {
-        int64_t i = base + threadIdx.x * kScanItems + k;
-        v[k] = i < n ? counts[order[i]] : 0;
-        running += v[k];
-        v[k] = running;
-    }
-    int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    int64_t inc = warp_inclusive_scan(running, lane);
-    if (lane == 31) warp_inc[warp] = inc;
-    __syncthreads();
-    int64_t wb = 0;
-    for (int w = 0; w < warp; w++) wb += warp_inc[w];
-    int64_t before = earlier + wb + inc - running;
-    for (int k = 0; k < kScanItems; k++) {
-        int64_t i = base + threadIdx.x * kScanItems + k;
-        if (i < n) {
-            int64_t end = before + v[k];
-            ends[i] = end;
-            if (i == n - 1) {
-                *pair_count = (int32_t)(end < 0x7fffffff ? end : 0x7fffffff);
-                *overflow = end > max_pairs ? 1 : 0;
-                *n_pairs_clamped = (int32_t)(end < max_pairs ? end : max_pairs);
-            }
-        }
-    }
-}
-
-// ---------------------------------------------------------------------------
-// Emission (sorted_visibility.py:373-484).
+// Emission (sorted_visibility.py:373-484), with the last step of the
+// depth-ordered scan (sorted_visibility.py:511-603): a block's first pair
+// offset is the sum of the pair counts of the earlier blocks (one warp adds
+// the block sums written by the last depth pass; they are L2-resident), and
+// its threads' offsets follow from a block scan.
 // ---------------------------------------------------------------------------
 constexpr int kLanePairs = 16;
 
@@ -730,43 +751,83 @@ __device__ __forceinline__ void flush_key_hist(const uint32_t* local, int passes
     }
 }
 
+struct EmitScan {
+    const int32_t* sorted_counts;
+    const unsigned long long* block_sums;
+    int32_t* pair_count;
+    int32_t* overflow;
+    int32_t* n_pairs_clamped;
+};
+
 template <typename K>
-__global__ void __launch_bounds__(256) emit_kernel(
-    const int32_t* __restrict__ order, const int32_t* __restrict__ counts,
-    const int64_t* __restrict__ ends, const int32_t* n_ptr, int64_t n_cap,
+__global__ void __launch_bounds__(kEmitThreads) emit_kernel(
+    const int32_t* __restrict__ order, EmitScan scan, const int32_t* n_ptr, int64_t n_cap,
     const float* __restrict__ mean, const float* __restrict__ conic,
     const float* __restrict__ alpha, gsb_bin_params p, int tiles_x, int tiles_y,
-    K* __restrict__ keys, int32_t* __restrict__ values, int32_t* __restrict__ queue,
-    int32_t* __restrict__ queue_count, int passes, int bits, uint32_t* __restrict__ key_hist)
+    K* __restrict__ keys, int32_t* __restrict__ values, int32_t* __restrict__ queue_gid,
+    int32_t* __restrict__ queue_off, int32_t* __restrict__ queue_count, int passes, int bits,
+    uint32_t* __restrict__ key_hist)
 {
     pdl_begin();
     __shared__ uint32_t local[4 * 256];
+    __shared__ long long warp_total[kEmitThreads / 32];
+    __shared__ long long block_prefix;
+    const int64_t n = read_count(n_ptr, n_cap);
+    const int b = blockIdx.x;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (n == 0) {
+        if (b == 0 && threadIdx.x == 0) {
+            *scan.pair_count = 0;
+            *scan.overflow = 0;
+            *scan.n_pairs_clamped = 0;
+        }
+        return;
+    }
+    if ((int64_t)b * kEmitThreads >= n) return;  // uniform per block
     for (int i = threadIdx.x; i < passes * 256; i += blockDim.x) local[i] = 0;
-    __syncthreads();
-    const KeyHist hist{local, passes, bits};
-    int64_t n = read_count(n_ptr, n_cap);
-    int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (warp == 0) {
+        unsigned long long acc = 0;
+#pragma unroll 4
+        for (int i = lane; i < b; i += 32) acc += scan.block_sums[i];
+        acc = warp_sum(acc);
+        if (lane == 0) block_prefix = (long long)acc;
+    }
+    const int64_t r = (int64_t)b * kEmitThreads + threadIdx.x;
     int32_t count = 0, gid = 0;
-    int64_t offset = 0;
     if (r < n) {
         gid = order[r];
-        count = counts[gid];
-        offset = ends[r] - count;
+        count = scan.sorted_counts[r];
     }
+    const long long inc = warp_inclusive_scan((long long)count, lane);
+    if (lane == 31) warp_total[warp] = inc;
+    __syncthreads();
+    long long before = block_prefix;
+    for (int w = 0; w < warp; w++) before += warp_total[w];
+    const int64_t offset = before + inc - count;
+    if (r == n - 1) {
+        const int64_t end = offset + count;
+        *scan.pair_count = (int32_t)(end < 0x7fffffff ? end : 0x7fffffff);
+        *scan.overflow = end > p.max_pairs ? 1 : 0;
+        *scan.n_pairs_clamped = (int32_t)(end < p.max_pairs ? end : p.max_pairs);
+    }
+    const KeyHist hist{local, passes, bits};
     if (count > 0 && count <= kLanePairs && offset < p.max_pairs) {
         Splat s = load_splat(mean, conic, alpha, gid);
         process_tiles<true, K>(s, p.tile_w, p.tile_h, tiles_x, tiles_y, gid, offset, p.max_pairs,
                                keys, values, hist);
     }
-    bool large = count > kLanePairs && offset < p.max_pairs;
-    unsigned queued = __ballot_sync(GSB_FULL_MASK, large);
+    const bool large = count > kLanePairs && offset < p.max_pairs;
+    const unsigned queued = __ballot_sync(GSB_FULL_MASK, large);
     if (queued) {
-        int lane = threadIdx.x & 31;
-        int leader = __ffs(queued) - 1;
+        const int leader = __ffs(queued) - 1;
         int first = 0;
         if (lane == leader) first = atomicAdd(queue_count, __popc(queued));
         first = __shfl_sync(GSB_FULL_MASK, first, leader);
-        if (large) queue[first + __popc(queued & lanemask_lt())] = (int32_t)r;
+        if (large) {
+            const int slot = first + __popc(queued & lanemask_lt());
+            queue_gid[slot] = gid;
+            queue_off[slot] = (int32_t)offset;
+        }
     }
     flush_key_hist(local, passes, key_hist);
 }
@@ -776,9 +837,8 @@ __global__ void __launch_bounds__(256) emit_kernel(
 // by binary search over the rows' exclusive offsets).
 template <typename K>
 __global__ void __launch_bounds__(256) emit_large_kernel(
-    const int32_t* __restrict__ queue, const int32_t* __restrict__ queue_count,
-    const int32_t* __restrict__ order, const int32_t* __restrict__ counts,
-    const int64_t* __restrict__ ends, const float* __restrict__ mean,
+    const int32_t* __restrict__ queue_gid, const int32_t* __restrict__ queue_off,
+    const int32_t* __restrict__ queue_count, const float* __restrict__ mean,
     const float* __restrict__ conic, const float* __restrict__ alpha, gsb_bin_params p,
     int tiles_x, int tiles_y, K* __restrict__ keys, int32_t* __restrict__ values, int passes,
     int bits, uint32_t* __restrict__ key_hist)
@@ -792,9 +852,8 @@ __global__ void __launch_bounds__(256) emit_large_kernel(
     int warps = gridDim.x * (blockDim.x / 32);
     int total = *queue_count;
     for (int item = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5); item < total; item += warps) {
-        int64_t r = queue[item];
-        int32_t gid = order[r];
-        int64_t offset = ends[r] - counts[gid];
+        const int32_t gid = queue_gid[item];
+        int64_t offset = queue_off[item];
         Splat s = load_splat(mean, conic, alpha, gid);
         Ellipse e = ellipse_bounds(s.px, s.py, s.c00, s.c01, s.c11, s.alpha, p.tile_w, p.tile_h,
                                    tiles_x, tiles_y);
@@ -872,27 +931,30 @@ void digit_plan(int64_t num_tiles, int& passes, int& bits)
     bits = (b + passes - 1) / passes;
 }
 
+// Workspace of one gsb_bin call.
+//  head (zeroed by the call's first kernel): scalars[8] ([0] binned
+//    Gaussians, [1] large-emission queue length, [2] pairs kept, [3] sort
+//    time-out), the depth and tile sorts' digit totals [4][256] each and
+//    their partition counters [4] each.
+//  bulk (zeroed by count_kernel): the per-block pair sums of the emission,
+//    then the two sorts' look-back words.
 struct BinLayout {
     uint32_t *depth_keys, *keys_a, *keys_b;
-    int32_t *order_a, *order_b;
-    int64_t* ends;
-    int64_t* block_sums;
-    int32_t *queue, *scalars;  // [0] binned, [1] queue count, [2] clamped pairs, [3] sort error
+    int32_t *order_a, *order_b, *sorted_counts;
+    int32_t *queue_gid, *queue_off;
+    uint32_t* head;
+    int64_t head_words;
+    uint32_t* bulk;
+    int64_t bulk_words;
+    int32_t* scalars;
+    unsigned long long* block_sums;
     void *emit_keys, *pair_keys_a, *pair_keys_b;
     int32_t *emit_ids, *pair_ids_a, *pair_ids_b;
     SortScratch depth_sort, pair_sort;
+    int tile_passes, tile_bits;
 };
 
-SortScratch carve_sort(Carver& c, int64_t items)
-{
-    SortScratch w;
-    w.partitions = ceil_div(items > 0 ? items : 1, kSortTile);
-    uint32_t* base = c.take<uint32_t>(4 * kMaxRadix + 4 * (int64_t)w.partitions * kMaxRadix + 8);
-    w.hist = base;
-    w.status = base ? base + 4 * kMaxRadix : nullptr;
-    w.counters = base ? reinterpret_cast<int32_t*>(w.status + 4 * (int64_t)w.partitions * kMaxRadix) : nullptr;
-    return w;
-}
+constexpr int64_t kHeadWords = 8 + 2 * 4 * kMaxRadix + 2 * 4;
 
 BinLayout carve_bin(char* base, const gsb_bin_params& p, size_t& used)
 {
@@ -901,24 +963,44 @@ BinLayout carve_bin(char* base, const gsb_bin_params& p, size_t& used)
     int64_t C = p.capacity > 0 ? p.capacity : 1;
     int64_t P = p.max_pairs > 0 ? p.max_pairs : 1;
     int64_t tiles = (int64_t)ceil_div(p.width, p.tile_w) * ceil_div(p.height, p.tile_h);
+    digit_plan(tiles > 0 ? tiles : 1, L.tile_passes, L.tile_bits);
     size_t key_bytes = tiles <= 65535 ? 2 : 4;
     L.depth_keys = c.take<uint32_t>(C);
     L.keys_a = c.take<uint32_t>(C);
     L.keys_b = c.take<uint32_t>(C);
     L.order_a = c.take<int32_t>(C);
     L.order_b = c.take<int32_t>(C);
-    L.ends = c.take<int64_t>(C);
-    L.block_sums = c.take<int64_t>(ceil_div(C, kScanTile));
-    L.queue = c.take<int32_t>(C);
-    L.scalars = c.take<int32_t>(8);
+    L.sorted_counts = c.take<int32_t>(C);
+    L.queue_gid = c.take<int32_t>(C);
+    L.queue_off = c.take<int32_t>(C);
     L.emit_keys = c.take<char>(P * key_bytes);
     L.pair_keys_a = c.take<char>(P * key_bytes);
     L.pair_keys_b = c.take<char>(P * key_bytes);
     L.emit_ids = c.take<int32_t>(P);
     L.pair_ids_a = c.take<int32_t>(P);
     L.pair_ids_b = c.take<int32_t>(P);
-    L.depth_sort = carve_sort(c, C);
-    L.pair_sort = carve_sort(c, P);
+    L.head_words = kHeadWords;
+    L.head = c.take<uint32_t>(kHeadWords);
+    L.scalars = reinterpret_cast<int32_t*>(L.head);
+    L.depth_sort.partitions = ceil_div(C, kSortTile);
+    L.depth_sort.radix = 256;
+    L.pair_sort.partitions = ceil_div(P, kSortTile);
+    L.pair_sort.radix = 1 << L.tile_bits;
+    const int64_t blocks = ceil_div(C, kEmitThreads);
+    const int64_t depth_status = 4 * (int64_t)L.depth_sort.partitions * L.depth_sort.radix;
+    const int64_t pair_status =
+        (int64_t)L.tile_passes * L.pair_sort.partitions * L.pair_sort.radix;
+    L.bulk_words = ((2 * blocks + depth_status + pair_status) + 3) & ~int64_t(3);
+    L.bulk = c.take<uint32_t>(L.bulk_words);
+    if (base) {
+        L.depth_sort.hist = L.head + 8;
+        L.pair_sort.hist = L.head + 8 + 4 * kMaxRadix;
+        L.depth_sort.counters = reinterpret_cast<int32_t*>(L.head + 8 + 8 * kMaxRadix);
+        L.pair_sort.counters = L.depth_sort.counters + 4;
+        L.block_sums = reinterpret_cast<unsigned long long*>(L.bulk);
+        L.depth_sort.status = L.bulk + 2 * blocks;
+        L.pair_sort.status = L.depth_sort.status + depth_status;
+    }
     used = c.used;
     return L;
 }
@@ -926,24 +1008,22 @@ BinLayout carve_bin(char* base, const gsb_bin_params& p, size_t& used)
 template <typename K>
 int tile_stage(cudaStream_t s, const gsb_bin_params& p, const BinLayout& L, int tiles_x,
                int tiles_y, int64_t num_tiles, const float* mean, const float* conic,
-               const float* alpha, const int32_t* point_counts, const int32_t* order,
-               int32_t* gaussian_ids, int32_t* tile_offsets, int32_t* overflow)
+               const float* alpha, const int32_t* order, int32_t* gaussian_ids,
+               int32_t* tile_offsets, int32_t* pair_count, int32_t* overflow)
 {
     K* emit_keys = static_cast<K*>(L.emit_keys);
     const int32_t* n_binned = L.scalars + 0;
     int64_t C = p.capacity;
-    int passes, bits;
-    digit_plan(num_tiles, passes, bits);
-    // The emission kernels also accumulate the tile sort's digit histograms
-    // (its scratch was zeroed at the start of gsb_bin).
-    gsb::launch(emit_kernel<K>, ceil_div(C > 0 ? C : 1, 256), 256, 0, s, 
-        order, point_counts, L.ends, n_binned, C, mean, conic, alpha, p, tiles_x, tiles_y,
-        emit_keys, L.emit_ids, L.queue, L.scalars + 1, passes, bits, L.pair_sort.hist);
+    const int passes = L.tile_passes, bits = L.tile_bits;
+    // The emission kernels also accumulate the tile sort's digit histograms.
+    EmitScan scan{L.sorted_counts, L.block_sums, pair_count, overflow, L.scalars + 2};
+    gsb::launch(emit_kernel<K>, ceil_div(C > 0 ? C : 1, kEmitThreads), kEmitThreads, 0, s, order,
+                scan, n_binned, C, mean, conic, alpha, p, tiles_x, tiles_y, emit_keys, L.emit_ids,
+                L.queue_gid, L.queue_off, L.scalars + 1, passes, bits, L.pair_sort.hist);
     if (int e = check_launch()) return e;
-    gsb::launch(emit_large_kernel<K>, 148 * 8, 256, 0, s, L.queue, L.scalars + 1, order, point_counts,
-                                                 L.ends, mean, conic, alpha, p, tiles_x, tiles_y,
-                                                 emit_keys, L.emit_ids, passes, bits,
-                                                 L.pair_sort.hist);
+    gsb::launch(emit_large_kernel<K>, 148 * 8, 256, 0, s, L.queue_gid, L.queue_off, L.scalars + 1,
+                mean, conic, alpha, p, tiles_x, tiles_y, emit_keys, L.emit_ids, passes, bits,
+                L.pair_sort.hist);
     if (int e = check_launch()) return e;
     const K* sorted_keys = nullptr;
     const int32_t* sorted_ids = nullptr;
@@ -951,10 +1031,10 @@ int tile_stage(cudaStream_t s, const gsb_bin_params& p, const BinLayout& L, int 
                                  static_cast<K*>(L.pair_keys_b), L.pair_ids_a, L.pair_ids_b,
                                  gaussian_ids, &sorted_keys, &sorted_ids, L.scalars + 2,
                                  p.max_pairs, passes, bits, false, L.pair_sort, nullptr,
-                                 L.scalars + 3, true))
+                                 L.scalars + 3, nullptr))
         return e;
-    gsb::launch(ranges_kernel<K>, 1024, 256, 0, s, sorted_keys, L.scalars + 2, p.max_pairs, (int)num_tiles,
-                                          tile_offsets, L.scalars + 3, overflow);
+    gsb::launch(ranges_kernel<K>, 1024, 256, 0, s, sorted_keys, L.scalars + 2, p.max_pairs,
+                (int)num_tiles, tile_offsets, L.scalars + 3, overflow);
     return check_launch();
 }
 
@@ -1000,39 +1080,35 @@ extern "C" int gsb_bin(gsb_stream_t stream, const gsb_bin_params* p, void* works
         return GSB_ERR_NULL;
     if ((reinterpret_cast<uintptr_t>(conic) & 15) || (reinterpret_cast<uintptr_t>(mean) & 7))
         return GSB_ERR_INVALID;
+    if (int e = configure_sort_kernels()) return e;
     cudaStream_t s = as_stream(stream);
     size_t used = 0;
     BinLayout L = carve_bin(static_cast<char*>(workspace), *p, used);
-    // Scalars, the depth sort's and the tile sort's scratch: one launch.
-    gsb::launch(zero_ranges_kernel, 296, 256, 0, s, reinterpret_cast<uint32_t*>(L.scalars), 8,
-                                           L.depth_sort.hist, sort_scratch_words(L.depth_sort),
-                                           L.pair_sort.hist, sort_scratch_words(L.pair_sort));
+    gsb::launch(zero_u32_kernel, 8, 256, 0, s, L.head, L.head_words);
     if (int e = check_launch()) return e;
     int64_t C = p->capacity;
     const uint32_t* sorted_depth_keys = nullptr;
     const int32_t* depth_order = L.order_a;
+    // count_kernel always runs: it also zeroes the bulk region.
+    const int count_blocks =
+        ceil_div(C > 0 ? C : 1, kCountSlots) > 296 ? ceil_div(C, kCountSlots) : 296;
+    gsb::launch(count_kernel, count_blocks, kCountThreads, 0, s, (int)C, mean, conic, alpha, depth,
+                visible, *p, tiles_x, tiles_y, point_counts, L.depth_keys, L.depth_sort.hist,
+                reinterpret_cast<uint4*>(L.bulk), L.bulk_words / 4);
+    if (int e = check_launch()) return e;
     if (C > 0) {
-        gsb::launch(count_kernel, ceil_div(C, 256), 256, 0, s, (int)C, mean, conic, alpha, depth, visible,
-                                                      *p, tiles_x, tiles_y, point_counts,
-                                                      L.depth_keys, L.depth_sort.hist);
-        if (int e = check_launch()) return e;
-        // Depth sort: pass 0 drops the Gaussians without pairs.
-        if (int e = onesweep_sort<uint32_t>(s, L.depth_keys, nullptr, L.keys_a, L.keys_b, L.order_a,
-                                            L.order_b, nullptr, &sorted_depth_keys, &depth_order,
-                                            nullptr, C, 4, 8, true, L.depth_sort, L.scalars + 0,
-                                            L.scalars + 3, true))
+        // Depth sort: pass 0 drops the Gaussians without pairs; the last pass
+        // writes the counts in depth order and their per-block sums.
+        const DepthTail tail{point_counts, L.sorted_counts, L.block_sums};
+        if (int e = onesweep_sort<uint32_t>(s, L.depth_keys, nullptr, L.keys_a, L.keys_b,
+                                            L.order_a, L.order_b, nullptr, &sorted_depth_keys,
+                                            &depth_order, nullptr, C, 4, 8, true, L.depth_sort,
+                                            L.scalars + 0, L.scalars + 3, &tail))
             return e;
     }
-    gsb::launch(scan_reduce_kernel, ceil_div(C > 0 ? C : 1, kScanTile), kScanThreads, 0, s, 
-        depth_order, point_counts, L.scalars + 0, C, L.block_sums);
-    if (int e = check_launch()) return e;
-    gsb::launch(scan_kernel, ceil_div(C > 0 ? C : 1, kScanTile), kScanThreads, 0, s, 
-        depth_order, point_counts, L.scalars + 0, C, L.block_sums, L.ends, p->max_pairs, pair_count,
-        overflow, L.scalars + 2);
-    if (int e = check_launch()) return e;
     if (num_tiles <= 65535)
         return tile_stage<uint16_t>(s, *p, L, tiles_x, tiles_y, num_tiles, mean, conic, alpha,
-                                    point_counts, depth_order, gaussian_ids, tile_offsets, overflow);
+                                    depth_order, gaussian_ids, tile_offsets, pair_count, overflow);
     return tile_stage<uint32_t>(s, *p, L, tiles_x, tiles_y, num_tiles, mean, conic, alpha,
-                                point_counts, depth_order, gaussian_ids, tile_offsets, overflow);
+                                depth_order, gaussian_ids, tile_offsets, pair_count, overflow);
 }
