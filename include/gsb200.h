@@ -47,7 +47,7 @@ enum {
     GSB_ERR_NULL = 4        /* required pointer is NULL */
 };
 
-#define GSB_ABI_VERSION 6
+#define GSB_ABI_VERSION 7
 
 /* Library utilities.  No counterpart in the reference, whose boundary
  * (cutlass.jax.cutlass_call) reports errors by raising in Python before
@@ -262,7 +262,11 @@ GSB_API int gsb_bin(gsb_stream_t stream, const gsb_bin_params* p, void* workspac
  * splats[C*12] (48-byte staged records), contribution_bits
  * [gsb_raster_bit_words()] (per 32-pair batch and pixel block, which pairs
  * gave at least one pixel of the block a composited fragment; only words of
- * batches the forward reached are written).
+ * batches the forward reached are written), fragment_stats[C*2] (may be
+ * NULL = not collected; not with GSB_RASTER_RGB_ONLY): per Gaussian the
+ * number of composited fragments and the sum of their compositing weights
+ * T*alpha, interleaved, zeroed then accumulated by the call -- the forward
+ * statistics of kernels/packed_rasterize.py:363-377.
  * ------------------------------------------------------------------------ */
 typedef struct {
     int capacity;
@@ -274,11 +278,15 @@ typedef struct {
                               writes no final_t / last / backward_work /
                               contribution_bits (they may be NULL); the
                               reference's record_contributions = False,
-                              kernels/packed_rasterizer.py:219-232 */
+                              kernels/packed_rasterizer.py:219-232;
+                              GSB_RASTER_CLAMP_RGB: write min(rgb, 1), the
+                              packed rasterizer's output
+                              (kernels/packed_rasterize.py:396) */
 } gsb_raster_params;
 
 #define GSB_RASTER_SPLATS_READY 1
 #define GSB_RASTER_RGB_ONLY 2
+#define GSB_RASTER_CLAMP_RGB 4
 
 GSB_API size_t gsb_raster_workspace_size(const gsb_raster_params* p);
 GSB_API size_t gsb_raster_bit_words(const gsb_raster_params* p);
@@ -288,7 +296,8 @@ GSB_API int gsb_raster_fwd(gsb_stream_t stream, const gsb_raster_params* p, void
                    const int8_t* visible, const int32_t* gaussian_ids,
                    const int32_t* tile_offsets, const float* background, float* rgb,
                    float* out_depth, float* out_alpha, float* final_t, int32_t* last,
-                   int32_t* backward_work, float* splats, uint32_t* contribution_bits);
+                   int32_t* backward_work, float* splats, uint32_t* contribution_bits,
+                   float* fragment_stats);
 
 /* The first stage of gsb_raster_fwd on its own: write the splat records of
  * every visible Gaussian.  It depends on the projection only, so a caller
@@ -328,10 +337,16 @@ typedef struct {
     int tile_w, tile_h;
     int cluster_size;
     int64_t max_pairs;
-    int flags;             /* GSB_RASTER_BWD_PREPARED: gsb_raster_bwd_prepare already ran */
+    int flags;             /* GSB_RASTER_BWD_PREPARED: gsb_raster_bwd_prepare already ran;
+                              GSB_RASTER_BWD_SYMMETRIC_CONIC: the packed
+                              backward's symmetric_conic convention
+                              (kernels/packed_rasterizer.py:98-177): gconic[1]
+                              takes both off-diagonal contributions and
+                              gconic[2] is left as zeroed */
 } gsb_raster_bwd_params;
 
 #define GSB_RASTER_BWD_PREPARED 1
+#define GSB_RASTER_BWD_SYMMETRIC_CONIC 2
 
 GSB_API int gsb_raster_bwd(gsb_stream_t stream, const gsb_raster_bwd_params* p, void* workspace,
                    size_t workspace_bytes, const float* splats, const float* depth,

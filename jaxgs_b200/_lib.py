@@ -61,7 +61,9 @@ class RasterParams(ctypes.Structure):
 
 RASTER_SPLATS_READY = 1
 RASTER_RGB_ONLY = 2
+RASTER_CLAMP_RGB = 4
 RASTER_BWD_PREPARED = 1
+RASTER_BWD_SYMMETRIC_CONIC = 2
 
 
 class RasterBwdParams(ctypes.Structure):
@@ -125,7 +127,7 @@ def _load():
     lib.gsb_bin.restype = ctypes.c_int
     lib.gsb_bin.argtypes = [vp, vp, vp, sz] + [vp] * 10
     lib.gsb_raster_fwd.restype = ctypes.c_int
-    lib.gsb_raster_fwd.argtypes = [vp, vp, vp, sz] + [vp] * 17
+    lib.gsb_raster_fwd.argtypes = [vp, vp, vp, sz] + [vp] * 18
     lib.gsb_raster_bwd.restype = ctypes.c_int
     lib.gsb_raster_bwd.argtypes = [vp, vp, vp, sz] + [vp] * 20
     lib.gsb_raster_pack.restype = ctypes.c_int
@@ -155,7 +157,7 @@ def _load():
 
 
 lib = _load()
-if lib.gsb_abi_version() != 6:
+if lib.gsb_abi_version() != 7:
     raise RuntimeError("libgsb200.so ABI version mismatch; rebuild with `python -m jaxgs_b200.build`")
 
 

@@ -91,5 +91,6 @@ def fused_loss(image: torch.Tensor, target: torch.Tensor, clip_input: bool = Fal
     """Mean 0.8 L1 + 0.2 (1 - SSIM) of an [H, W, 3] float32 image against a
     uint8 or float target (kernels/fused_loss.py:333-352), differentiable in
     the image.  clip_input: the loss of clip(image, 0, 1), its gradient
-    through the clip (1/2 at a bound), as the training step takes it."""
+    through the clip (1/2 at a bound), as rasterize_loss_and_grad (the
+    fp32 step path) takes it."""
     return _FusedLoss.apply(image, target, bool(clip_input))

@@ -219,6 +219,15 @@ struct Vec<1> {
     static __device__ __forceinline__ void set(T& v, int, float x) { v = x; }
 };
 
+template <int ROWS>
+__device__ __forceinline__ float row_sum(typename Vec<ROWS>::T v)
+{
+    float s = Vec<ROWS>::get(v, 0);
+#pragma unroll
+    for (int r = 1; r < ROWS; r++) s += Vec<ROWS>::get(v, r);
+    return s;
+}
+
 // Per-warp stash of up to 32 staged splats, every scalar duplicated so that
 // one broadcast shared load yields the (value, value) operand of a packed
 // instruction.
@@ -267,15 +276,18 @@ __device__ __forceinline__ Fragment<ROWS> fragment(const Stash& st, int k,
 // RECORD = false is the RGB-only forward of inference (the reference's
 // record_contributions = False, packed_rasterizer.py:219-232): the same
 // compositing, without final T, last index, backward work or contribution
-// bits.
-template <int ROWS, bool WANT_DEPTH, bool RECORD>
+// bits.  STATS also gathers the forward's fragment statistics per Gaussian
+// (packed_rasterize.py:363-377): the number of composited fragments and the
+// sum of their compositing weights T * alpha, as interleaved pairs.
+template <int ROWS, bool WANT_DEPTH, bool RECORD, bool STATS>
 __global__ void __launch_bounds__(256) raster_fwd_kernel(
     gsb_raster_params p, const float4* __restrict__ splats, const float* __restrict__ depth,
     const int32_t* __restrict__ ids, const int32_t* __restrict__ offsets,
     const int32_t* __restrict__ order, const float* __restrict__ background,
     float* __restrict__ rgb, float* __restrict__ out_depth, float* __restrict__ out_alpha,
     float* __restrict__ final_t, int32_t* __restrict__ last_out,
-    int32_t* __restrict__ backward_work, uint32_t* __restrict__ bits)
+    int32_t* __restrict__ backward_work, uint32_t* __restrict__ bits,
+    float* __restrict__ stats)
 {
     pdl_begin();
     using V = Vec<ROWS>;
@@ -313,6 +325,7 @@ __global__ void __launch_bounds__(256) raster_fwd_kernel(
             hit = block_hit<ROWS>(r0, bx0, by0);
             if (hit) {
                 stash_splat(st, lane, r0, __ldg(rec + 1), __ldg(rec + 2));
+                if (STATS) st.id[lane] = g;
                 if (WANT_DEPTH) {
                     const float d = __ldg(depth + g);
                     st.depth[lane] = make_float2(d, d);
@@ -362,6 +375,19 @@ __global__ void __launch_bounds__(256) raster_fwd_kernel(
                 active[r] = active[r] && !stop;
             }
             if (RECORD && valid_any) mine |= 1u << k;
+            if (STATS) {
+                // w is exactly zero where the fragment is not composited.
+                float count = 0.0f;
+#pragma unroll
+                for (int r = 0; r < ROWS; r++) count += valid[r] ? 1.0f : 0.0f;
+                count = warp_sum(count);
+                const float weight = warp_sum(row_sum<ROWS>(w));
+                if (lane == 0 && count != 0.0f) {
+                    float* sg = stats + (int64_t)st.id[k] * 2;
+                    atomicAdd(sg, count);
+                    atomicAdd(sg + 1, weight);
+                }
+            }
         }
         // Saturated lanes composite nothing more, so the warp's exit is
         // tested once per batch.
@@ -381,9 +407,19 @@ __global__ void __launch_bounds__(256) raster_fwd_kernel(
         if (tg.px < p.width && y < p.height) {
             const int64_t pix = (int64_t)y * p.width + tg.px;
             const float t = V::get(trans, r);
-            rgb[pix * 3] = V::get(cr, r) + t * __ldg(background);
-            rgb[pix * 3 + 1] = V::get(cg, r) + t * __ldg(background + 1);
-            rgb[pix * 3 + 2] = V::get(cb, r) + t * __ldg(background + 2);
+            float out_r = V::get(cr, r) + t * __ldg(background);
+            float out_g = V::get(cg, r) + t * __ldg(background + 1);
+            float out_b = V::get(cb, r) + t * __ldg(background + 2);
+            if (p.flags & GSB_RASTER_CLAMP_RGB) {
+                // The packed rasterizer's output, min(colour, 1)
+                // (packed_rasterize.py:396).
+                out_r = fminf(out_r, 1.0f);
+                out_g = fminf(out_g, 1.0f);
+                out_b = fminf(out_b, 1.0f);
+            }
+            rgb[pix * 3] = out_r;
+            rgb[pix * 3 + 1] = out_g;
+            rgb[pix * 3 + 2] = out_b;
             if (out_depth) out_depth[pix] = V::get(cd, r);
             if (out_alpha) out_alpha[pix] = 1.0f - t;
             if (RECORD) {
@@ -429,15 +465,6 @@ __device__ __forceinline__ float warp_sum8(float v[8], int lane)
     float s = v[0];
     s += __shfl_xor_sync(GSB_FULL_MASK, s, 2);
     s += __shfl_xor_sync(GSB_FULL_MASK, s, 1);
-    return s;
-}
-
-template <int ROWS>
-__device__ __forceinline__ float row_sum(typename Vec<ROWS>::T v)
-{
-    float s = Vec<ROWS>::get(v, 0);
-#pragma unroll
-    for (int r = 1; r < ROWS; r++) s += Vec<ROWS>::get(v, r);
     return s;
 }
 
@@ -487,7 +514,8 @@ __global__ void __launch_bounds__(256) raster_bwd_kernel(
 #pragma unroll
     for (int d = 16; d > 0; d >>= 1) top = max(top, __shfl_xor_sync(GSB_FULL_MASK, top, d));
     // Per-lane RED target after the reduction: lane 4j holds moment j
-    // (Sx, Sy, Sxx, Sxy, Syy, R, G, B), lane 13 repeats Sxy for conic[2],
+    // (Sx, Sy, Sxx, Sxy, Syy, R, G, B), lane 13 repeats Sxy for conic[2]
+    // (unless the symmetric convention folds it into conic[1]),
     // lane 1 adds the opacity gradient sum(ge) / o, lane 2 the depth one.
     const int group = lane >> 2, role = lane & 3;
     float* target = nullptr;
@@ -496,7 +524,7 @@ __global__ void __launch_bounds__(256) raster_bwd_kernel(
         if (group < 2) { target = gmean + group; stride = 2; }
         else if (group < 5) { target = gconic + (group == 2 ? 0 : group == 3 ? 1 : 3); stride = 4; }
         else { target = gcolor + (group - 5); stride = 3; }
-    } else if (lane == 13) {
+    } else if (lane == 13 && !(p.flags & GSB_RASTER_BWD_SYMMETRIC_CONIC)) {
         target = gconic + 2; stride = 4;
     } else if (lane == 1) {
         target = galpha; stride = 1;
@@ -504,7 +532,11 @@ __global__ void __launch_bounds__(256) raster_bwd_kernel(
         target = gdepth; stride = 1;
     }
     // Constant coefficient of the lane's moment (groups 2-4: -1/2, 5-7: 1).
-    const float kA = group < 5 ? -0.5f : 1.0f;
+    // Symmetric convention (packed_rasterize.py:130-175): conic[0][1] takes
+    // both off-diagonal contributions and conic[1][0] stays zero.
+    const float kA = group < 5 ? ((group == 3 && (p.flags & GSB_RASTER_BWD_SYMMETRIC_CONIC))
+                                      ? -1.0f : -0.5f)
+                               : 1.0f;
     if (top <= start) return;
     const int32_t top_batch = (top - 1 - start) >> 5;
     for (int32_t batch = top_batch; batch >= 0; batch--) {
@@ -694,20 +726,31 @@ void launch_fwd(cudaStream_t s, int tiles, int warps, bool want_depth, bool reco
                 const gsb_raster_params& p, const float4* sp, const float* depth,
                 const int32_t* ids, const int32_t* offsets, const int32_t* order, const float* bg,
                 float* rgb, float* od, float* oa, float* final_t, int32_t* last, int32_t* work,
-                uint32_t* bits)
+                uint32_t* bits, float* stats)
 {
     size_t smem = (size_t)warps * sizeof(Stash);
     auto go = [&](auto kernel) {
         gsb::launch(kernel, tiles, warps * 32, smem, s, p, sp, depth, ids, offsets, order, bg, rgb,
-                    od, oa, final_t, last, work, bits);
+                    od, oa, final_t, last, work, bits, stats);
     };
-    if (record) {
-        if (want_depth) go(raster_fwd_kernel<ROWS, true, true>);
-        else go(raster_fwd_kernel<ROWS, false, true>);
+    if (stats) {
+        if (want_depth) go(raster_fwd_kernel<ROWS, true, true, true>);
+        else go(raster_fwd_kernel<ROWS, false, true, true>);
+    } else if (record) {
+        if (want_depth) go(raster_fwd_kernel<ROWS, true, true, false>);
+        else go(raster_fwd_kernel<ROWS, false, true, false>);
     } else {
-        if (want_depth) go(raster_fwd_kernel<ROWS, true, false>);
-        else go(raster_fwd_kernel<ROWS, false, false>);
+        if (want_depth) go(raster_fwd_kernel<ROWS, true, false, false>);
+        else go(raster_fwd_kernel<ROWS, false, false, false>);
     }
+}
+
+__global__ void zero_f32_kernel(float* p, int64_t n)
+{
+    pdl_begin();
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+         i += (int64_t)gridDim.x * blockDim.x)
+        p[i] = 0.0f;
 }
 
 template <int ROWS>
@@ -792,13 +835,13 @@ bool raster_shape_ok(const gsb_raster_params& p)
 {
     return p.capacity >= 0 && p.width > 0 && p.height > 0 && tiles_ok(p.tile_w, p.tile_h) &&
            p.max_pairs >= 0 && p.max_pairs < (int64_t(1) << 31) &&
-           (p.flags & ~(GSB_RASTER_SPLATS_READY | GSB_RASTER_RGB_ONLY)) == 0;
+           (p.flags & ~(GSB_RASTER_SPLATS_READY | GSB_RASTER_RGB_ONLY | GSB_RASTER_CLAMP_RGB)) == 0;
 }
 
 bool raster_bwd_shape_ok(const gsb_raster_bwd_params& p)
 {
     return p.capacity >= 0 && p.width > 0 && p.height > 0 && tiles_ok(p.tile_w, p.tile_h) &&
-           (p.flags & ~GSB_RASTER_BWD_PREPARED) == 0;
+           (p.flags & ~(GSB_RASTER_BWD_PREPARED | GSB_RASTER_BWD_SYMMETRIC_CONIC)) == 0;
 }
 
 bool misaligned16(const void* a, const void* b)
@@ -827,10 +870,12 @@ extern "C" int gsb_raster_fwd(gsb_stream_t stream, const gsb_raster_params* p, v
                               const int8_t* visible, const int32_t* gaussian_ids,
                               const int32_t* tile_offsets, const float* background, float* rgb,
                               float* out_depth, float* out_alpha, float* final_t, int32_t* last,
-                              int32_t* backward_work, float* splats, uint32_t* contribution_bits)
+                              int32_t* backward_work, float* splats, uint32_t* contribution_bits,
+                              float* fragment_stats)
 {
     if (!p) return GSB_ERR_NULL;
     if (!raster_shape_ok(*p)) return GSB_ERR_INVALID;
+    if (fragment_stats && (p->flags & GSB_RASTER_RGB_ONLY)) return GSB_ERR_INVALID;
     if (!workspace || workspace_bytes < raster_ws(*p)) return GSB_ERR_WORKSPACE;
     const bool packed = (p->flags & GSB_RASTER_SPLATS_READY) != 0;
     const bool record = (p->flags & GSB_RASTER_RGB_ONLY) == 0;
@@ -846,6 +891,10 @@ extern "C" int gsb_raster_fwd(gsb_stream_t stream, const gsb_raster_params* p, v
     if (!packed) {
         if (int e = launch_pack(s, *p, mean, conic, color, alpha, visible, splats)) return e;
     }
+    if (fragment_stats && p->capacity > 0) {
+        gsb::launch(zero_f32_kernel, 296, 256, 0, s, fragment_stats, (int64_t)p->capacity * 2);
+        if (int e = check_launch()) return e;
+    }
     gsb::launch(order_tiles_kernel, 1, kOrderThreads, 0, s, tile_offsets, tiles, 1, order);
     if (int e = check_launch()) return e;
     int warps = warps_per_tile(p->tile_w, p->tile_h);
@@ -853,11 +902,11 @@ extern "C" int gsb_raster_fwd(gsb_stream_t stream, const gsb_raster_params* p, v
     if (rows_per_lane(p->tile_h) == 2)
         launch_fwd<2>(s, tiles, warps, out_depth != nullptr, record, *p, sp, depth, gaussian_ids,
                       tile_offsets, order, background, rgb, out_depth, out_alpha, final_t, last,
-                      backward_work, contribution_bits);
+                      backward_work, contribution_bits, fragment_stats);
     else
         launch_fwd<1>(s, tiles, warps, out_depth != nullptr, record, *p, sp, depth, gaussian_ids,
                       tile_offsets, order, background, rgb, out_depth, out_alpha, final_t, last,
-                      backward_work, contribution_bits);
+                      backward_work, contribution_bits, fragment_stats);
     return check_launch();
 }
 

@@ -308,14 +308,19 @@ def pack_splats(projected: ProjectedGaussians, camera: DeviceCamera, config: Cap
 def rasterize_forward(projected: ProjectedGaussians, table: SortedVisibilityTable,
                       camera: DeviceCamera, config: CapacityConfig, background=None,
                       want_depth: bool = True, want_alpha: bool = True,
-                      splats: torch.Tensor | None = None, record: bool = True):
+                      splats: torch.Tensor | None = None, record: bool = True,
+                      clamp_rgb: bool = False, fragment_stats: torch.Tensor | None = None):
     """sorted_rasterizer.py:15-70: returns (RenderResult, RasterCache).
 
     The table may reference only visible Gaussians (others are not staged).
     splats: records already written by pack_splats (the packing stage is
     then skipped).  record=False is the inference forward
     (packed_rasterizer.py:219-232, record_contributions=False): the same
-    image with no backward state, and the cache is None.
+    image with no backward state, and the cache is None.  clamp_rgb writes
+    min(rgb, 1), the packed rasterizer's output (packed_rasterize.py:396).
+    fragment_stats: a [C * 2] float32 tensor that receives the forward's
+    fragment statistics (count, weight per Gaussian, interleaved;
+    packed_rasterize.py:363-377); recording forward only.
     """
     _require_cuda(projected.mean, "rasterization")
     C = config.max_gaussians
@@ -332,8 +337,11 @@ def rasterize_forward(projected: ProjectedGaussians, table: SortedVisibilityTabl
     packed = splats is not None
     if not packed:
         splats = torch.empty(C, 12, dtype=_f32, device=dev)
+    if fragment_stats is not None and (not record or fragment_stats.numel() != 2 * C):
+        raise ValueError("fragment_stats needs the recording forward and C * 2 floats")
     p = _raster_params(camera, config, table.gaussian_ids.shape[0],
-                       (L.RASTER_SPLATS_READY if packed else 0) | (0 if record else L.RASTER_RGB_ONLY))
+                       (L.RASTER_SPLATS_READY if packed else 0) | (0 if record else L.RASTER_RGB_ONLY)
+                       | (L.RASTER_CLAMP_RGB if clamp_rgb else 0))
     bits = (torch.empty(max(int(L.lib.gsb_raster_bit_words(L.ref(p))), 1), dtype=_i32, device=dev)
             if record else None)
     ws = _workspace(L.lib.gsb_raster_workspace_size(L.ref(p)), dev)
@@ -343,7 +351,8 @@ def rasterize_forward(projected: ProjectedGaussians, table: SortedVisibilityTabl
         _ptr(_c(projected.color, _f32)), _ptr(_c(projected.alpha, _f32)),
         _ptr(_c(projected.visible, torch.int8)), _ptr(table.gaussian_ids),
         _ptr(table.tile_offsets), _ptr(_c(background, _f32)), _ptr(rgb), _ptr(out_depth),
-        _ptr(out_alpha), _ptr(final_t), _ptr(last), _ptr(work), _ptr(splats), _ptr(bits)),
+        _ptr(out_alpha), _ptr(final_t), _ptr(last), _ptr(work), _ptr(splats), _ptr(bits),
+        _ptr(None if fragment_stats is None else _c(fragment_stats, _f32))),
         "rasterization forward")
     cache = RasterCache(splats, final_t, last, work, bits) if record else None
     return RenderResult(rgb, out_depth, out_alpha), cache
@@ -355,7 +364,8 @@ class BackwardBuffers:
     collect_stats: also gather the fragment statistics (statistics())."""
 
     def __init__(self, table: SortedVisibilityTable, camera: DeviceCamera, config: CapacityConfig,
-                 visible_clusters=None, collect_stats: bool = False):
+                 visible_clusters=None, collect_stats: bool = False,
+                 symmetric_conic: bool = False):
         C = config.max_gaussians
         dev = table.gaussian_ids.device
         self.gmean = torch.empty(C, 2, dtype=_f32, device=dev)
@@ -365,12 +375,15 @@ class BackwardBuffers:
         self.galpha = torch.empty(C, dtype=_f32, device=dev)
         self.fragments = torch.empty(C * 3, dtype=_f32, device=dev) if collect_stats else None
         self.visible_clusters = visible_clusters
+        self.symmetric_conic = symmetric_conic
         self.max_pairs = int(table.gaussian_ids.shape[0])
         rp = _raster_params(camera, config, self.max_pairs)
         self.workspace = _workspace(L.lib.gsb_raster_workspace_size(L.ref(rp)), dev)
         self.prepared = False
 
     def params(self, camera: DeviceCamera, config: CapacityConfig, flags: int = 0):
+        if self.symmetric_conic:
+            flags |= L.RASTER_BWD_SYMMETRIC_CONIC
         return L.RasterBwdParams(config.max_gaussians, camera.width, camera.height,
                                  config.tile_size, config.raster_tile_height, config.cluster_size,
                                  self.max_pairs, flags)
@@ -502,3 +515,103 @@ def rasterize_loss_and_grad(projected: ProjectedGaussians, table: SortedVisibili
     if collect_stats:
         return loss, cot[0], cot[1]
     return loss, cot, torch.zeros(config.max_gaussians, 4, dtype=_f32, device=drgb.device)
+
+
+# ---------------------------------------------------------------------------
+# The packed rasterizer's entry points (kernels/packed_rasterizer.py:23-216),
+# the ones the reference's training step calls for 8- and 16-pixel-wide
+# tiles (training/step.py:74-80).
+# ---------------------------------------------------------------------------
+PACKED_TILES = ((8, 8), (8, 16), (12, 16), (16, 16))  # (tile_height, tile_size)
+
+
+def _check_packed_tiles(config: CapacityConfig) -> None:
+    if (config.raster_tile_height, config.tile_size) not in PACKED_TILES:
+        raise ValueError("Packed rasterizer supports tiles 8x8, 8x16, 12x16 and 16x16")
+
+
+def packed_forward(projected: ProjectedGaussians, table: SortedVisibilityTable,
+                   camera: DeviceCamera, config: CapacityConfig, collect_stats: bool = False):
+    """kernels/packed_rasterizer.py:23-95: (rgb [H, W, 3], cache, stats).
+
+    The same interface and output convention as the reference: rgb =
+    min(colour, 1) over no background; cache holds what packed_backward
+    needs (this backend's RasterCache: 48-byte splat records, final
+    transmittance, last index, backward work, contribution words, in place
+    of the reference's 32-byte half2 records); stats is the [C * 2]
+    (fragment count, compositing weight) pairs with collect_stats, else a
+    one-element placeholder, as the reference's output shapes are.  The
+    compositing is float32 (fp32 fragments and transmittance; the reference
+    packs them as half2), so images meet the 1e-4 fp32 bar.  The table may
+    reference only visible Gaussians."""
+    _check_packed_tiles(config)
+    _require_cuda(projected.mean, "packed rasterization")
+    C = config.max_gaussians
+    dev = projected.mean.device
+    stats = torch.empty(C * 2 if collect_stats else 1, dtype=_f32, device=dev)
+    result, cache = rasterize_forward(projected, table, camera, config, want_depth=False,
+                                      want_alpha=False, clamp_rgb=True,
+                                      fragment_stats=stats if collect_stats else None)
+    if not collect_stats:
+        stats.zero_()
+    return result.rgb, cache, stats
+
+
+def packed_backward(projected: ProjectedGaussians, table: SortedVisibilityTable,
+                    cache: RasterCache, image_grad: torch.Tensor, camera: DeviceCamera,
+                    config: CapacityConfig, collect_stats: bool = False, *,
+                    symmetric_conic: bool = False, visible_clusters=None,
+                    image_grad_scale: torch.Tensor | None = None,
+                    buffers: BackwardBuffers | None = None):
+    """kernels/packed_rasterizer.py:98-177: (cotangents, alpha_grad_sq_sum).
+
+    Field cotangents of the packed forward, with the reference's
+    conventions: the image gradient is taken as given (the forward's clamp
+    at 1 is not differentiated); symmetric_conic puts both off-diagonal
+    contributions into conic[0, 1] and leaves conic[1, 0] zero (the
+    analytic pullback reads their sum); with visible_clusters (which must
+    hold every Gaussian of the table) mean, conic and colour cotangents are
+    defined only in those clusters and depth cotangents nowhere, alpha
+    cotangents everywhere when collecting statistics; the radius cotangent
+    is zero.  alpha_grad_sq_sum is the per-Gaussian sum of squared opacity
+    cotangents ([C]) with collect_stats, else a one-element zero.
+    image_grad_scale is accepted for the reference's signature and not
+    needed: the float32 backward does no range scaling.  buffers: from
+    BackwardBuffers(..., symmetric_conic=...), optionally prepared on a
+    second stream."""
+    _check_packed_tiles(config)
+    del image_grad_scale
+    if buffers is None:
+        buffers = BackwardBuffers(table, camera, config, visible_clusters, collect_stats,
+                                  symmetric_conic=symmetric_conic)
+    elif buffers.symmetric_conic != symmetric_conic:
+        raise ValueError("buffers were made for the other conic convention")
+    out = rasterize_backward(projected, table, cache, image_grad.reshape(camera.height,
+                                                                         camera.width, 3),
+                             camera, config, buffers=buffers, collect_stats=collect_stats)
+    if collect_stats:
+        cot, stats = out
+        return cot, stats[:, 3].contiguous()
+    return out, _zeros(1, image_grad.device)
+
+
+def packed_loss_and_grad(projected: ProjectedGaussians, table: SortedVisibilityTable,
+                         camera: DeviceCamera, config: CapacityConfig, target: torch.Tensor,
+                         collect_stats: bool, *, symmetric_conic: bool = False,
+                         visible_clusters=None):
+    """kernels/packed_rasterizer.py:180-216: (loss, cotangents, stats).
+
+    packed_forward -> fused L1+SSIM on its (clamped) image -> packed_backward;
+    stats is the detached [C, 4] (fragment count, compositing weight, alpha
+    cotangent, squared opacity cotangent) with collect_stats, else zeros.
+    visible_clusters limits the defined cotangents as in packed_backward."""
+    image, cache, fragments = packed_forward(projected, table, camera, config, collect_stats)
+    loss, image_grad, scale = fused_loss_and_grad_with_scale(image, target)
+    gradients, square = packed_backward(projected, table, cache, image_grad, camera, config,
+                                        collect_stats, symmetric_conic=symmetric_conic,
+                                        visible_clusters=visible_clusters, image_grad_scale=scale)
+    if collect_stats:
+        stats = torch.stack((fragments[0::2], fragments[1::2], gradients.alpha, square), dim=1)
+    else:
+        stats = torch.zeros(config.max_gaussians, 4, dtype=_f32, device=image.device)
+    return loss, gradients, stats

@@ -1,23 +1,26 @@
 """The north-star training step: cluster cull -> compact projection -> binning
--> fp32 raster forward -> fused L1+SSIM (on clip(rgb,0,1)) -> raster backward
--> projection pullback, with no host synchronisation (one stream, plus a
-second one for the stages that can overlap).
+-> raster forward -> fused L1+SSIM -> raster backward -> projection pullback,
+with no host synchronisation (one stream, plus a second one for the stages
+that can overlap).
 
 Mirrors training/step.py:32-132 (compute_training_step) up to, not including,
 the optimizer: the result is the loss, the parameter gradients in compact
-visible-cluster order and the binning metrics.  The reference dispatches
-8x16 tiles to its half2 rasterizer (step.py:74-80); this backend uses the
-fp32 compositing of kernels/sorted_rasterizer.py:165-236 for every tile
-shape, which is the path whose images and gradients meet the 1e-4 / 1e-3
-parity bars.
+visible-cluster order and the binning metrics.  Like the reference
+(step.py:74-80), the packed tile shapes (kernels.PACKED_TILES: 8x8, 8x16,
+12x16, 16x16) take packed_loss_and_grad's conventions -- image min(rgb, 1),
+loss on it with the gradient taken as given, symmetric conic cotangents --
+and other shapes take rasterize_loss_and_grad's (loss on clip(rgb, 0, 1)
+with the clip's VJP); both run this backend's float32 compositing, which
+meets the 1e-4 / 1e-3 parity bars (the reference packs the former as half2).
 
 ``GraphedTrainingStep`` captures the whole step once as a CUDA graph and
 replays it: every size the kernels need is static (device-side counts bound
 the work), so a replay issues the ~40 launches without host involvement.
 
-Multi-GPU (view sharding): each rank renders its views, scatters the
-compact gradients into pool order (``scatter_compact``) and the ranks sum
-them with one NCCL all-reduce per step (torch.distributed).
+Multi-GPU (view sharding): each rank renders its views and writes its
+gradients in pool order; the ranks sum them with this library's own
+NVLink collectives (NvlsExchange, captured into the step's graph) or with
+NCCL (ViewShardedExchange).
 """
 
 from __future__ import annotations
@@ -59,7 +62,8 @@ def compute_training_step(pool: GaussianArrays, bounds, camera: DeviceCamera, ta
                           active_sh_only: bool = True, sh_color_only: bool = False,
                           keep_image: bool = False, stage_events: dict | None = None,
                           overlap: bool = True, pool_grads=None, collect_stats: bool = False,
-                          stats: torch.Tensor | None = None) -> StepOutput:
+                          stats: torch.Tensor | None = None,
+                          packed: bool | None = None) -> StepOutput:
     """training/step.py:32-89 without the optimizer update.
 
     bounds: world cluster bounds (center, extent, valid) on the device.
@@ -79,7 +83,12 @@ def compute_training_step(pool: GaussianArrays, bounds, camera: DeviceCamera, ta
     compositing weight, alpha cotangent, squared opacity cotangent); with
     stats given they are added into it in place (step.py:125-126,
     stats = stats + fragment_stats), and StepOutput.stats is that tensor.
+    packed: the packed_loss_and_grad conventions (see the module docstring);
+    None picks them for the packed tile shapes, as training/step.py:74-80
+    does (shapes it would reject take the fp32 conventions here).
     """
+    if packed is None:
+        packed = (config.raster_tile_height, config.tile_size) in K.PACKED_TILES
     stream = torch.cuda.current_stream()
 
     def mark(name):
@@ -120,16 +129,16 @@ def compute_training_step(pool: GaussianArrays, bounds, camera: DeviceCamera, ta
         stream.wait_stream(side)
     ev = mark("raster_fwd")
     result, cache = K.rasterize_forward(projected, table, camera, config, want_depth=False,
-                                        want_alpha=False, splats=splats)
+                                        want_alpha=False, splats=splats, clamp_rgb=packed)
     done(ev)
     buffers = K.BackwardBuffers(table, camera, config, visible_clusters=clusters,
-                                collect_stats=collect_stats)
+                                collect_stats=collect_stats, symmetric_conic=packed)
     if side is not None:
         side.wait_stream(stream)
         with torch.cuda.stream(side):
             K.prepare_rasterize_backward(cache, camera, config, buffers)
     ev = mark("loss")
-    loss, drgb, _ = K._fused_loss(result.rgb, target, False, clip_input=True)
+    loss, drgb, _ = K._fused_loss(result.rgb, target, False, clip_input=not packed)
     done(ev)
     if side is not None:
         stream.wait_stream(side)
@@ -488,13 +497,35 @@ class GraphedTrainingStep:
                 self.gradients = exchange.exchange(self.camera.center)
         self.launches_per_step = _lib.launch_count() - before
 
+    def _check_inputs(self, camera, target) -> None:
+        """The graph keeps the captured camera's image size and clip planes
+        and the target's shape; a camera or target that differs would be
+        replayed with the captured values, so it is refused."""
+        if isinstance(camera, DeviceCamera):
+            got = (camera.width, camera.height, float(camera.near), float(camera.far))
+            want = (self.camera.width, self.camera.height, float(self.camera.near),
+                    float(self.camera.far))
+            if got != want:
+                raise ValueError(f"camera (width, height, near, far) {got} differs from the "
+                                 f"captured {want}; capture another GraphedTrainingStep")
+        elif camera is not None and camera.numel() != self.camera_flat.numel():
+            raise ValueError(f"packed camera has {camera.numel()} values, expected "
+                             f"{self.camera_flat.numel()}")
+        if target is not None and (tuple(target.shape) != tuple(self.target.shape)
+                                   or target.dtype != self.target.dtype):
+            raise ValueError(f"target {tuple(target.shape)} {target.dtype} differs from the "
+                             f"captured {tuple(self.target.shape)} {self.target.dtype}")
+
     def upload(self, camera=None, target: torch.Tensor | None = None):
         """Stage the next step's inputs (pinned host tensors, not modified
         until that step has run) on a copy stream, so that their transfer
         overlaps the step in flight; the next call without arguments
         consumes them.  A data loader's prefetch: each step still moves its
         own inputs.  camera: a DeviceCamera or its packed [48] form
-        (DeviceCamera.pack), which moves in one copy."""
+        (DeviceCamera.pack), which moves in one copy.  A camera of another
+        image size or other clip planes, or a target of another shape or
+        dtype, raises ValueError: only the captured ones can be replayed."""
+        self._check_inputs(camera, target)
         dev = self.target.device
         if not hasattr(self, "_copy"):
             self._copy = torch.cuda.Stream(device=dev)
@@ -521,6 +552,7 @@ class GraphedTrainingStep:
         self._staged = (ready, camera is not None, target is not None)
 
     def __call__(self, camera: DeviceCamera | None = None, target: torch.Tensor | None = None) -> StepOutput:
+        self._check_inputs(camera, target)
         staged = getattr(self, "_staged", None)
         if staged is not None and camera is None and target is None:
             # Device-to-device copies of the staged inputs (microseconds).

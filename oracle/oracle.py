@@ -269,12 +269,20 @@ def clip_grad(image):
     return g
 
 
+PACKED_TILES = ((8, 8), (8, 16), (12, 16), (16, 16))  # (tile_h, tile_w)
+
+
 def training_step(pool, camera, target, *, degree, sh_dim, tile_w, tile_h, max_pairs,
-                  cluster_size=128, bounds=None, timings=None, clusters=None):
-    """Whole hot path of training/step.py:32-89 with the fp32 rasterizer of
-    kernels/sorted_rasterizer.py:165-236 (loss on clip(rgb, 0, 1)):
-    cluster cull -> compact projection -> binning -> raster -> loss -> raster
-    pullback -> projection pullback (compact, rgb_only, active SH only).
+                  cluster_size=128, bounds=None, timings=None, clusters=None, packed=None):
+    """Whole hot path of training/step.py:32-89: cluster cull -> compact
+    projection -> binning -> raster -> loss -> raster pullback -> projection
+    pullback (compact, rgb_only, active SH only).  The loss follows the
+    step's dispatch (training/step.py:74-80): for the packed tile shapes
+    packed_loss_and_grad's (kernels/packed_rasterizer.py:180-216: image
+    min(rgb, 1) over no background, its image gradient passed on as is,
+    packed_rasterize.py:396,440-463), else rasterize_loss_and_grad's
+    (kernels/sorted_rasterizer.py:165-236: loss on clip(rgb, 0, 1) with the
+    clip's VJP); compositing is fp32 either way.  packed overrides the choice.
 
     Returns dict(loss, grads (xyz, log_scale, rotation, opacity, sh) in
     compact order, clusters (ids, count), table, fwd, proj, stats (the [C, 4]
@@ -302,8 +310,13 @@ def training_step(pool, camera, target, *, degree, sh_dim, tile_w, tile_h, max_p
     fwd = raster_fwd(proj, table, W, H, tile_w, tile_h)
     t4 = clock()
     image = fwd["rgb"].reshape(H, W, 3)
-    value, grad = loss(np.clip(image, 0.0, 1.0), target)
-    grad = grad * clip_grad(image)
+    if packed is None:
+        packed = (tile_h, tile_w) in PACKED_TILES
+    if packed:
+        value, grad = loss(np.minimum(image, np.float32(1.0)), target)
+    else:
+        value, grad = loss(np.clip(image, 0.0, 1.0), target)
+        grad = grad * clip_grad(image)
     t5 = clock()
     cot = raster_bwd(proj, table, fwd, grad.reshape(-1), W, H, tile_w, tile_h)
     t6 = clock()

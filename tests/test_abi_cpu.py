@@ -28,7 +28,7 @@ def test_every_declared_symbol_is_exported():
 
 
 def test_abi_version_and_launch_counter():
-    assert L.lib.gsb_abi_version() == 6
+    assert L.lib.gsb_abi_version() == 7
     assert L.launch_count() >= 0
 
 
@@ -54,16 +54,20 @@ def test_invalid_parameters_are_rejected_before_launch():
     bwd = L.ProjectBwdParams(10, 16, 2, 3, 0.2, 128, 1, 1, 1, 1)  # colour-only needs 1
     assert L.lib.gsb_project_bwd(vp, L.ref(bwd), *([vp] * 22)) == 1
     rast = L.RasterParams(10, 64, 48, 12, 8, 100)  # tile width not a multiple of 8
-    assert L.lib.gsb_raster_fwd(vp, L.ref(rast), vp, 0, *([vp] * 17)) == 1
+    assert L.lib.gsb_raster_fwd(vp, L.ref(rast), vp, 0, *([vp] * 18)) == 1
     assert L.lib.gsb_raster_bit_words(L.ref(rast)) == 0
     rast = L.RasterParams(10, 64, 48, 16, 8, 100)
     assert L.lib.gsb_raster_bit_words(L.ref(rast)) == (100 // 32 + 4 * 6 + 1) * 2
-    rast = L.RasterParams(10, 64, 48, 16, 8, 100, 4)  # unknown flag
-    assert L.lib.gsb_raster_fwd(vp, L.ref(rast), vp, 0, *([vp] * 17)) == 1
+    rast = L.RasterParams(10, 64, 48, 16, 8, 100, 8)  # unknown flag
+    assert L.lib.gsb_raster_fwd(vp, L.ref(rast), vp, 0, *([vp] * 18)) == 1
     assert L.lib.gsb_raster_pack(vp, L.ref(rast), *([vp] * 6)) == 1
+    # Forward statistics are gathered only by the recording forward.
+    rast = L.RasterParams(10, 64, 48, 16, 8, 100, L.RASTER_RGB_ONLY | L.RASTER_CLAMP_RGB)
+    stats = ctypes.c_void_p(16)
+    assert L.lib.gsb_raster_fwd(vp, L.ref(rast), vp, 0, *([vp] * 17), stats) == 1
     rast = L.RasterParams(10, 64, 48, 16, 8, 100, L.RASTER_SPLATS_READY)
     assert L.lib.gsb_raster_pack(vp, L.ref(rast), *([vp] * 6)) == 4  # NULL pointers
-    rbwd = L.RasterBwdParams(10, 64, 48, 16, 8, 128, 100, 4)  # unknown flag
+    rbwd = L.RasterBwdParams(10, 64, 48, 16, 8, 128, 100, 4)  # unknown flag (1, 2 are known)
     assert L.lib.gsb_raster_bwd_prepare(vp, L.ref(rbwd), vp, 0, *([vp] * 9)) == 1
     rbwd = L.RasterBwdParams(10, 64, 48, 16, 8, 128, 100, L.RASTER_BWD_PREPARED)
     assert L.lib.gsb_raster_bwd_prepare(vp, L.ref(rbwd), vp, 0, *([vp] * 9)) == 2  # no workspace

@@ -220,6 +220,19 @@ def test_graphed_step_staged_upload_equals_direct_inputs():
     packed = step()
     torch.cuda.synchronize()
     assert float(packed.loss) == loss_direct
+    # Only the captured image size, clip planes and target shape replay.
+    for bad in (Camera.look_at((1.0, 0.3, -3.2), (0.2, 0.0, 0.0), cam.fx, cam.fy, cam.width,
+                               cam.height, near=cam.near * 2, far=cam.far),
+                Camera.look_at((1.0, 0.3, -3.2), (0.2, 0.0, 0.0), cam.fx, cam.fy, cam.width + 16,
+                               cam.height, near=cam.near, far=cam.far)):
+        with pytest.raises(ValueError, match="captured"):
+            step(DeviceCamera.from_camera(bad))
+        with pytest.raises(ValueError, match="captured"):
+            step.upload(DeviceCamera.from_camera(bad, device="cpu"))
+    with pytest.raises(ValueError, match="captured"):
+        step(target=torch.as_tensor(target[:, :64].copy(), device="cuda"))
+    with pytest.raises(ValueError, match="captured"):
+        step.upload(target=torch.as_tensor(target.astype(np.float32) / 255))
 
 
 def _np_sh_from_colors(xyz, centers, colors, degree, sh_dim):

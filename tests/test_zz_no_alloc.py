@@ -3,10 +3,12 @@
 Its per-tile temporaries live in a fixed array inside libgsb200.so, so it is
 compared here with gsb_loss (caller workspace) on the same inputs, on two
 calls in a row of different sizes and target types (the second call must not
-see the first call's leftovers).  This file is collected last so the check
-also covers a process where every other test already used the library; it
-passes alone in a fresh process as well (the first call does the per-device
-set-up).
+see the first call's leftovers).  Both entry points run the same kernels in
+the same order with no atomics, so their results must be equal bit for bit.
+This file is collected last so the check also covers a process where every
+other test already used the library; it passes alone in a fresh process as
+well (the first call does the per-device set-up).  Without a built library
+the module's tests are skipped rather than failing at collection.
 """
 
 import ctypes
@@ -15,12 +17,19 @@ import numpy as np
 import pytest
 import torch
 
-from jaxgs_b200 import _lib as L
-
 GSB_ERR_INVALID = 1
 
 
+def _library():
+    try:
+        from jaxgs_b200 import _lib
+    except (OSError, RuntimeError) as exc:  # library not built on this machine
+        pytest.skip(f"libgsb200.so unavailable: {exc}")
+    return _lib
+
+
 def _params(width, height, target_u8, clip_input):
+    L = _library()
     return L.LossParams(width, height, int(target_u8), int(clip_input))
 
 
@@ -34,6 +43,7 @@ def _outputs(shape):
 
 
 def _with_workspace(image, target, clip_input):
+    L = _library()
     h, w, _ = image.shape
     p = _params(w, h, target.dtype == torch.uint8, clip_input)
     ws_bytes = L.lib.gsb_loss_workspace_size(L.ref(p))
@@ -46,6 +56,7 @@ def _with_workspace(image, target, clip_input):
 
 
 def _without_workspace(image, target, clip_input):
+    L = _library()
     h, w, _ = image.shape
     p = _params(w, h, target.dtype == torch.uint8, clip_input)
     loss, grad, scale = _outputs(image.shape)
@@ -78,15 +89,16 @@ def test_noalloc_loss_matches_workspace_loss_on_two_calls_in_a_row():
         ref_loss, ref_grad, ref_scale = _with_workspace(image, target, clip)
         loss, grad, scale = _without_workspace(image, target, clip)
         torch.cuda.synchronize()
-        # Tolerances of the loss parity tests (loss 1e-5 relative).
-        np.testing.assert_allclose(float(loss), float(ref_loss), rtol=1e-5, atol=2e-6)
-        np.testing.assert_allclose(grad.cpu().numpy(), ref_grad.cpu().numpy(), rtol=2e-4, atol=2e-7)
-        np.testing.assert_allclose(float(scale), float(ref_scale), rtol=1e-5)
+        # Same kernels, same inputs, deterministic reductions: equal bits.
+        assert torch.equal(loss, ref_loss), (float(loss), float(ref_loss))
+        assert torch.equal(grad, ref_grad)
+        assert torch.equal(scale, ref_scale), (float(scale), float(ref_scale))
         assert np.isfinite(float(loss)) and float(scale) > 0
 
 
 def test_noalloc_loss_rejects_images_above_the_tile_limit():
     # Rejected before any CUDA call, so this runs without a GPU too.
+    L = _library()
     limit = 16384
     for w, h in ((4097, 2048), (4096, 2049), (65536, 129)):
         tiles = -(-w // 32) * -(-h // 16)
