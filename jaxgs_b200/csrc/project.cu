@@ -333,6 +333,12 @@ __device__ __forceinline__ bool project_bwd_body(
     float2 gm = make_float2(0.f, 0.f);
     float4 gcn = make_float4(0.f, 0.f, 0.f, 0.f);
     float gc0 = 0.f, gc1 = 0.f, gc2 = 0.f, gal = 0.f;
+    // The parameters and the colour are loaded with the cotangents, in one
+    // round trip, before it is known whether they are needed: a dependent
+    // chain of loads, not bandwidth, bounds this kernel.
+    float wx = 0.f, wy = 0.f, wz = 0.f, ls0 = 0.f, ls1 = 0.f, ls2 = 0.f, op = 0.f;
+    float col0 = 0.f, col1 = 0.f, col2 = 0.f;
+    float4 q = make_float4(0.f, 0.f, 0.f, 0.f);
     bool has = false;
     if (listed) {
         gm = __ldg(reinterpret_cast<const float2*>(gmean + g * 2));
@@ -341,6 +347,17 @@ __device__ __forceinline__ bool project_bwd_body(
         gc1 = gcolor[g * 3 + 1];
         gc2 = gcolor[g * 3 + 2];
         gal = galpha[g];
+        wx = __ldg(xyz + g * 3);
+        wy = __ldg(xyz + g * 3 + 1);
+        wz = __ldg(xyz + g * 3 + 2);
+        q = __ldg(reinterpret_cast<const float4*>(rotation + g * 4));
+        ls0 = __ldg(log_scale + g * 3);
+        ls1 = __ldg(log_scale + g * 3 + 1);
+        ls2 = __ldg(log_scale + g * 3 + 2);
+        op = __ldg(opacity + g);
+        col0 = __ldg(color + g * 3);
+        col1 = __ldg(color + g * 3 + 1);
+        col2 = __ldg(color + g * 3 + 2);
         has = gal != 0.0f || gm.x != 0.0f || gm.y != 0.0f || gcn.x != 0.0f || gcn.y != 0.0f ||
               gcn.z != 0.0f || gcn.w != 0.0f || gc0 != 0.0f || gc1 != 0.0f || gc2 != 0.0f;
         if (!p.rgb_only) has = has || gdepth[g] != 0.0f || gradius[g] != 0.0f;
@@ -359,13 +376,29 @@ __device__ __forceinline__ bool project_bwd_body(
         }
         return true;
     }
+    // With a staged SH output row, the SH input coefficients the direction
+    // gradient needs are copied into that row asynchronously now (16-byte
+    // cp.async, the thread's own row, so no barrier), overlapping the
+    // geometry; they are read back before the row is overwritten.
+    constexpr int kInChunks = (NB * 3) / 4;
+    const bool sh_async = SH_MODE == 0 && DEGREE >= 1 && sh_stage != nullptr &&
+                          (NB * 3) % 4 == 0 && ((p.sh_dim * 3) & 3) == 0 &&
+                          (reinterpret_cast<uintptr_t>(sh) & 15) == 0 &&
+                          kInChunks * 4 <= sh_stage_stride;
+    if (sh_async) {
+        const float4* src = reinterpret_cast<const float4*>(sh + g * (p.sh_dim * 3));
+        const uint32_t dst = (uint32_t)__cvta_generic_to_shared(osh);
+#pragma unroll
+        for (int k = 0; k < kInChunks; k++)
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst + 16 * k),
+                         "l"(src + k)
+                         : "memory");
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    }
     Cam cam;
     load_cam(cam, view, intr, center);
-    const float wx = xyz[g * 3], wy = xyz[g * 3 + 1], wz = xyz[g * 3 + 2];
-    const float4 q = __ldg(reinterpret_cast<const float4*>(rotation + g * 4));
     Geometry geo;
-    geometry(geo, cam, wx, wy, wz, q, log_scale[g * 3], log_scale[g * 3 + 1],
-             log_scale[g * 3 + 2], p.near_plane);
+    geometry(geo, cam, wx, wy, wz, q, ls0, ls1, ls2, p.near_plane);
     const float* v = cam.v;
     const float fx = cam.fx, fy = cam.fy;
     const float inv_z = 1.0f / geo.safe_z, inv_z2 = inv_z * inv_z;
@@ -443,7 +476,7 @@ __device__ __forceinline__ bool project_bwd_body(
         gqz /= qdenom;
     }
     *reinterpret_cast<float4*>(out_rotation + o * 4) = make_float4(gqw, gqx, gqy, gqz);
-    const float alpha = 1.0f / (1.0f + expf(-opacity[g]));
+    const float alpha = 1.0f / (1.0f + expf(-op));
     out_opacity[o] = gal * alpha * (1.0f - alpha);
 
     // SH: colour cotangents pass only where the colour was not clamped.
@@ -451,9 +484,33 @@ __device__ __forceinline__ bool project_bwd_body(
     const float dir_denom = sqrtf(fmaxf(vx * vx + vy * vy + vz * vz, 1e-16f));
     const float dx = vx / dir_denom, dy = vy / dir_denom, dz = vz / dir_denom;
     float gcc[3];
-    gcc[0] = color[g * 3] > 0.0f ? gc0 : 0.0f;
-    gcc[1] = color[g * 3 + 1] > 0.0f ? gc1 : 0.0f;
-    gcc[2] = color[g * 3 + 2] > 0.0f ? gc2 : 0.0f;
+    gcc[0] = col0 > 0.0f ? gc0 : 0.0f;
+    gcc[1] = col1 > 0.0f ? gc1 : 0.0f;
+    gcc[2] = col2 > 0.0f ? gc2 : 0.0f;
+    // dot_k = sum_ch gc_ch * coef[k][ch] for the direction gradient, formed
+    // before the SH gradient row (which may reuse the staged coefficients'
+    // storage) is written.
+    float dot[16];
+    if (DEGREE >= 1) {
+        float cf[NB * 3];
+        if (sh_async) {
+            asm volatile("cp.async.wait_all;" ::: "memory");
+#pragma unroll
+            for (int k = 0; k < kInChunks; k++) {
+                const float4 v4 = reinterpret_cast<const float4*>(osh)[k];
+                cf[4 * k] = v4.x;
+                cf[4 * k + 1] = v4.y;
+                cf[4 * k + 2] = v4.z;
+                cf[4 * k + 3] = v4.w;
+            }
+        } else {
+            load_sh<NB * 3>(sh, g, p.sh_dim * 3,
+                            ((p.sh_dim * 3) & 3) == 0 && (reinterpret_cast<uintptr_t>(sh) & 15) == 0,
+                            cf);
+        }
+#pragma unroll
+        for (int k = 0; k < NB; k++) dot[k] = gcc[0] * cf[3 * k] + gcc[1] * cf[3 * k + 1] + gcc[2] * cf[3 * k + 2];
+    }
     if (SH_MODE == 1) {
         osh[0] = gcc[0];
         osh[1] = gcc[1];
@@ -486,12 +543,6 @@ __device__ __forceinline__ bool project_bwd_body(
     // derivatives of projection_backward.py:259-330.
     float gdx = 0.0f, gdy = 0.0f, gdz = 0.0f;
     if (DEGREE >= 1) {
-        float cf[NB * 3];
-        load_sh<NB * 3>(sh, g, p.sh_dim * 3,
-                        ((p.sh_dim * 3) & 3) == 0 && (reinterpret_cast<uintptr_t>(sh) & 15) == 0, cf);
-        float dot[16];
-#pragma unroll
-        for (int k = 0; k < NB; k++) dot[k] = gcc[0] * cf[3 * k] + gcc[1] * cf[3 * k + 1] + gcc[2] * cf[3 * k + 2];
         const float xx = dx * dx, yy = dy * dy, zz = dz * dz;
         gdx -= kC1 * dot[3];
         gdy -= kC1 * dot[1];
@@ -538,8 +589,11 @@ __device__ __forceinline__ bool project_bwd_body(
 constexpr int kStageChunks = 12;
 constexpr int kStageStride4 = kStageChunks + 1;
 
+// Six blocks per SM (80 registers, a few bytes spilled) measured faster than
+// the five that 94 registers allow: the kernel waits on loads, so more
+// resident warps overlap more of them (config 2: 90 -> 84 us).
 template <int DEGREE, int SH_MODE>
-__global__ void __launch_bounds__(kProjThreads) project_bwd_kernel(
+__global__ void __launch_bounds__(kProjThreads, 6) project_bwd_kernel(
     gsb_project_bwd_params p, const float* __restrict__ xyz, const float* __restrict__ log_scale,
     const float* __restrict__ rotation, const float* __restrict__ opacity,
     const float* __restrict__ sh, const float* view, const float* intr, const float* center,
