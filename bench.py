@@ -232,15 +232,20 @@ def run_ours(args) -> None:
     visible_clusters = int(out.visible_clusters[1].item())
     binned = int((out.point_counts > 0).sum().item())
 
-    # The product step: captured once as a CUDA graph, replayed per view.
-    # NvlsExchange's launches are captured into the step's graph as well.
+    # The product step: captured as CUDA graphs (one per input buffer),
+    # replayed per view.  NvlsExchange's launches are captured into the
+    # step's graphs as well.
     captured = isinstance(exch, NvlsExchange)
     graphed = GraphedTrainingStep(pool, bounds, dcam, target, config, degree, **sharded,
                                   exchange=exch if captured else None)
-    current_center[0] = graphed.camera.center
     if captured:
         def exchange(out):
             return None
+    else:
+        def exchange(out):
+            """The NCCL exchange after the replay, with the replayed camera."""
+            if exch is not None:
+                exch.exchange(graphed.camera.center)
     for _ in range(max(args.warmup, 0)):
         out = graphed()
         exchange(out)
@@ -291,7 +296,12 @@ def run_ours(args) -> None:
         if i + 1 < n_e2e:
             graphed.upload(cam_packed, target_host)
         exchange(out)
-        e2e_loss[i].copy_(out.loss, non_blocking=True)
+        # The step's loss to the host on a side stream (GraphedTrainingStep
+        # makes the next replay of these buffers wait for the copy).
+        read = graphed.read_loss(e2e_loss[i])
+    if n_e2e:
+        # The last readback is part of the timed region.
+        stream.wait_event(read)
     e_end.record(stream)
     torch.cuda.synchronize()
     e2e_elapsed = e_start.elapsed_time(e_end) / 1e3 if not args.no_e2e else float("nan")

@@ -442,19 +442,26 @@ def scatter_compact(grads, clusters, config: CapacityConfig, out=None):
 
 
 class GraphedTrainingStep:
-    """compute_training_step captured once as a CUDA graph, then replayed.
+    """compute_training_step captured as CUDA graphs, then replayed.
 
     The pool, cluster bounds and the returned buffers keep their device
     addresses across replays (an in-place optimizer update of the pool is
-    seen by the next replay).  Each call copies the camera arrays and the
-    target into the graph's static inputs (host or device tensors; host
-    tensors should be pinned for asynchronous copies) and replays.  With
-    pool_grads the gradients land there in pool order on every replay.
+    seen by the next replay).  Inputs are double-buffered: the step is
+    captured once per input buffer (the captures share one memory pool and
+    replay in order on the current stream), so that upload() can write the
+    next step's camera and target straight into the buffer the next replay
+    reads while the current one runs -- a loader's prefetch with no
+    device-to-device copy.  A call with camera/target copies them into the
+    next buffer first (host or device tensors; host tensors should be pinned
+    for asynchronous copies); a call with neither replays the last inputs.
+    With pool_grads the gradients land there in pool order on every replay.
     exchange: an NvlsExchange built for this step (its step_kwargs passed
     here too); its exchange() is captured after the step, so each replay
     also sums the ranks' gradients with no host launch (every rank must
     replay in step).  The sums are self.gradients.
     """
+
+    BUFFERS = 2
 
     def __init__(self, pool: GaussianArrays, bounds, camera: DeviceCamera, target: torch.Tensor,
                  config: CapacityConfig, active_degree: int, *, active_sh_only: bool = True,
@@ -462,117 +469,185 @@ class GraphedTrainingStep:
                  collect_stats: bool = False,
                  stats: torch.Tensor | None = None, exchange=None):
         dev = pool.xyz.device
-        # The graph's camera arrays are views of one packed buffer, so a new
+        # Each buffer's camera arrays are views of one packed buffer, so a new
         # camera arrives in one copy (DeviceCamera.pack).
-        self.camera_flat = camera.pack().to(dev)
-        self.camera = DeviceCamera.packed_views(self.camera_flat, camera.width, camera.height,
-                                                camera.near, camera.far)
-        self.target = torch.empty_like(target, device=dev)
-        self.target.copy_(target)
-        args = (pool, bounds, self.camera, self.target, config, active_degree)
+        self.camera_flats, self.cameras, self.targets = [], [], []
+        for _ in range(self.BUFFERS):
+            flat = camera.pack().to(dev)
+            self.camera_flats.append(flat)
+            self.cameras.append(DeviceCamera.packed_views(flat, camera.width, camera.height,
+                                                          camera.near, camera.far))
+            buf = torch.empty_like(target, device=dev)
+            buf.copy_(target)
+            self.targets.append(buf)
         kwargs = dict(active_sh_only=active_sh_only, sh_color_only=sh_color_only,
                       pool_grads=pool_grads, collect_stats=collect_stats)
         side = torch.cuda.Stream(device=dev)
         side.wait_stream(torch.cuda.current_stream(dev))
         self.exchange = exchange
-        self.gradients = None
         with torch.cuda.stream(side):
             for _ in range(max(warmup, 1)):
-                compute_training_step(*args, **kwargs)
+                compute_training_step(pool, bounds, self.cameras[0], self.targets[0], config,
+                                      active_degree, **kwargs)
                 if exchange is not None:
-                    exchange.exchange(self.camera.center)
+                    exchange.exchange(self.cameras[0].center)
         torch.cuda.current_stream(dev).wait_stream(side)
         # Statistics accumulate across replays into `stats` (the warm-up steps
         # above do not touch it): the captured step adds into it in place.
         if collect_stats:
             kwargs["stats"] = stats if stats is not None else torch.zeros(
                 config.max_gaussians, 4, dtype=torch.float32, device=dev)
-        self.graph = torch.cuda.CUDAGraph()
         from . import _lib
 
+        mempool = torch.cuda.graph_pool_handle()
+        self.graphs, self.outs, self.sums = [], [], []
         before = _lib.launch_count()
-        with torch.cuda.graph(self.graph):
-            self.out = compute_training_step(*args, **kwargs)
-            if exchange is not None:
-                self.gradients = exchange.exchange(self.camera.center)
-        self.launches_per_step = _lib.launch_count() - before
+        for b in range(self.BUFFERS):
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, pool=mempool):
+                out = compute_training_step(pool, bounds, self.cameras[b], self.targets[b],
+                                            config, active_degree, **kwargs)
+                sums = exchange.exchange(self.cameras[b].center) if exchange is not None else None
+            self.graphs.append(graph)
+            self.outs.append(out)
+            self.sums.append(sums)
+        self.launches_per_step = (_lib.launch_count() - before) // self.BUFFERS
+        # Replay b has finished reading buffer b once done[b] has passed.
+        self._done = [torch.cuda.Event() for _ in range(self.BUFFERS)]
+        for ev in self._done:
+            ev.record(torch.cuda.current_stream(dev))
+        self._last = 0
+        self._staged = None
+        self._copy = None
+        self._readback = None
+        self._read_done = [None] * self.BUFFERS
+
+    @property
+    def out(self) -> StepOutput:
+        """The latest replay's output buffers."""
+        return self.outs[self._last]
+
+    @property
+    def camera(self) -> DeviceCamera:
+        """The latest replay's camera arrays (device views)."""
+        return self.cameras[self._last]
+
+    @property
+    def target(self) -> torch.Tensor:
+        return self.targets[self._last]
+
+    @property
+    def gradients(self):
+        """The latest replay's cross-rank gradient sums (with an exchange)."""
+        return self.sums[self._last]
 
     def _check_inputs(self, camera, target) -> None:
-        """The graph keeps the captured camera's image size and clip planes
+        """The graphs keep the captured camera's image size and clip planes
         and the target's shape; a camera or target that differs would be
         replayed with the captured values, so it is refused."""
+        ref_cam, ref_target = self.cameras[0], self.targets[0]
         if isinstance(camera, DeviceCamera):
             got = (camera.width, camera.height, float(camera.near), float(camera.far))
-            want = (self.camera.width, self.camera.height, float(self.camera.near),
-                    float(self.camera.far))
+            want = (ref_cam.width, ref_cam.height, float(ref_cam.near), float(ref_cam.far))
             if got != want:
                 raise ValueError(f"camera (width, height, near, far) {got} differs from the "
                                  f"captured {want}; capture another GraphedTrainingStep")
-        elif camera is not None and camera.numel() != self.camera_flat.numel():
+        elif camera is not None and camera.numel() != self.camera_flats[0].numel():
             raise ValueError(f"packed camera has {camera.numel()} values, expected "
-                             f"{self.camera_flat.numel()}")
-        if target is not None and (tuple(target.shape) != tuple(self.target.shape)
-                                   or target.dtype != self.target.dtype):
+                             f"{self.camera_flats[0].numel()}")
+        if target is not None and (tuple(target.shape) != tuple(ref_target.shape)
+                                   or target.dtype != ref_target.dtype):
             raise ValueError(f"target {tuple(target.shape)} {target.dtype} differs from the "
-                             f"captured {tuple(self.target.shape)} {self.target.dtype}")
+                             f"captured {tuple(ref_target.shape)} {ref_target.dtype}")
+
+    def _write_inputs(self, b: int, camera, target) -> None:
+        """Copy camera/target into buffer b on the current stream; inputs not
+        given are carried over from the latest buffer."""
+        last = self._last
+        if isinstance(camera, DeviceCamera):
+            dst = self.cameras[b]
+            for d, src in ((dst.planes, camera.planes), (dst.world_to_camera, camera.world_to_camera),
+                           (dst.intrinsics, camera.intrinsics), (dst.center, camera.center)):
+                d.copy_(src.reshape(d.shape), non_blocking=True)
+        elif camera is not None:
+            self.camera_flats[b].copy_(camera.reshape(-1), non_blocking=True)
+        elif b != last:
+            self.camera_flats[b].copy_(self.camera_flats[last], non_blocking=True)
+        if target is not None:
+            self.targets[b].copy_(target, non_blocking=True)
+        elif b != last:
+            self.targets[b].copy_(self.targets[last], non_blocking=True)
 
     def upload(self, camera=None, target: torch.Tensor | None = None):
-        """Stage the next step's inputs (pinned host tensors, not modified
-        until that step has run) on a copy stream, so that their transfer
-        overlaps the step in flight; the next call without arguments
-        consumes them.  A data loader's prefetch: each step still moves its
-        own inputs.  camera: a DeviceCamera or its packed [48] form
-        (DeviceCamera.pack), which moves in one copy.  A camera of another
-        image size or other clip planes, or a target of another shape or
-        dtype, raises ValueError: only the captured ones can be replayed."""
+        """Write the next step's inputs (pinned host tensors, not modified
+        until that step has run) into the next input buffer on a copy stream,
+        so that their transfer overlaps the step in flight; the next call
+        without arguments replays with them.  A data loader's prefetch: each
+        step still moves its own inputs.  camera: a DeviceCamera or its
+        packed [48] form (DeviceCamera.pack), which moves in one copy.  A
+        camera of another image size or other clip planes, or a target of
+        another shape or dtype, raises ValueError: only the captured ones can
+        be replayed."""
         self._check_inputs(camera, target)
-        dev = self.target.device
-        if not hasattr(self, "_copy"):
+        dev = self.targets[0].device
+        if self._copy is None:
             self._copy = torch.cuda.Stream(device=dev)
-            self._stage_camera = torch.empty_like(self.camera_flat)
-            self._stage_target = torch.empty_like(self.target)
-            self._consumed = torch.cuda.Event()
-        # The staging buffers are free once the previous staged step took them.
-        self._copy.wait_event(self._consumed)
+        if self._staged is not None:
+            # A second upload before the staged one was consumed replaces it.
+            torch.cuda.current_stream(dev).wait_event(self._staged[1])
+            self._staged = None
+        b = (self._last + 1) % self.BUFFERS
+        # The replay that last read buffer b must be done with it (inputs not
+        # given are copied over from the latest buffer, which the replay in
+        # flight only reads).
+        self._copy.wait_event(self._done[b])
         with torch.cuda.stream(self._copy):
-            if isinstance(camera, DeviceCamera):
-                staged = DeviceCamera.packed_views(self._stage_camera, camera.width,
-                                                   camera.height)
-                for dst, src in ((staged.planes, camera.planes),
-                                 (staged.world_to_camera, camera.world_to_camera),
-                                 (staged.intrinsics, camera.intrinsics),
-                                 (staged.center, camera.center)):
-                    dst.copy_(src.reshape(dst.shape), non_blocking=True)
-            elif camera is not None:
-                self._stage_camera.copy_(camera.reshape(-1), non_blocking=True)
-            if target is not None:
-                self._stage_target.copy_(target, non_blocking=True)
+            self._write_inputs(b, camera, target)
         ready = torch.cuda.Event()
         ready.record(self._copy)
-        self._staged = (ready, camera is not None, target is not None)
+        self._staged = (b, ready)
 
     def __call__(self, camera: DeviceCamera | None = None, target: torch.Tensor | None = None) -> StepOutput:
         self._check_inputs(camera, target)
-        staged = getattr(self, "_staged", None)
-        if staged is not None and camera is None and target is None:
-            # Device-to-device copies of the staged inputs (microseconds).
-            ready, has_camera, has_target = staged
-            current = torch.cuda.current_stream(self.target.device)
-            current.wait_event(ready)
-            if has_camera:
-                self.camera_flat.copy_(self._stage_camera, non_blocking=True)
-            if has_target:
-                self.target.copy_(self._stage_target, non_blocking=True)
-            self._consumed.record(current)
+        stream = torch.cuda.current_stream(self.targets[0].device)
+        staged = self._staged
+        if staged is not None:
+            b, ready = staged
+            stream.wait_event(ready)
             self._staged = None
+            if camera is not None or target is not None:
+                self._write_inputs(b, camera, target)
+        elif camera is not None or target is not None:
+            b = (self._last + 1) % self.BUFFERS
+            self._write_inputs(b, camera, target)
         else:
-            if camera is not None:
-                for dst, src in ((self.camera.world_to_camera, camera.world_to_camera),
-                                 (self.camera.intrinsics, camera.intrinsics),
-                                 (self.camera.center, camera.center),
-                                 (self.camera.planes, camera.planes)):
-                    dst.copy_(src, non_blocking=True)
-            if target is not None:
-                self.target.copy_(target, non_blocking=True)
-        self.graph.replay()
-        return self.out
+            b = self._last
+        if self._read_done[b] is not None:
+            # A loss readback of this buffer's previous replay must finish
+            # before the replay overwrites it.
+            stream.wait_event(self._read_done[b])
+            self._read_done[b] = None
+        self.graphs[b].replay()
+        self._done[b].record(stream)
+        self._last = b
+        return self.outs[b]
+
+    def read_loss(self, dst: torch.Tensor) -> torch.cuda.Event:
+        """Copy the latest replay's loss into dst (one float, pinned host
+        memory) without holding up the next replay: the copy runs on a side
+        stream after the step, and the replay that next overwrites this loss
+        waits for the copy.  Returns the event that marks the copy done (dst
+        is valid once it has passed)."""
+        b = self._last
+        dev = self.targets[0].device
+        if self._readback is None:
+            self._readback = torch.cuda.Stream(device=dev)
+        step_done = torch.cuda.Event()
+        step_done.record(torch.cuda.current_stream(dev))
+        self._readback.wait_event(step_done)
+        with torch.cuda.stream(self._readback):
+            dst.copy_(self.outs[b].loss, non_blocking=True)
+        copied = torch.cuda.Event()
+        copied.record(self._readback)
+        self._read_done[b] = copied
+        return copied

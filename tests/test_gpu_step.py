@@ -235,6 +235,57 @@ def test_graphed_step_staged_upload_equals_direct_inputs():
         step.upload(target=torch.as_tensor(target.astype(np.float32) / 255))
 
 
+def test_graphed_step_double_buffered_inputs_and_loss_readback():
+    """Uploads alternate between the two input buffers: every staged step
+    gives the loss of a direct call with the same inputs, an upload of only
+    the camera keeps the latest target, a call with no inputs repeats the
+    latest step, and read_loss delivers each step's loss to pinned host
+    memory."""
+    from jaxgs_b200.scene import Camera, CapacityConfig, config0_scene, world_cluster_bounds
+    from jaxgs_b200.step import GraphedTrainingStep
+    from jaxgs_b200.types import DeviceCamera, GaussianArrays
+
+    pool_np, cam, target = config0_scene()
+    n = pool_np["xyz"].shape[0]
+    config = CapacityConfig(n, 128, 16, 16, 3, n * 64, tile_height=8)
+    bounds = tuple(torch.as_tensor(a, device="cuda") for a in world_cluster_bounds(pool_np, 128))
+    pool = GaussianArrays.from_numpy(pool_np)
+    step = GraphedTrainingStep(pool, bounds, DeviceCamera.from_camera(cam),
+                               torch.as_tensor(target, device="cuda"), config, 3)
+    cams = [cam] + [Camera.look_at((0.8 * k - 1.0, 0.3, -3.5), (0.1 * k, 0.0, 0.0), cam.fx, cam.fy,
+                                   cam.width, cam.height, near=cam.near, far=cam.far)
+                    for k in range(3)]
+    targets = [target, np.ascontiguousarray(target[::-1]), np.ascontiguousarray(target[:, ::-1]),
+               np.ascontiguousarray(255 - target)]
+    expected = []
+    for c, t in zip(cams, targets):
+        out = step(DeviceCamera.from_camera(c), torch.as_tensor(t, device="cuda"))
+        expected.append(float(out.loss))
+    torch.cuda.synchronize()
+    assert len(set(expected)) == len(expected)
+    host = torch.empty(8, dtype=torch.float32).pin_memory()
+    packed = [DeviceCamera.from_camera(c, device="cpu").pack().pin_memory() for c in cams]
+    pinned = [torch.as_tensor(t).pin_memory() for t in targets]
+    order = [2, 0, 3, 1, 2]
+    step.upload(packed[order[0]], pinned[order[0]])
+    for i, k in enumerate(order):
+        step()
+        if i + 1 < len(order):
+            step.upload(packed[order[i + 1]], pinned[order[i + 1]])
+        read = step.read_loss(host[i])
+    read.synchronize()
+    for i, k in enumerate(order):
+        assert float(host[i]) == expected[k], (i, k)
+    # Camera only: the target of the latest step (order[-1]) is kept.
+    step.upload(packed[1])
+    out = step()
+    again = step()
+    torch.cuda.synchronize()
+    direct = step(DeviceCamera.from_camera(cams[1]), torch.as_tensor(targets[order[-1]], device="cuda"))
+    torch.cuda.synchronize()
+    assert float(out.loss) == float(again.loss) == float(direct.loss)
+
+
 def _np_sh_from_colors(xyz, centers, colors, degree, sh_dim):
     """training/sh_pullback.py:18-53 in numpy (float64), summed over views."""
     out = np.zeros((xyz.shape[0], sh_dim, 3))
