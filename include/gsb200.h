@@ -47,7 +47,7 @@ enum {
     GSB_ERR_NULL = 4        /* required pointer is NULL */
 };
 
-#define GSB_ABI_VERSION 7
+#define GSB_ABI_VERSION 8
 
 /* Library utilities.  No counterpart in the reference, whose boundary
  * (cutlass.jax.cutlass_call) reports errors by raising in Python before
@@ -449,6 +449,11 @@ GSB_API int gsb_loss_noalloc(gsb_stream_t stream, const gsb_loss_params* p, cons
  *    through the multicast address of that row into every GPU's copy.  The
  *    receiving copies must hold zeros where nothing is sent: clear them
  *    after each use.  A gsb_exchange_barrier afterwards publishes the rows.
+ *  - error (the barrier's error word, may be NULL): the three data calls
+ *    return at once on the device when it is set, leaving every buffer as
+ *    it is, since after a barrier that gave up their inputs are not known
+ *    to be complete.  The sums are then stale: check the word (on the host,
+ *    between steps) before an optimizer consumes them.
  * ------------------------------------------------------------------------ */
 typedef struct {
     int world;
@@ -459,11 +464,11 @@ GSB_API int gsb_exchange_barrier(gsb_stream_t stream, const gsb_exchange_params*
                          uint32_t* const* peer_flags, const uint32_t* flags, uint32_t* epoch,
                          int32_t* error);
 GSB_API int gsb_nvls_allreduce(gsb_stream_t stream, const gsb_exchange_params* p, float* multicast,
-                       int64_t count);
+                       int64_t count, const int32_t* error);
 GSB_API int gsb_multicast_nonzero(gsb_stream_t stream, const float* src, float* multicast,
-                          int64_t count);
+                          int64_t count, const int32_t* error);
 GSB_API int gsb_p2p_allreduce(gsb_stream_t stream, const gsb_exchange_params* p,
-                      float* const* buffers, int64_t count);
+                      float* const* buffers, int64_t count, const int32_t* error);
 
 #ifdef __cplusplus
 }

@@ -140,11 +140,11 @@ def _load():
         getattr(lib, name).restype = ctypes.c_int
         getattr(lib, name).argtypes = [vp, vp] + [vp] * n
     lib.gsb_nvls_allreduce.restype = ctypes.c_int
-    lib.gsb_nvls_allreduce.argtypes = [vp, vp, vp, ctypes.c_int64]
+    lib.gsb_nvls_allreduce.argtypes = [vp, vp, vp, ctypes.c_int64, vp]
     lib.gsb_multicast_nonzero.restype = ctypes.c_int
-    lib.gsb_multicast_nonzero.argtypes = [vp, vp, vp, ctypes.c_int64]
+    lib.gsb_multicast_nonzero.argtypes = [vp, vp, vp, ctypes.c_int64, vp]
     lib.gsb_p2p_allreduce.restype = ctypes.c_int
-    lib.gsb_p2p_allreduce.argtypes = [vp, vp, vp, ctypes.c_int64]
+    lib.gsb_p2p_allreduce.argtypes = [vp, vp, vp, ctypes.c_int64, vp]
     lib.gsb_sparse_adam.restype = ctypes.c_int
     lib.gsb_sparse_adam.argtypes = [vp, vp] + [vp] * 8
     lib.gsb_densify_scores.restype = ctypes.c_int
@@ -157,7 +157,7 @@ def _load():
 
 
 lib = _load()
-if lib.gsb_abi_version() != 7:
+if lib.gsb_abi_version() != 8:
     raise RuntimeError("libgsb200.so ABI version mismatch; rebuild with `python -m jaxgs_b200.build`")
 
 

@@ -77,10 +77,15 @@ __global__ void exchange_barrier_kernel(int world, int rank, uint32_t* const* pe
 
 constexpr int kUnroll = 4;  // independent 16-byte chunks in flight per thread
 
-// Shard [begin, end) of the multicast buffer, in float4 chunks.
-__global__ void nvls_allreduce_kernel(float* mc, int64_t begin4, int64_t end4)
+// Shard [begin, end) of the multicast buffer, in float4 chunks.  Every
+// collective returns at once when the exchange's error word is set (a
+// barrier gave up waiting for a peer): its inputs are then not known to be
+// complete, and the buffers are left as they are.
+__global__ void nvls_allreduce_kernel(float* mc, int64_t begin4, int64_t end4,
+                                      const int32_t* error)
 {
     pdl_begin();
+    if (error && *reinterpret_cast<const volatile int32_t*>(error)) return;
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     for (int64_t i = begin4 + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < end4;
          i += stride * kUnroll) {
@@ -101,9 +106,11 @@ __global__ void nvls_allreduce_kernel(float* mc, int64_t begin4, int64_t end4)
 // Chunks that are all zero are not sent: the receiving copies hold zeros
 // there (they are cleared after each use), and most of a view's colour
 // cotangents are zero.
-__global__ void multicast_nonzero_kernel(const float4* __restrict__ src, float* mc, int64_t n4)
+__global__ void multicast_nonzero_kernel(const float4* __restrict__ src, float* mc, int64_t n4,
+                                         const int32_t* error)
 {
     pdl_begin();
+    if (error && *reinterpret_cast<const volatile int32_t*>(error)) return;
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += stride * kUnroll) {
         float4 v[kUnroll];
@@ -127,9 +134,11 @@ struct PeerBuffers {
 };
 constexpr int kP2PUnroll = 2;
 
-__global__ void p2p_allreduce_kernel(PeerBuffers peers, int world, int64_t begin4, int64_t end4)
+__global__ void p2p_allreduce_kernel(PeerBuffers peers, int world, int64_t begin4, int64_t end4,
+                                     const int32_t* error)
 {
     pdl_begin();
+    if (error && *reinterpret_cast<const volatile int32_t*>(error)) return;
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     for (int64_t i = begin4 + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < end4;
          i += stride * kP2PUnroll) {
@@ -186,7 +195,7 @@ extern "C" int gsb_exchange_barrier(gsb_stream_t stream, const gsb_exchange_para
 }
 
 extern "C" int gsb_nvls_allreduce(gsb_stream_t stream, const gsb_exchange_params* p,
-                                  float* multicast, int64_t count)
+                                  float* multicast, int64_t count, const int32_t* error)
 {
     if (!p) return GSB_ERR_NULL;
     if (p->world < 1 || p->rank < 0 || p->rank >= p->world || count < 0 || (count & 3) != 0)
@@ -201,12 +210,13 @@ extern "C" int gsb_nvls_allreduce(gsb_stream_t stream, const gsb_exchange_params
     // against 142 us with eight and 149 us with sixteen.
     const int64_t want = (end - begin + 256 * kUnroll - 1) / (256 * kUnroll);
     const int blocks = (int)(want < 148 * 4 ? want : 148 * 4);
-    gsb::launch(nvls_allreduce_kernel, blocks, 256, 0, as_stream(stream), multicast, begin, end);
+    gsb::launch(nvls_allreduce_kernel, blocks, 256, 0, as_stream(stream), multicast, begin, end,
+                error);
     return check_launch();
 }
 
 extern "C" int gsb_multicast_nonzero(gsb_stream_t stream, const float* src, float* multicast,
-                                     int64_t count)
+                                     int64_t count, const int32_t* error)
 {
     if (count < 0 || (count & 3) != 0) return GSB_ERR_INVALID;
     if (count == 0) return GSB_OK;
@@ -216,12 +226,12 @@ extern "C" int gsb_multicast_nonzero(gsb_stream_t stream, const float* src, floa
     const int64_t want = (n4 + 256 * kUnroll - 1) / (256 * kUnroll);
     const int blocks = (int)(want < 148 * 2 ? want : 148 * 2);
     gsb::launch(multicast_nonzero_kernel, blocks, 256, 0, as_stream(stream),
-                reinterpret_cast<const float4*>(src), multicast, n4);
+                reinterpret_cast<const float4*>(src), multicast, n4, error);
     return check_launch();
 }
 
 extern "C" int gsb_p2p_allreduce(gsb_stream_t stream, const gsb_exchange_params* p,
-                                 float* const* buffers, int64_t count)
+                                 float* const* buffers, int64_t count, const int32_t* error)
 {
     if (!p) return GSB_ERR_NULL;
     if (p->world < 1 || p->world > kMaxPeers || p->rank < 0 || p->rank >= p->world || count < 0 ||
@@ -241,6 +251,6 @@ extern "C" int gsb_p2p_allreduce(gsb_stream_t stream, const gsb_exchange_params*
     const int64_t want = (end - begin + 256 * kP2PUnroll - 1) / (256 * kP2PUnroll);
     const int blocks = (int)(want < 148 * 4 ? want : 148 * 4);
     gsb::launch(p2p_allreduce_kernel, blocks, 256, 0, as_stream(stream), peers, p->world, begin,
-                end);
+                end, error);
     return check_launch();
 }

@@ -150,8 +150,12 @@ def sparse_adam_update(pool: GaussianArrays, state: AdamState, gradients, visibl
             raise ValueError(f"{name} moments must have the field's shape")
         if gradient.dtype != torch.float32:
             raise ValueError(f"{name} gradient must be float32")
-        if gradient.numel() != value.numel() and not compact_gradients:
-            raise ValueError(f"{name} gradient must cover every coefficient of the pool")
+        # Compact gradients also have the pool's shape (the visible-cluster
+        # prefix, tail undefined): the kernel reads up to the listed
+        # clusters' rows, which only the device knows, and never past C rows.
+        if gradient.numel() != value.numel():
+            raise ValueError(f"{name} gradient must have the field's size "
+                             f"({value.numel()} floats, compact or pool order)")
         if gradient.dim() > 1 and tuple(gradient.shape[1:]) != tuple(value.shape[1:]):
             raise ValueError(f"{name} gradient rows must have the field's shape "
                              "(every SH coefficient)")

@@ -355,19 +355,20 @@ class NvlsExchange:
         if camera_center is None:
             raise ValueError("NvlsExchange.exchange needs this rank's camera centre")
         self.own_row[:3].copy_(camera_center.reshape(3))
+        err = ctypes.c_void_p(self.error.data_ptr())
         L.check(L.lib.gsb_multicast_nonzero(ctypes.c_void_p(main.cuda_stream),
                                             ctypes.c_void_p(self.own_row.data_ptr()),
-                                            ctypes.c_void_p(self.mc_row), self.row_floats),
+                                            ctypes.c_void_p(self.mc_row), self.row_floats, err),
                 "colour row all-gather")
         self._barrier()
         self.side.wait_stream(main)
         if self.allreduce == "p2p":
             L.check(L.lib.gsb_p2p_allreduce(ctypes.c_void_p(main.cuda_stream), L.ref(self.params),
-                                            self.geo_peers, self.geo_count), "P2P all-reduce")
+                                            self.geo_peers, self.geo_count, err), "P2P all-reduce")
         else:
             L.check(L.lib.gsb_nvls_allreduce(ctypes.c_void_p(main.cuda_stream),
                                              L.ref(self.params), ctypes.c_void_p(self.mc_geo),
-                                             self.geo_count), "NVLS all-reduce")
+                                             self.geo_count, err), "NVLS all-reduce")
         with torch.cuda.stream(self.side):
             K.sh_from_colors(self.xyz, None, self.rows, self.degree, self.sh_dim, out=self.sh)
             # The all-gather skips all-zero chunks, so the table must be zero
@@ -379,7 +380,10 @@ class NvlsExchange:
         return (*self.pool_grads[:4], self.sh)
 
     def failed(self) -> bool:
-        """Did a barrier give up waiting for a peer (host read, synchronises)?"""
+        """Did a barrier give up waiting for a peer (host read, synchronises)?
+        Once it did, the collectives return without touching their buffers,
+        so the sums are stale: check this (or a StepMonitor) before an
+        optimizer consumes them."""
         return bool(self.error.item())
 
 

@@ -28,7 +28,7 @@ def test_every_declared_symbol_is_exported():
 
 
 def test_abi_version_and_launch_counter():
-    assert L.lib.gsb_abi_version() == 7
+    assert L.lib.gsb_abi_version() == 8
     assert L.launch_count() >= 0
 
 
@@ -104,16 +104,16 @@ def test_optimizer_density_and_exchange_entry_points_validate_before_launch():
     assert L.lib.gsb_densify_scores(vp, 10, *([vp] * 5)) == 4
     assert L.lib.gsb_densify_scores(vp, 0, *([vp] * 5)) == 0
     assert L.lib.gsb_decay_opacity(vp, 10, vp, vp) == 4
-    assert L.lib.gsb_multicast_nonzero(vp, vp, vp, 6) == 1  # not a multiple of 4
-    assert L.lib.gsb_multicast_nonzero(vp, ctypes.c_void_p(8), ctypes.c_void_p(16), 8) == 1
-    assert L.lib.gsb_multicast_nonzero(vp, vp, vp, 0) == 0
+    assert L.lib.gsb_multicast_nonzero(vp, vp, vp, 6, vp) == 1  # not a multiple of 4
+    assert L.lib.gsb_multicast_nonzero(vp, ctypes.c_void_p(8), ctypes.c_void_p(16), 8, vp) == 1
+    assert L.lib.gsb_multicast_nonzero(vp, vp, vp, 0, vp) == 0
     nine = L.ExchangeParams(9, 0)  # more ranks than the P2P form takes
     buffers = (ctypes.c_void_p * 9)(*([16] * 9))
-    assert L.lib.gsb_p2p_allreduce(vp, L.ref(nine), buffers, 8) == 1
+    assert L.lib.gsb_p2p_allreduce(vp, L.ref(nine), buffers, 8, vp) == 1
     two = L.ExchangeParams(2, 0)
-    assert L.lib.gsb_p2p_allreduce(vp, L.ref(two), (ctypes.c_void_p * 2)(16, 24), 8) == 1
-    assert L.lib.gsb_p2p_allreduce(vp, L.ref(two), (ctypes.c_void_p * 2)(16, None), 8) == 4
-    assert L.lib.gsb_p2p_allreduce(vp, L.ref(L.ExchangeParams(2, 2)), buffers, 8) == 1
+    assert L.lib.gsb_p2p_allreduce(vp, L.ref(two), (ctypes.c_void_p * 2)(16, 24), 8, vp) == 1
+    assert L.lib.gsb_p2p_allreduce(vp, L.ref(two), (ctypes.c_void_p * 2)(16, None), 8, vp) == 4
+    assert L.lib.gsb_p2p_allreduce(vp, L.ref(L.ExchangeParams(2, 2)), buffers, 8, vp) == 1
 
 
 def test_sparse_adam_python_checks_refuse_mismatched_rows():

@@ -102,3 +102,43 @@ def test_two_rank_view_sharded_gradients(kind):
     for g, e in zip(got, expected):
         e = e.cpu().numpy()
         assert rel_l2(g.reshape(-1), e.reshape(-1)) < 1e-5
+
+
+def test_barrier_time_out_sets_the_error_word_and_stops_the_all_reduce():
+    """A barrier whose peer never arrives (world 2, one rank running on one
+    GPU; the second flag slot is never written) gives up after its bounded
+    wait, sets the error word and returns, leaving the GPU usable.  The P2P
+    all-reduce that follows reads the word and leaves both copies as they
+    are; the same call without the word sums shard 0 into both (control).
+    Every address is this GPU's own memory."""
+    import ctypes
+
+    from jaxgs_b200 import _lib as L
+
+    dev = torch.device("cuda", 0)
+    ptr = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+    stream = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+    p = L.ExchangeParams(2, 0)
+    flags = torch.zeros(2, dtype=torch.int32, device=dev)  # this rank's slots
+    stand_in = torch.zeros(2, dtype=torch.int32, device=dev)  # in place of rank 1's slots
+    peer_flags = torch.tensor([flags.data_ptr(), stand_in.data_ptr()], dtype=torch.int64,
+                              device=dev)
+    epoch = torch.zeros(1, dtype=torch.int32, device=dev)
+    error = torch.zeros(1, dtype=torch.int32, device=dev)
+    L.check(L.lib.gsb_exchange_barrier(stream, L.ref(p), ptr(peer_flags), ptr(flags), ptr(epoch),
+                                       ptr(error)), "barrier")
+    torch.cuda.synchronize()
+    assert int(error.item()) == 1
+    assert int(epoch.item()) == 1 and int(stand_in[0].item()) == 1
+    a = torch.arange(64, dtype=torch.float32, device=dev)
+    b = 100.0 + a
+    a0, b0 = a.clone(), b.clone()
+    copies = (ctypes.c_void_p * 2)(a.data_ptr(), b.data_ptr())
+    L.check(L.lib.gsb_p2p_allreduce(stream, L.ref(p), copies, 64, ptr(error)), "P2P all-reduce")
+    torch.cuda.synchronize()
+    assert torch.equal(a, a0) and torch.equal(b, b0)
+    L.check(L.lib.gsb_p2p_allreduce(stream, L.ref(p), copies, 64, None), "P2P all-reduce")
+    torch.cuda.synchronize()
+    total = a0[:32] + b0[:32]
+    assert torch.equal(a[:32], total) and torch.equal(b[:32], total)
+    assert torch.equal(a[32:], a0[32:]) and torch.equal(b[32:], b0[32:])

@@ -1,7 +1,7 @@
 """sparse_adam_update refuses an incompatible call before any launch
 (tests/test_chex_contracts.py:57-76): a mask that is not one flag per
-slot, moments of another shape, a gradient of another dtype; the pool and
-the state stay as they were."""
+slot, moments of another shape, a gradient of another dtype or size (in
+pool or compact order); the pool and the state stay as they were."""
 
 import dataclasses
 
@@ -11,7 +11,8 @@ import pytest
 torch = pytest.importorskip("torch")
 
 
-@pytest.mark.parametrize("invalid", ["mask", "moment_shape", "gradient_dtype", "gradient_rows"])
+@pytest.mark.parametrize("invalid", ["mask", "moment_shape", "gradient_dtype", "gradient_rows",
+                                     "compact_short"])
 def test_sparse_adam_update_rejects_incompatible_state(invalid):
     from jaxgs_b200.optimizer import create_adam_state, sparse_adam_update
     from jaxgs_b200.scene import CapacityConfig, create_gaussians, seed_gaussians
@@ -25,20 +26,25 @@ def test_sparse_adam_update_rejects_incompatible_state(invalid):
     gradients = [torch.ones_like(getattr(pool, n)) for n in names]
     visible = pool.alive.to(torch.bool)
     message = {"mask": "one flag per pool slot", "moment_shape": "moments",
-               "gradient_dtype": "float32", "gradient_rows": "coefficient"}[invalid]
+               "gradient_dtype": "float32", "gradient_rows": "field's size",
+               "compact_short": "field's size"}[invalid]
     if invalid == "mask":
         visible = visible[:, None]
     elif invalid == "moment_shape":
         state = dataclasses.replace(state, m=(torch.zeros(1, 3), *state.m[1:]))
     elif invalid == "gradient_dtype":
         gradients[4] = gradients[4].double()
-    else:
+    elif invalid == "gradient_rows":
         gradients[4] = torch.ones(2, 1, 3)
+    else:
+        # A compact gradient shorter than the field: the listed clusters'
+        # rows (known only on the device) could reach past it.
+        gradients[0] = torch.ones(1, 3)
     before = [getattr(pool, n).clone() for n in names]
     clusters = (torch.zeros(2, dtype=torch.int32), torch.ones(1, dtype=torch.int32))
     with pytest.raises(ValueError, match=message):
         sparse_adam_update(pool, state, gradients, visible, 0, 1.0, compacted_clusters=clusters,
-                           cluster_size=1)
+                           cluster_size=1, compact_gradients=invalid == "compact_short")
     for n, b in zip(names, before):
         assert torch.equal(getattr(pool, n), b)
     assert int(state.step.sum()) == 0
