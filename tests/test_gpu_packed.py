@@ -7,7 +7,7 @@ Checked against the oracle with the packed conventions (image min(rgb, 1)
 over no background, the image gradient passed on as given) and against the
 float32 entry points they share kernels with: the symmetric conic
 convention (conic[0, 1] holds both off-diagonal contributions, conic[1, 0]
-stays zero, tests/test_packed.py:414-443) folds the general one exactly,
+stays zero, tests/test_packed.py:79-137) folds the general one exactly,
 and the projection pullback gives the same parameter gradients from both.
 Bars: images 1e-4 max-abs away from threshold-ambiguous pixels, loss 1e-5
 relative, cotangents 1e-3 relative L2.

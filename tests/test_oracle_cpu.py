@@ -633,3 +633,25 @@ def test_oracle_active_sh_and_color_only_pullbacks_match_the_full_one(degree, em
                                full_sh[:, :1], rtol=2e-5, atol=2e-6)
     if not empty:
         assert np.abs(full_sh[:, 0]).max() > 0
+
+
+def test_every_reference_case_names_existing_tests():
+    """tests/golden/known_answers.json lists each reference test that pins
+    this path's values and the tests here that re-express it: each named
+    test function exists, and every case says how the reference obtains its
+    expectation."""
+    import ast
+    import json
+    from pathlib import Path
+
+    root = Path(__file__).resolve().parents[1]
+    cases = json.loads((root / "tests/golden/known_answers.json").read_text())["reference_cases"]
+    defined = {}
+    for case in cases["cases"]:
+        assert case["expectation"] in ("fixed", "jax", "rule"), case
+        for name in case["repo"]:
+            path, func = name.split("::")
+            if path not in defined:
+                tree = ast.parse((root / path).read_text())
+                defined[path] = {n.name for n in ast.walk(tree) if isinstance(n, ast.FunctionDef)}
+            assert func in defined[path], name
