@@ -1,7 +1,8 @@
 """COLMAP scenes (jaxgs_b200.colmap) against the cases of the reference's
 tests/test_dataset.py:19-61 and :110-185: text and binary reconstructions,
 downsampling, SIMPLE_PINHOLE and a flat sparse directory, the refusals,
-and the training resolution rule."""
+and the training resolution rule; also image names in subfolders and the
+whole camera-model table of the binary format."""
 
 import struct
 
@@ -69,10 +70,14 @@ def test_simple_pinhole_and_sparse_without_subdirectory(tmp_path):
                                rtol=1e-6)
     assert all(points.shape == (0, 3) for points in load_colmap_points(tmp_path))
     (sparse / "images.txt").write_text("1 1 0 0 0 0 0 0 1 incomplete.png\n")
-    with pytest.raises(ValueError, match="two lines"):
+    with pytest.raises(ValueError, match="a pose line and a points line"):
         load_colmap(tmp_path)
-    (sparse / "cameras.txt").write_text("1 OPENCV 9 5 6 6 4.5 2.5\n")
+    (sparse / "images.txt").write_text("1 1 0 0 0 0 0 0 1 image with spaces.png\n\n")
+    (sparse / "cameras.txt").write_text("1 OPENCV 9 5 6 6 4.5 2.5 0.1 0 0 0\n")
     with pytest.raises(ValueError, match="undistorted"):
+        load_colmap(tmp_path)
+    (sparse / "cameras.txt").write_text("2 PINHOLE 9 5 6 6 4.5 2.5\n")
+    with pytest.raises(ValueError, match="camera 1 is not in"):
         load_colmap(tmp_path)
 
 
@@ -88,7 +93,7 @@ def test_colmap_rejects_truncated_or_unsupported_binary(tmp_path, damage):
         expected = "truncated COLMAP binary"
     elif damage == "model":
         cameras = struct.pack("<QiiQQ", 1, 1, 99, 4, 4)
-        expected = "unsupported COLMAP model"
+        expected = "not a COLMAP camera model"
     (sparse / "cameras.bin").write_bytes(cameras)
     (sparse / "images.bin").write_bytes(images + b"missing terminator")
     with pytest.raises(ValueError, match=expected):
@@ -118,3 +123,31 @@ def test_training_resolution_matches_native_resize(tmp_path, width, height, reso
     np.testing.assert_array_equal(frame.load_rgb(), resized)
     with pytest.raises(ValueError, match="resolution"):
         load_colmap_images(tmp_path, "pyramid", resolution=0)
+
+
+def test_binary_cameras_of_every_model_parse_and_only_pinholes_are_used(tmp_path):
+    """Every COLMAP model's parameter count is known, so a reconstruction
+    that mixes models parses; a frame of a distorted camera is refused."""
+    from jaxgs_b200.colmap import CAMERA_MODELS, read_cameras
+
+    sparse = tmp_path / "sparse"
+    sparse.mkdir()
+    blob = struct.pack("<Q", len(CAMERA_MODELS))
+    for model_id, (_, n) in CAMERA_MODELS.items():
+        blob += struct.pack("<iiQQ", model_id + 1, model_id, 8, 6) + struct.pack(
+            f"<{n}d", *[float(k + 1) for k in range(n)])
+    (sparse / "cameras.bin").write_bytes(blob)
+    cameras = read_cameras(sparse, binary=True)
+    assert [cameras[i + 1].model for i in range(len(CAMERA_MODELS))] == [
+        name for name, _ in CAMERA_MODELS.values()]
+    assert cameras[2].params == (1.0, 2.0, 3.0, 4.0)
+    images = struct.pack("<Qi4d3di", 1, 1, 1, 0, 0, 0, 0, 0, 0, 5) + b"a/b.png\0" + \
+        struct.pack("<Q", 2) + struct.pack("<ddq", 1, 2, -1) * 2
+    (sparse / "images.bin").write_bytes(images)
+    with pytest.raises(ValueError, match="not an undistorted pinhole"):
+        load_colmap(tmp_path)
+    images = images[:8] + struct.pack("<i4d3di", 1, 1, 0, 0, 0, 0, 0, 0, 2) + images[72:]
+    (sparse / "images.bin").write_bytes(images)
+    (frame,) = load_colmap(tmp_path)
+    assert frame.image_path == tmp_path / "images" / "a" / "b.png"
+    assert (frame.camera.width, frame.camera.height) == (8, 6)
