@@ -47,7 +47,7 @@ enum {
     GSB_ERR_NULL = 4        /* required pointer is NULL */
 };
 
-#define GSB_ABI_VERSION 8
+#define GSB_ABI_VERSION 9
 
 /* Library utilities.  No counterpart in the reference, whose boundary
  * (cutlass.jax.cutlass_call) reports errors by raising in Python before
@@ -173,6 +173,40 @@ GSB_API int gsb_sparse_adam(gsb_stream_t stream, const gsb_adam_params* p, float
                     float* mean, float* variance, const float* gradient, const int8_t* alive,
                     const int32_t* cluster_ids, const int32_t* cluster_count,
                     const float* rate);
+
+/* ------------------------------------------------------------------------
+ * Sparse Adam of the SH field with the SH gradient rebuilt inside the update.
+ * Replaces the deferred SH pullback of training/optimizer.py:180-261
+ * (optax_update with sh_pullback_center, which wraps the update in
+ * training/sh_pullback.py:18-53 with_sh_pullback) fused with the "sh" field
+ * of kernels/sparse_adam.py:98-136 update_field.  For every alive slot of
+ * the listed clusters the gradient
+ *   g[k][c] = sum over views v of Y_k(dir_v) * colour_v[c]
+ * (k below (degree + 1)^2; zero for the bands above) is formed in shared
+ * memory with the arithmetic of gsb_sh_from_colors, and the LiteGS update of
+ * gsb_sparse_adam (is_sh) is applied to all sh_dim * 3 channels, so the
+ * [C, sh_dim, 3] gradient is never written or read.
+ * colors + v * view_stride: view v's masked colour cotangents (the
+ * sh_color_only output of gsb_project_bwd), [C*3] in pool order or, with
+ * compact_colors, the visible-cluster prefix [count * cluster_size * 3];
+ * centers + v * center_stride: view v's camera centre; strides in floats,
+ * 0 = dense.  sh/mean/variance[C * sh_dim * 3] are updated in place.
+ * ------------------------------------------------------------------------ */
+typedef struct {
+    int capacity;
+    int sh_dim;          /* coefficients per slot, 1..16 */
+    int degree;          /* active SH degree, 0..3 */
+    int cluster_size;
+    int views;
+    int compact_colors;
+    int64_t view_stride;
+    int64_t center_stride;
+} gsb_adam_sh_params;
+
+GSB_API int gsb_sparse_adam_sh(gsb_stream_t stream, const gsb_adam_sh_params* p, float* sh,
+                       float* mean, float* variance, const float* xyz, const float* centers,
+                       const float* colors, const int8_t* alive, const int32_t* cluster_ids,
+                       const int32_t* cluster_count, const float* rate);
 
 /* ------------------------------------------------------------------------
  * Density-control consumers of the fragment statistics.

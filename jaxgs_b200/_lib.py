@@ -78,6 +78,13 @@ class AdamParams(ctypes.Structure):
                 ("compact_gradients", ctypes.c_int)]
 
 
+class AdamShParams(ctypes.Structure):
+    _fields_ = [("capacity", ctypes.c_int), ("sh_dim", ctypes.c_int), ("degree", ctypes.c_int),
+                ("cluster_size", ctypes.c_int), ("views", ctypes.c_int),
+                ("compact_colors", ctypes.c_int), ("view_stride", ctypes.c_int64),
+                ("center_stride", ctypes.c_int64)]
+
+
 class LossParams(ctypes.Structure):
     _fields_ = [("width", ctypes.c_int), ("height", ctypes.c_int), ("target_u8", ctypes.c_int),
                 ("clip_input", ctypes.c_int)]
@@ -93,7 +100,7 @@ SYMBOLS = (
     "gsb_raster_pack", "gsb_raster_bwd_prepare",
     "gsb_loss_workspace_size", "gsb_loss", "gsb_loss_noalloc",
     "gsb_exchange_barrier", "gsb_nvls_allreduce", "gsb_multicast_nonzero", "gsb_p2p_allreduce",
-    "gsb_sparse_adam", "gsb_densify_scores", "gsb_decay_opacity",
+    "gsb_sparse_adam", "gsb_sparse_adam_sh", "gsb_densify_scores", "gsb_decay_opacity",
 )
 
 
@@ -147,6 +154,8 @@ def _load():
     lib.gsb_p2p_allreduce.argtypes = [vp, vp, vp, ctypes.c_int64, vp]
     lib.gsb_sparse_adam.restype = ctypes.c_int
     lib.gsb_sparse_adam.argtypes = [vp, vp] + [vp] * 8
+    lib.gsb_sparse_adam_sh.restype = ctypes.c_int
+    lib.gsb_sparse_adam_sh.argtypes = [vp, vp] + [vp] * 10
     lib.gsb_densify_scores.restype = ctypes.c_int
     lib.gsb_densify_scores.argtypes = [vp, ctypes.c_int64] + [vp] * 5
     lib.gsb_decay_opacity.restype = ctypes.c_int
@@ -157,7 +166,7 @@ def _load():
 
 
 lib = _load()
-if lib.gsb_abi_version() != 8:
+if lib.gsb_abi_version() != 9:
     raise RuntimeError("libgsb200.so ABI version mismatch; rebuild with `python -m jaxgs_b200.build`")
 
 

@@ -9,13 +9,12 @@
 // straight-line code.  HBM-bound: 286 B/Gaussian forward, 524 B/Gaussian
 // backward (236 B with colour-only SH gradients).
 #include "gsb_common.cuh"
+#include "sh.cuh"
 
 namespace gsb {
 namespace {
 
 constexpr int kProjThreads = 128;
-constexpr float kC0 = 0.28209479177387814f;
-constexpr float kC1 = 0.4886025119029199f;
 
 struct Cam {
     float v[12];
@@ -83,35 +82,6 @@ __device__ __forceinline__ bool cluster_listed_warp(const int32_t* ids, int coun
     const bool below = pos < hi && __ldg(ids + pos) < c0;
     const int first = lo + __popc(__ballot_sync(GSB_FULL_MASK, below));
     return first < count && __ldg(ids + first) == c0;
-}
-
-// SH basis values (LiteGS/3DGS real SH order, reference/sh.py:8-36).
-template <int DEGREE>
-__device__ __forceinline__ void sh_basis(float dx, float dy, float dz, float b[16])
-{
-    float xx = dx * dx, yy = dy * dy, zz = dz * dz;
-    b[0] = kC0;
-    if (DEGREE >= 1) {
-        b[1] = -kC1 * dy;
-        b[2] = kC1 * dz;
-        b[3] = -kC1 * dx;
-    }
-    if (DEGREE >= 2) {
-        b[4] = 1.0925484305920792f * dx * dy;
-        b[5] = -1.0925484305920792f * dy * dz;
-        b[6] = 0.31539156525252005f * (2.0f * zz - xx - yy);
-        b[7] = -1.0925484305920792f * dx * dz;
-        b[8] = 0.5462742152960396f * (xx - yy);
-    }
-    if (DEGREE >= 3) {
-        b[9] = -0.5900435899266435f * dy * (3.0f * xx - yy);
-        b[10] = 2.890611442640554f * dx * dy * dz;
-        b[11] = -0.4570457994644658f * dy * (4.0f * zz - xx - yy);
-        b[12] = 0.3731763325901154f * dz * (2.0f * zz - 3.0f * xx - 3.0f * yy);
-        b[13] = -0.4570457994644658f * dx * (4.0f * zz - xx - yy);
-        b[14] = 1.445305721320277f * dz * (xx - yy);
-        b[15] = -0.5900435899266435f * dx * (xx - 3.0f * yy);
-    }
 }
 
 // Loads floats [0, N) of one Gaussian's SH row (row stride `row` floats):
@@ -665,24 +635,8 @@ __global__ void __launch_bounds__(kProjThreads) sh_from_colors_kernel(
 #pragma unroll
     for (int c = 0; c < NB * 3; c++) acc[c] = 0.0f;
     if (active) {
-        const float wx = xyz[g * 3], wy = xyz[g * 3 + 1], wz = xyz[g * 3 + 2];
-        for (int v = 0; v < views; v++) {
-            const float* col = colors + v * view_stride + g * 3;
-            const float c0 = col[0], c1 = col[1], c2 = col[2];
-            if (c0 == 0.0f && c1 == 0.0f && c2 == 0.0f) continue;
-            const float* cv = centers + v * center_stride;
-            const float vx = wx - __ldg(cv), vy = wy - __ldg(cv + 1), vz = wz - __ldg(cv + 2);
-            const float dir_denom = sqrtf(fmaxf(vx * vx + vy * vy + vz * vz, 1e-16f));
-            const float dx = vx / dir_denom, dy = vy / dir_denom, dz = vz / dir_denom;
-            float bas[16];
-            sh_basis<DEGREE>(dx, dy, dz, bas);
-#pragma unroll
-            for (int k = 0; k < NB; k++) {
-                acc[k * 3] = fmaf(bas[k], c0, acc[k * 3]);
-                acc[k * 3 + 1] = fmaf(bas[k], c1, acc[k * 3 + 1]);
-                acc[k * 3 + 2] = fmaf(bas[k], c2, acc[k * 3 + 2]);
-            }
-        }
+        sh_expand_views<DEGREE>(xyz[g * 3], xyz[g * 3 + 1], xyz[g * 3 + 2], views,
+                                colors + g * 3, view_stride, centers, center_stride, acc);
     }
     const int n = sh_dim * 3;
     const int chunks = n >> 2;

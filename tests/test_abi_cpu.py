@@ -28,7 +28,7 @@ def test_every_declared_symbol_is_exported():
 
 
 def test_abi_version_and_launch_counter():
-    assert L.lib.gsb_abi_version() == 8
+    assert L.lib.gsb_abi_version() == 9
     assert L.launch_count() >= 0
 
 
@@ -100,6 +100,16 @@ def test_optimizer_density_and_exchange_entry_points_validate_before_launch():
     adam = L.AdamParams(10, 3, 128, 0, 0)
     assert L.lib.gsb_sparse_adam(vp, L.ref(adam), *([vp] * 8)) == 4
     assert L.lib.gsb_sparse_adam(vp, L.ref(L.AdamParams(0, 3, 128, 0, 0)), *([vp] * 8)) == 0
+    sh = L.AdamShParams(10, 17, 3, 128, 1, 1, 0, 0)  # more than 16 coefficients
+    assert L.lib.gsb_sparse_adam_sh(vp, L.ref(sh), *([vp] * 10)) == 1
+    sh = L.AdamShParams(10, 4, 2, 128, 1, 1, 0, 0)  # (2+1)^2 > sh_dim
+    assert L.lib.gsb_sparse_adam_sh(vp, L.ref(sh), *([vp] * 10)) == 1
+    sh = L.AdamShParams(10, 16, 3, 128, 1, 1, 0, 2)  # centre stride below 3
+    assert L.lib.gsb_sparse_adam_sh(vp, L.ref(sh), *([vp] * 10)) == 1
+    sh = L.AdamShParams(10, 16, 3, 128, 1, 1, 0, 0)
+    assert L.lib.gsb_sparse_adam_sh(vp, L.ref(sh), *([vp] * 10)) == 4
+    sh = L.AdamShParams(0, 16, 3, 128, 1, 1, 0, 0)
+    assert L.lib.gsb_sparse_adam_sh(vp, L.ref(sh), *([vp] * 10)) == 0
     assert L.lib.gsb_densify_scores(vp, -1, *([vp] * 5)) == 1
     assert L.lib.gsb_densify_scores(vp, 10, *([vp] * 5)) == 4
     assert L.lib.gsb_densify_scores(vp, 0, *([vp] * 5)) == 0

@@ -129,3 +129,111 @@ def test_sparse_adam_after_the_training_step():
         np.testing.assert_array_equal(getattr(pool, name).cpu().numpy().reshape(-1), exp[0])
         np.testing.assert_array_equal(state.m[i].cpu().numpy().reshape(-1), exp[1])
     assert int(state.step.sum().item()) == int((visible.cpu().numpy() & pool_np["alive"]).sum())
+
+
+@pytest.mark.parametrize("degree,views,cluster_size,compact",
+                         [(3, 1, 128, True), (3, 3, 128, False), (1, 2, 5, True), (0, 1, 128, False),
+                          (2, 1, 200, True)])
+def test_sh_adam_from_colours_equals_expansion_then_update(degree, views, cluster_size, compact):
+    """gsb_sparse_adam_sh (SH gradient rebuilt inside the update) against the
+    unfused pair it replaces, gsb_sh_from_colors (training/sh_pullback.py:18-53)
+    then gsb_sparse_adam on the materialised [C, 16, 3] gradient: value and
+    both moments bit for bit, with dead slots, zero colour rows, a partial
+    last cluster and clusters of more than one block of slots."""
+    from jaxgs_b200 import kernels as K
+    from jaxgs_b200.optimizer import update_field, update_sh_from_colors
+
+    rng = np.random.default_rng(degree * 31 + views * 7 + cluster_size)
+    capacity, sh_dim = 1000, 16
+    n_clusters = -(-capacity // cluster_size)
+    listed = np.sort(rng.choice(n_clusters, size=max(1, n_clusters // 2), replace=False))
+    ids = np.zeros(n_clusters, np.int32)
+    ids[:len(listed)] = listed
+    count = len(listed)
+    clusters = (_dev(ids), _dev(np.array([count], np.int32)))
+    alive = (rng.random(capacity) < 0.9).astype(np.uint8)
+    xyz = rng.normal(0, 3, (capacity, 3)).astype(np.float32)
+    centers = rng.normal(0, 6, (views, 3)).astype(np.float32)
+    colors = rng.normal(0, 0.2, (views, capacity, 3)).astype(np.float32)
+    colors[:, rng.random(capacity) < 0.3] = 0.0  # slots a view does not see
+    value = rng.normal(0, 1, (capacity, sh_dim, 3)).astype(np.float32)
+    mean = rng.normal(0, 0.1, value.shape).astype(np.float32)
+    var = (rng.random(value.shape) * 0.01).astype(np.float32)
+    rate = float(O.parameter_learning_rates(5, 1.0, 30000, **ADAM_RATES)[4])
+
+    gsh = K.sh_from_colors(_dev(xyz), _dev(centers), _dev(colors), degree, sh_dim)
+    x0, m0, v0 = _dev(value), _dev(mean), _dev(var)
+    update_field(x0, m0, v0, gsh, _dev(alive), clusters, rate, cluster_size, True, False)
+
+    if compact:
+        # The listed clusters' rows in list order; ids are sorted, so only
+        # the last listed cluster can be partial and the prefix fits in C
+        # rows.  Rows past it are NaN: they must never be read.
+        slots = (ids[:count, None] * cluster_size + np.arange(cluster_size)).reshape(-1)
+        slots = slots[slots < capacity]
+        given = np.full((views, capacity, 3), np.nan, np.float32)
+        given[:, :len(slots)] = colors[:, slots]
+    else:
+        given = colors
+    x1, m1, v1 = _dev(value), _dev(mean), _dev(var)
+    update_sh_from_colors(x1, m1, v1, _dev(xyz), _dev(centers), _dev(given), _dev(alive),
+                          clusters, rate, cluster_size, degree, compact)
+    torch.cuda.synchronize()
+    for got, ref, what in ((x1, x0, "value"), (m1, m0, "mean"), (v1, v0, "variance")):
+        assert torch.equal(got, ref), what
+    assert not torch.equal(x1, _dev(value))
+
+
+def test_sparse_adam_update_with_sh_pullback_center_equals_the_unfused_update():
+    """sparse_adam_update(..., sh_pullback_center=camera centre) on the
+    step's sh_color_only gradients (training/step.py:55-66 and :95-111, the
+    reference's deferred SH update) equals the unfused update of the same
+    gradients: the colour cotangent expanded by gsb_sh_from_colors at the
+    positions before the update, then gsb_sparse_adam on every field; all
+    fields and moments bit for bit, and the step counts alike."""
+    from jaxgs_b200 import kernels as K
+    from jaxgs_b200.optimizer import (create_adam_state, parameter_learning_rates,
+                                      sparse_adam_update, update_field)
+    from jaxgs_b200.scene import CapacityConfig, config0_scene, world_cluster_bounds
+    from jaxgs_b200.step import compute_training_step
+    from jaxgs_b200.types import DeviceCamera, GaussianArrays
+
+    pool_np, cam, target = config0_scene()
+    n = pool_np["xyz"].shape[0]
+    config = CapacityConfig(n, 128, 16, 16, 3, n * 64, tile_height=8)
+    c, e, v = world_cluster_bounds(pool_np, 128)
+    bounds = (_dev(c), _dev(e), _dev(v.astype(np.uint8)))
+    dcam = DeviceCamera.from_camera(cam)
+    pool = GaussianArrays.from_numpy(pool_np)
+    out = compute_training_step(pool, bounds, dcam, _dev(target), config, 2, sh_color_only=True)
+    assert out.gradients[4].numel() == n * 3
+    count = int(out.visible_clusters[1].item())
+    listed = out.visible_clusters[0][:count].long()
+    slots = (listed[:, None] * 128 + torch.arange(128, device="cuda")).reshape(-1)
+    slots = slots[slots < n]
+    visible = torch.zeros(n, dtype=torch.bool, device="cuda")
+    visible[slots] = True
+
+    state = create_adam_state(pool)
+    sparse_adam_update(pool, state, out.gradients, visible, 10, 3.0,
+                       compacted_clusters=out.visible_clusters, compact_gradients=True,
+                       sh_pullback_center=dcam.center, active_degree=2)
+
+    ref = GaussianArrays.from_numpy(pool_np)
+    ref_state = create_adam_state(ref)
+    colors = torch.zeros(n, 3, device="cuda")
+    colors[slots] = out.gradients[4].reshape(-1, 3)[:slots.numel()]
+    gsh = K.sh_from_colors(ref.xyz, dcam.center.reshape(1, 3), colors[None], 2, 16)
+    rates = parameter_learning_rates(10, 3.0)
+    for i, name in enumerate(NAMES):
+        grad = gsh if name == "sh" else out.gradients[i]
+        update_field(getattr(ref, name), ref_state.m[i], ref_state.v[i], grad.contiguous(),
+                     ref.alive, out.visible_clusters, rates[i], 128, name == "sh",
+                     name != "sh")
+    torch.cuda.synchronize()
+    for i, name in enumerate(NAMES):
+        assert torch.equal(getattr(pool, name), getattr(ref, name)), name
+        assert torch.equal(state.m[i], ref_state.m[i]) and torch.equal(state.v[i],
+                                                                      ref_state.v[i]), name
+    assert not torch.equal(pool.sh, GaussianArrays.from_numpy(pool_np).sh)
+    assert int(state.step.sum().item()) == int((visible & pool.alive.bool()).sum().item())
