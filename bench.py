@@ -11,10 +11,12 @@ pullback to xyz/log_scale/rotation/opacity/SH (degree 3).  Synthetic data.
 
 Multi-GPU (torchrun, one rank per GPU): every rank renders one view per step
 (ring camera r of BASELINE config 3's ring, radius 6) and the ranks sum the
-per-view gradients (jaxgs_b200.step.ViewShardedExchange: all-reduce of the
-geometric gradients, all-gather of the 3-float colour cotangents, SH
-expansion of all views on every rank); value = views of all ranks /
-max-over-ranks time.
+per-view gradients inside the step's CUDA graph (jaxgs_b200.step.NvlsExchange:
+peer or NVLS all-reduce of the geometric gradients, multicast all-gather of
+the non-zero colour cotangents, SH expansion of all views on every rank;
+GSB_EXCHANGE=nccl takes ViewShardedExchange's NCCL collectives instead);
+value = views of all ranks / max-over-ranks time.  stage_ms.exchange is the
+exchange's own time in the eager steps.
 
 --impl reference times the reference path's CPU restatement (oracle/, the
 reference being JAX code that is not installed here) on the host cores.
@@ -40,6 +42,8 @@ UNIT = "views/s"
 
 
 def _config():
+    """Config 2's capacities; run_ours sizes the pair arena from the count
+    pass (the 8M here, the reference's default, is only the probe's)."""
     from jaxgs_b200.scene import CapacityConfig
 
     return CapacityConfig(max_gaussians=1_000_000, cluster_size=128, tile_size=16, sh_degree=3,
@@ -179,6 +183,15 @@ def run_ours(args) -> None:
     bounds = (torch.as_tensor(center, device=device), torch.as_tensor(extent, device=device),
               torch.as_tensor(valid.astype(np.uint8), device=device))
     dcam = DeviceCamera.from_camera(camera, device=device)
+    # The pair arena from the count pass over the ring's eight views (the
+    # same on every rank), not a fixed default.
+    from jaxgs_b200.scene import ring_cameras
+    from jaxgs_b200.step import size_pair_arena
+
+    ring = [DeviceCamera.from_camera(c, device=device)
+            for c in ring_cameras(8, radius=6.0, height=1.5)]
+    config = size_pair_arena(pool, bounds, ring, config, 3)
+    del ring
     target = _target(camera, device)
     target_host = target.cpu().pin_memory()
     cam_host = [t.cpu().pin_memory() for t in (dcam.world_to_camera, dcam.intrinsics,
@@ -220,7 +233,14 @@ def run_ours(args) -> None:
         exchange(out)
     for _ in range(args.steps):
         out = eager_step(dcam, target, record=True)
-        exchange(out)
+        if exch is not None:
+            # The exchange as its own stage: barrier, gradient sum, colour
+            # all-gather and SH expansion, on the launching stream.
+            ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+            ev[0].record(stream)
+            exchange(out)
+            ev[1].record(stream)
+            stage_events[-1]["exchange"] = ev
     torch.cuda.synchronize()
     stage_ms = {}
     for events in stage_events:
@@ -231,6 +251,7 @@ def run_ours(args) -> None:
     overflow = bool(out.overflow.item())
     visible_clusters = int(out.visible_clusters[1].item())
     binned = int((out.point_counts > 0).sum().item())
+    visits = _backward_visits(pool, bounds, dcam, config, degree) if rank == 0 else 0
 
     # The product step: captured as CUDA graphs (one per input buffer),
     # replayed per view.  NvlsExchange's launches are captured into the
@@ -311,6 +332,15 @@ def run_ours(args) -> None:
     # cluster sparse Adam over the step's compact gradients.
     inference = _time_inference(pool, camera, stream) if world == 1 else None
     optimizer = _time_optimizer(pool, graphed.out, stream) if world == 1 else None
+    # The reference's default step defers the SH pullback to its optimizer
+    # (training/step.py:55-66): the same view's colour-only gradients feed the
+    # update that rebuilds SH gradients itself.
+    deferred = None
+    if world == 1:
+        colour_out = compute_training_step(pool, bounds, dcam, target, config, degree,
+                                           sh_color_only=True)
+        deferred = _time_optimizer(pool, colour_out, stream, center=dcam.center)
+    heavy = _time_config4(stream) if world == 1 and not args.no_config4 else None
     d2h = 4
 
     if world > 1:
@@ -331,6 +361,7 @@ def run_ours(args) -> None:
             "config": {"workload": "BASELINE config 2: 1M-Gaussian training step, 1237x822, 8x16 tiles, SH3",
                        "gaussians": 1_000_000, "width": 1237, "height": 822, "tile": "8x16",
                        "views_per_gpu_per_step": 1, "pairs": pairs, "overflow": overflow,
+                       "pair_arena": config.max_visibility_pairs,
                        "visible_clusters": visible_clusters, "binned_gaussians": binned,
                        "l2": "inputs larger than L2 (236 MB pool)",
                        "launch": "CUDA graph replay of the whole step",
@@ -342,34 +373,25 @@ def run_ours(args) -> None:
             "clocks": clocks,
             "stage_ms": {k: round(v, 4) for k, v in stage_ms.items()},
         }
-        line["roofline"] = _roofline(stage_ms, peak, peak_kind, pairs, binned)
+        # Nine reductions per visit under the packed conventions (two mean,
+        # three conic with the off-diagonal once, three colour, opacity).
+        line["roofline"] = _roofline(stage_ms, peak, peak_kind, pairs, binned, visits,
+                                     clocks.get("sm_mhz") or 1965.0, 9)
         if inference is not None:
             line["inference"] = inference
-        if optimizer is not None:
-            optimizer["frac"] = round(optimizer["achieved_gbs"] / peak, 4)
-            optimizer["peak_gbs"] = peak
-            line["optimizer"] = optimizer
+        for key, entry in (("optimizer", optimizer), ("optimizer_deferred_sh", deferred)):
+            if entry is not None:
+                entry["frac"] = round(entry["achieved_gbs"] / peak, 4)
+                entry["peak_gbs"] = peak
+                line[key] = entry
+        if heavy is not None:
+            line["config4"] = heavy
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(pool_np, camera, target.cpu().numpy())
         print(json.dumps(line), flush=True)
     if world > 1:
         del graphed
         dist.destroy_process_group()
-
-
-def _profile_value(name: str, key: str):
-    """A figure recorded in a committed ncu summary (profiles/<name>.md,
-    line `key: value`), or None."""
-    path = ROOT / "profiles" / f"{name}.md"
-    if not path.exists():
-        return None
-    for line in path.read_text().splitlines():
-        if line.strip().startswith(key + ":"):
-            try:
-                return float(line.split(":", 1)[1].strip().split()[0])
-            except ValueError:
-                return None
-    return None
 
 
 def _exchange_text(exch, config) -> str:
@@ -410,16 +432,20 @@ def _time_inference(pool, camera, stream, iters: int = 30) -> dict:
             "overflow": bool(overflow.item())}
 
 
-def _time_optimizer(pool, out, stream, iters: int = 20) -> dict:
-    """sparse_adam_update's five field launches (gsb_sparse_adam) over the
-    step's compact gradients, CUDA events on the launching stream.
-    Algorithmic bytes: per element of an alive listed slot, value, both
-    moments and the gradient read (16 B) and value and moments written
-    (12 B); 59 elements per Gaussian at SH degree 3."""
+def _time_optimizer(pool, out, stream, iters: int = 20, center=None) -> dict:
+    """sparse_adam_update's field launches over the step's compact
+    gradients, CUDA events on the launching stream.  Algorithmic bytes: per
+    element of an alive listed slot, value, both moments and the gradient
+    read (16 B) and value and moments written (12 B); 59 elements per
+    Gaussian at SH degree 3.  With `center` the SH gradient is the step's
+    colour cotangent and the SH field's update rebuilds it
+    (gsb_sparse_adam_sh): 24 B per SH element plus the colour cotangent and
+    position read (24 B per slot)."""
     import torch
 
     from jaxgs_b200.optimizer import (PARAMETER_NAMES, create_adam_state,
-                                      parameter_learning_rates, update_field)
+                                      parameter_learning_rates, update_field,
+                                      update_sh_from_colors)
 
     state = create_adam_state(pool)
     rates = torch.tensor(parameter_learning_rates(100, 1.0), dtype=torch.float32,
@@ -427,6 +453,11 @@ def _time_optimizer(pool, out, stream, iters: int = 20) -> dict:
 
     def update():
         for i, name in enumerate(PARAMETER_NAMES):
+            if name == "sh" and center is not None:
+                update_sh_from_colors(pool.sh, state.m[i], state.v[i], pool.xyz, center,
+                                      out.gradients[i], pool.alive, out.visible_clusters,
+                                      rates[i:i + 1], 128, 3, True)
+                continue
             update_field(getattr(pool, name), state.m[i], state.v[i], out.gradients[i],
                          pool.alive, out.visible_clusters, rates[i:i + 1], 128, name == "sh",
                          True)
@@ -446,37 +477,165 @@ def _time_optimizer(pool, out, stream, iters: int = 20) -> dict:
     slots = (ids[:, None] * 128 + torch.arange(128, device=ids.device)).reshape(-1)
     slots = slots[slots < pool.alive.shape[0]]
     alive = int(pool.alive[slots].to(torch.int64).sum().item())
-    elements = alive * sum(getattr(pool, n)[0].numel() for n in PARAMETER_NAMES)
-    nbytes = elements * 28
-    return {"kernel": "sparse Adam, 5 fields (gsb_sparse_adam)", "ms": round(ms, 4),
-            "slots": alive, "bytes": nbytes, "achieved_gbs": round(nbytes / ms / 1e6, 1),
-            "unit": "GB/s"}
+    other = sum(getattr(pool, n)[0].numel() for n in PARAMETER_NAMES[:4])
+    sh = pool.sh[0].numel()
+    if center is None:
+        nbytes = alive * (other + sh) * 28
+        what = "sparse Adam, 5 fields (gsb_sparse_adam)"
+    else:
+        nbytes = alive * (other * 28 + sh * 24 + 24)
+        what = ("sparse Adam, 4 fields (gsb_sparse_adam) + SH rebuilt from the colour "
+                "cotangent inside its update (gsb_sparse_adam_sh)")
+    return {"kernel": what, "ms": round(ms, 4), "slots": alive, "bytes": nbytes,
+            "achieved_gbs": round(nbytes / ms / 1e6, 1), "unit": "GB/s"}
 
 
-def _roofline(stage_ms, peak, peak_kind, pairs, binned):
+def _time_config4(stream, steps: int = 24, warmup: int = 3) -> dict:
+    """BASELINE config 4 on one GPU: the heavy-tailed 6M-Gaussian scene, its
+    eight 1600x1067 ring cameras (radius 8, fx = fy = 1350), synthetic uint8
+    targets, 8x16 tiles, the pair arena sized from the count pass over the
+    eight views.  Each step is one view's whole training step, the graph
+    replayed with the next camera and target copied in from the device;
+    CUDA events around `steps` replays."""
+    import numpy as np
+    import torch
+
+    from jaxgs_b200.scene import CapacityConfig, config4_scene, ring_cameras, world_cluster_bounds
+    from jaxgs_b200.step import GraphedTrainingStep, required_pairs, size_pair_arena
+    from jaxgs_b200.types import DeviceCamera, GaussianArrays
+
+    pool_np = config4_scene()
+    n = pool_np["xyz"].shape[0]
+    device = torch.device("cuda", torch.cuda.current_device())
+    pool = GaussianArrays.from_numpy(pool_np, device=device)
+    center, extent, valid = world_cluster_bounds(pool_np, 128)
+    del pool_np
+    bounds = (torch.as_tensor(center, device=device), torch.as_tensor(extent, device=device),
+              torch.as_tensor(valid.astype(np.uint8), device=device))
+    cams = [DeviceCamera.from_camera(c, device=device) for c in
+            ring_cameras(8, radius=8.0, height=1.5, width=1600, height_px=1067, focal=1350.0)]
+    rng = np.random.default_rng(8)
+    targets = [torch.as_tensor(rng.integers(0, 256, (1067, 1600, 3), dtype=np.uint8),
+                               device=device) for _ in cams]
+    default = CapacityConfig(n, 128, 16, 16, 3, 8_000_000, tile_height=8)
+    pairs = [required_pairs(pool, bounds, c, default, 3) for c in cams]
+    config = size_pair_arena(pool, bounds, cams, default, 3)
+    graphed = GraphedTrainingStep(pool, bounds, cams[0], targets[0], config, 3)
+    for i in range(warmup):
+        graphed(cams[i % 8], targets[i % 8])
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for i in range(steps):
+        out = graphed(cams[i % 8], targets[i % 8])
+    b.record(stream)
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / steps
+    return {"workload": "BASELINE config 4: 6M-Gaussian heavy-tailed scene, 1600x1067, 8 ring "
+                        "cameras cycled, one view per step, 8x16 tiles, SH3",
+            "views_per_s": round(1e3 / ms, 1), "ms_per_view": round(ms, 4),
+            "pairs_per_view": {"min": min(pairs), "max": max(pairs),
+                               "mean": int(sum(pairs) / len(pairs))},
+            "arena": config.max_visibility_pairs, "reference_default_arena": 8_000_000,
+            "overflow": bool(out.overflow.item())}
+
+
+# DRAM traffic of one raster_bwd_kernel launch on this workload
+# (dram__bytes_read.sum + dram__bytes_write.sum, one-kernel ncu capture of
+# `python bench.py --steps 1 --warmup 1 --no-cpu-baseline --no-e2e`,
+# profiles/raster_bwd_config2.md): 87.42 MB read + 4.38 MB written.
+RASTER_BWD_DRAM_BYTES = 91_801_600
+# FP32 work per backward fragment evaluation (one splat at one pixel): the
+# alpha, transmittance, colour and moment arithmetic of the reverse pass.
+BWD_FLOP_PER_FRAGMENT = 35
+SM_COUNT, FP32_LANES_PER_SM = 148, 128
+
+
+def _backward_visits(pool, bounds, camera, config, degree) -> int:
+    """Contributing (splat, warp) visits of the raster backward on the bench
+    view, counted from the forward's contribution words exactly as
+    raster_bwd_kernel walks them: for each warp (8x8 pixels of a tile), the
+    words of the batches up to its last composited pair, the top word masked
+    above that pair.  Each visit evaluates the splat at the warp's 64
+    pixels.  Runs outside every timed region."""
+    from jaxgs_b200 import kernels as K
+
+    clusters, _ = K.compact_visible_clusters(bounds, camera, config, want_slots=False)
+    projected, _ = K.project_with_compact_pullback(pool, camera, config, degree, clusters,
+                                                   rgb_only=True, visible_color_only=True)
+    table = K.build_sorted_visibility_table_cute(projected, camera, config)
+    _, cache = K.rasterize_forward(projected, table, camera, config, want_depth=False,
+                                   want_alpha=False, clamp_rgb=True)
+    return count_visits(cache.last, table.tile_offsets, cache.contribution_bits, camera.width,
+                        camera.height, config.tile_size, config.raster_tile_height)
+
+
+def count_visits(last, tile_offsets, bits, W: int, H: int, tw: int, th: int) -> int:
+    """Set contribution bits that raster_bwd_kernel visits, from the
+    per-pixel last pair (last), the tile offsets and the contribution words
+    (torch tensors on any device)."""
+    import torch
+
+    rows = 2 if th % 8 == 0 else 1
+    blocks_x, block_h = tw // 8, 4 * rows
+    warps = blocks_x * (th // block_h)
+    tiles_x = -(-W // tw)
+    dev = last.device
+    y = torch.arange(H, device=dev)[:, None].expand(H, W).reshape(-1)
+    x = torch.arange(W, device=dev)[None, :].expand(H, W).reshape(-1)
+    tile = (y // th) * tiles_x + x // tw
+    warp = (x % tw) // 8 + ((y % th) // block_h) * blocks_x
+    offsets = tile_offsets.long()
+    T = offsets.numel() - 1
+    start = offsets[:-1].repeat_interleave(warps)
+    top = start.clone().scatter_reduce_(0, tile * warps + warp, last.long(), "amax")
+    n_batches = torch.where(top > start, ((top - 1 - start) >> 5) + 1, torch.zeros_like(top))
+    owner = torch.arange(T * warps, device=dev).repeat_interleave(n_batches)
+    first = torch.cumsum(n_batches, 0) - n_batches
+    batch = torch.arange(owner.numel(), device=dev) - first[owner]
+    t_idx, w_idx = owner // warps, owner % warps
+    word_at = ((start[owner] >> 5) + t_idx + batch) * warps + w_idx
+    words = bits.long()[word_at] & 0xFFFFFFFF
+    is_top = batch == n_batches[owner] - 1
+    k_max = (top[owner] - 1 - start[owner]) & 31
+    words = torch.where(is_top, words & ((2 << k_max) - 1), words)
+    bytes_ = torch.stack([(words >> s) & 255 for s in (0, 8, 16, 24)])
+    table8 = torch.tensor([bin(i).count("1") for i in range(256)], device=dev)
+    return int(table8[bytes_].sum().item())
+
+
+def _roofline(stage_ms, peak, peak_kind, pairs, binned, visits, sm_mhz, atomics_per_visit):
     """Roofline of the dominant kernel, the fp32 raster backward.
 
-    Algorithmic bytes per launch (the minimum traffic the pass needs): per
-    pixel final T, last index and dL/drgb (20 B); per pair of the table its
-    id and 48-byte splat record (52 B); per binned Gaussian the ten f32
-    cotangents it accumulates (40 B, read + write via L2 atomics counted
-    once).  The kernel is issue-bound (SIMT), not HBM-bound: the fraction
-    says how far it is from the copy roofline, the `simt` entry gives the
-    issue-slot figures from the committed profile.
+    The kernel is bound by SIMT issue, so the roofline is fragment
+    evaluations per second against the FP32 SIMT ceiling: 148 SMs x 128 FP32
+    lanes x the SM clock sampled during the timed region, divided by the
+    35 flop a fragment costs (packed f32x2 instructions can take it past
+    1.0).  A fragment is one splat at one pixel of a contributing
+    (splat, warp) visit (64 pixels).  The bytes are reported beside it:
+    per pixel final T, last index and dL/drgb (20 B); per pair of the table
+    its id and 48-byte splat record (52 B); per binned Gaussian the ten f32
+    cotangents it accumulates (40 B); traffic is the DRAM figure of the
+    committed one-kernel capture.
     """
     ms = stage_ms.get("raster_bwd")
-    if not ms:
+    if not ms or not visits:
         return None
-    pixels = 1237 * 822
-    algo = pixels * 20 + pairs * 52 + binned * 40
-    achieved = algo / (ms * 1e-3) / 1e9
-    traffic = _profile_value("raster_bwd_config2", "dram_bytes_per_launch")
-    return {"kernel": "raster_bwd (zero + order + main kernel, one call)", "bound": "hbm",
-            "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-            "frac": round(achieved / peak, 4), "traffic": traffic,
-            "algorithmic_bytes": int(algo), "peak_source": peak_kind,
-            "simt": {"issue_active_pct": _profile_value("raster_bwd_config2", "issue_active_pct"),
-                     "fp32_pipe_pct": _profile_value("raster_bwd_config2", "fma_pipe_pct")}}
+    seconds = ms * 1e-3
+    fragments = visits * 64
+    achieved = fragments / seconds / 1e9
+    ceiling = SM_COUNT * FP32_LANES_PER_SM * sm_mhz * 1e6 / BWD_FLOP_PER_FRAGMENT / 1e9
+    algo = 1237 * 822 * 20 + pairs * 52 + binned * 40
+    gbs = algo / seconds / 1e9
+    return {"kernel": "raster_bwd (zero + order + main kernel, one call)", "bound": "simt",
+            "achieved": round(achieved, 1), "peak": round(ceiling, 1), "unit": "Gfragment/s",
+            "frac": round(achieved / ceiling, 4), "traffic": RASTER_BWD_DRAM_BYTES,
+            "fragments": fragments, "visits": visits,
+            "atomics_per_s": round(visits * atomics_per_visit / seconds / 1e9, 2),
+            "peak_source": f"FP32 SIMT: {SM_COUNT} SMs x {FP32_LANES_PER_SM} lanes x "
+                           f"{sm_mhz:.0f} MHz / {BWD_FLOP_PER_FRAGMENT} flop per fragment",
+            "bytes": {"algorithmic": int(algo), "achieved_gbs": round(gbs, 1), "peak_gbs": peak,
+                      "frac": round(gbs / peak, 4), "peak_source": peak_kind}}
 
 
 def cpu_baseline(pool_np, camera, target, budget_s: float = 30.0) -> dict:
@@ -548,6 +707,8 @@ def main() -> None:
                         help="skip the oracle timing (profiling runs)")
     parser.add_argument("--no-e2e", action="store_true",
                         help="skip the host-buffer end-to-end loop (profiling runs)")
+    parser.add_argument("--no-config4", action="store_true",
+                        help="skip the config-4 (6M Gaussians, 1600x1067) throughput figure")
     args = parser.parse_args()
     if args.warmup < 3:
         args.warmup = 3

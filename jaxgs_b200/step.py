@@ -26,7 +26,7 @@ NCCL (ViewShardedExchange).
 from __future__ import annotations
 
 import math
-from dataclasses import dataclass
+from dataclasses import dataclass, replace
 
 import torch
 
@@ -155,6 +155,35 @@ def compute_training_step(pool: GaussianArrays, bounds, camera: DeviceCamera, ta
     done(ev)
     return StepOutput(loss, grads, clusters, table.pair_count, table.overflow,
                       table.point_counts, result.rgb if keep_image else None, fragment_stats)
+
+
+def required_pairs(pool: GaussianArrays, bounds, camera: DeviceCamera, config: CapacityConfig,
+                   active_degree: int) -> int:
+    """The (tile, Gaussian) pairs one view needs: the binning's pair count,
+    which is not clamped to config.max_visibility_pairs (a view that
+    overflows the arena still reports its total, sorted_binning.py:78 and
+    :116).  Culls, projects and bins the view once; reads the count back
+    to the host."""
+    clusters, _ = K.compact_visible_clusters(bounds, camera, config, want_slots=False)
+    projected, _ = K.project_with_compact_pullback(pool, camera, config, active_degree, clusters,
+                                                   rgb_only=True, visible_color_only=True)
+    table = K.build_sorted_visibility_table_cute(projected, camera, config)
+    return int(table.pair_count.item())
+
+
+def size_pair_arena(pool: GaussianArrays, bounds, cameras, config: CapacityConfig,
+                    active_degree: int, margin: float = 1.25,
+                    granule: int = 1 << 20) -> CapacityConfig:
+    """config with max_visibility_pairs sized from the count pass: the
+    largest required_pairs over `cameras` times `margin`, rounded up to a
+    multiple of `granule` (a fixed default such as the reference's 8M can
+    overflow a dense view; an oversized one costs memory and the sort
+    grids' idle blocks)."""
+    need = max(required_pairs(pool, bounds, cam, config, active_degree) for cam in cameras)
+    pairs = max(granule, -(-int(math.ceil(need * margin)) // granule) * granule)
+    if pairs >= 1 << 31:
+        raise ValueError(f"{need} pairs per view exceed the 2^31 arena limit")
+    return replace(config, max_visibility_pairs=pairs)
 
 
 def render(camera: DeviceCamera, gaussians: GaussianArrays, visible_clusters, active_degree: int,

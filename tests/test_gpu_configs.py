@@ -115,6 +115,55 @@ def test_config3_training_step_matches_oracle():
         assert err < 1e-3, (name, err)
 
 
+@pytest.mark.timeout(1500)
+def test_config4_training_step_with_an_arena_sized_from_the_count_pass():
+    """BASELINE config 4 as a training step: the heavy-tailed 6M-Gaussian
+    scene at 1600x1067 needs more pairs than the reference's default 8M
+    arena (config/default.toml:53).  size_pair_arena sizes the arena from
+    the count pass, and the step then matches the oracle's whole step
+    without overflow (loss 1e-5 relative, gradients 1e-3 relative L2)."""
+    from jaxgs_b200.scene import CapacityConfig, config4_scene, ring_cameras, world_cluster_bounds
+    from jaxgs_b200.step import compute_training_step, required_pairs, size_pair_arena
+    from jaxgs_b200.types import DeviceCamera
+
+    pool = config4_scene()
+    n = pool["xyz"].shape[0]
+    cam = ring_cameras(8, radius=8.0, height=1.5, width=1600, height_px=1067, focal=1350.0)[3]
+    target = np.random.default_rng(7).integers(0, 256, (1067, 1600, 3), dtype=np.uint8)
+    bounds_np = world_cluster_bounds(pool, 128)
+    bounds = (torch.as_tensor(bounds_np[0], device="cuda"),
+              torch.as_tensor(bounds_np[1], device="cuda"),
+              torch.as_tensor(bounds_np[2].astype(np.uint8), device="cuda"))
+    gpu_pool = _pool(pool)
+    dcam = DeviceCamera.from_camera(cam)
+    default = CapacityConfig(n, 128, 16, 16, 3, 8_000_000, tile_height=8)
+    need = required_pairs(gpu_pool, bounds, dcam, default, 3)
+    assert need > 8_000_000
+    config = size_pair_arena(gpu_pool, bounds, [dcam], default, 3)
+    assert need <= config.max_visibility_pairs <= 1.25 * need + (1 << 20)
+    out = compute_training_step(gpu_pool, bounds, dcam, torch.as_tensor(target, device="cuda"),
+                                config, 3)
+    torch.cuda.synchronize()
+    assert not bool(out.overflow.item()) and int(out.pair_count.item()) == need
+    ids = out.visible_clusters[0].cpu().numpy()
+    count = int(out.visible_clusters[1].item())
+    del gpu_pool
+    exp = O.training_step(pool, cam, target, degree=3, sh_dim=16, tile_w=16, tile_h=8,
+                          max_pairs=config.max_visibility_pairs, bounds=bounds_np,
+                          clusters=(ids, count))
+    # The oracle's step projects on the host: its fields differ from the
+    # GPU's by ulps, which can move a pair across an ellipse edge (the
+    # binning of identical fields is bit-exact, tested above at this config).
+    assert abs(exp["table"]["pair_count"] - need) <= 1e-5 * need and not exp["table"]["overflow"]
+    loss = float(out.loss)
+    assert abs(loss - exp["loss"]) <= 1e-5 * abs(exp["loss"]), (loss, exp["loss"])
+    rows = count * 128
+    for name, got, ref in zip(("xyz", "log_scale", "rotation", "opacity", "sh"), out.gradients,
+                              exp["grads"]):
+        err = rel_l2(got.cpu().numpy().reshape(n, -1)[:rows], ref.reshape(n, -1)[:rows])
+        assert err < 1e-3, (name, err)
+
+
 @pytest.mark.timeout(900)
 def test_config2_training_step_matches_oracle_on_every_pixel():
     from jaxgs_b200.scene import (CapacityConfig, config1_camera, config1_scene,
