@@ -251,7 +251,9 @@ def run_ours(args) -> None:
     overflow = bool(out.overflow.item())
     visible_clusters = int(out.visible_clusters[1].item())
     binned = int((out.point_counts > 0).sum().item())
-    visits = _backward_visits(pool, bounds, dcam, config, degree) if rank == 0 else 0
+    # Every rank counts its own view's visits (only rank 0's is reported), so
+    # no rank reaches the exchange's barriers while another is still here.
+    visits = _backward_visits(pool, bounds, dcam, config, degree)
 
     # The product step: captured as CUDA graphs (one per input buffer),
     # replayed per view.  NvlsExchange's launches are captured into the
