@@ -203,10 +203,16 @@ def run_ours(args) -> None:
         if use_nvls:
             # GSB_ALLREDUCE: "auto" (default), "p2p" or "nvls" sum of the geometric gradients.
             exch = NvlsExchange(pool, config, degree,
-                                allreduce=os.environ.get("GSB_ALLREDUCE", "auto"))
+                                allreduce=os.environ.get("GSB_ALLREDUCE", "auto"),
+                                deferred_sh=args.sh == "deferred")
         else:
             exch = ViewShardedExchange(pool, config, degree)
-    sharded = exch.step_kwargs if exch is not None else {}
+    # The reference's default step (optimizer "optax", config/default.toml:54)
+    # defers the SH pullback to the optimizer (training/step.py:55-66): the
+    # pullback gives the masked colour cotangent and the update rebuilds the
+    # SH gradients.  --sh materialized writes all 16 SH gradients instead.
+    deferred_sh = args.sh == "deferred" and not isinstance(exch, ViewShardedExchange)
+    sharded = exch.step_kwargs if exch is not None else {"sh_color_only": deferred_sh}
     stream = torch.cuda.current_stream()
     stage_events = []
     current_center = [dcam.center]
@@ -333,15 +339,42 @@ def run_ours(args) -> None:
     # consumer of the gradients (it updates the pool in place): visible-
     # cluster sparse Adam over the step's compact gradients.
     inference = _time_inference(pool, camera, stream) if world == 1 else None
-    optimizer = _time_optimizer(pool, graphed.out, stream) if world == 1 else None
-    # The reference's default step defers the SH pullback to its optimizer
-    # (training/step.py:55-66): the same view's colour-only gradients feed the
-    # update that rebuilds SH gradients itself.
-    deferred = None
+    # The optimizer timings below update the pool; every measurement starts
+    # from the benchmark's scene.
+    fields = ("xyz", "log_scale", "rotation", "opacity", "sh")
+    snapshot = [getattr(pool, f).clone() for f in fields]
+
+    def restore():
+        for f, saved in zip(fields, snapshot):
+            getattr(pool, f).copy_(saved)
+
+    optimizer = deferred = materialized = None
     if world == 1:
+        # The step with the other SH form (all 16 SH gradients written by the
+        # pullback, or deferred), on the same scene.
+        materialized = _time_step_variant(pool, bounds, dcam, target, config, degree, stream,
+                                          args.steps, sh_color_only=not deferred_sh)
+        # Both forms of the update: rebuilding SH gradients from the colour
+        # cotangent (the reference's default) and reading materialised ones.
         colour_out = compute_training_step(pool, bounds, dcam, target, config, degree,
                                            sh_color_only=True)
         deferred = _time_optimizer(pool, colour_out, stream, center=dcam.center)
+        restore()
+        full_out = compute_training_step(pool, bounds, dcam, target, config, degree)
+        optimizer = _time_optimizer(pool, full_out, stream)
+        restore()
+        del colour_out, full_out
+    # The whole training iteration (step, exchange, optimizer update) on the
+    # same graph, every rank; it trains the scene as it goes.
+    iteration = None
+    if world == 1 or captured:
+        iteration = _time_iteration(graphed, pool, stream, args.steps, world, deferred_sh,
+                                    dcam.center)
+        restore()
+    if iteration is not None and world > 1:
+        iteration["ms_per_step"] = _max_over_ranks(iteration["ms_per_step"], device)
+        iteration["views_per_s"] = round(world * 1e3 / iteration["ms_per_step"], 1)
+    del snapshot
     heavy = _time_config4(stream) if world == 1 and not args.no_config4 else None
     d2h = 4
 
@@ -368,6 +401,10 @@ def run_ours(args) -> None:
                        "l2": "inputs larger than L2 (236 MB pool)",
                        "launch": "CUDA graph replay of the whole step",
                        "parallelism": f"view-sharded dp{world}" if world > 1 else "single view",
+                       "sh_gradients": ("deferred to the optimizer update as in the reference's "
+                                        "default step (masked colour cotangents, SH rebuilt by "
+                                        "gsb_sparse_adam_sh)" if deferred_sh else
+                                        "all 16 coefficients written by the pullback"),
                        "exchange": _exchange_text(exch, config) if exch is not None else None},
             "e2e": {"value": None if args.no_e2e else round(world * args.steps / e2e_elapsed, 2),
                     "unit": UNIT, "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": d2h},
@@ -381,6 +418,9 @@ def run_ours(args) -> None:
                                      clocks.get("sm_mhz") or 1965.0, 9)
         if inference is not None:
             line["inference"] = inference
+        line["iteration"] = iteration
+        if materialized is not None:
+            line["other_sh_form"] = materialized
         for key, entry in (("optimizer", optimizer), ("optimizer_deferred_sh", deferred)):
             if entry is not None:
                 entry["frac"] = round(entry["achieved_gbs"] / peak, 4)
@@ -490,6 +530,95 @@ def _time_optimizer(pool, out, stream, iters: int = 20, center=None) -> dict:
                 "cotangent inside its update (gsb_sparse_adam_sh)")
     return {"kernel": what, "ms": round(ms, 4), "slots": alive, "bytes": nbytes,
             "achieved_gbs": round(nbytes / ms / 1e6, 1), "unit": "GB/s"}
+
+
+def _max_over_ranks(x: float, device) -> float:
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([float(x)], device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return round(float(t), 4)
+
+
+def _time_iteration(graphed, pool, stream, steps: int, world: int, deferred_sh: bool,
+                    center) -> dict:
+    """The whole training iteration: the graph replay (step and, with
+    several ranks, the exchange) followed by the sparse Adam update of every
+    field from its output (deferred SH: rebuilt from the colour cotangent
+    or, view-sharded, from the gathered colour rows of every view).  CUDA
+    events around `steps` iterations after three untimed ones."""
+    import torch
+
+    from jaxgs_b200.optimizer import (PARAMETER_NAMES, create_adam_state,
+                                      parameter_learning_rates, update_field,
+                                      update_sh_from_colors, update_sh_from_rows)
+
+    state = create_adam_state(pool)
+    rates = torch.tensor(parameter_learning_rates(100, 1.0), dtype=torch.float32,
+                         device=pool.xyz.device)
+    n_clusters = -(-pool.xyz.shape[0] // 128)
+    all_clusters = (torch.arange(n_clusters, dtype=torch.int32, device=pool.xyz.device),
+                    torch.tensor([n_clusters], dtype=torch.int32, device=pool.xyz.device))
+
+    def one():
+        out = graphed()
+        if world > 1:
+            grads, clusters, compact = graphed.gradients, all_clusters, False
+        else:
+            grads, clusters, compact = out.gradients, out.visible_clusters, True
+        # SH first: its directions use the positions before the xyz update.
+        i = len(PARAMETER_NAMES) - 1
+        if deferred_sh and world > 1:
+            update_sh_from_rows(pool.sh, state.m[i], state.v[i], pool.xyz, grads[i], pool.alive,
+                                clusters, rates[i:i + 1], 128, 3)
+        elif deferred_sh:
+            update_sh_from_colors(pool.sh, state.m[i], state.v[i], pool.xyz, center, grads[i],
+                                  pool.alive, clusters, rates[i:i + 1], 128, 3, compact)
+        else:
+            update_field(pool.sh, state.m[i], state.v[i], grads[i], pool.alive, clusters,
+                         rates[i:i + 1], 128, True, compact)
+        for i, name in enumerate(PARAMETER_NAMES[:-1]):
+            update_field(getattr(pool, name), state.m[i], state.v[i], grads[i], pool.alive,
+                         clusters, rates[i:i + 1], 128, False, compact)
+
+    for _ in range(3):
+        one()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(steps):
+        one()
+    b.record(stream)
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / steps
+    return {"what": "graph replay of the step (and exchange) + sparse Adam on every field",
+            "ms_per_step": round(ms, 4), "views_per_s": round(world * 1e3 / ms, 1)}
+
+
+def _time_step_variant(pool, bounds, camera, target, config, degree, stream, steps: int,
+                       sh_color_only: bool) -> dict:
+    """The single-view step in the other SH form (graph replays, CUDA
+    events), to show what the choice costs."""
+    import torch
+
+    from jaxgs_b200.step import GraphedTrainingStep
+
+    graphed = GraphedTrainingStep(pool, bounds, camera, target, config, degree,
+                                  sh_color_only=sh_color_only)
+    for _ in range(3):
+        graphed()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(steps):
+        graphed()
+    b.record(stream)
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / steps
+    return {"sh_gradients": "deferred (colour cotangent)" if sh_color_only else
+            "all 16 coefficients written by the pullback",
+            "ms_per_step": round(ms, 4), "views_per_s": round(1e3 / ms, 2)}
 
 
 def _time_config4(stream, steps: int = 24, warmup: int = 3) -> dict:
@@ -709,6 +838,9 @@ def main() -> None:
                         help="skip the oracle timing (profiling runs)")
     parser.add_argument("--no-e2e", action="store_true",
                         help="skip the host-buffer end-to-end loop (profiling runs)")
+    parser.add_argument("--sh", choices=["deferred", "materialized"], default="deferred",
+                        help="SH gradients of the step: the reference's deferred form (default) "
+                             "or all 16 coefficients from the pullback")
     parser.add_argument("--no-config4", action="store_true",
                         help="skip the config-4 (6M Gaussians, 1600x1067) throughput figure")
     args = parser.parse_args()

@@ -206,10 +206,12 @@ extern "C" int gsb_nvls_allreduce(gsb_stream_t stream, const gsb_exchange_params
     const int64_t per = (n4 + p->world - 1) / p->world;
     const int64_t begin = per * p->rank, end = begin + per < n4 ? begin + per : n4;
     if (begin >= end) return GSB_OK;
-    // Four blocks per SM: measured at 2 ranks (44 MB with its barrier) 135 us
-    // against 142 us with eight and 149 us with sixteen.
+    // One block per SM: the 44 MB all-reduce alone measured 124 us at 8 ranks
+    // against 140 us with two to eight blocks per SM (126 against 139 us at
+    // 2 ranks); more requests in flight do not move more bytes through the
+    // switch.
     const int64_t want = (end - begin + 256 * kUnroll - 1) / (256 * kUnroll);
-    const int blocks = (int)(want < 148 * 4 ? want : 148 * 4);
+    const int blocks = (int)(want < 148 ? want : 148);
     gsb::launch(nvls_allreduce_kernel, blocks, 256, 0, as_stream(stream), multicast, begin, end,
                 error);
     return check_launch();
@@ -248,8 +250,10 @@ extern "C" int gsb_p2p_allreduce(gsb_stream_t stream, const gsb_exchange_params*
     const int64_t per = (n4 + p->world - 1) / p->world;
     const int64_t begin = per * p->rank, end = begin + per < n4 ? begin + per : n4;
     if (begin >= end) return GSB_OK;
+    // One block per SM: 79 us at 2 ranks and 143 us at 8 for 44 MB, against
+    // 86 and 157 us with four blocks per SM.
     const int64_t want = (end - begin + 256 * kP2PUnroll - 1) / (256 * kP2PUnroll);
-    const int blocks = (int)(want < 148 * 4 ? want : 148 * 4);
+    const int blocks = (int)(want < 148 ? want : 148);
     gsb::launch(p2p_allreduce_kernel, blocks, 256, 0, as_stream(stream), peers, p->world, begin,
                 end, error);
     return check_launch();

@@ -182,13 +182,58 @@ def update_sh_from_colors(sh: torch.Tensor, mean: torch.Tensor, variance: torch.
     return sh, mean, variance
 
 
+def update_sh_from_rows(sh: torch.Tensor, mean: torch.Tensor, variance: torch.Tensor,
+                        xyz: torch.Tensor, rows: torch.Tensor, alive: torch.Tensor, clusters,
+                        rate, cluster_size: int, degree: int):
+    """update_sh_from_colors for the view-sharded exchange's gathered rows:
+    rows [V, >= 4 + C*3], each a view's camera centre (3 floats and a pad)
+    followed by its masked colour cotangents in pool order
+    (NvlsExchange(deferred_sh=True).exchange() returns them), read in
+    place."""
+    capacity = int(sh.shape[0])
+    if rows.dim() != 2 or rows.shape[1] < 4 + capacity * 3 or not rows.is_contiguous():
+        raise ValueError("colour rows must be [V, >= 4 + C*3] contiguous")
+    if not rows.is_cuda or rows.dtype != torch.float32:
+        raise ValueError("sparse Adam needs float32 CUDA tensors")
+    if sh.dim() != 3 or sh.shape[2] != 3 or sh.shape != mean.shape or sh.shape != variance.shape:
+        raise ValueError("sh and moments must be [C, sh_dim, 3] of one shape")
+    if int(alive.shape[0]) != capacity or tuple(xyz.shape) != (capacity, 3):
+        raise ValueError("xyz and alive must have one row per SH row")
+    sh_dim = int(sh.shape[1])
+    if not 0 <= degree <= 3 or (degree + 1) ** 2 > sh_dim:
+        raise ValueError(f"degree {degree} needs (degree + 1)^2 <= {sh_dim} coefficients")
+    for t in (sh, mean, variance):
+        if not t.is_cuda or t.dtype != torch.float32 or not t.is_contiguous():
+            raise ValueError("sh and moments must be contiguous float32 CUDA tensors")
+    if capacity == 0:
+        return sh, mean, variance
+    ids, count = clusters
+    if not torch.is_tensor(rate):
+        rate = torch.full((1,), float(rate), dtype=torch.float32, device=sh.device)
+    alive8 = alive if alive.dtype == torch.int8 else (
+        alive.view(torch.int8) if alive.dtype == torch.uint8 else alive.to(torch.int8))
+    row = int(rows.shape[1])
+    p = L.AdamShParams(capacity, sh_dim, int(degree), int(cluster_size), int(rows.shape[0]), 0,
+                       row, row)
+    ptr = lambda t: t.data_ptr()
+    L.check(L.lib.gsb_sparse_adam_sh(_stream(), L.ref(p), ptr(sh), ptr(mean), ptr(variance),
+                                     ptr(xyz.contiguous()), ptr(rows), ptr(rows) + 16,
+                                     ptr(alive8.contiguous()),
+                                     ptr(ids.to(torch.int32).contiguous()),
+                                     ptr(count.to(torch.int32).contiguous()),
+                                     ptr(rate.to(torch.float32).contiguous())),
+            "sparse Adam (SH from gathered colour rows)")
+    return sh, mean, variance
+
+
 def sparse_adam_update(pool: GaussianArrays, state: AdamState, gradients, visible: torch.Tensor,
                        step: float, spatial_scale: float, max_steps: int | None = None, *,
                        compacted_clusters, cluster_size: int = 128,
                        compact_gradients: bool = False,
                        optimization: OptimizationConfig = OptimizationConfig(),
                        sh_pullback_center: torch.Tensor | None = None,
-                       active_degree: int | None = None):
+                       active_degree: int | None = None,
+                       sh_pullback_rows: torch.Tensor | None = None):
     """training/optimizer.py:276-341 with compacted clusters: LiteGS Adam on
     every field of the listed clusters' alive slots, in place on the pool and
     the state; state.step counts the update in every slot of `visible` that
@@ -201,7 +246,10 @@ def sparse_adam_update(pool: GaussianArrays, state: AdamState, gradients, visibl
     active_degree defaults to the pool's full degree).  Every field, moment
     and gradient is checked before the first launch, so a rejected call
     leaves the pool and the state untouched (the reference's trace-time
-    checks, tests/test_chex_contracts.py:57-76).  Returns (pool, state)."""
+    checks, tests/test_chex_contracts.py:57-76).  sh_pullback_rows: the
+    view-sharded form, the gathered rows of every view (camera centre, pad,
+    pool-order colour cotangents; NvlsExchange(deferred_sh=True)); the SH
+    gradient argument is then ignored.  Returns (pool, state)."""
     capacity = int(pool.alive.shape[0])
     if tuple(visible.shape) != (capacity,):
         raise ValueError("visible must hold one flag per pool slot")
@@ -214,6 +262,8 @@ def sparse_adam_update(pool: GaussianArrays, state: AdamState, gradients, visibl
             raise ValueError(f"{name} moments must have the field's shape")
         if gradient.dtype != torch.float32:
             raise ValueError(f"{name} gradient must be float32")
+        if name == "sh" and sh_pullback_rows is not None:
+            continue
         if name == "sh" and sh_pullback_center is not None:
             if gradient.numel() != capacity * 3:
                 raise ValueError("with sh_pullback_center the sh gradient is the colour "
@@ -230,6 +280,10 @@ def sparse_adam_update(pool: GaussianArrays, state: AdamState, gradients, visibl
                              "(every SH coefficient)")
     sh_dim = int(pool.sh.shape[1])
     degree = int(round(sh_dim ** 0.5)) - 1 if active_degree is None else int(active_degree)
+    if sh_pullback_rows is not None and sh_pullback_center is not None:
+        raise ValueError("give sh_pullback_center or sh_pullback_rows, not both")
+    if sh_pullback_rows is not None and not (0 <= degree <= 3 and (degree + 1) ** 2 <= sh_dim):
+        raise ValueError(f"active_degree {degree} does not fit {sh_dim} SH coefficients")
     if sh_pullback_center is not None:
         if sh_pullback_center.numel() != 3:
             raise ValueError("sh_pullback_center must be one camera centre (3 floats)")
@@ -239,13 +293,18 @@ def sparse_adam_update(pool: GaussianArrays, state: AdamState, gradients, visibl
     dev = pool.xyz.device
     rate_t = torch.tensor(rates, dtype=torch.float32, device=dev)
     order = list(enumerate(zip(PARAMETER_NAMES, gradients)))
-    if sh_pullback_center is not None:
+    if sh_pullback_center is not None or sh_pullback_rows is not None:
         # The SH directions use the positions before this update (the
         # reference's transform sees the parameters it updates), so the SH
         # field goes first; the fields are otherwise independent.
         order = order[-1:] + order[:-1]
     for i, (name, gradient) in order:
         value = getattr(pool, name)
+        if name == "sh" and sh_pullback_rows is not None:
+            update_sh_from_rows(value, state.m[i], state.v[i], pool.xyz, sh_pullback_rows,
+                                pool.alive, compacted_clusters, rate_t[i:i + 1], cluster_size,
+                                degree)
+            continue
         if name == "sh" and sh_pullback_center is not None:
             update_sh_from_colors(value, state.m[i], state.v[i], pool.xyz,
                                   sh_pullback_center.to(dev, torch.float32), gradient,

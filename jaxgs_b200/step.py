@@ -283,6 +283,17 @@ class NvlsExchange:
     call is made per step and every launch can be captured in a CUDA graph.
     Build it only when NvlsExchange.available(group) says the GPUs share
     multicast.
+
+    deferred_sh: the SH gradients stay in the reference's deferred form
+    (training/step.py:55-66): exchange() gathers every view's colour row
+    and camera centre into the table and returns the rows instead of
+    expanding them, and the optimizer rebuilds the SH gradients
+    (sparse_adam_update(..., sh_pullback_rows=rows)).  The table is then
+    cleared by begin_step() (call it before the step's work, after the
+    previous rows' consumer) or at the start of exchange(), before the
+    first barrier, so that no peer pushes into it before this rank has
+    consumed the previous rows; the push runs beside the geometric
+    all-reduce, after that barrier.
     """
 
     @staticmethod
@@ -298,7 +309,8 @@ class NvlsExchange:
             return False
 
     def __init__(self, pool: GaussianArrays, config: CapacityConfig, active_degree: int,
-                 group=None, active_sh_only: bool = True, allreduce: str = "auto"):
+                 group=None, active_sh_only: bool = True, allreduce: str = "auto",
+                 deferred_sh: bool = False):
         import ctypes
 
         import torch.distributed as dist
@@ -353,12 +365,19 @@ class NvlsExchange:
         for n, shape in ((C * 3, (C, 3)), (C * 3, (C, 3)), (C * 4, (C, 4)), (C, (C, 1))):
             views.append(self.geometric[at:at + n].view(shape))
             at += n
-        # The pullback's colour-only output [C, 1, 3] is this rank's row.
-        self.own_row = self.rows[self.rank]
+        # The pullback's colour-only output [C, 1, 3] is this rank's row: row
+        # r of the table itself, or (deferred, where the table is cleared
+        # while the step runs) a local row that the push copies into it.
+        self.deferred_sh = bool(deferred_sh)
+        if self.deferred_sh:
+            self.own_row = torch.zeros(self.row_floats, dtype=torch.float32, device=dev)
+        else:
+            self.own_row = self.rows[self.rank]
         colours = self.own_row[4:4 + C * 3].view(C, 1, 3)
         self.pool_grads = (*views, colours)
         self.step_kwargs = dict(pool_grads=self.pool_grads, sh_color_only=True)
         self.side = torch.cuda.Stream(device=dev)
+        self._cleared = False
         torch.cuda.synchronize(dev)
         dist.barrier(group)
 
@@ -372,11 +391,60 @@ class NvlsExchange:
             ctypes.c_void_p(self.epoch.data_ptr()), ctypes.c_void_p(self.error.data_ptr())),
             "exchange barrier")
 
+    def begin_step(self) -> None:
+        """Deferred mode: clear the colour table on the side stream, after
+        everything queued so far on the current stream (the consumer of the
+        previous rows); exchange() waits for it before its first barrier.
+        Lets the clearing overlap the step's work; optional."""
+        if not self.deferred_sh:
+            return
+        self.side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(self.side):
+            self.table.zero_()
+        self._cleared = True
+
+    def _allreduce(self, stream, err) -> None:
+        import ctypes
+
+        L = self.L
+        if self.allreduce == "p2p":
+            L.check(L.lib.gsb_p2p_allreduce(ctypes.c_void_p(stream.cuda_stream), L.ref(self.params),
+                                            self.geo_peers, self.geo_count, err), "P2P all-reduce")
+        else:
+            L.check(L.lib.gsb_nvls_allreduce(ctypes.c_void_p(stream.cuda_stream),
+                                             L.ref(self.params), ctypes.c_void_p(self.mc_geo),
+                                             self.geo_count, err), "NVLS all-reduce")
+
+    def _exchange_deferred(self, main, err):
+        """Clear (unless begin_step did) -> barrier -> colour push beside the
+        geometric all-reduce -> barrier; returns the gathered rows."""
+        import ctypes
+
+        L = self.L
+        if not self._cleared:
+            self.begin_step()
+        self._cleared = False
+        main.wait_stream(self.side)
+        self._barrier()
+        self.side.wait_stream(main)
+        with torch.cuda.stream(self.side):
+            L.check(L.lib.gsb_multicast_nonzero(ctypes.c_void_p(self.side.cuda_stream),
+                                                ctypes.c_void_p(self.own_row.data_ptr()),
+                                                ctypes.c_void_p(self.mc_row), self.row_floats,
+                                                err), "colour row all-gather")
+        self._allreduce(main, err)
+        main.wait_stream(self.side)
+        self._barrier()
+        return (*self.pool_grads[:4], self.rows)
+
     def exchange(self, camera_center: torch.Tensor | None = None):
         """Sum the ranks' gradients after a step run with step_kwargs;
         returns (xyz, log_scale, rotation, opacity, sh) in pool order,
-        identical on every rank.  camera_center: this rank's camera centre
-        [3] on the device (it travels with the colour row)."""
+        identical on every rank -- with deferred_sh the last item is the
+        gathered colour rows [world, row_floats] (each: camera centre, pad,
+        C*3 masked colour cotangents) instead of SH gradients.
+        camera_center: this rank's camera centre [3] on the device (it
+        travels with the colour row)."""
         import ctypes
 
         L = self.L
@@ -385,19 +453,15 @@ class NvlsExchange:
             raise ValueError("NvlsExchange.exchange needs this rank's camera centre")
         self.own_row[:3].copy_(camera_center.reshape(3))
         err = ctypes.c_void_p(self.error.data_ptr())
+        if self.deferred_sh:
+            return self._exchange_deferred(main, err)
         L.check(L.lib.gsb_multicast_nonzero(ctypes.c_void_p(main.cuda_stream),
                                             ctypes.c_void_p(self.own_row.data_ptr()),
                                             ctypes.c_void_p(self.mc_row), self.row_floats, err),
                 "colour row all-gather")
         self._barrier()
         self.side.wait_stream(main)
-        if self.allreduce == "p2p":
-            L.check(L.lib.gsb_p2p_allreduce(ctypes.c_void_p(main.cuda_stream), L.ref(self.params),
-                                            self.geo_peers, self.geo_count, err), "P2P all-reduce")
-        else:
-            L.check(L.lib.gsb_nvls_allreduce(ctypes.c_void_p(main.cuda_stream),
-                                             L.ref(self.params), ctypes.c_void_p(self.mc_geo),
-                                             self.geo_count, err), "NVLS all-reduce")
+        self._allreduce(main, err)
         with torch.cuda.stream(self.side):
             K.sh_from_colors(self.xyz, None, self.rows, self.degree, self.sh_dim, out=self.sh)
             # The all-gather skips all-zero chunks, so the table must be zero
@@ -489,9 +553,10 @@ class GraphedTrainingStep:
     for asynchronous copies); a call with neither replays the last inputs.
     With pool_grads the gradients land there in pool order on every replay.
     exchange: an NvlsExchange built for this step (its step_kwargs passed
-    here too); its exchange() is captured after the step, so each replay
-    also sums the ranks' gradients with no host launch (every rank must
-    replay in step).  The sums are self.gradients.
+    here too); its exchange() is captured after the step (and, deferred,
+    its begin_step() before it), so each replay also sums the ranks'
+    gradients with no host launch (every rank must replay in step).  The
+    sums are self.gradients.
     """
 
     BUFFERS = 2
@@ -518,8 +583,11 @@ class GraphedTrainingStep:
         side = torch.cuda.Stream(device=dev)
         side.wait_stream(torch.cuda.current_stream(dev))
         self.exchange = exchange
+        begin = getattr(exchange, "begin_step", None)
         with torch.cuda.stream(side):
             for _ in range(max(warmup, 1)):
+                if begin is not None:
+                    begin()
                 compute_training_step(pool, bounds, self.cameras[0], self.targets[0], config,
                                       active_degree, **kwargs)
                 if exchange is not None:
@@ -538,6 +606,8 @@ class GraphedTrainingStep:
         for b in range(self.BUFFERS):
             graph = torch.cuda.CUDAGraph()
             with torch.cuda.graph(graph, pool=mempool):
+                if begin is not None:
+                    begin()
                 out = compute_training_step(pool, bounds, self.cameras[b], self.targets[b],
                                             config, active_degree, **kwargs)
                 sums = exchange.exchange(self.cameras[b].center) if exchange is not None else None

@@ -1,7 +1,9 @@
 """View-sharded step on two GPUs (one rank per GPU): the gradients that the
 exchange (ViewShardedExchange over NCCL, or NvlsExchange with this library's
-collectives, its all-reduce in the switch or by peer loads and stores) leaves on every rank equal the single-process
-sum of the two views' full gradients, over several steps in a row.  Skipped
+collectives, its all-reduce in the switch or by peer loads and stores, with
+the SH gradients expanded in the exchange or deferred to the optimizer as
+gathered colour rows) leaves on every rank equal the single-process sum of
+the two views' full gradients, over several steps in a row.  Skipped
 with fewer than two GPUs (NvlsExchange also without multicast support)."""
 
 import os
@@ -51,8 +53,10 @@ def _rank(rank, world, port, path, kind):
             if rank == 0:
                 np.savez(path, skipped=np.ones(1))
             return
+        deferred = kind.endswith("-deferred")
         if nvls:
-            exch = NvlsExchange(pool, config, 3, allreduce=kind)
+            exch = NvlsExchange(pool, config, 3, allreduce=kind.split("-")[0],
+                                deferred_sh=deferred)
         else:
             exch = ViewShardedExchange(pool, config, 3)
         # NvlsExchange: the exchange is captured into the step's graph.
@@ -64,6 +68,24 @@ def _rank(rank, world, port, path, kind):
         torch.cuda.synchronize()
         if nvls:
             assert not exch.failed()
+        if deferred:
+            from jaxgs_b200 import kernels as K
+            from jaxgs_b200.optimizer import update_field, update_sh_from_rows
+
+            rows = grads[4]
+            sh = K.sh_from_colors(pool.xyz, None, rows, 3, 16)
+            # The optimizer's own expansion of the rows equals expanding
+            # them first and updating with the result, bit for bit.
+            n_clusters = -(-pool.xyz.shape[0] // 128)
+            clusters = (torch.arange(n_clusters, dtype=torch.int32, device=device),
+                        torch.tensor([n_clusters], dtype=torch.int32, device=device))
+            fused = [pool.sh.clone(), torch.full_like(pool.sh, 0.01), torch.full_like(pool.sh, 1e-3)]
+            plain = [t.clone() for t in fused]
+            update_sh_from_rows(*fused, pool.xyz, rows, pool.alive, clusters, 0.001, 128, 3)
+            update_field(*plain, sh, pool.alive, clusters, 0.001, 128, True, False)
+            torch.cuda.synchronize()
+            assert all(torch.equal(a, b) for a, b in zip(fused, plain))
+            grads = (*grads[:4], sh)
         if rank == 0:
             np.savez(path, *[g.cpu().numpy() for g in grads])
         dist.barrier()
@@ -73,7 +95,7 @@ def _rank(rank, world, port, path, kind):
 
 
 @pytest.mark.timeout(600)
-@pytest.mark.parametrize("kind", ["nccl", "nvls", "p2p"])
+@pytest.mark.parametrize("kind", ["nccl", "nvls", "p2p", "nvls-deferred", "p2p-deferred"])
 def test_two_rank_view_sharded_gradients(kind):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
