@@ -204,7 +204,8 @@ def run_ours(args) -> None:
             # GSB_ALLREDUCE: "auto" (default), "p2p" or "nvls" sum of the geometric gradients.
             exch = NvlsExchange(pool, config, degree,
                                 allreduce=os.environ.get("GSB_ALLREDUCE", "auto"),
-                                deferred_sh=args.sh == "deferred")
+                                deferred_sh=args.sh == "deferred",
+                                colour_push=os.environ.get("GSB_COLOUR_PUSH", "compact"))
         else:
             exch = ViewShardedExchange(pool, config, degree)
     # The reference's default step (optimizer "optax", config/default.toml:54)
@@ -442,6 +443,14 @@ def _exchange_text(exch, config) -> str:
 
     geo = exch.geometric.numel() * 4 / 1e6
     colours = config.max_gaussians * 12 / 1e6
+    if isinstance(exch, NvlsExchange) and exch.deferred_sh:
+        form = ("compact (id, rgb) entries of the Gaussians with a non-zero colour cotangent"
+                if exch.compact_push else
+                f"the non-zero 16-byte chunks of {colours:.0f} MB colour cotangents")
+        return (f"per step, own kernels in the step's CUDA graph: {exch.allreduce.upper()} "
+                f"all-reduce of {geo:.0f} MB geometric gradients beside the NVLS multicast "
+                f"all-gather of every rank's colour row as {form}, scattered into dense rows; "
+                "SH gradients rebuilt by the optimizer update")
     if isinstance(exch, NvlsExchange):
         return (f"per step, own kernels in the step's CUDA graph: {exch.allreduce.upper()} "
                 f"all-reduce of {geo:.0f} MB geometric gradients, NVLS multicast all-gather of "

@@ -47,7 +47,7 @@ enum {
     GSB_ERR_NULL = 4        /* required pointer is NULL */
 };
 
-#define GSB_ABI_VERSION 9
+#define GSB_ABI_VERSION 10
 
 /* Library utilities.  No counterpart in the reference, whose boundary
  * (cutlass.jax.cutlass_call) reports errors by raising in Python before
@@ -503,6 +503,24 @@ GSB_API int gsb_multicast_nonzero(gsb_stream_t stream, const float* src, float* 
                           int64_t count, const int32_t* error);
 GSB_API int gsb_p2p_allreduce(gsb_stream_t stream, const gsb_exchange_params* p,
                       float* const* buffers, int64_t count, const int32_t* error);
+
+/* The colour all-gather in compact form (no reference counterpart; part of
+ * the view-sharded exchange).  gsb_colour_push_compact appends an entry
+ * (id as int bits, r, g, b) for every Gaussian whose colour cotangent in
+ * row[4 + 3g .. 4 + 3g + 2] is non-zero to this rank's compact row through
+ * its multicast address, then the header (row[0..2], the camera centre, and
+ * the entry count as int bits); a compact row holds 4 + 4 * capacity floats
+ * and the entry order is unspecified.  counter: one device int32 of
+ * scratch, set to zero by the call.  gsb_colour_expand scatters every
+ * view's entries of a gathered compact table [world][4 + 4 * capacity]
+ * into dense rows [world][dense_row] (centre, pad, capacity * 3 colours),
+ * which the caller clears beforehand.  Both return at once when the
+ * exchange's error word is set. */
+GSB_API int gsb_colour_push_compact(gsb_stream_t stream, const float* row, int64_t capacity,
+                            float* multicast, int32_t* counter, const int32_t* error);
+GSB_API int gsb_colour_expand(gsb_stream_t stream, const float* table, int world,
+                      int64_t capacity, float* dense, int64_t dense_row,
+                      const int32_t* error);
 
 #ifdef __cplusplus
 }

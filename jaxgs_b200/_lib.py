@@ -100,6 +100,7 @@ SYMBOLS = (
     "gsb_raster_pack", "gsb_raster_bwd_prepare",
     "gsb_loss_workspace_size", "gsb_loss", "gsb_loss_noalloc",
     "gsb_exchange_barrier", "gsb_nvls_allreduce", "gsb_multicast_nonzero", "gsb_p2p_allreduce",
+    "gsb_colour_push_compact", "gsb_colour_expand",
     "gsb_sparse_adam", "gsb_sparse_adam_sh", "gsb_densify_scores", "gsb_decay_opacity",
 )
 
@@ -152,6 +153,10 @@ def _load():
     lib.gsb_multicast_nonzero.argtypes = [vp, vp, vp, ctypes.c_int64, vp]
     lib.gsb_p2p_allreduce.restype = ctypes.c_int
     lib.gsb_p2p_allreduce.argtypes = [vp, vp, vp, ctypes.c_int64, vp]
+    lib.gsb_colour_push_compact.restype = ctypes.c_int
+    lib.gsb_colour_push_compact.argtypes = [vp, vp, ctypes.c_int64, vp, vp, vp]
+    lib.gsb_colour_expand.restype = ctypes.c_int
+    lib.gsb_colour_expand.argtypes = [vp, vp, ctypes.c_int, ctypes.c_int64, vp, ctypes.c_int64, vp]
     lib.gsb_sparse_adam.restype = ctypes.c_int
     lib.gsb_sparse_adam.argtypes = [vp, vp] + [vp] * 8
     lib.gsb_sparse_adam_sh.restype = ctypes.c_int
@@ -166,7 +171,7 @@ def _load():
 
 
 lib = _load()
-if lib.gsb_abi_version() != 9:
+if lib.gsb_abi_version() != 10:
     raise RuntimeError("libgsb200.so ABI version mismatch; rebuild with `python -m jaxgs_b200.build`")
 
 

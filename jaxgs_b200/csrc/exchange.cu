@@ -22,6 +22,13 @@
 //     moves (world - 1) / world of the buffer in each direction, about what
 //     the switch-reduced form moves, with ordinary loads that keep many
 //     requests in flight.
+//   * gsb_colour_push_compact / gsb_colour_expand: the colour all-gather in
+//     compact form.  Each rank appends (id, r, g, b) for every Gaussian with
+//     a non-zero colour cotangent to its compact row through the multicast
+//     address, a warp's entries at consecutive addresses (one atomic per
+//     warp), so the switch carries whole lines instead of the scattered
+//     16-byte chunks of gsb_multicast_nonzero; after the next barrier every
+//     rank scatters each view's entries into its local dense rows.
 // Callers put a barrier between a producer and these collectives and after
 // them (the sum is complete on every GPU only once every shard is stored).
 // No TMA and no cluster-multicast loads are used: peers' memory is touched
@@ -126,6 +133,79 @@ __global__ void multicast_nonzero_kernel(const float4* __restrict__ src, float* 
     // block, cumulative over the block's stores through the block barrier.
     __syncthreads();
     if (threadIdx.x == 0) __threadfence_system();
+}
+
+// Compact row layout: [centre x, y, z, entry count (int bits) | entries of
+// (id (int bits), r, g, b)], 4 + 4 * capacity floats.  The count is
+// written by compact_header_kernel after every entry is stored.
+__global__ void compact_push_kernel(const float* __restrict__ row, int64_t capacity, float* mc,
+                                    int32_t* counter, const int32_t* error)
+{
+    pdl_begin();
+    if (error && *reinterpret_cast<const volatile int32_t*>(error)) return;
+    const int lane = threadIdx.x & 31;
+    const float* colours = row + 4;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    // Every lane of a warp runs the same number of iterations (the bound is
+    // rounded up to whole warps), so the ballots see full warps.
+    const int64_t bound = (capacity + 31) & ~int64_t(31);
+    for (int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; g < bound; g += stride) {
+        float r = 0.0f, gg = 0.0f, b = 0.0f;
+        if (g < capacity) {
+            r = __ldg(colours + g * 3);
+            gg = __ldg(colours + g * 3 + 1);
+            b = __ldg(colours + g * 3 + 2);
+        }
+        const bool live = r != 0.0f || gg != 0.0f || b != 0.0f;
+        const unsigned mask = __ballot_sync(GSB_FULL_MASK, live);
+        if (mask == 0) continue;
+        int base = 0;
+        if (lane == 0) base = atomicAdd(counter, __popc(mask));
+        base = __shfl_sync(GSB_FULL_MASK, base, 0);
+        if (live) {
+            const int at = base + __popc(mask & lanemask_lt());
+            multimem_st_v4(mc + 4 + (int64_t)at * 4,
+                           make_float4(__int_as_float((int)g), r, gg, b));
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) __threadfence_system();
+}
+
+// One thread: the row's header (centre and entry count) after the entries.
+__global__ void compact_header_kernel(const float* __restrict__ row, float* mc,
+                                      const int32_t* counter, const int32_t* error)
+{
+    pdl_begin();
+    if (error && *reinterpret_cast<const volatile int32_t*>(error)) return;
+    multimem_st_v4(mc, make_float4(row[0], row[1], row[2], __int_as_float(*counter)));
+    __threadfence_system();
+}
+
+// grid.y: view; each view's entries scattered into its dense row [centre,
+// pad, capacity * 3 colours] (cleared beforehand), the centre copied.
+__global__ void compact_expand_kernel(const float* __restrict__ table, int64_t capacity,
+                                      int64_t compact_row, float* dense, int64_t dense_row,
+                                      const int32_t* error)
+{
+    pdl_begin();
+    if (error && *reinterpret_cast<const volatile int32_t*>(error)) return;
+    const int v = blockIdx.y;
+    const float* src = table + (int64_t)v * compact_row;
+    float* dst = dense + (int64_t)v * dense_row;
+    const int64_t n = __float_as_int(__ldg(src + 3));
+    const int64_t count = n < 0 ? 0 : (n > capacity ? capacity : n);
+    if (blockIdx.x == 0 && threadIdx.x < 3) dst[threadIdx.x] = __ldg(src + threadIdx.x);
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < count; i += stride) {
+        const float4 e = __ldg(reinterpret_cast<const float4*>(src + 4) + i);
+        const int64_t g = __float_as_int(e.x);
+        if (g < 0 || g >= capacity) continue;
+        float* c = dst + 4 + g * 3;
+        c[0] = e.y;
+        c[1] = e.z;
+        c[2] = e.w;
+    }
 }
 
 constexpr int kMaxPeers = 8;
@@ -256,5 +336,39 @@ extern "C" int gsb_p2p_allreduce(gsb_stream_t stream, const gsb_exchange_params*
     const int blocks = (int)(want < 148 ? want : 148);
     gsb::launch(p2p_allreduce_kernel, blocks, 256, 0, as_stream(stream), peers, p->world, begin,
                 end, error);
+    return check_launch();
+}
+
+extern "C" int gsb_colour_push_compact(gsb_stream_t stream, const float* row, int64_t capacity,
+                                       float* multicast, int32_t* counter, const int32_t* error)
+{
+    if (capacity < 0 || capacity >= ((int64_t)1 << 31)) return GSB_ERR_INVALID;
+    if (!row || !multicast || !counter) return GSB_ERR_NULL;
+    if (!aligned16(row) || !aligned16(multicast)) return GSB_ERR_INVALID;
+    cudaStream_t s = as_stream(stream);
+    if (cudaMemsetAsync(counter, 0, sizeof(int32_t), s) != cudaSuccess) return check_launch();
+    if (capacity > 0) {
+        const int64_t want = (capacity + 255) / 256;
+        const int blocks = (int)(want < 148 * 4 ? want : 148 * 4);
+        gsb::launch(compact_push_kernel, blocks, 256, 0, s, row, capacity, multicast, counter,
+                    error);
+    }
+    gsb::launch(compact_header_kernel, 1, 1, 0, s, row, multicast,
+                static_cast<const int32_t*>(counter), error);
+    return check_launch();
+}
+
+extern "C" int gsb_colour_expand(gsb_stream_t stream, const float* table, int world,
+                                 int64_t capacity, float* dense, int64_t dense_row,
+                                 const int32_t* error)
+{
+    if (world < 1 || world > 65535 || capacity < 0 || capacity >= ((int64_t)1 << 31) ||
+        dense_row < 4 + capacity * 3)
+        return GSB_ERR_INVALID;
+    if (!table || !dense) return GSB_ERR_NULL;
+    if (!aligned16(table)) return GSB_ERR_INVALID;
+    const int64_t compact_row = 4 + 4 * capacity;
+    gsb::launch(compact_expand_kernel, dim3(148, world), 256, 0, as_stream(stream), table,
+                capacity, compact_row, dense, dense_row, error);
     return check_launch();
 }

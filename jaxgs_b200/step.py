@@ -293,7 +293,12 @@ class NvlsExchange:
     previous rows' consumer) or at the start of exchange(), before the
     first barrier, so that no peer pushes into it before this rank has
     consumed the previous rows; the push runs beside the geometric
-    all-reduce, after that barrier.
+    all-reduce, after that barrier.  colour_push ("compact", the default,
+    or "sparse"): deferred rows travel as compact (id, r, g, b) entries of
+    the Gaussians with a non-zero colour cotangent, whole lines through the
+    switch, and are scattered into the dense rows after the second barrier
+    (gsb_colour_push_compact, gsb_colour_expand); "sparse" stores the dense
+    row's non-zero 16-byte chunks straight into every copy.
     """
 
     @staticmethod
@@ -310,7 +315,7 @@ class NvlsExchange:
 
     def __init__(self, pool: GaussianArrays, config: CapacityConfig, active_degree: int,
                  group=None, active_sh_only: bool = True, allreduce: str = "auto",
-                 deferred_sh: bool = False):
+                 deferred_sh: bool = False, colour_push: str = "compact"):
         import ctypes
 
         import torch.distributed as dist
@@ -333,6 +338,16 @@ class NvlsExchange:
         # Row r = [camera centre 3 | pad 1 | colour cotangents C*3 | pad].
         self.row_floats = 4 + -(-(C * 3) // 4) * 4
         self.table = symm_mem.empty(self.world * self.row_floats, dtype=torch.float32, device=dev)
+        if colour_push not in ("compact", "sparse"):
+            raise ValueError("colour_push must be 'compact' or 'sparse'")
+        self.compact_push = bool(deferred_sh) and colour_push == "compact"
+        if self.compact_push:
+            # Row r = [centre 3 | entry count | C entries of (id, r, g, b)].
+            self.compact_floats = 4 + 4 * C
+            self.compact = symm_mem.empty(self.world * self.compact_floats, dtype=torch.float32,
+                                          device=dev)
+            self.compact.zero_()
+            self.counter = torch.zeros(1, dtype=torch.int32, device=dev)
         self.flags = symm_mem.empty(self.world, dtype=torch.int32, device=dev)
         self.flags.zero_()
         self.geometric.zero_()
@@ -343,6 +358,12 @@ class NvlsExchange:
         if not (int(h_geo.multicast_ptr) and int(h_tab.multicast_ptr)):
             raise RuntimeError("NVLS multicast is not available for this group")
         self._handles = (h_geo, h_tab, h_flags)
+        if self.compact_push:
+            h_cmp = symm_mem.rendezvous(self.compact, group)
+            if not int(h_cmp.multicast_ptr):
+                raise RuntimeError("NVLS multicast is not available for this group")
+            self._handles += (h_cmp,)
+            self.mc_compact = int(h_cmp.multicast_ptr) + self.rank * self.compact_floats * 4
         self.mc_geo = int(h_geo.multicast_ptr)
         # allreduce: "p2p" (plain peer loads/stores, up to 8 ranks), "nvls"
         # (multimem reduction in the switch) or "auto".  Per GPU and direction
@@ -428,13 +449,25 @@ class NvlsExchange:
         self._barrier()
         self.side.wait_stream(main)
         with torch.cuda.stream(self.side):
-            L.check(L.lib.gsb_multicast_nonzero(ctypes.c_void_p(self.side.cuda_stream),
-                                                ctypes.c_void_p(self.own_row.data_ptr()),
-                                                ctypes.c_void_p(self.mc_row), self.row_floats,
-                                                err), "colour row all-gather")
+            if self.compact_push:
+                L.check(L.lib.gsb_colour_push_compact(
+                    ctypes.c_void_p(self.side.cuda_stream), ctypes.c_void_p(self.own_row.data_ptr()),
+                    self.xyz.shape[0], ctypes.c_void_p(self.mc_compact),
+                    ctypes.c_void_p(self.counter.data_ptr()), err), "compact colour push")
+            else:
+                L.check(L.lib.gsb_multicast_nonzero(ctypes.c_void_p(self.side.cuda_stream),
+                                                    ctypes.c_void_p(self.own_row.data_ptr()),
+                                                    ctypes.c_void_p(self.mc_row), self.row_floats,
+                                                    err), "colour row all-gather")
         self._allreduce(main, err)
         main.wait_stream(self.side)
         self._barrier()
+        if self.compact_push:
+            L.check(L.lib.gsb_colour_expand(ctypes.c_void_p(main.cuda_stream),
+                                            ctypes.c_void_p(self.compact.data_ptr()), self.world,
+                                            self.xyz.shape[0],
+                                            ctypes.c_void_p(self.table.data_ptr()),
+                                            self.row_floats, err), "colour expand")
         return (*self.pool_grads[:4], self.rows)
 
     def exchange(self, camera_center: torch.Tensor | None = None):

@@ -2,7 +2,7 @@
 exchange (ViewShardedExchange over NCCL, or NvlsExchange with this library's
 collectives, its all-reduce in the switch or by peer loads and stores, with
 the SH gradients expanded in the exchange or deferred to the optimizer as
-gathered colour rows) leaves on every rank equal the single-process sum of
+gathered colour rows, pushed as compact entries or sparse chunks) leaves on every rank equal the single-process sum of
 the two views' full gradients, over several steps in a row.  Skipped
 with fewer than two GPUs (NvlsExchange also without multicast support)."""
 
@@ -53,10 +53,11 @@ def _rank(rank, world, port, path, kind):
             if rank == 0:
                 np.savez(path, skipped=np.ones(1))
             return
-        deferred = kind.endswith("-deferred")
+        deferred = "-deferred" in kind
         if nvls:
             exch = NvlsExchange(pool, config, 3, allreduce=kind.split("-")[0],
-                                deferred_sh=deferred)
+                                deferred_sh=deferred,
+                                colour_push="sparse" if kind.endswith("-sparse") else "compact")
         else:
             exch = ViewShardedExchange(pool, config, 3)
         # NvlsExchange: the exchange is captured into the step's graph.
@@ -95,7 +96,8 @@ def _rank(rank, world, port, path, kind):
 
 
 @pytest.mark.timeout(600)
-@pytest.mark.parametrize("kind", ["nccl", "nvls", "p2p", "nvls-deferred", "p2p-deferred"])
+@pytest.mark.parametrize("kind", ["nccl", "nvls", "p2p", "nvls-deferred", "p2p-deferred",
+                                  "p2p-deferred-sparse"])
 def test_two_rank_view_sharded_gradients(kind):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
