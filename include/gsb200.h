@@ -47,7 +47,7 @@ enum {
     GSB_ERR_NULL = 4        /* required pointer is NULL */
 };
 
-#define GSB_ABI_VERSION 10
+#define GSB_ABI_VERSION 11
 
 /* Library utilities.  No counterpart in the reference, whose boundary
  * (cutlass.jax.cutlass_call) reports errors by raising in Python before
@@ -510,17 +510,20 @@ GSB_API int gsb_p2p_allreduce(gsb_stream_t stream, const gsb_exchange_params* p,
  * row[4 + 3g .. 4 + 3g + 2] is non-zero to this rank's compact row through
  * its multicast address, then the header (row[0..2], the camera centre, and
  * the entry count as int bits); a compact row holds 4 + 4 * capacity floats
- * and the entry order is unspecified.  counter: one device int32 of
- * scratch, set to zero by the call.  gsb_colour_expand scatters every
- * view's entries of a gathered compact table [world][4 + 4 * capacity]
- * into dense rows [world][dense_row] (centre, pad, capacity * 3 colours),
- * which the caller clears beforehand.  Both return at once when the
+ * and the entry order is unspecified.  Two tables alternate: the device
+ * word *slot picks multicast0/table0 (even) or multicast1/table1 (odd).
+ * counter: one device int32 of scratch, set to zero by the call.
+ * gsb_colour_expand scatters every view's entries of the slot's gathered
+ * compact table [world][4 + 4 * capacity] into dense rows
+ * [world][dense_row] (centre, pad, capacity * 3 colours), which the caller
+ * clears beforehand, then advances *slot.  Both return at once when the
  * exchange's error word is set. */
 GSB_API int gsb_colour_push_compact(gsb_stream_t stream, const float* row, int64_t capacity,
-                            float* multicast, int32_t* counter, const int32_t* error);
-GSB_API int gsb_colour_expand(gsb_stream_t stream, const float* table, int world,
-                      int64_t capacity, float* dense, int64_t dense_row,
-                      const int32_t* error);
+                            float* multicast0, float* multicast1, const int32_t* slot,
+                            int32_t* counter, const int32_t* error);
+GSB_API int gsb_colour_expand(gsb_stream_t stream, const float* table0, const float* table1,
+                      int32_t* slot, int world, int64_t capacity, float* dense,
+                      int64_t dense_row, const int32_t* error);
 
 #ifdef __cplusplus
 }

@@ -154,9 +154,10 @@ def _load():
     lib.gsb_p2p_allreduce.restype = ctypes.c_int
     lib.gsb_p2p_allreduce.argtypes = [vp, vp, vp, ctypes.c_int64, vp]
     lib.gsb_colour_push_compact.restype = ctypes.c_int
-    lib.gsb_colour_push_compact.argtypes = [vp, vp, ctypes.c_int64, vp, vp, vp]
+    lib.gsb_colour_push_compact.argtypes = [vp, vp, ctypes.c_int64, vp, vp, vp, vp, vp]
     lib.gsb_colour_expand.restype = ctypes.c_int
-    lib.gsb_colour_expand.argtypes = [vp, vp, ctypes.c_int, ctypes.c_int64, vp, ctypes.c_int64, vp]
+    lib.gsb_colour_expand.argtypes = [vp, vp, vp, vp, ctypes.c_int, ctypes.c_int64, vp,
+                                      ctypes.c_int64, vp]
     lib.gsb_sparse_adam.restype = ctypes.c_int
     lib.gsb_sparse_adam.argtypes = [vp, vp] + [vp] * 8
     lib.gsb_sparse_adam_sh.restype = ctypes.c_int
@@ -171,7 +172,7 @@ def _load():
 
 
 lib = _load()
-if lib.gsb_abi_version() != 10:
+if lib.gsb_abi_version() != 11:
     raise RuntimeError("libgsb200.so ABI version mismatch; rebuild with `python -m jaxgs_b200.build`")
 
 

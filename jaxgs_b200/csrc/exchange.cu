@@ -137,12 +137,17 @@ __global__ void multicast_nonzero_kernel(const float4* __restrict__ src, float* 
 
 // Compact row layout: [centre x, y, z, entry count (int bits) | entries of
 // (id (int bits), r, g, b)], 4 + 4 * capacity floats.  The count is
-// written by compact_header_kernel after every entry is stored.
-__global__ void compact_push_kernel(const float* __restrict__ row, int64_t capacity, float* mc,
-                                    int32_t* counter, const int32_t* error)
+// written by compact_header_kernel after every entry is stored.  Two tables
+// alternate: *slot (a device word, advanced by the expand call) picks the
+// one a call pushes into and expands, so a rank can push its next step's
+// entries while a slower peer still expands the previous ones.
+__global__ void compact_push_kernel(const float* __restrict__ row, int64_t capacity, float* mc0,
+                                    float* mc1, const int32_t* slot, int32_t* counter,
+                                    const int32_t* error)
 {
     pdl_begin();
     if (error && *reinterpret_cast<const volatile int32_t*>(error)) return;
+    float* mc = (__ldg(slot) & 1) ? mc1 : mc0;
     const int lane = threadIdx.x & 31;
     const float* colours = row + 4;
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
@@ -173,25 +178,28 @@ __global__ void compact_push_kernel(const float* __restrict__ row, int64_t capac
 }
 
 // One thread: the row's header (centre and entry count) after the entries.
-__global__ void compact_header_kernel(const float* __restrict__ row, float* mc,
-                                      const int32_t* counter, const int32_t* error)
+__global__ void compact_header_kernel(const float* __restrict__ row, float* mc0, float* mc1,
+                                      const int32_t* slot, const int32_t* counter,
+                                      const int32_t* error)
 {
     pdl_begin();
     if (error && *reinterpret_cast<const volatile int32_t*>(error)) return;
+    float* mc = (*slot & 1) ? mc1 : mc0;
     multimem_st_v4(mc, make_float4(row[0], row[1], row[2], __int_as_float(*counter)));
     __threadfence_system();
 }
 
 // grid.y: view; each view's entries scattered into its dense row [centre,
 // pad, capacity * 3 colours] (cleared beforehand), the centre copied.
-__global__ void compact_expand_kernel(const float* __restrict__ table, int64_t capacity,
-                                      int64_t compact_row, float* dense, int64_t dense_row,
-                                      const int32_t* error)
+__global__ void compact_expand_kernel(const float* __restrict__ table0,
+                                      const float* __restrict__ table1, const int32_t* slot,
+                                      int64_t capacity, int64_t compact_row, float* dense,
+                                      int64_t dense_row, const int32_t* error)
 {
     pdl_begin();
     if (error && *reinterpret_cast<const volatile int32_t*>(error)) return;
     const int v = blockIdx.y;
-    const float* src = table + (int64_t)v * compact_row;
+    const float* src = ((*slot & 1) ? table1 : table0) + (int64_t)v * compact_row;
     float* dst = dense + (int64_t)v * dense_row;
     const int64_t n = __float_as_int(__ldg(src + 3));
     const int64_t count = n < 0 ? 0 : (n > capacity ? capacity : n);
@@ -206,6 +214,14 @@ __global__ void compact_expand_kernel(const float* __restrict__ table, int64_t c
         c[1] = e.z;
         c[2] = e.w;
     }
+}
+
+// One thread, after the expand: the next call uses the other table.
+__global__ void compact_flip_kernel(int32_t* slot, const int32_t* error)
+{
+    pdl_begin();
+    if (error && *reinterpret_cast<const volatile int32_t*>(error)) return;
+    *slot ^= 1;
 }
 
 constexpr int kMaxPeers = 8;
@@ -340,35 +356,39 @@ extern "C" int gsb_p2p_allreduce(gsb_stream_t stream, const gsb_exchange_params*
 }
 
 extern "C" int gsb_colour_push_compact(gsb_stream_t stream, const float* row, int64_t capacity,
-                                       float* multicast, int32_t* counter, const int32_t* error)
+                                       float* multicast0, float* multicast1, const int32_t* slot,
+                                       int32_t* counter, const int32_t* error)
 {
     if (capacity < 0 || capacity >= ((int64_t)1 << 31)) return GSB_ERR_INVALID;
-    if (!row || !multicast || !counter) return GSB_ERR_NULL;
-    if (!aligned16(row) || !aligned16(multicast)) return GSB_ERR_INVALID;
+    if (!row || !multicast0 || !multicast1 || !slot || !counter) return GSB_ERR_NULL;
+    if (!aligned16(row) || !aligned16(multicast0) || !aligned16(multicast1))
+        return GSB_ERR_INVALID;
     cudaStream_t s = as_stream(stream);
     if (cudaMemsetAsync(counter, 0, sizeof(int32_t), s) != cudaSuccess) return check_launch();
     if (capacity > 0) {
         const int64_t want = (capacity + 255) / 256;
         const int blocks = (int)(want < 148 * 4 ? want : 148 * 4);
-        gsb::launch(compact_push_kernel, blocks, 256, 0, s, row, capacity, multicast, counter,
-                    error);
+        gsb::launch(compact_push_kernel, blocks, 256, 0, s, row, capacity, multicast0, multicast1,
+                    slot, counter, error);
     }
-    gsb::launch(compact_header_kernel, 1, 1, 0, s, row, multicast,
+    gsb::launch(compact_header_kernel, 1, 1, 0, s, row, multicast0, multicast1, slot,
                 static_cast<const int32_t*>(counter), error);
     return check_launch();
 }
 
-extern "C" int gsb_colour_expand(gsb_stream_t stream, const float* table, int world,
-                                 int64_t capacity, float* dense, int64_t dense_row,
-                                 const int32_t* error)
+extern "C" int gsb_colour_expand(gsb_stream_t stream, const float* table0, const float* table1,
+                                 int32_t* slot, int world, int64_t capacity, float* dense,
+                                 int64_t dense_row, const int32_t* error)
 {
     if (world < 1 || world > 65535 || capacity < 0 || capacity >= ((int64_t)1 << 31) ||
         dense_row < 4 + capacity * 3)
         return GSB_ERR_INVALID;
-    if (!table || !dense) return GSB_ERR_NULL;
-    if (!aligned16(table)) return GSB_ERR_INVALID;
+    if (!table0 || !table1 || !slot || !dense) return GSB_ERR_NULL;
+    if (!aligned16(table0) || !aligned16(table1)) return GSB_ERR_INVALID;
     const int64_t compact_row = 4 + 4 * capacity;
-    gsb::launch(compact_expand_kernel, dim3(148, world), 256, 0, as_stream(stream), table,
-                capacity, compact_row, dense, dense_row, error);
+    cudaStream_t s = as_stream(stream);
+    gsb::launch(compact_expand_kernel, dim3(148, world), 256, 0, s, table0, table1,
+                static_cast<const int32_t*>(slot), capacity, compact_row, dense, dense_row, error);
+    gsb::launch(compact_flip_kernel, 1, 1, 0, s, slot, error);
     return check_launch();
 }

@@ -286,19 +286,24 @@ class NvlsExchange:
 
     deferred_sh: the SH gradients stay in the reference's deferred form
     (training/step.py:55-66): exchange() gathers every view's colour row
-    and camera centre into the table and returns the rows instead of
-    expanding them, and the optimizer rebuilds the SH gradients
-    (sparse_adam_update(..., sh_pullback_rows=rows)).  The table is then
+    and camera centre into dense rows and returns them instead of expanding
+    them, and the optimizer rebuilds the SH gradients
+    (sparse_adam_update(..., sh_pullback_rows=rows)).  The dense rows are
     cleared by begin_step() (call it before the step's work, after the
-    previous rows' consumer) or at the start of exchange(), before the
-    first barrier, so that no peer pushes into it before this rank has
-    consumed the previous rows; the push runs beside the geometric
-    all-reduce, after that barrier.  colour_push ("compact", the default,
-    or "sparse"): deferred rows travel as compact (id, r, g, b) entries of
-    the Gaussians with a non-zero colour cotangent, whole lines through the
-    switch, and are scattered into the dense rows after the second barrier
-    (gsb_colour_push_compact, gsb_colour_expand); "sparse" stores the dense
-    row's non-zero 16-byte chunks straight into every copy.
+    previous rows' consumer) or at the start of exchange().
+    colour_push says how the rows travel:
+      "compact" (default): this rank appends (id, r, g, b) for every
+        Gaussian with a non-zero colour cotangent to its row of a symmetric
+        table through the multicast address, whole lines through the switch
+        (gsb_colour_push_compact), and after the second barrier every rank
+        scatters the entries into its local dense rows (gsb_colour_expand).
+        Two tables alternate by a device word, so the push leaves right
+        after the step, beside the first barrier: a peer still expanding
+        the previous step's entries reads the other table.
+      "sparse": the dense rows themselves are the symmetric table; the
+        dense row's non-zero 16-byte chunks are stored into every copy
+        after the first barrier (a peer must not push into rows this rank
+        has not consumed yet), beside the all-reduce.
     """
 
     @staticmethod
@@ -342,12 +347,14 @@ class NvlsExchange:
             raise ValueError("colour_push must be 'compact' or 'sparse'")
         self.compact_push = bool(deferred_sh) and colour_push == "compact"
         if self.compact_push:
-            # Row r = [centre 3 | entry count | C entries of (id, r, g, b)].
+            # Two tables of rows [centre 3 | entry count | C entries of
+            # (id, r, g, b)], alternating by a device word.
             self.compact_floats = 4 + 4 * C
-            self.compact = symm_mem.empty(self.world * self.compact_floats, dtype=torch.float32,
-                                          device=dev)
+            self.compact = symm_mem.empty(2 * self.world * self.compact_floats,
+                                          dtype=torch.float32, device=dev)
             self.compact.zero_()
             self.counter = torch.zeros(1, dtype=torch.int32, device=dev)
+            self.slot = torch.zeros(1, dtype=torch.int32, device=dev)
         self.flags = symm_mem.empty(self.world, dtype=torch.int32, device=dev)
         self.flags.zero_()
         self.geometric.zero_()
@@ -363,7 +370,10 @@ class NvlsExchange:
             if not int(h_cmp.multicast_ptr):
                 raise RuntimeError("NVLS multicast is not available for this group")
             self._handles += (h_cmp,)
-            self.mc_compact = int(h_cmp.multicast_ptr) + self.rank * self.compact_floats * 4
+            table_bytes = self.world * self.compact_floats * 4
+            self.mc_compact = [int(h_cmp.multicast_ptr) + t * table_bytes
+                               + self.rank * self.compact_floats * 4 for t in (0, 1)]
+            self.compact_tables = [self.compact.data_ptr() + t * table_bytes for t in (0, 1)]
         self.mc_geo = int(h_geo.multicast_ptr)
         # allreduce: "p2p" (plain peer loads/stores, up to 8 ranks), "nvls"
         # (multimem reduction in the switch) or "auto".  Per GPU and direction
@@ -436,12 +446,45 @@ class NvlsExchange:
                                              L.ref(self.params), ctypes.c_void_p(self.mc_geo),
                                              self.geo_count, err), "NVLS all-reduce")
 
+    def _exchange_compact(self, main, err):
+        """Deferred SH, compact colour push: the push goes out at once (into
+        the table the device slot picks; a peer may still be expanding the
+        other one), then barrier -> geometric all-reduce -> barrier ->
+        expand into the dense rows (cleared by begin_step) and advance the
+        slot; returns the dense rows."""
+        import ctypes
+
+        L = self.L
+        if not self._cleared:
+            self.begin_step()
+        self._cleared = False
+        self.side.wait_stream(main)
+        with torch.cuda.stream(self.side):
+            L.check(L.lib.gsb_colour_push_compact(
+                ctypes.c_void_p(self.side.cuda_stream), ctypes.c_void_p(self.own_row.data_ptr()),
+                self.xyz.shape[0], ctypes.c_void_p(self.mc_compact[0]),
+                ctypes.c_void_p(self.mc_compact[1]), ctypes.c_void_p(self.slot.data_ptr()),
+                ctypes.c_void_p(self.counter.data_ptr()), err), "compact colour push")
+        self._barrier()
+        self._allreduce(main, err)
+        main.wait_stream(self.side)
+        self._barrier()
+        L.check(L.lib.gsb_colour_expand(ctypes.c_void_p(main.cuda_stream),
+                                        ctypes.c_void_p(self.compact_tables[0]),
+                                        ctypes.c_void_p(self.compact_tables[1]),
+                                        ctypes.c_void_p(self.slot.data_ptr()), self.world,
+                                        self.xyz.shape[0], ctypes.c_void_p(self.table.data_ptr()),
+                                        self.row_floats, err), "colour expand")
+        return (*self.pool_grads[:4], self.rows)
+
     def _exchange_deferred(self, main, err):
         """Clear (unless begin_step did) -> barrier -> colour push beside the
         geometric all-reduce -> barrier; returns the gathered rows."""
         import ctypes
 
         L = self.L
+        if self.compact_push:
+            return self._exchange_compact(main, err)
         if not self._cleared:
             self.begin_step()
         self._cleared = False
@@ -449,25 +492,13 @@ class NvlsExchange:
         self._barrier()
         self.side.wait_stream(main)
         with torch.cuda.stream(self.side):
-            if self.compact_push:
-                L.check(L.lib.gsb_colour_push_compact(
-                    ctypes.c_void_p(self.side.cuda_stream), ctypes.c_void_p(self.own_row.data_ptr()),
-                    self.xyz.shape[0], ctypes.c_void_p(self.mc_compact),
-                    ctypes.c_void_p(self.counter.data_ptr()), err), "compact colour push")
-            else:
-                L.check(L.lib.gsb_multicast_nonzero(ctypes.c_void_p(self.side.cuda_stream),
-                                                    ctypes.c_void_p(self.own_row.data_ptr()),
-                                                    ctypes.c_void_p(self.mc_row), self.row_floats,
-                                                    err), "colour row all-gather")
+            L.check(L.lib.gsb_multicast_nonzero(ctypes.c_void_p(self.side.cuda_stream),
+                                                ctypes.c_void_p(self.own_row.data_ptr()),
+                                                ctypes.c_void_p(self.mc_row), self.row_floats,
+                                                err), "colour row all-gather")
         self._allreduce(main, err)
         main.wait_stream(self.side)
         self._barrier()
-        if self.compact_push:
-            L.check(L.lib.gsb_colour_expand(ctypes.c_void_p(main.cuda_stream),
-                                            ctypes.c_void_p(self.compact.data_ptr()), self.world,
-                                            self.xyz.shape[0],
-                                            ctypes.c_void_p(self.table.data_ptr()),
-                                            self.row_floats, err), "colour expand")
         return (*self.pool_grads[:4], self.rows)
 
     def exchange(self, camera_center: torch.Tensor | None = None):

@@ -28,7 +28,7 @@ def test_every_declared_symbol_is_exported():
 
 
 def test_abi_version_and_launch_counter():
-    assert L.lib.gsb_abi_version() == 10
+    assert L.lib.gsb_abi_version() == 11
     assert L.launch_count() >= 0
 
 
@@ -124,12 +124,13 @@ def test_optimizer_density_and_exchange_entry_points_validate_before_launch():
     assert L.lib.gsb_p2p_allreduce(vp, L.ref(two), (ctypes.c_void_p * 2)(16, 24), 8, vp) == 1
     assert L.lib.gsb_p2p_allreduce(vp, L.ref(two), (ctypes.c_void_p * 2)(16, None), 8, vp) == 4
     assert L.lib.gsb_p2p_allreduce(vp, L.ref(L.ExchangeParams(2, 2)), buffers, 8, vp) == 1
-    assert L.lib.gsb_colour_push_compact(vp, vp, -1, vp, vp, vp) == 1
-    assert L.lib.gsb_colour_push_compact(vp, vp, 10, vp, vp, vp) == 4
-    assert L.lib.gsb_colour_push_compact(vp, ctypes.c_void_p(8), 10, ctypes.c_void_p(16),
-                                         ctypes.c_void_p(16), vp) == 1  # misaligned row
-    assert L.lib.gsb_colour_expand(vp, vp, 2, 10, vp, 33, vp) == 1  # dense row < 4 + 3C
-    assert L.lib.gsb_colour_expand(vp, vp, 2, 10, vp, 34, vp) == 4
+    a16, a8 = ctypes.c_void_p(16), ctypes.c_void_p(8)
+    assert L.lib.gsb_colour_push_compact(vp, vp, -1, vp, vp, vp, vp, vp) == 1
+    assert L.lib.gsb_colour_push_compact(vp, vp, 10, vp, vp, vp, vp, vp) == 4
+    assert L.lib.gsb_colour_push_compact(vp, a8, 10, a16, a16, a16, a16, vp) == 1  # misaligned row
+    assert L.lib.gsb_colour_push_compact(vp, a16, 10, a16, a8, a16, a16, vp) == 1  # misaligned table
+    assert L.lib.gsb_colour_expand(vp, a16, a16, a16, 2, 10, a16, 33, vp) == 1  # dense row < 4 + 3C
+    assert L.lib.gsb_colour_expand(vp, vp, vp, vp, 2, 10, vp, 34, vp) == 4
 
 
 def test_sparse_adam_python_checks_refuse_mismatched_rows():
