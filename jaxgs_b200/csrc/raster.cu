@@ -440,32 +440,46 @@ __global__ void __launch_bounds__(256) raster_fwd_kernel(
     }
 }
 
-// Transposed butterfly over 8 values: afterwards lane l holds the warp sum
-// of value (l >> 2).  9 shuffles instead of 8 x 5.
-__device__ __forceinline__ float warp_sum8(float v[8], int lane)
+// Transposed butterfly over 16 values: afterwards lane l holds the warp sum
+// of value ((l >> 1) & 15).  16 shuffles for 16 sums.
+__device__ __forceinline__ float warp_sum16(float v[16], int lane)
 {
-    const bool b4 = lane & 16, b3 = lane & 8, b2 = lane & 4;
+    const bool b4 = lane & 16, b3 = lane & 8, b2 = lane & 4, b1 = lane & 2;
 #pragma unroll
-    for (int j = 0; j < 4; j++) {
-        float keep = b4 ? v[j + 4] : v[j];
-        float send = b4 ? v[j] : v[j + 4];
+    for (int j = 0; j < 8; j++) {
+        float keep = b4 ? v[j + 8] : v[j];
+        float send = b4 ? v[j] : v[j + 8];
         v[j] = keep + __shfl_xor_sync(GSB_FULL_MASK, send, 16);
     }
 #pragma unroll
-    for (int j = 0; j < 2; j++) {
-        float keep = b3 ? v[j + 2] : v[j];
-        float send = b3 ? v[j] : v[j + 2];
+    for (int j = 0; j < 4; j++) {
+        float keep = b3 ? v[j + 4] : v[j];
+        float send = b3 ? v[j] : v[j + 4];
         v[j] = keep + __shfl_xor_sync(GSB_FULL_MASK, send, 8);
     }
-    {
-        float keep = b2 ? v[1] : v[0];
-        float send = b2 ? v[0] : v[1];
-        v[0] = keep + __shfl_xor_sync(GSB_FULL_MASK, send, 4);
+#pragma unroll
+    for (int j = 0; j < 2; j++) {
+        float keep = b2 ? v[j + 2] : v[j];
+        float send = b2 ? v[j] : v[j + 2];
+        v[j] = keep + __shfl_xor_sync(GSB_FULL_MASK, send, 4);
     }
-    float s = v[0];
-    s += __shfl_xor_sync(GSB_FULL_MASK, s, 2);
+    float keep = b1 ? v[1] : v[0];
+    float send = b1 ? v[0] : v[1];
+    float s = keep + __shfl_xor_sync(GSB_FULL_MASK, send, 2);
     s += __shfl_xor_sync(GSB_FULL_MASK, s, 1);
     return s;
+}
+
+// Warp sums of two values: lanes 0-15 get the first's, 16-31 the second's.
+__device__ __forceinline__ float warp_sum_pair(float a, float b, int lane)
+{
+    const bool hi = lane & 16;
+    float t = (hi ? b : a) + __shfl_xor_sync(GSB_FULL_MASK, hi ? a : b, 16);
+    t += __shfl_xor_sync(GSB_FULL_MASK, t, 8);
+    t += __shfl_xor_sync(GSB_FULL_MASK, t, 4);
+    t += __shfl_xor_sync(GSB_FULL_MASK, t, 2);
+    t += __shfl_xor_sync(GSB_FULL_MASK, t, 1);
+    return t;
 }
 
 template <int ROWS, bool WANT_DEPTH, bool STATS>
@@ -513,31 +527,109 @@ __global__ void __launch_bounds__(256) raster_bwd_kernel(
     }
 #pragma unroll
     for (int d = 16; d > 0; d >>= 1) top = max(top, __shfl_xor_sync(GSB_FULL_MASK, top, d));
-    // Per-lane RED target after the reduction: lane 4j holds moment j
-    // (Sx, Sy, Sxx, Sxy, Syy, R, G, B), lane 13 repeats Sxy for conic[2]
-    // (unless the symmetric convention folds it into conic[1]),
-    // lane 1 adds the opacity gradient sum(ge) / o, lane 2 the depth one.
-    const int group = lane >> 2, role = lane & 3;
+    // Two contributing splats per pass of the reduction: after warp_sum16
+    // lanes 2j, 2j+1 hold moment j (Sx, Sy, Sxx, Sxy, Syy, R, G, B) of the
+    // first splat and lanes 16 + 2j, 16 + 2j + 1 that of the second.  Even
+    // lanes add their moment; odd lane 1 the opacity gradient sum(ge) / o,
+    // odd lane 3 the depth one, odd lane 7 repeats Sxy for conic[2] (unless
+    // the symmetric convention folds it into conic[1]); the same +16.
+    const int role_lane = lane & 15, j = role_lane >> 1;
     float* target = nullptr;
     int stride = 0;
-    if (role == 0) {
-        if (group < 2) { target = gmean + group; stride = 2; }
-        else if (group < 5) { target = gconic + (group == 2 ? 0 : group == 3 ? 1 : 3); stride = 4; }
-        else { target = gcolor + (group - 5); stride = 3; }
-    } else if (lane == 13 && !(p.flags & GSB_RASTER_BWD_SYMMETRIC_CONIC)) {
+    if ((role_lane & 1) == 0) {
+        if (j < 2) { target = gmean + j; stride = 2; }
+        else if (j < 5) { target = gconic + (j == 2 ? 0 : j == 3 ? 1 : 3); stride = 4; }
+        else { target = gcolor + (j - 5); stride = 3; }
+    } else if (role_lane == 7 && !(p.flags & GSB_RASTER_BWD_SYMMETRIC_CONIC)) {
         target = gconic + 2; stride = 4;
-    } else if (lane == 1) {
+    } else if (role_lane == 1) {
         target = galpha; stride = 1;
-    } else if (WANT_DEPTH && lane == 2) {
+    } else if (WANT_DEPTH && role_lane == 3) {
         target = gdepth; stride = 1;
     }
-    // Constant coefficient of the lane's moment (groups 2-4: -1/2, 5-7: 1).
+    // Constant coefficient of the lane's moment (2-4: -1/2, 5-7: 1).
     // Symmetric convention (packed_rasterize.py:130-175): conic[0][1] takes
     // both off-diagonal contributions and conic[1][0] stays zero.
-    const float kA = group < 5 ? ((group == 3 && (p.flags & GSB_RASTER_BWD_SYMMETRIC_CONIC))
-                                      ? -1.0f : -0.5f)
-                               : 1.0f;
+    const float kA = j < 5 ? ((j == 3 && (p.flags & GSB_RASTER_BWD_SYMMETRIC_CONIC)) ? -1.0f
+                                                                                      : -0.5f)
+                           : 1.0f;
+    const bool second = lane & 16;
     if (top <= start) return;
+    // One splat's pass over the lane's pixels, in reverse compositing
+    // order: updates T_after and gtrans, returns the lane's moments.
+    auto visit = [&](int k, int32_t idx, float (&v)[8], float& S0, float& Z) {
+        const Fragment<ROWS> f = fragment<ROWS>(st, k, pcx, pcy);
+        const float4 q3 = st.q3[k], q4 = st.q4[k];
+        T e;
+#pragma unroll
+        for (int r = 0; r < ROWS; r++) V::set(e, r, __expf(V::get(f.power, r)));
+        const T raw = V::mul(V::lo(q3), e);
+        T a, inv;
+        bool valid[ROWS];
+#pragma unroll
+        for (int r = 0; r < ROWS; r++) {
+            const float rr = V::get(raw, r);
+            valid[r] = idx < last[r] && V::get(f.power, r) <= 0.0f && rr >= kMinAlpha;
+            // Branch-free: with a = 0 the transmittance, the colour
+            // behind and every accumulated term stay exactly unchanged.
+            V::set(a, r, valid[r] ? fminf(kMaxAlpha, rr) : 0.0f);
+        }
+        const T one_minus = V::fma(a, V::splat(-1.0f), V::splat(1.0f));
+#pragma unroll
+        for (int r = 0; r < ROWS; r++) V::set(inv, r, __fdividef(1.0f, V::get(one_minus, r)));
+        const T T_before = V::mul(T_after, inv);
+        const T w = V::mul(T_before, a);
+        T gw = V::fma(gB, V::hi(q4), V::fma(gG, V::lo(q4), V::mul(gR, V::hi(q3))));
+        if (WANT_DEPTH) {
+            const float2 d = st.depth[k];
+            gw = V::fma(gD, V::lo(make_float4(d.x, d.y, d.x, d.y)), gw);
+        }
+        // ga = T_before (gw - gtrans); gtrans' = a gw + (1 - a) gtrans
+        // (an exact no-op when a = 0).
+        const T ga = V::mul(T_before, V::fma(gtrans, V::splat(-1.0f), gw));
+        gtrans = V::fma(a, gw, V::mul(one_minus, gtrans));
+        const float R = row_sum<ROWS>(V::mul(w, gR));
+        const float G = row_sum<ROWS>(V::mul(w, gG));
+        const float B = row_sum<ROWS>(V::mul(w, gB));
+        Z = 0.0f;
+        if (WANT_DEPTH) Z = row_sum<ROWS>(V::mul(w, gD));
+        T ge = V::mul(ga, raw);
+        float count = 0.0f, square = 0.0f;
+#pragma unroll
+        for (int r = 0; r < ROWS; r++) {
+            const bool live = valid[r] && V::get(raw, r) < kMaxAlpha;
+            V::set(ge, r, live ? V::get(ge, r) : 0.0f);
+            V::set(T_after, r, valid[r] ? V::get(T_before, r) : V::get(T_after, r));
+            if (STATS) {
+                // Fragment statistics (sorted_rasterize.py:155-203): one
+                // count per composited fragment, and the squared opacity
+                // cotangent ga * e of each unsaturated one.
+                const float go = live ? V::get(ga, r) * V::get(e, r) : 0.0f;
+                count += valid[r] ? 1.0f : 0.0f;
+                square = fmaf(go, go, square);
+            }
+        }
+        if (STATS) {
+            // w is exactly zero where the fragment is not composited.
+            const float weight = warp_sum(row_sum<ROWS>(w));
+            count = warp_sum(count);
+            square = warp_sum(square);
+            if (lane == 0 && count != 0.0f) {
+                float* st_g = stats + (int64_t)st.id[k] * 3;
+                atomicAdd(st_g, count);
+                atomicAdd(st_g + 1, weight);
+                atomicAdd(st_g + 2, square);
+            }
+        }
+        const T gedy = V::mul(ge, f.dy);
+        S0 = row_sum<ROWS>(ge);
+        const float Sy = row_sum<ROWS>(gedy);
+        const float Syy = row_sum<ROWS>(V::mul(gedy, f.dy));
+        const float dx = V::get(f.dx, 0);
+        const float Sx = dx * S0;
+        v[0] = Sx; v[1] = Sy; v[2] = dx * Sx; v[3] = dx * Sy;
+        v[4] = Syy; v[5] = R; v[6] = G; v[7] = B;
+    };
     const int32_t top_batch = (top - 1 - start) >> 5;
     for (int32_t batch = top_batch; batch >= 0; batch--) {
         uint32_t word = __ldg(bits + bit_word(start, tile, batch, warps, warp));
@@ -559,93 +651,38 @@ __global__ void __launch_bounds__(256) raster_bwd_kernel(
         }
         __syncwarp();
         while (word) {
-            const int k = 31 - __clz(word);
-            word &= ~(1u << k);
-            const int32_t idx = base + k;
-            const Fragment<ROWS> f = fragment<ROWS>(st, k, pcx, pcy);
-            const float4 q3 = st.q3[k], q4 = st.q4[k];
-            T e;
+            const int k1 = 31 - __clz(word);
+            word &= ~(1u << k1);
+            float v[16], S0a, Za;
+            float (&va)[8] = *reinterpret_cast<float(*)[8]>(&v[0]);
+            float (&vb)[8] = *reinterpret_cast<float(*)[8]>(&v[8]);
+            visit(k1, base + k1, va, S0a, Za);
+            const bool has2 = word != 0;  // uniform over the warp
+            int k2 = k1;
+            float S0b = 0.0f, Zb = 0.0f;
 #pragma unroll
-            for (int r = 0; r < ROWS; r++) V::set(e, r, __expf(V::get(f.power, r)));
-            const T raw = V::mul(V::lo(q3), e);
-            T a, inv;
-            bool valid[ROWS];
-#pragma unroll
-            for (int r = 0; r < ROWS; r++) {
-                const float rr = V::get(raw, r);
-                valid[r] = idx < last[r] && V::get(f.power, r) <= 0.0f && rr >= kMinAlpha;
-                // Branch-free: with a = 0 the transmittance, the colour
-                // behind and every accumulated term stay exactly unchanged.
-                V::set(a, r, valid[r] ? fminf(kMaxAlpha, rr) : 0.0f);
+            for (int i = 0; i < 8; i++) vb[i] = 0.0f;
+            if (has2) {
+                k2 = 31 - __clz(word);
+                word &= ~(1u << k2);
+                visit(k2, base + k2, vb, S0b, Zb);
             }
-            const T one_minus = V::fma(a, V::splat(-1.0f), V::splat(1.0f));
-#pragma unroll
-            for (int r = 0; r < ROWS; r++) V::set(inv, r, __fdividef(1.0f, V::get(one_minus, r)));
-            const T T_before = V::mul(T_after, inv);
-            const T w = V::mul(T_before, a);
-            T gw = V::fma(gB, V::hi(q4), V::fma(gG, V::lo(q4), V::mul(gR, V::hi(q3))));
-            if (WANT_DEPTH) {
-                const float2 d = st.depth[k];
-                gw = V::fma(gD, V::lo(make_float4(d.x, d.y, d.x, d.y)), gw);
-            }
-            // ga = T_before (gw - gtrans); gtrans' = a gw + (1 - a) gtrans
-            // (an exact no-op when a = 0).
-            const T ga = V::mul(T_before, V::fma(gtrans, V::splat(-1.0f), gw));
-            gtrans = V::fma(a, gw, V::mul(one_minus, gtrans));
-            const float R = row_sum<ROWS>(V::mul(w, gR));
-            const float G = row_sum<ROWS>(V::mul(w, gG));
-            const float B = row_sum<ROWS>(V::mul(w, gB));
+            const float s = warp_sum16(v, lane);
+            const float S0 = warp_sum_pair(S0a, S0b, lane);
             float Z = 0.0f;
-            if (WANT_DEPTH) Z = row_sum<ROWS>(V::mul(w, gD));
-            T ge = V::mul(ga, raw);
-            float count = 0.0f, square = 0.0f;
-#pragma unroll
-            for (int r = 0; r < ROWS; r++) {
-                const bool live = valid[r] && V::get(raw, r) < kMaxAlpha;
-                V::set(ge, r, live ? V::get(ge, r) : 0.0f);
-                V::set(T_after, r, valid[r] ? V::get(T_before, r) : V::get(T_after, r));
-                if (STATS) {
-                    // Fragment statistics (sorted_rasterize.py:155-203): one
-                    // count per composited fragment, and the squared opacity
-                    // cotangent ga * e of each unsaturated one.
-                    const float go = live ? V::get(ga, r) * V::get(e, r) : 0.0f;
-                    count += valid[r] ? 1.0f : 0.0f;
-                    square = fmaf(go, go, square);
-                }
-            }
-            if (STATS) {
-                // w is exactly zero where the fragment is not composited.
-                const float weight = warp_sum(row_sum<ROWS>(w));
-                count = warp_sum(count);
-                square = warp_sum(square);
-                if (lane == 0 && count != 0.0f) {
-                    float* st_g = stats + (int64_t)st.id[k] * 3;
-                    atomicAdd(st_g, count);
-                    atomicAdd(st_g + 1, weight);
-                    atomicAdd(st_g + 2, square);
-                }
-            }
-            const T gedy = V::mul(ge, f.dy);
-            float S0 = row_sum<ROWS>(ge);
-            const float Sy = row_sum<ROWS>(gedy);
-            const float Syy = row_sum<ROWS>(V::mul(gedy, f.dy));
-            const float dx = V::get(f.dx, 0);
-            const float Sx = dx * S0;
-            float v[8] = {Sx, Sy, dx * Sx, dx * Sy, Syy, R, G, B};
-            const float s = warp_sum8(v, lane);
-            S0 = warp_sum(S0);
-            if (WANT_DEPTH) Z = warp_sum(Z);
+            if (WANT_DEPTH) Z = warp_sum_pair(Za, Zb, lane);
             // gmean.x = c00 Sx + cbar Sy, gmean.y = c11 Sy + cbar Sx with c = -2 c';
             // gconic = -Sxx/2, -Sxy/2 (twice), -Syy/2; gcolor = R, G, B;
             // galpha = sum(ge) / o.
+            const int k = second ? k2 : k1;
             const float4 q1 = st.q1[k], q2 = st.q2[k];
-            const float other = __shfl_xor_sync(GSB_FULL_MASK, s, 4);
-            const float coef_a = group == 0 ? -2.0f * q1.x : (group == 1 ? -2.0f * q2.z : kA);
-            const float coef_b = group < 2 ? -(q2.x + q1.z) : 0.0f;
+            const float other = __shfl_xor_sync(GSB_FULL_MASK, s, 2);
+            const float coef_a = j == 0 ? -2.0f * q1.x : (j == 1 ? -2.0f * q2.z : kA);
+            const float coef_b = j < 2 ? -(q2.x + q1.z) : 0.0f;
             float value = coef_a * s + coef_b * other;
-            if (lane == 1) value = __fdividef(S0, q3.x);
-            if (WANT_DEPTH && lane == 2) value = Z;
-            if (target) atomicAdd(target + (int64_t)st.id[k] * stride, value);
+            if (role_lane == 1) value = __fdividef(S0, st.q3[k].x);
+            if (WANT_DEPTH && role_lane == 3) value = Z;
+            if (target && (has2 || !second)) atomicAdd(target + (int64_t)st.id[k] * stride, value);
         }
         __syncwarp();
     }
