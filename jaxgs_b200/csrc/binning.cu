@@ -733,11 +733,14 @@ int onesweep_sort(cudaStream_t s, const K* keys_in, const int32_t* vals_in, K* k
 // ---------------------------------------------------------------------------
 // Emission (sorted_visibility.py:373-484), with the last step of the
 // depth-ordered scan (sorted_visibility.py:511-603): a block's first pair
-// offset is the sum of the pair counts of the earlier blocks (one warp adds
-// the block sums written by the last depth pass; they are L2-resident), and
-// its threads' offsets follow from a block scan.
+// offset is the sum of the pair counts of the earlier blocks (the block's
+// threads add the block sums written by the last depth pass; they are
+// L2-resident), and its threads' offsets follow from a block scan.
+// A Gaussian with at most kLanePairs pairs is walked by its own thread;
+// larger ones are queued for a warp each (emit_large_kernel).  32 measured
+// fastest on config 2 (8: +10 %, 16: +2.7 %, 64: +3 % of the binning).
 // ---------------------------------------------------------------------------
-constexpr int kLanePairs = 16;
+constexpr int kLanePairs = 32;
 
 // Adds the block's digit counts to the tile sort's global histograms
 // (hist[pass * 256 + digit], the layout onesweep_sort reads).
@@ -771,7 +774,7 @@ __global__ void __launch_bounds__(kEmitThreads) emit_kernel(
     pdl_begin();
     __shared__ uint32_t local[4 * 256];
     __shared__ long long warp_total[kEmitThreads / 32];
-    __shared__ long long block_prefix;
+    __shared__ unsigned long long prefix_part[kEmitThreads / 32];
     const int64_t n = read_count(n_ptr, n_cap);
     const int b = blockIdx.x;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -785,12 +788,14 @@ __global__ void __launch_bounds__(kEmitThreads) emit_kernel(
     }
     if ((int64_t)b * kEmitThreads >= n) return;  // uniform per block
     for (int i = threadIdx.x; i < passes * 256; i += blockDim.x) local[i] = 0;
-    if (warp == 0) {
+    {
+        // Every thread adds a strided share of the earlier blocks' sums, so
+        // the loads are in flight together instead of one warp's chain.
         unsigned long long acc = 0;
 #pragma unroll 4
-        for (int i = lane; i < b; i += 32) acc += scan.block_sums[i];
+        for (int i = threadIdx.x; i < b; i += kEmitThreads) acc += scan.block_sums[i];
         acc = warp_sum(acc);
-        if (lane == 0) block_prefix = (long long)acc;
+        if (lane == 0) prefix_part[warp] = acc;
     }
     const int64_t r = (int64_t)b * kEmitThreads + threadIdx.x;
     int32_t count = 0, gid = 0;
@@ -801,7 +806,9 @@ __global__ void __launch_bounds__(kEmitThreads) emit_kernel(
     const long long inc = warp_inclusive_scan((long long)count, lane);
     if (lane == 31) warp_total[warp] = inc;
     __syncthreads();
-    long long before = block_prefix;
+    long long before = 0;
+#pragma unroll
+    for (int w = 0; w < kEmitThreads / 32; w++) before += (long long)prefix_part[w];
     for (int w = 0; w < warp; w++) before += warp_total[w];
     const int64_t offset = before + inc - count;
     if (r == n - 1) {

@@ -187,12 +187,13 @@ def test_binning_tile_key_width(tiles_x):
 @pytest.mark.parametrize("seed", [3, 4])
 def test_binning_random_ellipses_bit_exact(tile_h, tile_w, seed):
     """Small, huge, thin and degenerate ellipses with depth ties (exercises
-    per-lane and whole-warp emission and > 32-row Gaussians)."""
+    per-lane emission (<= 32 pairs), whole-warp emission (more) and > 32-row
+    Gaussians)."""
     rng = np.random.default_rng(seed)
     proj = splats(rng, 2048, 640, 360, radius=(0.4, 60.0), huge=8)
     table, exp = _bin_both(proj, 640, 360, tile_w, tile_h, 1 << 19)
     counts = exp["point_counts"]
-    assert np.any((counts > 0) & (counts <= 16)) and np.any(counts > 16)
+    assert np.any((counts > 16) & (counts <= 32)) and np.any(counts > 32)
     _assert_tables_equal(table, exp)
 
 
