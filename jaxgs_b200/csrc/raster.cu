@@ -10,16 +10,18 @@
 // (ROWS = 2 when tile_h is a multiple of 8, else 1).
 //  * Forward: a warp walks the tile's pairs in 32-pair batches; each lane
 //    stages one 48-byte splat record and tests the splat's conservative
-//    1/256-level bounding box against the warp's block, so one ballot skips
-//    every splat that cannot reach the block.  Warps stop independently once
+//    1/256-level bounding box, then the ellipse itself (ellipse_hit), against
+//    the warp's block, so one ballot skips every splat that cannot reach the
+//    block.  Warps stop independently once
 //    all their pixels are saturated, and record per batch a 32-bit word of
 //    the pairs that composited at least one fragment of the block.
 //  * Backward: a warp reads those words from its top pair down and visits
 //    only the set bits (exact pruning), recomputing each fragment in reverse.
 //    Per splat every lane accumulates moments of its pixels' power gradients
 //    (sum ge, ge*dy, ge*dy^2; the lane's column fixes dx) and colour
-//    gradients; a transposed butterfly reduces eight of them in nine
-//    shuffles, and one predicated RED per warp adds the ten cotangents.
+//    gradients; the moments of two contributing splats are reduced together
+//    by one 16-value transposed butterfly, and one predicated RED per warp
+//    adds both splats' cotangents.
 //
 // The power is evaluated with the host oracle's operation order (the conic
 // scaled by -1/2, shared c00*dx / c10*dx, fused dy terms), so it is
@@ -39,6 +41,27 @@ constexpr float kMinT = 1.0f / 8192.0f;
 //   r2 = (red, green, blue, opacity)
 // ext_x = -inf marks a splat that can never reach alpha 1/256; +inf one whose
 // conic is not positive definite (never skipped).
+__host__ __device__ __forceinline__ void pack_record(float2 m, float4 c, float o, float red,
+                                                    float green, float blue, float4 r[3])
+{
+    float ex, ey;
+    float b = 0.5f * (c.y + c.z);
+    float det = c.x * c.w - b * b;
+    if (!(o * 256.0f >= 0.99999f)) {
+        ex = ey = -INFINITY;
+    } else if (!(c.x > 0.0f && c.w > 0.0f && det > 0.0f)) {
+        ex = ey = INFINITY;
+    } else {
+        // q = d^T C d <= level  <=>  o * exp(-q/2) >= 1/256; 0.1% + margin.
+        float level = 2.0f * logf(fmaxf(o * 256.0f, 1.0f)) * 1.001f + 1e-3f;
+        ex = sqrtf(level * c.w / det) * 1.0005f + 1e-3f;
+        ey = sqrtf(level * c.x / det) * 1.0005f + 1e-3f;
+    }
+    r[0] = make_float4(m.x, m.y, ex, ey);
+    r[1] = make_float4(-0.5f * c.x, -0.5f * c.y, -0.5f * c.z, -0.5f * c.w);
+    r[2] = make_float4(red, green, blue, o);
+}
+
 __global__ void pack_kernel(int64_t capacity, const float* __restrict__ mean,
                             const float* __restrict__ conic, const float* __restrict__ color,
                             const float* __restrict__ alpha, const int8_t* __restrict__ visible,
@@ -47,26 +70,14 @@ __global__ void pack_kernel(int64_t capacity, const float* __restrict__ mean,
     pdl_begin();
     int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (g >= capacity || visible[g] == 0) return;
-    float2 m = *reinterpret_cast<const float2*>(mean + g * 2);
-    float4 c = *reinterpret_cast<const float4*>(conic + g * 4);
-    float o = alpha[g];
-    float ex, ey;
-    float b = 0.5f * (c.y + c.z);
-    float det = c.x * c.w - b * b;
-    if (!(o * 256.0f >= 0.99999f)) {
-        ex = ey = -__int_as_float(0x7f800000);
-    } else if (!(c.x > 0.0f && c.w > 0.0f && det > 0.0f)) {
-        ex = ey = __int_as_float(0x7f800000);
-    } else {
-        // q = d^T C d <= level  <=>  o * exp(-q/2) >= 1/256; 0.1% + margin.
-        float level = 2.0f * logf(fmaxf(o * 256.0f, 1.0f)) * 1.001f + 1e-3f;
-        ex = sqrtf(level * c.w / det) * 1.0005f + 1e-3f;
-        ey = sqrtf(level * c.x / det) * 1.0005f + 1e-3f;
-    }
-    float4* r = splats + g * 3;
-    r[0] = make_float4(m.x, m.y, ex, ey);
-    r[1] = make_float4(-0.5f * c.x, -0.5f * c.y, -0.5f * c.z, -0.5f * c.w);
-    r[2] = make_float4(color[g * 3], color[g * 3 + 1], color[g * 3 + 2], o);
+    float4 r[3];
+    pack_record(*reinterpret_cast<const float2*>(mean + g * 2),
+                *reinterpret_cast<const float4*>(conic + g * 4), alpha[g], color[g * 3],
+                color[g * 3 + 1], color[g * 3 + 2], r);
+    float4* out = splats + g * 3;
+    out[0] = r[0];
+    out[1] = r[1];
+    out[2] = r[2];
 }
 
 // Heaviest-first tile permutation: counting sort into 256 buckets, eight per
@@ -172,10 +183,64 @@ __device__ __forceinline__ Geom<ROWS> geom(int width, int tile_w, int tile_h, in
 
 // Can the splat reach alpha >= 1/256 at any pixel centre of the block?
 template <int ROWS>
-__device__ __forceinline__ bool block_hit(float4 r0, float bx0, float by0)
+__host__ __device__ __forceinline__ bool block_hit(float4 r0, float bx0, float by0)
 {
     return r0.x - r0.z <= bx0 + 7.5f && r0.x + r0.z >= bx0 + 0.5f &&
            r0.y - r0.w <= by0 + (4 * ROWS - 0.5f) && r0.y + r0.w >= by0 + 0.5f;
+}
+
+// Can the splat reach alpha >= 1/256 at any pixel centre of the block?  The
+// exact form of block_hit: the largest power over the rectangle of the
+// block's pixel centres (a concave quadratic, so its maximum is the mean when
+// the rectangle holds it, else on an edge at the clamped vertex) against
+// ln(1 / (256 o)), less a margin far above the rounding of both this
+// evaluation and the fragment's (1e-4 plus 1e-5 of the quadratic's term
+// sizes), so it never rejects a splat a pixel would composite.  Splats with
+// a non-positive-definite conic (ext = +inf) always pass.
+__host__ __device__ __forceinline__ float fast_recip(float x)
+{
+#ifdef __CUDA_ARCH__
+    return __fdividef(1.0f, x);
+#else
+    return 1.0f / x;
+#endif
+}
+
+__host__ __device__ __forceinline__ float fast_log(float x)
+{
+#ifdef __CUDA_ARCH__
+    return __logf(x);
+#else
+    return logf(x);
+#endif
+}
+
+template <int ROWS>
+__host__ __device__ __forceinline__ bool ellipse_hit(float4 r0, float4 r1, float o, float bx0,
+                                                     float by0)
+{
+    if (!(r0.z < INFINITY)) return true;
+    const float x0 = bx0 + 0.5f - r0.x, x1 = bx0 + 7.5f - r0.x;
+    const float y0 = by0 + 0.5f - r0.y, y1 = by0 + (4 * ROWS - 0.5f) - r0.y;
+    if (x0 <= 0.0f && x1 >= 0.0f && y0 <= 0.0f && y1 >= 0.0f) return true;
+    // power(dx, dy) = a dx^2 + b dx dy + c dy^2, a = -c00/2 < 0, c = -c11/2 < 0.
+    const float a = r1.x, b = r1.y + r1.z, c = r1.w;
+    const float ky = -0.5f * b * fast_recip(c), kx = -0.5f * b * fast_recip(a);
+    float best = -INFINITY;
+    const float xs[2] = {x0, x1}, ys[2] = {y0, y1};
+#pragma unroll
+    for (int i = 0; i < 2; i++) {
+        const float x = xs[i];
+        const float y = fminf(fmaxf(ky * x, y0), y1);
+        best = fmaxf(best, fmaf(x, fmaf(a, x, b * y), c * y * y));
+        const float yy = ys[i];
+        const float xx = fminf(fmaxf(kx * yy, x0), x1);
+        best = fmaxf(best, fmaf(xx, fmaf(a, xx, b * yy), c * yy * yy));
+    }
+    const float rx = fmaxf(x0 * x0, x1 * x1), ry = fmaxf(y0 * y0, y1 * y1);
+    const float size = fabsf(a) * rx + fabsf(b) * sqrtf(rx * ry) + fabsf(c) * ry;
+    const float thr = -fast_log(256.0f * o);
+    return best >= thr - (1e-4f + 1e-5f * size);
 }
 
 __device__ __forceinline__ uint32_t bit_word(int32_t start, int tile, int batch, int warps, int warp)
@@ -280,7 +345,10 @@ __device__ __forceinline__ Fragment<ROWS> fragment(const Stash& st, int k,
 // (packed_rasterize.py:363-377): the number of composited fragments and the
 // sum of their compositing weights T * alpha, as interleaved pairs.
 template <int ROWS, bool WANT_DEPTH, bool RECORD, bool STATS>
-__global__ void __launch_bounds__(256) raster_fwd_kernel(
+// At most 48 registers (five 256-thread blocks' worth per SM): with the
+// exact block test the compiler would take 58, and 48 keeps 19 two-warp CTAs
+// per SM (2 % faster on config 2; the depth-writing instances spill 8-16 B).
+__global__ void __launch_bounds__(256, 5) raster_fwd_kernel(
     gsb_raster_params p, const float4* __restrict__ splats, const float* __restrict__ depth,
     const int32_t* __restrict__ ids, const int32_t* __restrict__ offsets,
     const int32_t* __restrict__ order, const float* __restrict__ background,
@@ -323,8 +391,14 @@ __global__ void __launch_bounds__(256) raster_fwd_kernel(
             const float4* rec = splats + (int64_t)g * 3;
             float4 r0 = __ldg(rec);
             hit = block_hit<ROWS>(r0, bx0, by0);
+            float4 r1, r2;
             if (hit) {
-                stash_splat(st, lane, r0, __ldg(rec + 1), __ldg(rec + 2));
+                r1 = __ldg(rec + 1);
+                r2 = __ldg(rec + 2);
+                hit = ellipse_hit<ROWS>(r0, r1, r2.w, bx0, by0);
+            }
+            if (hit) {
+                stash_splat(st, lane, r0, r1, r2);
                 if (STATS) st.id[lane] = g;
                 if (WANT_DEPTH) {
                     const float d = __ldg(depth + g);
