@@ -237,8 +237,8 @@ __host__ __device__ __forceinline__ bool ellipse_hit(float4 r0, float4 r1, float
         const float xx = fminf(fmaxf(kx * yy, x0), x1);
         best = fmaxf(best, fmaf(xx, fmaf(a, xx, b * yy), c * yy * yy));
     }
-    const float rx = fmaxf(x0 * x0, x1 * x1), ry = fmaxf(y0 * y0, y1 * y1);
-    const float size = fabsf(a) * rx + fabsf(b) * sqrtf(rx * ry) + fabsf(c) * ry;
+    const float mx = fmaxf(fabsf(x0), fabsf(x1)), my = fmaxf(fabsf(y0), fabsf(y1));
+    const float size = fabsf(a) * mx * mx + fabsf(b) * mx * my + fabsf(c) * my * my;
     const float thr = -fast_log(256.0f * o);
     return best >= thr - (1e-4f + 1e-5f * size);
 }
