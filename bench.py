@@ -682,8 +682,8 @@ def _time_config4(stream, steps: int = 24, warmup: int = 3) -> dict:
 
 # DRAM traffic of one raster_bwd_kernel launch on this workload
 # (dram__bytes_read.sum + dram__bytes_write.sum, one-kernel ncu capture of
-# `python bench.py --steps 1 --warmup 1 --no-cpu-baseline --no-e2e`,
-# profiles/raster_bwd_config2.md): 87.37 MB read + 4.76 MB written.
+# `python bench.py --steps 1 --warmup 1 --no-cpu-baseline --no-e2e`, the
+# launch after the first): 87.37 MB read + 4.76 MB written.
 RASTER_BWD_DRAM_BYTES = 92_134_400
 # FP32 work per backward fragment evaluation (one splat at one pixel): the
 # alpha, transmittance, colour and moment arithmetic of the reverse pass.
